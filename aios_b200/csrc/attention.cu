@@ -1,0 +1,690 @@
+// Paged GQA attention for the CandidateGroup path (replaces the FlashInfer
+// paged prefill/decode wrappers of aios/attention/flashinfer.py and the SDPA
+// fallback _sdpa_prefill_attention, aios/attention/flashinfer.py:33-91).
+//
+// KV layout: the reference MHAKVCache buffer [2, L, pages, page_size, Hkv, d]
+// (aios/kvcache/mha_pool.py:28-37). A token slot s (= page * page_size + offset)
+// of one layer lives at k_cache + s * Hkv * d, so every kernel takes a per-token
+// slot table ("page table", [rows, max_len] int32) and works for page_size 1
+// and 16 alike.
+//
+// Decode is a cascade: one CTA per KV head stages each shared-prefix KV slot in
+// shared memory ONCE and scores it against all rows x GQA-group query heads,
+// then adds each row's own suffix slots; partial softmax states merge online.
+// The decode kernel also owns the step's q/k RMSNorm, bf16 RoPE and the KV store
+// of the new token (aios/models/qwen3.py:60-70 + aios/kernel/store.py), so the
+// raw qkv projection output is its only input.
+#include <algorithm>
+
+#include "abi_util.h"
+#include "common.cuh"
+
+namespace aiosb {
+namespace {
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kKeyChunk = 64;  // keys staged per shared-memory chunk
+constexpr int kMaxQPerWarp = 8;
+constexpr int kMaxQueries = kAttnWarps * kMaxQPerWarp;  // 64 query vectors per CTA
+
+// Online-softmax state of one query vector, lane-distributed over head dims.
+template <int D>
+struct QState {
+  float m, l;
+  float acc[D / 32];
+};
+
+template <int D>
+__device__ __forceinline__ void qstate_init(QState<D>& s) {
+  s.m = -INFINITY;
+  s.l = 0.f;
+#pragma unroll
+  for (int i = 0; i < D / 32; ++i) s.acc[i] = 0.f;
+}
+
+// Folds one block of up to 64 keys into `st`. s0/s1 are this lane's scores for
+// keys lane and lane+32 (-inf when masked); v_at(j, i) returns V[j][i*32+lane].
+template <int D, typename VFn>
+__device__ __forceinline__ void fold_scores(QState<D>& st, float s0, float s1, int nk, VFn v_at) {
+  const float cmax = warp_max(fmaxf(s0, s1));
+  if (cmax == -INFINITY) return;
+  const float m_new = fmaxf(st.m, cmax);
+  const float corr = expf(st.m - m_new);
+  const float p0 = expf(s0 - m_new), p1 = expf(s1 - m_new);
+  st.l = st.l * corr + warp_sum(p0 + p1);
+#pragma unroll
+  for (int i = 0; i < D / 32; ++i) st.acc[i] *= corr;
+  for (int j = 0; j < nk; ++j) {
+    const float p = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+#pragma unroll
+    for (int i = 0; i < D / 32; ++i) st.acc[i] += p * v_at(j, i);
+  }
+  st.m = m_new;
+}
+
+// q (fp32, shared, broadcast) . K row (bf16 pairs).
+template <int D>
+__device__ __forceinline__ float dot_q_k(const float* q, const __nv_bfloat162* k) {
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < D / 2; ++w) {
+    const float2 kv = __bfloat1622float2(k[w]);
+    s += q[2 * w] * kv.x + q[2 * w + 1] * kv.y;
+  }
+  return s;
+}
+
+// Stage keys [k0, k0+nk) of one slot list for KV head h into shared memory.
+// Ks rows are padded to D+2 elements (odd word stride: conflict-free per-lane
+// row reads); Vs rows are dense.
+template <int D>
+__device__ __forceinline__ void stage_chunk(const __nv_bfloat16* __restrict__ k_cache,
+                                            const __nv_bfloat16* __restrict__ v_cache, int64_t tok_stride, int h,
+                                            const int32_t* __restrict__ slots, int k0, int nk, int64_t num_slots,
+                                            __nv_bfloat16* Ks, __nv_bfloat16* Vs, int32_t* status) {
+  constexpr int kWords = D / 2;  // 32-bit words per row
+  for (int idx = threadIdx.x; idx < nk * kWords; idx += blockDim.x) {
+    const int j = idx / kWords, w = idx % kWords;
+    int64_t slot = slots[k0 + j];
+    if (slot < 0 || slot >= num_slots) {
+      if (w == 0) report(status, AIOSB_DEV_SLOT_RANGE);
+      slot = 0;
+    }
+    const uint32_t* kr = reinterpret_cast<const uint32_t*>(k_cache + slot * tok_stride + (int64_t)h * D);
+    const uint32_t* vr = reinterpret_cast<const uint32_t*>(v_cache + slot * tok_stride + (int64_t)h * D);
+    reinterpret_cast<uint32_t*>(Ks)[j * (kWords + 1) + w] = kr[w];
+    reinterpret_cast<uint32_t*>(Vs)[j * kWords + w] = vr[w];
+  }
+}
+
+// RMSNorm of one head vector (lane-distributed: element i*32+lane), rounded to
+// bf16, then bf16 RoPE exactly as aios/layers/attention.py:6-16 computes it:
+// out = bf16(bf16(x*cos) + bf16(rotate_half(x)*sin)).
+template <int D>
+__device__ __forceinline__ void norm_rope(float (&x)[D / 32], const __nv_bfloat16* __restrict__ w, float eps,
+                                          const __nv_bfloat16* cos_row, const __nv_bfloat16* sin_row,
+                                          bool do_norm, bool do_rope, int lane, float* tmp /*shared D floats*/) {
+  constexpr int DPL = D / 32;
+  if (do_norm) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) ss += x[i] * x[i];
+    ss = warp_sum(ss);
+    const float rcp = 1.0f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) x[i] = round_bf16(x[i] * rcp * bf16_to_f(w[i * 32 + lane]));
+  }
+  if (do_rope) {
+    // rotate_half needs element (e + D/2) mod D: exchange through shared memory.
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) tmp[i * 32 + lane] = x[i];
+    __syncwarp();
+    float r[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int e = i * 32 + lane;
+      r[i] = e < D / 2 ? -tmp[e + D / 2] : tmp[e - D / 2];
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const int e = i * 32 + lane;
+      const float a = round_bf16(x[i] * bf16_to_f(cos_row[e]));
+      const float b = round_bf16(r[i] * bf16_to_f(sin_row[e]));
+      x[i] = round_bf16(a + b);
+    }
+  }
+}
+
+struct DecodeArgs {
+  // fused prologue inputs (qkv != nullptr) or pre-rotated q (q != nullptr)
+  const __nv_bfloat16* qkv;  // [R, qkv_stride]: q heads | k heads | v heads (raw projection)
+  int64_t qkv_stride;
+  const __nv_bfloat16* q;  // [R, q_stride] already normalised/rotated (no prologue)
+  int64_t q_stride;
+  const __nv_bfloat16* q_norm_w;
+  const __nv_bfloat16* k_norm_w;
+  float eps;
+  const __nv_bfloat16* cos_tab;  // [max_pos, D] bf16
+  const __nv_bfloat16* sin_tab;
+  int max_pos;
+  const int32_t* positions;  // [R]
+  const int32_t* out_loc;    // [R] slot of the new token
+  // cache + slot table
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int64_t num_slots;
+  const int32_t* page_table;
+  int64_t table_stride;
+  const int32_t* row_table;   // [R] page-table row of each local row
+  const int32_t* seq_lens;    // [R] keys per row including the new token
+  const int32_t* prefix_len;  // device scalar: shared prefix keys (0 = none)
+  const int32_t* active;      // [R] nonzero = row runs; nullptr = all rows
+  int rows, hq, hkv;
+  float scale;
+  __nv_bfloat16* out;  // [R, out_stride]
+  int64_t out_stride;
+  int32_t* status;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads)
+    attn_decode_kernel(const DecodeArgs a) {
+  constexpr int DPL = D / 32;
+  extern __shared__ uint8_t smem_raw[];
+  const int h = blockIdx.x;
+  const int g = a.hq / a.hkv;
+  const int Q = a.rows * g;
+  float* q_s = reinterpret_cast<float*>(smem_raw);                          // [Q][D]
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(q_s + Q * D);        // [64][D+2]
+  __nv_bfloat16* Vs = Ks + kKeyChunk * (D + 2);                              // [64][D]
+  float* tmp = reinterpret_cast<float*>(Vs + kKeyChunk * D);                 // [warps][D]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tok_stride = (int64_t)a.hkv * D;
+
+  pdl_wait();
+  const int P = a.prefix_len != nullptr ? *a.prefix_len : 0;
+
+  // ---- prologue: q heads of this group (+ new k/v of this head) per row.
+  const int items = a.rows * (g + 1);
+  for (int it = warp; it < items; it += kAttnWarps) {
+    const int r = it / (g + 1), j = it % (g + 1);
+    const bool act = a.active == nullptr || a.active[r] != 0;
+    float* tw = tmp + warp * D;
+    if (j < g) {
+      float x[DPL];
+      const int qh = h * g + j;
+      if (act) {
+        if (a.qkv != nullptr) {
+          const __nv_bfloat16* src = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)qh * D;
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(src[i * 32 + lane]);
+          int pos = a.positions[r];
+          if (pos < 0 || pos >= a.max_pos) {
+            if (lane == 0) report(a.status, AIOSB_DEV_POSITION_RANGE);
+            pos = 0;
+          }
+          norm_rope<D>(x, a.q_norm_w, a.eps, a.cos_tab + (int64_t)pos * D, a.sin_tab + (int64_t)pos * D, true, true,
+                       lane, tw);
+        } else {
+          const __nv_bfloat16* src = a.q + (int64_t)r * a.q_stride + (int64_t)qh * D;
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(src[i * 32 + lane]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) x[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) q_s[(r * g + j) * D + i * 32 + lane] = x[i];
+    } else if (act && a.qkv != nullptr) {
+      const __nv_bfloat16* ksrc = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(a.hq + h) * D;
+      const __nv_bfloat16* vsrc = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(a.hq + a.hkv + h) * D;
+      float x[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(ksrc[i * 32 + lane]);
+      int pos = a.positions[r];
+      if (pos < 0 || pos >= a.max_pos) {
+        if (lane == 0) report(a.status, AIOSB_DEV_POSITION_RANGE);
+        pos = 0;
+      }
+      norm_rope<D>(x, a.k_norm_w, a.eps, a.cos_tab + (int64_t)pos * D, a.sin_tab + (int64_t)pos * D, true, true,
+                   lane, tw);
+      const int64_t slot = a.out_loc[r];
+      if (slot >= 0 && slot < a.num_slots) {
+        __nv_bfloat16* kd = a.k_cache + slot * tok_stride + (int64_t)h * D;
+        __nv_bfloat16* vd = a.v_cache + slot * tok_stride + (int64_t)h * D;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          kd[i * 32 + lane] = f_to_bf16(x[i]);
+          vd[i * 32 + lane] = vsrc[i * 32 + lane];
+        }
+      } else if (lane == 0) {
+        report(a.status, AIOSB_DEV_SLOT_RANGE);
+      }
+    }
+  }
+  __syncthreads();  // q_s complete; new K/V visible to the whole CTA
+
+  QState<D> st[kMaxQPerWarp];
+#pragma unroll
+  for (int s = 0; s < kMaxQPerWarp; ++s) qstate_init<D>(st[s]);
+
+  // ---- shared prefix: each slot staged once, scored against every query.
+  if (P > 0) {
+    const int32_t* pslots = a.page_table + (int64_t)a.row_table[0] * a.table_stride;
+    for (int k0 = 0; k0 < P; k0 += kKeyChunk) {
+      const int nk = min(kKeyChunk, P - k0);
+      stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, pslots, k0, nk, a.num_slots, Ks, Vs, a.status);
+      __syncthreads();
+#pragma unroll
+      for (int s = 0; s < kMaxQPerWarp; ++s) {
+        const int qi = warp + s * kAttnWarps;
+        if (qi < Q) {
+          const int r = qi / g;
+          if (a.active == nullptr || a.active[r] != 0) {
+            const float* qv = q_s + qi * D;
+            const __nv_bfloat162* K2 = reinterpret_cast<const __nv_bfloat162*>(Ks);
+            const float s0 = lane < nk ? dot_q_k<D>(qv, K2 + lane * (D / 2 + 1)) * a.scale : -INFINITY;
+            const float s1 = lane + 32 < nk ? dot_q_k<D>(qv, K2 + (lane + 32) * (D / 2 + 1)) * a.scale : -INFINITY;
+            fold_scores<D>(st[s], s0, s1, nk, [&](int j, int i) { return bf16_to_f(Vs[j * D + i * 32 + lane]); });
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+
+  // ---- per-row suffix keys [P, seq_len) straight from the paged cache.
+#pragma unroll
+  for (int s = 0; s < kMaxQPerWarp; ++s) {
+    const int qi = warp + s * kAttnWarps;
+    if (qi < Q) {
+      const int r = qi / g;
+      if (a.active == nullptr || a.active[r] != 0) {
+        const int32_t* rslots = a.page_table + (int64_t)a.row_table[r] * a.table_stride;
+        const int L = a.seq_lens[r];
+        const float* qv = q_s + qi * D;
+        for (int k0 = P; k0 < L; k0 += 64) {
+          const int nk = min(64, L - k0);
+          int64_t sl0 = lane < nk ? rslots[k0 + lane] : 0;
+          int64_t sl1 = lane + 32 < nk ? rslots[k0 + lane + 32] : 0;
+          if (sl0 < 0 || sl0 >= a.num_slots) { report(a.status, AIOSB_DEV_SLOT_RANGE); sl0 = 0; }
+          if (sl1 < 0 || sl1 >= a.num_slots) { report(a.status, AIOSB_DEV_SLOT_RANGE); sl1 = 0; }
+          const float s0 = lane < nk ? dot_q_k<D>(qv, reinterpret_cast<const __nv_bfloat162*>(
+                                                          a.k_cache + sl0 * tok_stride + (int64_t)h * D)) * a.scale
+                                     : -INFINITY;
+          const float s1 = lane + 32 < nk ? dot_q_k<D>(qv, reinterpret_cast<const __nv_bfloat162*>(
+                                                               a.k_cache + sl1 * tok_stride + (int64_t)h * D)) * a.scale
+                                          : -INFINITY;
+          fold_scores<D>(st[s], s0, s1, nk, [&](int j, int i) {
+            const int64_t sj = __shfl_sync(0xffffffffu, j < 32 ? sl0 : sl1, j & 31);
+            return bf16_to_f(a.v_cache[sj * tok_stride + (int64_t)h * D + i * 32 + lane]);
+          });
+        }
+      }
+    }
+  }
+
+  // ---- normalise and store.
+#pragma unroll
+  for (int s = 0; s < kMaxQPerWarp; ++s) {
+    const int qi = warp + s * kAttnWarps;
+    if (qi < Q) {
+      const int r = qi / g, j = qi % g;
+      const float inv = st[s].l > 0.f ? 1.0f / st[s].l : 0.f;
+      __nv_bfloat16* dst = a.out + (int64_t)r * a.out_stride + (int64_t)(h * g + j) * D;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st[s].acc[i] * inv);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace aiosb
+
+namespace aiosb {
+namespace {
+
+// ---- prefill prologue: q/k RMSNorm + RoPE, K/V store ----------------------
+// One warp per (token, head) item; q heads write the rotated q buffer, KV heads
+// write the paged cache at out_loc[t].
+struct PrologueArgs {
+  const __nv_bfloat16* qkv;
+  int64_t qkv_stride;
+  int64_t tokens;
+  int hq, hkv;
+  const __nv_bfloat16* q_norm_w;
+  const __nv_bfloat16* k_norm_w;
+  float eps;
+  const __nv_bfloat16* cos_tab;
+  const __nv_bfloat16* sin_tab;
+  int max_pos;
+  const int32_t* positions;
+  const int32_t* out_loc;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int64_t num_slots;
+  __nv_bfloat16* q_out;
+  int64_t q_out_stride;
+  int32_t* status;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads) qk_norm_rope_store_kernel(const PrologueArgs a) {
+  constexpr int DPL = D / 32;
+  __shared__ float tmp_all[kAttnWarps][D];
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int heads = a.hq + a.hkv;
+  const int64_t item = (int64_t)blockIdx.x * kAttnWarps + warp;
+  if (item >= a.tokens * heads) return;
+  const int64_t t = item / heads;
+  const int hh = (int)(item % heads);
+  int pos = a.positions[t];
+  if (pos < 0 || pos >= a.max_pos) {
+    if (lane == 0) report(a.status, AIOSB_DEV_POSITION_RANGE);
+    pos = 0;
+  }
+  const __nv_bfloat16* row = a.qkv + t * a.qkv_stride;
+  float x[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(row[(int64_t)hh * D + i * 32 + lane]);
+  const bool is_q = hh < a.hq;
+  norm_rope<D>(x, is_q ? a.q_norm_w : a.k_norm_w, a.eps, a.cos_tab + (int64_t)pos * D, a.sin_tab + (int64_t)pos * D,
+               true, true, lane, tmp_all[warp]);
+  if (is_q) {
+    __nv_bfloat16* dst = a.q_out + t * a.q_out_stride + (int64_t)hh * D;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(x[i]);
+    return;
+  }
+  const int kh = hh - a.hq;
+  const int64_t slot = a.out_loc[t];
+  if (slot < 0 || slot >= a.num_slots) {
+    if (lane == 0) report(a.status, AIOSB_DEV_SLOT_RANGE);
+    return;
+  }
+  const int64_t tok_stride = (int64_t)a.hkv * D;
+  __nv_bfloat16* kd = a.k_cache + slot * tok_stride + (int64_t)kh * D;
+  __nv_bfloat16* vd = a.v_cache + slot * tok_stride + (int64_t)kh * D;
+  const __nv_bfloat16* vs = row + (int64_t)(a.hq + a.hkv + kh) * D;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) {
+    kd[i * 32 + lane] = f_to_bf16(x[i]);
+    vd[i * 32 + lane] = vs[i * 32 + lane];
+  }
+}
+
+// ---- prefill attention: causal, cached-prefix offset, varlen requests ------
+// CTA = (KV head, query tile of `tile_tokens` tokens of one request). Keys
+// [0, cached_len + last query + 1) of the request's slot list are staged once
+// per chunk and scored against all tile tokens x GQA heads with the causal mask
+// key_pos <= cached_len + token index (aios/attention/flashinfer.py:33-91).
+struct PrefillArgs {
+  const __nv_bfloat16* q;
+  int64_t q_stride;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  int64_t num_slots;
+  const int32_t* page_table;
+  int64_t table_stride;
+  const int32_t* req_q_start;
+  const int32_t* req_q_len;
+  const int32_t* req_cached_len;
+  const int32_t* req_table_row;
+  const int32_t* tile_req;
+  const int32_t* tile_q0;
+  int tile_tokens;
+  int hq, hkv;
+  float scale;
+  __nv_bfloat16* out;
+  int64_t out_stride;
+  int32_t* status;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const PrefillArgs a) {
+  constexpr int DPL = D / 32;
+  extern __shared__ uint8_t smem_raw[];
+  const int h = blockIdx.x;
+  const int tile = blockIdx.y;
+  const int g = a.hq / a.hkv;
+  float* q_s = reinterpret_cast<float*>(smem_raw);
+  const int Qmax = a.tile_tokens * g;
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(q_s + Qmax * D);
+  __nv_bfloat16* Vs = Ks + kKeyChunk * (D + 2);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tok_stride = (int64_t)a.hkv * D;
+
+  pdl_wait();
+  const int req = a.tile_req[tile];
+  const int q0 = a.tile_q0[tile];
+  const int qlen = a.req_q_len[req];
+  const int nq = min(a.tile_tokens, qlen - q0);
+  const int cached = a.req_cached_len[req];
+  const int64_t qbase = a.req_q_start[req];
+  const int32_t* slots = a.page_table + (int64_t)a.req_table_row[req] * a.table_stride;
+  const int Q = nq * g;
+  for (int idx = threadIdx.x; idx < Q * D; idx += blockDim.x) {
+    const int qi = idx / D, e = idx % D;
+    const int t = qi / g, j = qi % g;
+    q_s[idx] = bf16_to_f(a.q[(qbase + q0 + t) * a.q_stride + (int64_t)(h * g + j) * D + e]);
+  }
+  QState<D> st[kMaxQPerWarp];
+#pragma unroll
+  for (int s = 0; s < kMaxQPerWarp; ++s) qstate_init<D>(st[s]);
+  __syncthreads();
+
+  const int kv_end = cached + q0 + nq;
+  for (int k0 = 0; k0 < kv_end; k0 += kKeyChunk) {
+    const int nk = min(kKeyChunk, kv_end - k0);
+    stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, slots, k0, nk, a.num_slots, Ks, Vs, a.status);
+    __syncthreads();
+#pragma unroll
+    for (int s = 0; s < kMaxQPerWarp; ++s) {
+      const int qi = warp + s * kAttnWarps;
+      if (qi < Q) {
+        const int qpos = cached + q0 + qi / g;  // absolute position of this query
+        const float* qv = q_s + qi * D;
+        const __nv_bfloat162* K2 = reinterpret_cast<const __nv_bfloat162*>(Ks);
+        const int kp0 = k0 + lane, kp1 = k0 + lane + 32;
+        const float s0 = (lane < nk && kp0 <= qpos) ? dot_q_k<D>(qv, K2 + lane * (D / 2 + 1)) * a.scale : -INFINITY;
+        const float s1 =
+            (lane + 32 < nk && kp1 <= qpos) ? dot_q_k<D>(qv, K2 + (lane + 32) * (D / 2 + 1)) * a.scale : -INFINITY;
+        fold_scores<D>(st[s], s0, s1, nk, [&](int j, int i) { return bf16_to_f(Vs[j * D + i * 32 + lane]); });
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int s = 0; s < kMaxQPerWarp; ++s) {
+    const int qi = warp + s * kAttnWarps;
+    if (qi < Q) {
+      const int t = qi / g, j = qi % g;
+      const float inv = st[s].l > 0.f ? 1.0f / st[s].l : 0.f;
+      __nv_bfloat16* dst = a.out + (qbase + q0 + t) * a.out_stride + (int64_t)(h * g + j) * D;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st[s].acc[i] * inv);
+    }
+  }
+}
+
+template <int D>
+size_t decode_smem(int queries) {
+  return (size_t)queries * D * 4 + (size_t)kKeyChunk * (D + 2) * 2 + (size_t)kKeyChunk * D * 2 +
+         (size_t)kAttnWarps * D * 4;
+}
+template <int D>
+size_t prefill_smem(int queries) {
+  return (size_t)queries * D * 4 + (size_t)kKeyChunk * (D + 2) * 2 + (size_t)kKeyChunk * D * 2;
+}
+
+template <typename K>
+void allow_smem(K kern, size_t bytes) {
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+}  // namespace
+}  // namespace aiosb
+
+using namespace aiosb;
+
+extern "C" int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const void* q, int64_t q_stride,
+                                      const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_tab,
+                                      const void* sin_tab, int64_t max_pos, const int32_t* positions,
+                                      const int32_t* out_loc, void* k_cache, void* v_cache, int64_t num_slots,
+                                      const int32_t* page_table, int64_t table_stride, const int32_t* row_table,
+                                      const int32_t* seq_lens, const int32_t* prefix_len, const int32_t* active,
+                                      int64_t rows, int64_t num_qo_heads, int64_t num_kv_heads, int64_t head_dim,
+                                      float scale, void* out, int64_t out_stride, int32_t* status, void* stream) {
+  AIOSB_REQUIRE(rows >= 0 && num_kv_heads > 0 && num_qo_heads > 0 && num_qo_heads % num_kv_heads == 0,
+                AIOSB_ERR_INVALID_ARG, "query head count must be divisible by KV head count");
+  AIOSB_REQUIRE(head_dim == 64 || head_dim == 96 || head_dim == 128, AIOSB_ERR_UNSUPPORTED,
+                "attention_decode: head_dim %lld unsupported (64, 96, 128)", (long long)head_dim);
+  const int64_t g = num_qo_heads / num_kv_heads;
+  AIOSB_REQUIRE(rows * g <= kMaxQueries, AIOSB_ERR_UNSUPPORTED,
+                "attention_decode: rows * group = %lld exceeds %d", (long long)(rows * g), kMaxQueries);
+  if (rows == 0) return AIOSB_OK;
+  AIOSB_REQUIRE((qkv != nullptr) != (q != nullptr), AIOSB_ERR_INVALID_ARG,
+                "attention_decode: pass exactly one of qkv (fused prologue) or q (pre-rotated)");
+  AIOSB_REQUIRE(k_cache && v_cache && page_table && row_table && seq_lens && out && positions,
+                AIOSB_ERR_INVALID_ARG, "attention_decode: null pointer");
+  AIOSB_REQUIRE(qkv == nullptr || (q_norm_w && k_norm_w && cos_tab && sin_tab && out_loc), AIOSB_ERR_INVALID_ARG,
+                "attention_decode: fused prologue needs norm weights, rope tables and out_loc");
+  DecodeArgs a;
+  a.qkv = (const __nv_bfloat16*)qkv;
+  a.qkv_stride = qkv_stride;
+  a.q = (const __nv_bfloat16*)q;
+  a.q_stride = q_stride;
+  a.q_norm_w = (const __nv_bfloat16*)q_norm_w;
+  a.k_norm_w = (const __nv_bfloat16*)k_norm_w;
+  a.eps = eps;
+  a.cos_tab = (const __nv_bfloat16*)cos_tab;
+  a.sin_tab = (const __nv_bfloat16*)sin_tab;
+  a.max_pos = (int)max_pos;
+  a.positions = positions;
+  a.out_loc = out_loc;
+  a.k_cache = (__nv_bfloat16*)k_cache;
+  a.v_cache = (__nv_bfloat16*)v_cache;
+  a.num_slots = num_slots;
+  a.page_table = page_table;
+  a.table_stride = table_stride;
+  a.row_table = row_table;
+  a.seq_lens = seq_lens;
+  a.prefix_len = prefix_len;
+  a.active = active;
+  a.rows = (int)rows;
+  a.hq = (int)num_qo_heads;
+  a.hkv = (int)num_kv_heads;
+  a.scale = scale;
+  a.out = (__nv_bfloat16*)out;
+  a.out_stride = out_stride;
+  a.status = status;
+  const int Q = (int)(rows * g);
+  cudaError_t e;
+  const dim3 grid((unsigned)num_kv_heads), block(kAttnThreads);
+  cudaStream_t s = as_stream(stream);
+  if (head_dim == 64) {
+    allow_smem(attn_decode_kernel<64>, decode_smem<64>(kMaxQueries));
+    e = launch_pdl(attn_decode_kernel<64>, grid, block, decode_smem<64>(Q), s, a);
+  } else if (head_dim == 96) {
+    allow_smem(attn_decode_kernel<96>, decode_smem<96>(kMaxQueries));
+    e = launch_pdl(attn_decode_kernel<96>, grid, block, decode_smem<96>(Q), s, a);
+  } else {
+    allow_smem(attn_decode_kernel<128>, decode_smem<128>(kMaxQueries));
+    e = launch_pdl(attn_decode_kernel<128>, grid, block, decode_smem<128>(Q), s, a);
+  }
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attention_decode: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_qk_norm_rope_store(const void* qkv, int64_t qkv_stride, int64_t tokens, int64_t num_qo_heads,
+                                        int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w,
+                                        const void* k_norm_w, float eps, const void* cos_tab, const void* sin_tab,
+                                        int64_t max_pos, const int32_t* positions, const int32_t* out_loc,
+                                        void* k_cache, void* v_cache, int64_t num_slots, void* q_out,
+                                        int64_t q_out_stride, int32_t* status, void* stream) {
+  AIOSB_REQUIRE(tokens >= 0 && num_qo_heads > 0 && num_kv_heads > 0, AIOSB_ERR_INVALID_ARG,
+                "qk_norm_rope_store: bad sizes");
+  AIOSB_REQUIRE(head_dim == 64 || head_dim == 96 || head_dim == 128, AIOSB_ERR_UNSUPPORTED,
+                "qk_norm_rope_store: head_dim %lld unsupported (64, 96, 128)", (long long)head_dim);
+  if (tokens == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(qkv && q_norm_w && k_norm_w && cos_tab && sin_tab && positions && out_loc && k_cache && v_cache &&
+                    q_out,
+                AIOSB_ERR_INVALID_ARG, "qk_norm_rope_store: null pointer");
+  PrologueArgs a;
+  a.qkv = (const __nv_bfloat16*)qkv;
+  a.qkv_stride = qkv_stride;
+  a.tokens = tokens;
+  a.hq = (int)num_qo_heads;
+  a.hkv = (int)num_kv_heads;
+  a.q_norm_w = (const __nv_bfloat16*)q_norm_w;
+  a.k_norm_w = (const __nv_bfloat16*)k_norm_w;
+  a.eps = eps;
+  a.cos_tab = (const __nv_bfloat16*)cos_tab;
+  a.sin_tab = (const __nv_bfloat16*)sin_tab;
+  a.max_pos = (int)max_pos;
+  a.positions = positions;
+  a.out_loc = out_loc;
+  a.k_cache = (__nv_bfloat16*)k_cache;
+  a.v_cache = (__nv_bfloat16*)v_cache;
+  a.num_slots = num_slots;
+  a.q_out = (__nv_bfloat16*)q_out;
+  a.q_out_stride = q_out_stride;
+  a.status = status;
+  const int64_t items = tokens * (num_qo_heads + num_kv_heads);
+  const dim3 grid((unsigned)((items + kAttnWarps - 1) / kAttnWarps)), block(kAttnThreads);
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e;
+  if (head_dim == 64) e = launch_pdl(qk_norm_rope_store_kernel<64>, grid, block, 0, s, a);
+  else if (head_dim == 96) e = launch_pdl(qk_norm_rope_store_kernel<96>, grid, block, 0, s, a);
+  else e = launch_pdl(qk_norm_rope_store_kernel<128>, grid, block, 0, s, a);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "qk_norm_rope_store: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_prefill_tile_tokens(int64_t num_qo_heads, int64_t num_kv_heads) {
+  if (num_kv_heads <= 0 || num_qo_heads <= 0 || num_qo_heads % num_kv_heads) return 0;
+  const int64_t g = num_qo_heads / num_kv_heads;
+  return g > kMaxQueries ? 0 : (int)(kMaxQueries / g);
+}
+
+extern "C" int aiosb_attention_prefill(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                                       int64_t num_slots, const int32_t* page_table, int64_t table_stride,
+                                       const int32_t* req_q_start, const int32_t* req_q_len,
+                                       const int32_t* req_cached_len, const int32_t* req_table_row,
+                                       const int32_t* tile_req, const int32_t* tile_q0, int64_t num_tiles,
+                                       int64_t tile_tokens, int64_t num_qo_heads, int64_t num_kv_heads,
+                                       int64_t head_dim, float scale, void* out, int64_t out_stride, int32_t* status,
+                                       void* stream) {
+  AIOSB_REQUIRE(num_tiles >= 0 && num_kv_heads > 0 && num_qo_heads % num_kv_heads == 0, AIOSB_ERR_INVALID_ARG,
+                "query head count must be divisible by KV head count");
+  AIOSB_REQUIRE(head_dim == 64 || head_dim == 96 || head_dim == 128, AIOSB_ERR_UNSUPPORTED,
+                "attention_prefill: head_dim %lld unsupported (64, 96, 128)", (long long)head_dim);
+  const int64_t g = num_qo_heads / num_kv_heads;
+  AIOSB_REQUIRE(tile_tokens >= 1 && tile_tokens * g <= kMaxQueries, AIOSB_ERR_INVALID_ARG,
+                "attention_prefill: tile_tokens * group must be in [1, %d]", kMaxQueries);
+  if (num_tiles == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(q && k_cache && v_cache && page_table && req_q_start && req_q_len && req_cached_len &&
+                    req_table_row && tile_req && tile_q0 && out,
+                AIOSB_ERR_INVALID_ARG, "attention_prefill: null pointer");
+  PrefillArgs a;
+  a.q = (const __nv_bfloat16*)q;
+  a.q_stride = q_stride;
+  a.k_cache = (const __nv_bfloat16*)k_cache;
+  a.v_cache = (const __nv_bfloat16*)v_cache;
+  a.num_slots = num_slots;
+  a.page_table = page_table;
+  a.table_stride = table_stride;
+  a.req_q_start = req_q_start;
+  a.req_q_len = req_q_len;
+  a.req_cached_len = req_cached_len;
+  a.req_table_row = req_table_row;
+  a.tile_req = tile_req;
+  a.tile_q0 = tile_q0;
+  a.tile_tokens = (int)tile_tokens;
+  a.hq = (int)num_qo_heads;
+  a.hkv = (int)num_kv_heads;
+  a.scale = scale;
+  a.out = (__nv_bfloat16*)out;
+  a.out_stride = out_stride;
+  a.status = status;
+  const int Q = (int)(tile_tokens * g);
+  const dim3 grid((unsigned)num_kv_heads, (unsigned)num_tiles), block(kAttnThreads);
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e;
+  if (head_dim == 64) {
+    allow_smem(attn_prefill_kernel<64>, prefill_smem<64>(kMaxQueries));
+    e = launch_pdl(attn_prefill_kernel<64>, grid, block, prefill_smem<64>(Q), s, a);
+  } else if (head_dim == 96) {
+    allow_smem(attn_prefill_kernel<96>, prefill_smem<96>(kMaxQueries));
+    e = launch_pdl(attn_prefill_kernel<96>, grid, block, prefill_smem<96>(Q), s, a);
+  } else {
+    allow_smem(attn_prefill_kernel<128>, prefill_smem<128>(kMaxQueries));
+    e = launch_pdl(attn_prefill_kernel<128>, grid, block, prefill_smem<128>(Q), s, a);
+  }
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attention_prefill: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}

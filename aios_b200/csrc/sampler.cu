@@ -1,0 +1,653 @@
+// Raw-logprob sampler (replaces aios/engine/sample.py:54-163) and the
+// CandidateGroup step bookkeeping of aios/ime.py:970-1054, on the device.
+//
+// One CTA samples one logits row, entirely in shared memory:
+//   raw log-softmax of the bf16 logits (fp32, aios/engine/sample.py:74);
+//   forbidden ids -> -inf on the sampling copy only (sample.py:76-111);
+//   greedy: first index of the maximum (torch argmax);
+//   otherwise: scaled = logits / T (fp32), top-k by an exact 4-pass radix select
+//   of the k-th largest key, candidates sorted by (value desc, token id asc),
+//   softmax, top-p keep-mask with the one-position shift of sample.py:140-146,
+//   re-softmax, index = #(cumsum < u) clamped (sample.py:161-165).
+// Cumulative sums accumulate in fp64 and round each prefix to fp32, the way
+// torch's CPU cumsum does for float tensors. Equal logits are ordered by
+// ascending token id; torch.topk leaves that order unspecified.
+#include <algorithm>
+
+#include "abi_util.h"
+#include "common.cuh"
+
+namespace aiosb {
+namespace {
+
+constexpr int kSampThreads = 512;
+constexpr int kMaxVocab = 32768;
+constexpr int kMaxSortK = 2048;  // candidates sorted in shared memory (top-k path)
+
+struct SampleParams {
+  float temperature;
+  int top_k;  // <= 0: no top-k
+  float top_p;
+  int greedy;
+};
+
+// Order-preserving uint32 key of an fp32 value (larger value -> larger key).
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Fixed part of the per-CTA shared memory; the fp32 logits row (V floats)
+// follows it in dynamic shared memory.
+struct RowSmem {
+  unsigned long long cand[kMaxSortK];   // (~key << 32 | id) sort keys
+  float cval[kMaxSortK];                // candidate scaled logits in sorted order
+  int cid[kMaxSortK];
+  float prob[kMaxSortK];
+  unsigned int hist[256];
+  float red[32];
+  int ired[32];
+  int misc[8];
+};
+
+// Block reduction of (value, index): max value, lowest index among ties.
+__device__ __forceinline__ void block_argmax(float v, int i, RowSmem& s, float& out_v, int& out_i) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+  }
+  __syncthreads();
+  if (lane == 0) { s.red[warp] = v; s.ired[warp] = i; }
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (int)(blockDim.x >> 5) ? s.red[lane] : -INFINITY;
+    i = lane < (int)(blockDim.x >> 5) ? s.ired[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+      if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+    }
+    if (lane == 0) { s.red[0] = v; s.ired[0] = i; }
+  }
+  __syncthreads();
+  out_v = s.red[0];
+  out_i = s.ired[0];
+  __syncthreads();
+}
+
+// Exclusive block scan of one int per thread (blockDim.x <= 1024).
+__device__ __forceinline__ int block_exclusive_scan(int x, RowSmem& s, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  __syncthreads();
+  if (lane == 31) s.ired[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int w = lane < nw ? s.ired[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    if (lane < nw) s.ired[lane] = wi - w;  // exclusive warp offsets
+    if (lane == nw - 1) s.misc[7] = wi;
+  }
+  __syncthreads();
+  const int res = s.ired[warp] + incl - x;
+  total = s.misc[7];
+  __syncthreads();
+  return res;
+}
+
+// Samples one row held in row[0..V) (sampling logits, forbidden already -inf).
+// Returns the token id (same value in every thread).
+__device__ int sample_row(RowSmem& s, float* row, int V, const SampleParams& p, float u) {
+  const int tid = threadIdx.x;
+  if (p.greedy) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < V; i += blockDim.x) {
+      const float v = row[i];
+      if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+    float mv;
+    int mi;
+    block_argmax(bv, bi, s, mv, mi);
+    return mi == 0x7fffffff ? 0 : mi;
+  }
+  // scaled = sampling_logits.float() / temperature  (sample.py:120)
+  for (int i = tid; i < V; i += blockDim.x) row[i] = row[i] / p.temperature;
+  __syncthreads();
+  int k;
+  bool sorted_path;
+  if (p.top_k > 0) {
+    k = min(p.top_k, V);
+    sorted_path = true;
+  } else if (p.top_p >= 1.0f) {
+    k = V;
+    sorted_path = false;  // candidates are all ids in index order (sample.py:126-130)
+  } else {
+    k = V;
+    sorted_path = true;  // full descending sort (sample.py:131-132)
+  }
+  if (sorted_path) {
+    // ---- radix select of the k-th largest order key.
+    uint32_t prefix = 0, mask = 0;
+    int remaining = k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += blockDim.x) s.hist[b] = 0;
+      __syncthreads();
+      for (int i = tid; i < V; i += blockDim.x) {
+        const uint32_t key = order_key(row[i]);
+        if ((key & mask) == prefix) atomicAdd(&s.hist[(key >> shift) & 0xFFu], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int acc = 0, b = 255;
+        for (; b > 0; --b) {
+          if (acc + (int)s.hist[b] >= remaining) break;
+          acc += (int)s.hist[b];
+        }
+        s.misc[0] = b;
+        s.misc[1] = remaining - acc;
+      }
+      __syncthreads();
+      prefix |= (uint32_t)s.misc[0] << shift;
+      mask |= 0xFFu << shift;
+      remaining = s.misc[1];
+      __syncthreads();
+    }
+    const uint32_t thr = prefix;  // key of the k-th largest value
+    const int need_eq = remaining;  // how many keys == thr to take (lowest ids first)
+    // ---- collect candidates in index order: each thread owns a contiguous id range.
+    const int per = (V + blockDim.x - 1) / blockDim.x;
+    const int lo = min(V, tid * per), hi = min(V, lo + per);
+    int n_gt = 0, n_eq = 0;
+    for (int i = lo; i < hi; ++i) {
+      const uint32_t key = order_key(row[i]);
+      n_gt += key > thr;
+      n_eq += key == thr;
+    }
+    int tot_gt, tot_eq;
+    const int off_gt = block_exclusive_scan(n_gt, s, tot_gt);
+    const int off_eq = block_exclusive_scan(n_eq, s, tot_eq);
+    int wg = off_gt, we = off_eq;
+    for (int i = lo; i < hi; ++i) {
+      const float v = row[i];
+      const uint32_t key = order_key(v);
+      int slot = -1;
+      if (key > thr) slot = wg++;
+      else if (key == thr) {
+        if (we < need_eq) slot = tot_gt + we;
+        ++we;
+      }
+      if (slot >= 0 && slot < kMaxSortK)
+        s.cand[slot] = ((unsigned long long)(~key) << 32) | (unsigned long long)(uint32_t)i;
+    }
+    // ---- bitonic sort ascending on (~key, id) = value desc, id asc.
+    int np = 1;
+    while (np < k) np <<= 1;
+    for (int i = k + tid; i < np; i += blockDim.x) s.cand[i] = ~0ull;
+    __syncthreads();
+    for (int size = 2; size <= np; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = tid; i < np; i += blockDim.x) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const bool up = (i & size) == 0;
+            const unsigned long long a = s.cand[i], b = s.cand[j];
+            if ((a > b) == up) { s.cand[i] = b; s.cand[j] = a; }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int i = tid; i < k; i += blockDim.x) {
+      const int id = (int)(uint32_t)(s.cand[i] & 0xffffffffull);
+      s.cid[i] = id;
+      s.cval[i] = row[id];
+    }
+    __syncthreads();
+  }
+  // ---- softmax over the candidates (sample.py:134), index order = sorted order.
+  const float* cv = sorted_path ? s.cval : row;
+  float mx = -INFINITY;
+  for (int i = tid; i < k; i += blockDim.x) mx = fmaxf(mx, cv[i]);
+  mx = block_max(mx, s.red);
+  float* pr = sorted_path ? s.prob : row;  // full-vocab path rewrites the row in place
+  float sum = 0.f;
+  for (int i = tid; i < k; i += blockDim.x) {
+    const float e = expf(cv[i] - mx);
+    pr[i] = e;
+    sum += e;
+  }
+  sum = block_sum(sum, s.red);
+  __syncthreads();
+  const float inv_sum = 1.0f / sum;  // torch's softmax scales by the reciprocal
+  for (int i = tid; i < k; i += blockDim.x) pr[i] = pr[i] * inv_sum;
+  __syncthreads();
+  if (p.top_p < 1.0f) {
+    // remove[i] = cumsum[i-1] > top_p for i >= 1 (shifted mask, first kept).
+    if (tid == 0) {
+      double acc = 0.0;
+      int keep = 1;
+      for (int i = 0; i < k; ++i) {
+        acc += (double)pr[i];
+        if ((float)acc > p.top_p) { keep = i + 1; break; }
+        keep = i + 1;
+      }
+      s.misc[2] = keep;
+    }
+    __syncthreads();
+    const int keep = s.misc[2];
+    // re-softmax over the kept prefix (masked entries are -inf -> probability 0).
+    float sum2 = 0.f;
+    for (int i = tid; i < k; i += blockDim.x) {
+      const float e = i < keep ? expf(cv[i] - mx) : 0.f;
+      pr[i] = e;
+      sum2 += e;
+    }
+    sum2 = block_sum(sum2, s.red);
+    __syncthreads();
+    const float inv_sum2 = 1.0f / sum2;
+    for (int i = tid; i < k; i += blockDim.x) pr[i] = pr[i] * inv_sum2;
+    __syncthreads();
+  }
+  // ---- inverse CDF: index = #(cumsum < u), clamped to k-1.
+  if (tid == 0) {
+    double acc = 0.0;
+    int idx = 0;
+    for (int i = 0; i < k; ++i) {
+      acc += (double)pr[i];
+      if ((float)acc < u) idx = i + 1;
+      else break;
+    }
+    if (idx > k - 1) idx = k - 1;
+    s.misc[3] = sorted_path ? s.cid[idx] : idx;
+  }
+  __syncthreads();
+  const int tok = s.misc[3];
+  __syncthreads();
+  return tok;
+}
+
+// Loads a bf16 logits row into s.row and returns its raw log-softmax pieces.
+__device__ __forceinline__ void load_row(RowSmem& s, float* row, const __nv_bfloat16* lrow, int V, float& mx,
+                                         float& lse) {
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = bf16_to_f(lrow[i]);
+    row[i] = v;
+    m = fmaxf(m, v);
+  }
+  m = block_max(m, s.red);
+  float se = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) se += expf(row[i] - m);
+  se = block_sum(se, s.red);
+  mx = m;
+  lse = logf(se);
+  __syncthreads();
+}
+
+}  // namespace
+}  // namespace aiosb
+
+namespace aiosb {
+namespace {
+
+// Applies forbidden ids to the sampling row: a shared list, then per-row ids.
+__device__ __forceinline__ void apply_forbidden(float* row, int V, const int32_t* ids, int n) {
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const int id = ids[j];
+    if (id >= 0 && id < V) row[id] = -INFINITY;
+  }
+}
+
+// ---- generic sampler: Sampler.sample_with_logprobs ------------------------
+__global__ void __launch_bounds__(kSampThreads)
+    sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int V, SampleParams p,
+                  const float* __restrict__ uniforms, const int32_t* __restrict__ forbidden, int n_forbidden,
+                  const int64_t* __restrict__ forbidden_rows, int n_forbidden_rows, int64_t* __restrict__ tok_out,
+                  float* __restrict__ lp_out, int32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
+  float* row = reinterpret_cast<float*>(smem_raw + sizeof(RowSmem));
+  pdl_wait();
+  const int r = blockIdx.x;
+  const __nv_bfloat16* lrow = logits + (int64_t)r * row_stride;
+  float mx, lse;
+  load_row(s, row, lrow, V, mx, lse);
+  apply_forbidden(row, V, forbidden, n_forbidden);
+  if (forbidden_rows != nullptr) {
+    for (int j = threadIdx.x; j < n_forbidden_rows; j += blockDim.x) {
+      const int64_t id = forbidden_rows[(int64_t)r * n_forbidden_rows + j];
+      if (id >= 0 && id < V) row[id] = -INFINITY;
+      else report(status, AIOSB_DEV_TOKEN_RANGE);
+    }
+  }
+  __syncthreads();
+  const float u = uniforms != nullptr ? uniforms[r] : 0.5f;
+  const int tok = sample_row(s, row, V, p, u);
+  if (threadIdx.x == 0) {
+    tok_out[r] = tok;
+    lp_out[r] = (bf16_to_f(lrow[tok]) - mx) - lse;
+  }
+}
+
+// ---- CandidateGroup step ----------------------------------------------------
+// CTA r samples local row r of the group (aios/ime.py:998-1037); the last CTA
+// to finish runs the step's host-free epilogue: compaction of finished rows,
+// FIFO slot allocation in active-row order (aios/scheduler/cache.py:46-51),
+// page-table writes (aios/ime.py:1229) and the next forward's metadata.
+__global__ void __launch_bounds__(kSampThreads) group_step_kernel(aiosb_group_ptrs g) {
+  extern __shared__ uint8_t smem_raw[];
+  RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
+  float* row = reinterpret_cast<float*>(smem_raw + sizeof(RowSmem));
+  pdl_wait();
+  aiosb_group_state* st = g.state;
+  const int r = blockIdx.x;
+  const int step = st->step;
+  const int V = st->vocab;
+  const int S = st->max_steps;
+  const bool run = st->done == 0 && g.active[r] != 0;
+  if (run) {
+    const __nv_bfloat16* lrow = reinterpret_cast<const __nv_bfloat16*>(g.logits) + (int64_t)r * V;
+    float mx, lse;
+    load_row(s, row, lrow, V, mx, lse);
+    if (step < st->min_new_tokens) apply_forbidden(row, V, g.minlen_ids, st->n_minlen);
+    // Refill exact-repeat bans (aios/ime.py:974-996): for every banned sequence
+    // b, ban its token at `step` if this row's output so far equals its prefix,
+    // otherwise ban the pad id (the reference fills non-matching slots with pad).
+    if (st->n_banned > 0 && step >= st->ban_min_prefix && step < st->banned_width) {
+      for (int b = threadIdx.x; b < st->n_banned; b += blockDim.x) {
+        const int32_t* seq = g.banned + (int64_t)b * st->banned_width;
+        bool match = g.banned_len[b] > step;
+        for (int t = 0; t < step && match; ++t) match = g.output_ids[(int64_t)r * S + t] == seq[t];
+        const int id = match ? seq[step] : st->pad_id;
+        if (id >= 0 && id < V) row[id] = -INFINITY;
+      }
+    }
+    __syncthreads();
+    SampleParams p;
+    p.temperature = st->temperature;
+    p.top_k = st->top_k;
+    p.top_p = st->top_p;
+    p.greedy = st->greedy;
+    const float u = g.uniforms[(int64_t)r * S + step];
+    const int tok = sample_row(s, row, V, p, u);
+    if (threadIdx.x == 0) {
+      const float lp = (bf16_to_f(lrow[tok]) - mx) - lse;
+      const bool eos = tok == st->eos_id;
+      const bool emitted = !eos;
+      g.output_ids[(int64_t)r * S + step] = emitted ? tok : st->pad_id;
+      g.counts[r] += emitted ? 1 : 0;
+      g.logprob_sums[r] += emitted ? lp : 0.f;
+      g.token_logprobs[(int64_t)r * S + step] = emitted ? lp : 0.f;
+      bool terminal = false;
+      for (int j = 0; j < st->n_terminal; ++j) terminal |= emitted && tok == g.terminal_ids[j];
+      if (eos) g.stop_codes[r] = 1;
+      if (terminal) g.stop_codes[r] = 2;
+      g.finished[r] = (eos || terminal) ? 1 : 0;
+      g.tokens[r] = tok;
+    }
+  }
+  // ---- last CTA: step epilogue.
+  __syncthreads();
+  __shared__ int is_last;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(&st->arrive, 1);
+    is_last = prev == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!is_last || threadIdx.x != 0) return;
+  __threadfence();
+  st->arrive = 0;
+  if (st->done) return;
+  const int R = st->rows;
+  const bool cancel = g.cancel_flag != nullptr && *reinterpret_cast<volatile const int32_t*>(g.cancel_flag) != 0;
+  int n = 0;
+  for (int i = 0; i < R; ++i) {
+    if (g.active[i] && g.finished[i]) g.active[i] = 0;
+    n += g.active[i] != 0;
+  }
+  bool done = step + 1 >= S || n == 0 || cancel;
+  if (!done) {
+    const int pos = st->prefix_len + step;  // position of the token sampled now
+    const int P = st->page_size;
+    const bool new_page = P <= 1 || (step % P) == 0;
+    int64_t k = 0;
+    const int64_t need = new_page ? n : 0;
+    if (st->head + need > st->tail) {
+      report(g.status, AIOSB_DEV_POOL_EMPTY);
+      done = true;
+    } else {
+      for (int i = 0; i < R; ++i) {
+        if (!g.active[i]) continue;
+        int64_t slot;
+        if (P <= 1) {
+          slot = g.ring[(st->head + k) % st->capacity];
+          ++k;
+        } else {
+          if (new_page) {
+            g.row_page[i] = g.ring[(st->head + k) % st->capacity];
+            ++k;
+          }
+          slot = (int64_t)g.row_page[i] * P + (step % P);
+        }
+        g.page_table[(int64_t)(st->row_offset + i) * st->table_stride + pos] = (int32_t)slot;
+        g.out_loc[i] = (int32_t)slot;
+        g.positions[i] = pos;
+        g.seq_lens[i] = pos + 1;
+      }
+      st->head += k;
+      st->active_model_tokens += n;
+      st->n_active = n;
+      st->step = step + 1;
+    }
+  }
+  if (done) {
+    st->done = 1;
+    st->cancelled = cancel ? 1 : 0;
+    for (int i = 0; i < R; ++i) g.active[i] = 0;
+    st->n_active = 0;
+  }
+  if (g.host_mirror != nullptr) {
+    volatile int32_t* m = g.host_mirror;
+    m[1] = st->done;
+    m[2] = st->cancelled;
+    m[3] = st->n_active;
+    __threadfence_system();
+    m[0] = step + 1;  // steps sampled so far; written last
+    __threadfence_system();
+  }
+}
+
+// ---- round start: reset per-row outputs, broadcast prefix logits, draw the
+// stateless uniform streams (aios/engine/sample.py:12-45).
+__device__ __forceinline__ float splitmix_uniform(uint64_t seed, uint64_t step) {
+  uint64_t v = seed + (step + 1ull) * 0x9E3779B97F4A7C15ull;
+  v = (v ^ (v >> 30)) * 0xBF58476D1CE4E5B9ull;
+  v = (v ^ (v >> 27)) * 0x94D049BB133111EBull;
+  v ^= v >> 31;
+  const double d = ((double)((v >> 11) & ((1ull << 53) - 1ull)) + 0.5) / 9007199254740992.0;
+  return __double2float_rn(d);
+}
+
+__global__ void group_begin_kernel(aiosb_group_ptrs g, const __nv_bfloat16* __restrict__ prefix_logits,
+                                   uint64_t seed_base, int attempts) {
+  pdl_wait();
+  aiosb_group_state* st = g.state;
+  const int R = st->rows, S = st->max_steps, V = st->vocab;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nthr = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = tid; i < (int64_t)R * V; i += nthr) reinterpret_cast<__nv_bfloat16*>(g.logits)[i] = prefix_logits[i % V];
+  for (int64_t i = tid; i < (int64_t)R * S; i += nthr) {
+    const int r = (int)(i / S), t = (int)(i % S);
+    g.uniforms[i] = splitmix_uniform(seed_base + (uint64_t)r, (uint64_t)t);
+    g.output_ids[i] = st->pad_id;
+    g.token_logprobs[i] = 0.f;
+  }
+  for (int64_t i = tid; i < R; i += nthr) {
+    g.counts[i] = 0;
+    g.logprob_sums[i] = 0.f;
+    g.stop_codes[i] = 0;
+    g.finished[i] = 0;
+    g.active[i] = i < attempts ? 1 : 0;
+    g.row_page[i] = -1;
+    g.out_loc[i] = -1;
+  }
+}
+
+__global__ void uniforms_kernel(const int64_t* __restrict__ seeds, int64_t rows, int64_t steps,
+                                float* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * steps) return;
+  out[i] = splitmix_uniform((uint64_t)seeds[i / steps], (uint64_t)(i % steps));
+}
+
+// ---- free-slot FIFO (aios/scheduler/cache.py:9-51) on a ring of `capacity`
+// int32 entries; head/tail are monotonically increasing logical indices.
+__global__ void slot_alloc_kernel(const int32_t* __restrict__ ring, int64_t capacity, int64_t head, int64_t n,
+                                  int32_t* __restrict__ out) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = ring[(head + i) % capacity];
+}
+
+__global__ void slot_free_kernel(int32_t* __restrict__ ring, int64_t capacity, int64_t tail,
+                                 const int32_t* __restrict__ slots, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    ring[(tail + i) % capacity] = slots[i];
+}
+
+// Appends ring[begin .. begin+n) at the tail. Source and destination may
+// overlap modulo the capacity; one CTA reads each 4096-entry chunk completely
+// before writing it, and chunks run in increasing order, which never
+// overwrites an entry that is still to be read.
+constexpr int kFreeChunk = 4096;
+__global__ void __launch_bounds__(1024) slot_free_range_kernel(int32_t* ring, int64_t capacity, int64_t begin,
+                                                               int64_t n, int64_t tail) {
+  for (int64_t c0 = 0; c0 < n; c0 += kFreeChunk) {
+    int32_t v[kFreeChunk / 1024];
+#pragma unroll
+    for (int j = 0; j < kFreeChunk / 1024; ++j) {
+      const int64_t i = c0 + j * 1024 + threadIdx.x;
+      v[j] = i < n ? ring[(begin + i) % capacity] : 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kFreeChunk / 1024; ++j) {
+      const int64_t i = c0 + j * 1024 + threadIdx.x;
+      if (i < n) ring[(tail + i) % capacity] = v[j];
+    }
+    __syncthreads();
+  }
+}
+
+size_t sample_smem(int V) { return sizeof(RowSmem) + (size_t)V * sizeof(float); }
+
+}  // namespace
+}  // namespace aiosb
+
+using namespace aiosb;
+
+extern "C" int aiosb_sample(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride, float temperature,
+                            int64_t top_k, float top_p, int greedy, const float* uniforms, const int32_t* forbidden,
+                            int64_t n_forbidden, const int64_t* forbidden_rows, int64_t n_forbidden_rows,
+                            int64_t* token_out, float* logprob_out, int32_t* status, void* stream) {
+  AIOSB_REQUIRE(rows >= 0 && vocab > 0 && vocab <= kMaxVocab && row_stride >= vocab, AIOSB_ERR_INVALID_ARG,
+                "sample: bad sizes (vocab must be in [1, %d])", kMaxVocab);
+  AIOSB_REQUIRE(greedy || temperature > 0.f, AIOSB_ERR_INVALID_ARG, "sample: temperature must be positive");
+  if (!greedy) {
+    const int64_t k = top_k > 0 ? std::min<int64_t>(top_k, vocab) : (top_p < 1.0f ? vocab : 0);
+    AIOSB_REQUIRE(k <= kMaxSortK, AIOSB_ERR_UNSUPPORTED,
+                  "sample: top-k/top-p candidate set of %lld exceeds the %d-entry sort", (long long)k, kMaxSortK);
+  }
+  if (rows == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(logits && token_out && logprob_out, AIOSB_ERR_INVALID_ARG, "sample: null pointer");
+  SampleParams p;
+  p.temperature = temperature;
+  p.top_k = (int)top_k;
+  p.top_p = top_p;
+  p.greedy = greedy;
+  const size_t smem = sample_smem((int)vocab);
+  cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem(kMaxVocab));
+  cudaError_t e = launch_pdl(sample_kernel, dim3((unsigned)rows), dim3(kSampThreads), smem, as_stream(stream),
+                             (const __nv_bfloat16*)logits, row_stride, (int)vocab, p, uniforms, forbidden,
+                             (int)n_forbidden, forbidden_rows, (int)n_forbidden_rows, token_out, logprob_out, status);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "sample: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_group_begin(const aiosb_group_ptrs* g, const void* prefix_logits, uint64_t seed_base,
+                                 int64_t attempts, int64_t rows, void* stream) {
+  AIOSB_REQUIRE(g && g->state && prefix_logits, AIOSB_ERR_INVALID_ARG, "group_begin: null pointer");
+  AIOSB_REQUIRE(attempts >= 1 && attempts <= rows, AIOSB_ERR_INVALID_ARG, "group_begin: attempts outside [1, rows]");
+  cudaError_t e = launch_pdl(group_begin_kernel, dim3(64), dim3(256), 0, as_stream(stream), *g,
+                             (const __nv_bfloat16*)prefix_logits, seed_base, (int)attempts);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_begin: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t vocab, int64_t top_k_max,
+                                void* stream) {
+  AIOSB_REQUIRE(g && g->state, AIOSB_ERR_INVALID_ARG, "group_step: null pointer");
+  AIOSB_REQUIRE(rows >= 1 && vocab > 0 && vocab <= kMaxVocab, AIOSB_ERR_INVALID_ARG,
+                "group_step: rows >= 1 and vocab in [1, %d]", kMaxVocab);
+  AIOSB_REQUIRE(top_k_max <= kMaxSortK, AIOSB_ERR_UNSUPPORTED, "group_step: top_k above %d", kMaxSortK);
+  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem(kMaxVocab));
+  cudaError_t e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads), sample_smem((int)vocab),
+                             as_stream(stream), *g);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_stateless_uniforms(const int64_t* seeds, int64_t rows, int64_t steps, float* out, void* stream) {
+  AIOSB_REQUIRE(rows >= 0 && steps >= 1, AIOSB_ERR_INVALID_ARG, "steps must be positive");
+  if (rows == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(seeds && out, AIOSB_ERR_INVALID_ARG, "stateless_uniforms: null pointer");
+  const int64_t n = rows * steps;
+  uniforms_kernel<<<(unsigned)((n + 255) / 256), 256, 0, as_stream(stream)>>>(seeds, rows, steps, out);
+  return check_launch("stateless_uniforms");
+}
+
+extern "C" int aiosb_slot_alloc(const int32_t* ring, int64_t capacity, int64_t head, int64_t n, int32_t* out,
+                                void* stream) {
+  AIOSB_REQUIRE(capacity > 0 && n >= 0 && n <= capacity && head >= 0, AIOSB_ERR_INVALID_ARG, "slot_alloc: bad sizes");
+  if (n == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(ring && out, AIOSB_ERR_INVALID_ARG, "slot_alloc: null pointer");
+  slot_alloc_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 1024), 256, 0, as_stream(stream)>>>(
+      ring, capacity, head, n, out);
+  return check_launch("slot_alloc");
+}
+
+extern "C" int aiosb_slot_free(int32_t* ring, int64_t capacity, int64_t tail, const int32_t* slots, int64_t n,
+                               void* stream) {
+  AIOSB_REQUIRE(capacity > 0 && n >= 0 && n <= capacity && tail >= 0, AIOSB_ERR_INVALID_ARG, "slot_free: bad sizes");
+  if (n == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(ring && slots, AIOSB_ERR_INVALID_ARG, "slot_free: null pointer");
+  slot_free_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 1024), 256, 0, as_stream(stream)>>>(
+      ring, capacity, tail, slots, n);
+  return check_launch("slot_free");
+}
+
+extern "C" int aiosb_slot_free_range(int32_t* ring, int64_t capacity, int64_t begin, int64_t n, int64_t tail,
+                                     void* stream) {
+  AIOSB_REQUIRE(capacity > 0 && n >= 0 && n <= capacity && begin >= 0 && tail >= 0, AIOSB_ERR_INVALID_ARG,
+                "slot_free_range: bad sizes");
+  if (n == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(ring, AIOSB_ERR_INVALID_ARG, "slot_free_range: null pointer");
+  slot_free_range_kernel<<<1, 1024, 0, as_stream(stream)>>>(ring, capacity, begin, n, tail);
+  return check_launch("slot_free_range");
+}

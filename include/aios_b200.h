@@ -1,0 +1,284 @@
+/*
+ * aios_b200 — C ABI of the B200-native (sm_100a) CandidateGroup hot path.
+ *
+ * Every entry point takes plain device pointers, element counts and strides,
+ * plus the caller's CUDA stream as `void*` (a cudaStream_t; NULL is the legacy
+ * default stream). No torch type crosses this boundary.
+ *
+ * Ownership: all buffers are owned by the caller. The library never allocates or
+ *   frees device memory; it launches kernels on the given stream and returns.
+ * Errors: every call returns 0 (AIOSB_OK) or a negative AIOSB_ERR_* code before
+ *   launching anything; aiosb_last_error() gives the message of the calling
+ *   thread's last failure. Kernels never trap: faults that can only be seen on
+ *   the device (a slot index outside the pool, an exhausted free list, a bounded
+ *   wait that ran out) are written as an AIOSB_DEV_* code into the caller's int32
+ *   status word (first error wins) and the kernel returns.
+ * Threading: stateless apart from the per-thread error message; calls may come
+ *   from any host thread as long as the caller orders them on its stream.
+ *
+ * Each entry point names the reference interface it replaces
+ * (paths inside the 7155/aios repository).
+ */
+#ifndef AIOS_B200_H_
+#define AIOS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define AIOSB_API __attribute__((visibility("default")))
+#else
+#define AIOSB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes ------------------------------------------------------- */
+#define AIOSB_OK 0
+#define AIOSB_ERR_INVALID_ARG -1 /* shape, size or pointer argument rejected      */
+#define AIOSB_ERR_UNSUPPORTED -2 /* dims this build has no kernel for             */
+#define AIOSB_ERR_MISALIGNED -3  /* pointer or stride breaks a 16-byte rule        */
+#define AIOSB_ERR_LAUNCH -4      /* cudaLaunch* or driver call failed              */
+
+/* ---- device status codes (written into the caller's status word) -------- */
+#define AIOSB_DEV_WAIT_TIMEOUT 1  /* a bounded mbarrier / flag wait ran out        */
+#define AIOSB_DEV_SLOT_RANGE 2    /* KV slot index outside [0, num_slots)          */
+#define AIOSB_DEV_TOKEN_RANGE 3   /* token id outside [0, vocab)                    */
+#define AIOSB_DEV_POOL_EMPTY 4    /* free-slot FIFO had fewer entries than asked    */
+#define AIOSB_DEV_POSITION_RANGE 5 /* RoPE position outside the cos/sin table      */
+
+/* GEMM epilogues for aiosb_linear. */
+#define AIOSB_EPI_STORE 0    /* y = x W^T, bf16                                         */
+#define AIOSB_EPI_SILU_MUL 1 /* W rows interleaved in 64-row gate/up blocks;
+                                y[:, f] = silu(x Wg^T) * (x Wu^T), bf16              */
+
+/* Library version (major*10000 + minor*100 + patch). */
+AIOSB_API int aiosb_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated to
+ * len) and returns its AIOSB_ERR_* code (0 if none). */
+AIOSB_API int aiosb_last_error(char* buf, size_t len);
+
+/* ---- KV cache scatter ----------------------------------------------------
+ * Replaces aios/kernel/store.py:32-61 (store_cache) as called by
+ * aios/kvcache/mha_pool.py:45-56 (MHAKVCache.store_kv).
+ * k_cache[indices[t], :] = k[t, :]; v_cache[indices[t], :] = v[t, :] for
+ * t < num_tokens, over `width` = num_kv_heads * head_dim bf16 elements.
+ * Strides are in elements. Indices outside [0, num_slots) are skipped and
+ * reported as AIOSB_DEV_SLOT_RANGE. */
+AIOSB_API int aiosb_kv_store(void* k_cache, void* v_cache, int64_t cache_token_stride, int64_t num_slots,
+                   const int32_t* indices, int64_t num_tokens, const void* k, int64_t k_token_stride,
+                   const void* v, int64_t v_token_stride, int64_t width, int32_t* status, void* stream);
+
+/* ---- Block AttnRes depth mixer -------------------------------------------
+ * Replaces aios/kernel/attnres.py:130-223 (triton_attnres_mix: the two Triton
+ * kernels _attnres_score_kernel 8-57 and _attnres_value_kernel 60-127) in one
+ * kernel. bank: [sources, tokens, hidden] bf16 contiguous; partial: [tokens,
+ * hidden] bf16 or NULL; weighted_query: [hidden] fp32; out: [tokens, hidden] bf16.
+ * score = (x . wq) * rsqrt(mean(x^2) + eps) in fp32, softmax over depth in
+ * fp32, weights rounded to bf16, out = sum_s w_s x_s accumulated in fp32.
+ * hidden must be a multiple of 8; sources + (partial != NULL) <= 16. */
+AIOSB_API int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t tokens, int64_t hidden, const void* partial,
+                      const float* weighted_query, float eps, void* out, void* stream);
+
+/* ---- RMSNorm ---------------------------------------------------------------
+ * Replaces aios/layers/norm.py:10-22 (RMSNorm.forward / forward_inplace, the
+ * FlashInfer rmsnorm). Normalises rows of `hidden` elements:
+ * out = x * rsqrt(mean(x^2) + eps) * weight, fp32 math, bf16 in/out.
+ * Row r lives at x + (r / heads_per_token) * token_stride + (r % heads_per_token)
+ * * hidden (the same for out with out_token_stride), so per-head q/k norms of a
+ * packed qkv row are one call. out may equal x. */
+AIOSB_API int aiosb_rmsnorm(const void* x, int64_t rows, int64_t hidden, int64_t heads_per_token, int64_t token_stride,
+                  const void* weight, float eps, void* out, int64_t out_token_stride, void* stream);
+
+/* Replaces aios/layers/norm.py:25-39 (RMSNormFused with a residual, the
+ * FlashInfer fused_add_rmsnorm): residual = x + residual (bf16 store), then
+ * x = rmsnorm(fp32 sum) * weight, in place on [rows, hidden] contiguous rows. */
+AIOSB_API int aiosb_add_rmsnorm(void* x, void* residual, int64_t rows, int64_t hidden, const void* weight, float eps,
+                      void* stream);
+
+/* ---- SwiGLU ----------------------------------------------------------------
+ * Replaces aios/layers/activation.py:9-12 (silu_and_mul): out[r, f] =
+ * silu(x[r, f]) * x[r, F + f], fp32 math, bf16 in/out; x is [rows, 2F]. */
+AIOSB_API int aiosb_silu_mul(const void* x, int64_t rows, int64_t f, void* out, void* stream);
+
+/* ---- Embedding gather ------------------------------------------------------
+ * Replaces aios/layers/embedding.py:17-18 (Embedding.forward). ids are int64
+ * (ids_is_int64 != 0) or int32; out[t] = weight[ids[t]]. Out-of-range ids write
+ * zeros and report AIOSB_DEV_TOKEN_RANGE. */
+AIOSB_API int aiosb_embedding(const void* ids, int ids_is_int64, int64_t num_tokens, const void* weight, int64_t vocab,
+                    int64_t hidden, void* out, int32_t* status, void* stream);
+
+/* ---- Linear (tcgen05 tensor-core GEMM) -------------------------------------
+ * Replaces the cuBLAS GEMMs behind aios/layers/linear.py:16-17 (Linear.forward)
+ * and aios/layers/embedding.py:34-41 (LMHead.forward): y = x W^T.
+ * x: [rows, k] bf16 row-major, row stride k; w: [n, k] bf16 row-major;
+ * y: [rows, y_cols] bf16 with row stride y_row_stride, where y_cols = n
+ * (AIOSB_EPI_STORE) or n/2 (AIOSB_EPI_SILU_MUL, w rows packed as
+ * [gate 0..63 | up 0..63 | gate 64..127 | up 64..127 | ...]).
+ * Requires n % 128 == 0, k % 64 == 0, 16-byte aligned x/w/y. */
+AIOSB_API int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
+                 int64_t y_row_stride, int epilogue, int32_t* status, void* stream);
+
+/* ---- Attention ---------------------------------------------------------------
+ * KV slots: token slot s of one layer lives at k_cache + s * num_kv_heads *
+ * head_dim (the MHAKVCache layout [pages, page_size, Hkv, d] flattened); slot
+ * lists come from the page table [rows, table_stride] int32. head_dim in
+ * {64, 96, 128}.
+ *
+ * Decode replaces aios/attention/flashinfer.py:374-394 (FlashInferAttentionBackend
+ * ._decode + plan) and, when qkv != NULL, also the q/k RMSNorm + bf16 RoPE of
+ * aios/models/qwen3.py:60-70 and the KV store of the new token
+ * (aios/kernel/store.py:32-61). Cascade: keys [0, *prefix_len) are read from
+ * page_table row row_table[0] once per KV head for every row (the candidate rows
+ * of a group share their prefix slots); keys [*prefix_len, seq_lens[r]) come from
+ * row row_table[r]. Pass either qkv (raw projection [rows, qkv_stride]: q | k | v
+ * heads) or q (already normalised and rotated [rows, q_stride]). Rows with
+ * active[r] == 0 are skipped (output zeros, no store); active may be NULL.
+ * rows * (num_qo_heads / num_kv_heads) <= 64. out: [rows, out_stride] bf16. */
+AIOSB_API int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const void* q, int64_t q_stride,
+                           const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_tab,
+                           const void* sin_tab, int64_t max_pos, const int32_t* positions, const int32_t* out_loc,
+                           void* k_cache, void* v_cache, int64_t num_slots, const int32_t* page_table,
+                           int64_t table_stride, const int32_t* row_table, const int32_t* seq_lens,
+                           const int32_t* prefix_len, const int32_t* active, int64_t rows, int64_t num_qo_heads,
+                           int64_t num_kv_heads, int64_t head_dim, float scale, void* out, int64_t out_stride,
+                           int32_t* status, void* stream);
+
+/* Prefill prologue: replaces the q/k RMSNorm (aios/models/qwen3.py:66-67),
+ * apply_rotary_pos_emb (aios/layers/attention.py:11-16) and store_kv
+ * (aios/attention/flashinfer.py:312) of a prefill batch. q heads are written,
+ * normalised and rotated, to q_out; k (normalised, rotated) and v go to the
+ * cache slots out_loc[t]. cos_tab/sin_tab: [max_pos, head_dim] bf16. */
+AIOSB_API int aiosb_qk_norm_rope_store(const void* qkv, int64_t qkv_stride, int64_t tokens, int64_t num_qo_heads,
+                             int64_t num_kv_heads, int64_t head_dim, const void* q_norm_w, const void* k_norm_w,
+                             float eps, const void* cos_tab, const void* sin_tab, int64_t max_pos,
+                             const int32_t* positions, const int32_t* out_loc, void* k_cache, void* v_cache,
+                             int64_t num_slots, void* q_out, int64_t q_out_stride, int32_t* status, void* stream);
+
+/* Tokens per prefill query tile for this head grouping (0 if unsupported). */
+AIOSB_API int aiosb_prefill_tile_tokens(int64_t num_qo_heads, int64_t num_kv_heads);
+
+/* Prefill attention: replaces the paged prefill of aios/attention/flashinfer.py:
+ * 300-326 and _sdpa_prefill_attention (33-91): causal attention of each
+ * request's new tokens over its slot list, query i at absolute position
+ * cached_len + i. Requests: q rows [q_start, q_start + q_len) of q, keys from
+ * page_table row table_row. The grid is a list of tiles (request, first query
+ * token) of tile_tokens tokens each. */
+AIOSB_API int aiosb_attention_prefill(const void* q, int64_t q_stride, const void* k_cache, const void* v_cache,
+                            int64_t num_slots, const int32_t* page_table, int64_t table_stride,
+                            const int32_t* req_q_start, const int32_t* req_q_len, const int32_t* req_cached_len,
+                            const int32_t* req_table_row, const int32_t* tile_req, const int32_t* tile_q0,
+                            int64_t num_tiles, int64_t tile_tokens, int64_t num_qo_heads, int64_t num_kv_heads,
+                            int64_t head_dim, float scale, void* out, int64_t out_stride, int32_t* status,
+                            void* stream);
+
+/* ---- Sampler -----------------------------------------------------------------
+ * Replaces aios/engine/sample.py:54-163 (Sampler.sample_with_logprobs with
+ * uniforms): per row, raw log-softmax of the bf16 logits, forbidden ids (the
+ * shared list and row-specific int64 [rows, n_forbidden_rows]) set to -inf on the
+ * sampling copy, then greedy argmax or temperature / top-k / top-p inverse-CDF
+ * sampling with uniforms[r]. Ties between equal logits order by ascending token
+ * id. Outputs token ids (int64) and raw log-probabilities (fp32).
+ * vocab <= 32768; the sorted candidate set (top_k, or the whole vocabulary for a
+ * top-p-only sampler) must not exceed 2048 entries. */
+AIOSB_API int aiosb_sample(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride, float temperature,
+                 int64_t top_k, float top_p, int greedy, const float* uniforms, const int32_t* forbidden,
+                 int64_t n_forbidden, const int64_t* forbidden_rows, int64_t n_forbidden_rows, int64_t* token_out,
+                 float* logprob_out, int32_t* status, void* stream);
+
+/* Replaces stateless_uniforms (aios/engine/sample.py:12-45): out[r, t] is the
+ * splitmix64 uniform of (seeds[r], t), computed in fp64 and rounded to fp32. */
+AIOSB_API int aiosb_stateless_uniforms(const int64_t* seeds, int64_t rows, int64_t steps, float* out, void* stream);
+
+/* ---- Free-slot FIFO ----------------------------------------------------------
+ * Replaces CacheManager.allocate / _free (aios/scheduler/cache.py:16-18,46-51):
+ * the free list is a device ring of `capacity` int32 slot (or page) ids with
+ * logical head/tail counters kept by the caller; allocate takes the first n
+ * entries, free appends at the tail, so the order is the reference's FIFO order.
+ * slot_free copies from a separate array; slot_free_range appends ring entries
+ * [begin, begin + n) (already allocated: begin + n <= head <= tail). */
+AIOSB_API int aiosb_slot_alloc(const int32_t* ring, int64_t capacity, int64_t head, int64_t n, int32_t* out, void* stream);
+AIOSB_API int aiosb_slot_free(int32_t* ring, int64_t capacity, int64_t tail, const int32_t* slots, int64_t n, void* stream);
+AIOSB_API int aiosb_slot_free_range(int32_t* ring, int64_t capacity, int64_t begin, int64_t n, int64_t tail, void* stream);
+
+/* ---- CandidateGroup step -----------------------------------------------------
+ * Device state of one branch batch (aios/ime.py:891-1054), written by the host
+ * at round start and advanced by aiosb_group_step. */
+typedef struct aiosb_group_state {
+  int32_t step;            /* next step to sample                                   */
+  int32_t max_steps;       /* max_new_tokens; row stride of the [rows, steps] arrays */
+  int32_t min_new_tokens;  /* EOS/terminal ids banned while step < this             */
+  int32_t prefix_len;      /* tokens of the shared prefix                           */
+  int32_t row_offset;      /* first page-table row of this batch                    */
+  int32_t rows;            /* local rows (attempts)                                 */
+  int32_t vocab;
+  int32_t eos_id;
+  int32_t pad_id;
+  int32_t greedy;
+  int32_t top_k;
+  float temperature;
+  float top_p;
+  int32_t page_size;       /* 1 or 16                                               */
+  int32_t n_terminal;      /* terminal punctuation ids (stop code 2)                */
+  int32_t n_minlen;        /* ids banned before min_new_tokens                      */
+  int32_t n_banned;        /* refill exact-repeat sequences                         */
+  int32_t banned_width;
+  int32_t ban_min_prefix;  /* refill_ban_min_prefix_tokens                          */
+  int32_t done;
+  int32_t cancelled;
+  int32_t n_active;
+  int32_t active_model_tokens;
+  int32_t arrive;          /* last-CTA counter, 0 between launches                  */
+  int64_t head;            /* free-slot FIFO logical head / tail / ring capacity    */
+  int64_t tail;
+  int64_t capacity;
+  int64_t table_stride;    /* page-table row stride (elements)                      */
+} aiosb_group_state;
+
+typedef struct aiosb_group_ptrs {
+  aiosb_group_state* state;
+  const int32_t* cancel_flag; /* host-mapped word set by the canceller, or NULL    */
+  int32_t* host_mirror;       /* host-mapped [steps_done, done, cancelled, n_active] */
+  void* logits;               /* [rows, vocab] bf16: next step's logits            */
+  float* uniforms;            /* [rows, max_steps]                                  */
+  int32_t* output_ids;        /* [rows, max_steps]                                  */
+  float* token_logprobs;      /* [rows, max_steps]                                  */
+  int32_t* counts;            /* [rows]                                             */
+  float* logprob_sums;        /* [rows]                                             */
+  int32_t* stop_codes;        /* [rows] 0 / 1 eos / 2 terminal                      */
+  int32_t* active;            /* [rows]                                             */
+  int32_t* finished;          /* [rows] scratch                                     */
+  int32_t* tokens;            /* [rows] decode input ids                            */
+  int32_t* positions;         /* [rows]                                             */
+  int32_t* seq_lens;          /* [rows]                                             */
+  int32_t* out_loc;           /* [rows] KV slot of the decode token                 */
+  int32_t* row_page;          /* [rows] current suffix page (page_size > 1)         */
+  const int32_t* terminal_ids;
+  const int32_t* minlen_ids;
+  const int32_t* banned;      /* [n_banned, banned_width]                           */
+  const int32_t* banned_len;  /* [n_banned]                                         */
+  int32_t* page_table;
+  const int32_t* ring;        /* free-slot FIFO                                     */
+  int32_t* status;
+} aiosb_group_ptrs;
+
+/* Round start: resets the per-row outputs, copies the prefix logits [vocab] into
+ * every row of `logits`, draws the uniform streams of seeds seed_base + r and
+ * marks rows [0, attempts) active. */
+AIOSB_API int aiosb_group_begin(const aiosb_group_ptrs* g, const void* prefix_logits, uint64_t seed_base, int64_t attempts,
+                      int64_t rows, void* stream);
+
+/* One sampling step of every active row plus the step epilogue (finished-row
+ * compaction, FIFO slot allocation in row order, page-table write, next forward's
+ * tokens/positions/seq_lens/out_loc). Reads everything it needs from device
+ * memory, so one captured launch serves every step of every round. */
+AIOSB_API int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t vocab, int64_t top_k_max, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AIOS_B200_H_ */
