@@ -311,9 +311,11 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, GemmArgs a, int m_
 
 // Split-K factor: the largest divisor of the K chunk count (<= 16) that keeps
 // the grid within one wave of CTAs.
+int g_max_split = kMaxSplit;  // lowered to 8 if 16-CTA clusters cannot launch
+
 int choose_split(int64_t tiles, int64_t chunks, int sms) {
   int best = 1;
-  for (int d = 2; d <= kMaxSplit; ++d)
+  for (int d = 2; d <= g_max_split; ++d)
     if (chunks % d == 0 && tiles * d <= sms) best = d;
   return best;
 }
@@ -357,11 +359,24 @@ extern "C" int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* 
   rc = make_map(&tx, x, rows, k, (uint32_t)bn);
   if (rc) return rc;
   cudaStream_t s = as_stream(stream);
-  switch (bn) {
-    case 16: return launch_gemm<16>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
-    case 32: return launch_gemm<32>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
-    case 64: return launch_gemm<64>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
-    case 128: return launch_gemm<128>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
-    default: return launch_gemm<256>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
+  auto launch = [&]() {
+    switch (bn) {
+      case 16: return launch_gemm<16>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
+      case 32: return launch_gemm<32>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
+      case 64: return launch_gemm<64>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
+      case 128: return launch_gemm<128>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
+      default: return launch_gemm<256>(tw, tx, a, (int)m_tiles, (int)n_tiles, s);
+    }
+  };
+  rc = launch();
+  if (rc != AIOSB_OK && a.split > 8) {
+    // Non-portable 16-CTA clusters are an opt-in; fall back to portable sizes.
+    (void)cudaGetLastError();
+    g_max_split = 8;
+    a.split = choose_split(m_tiles * n_tiles, chunks, sm_count());
+    a.chunks_per_split = (int)(chunks / a.split);
+    a.stages = std::min(a.chunks_per_split, max_stages_for(bn));
+    rc = launch();
   }
+  return rc;
 }

@@ -1,0 +1,548 @@
+"""Torch-tensor wrappers over the C ABI (``aios_b200._lib``).
+
+Each wrapper validates shapes/dtypes on the host, passes raw device addresses and
+the current CUDA stream, and never computes anything itself: every op here runs
+as a hand-written sm_100a kernel. Device-side errors land in a per-device int32
+status word that :func:`check_status` turns into a ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+_STATUS: dict[int, torch.Tensor] = {}
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """The per-device int32 status word that kernels report device faults into."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    st = _STATUS.get(index)
+    if st is None:
+        st = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+        _STATUS[index] = st
+    return st
+
+
+def check_status(device: torch.device, reset: bool = True) -> None:
+    """Raises if any kernel on `device` reported a device-side fault (syncs)."""
+    st = status_word(device)
+    code = int(st.item())
+    if code:
+        if reset:
+            st.zero_()
+        raise RuntimeError(f"aios_b200 device status {code}: {_lib.DEVICE_STATUS_NAMES.get(code, 'unknown')}")
+
+
+def _require_cuda(*tensors: torch.Tensor, what: str) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError(f"{what} requires CUDA tensors")
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+# ---------------------------------------------------------------------------
+# KV store (aios/kernel/store.py:32-61)
+# ---------------------------------------------------------------------------
+def store_cache(
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    indices: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+) -> None:
+    """Scatter a flat batch of K/V vectors into a contiguous CUDA cache."""
+    if k_cache.ndim != 3 or v_cache.ndim != 3:
+        raise ValueError("KV cache must have shape (num_slots, num_heads, head_dim)")
+    if k.shape[1:] != k_cache.shape[1:] or v.shape[1:] != v_cache.shape[1:]:
+        raise ValueError("K/V input shape does not match the cache layout")
+    if indices.numel() != k.shape[0] or k.shape != v.shape:
+        raise ValueError("KV write indices and K/V tensors must have matching token counts")
+    _require_cuda(k_cache, v_cache, indices, k, v, what="store_cache")
+    if k.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise ValueError("store_cache expects bf16 K/V and cache")
+    for name, t in (("k", k), ("v", v)):
+        if t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+            raise ValueError(f"{name} rows must be contiguous within a token")
+    if not (k_cache[0].is_contiguous() and v_cache[0].is_contiguous()):
+        raise ValueError("KV cache rows must be contiguous")
+    idx = indices.to(torch.int32).contiguous()
+    width = k_cache.shape[1] * k_cache.shape[2]
+    _lib.call(
+        "aiosb_kv_store",
+        k_cache.data_ptr(),
+        v_cache.data_ptr(),
+        k_cache.stride(0),
+        k_cache.shape[0],
+        idx.data_ptr(),
+        k.shape[0],
+        k.data_ptr(),
+        k.stride(0),
+        v.data_ptr(),
+        v.stride(0),
+        width,
+        status_word(k.device).data_ptr(),
+        _stream(k.device),
+    )
+
+
+# ---------------------------------------------------------------------------
+# AttnRes mixer (aios/kernel/attnres.py:130-223)
+# ---------------------------------------------------------------------------
+def b200_attnres_mix(
+    bank: torch.Tensor,
+    partial: torch.Tensor | None,
+    weighted_query: torch.Tensor,
+    eps: float,
+    *,
+    score_buffer: torch.Tensor | None = None,
+    output_buffer: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """FP32 depth routing and BF16 value aggregation in one sm_100a kernel.
+
+    Same signature and layout checks as the reference ``triton_attnres_mix``;
+    ``score_buffer`` is accepted and validated but unused, because the fused
+    kernel keeps the [S, N] scores in registers.
+    """
+    if not bank.is_cuda:
+        raise ValueError("B200 AttnRes requires CUDA tensors")
+    if bank.ndim != 3:
+        raise ValueError("bank must have shape [S,N,D]")
+    if not bank.is_contiguous():
+        raise ValueError("bank must be contiguous for the B200 pointer layout")
+    bank_sources, num_tokens, hidden_size = bank.shape
+    if bank_sources < 1 or num_tokens < 1 or hidden_size < 1:
+        raise ValueError("bank dimensions must be positive")
+    total_sources = bank_sources + int(partial is not None)
+    if partial is not None and partial.shape != bank.shape[1:]:
+        raise ValueError("partial must match bank [N,D]")
+    if partial is not None and not partial.is_contiguous():
+        raise ValueError("partial must be contiguous")
+    if weighted_query.shape != (hidden_size,):
+        raise ValueError("weighted_query must match hidden size")
+    if not weighted_query.is_contiguous():
+        raise ValueError("weighted_query must be contiguous")
+    if weighted_query.dtype != torch.float32:
+        raise ValueError("weighted_query must be float32")
+    if bank.dtype != torch.bfloat16 or (partial is not None and partial.dtype != torch.bfloat16):
+        raise ValueError("B200 AttnRes expects bf16 bank/partial")
+    if score_buffer is not None:
+        if score_buffer.dtype != torch.float32 or score_buffer.device != bank.device:
+            raise ValueError("score_buffer must be CUDA float32 on bank device")
+        if (
+            score_buffer.shape[0] < total_sources
+            or score_buffer.shape[1] != num_tokens
+            or not score_buffer.is_contiguous()
+        ):
+            raise ValueError("score_buffer must be contiguous [capacity_sources, num_tokens]")
+    if output_buffer is None:
+        output = torch.empty_like(bank[0])
+    else:
+        if output_buffer.shape != bank.shape[1:]:
+            raise ValueError("output_buffer must match bank [N,D]")
+        if output_buffer.dtype != bank.dtype or output_buffer.device != bank.device:
+            raise ValueError("output_buffer must match bank dtype/device")
+        if not output_buffer.is_contiguous():
+            raise ValueError("output_buffer must be contiguous")
+        output = output_buffer
+    _lib.call(
+        "aiosb_attnres_mix",
+        bank.data_ptr(),
+        bank_sources,
+        num_tokens,
+        hidden_size,
+        _ptr(partial),
+        weighted_query.data_ptr(),
+        float(eps),
+        output.data_ptr(),
+        _stream(bank.device),
+    )
+    return output
+
+
+# ---------------------------------------------------------------------------
+# Norms / activations / embedding (aios/layers/{norm,activation,embedding}.py)
+# ---------------------------------------------------------------------------
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm over the last dim of a 2-D [T, H] or 3-D [T, heads, d] view."""
+    _require_cuda(x, weight, what="rmsnorm")
+    if out is None:
+        out = torch.empty_like(x)
+    if x.ndim == 2:
+        x3, o3 = x.unsqueeze(1), out.unsqueeze(1)
+    elif x.ndim == 3:
+        x3, o3 = x, out
+    else:
+        raise ValueError("rmsnorm expects a 2-D or 3-D tensor")
+    hidden = x3.shape[2]
+    if weight.shape != (hidden,):
+        raise ValueError("rmsnorm weight must match the last dimension")
+    for t in (x3, o3):
+        if t.stride(2) != 1 or (t.shape[1] > 1 and t.stride(1) != hidden):
+            raise ValueError("rmsnorm rows must be dense within a token")
+    _lib.call(
+        "aiosb_rmsnorm",
+        x3.data_ptr(),
+        x3.shape[0] * x3.shape[1],
+        hidden,
+        x3.shape[1],
+        x3.stride(0),
+        weight.data_ptr(),
+        float(eps),
+        o3.data_ptr(),
+        o3.stride(0),
+        _stream(x.device),
+    )
+    return out
+
+
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float) -> None:
+    """residual += x; x = rmsnorm(residual) (in place, FlashInfer semantics)."""
+    _require_cuda(x, residual, weight, what="fused_add_rmsnorm")
+    if x.shape != residual.shape or x.ndim != 2 or not x.is_contiguous() or not residual.is_contiguous():
+        raise ValueError("fused_add_rmsnorm expects matching contiguous [T, H] tensors")
+    _lib.call(
+        "aiosb_add_rmsnorm",
+        x.data_ptr(),
+        residual.data_ptr(),
+        x.shape[0],
+        x.shape[1],
+        weight.data_ptr(),
+        float(eps),
+        _stream(x.device),
+    )
+
+
+def silu_and_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _require_cuda(x, what="silu_and_mul")
+    if x.ndim != 2 or x.shape[1] % 2 or not x.is_contiguous():
+        raise ValueError("silu_and_mul expects a contiguous [T, 2F] tensor")
+    f = x.shape[1] // 2
+    if out is None:
+        out = torch.empty((x.shape[0], f), dtype=x.dtype, device=x.device)
+    _lib.call("aiosb_silu_mul", x.data_ptr(), x.shape[0], f, out.data_ptr(), _stream(x.device))
+    return out
+
+
+def embedding(ids: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _require_cuda(ids, weight, what="embedding")
+    ids = ids.contiguous()
+    if ids.dtype not in (torch.int64, torch.int32):
+        raise ValueError("embedding ids must be int32 or int64")
+    if out is None:
+        out = torch.empty((ids.numel(), weight.shape[1]), dtype=weight.dtype, device=weight.device)
+    _lib.call(
+        "aiosb_embedding",
+        ids.data_ptr(),
+        int(ids.dtype == torch.int64),
+        ids.numel(),
+        weight.data_ptr(),
+        weight.shape[0],
+        weight.shape[1],
+        out.data_ptr(),
+        status_word(ids.device).data_ptr(),
+        _stream(ids.device),
+    )
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Linear (tcgen05 GEMM)
+# ---------------------------------------------------------------------------
+def linear(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    out: torch.Tensor | None = None,
+    epilogue: int = _lib.EPI_STORE,
+) -> torch.Tensor:
+    """y = x @ weight.T on the tensor cores (bf16 in, fp32 accumulate, bf16 out)."""
+    _require_cuda(x, weight, what="linear")
+    if x.ndim != 2 or weight.ndim != 2 or x.shape[1] != weight.shape[1]:
+        raise ValueError("linear expects x [T, K] and weight [N, K]")
+    if not x.is_contiguous() or not weight.is_contiguous():
+        raise ValueError("linear expects contiguous x and weight")
+    n = weight.shape[0]
+    cols = n if epilogue == _lib.EPI_STORE else n // 2
+    if out is None:
+        out = torch.empty((x.shape[0], cols), dtype=x.dtype, device=x.device)
+    if out.stride(1) != 1:
+        raise ValueError("linear output rows must be contiguous")
+    _lib.call(
+        "aiosb_linear",
+        x.data_ptr(),
+        x.shape[0],
+        x.shape[1],
+        weight.data_ptr(),
+        n,
+        out.data_ptr(),
+        out.stride(0),
+        epilogue,
+        status_word(x.device).data_ptr(),
+        _stream(x.device),
+    )
+    return out
+
+
+def pack_gate_up(weight: torch.Tensor) -> torch.Tensor:
+    """[gate | up] rows ([2F, K]) -> 64-row interleaved blocks for EPI_SILU_MUL."""
+    two_f, k = weight.shape
+    f = two_f // 2
+    if f % 64:
+        raise ValueError("gate/up width must be a multiple of 64")
+    gate = weight[:f].reshape(f // 64, 64, k)
+    up = weight[f:].reshape(f // 64, 64, k)
+    return torch.stack((gate, up), dim=1).reshape(two_f, k).contiguous()
+
+
+# ---------------------------------------------------------------------------
+# Attention
+# ---------------------------------------------------------------------------
+def attention_decode(
+    *,
+    out: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    page_table: torch.Tensor,
+    row_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    positions: torch.Tensor,
+    num_qo_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    scale: float,
+    qkv: torch.Tensor | None = None,
+    q: torch.Tensor | None = None,
+    q_norm_w: torch.Tensor | None = None,
+    k_norm_w: torch.Tensor | None = None,
+    eps: float = 1e-6,
+    cos: torch.Tensor | None = None,
+    sin: torch.Tensor | None = None,
+    out_loc: torch.Tensor | None = None,
+    prefix_len: torch.Tensor | None = None,
+    active: torch.Tensor | None = None,
+) -> torch.Tensor:
+    rows = out.shape[0]
+    num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    src = qkv if qkv is not None else q
+    _lib.call(
+        "aiosb_attention_decode",
+        _ptr(qkv),
+        qkv.stride(0) if qkv is not None else 0,
+        _ptr(q),
+        q.stride(0) if q is not None else 0,
+        _ptr(q_norm_w),
+        _ptr(k_norm_w),
+        float(eps),
+        _ptr(cos),
+        _ptr(sin),
+        cos.shape[0] if cos is not None else 0,
+        positions.data_ptr(),
+        _ptr(out_loc),
+        k_cache.data_ptr(),
+        v_cache.data_ptr(),
+        num_slots,
+        page_table.data_ptr(),
+        page_table.stride(0),
+        row_table.data_ptr(),
+        seq_lens.data_ptr(),
+        _ptr(prefix_len),
+        _ptr(active),
+        rows,
+        num_qo_heads,
+        num_kv_heads,
+        head_dim,
+        float(scale),
+        out.data_ptr(),
+        out.stride(0),
+        status_word(src.device).data_ptr(),
+        _stream(src.device),
+    )
+    return out
+
+
+def qk_norm_rope_store(
+    *,
+    qkv: torch.Tensor,
+    num_qo_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    q_norm_w: torch.Tensor,
+    k_norm_w: torch.Tensor,
+    eps: float,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    positions: torch.Tensor,
+    out_loc: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    q_out: torch.Tensor,
+) -> torch.Tensor:
+    num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    _lib.call(
+        "aiosb_qk_norm_rope_store",
+        qkv.data_ptr(),
+        qkv.stride(0),
+        qkv.shape[0],
+        num_qo_heads,
+        num_kv_heads,
+        head_dim,
+        q_norm_w.data_ptr(),
+        k_norm_w.data_ptr(),
+        float(eps),
+        cos.data_ptr(),
+        sin.data_ptr(),
+        cos.shape[0],
+        positions.data_ptr(),
+        out_loc.data_ptr(),
+        k_cache.data_ptr(),
+        v_cache.data_ptr(),
+        num_slots,
+        q_out.data_ptr(),
+        q_out.stride(0),
+        status_word(qkv.device).data_ptr(),
+        _stream(qkv.device),
+    )
+    return q_out
+
+
+def prefill_tile_tokens(num_qo_heads: int, num_kv_heads: int) -> int:
+    n = _lib.load().aiosb_prefill_tile_tokens(num_qo_heads, num_kv_heads)
+    if n <= 0:
+        raise ValueError("unsupported head grouping for prefill attention")
+    return n
+
+
+def attention_prefill(
+    *,
+    q: torch.Tensor,
+    out: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    page_table: torch.Tensor,
+    meta: torch.Tensor,
+    num_requests: int,
+    num_tiles: int,
+    tile_tokens: int,
+    num_qo_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    scale: float,
+) -> torch.Tensor:
+    """``meta`` is one int32 device tensor holding, back to back, the request
+    arrays q_start, q_len, cached_len, table_row ([num_requests] each) and the
+    tile arrays tile_req, tile_q0 ([num_tiles] each)."""
+    num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    base = meta.data_ptr()
+    r = num_requests * 4
+    _lib.call(
+        "aiosb_attention_prefill",
+        q.data_ptr(),
+        q.stride(0),
+        k_cache.data_ptr(),
+        v_cache.data_ptr(),
+        num_slots,
+        page_table.data_ptr(),
+        page_table.stride(0),
+        base,
+        base + r,
+        base + 2 * r,
+        base + 3 * r,
+        base + 4 * r,
+        base + 4 * r + num_tiles * 4,
+        num_tiles,
+        tile_tokens,
+        num_qo_heads,
+        num_kv_heads,
+        head_dim,
+        float(scale),
+        out.data_ptr(),
+        out.stride(0),
+        status_word(q.device).data_ptr(),
+        _stream(q.device),
+    )
+    return out
+
+
+def prefill_meta(
+    q_lens: list[int], cached_lens: list[int], table_rows: list[int], tile_tokens: int
+) -> tuple[list[int], int]:
+    """Host-side request/tile arrays for :func:`attention_prefill`."""
+    q_start, acc = [], 0
+    tile_req, tile_q0 = [], []
+    for i, n in enumerate(q_lens):
+        q_start.append(acc)
+        acc += n
+        for q0 in range(0, n, tile_tokens):
+            tile_req.append(i)
+            tile_q0.append(q0)
+    return [*q_start, *q_lens, *cached_lens, *table_rows, *tile_req, *tile_q0], len(tile_req)
+
+
+# ---------------------------------------------------------------------------
+# Sampler / uniforms / slot FIFO
+# ---------------------------------------------------------------------------
+def sample(
+    logits: torch.Tensor,
+    *,
+    temperature: float,
+    top_k: int,
+    top_p: float,
+    greedy: bool,
+    uniforms: torch.Tensor | None,
+    forbidden: torch.Tensor | None = None,
+    forbidden_rows: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    rows, vocab = logits.shape
+    dev = logits.device
+    tok = torch.empty((rows, 1), dtype=torch.int64, device=dev)
+    lp = torch.empty((rows, 1), dtype=torch.float32, device=dev)
+    _lib.call(
+        "aiosb_sample",
+        logits.data_ptr(),
+        rows,
+        vocab,
+        logits.stride(0),
+        float(temperature),
+        int(top_k),
+        float(top_p),
+        int(bool(greedy)),
+        _ptr(uniforms),
+        _ptr(forbidden),
+        0 if forbidden is None else forbidden.numel(),
+        _ptr(forbidden_rows),
+        0 if forbidden_rows is None else forbidden_rows.shape[1],
+        tok.data_ptr(),
+        lp.data_ptr(),
+        status_word(dev).data_ptr(),
+        _stream(dev),
+    )
+    return tok, lp
+
+
+def stateless_uniforms_device(seeds: torch.Tensor, steps: int) -> torch.Tensor:
+    out = torch.empty((seeds.numel(), steps), dtype=torch.float32, device=seeds.device)
+    _lib.call("aiosb_stateless_uniforms", seeds.data_ptr(), seeds.numel(), steps, out.data_ptr(), _stream(seeds.device))
+    return out
+
+
+def slot_alloc(ring: torch.Tensor, head: int, n: int) -> torch.Tensor:
+    out = torch.empty(n, dtype=torch.int32, device=ring.device)
+    _lib.call("aiosb_slot_alloc", ring.data_ptr(), ring.numel(), head, n, out.data_ptr(), _stream(ring.device))
+    return out
+
+
+def slot_free(ring: torch.Tensor, tail: int, slots: torch.Tensor) -> None:
+    slots = slots.to(torch.int32).contiguous()
+    _lib.call("aiosb_slot_free", ring.data_ptr(), ring.numel(), tail, slots.data_ptr(), slots.numel(), _stream(ring.device))
+
+
+def slot_free_range(ring: torch.Tensor, begin: int, n: int, tail: int) -> None:
+    _lib.call("aiosb_slot_free_range", ring.data_ptr(), ring.numel(), begin, n, tail, _stream(ring.device))

@@ -1,0 +1,317 @@
+"""Per-kernel parity on the GPU: every C-ABI kernel against the CPU oracle.
+
+Integer/index work (KV scatter, uniforms, slot FIFO, sampled token ids given the
+same logits) must match bit for bit; floating-point kernels compare against the
+oracle's fp32 math with the tolerance written in each test.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from aios_b200 import _lib
+from aios_b200.kernel import ops
+from oracle import ops as oops
+from oracle import sampler as osamp
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16_close(actual: torch.Tensor, expected: torch.Tensor, ulps: float = 2.0, atol: float = 1e-6) -> None:
+    """|a - e| <= ulps * bf16 spacing(|e|) + atol, elementwise."""
+    a, e = actual.float().cpu(), expected.float().cpu()
+    spacing = torch.clamp(e.abs(), min=2.0**-126) * 2.0**-7
+    bad = (a - e).abs() > ulps * spacing + atol
+    assert not bool(bad.any()), f"{int(bad.sum())} mismatches; max abs diff {float((a - e).abs().max())}"
+
+
+@pytest.mark.parametrize("rows", [1, 8, 13, 33, 100, 300])
+@pytest.mark.parametrize("n,k", [(1280, 768), (768, 768), (768, 2048), (1152, 768), (16384, 768)])
+def test_linear_tcgen05_matches_fp32(cuda_device, rows: int, n: int, k: int) -> None:
+    g = torch.Generator().manual_seed(rows * 7 + n + k)
+    x = torch.randn(rows, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    ref = x.float() @ w.float().T
+    y = ops.linear(x.to(cuda_device), w.to(cuda_device))
+    torch.cuda.synchronize()
+    ops.check_status(cuda_device)
+    # fp32 accumulation in a different order + one bf16 rounding: 1 ulp + tiny abs.
+    _bf16_close(y, ref, ulps=1.0, atol=1e-4 * math.sqrt(k))
+
+
+@pytest.mark.parametrize("rows", [1, 8, 33])
+def test_linear_silu_mul_epilogue(cuda_device, rows: int) -> None:
+    g = torch.Generator().manual_seed(5 + rows)
+    f, k = 2048, 768
+    x = torch.randn(rows, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(2 * f, k, generator=g) * 0.02).to(torch.bfloat16)
+    gate_up = (x.float() @ w.float().T).to(torch.bfloat16)  # reference rounds gate_up to bf16
+    ref = oops.silu_and_mul(gate_up)
+    y = ops.linear(x.to(cuda_device), ops.pack_gate_up(w.to(cuda_device)), epilogue=_lib.EPI_SILU_MUL)
+    torch.cuda.synchronize()
+    assert y.shape == (rows, f)
+    _bf16_close(y, ref, ulps=2.0, atol=1e-4)
+
+
+def test_rmsnorm_variants(cuda_device) -> None:
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(13, 768, generator=g).to(torch.bfloat16)
+    w = (1.0 + 0.1 * torch.randn(768, generator=g)).to(torch.bfloat16)
+    y = ops.rmsnorm(x.to(cuda_device), w.to(cuda_device), 1e-6)
+    _bf16_close(y, oops.rmsnorm(x, w, 1e-6), ulps=1.0)
+    # per-head view of a packed qkv row: [T, H, d] with token stride > H*d
+    qkv = torch.randn(5, 1280, generator=g).to(torch.bfloat16)
+    hw = (1.0 + 0.1 * torch.randn(64, generator=g)).to(torch.bfloat16)
+    qd = qkv.to(cuda_device)
+    view = qd[:, :768].view(5, 12, 64)
+    ops.rmsnorm(view, hw.to(cuda_device), 1e-6, out=view)
+    ref = oops.rmsnorm(qkv[:, :768].view(5, 12, 64), hw, 1e-6)
+    _bf16_close(qd[:, :768].view(5, 12, 64), ref, ulps=1.0)
+    assert torch.equal(qd[:, 768:].cpu(), qkv[:, 768:])  # untouched k/v part
+
+
+def test_fused_add_rmsnorm_and_silu(cuda_device) -> None:
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(9, 768, generator=g).to(torch.bfloat16)
+    r = torch.randn(9, 768, generator=g).to(torch.bfloat16)
+    w = (1.0 + 0.1 * torch.randn(768, generator=g)).to(torch.bfloat16)
+    xd, rd = x.to(cuda_device), r.to(cuda_device)
+    ops.fused_add_rmsnorm(xd, rd, w.to(cuda_device), 1e-6)
+    ex, er = oops.fused_add_rmsnorm(x, r, w, 1e-6)
+    assert torch.equal(rd.cpu(), er)  # residual sum rounds once: bit-exact
+    _bf16_close(xd, ex, ulps=1.0)
+    gu = torch.randn(7, 4096, generator=g).to(torch.bfloat16)
+    _bf16_close(ops.silu_and_mul(gu.to(cuda_device)), oops.silu_and_mul(gu), ulps=1.0)
+
+
+def test_embedding_and_kv_store_bit_exact(cuda_device) -> None:
+    g = torch.Generator().manual_seed(6)
+    table = torch.randn(100, 768, generator=g).to(torch.bfloat16)
+    ids = torch.tensor([5, 0, 99, 42], dtype=torch.int64)
+    out = ops.embedding(ids.to(cuda_device), table.to(cuda_device))
+    assert torch.equal(out.cpu(), table[ids])
+    # store_cache into a [slots, Hkv, d] cache from strided k/v views of qkv
+    slots, hkv, d = 64, 4, 64
+    kc = torch.zeros(slots, hkv, d, dtype=torch.bfloat16, device=cuda_device)
+    vc = torch.zeros_like(kc)
+    qkv = torch.randn(6, 1280, generator=g).to(torch.bfloat16).to(cuda_device)
+    k = qkv[:, 768:1024].view(6, hkv, d)
+    v = qkv[:, 1024:].view(6, hkv, d)
+    idx = torch.tensor([3, 60, 7, 0, 31, 12], dtype=torch.int32, device=cuda_device)
+    ops.store_cache(kc, vc, idx, k, v)
+    torch.cuda.synchronize()
+    ops.check_status(cuda_device)
+    assert torch.equal(kc[idx.long()].cpu(), k.cpu()) and torch.equal(vc[idx.long()].cpu(), v.cpu())
+    untouched = torch.ones(slots, dtype=torch.bool)
+    untouched[idx.long().cpu()] = False
+    assert int(kc.cpu()[untouched].abs().sum()) == 0
+
+
+@pytest.mark.parametrize("sources,tokens,partial", [(8, 8, True), (1, 8, True), (9, 8, False), (4, 33, True), (8, 4096, True)])
+def test_attnres_mix_matches_oracle(cuda_device, sources: int, tokens: int, partial: bool) -> None:
+    g = torch.Generator().manual_seed(11 + sources + tokens)
+    bank = torch.randn(sources, tokens, 768, generator=g).to(torch.bfloat16)
+    part = torch.randn(tokens, 768, generator=g).to(torch.bfloat16) if partial else None
+    wq = torch.randn(768, generator=g) * 0.02
+    out = ops.b200_attnres_mix(
+        bank.to(cuda_device), None if part is None else part.to(cuda_device), wq.to(cuda_device), 1e-6
+    )
+    fused = oops.attnres_mix_fused(bank, part, wq, 1e-6)
+    eager = oops.attnres_mix_eager(bank, part, wq, 1e-6)
+    _bf16_close(out, fused, ulps=1.0, atol=1e-5)
+    # the parity bar vs the eager (training) semantics: 1e-2 relative
+    torch.testing.assert_close(out.float().cpu(), eager.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_attnres_mix_rejects_bad_layout(cuda_device) -> None:
+    bank = torch.zeros(2, 3, 768, dtype=torch.bfloat16, device=cuda_device)
+    wq = torch.zeros(768, device=cuda_device)
+    with pytest.raises(ValueError, match="partial must match"):
+        ops.b200_attnres_mix(bank, torch.zeros(3, 767, dtype=torch.bfloat16, device=cuda_device), wq, 1e-6)
+    with pytest.raises(ValueError, match="contiguous"):
+        ops.b200_attnres_mix(bank.transpose(0, 1), None, wq, 1e-6)
+
+
+def _rope_tables(d: int, max_pos: int, device):
+    cos, sin = oops.rope_cache(d, max_pos, 1e6)
+    return cos, sin, cos.to(torch.bfloat16).to(device), sin.to(torch.bfloat16).to(device)
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(12, 4, 64), (8, 2, 96)])
+@pytest.mark.parametrize("page_size", [1, 16])
+def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int, d: int, page_size: int) -> None:
+    """8 candidate rows sharing a 13-token prefix, 5 suffix tokens each (the
+    newest one stored by the kernel itself)."""
+    g = torch.Generator().manual_seed(hq * d + page_size)
+    rows, prefix, suffix = 8, 13, 5
+    num_pages = 64
+    num_slots = num_pages * page_size
+    cos, sin, cos_b, sin_b = _rope_tables(d, 512, cuda_device)
+    eps, scale = 1e-6, d**-0.5
+    kc = torch.zeros(num_slots, hkv, d, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    table = torch.zeros(rows, 64, dtype=torch.int32)
+    if page_size == 1:
+        perm = torch.randperm(num_slots, generator=g)
+        prefix_slots = perm[:prefix]
+        suffix_slots = [perm[prefix + r * suffix : prefix + (r + 1) * suffix] for r in range(rows)]
+    else:
+        # prefix on pages[0] (13 of 16 tokens used), each row's suffix on its own page
+        pages = torch.randperm(num_pages, generator=g)
+        prefix_slots = pages[0] * page_size + torch.arange(prefix)
+        suffix_slots = [pages[1 + r] * page_size + torch.arange(suffix) for r in range(rows)]
+    for r in range(rows):
+        table[r, :prefix] = prefix_slots.to(torch.int32)
+        table[r, prefix : prefix + suffix] = suffix_slots[r].to(torch.int32)
+    # pre-existing cache content (already normalised/rotated as the model stores it)
+    for s in range(num_slots):
+        kc[s] = torch.randn(hkv, d, generator=g).to(torch.bfloat16)
+        vc[s] = torch.randn(hkv, d, generator=g).to(torch.bfloat16)
+    qkv = torch.randn(rows, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16)
+    qn = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    kn = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    pos = prefix + suffix - 1
+    out_loc = table[:, pos].clone()
+    # oracle: norm + rope + store + attention
+    q = qkv[:, : hq * d].view(rows, hq, d)
+    k = qkv[:, hq * d : (hq + hkv) * d].view(rows, hkv, d)
+    v = qkv[:, (hq + hkv) * d :].view(rows, hkv, d)
+    qr = oops.apply_rope(oops.rmsnorm(q, qn, eps), cos[[pos] * rows], sin[[pos] * rows])
+    kr = oops.apply_rope(oops.rmsnorm(k, kn, eps), cos[[pos] * rows], sin[[pos] * rows])
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+    kc_ref[out_loc.long()] = kr
+    vc_ref[out_loc.long()] = v
+    expected = torch.stack([
+        oops.attention(qr[r : r + 1], kc_ref[table[r, : pos + 1].long()], vc_ref[table[r, : pos + 1].long()],
+                       torch.tensor([pos]), scale)[0]
+        for r in range(rows)
+    ])
+    dev = cuda_device
+    kcd, vcd = kc.to(dev), vc.to(dev)
+    out = torch.empty(rows, hq * d, dtype=torch.bfloat16, device=dev)
+    ops.attention_decode(
+        out=out, k_cache=kcd, v_cache=vcd, page_table=table.to(dev),
+        row_table=torch.arange(rows, dtype=torch.int32, device=dev),
+        seq_lens=torch.full((rows,), pos + 1, dtype=torch.int32, device=dev),
+        positions=torch.full((rows,), pos, dtype=torch.int32, device=dev),
+        num_qo_heads=hq, num_kv_heads=hkv, head_dim=d, scale=scale,
+        qkv=qkv.to(dev), q_norm_w=qn.to(dev), k_norm_w=kn.to(dev), eps=eps, cos=cos_b, sin=sin_b,
+        out_loc=out_loc.to(dev), prefix_len=torch.tensor([prefix], dtype=torch.int32, device=dev),
+    )
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    # the stored K must be the bf16 rope of the bf16 norm, bit for bit
+    assert torch.equal(kcd[out_loc.long()].cpu(), kr)
+    assert torch.equal(vcd[out_loc.long()].cpu(), v)
+    _bf16_close(out.view(rows, hq, d), expected, ulps=2.0, atol=2e-3)
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(12, 4, 64), (8, 2, 96)])
+def test_prefill_attention_with_cached_prefix(cuda_device, hq: int, hkv: int, d: int) -> None:
+    g = torch.Generator().manual_seed(21 + d)
+    cached, new = 9, 24
+    total = cached + new
+    num_slots = 128
+    cos, sin, cos_b, sin_b = _rope_tables(d, 512, cuda_device)
+    eps, scale = 1e-6, d**-0.5
+    perm = torch.randperm(num_slots, generator=g)
+    slots = perm[:total].to(torch.int32)
+    kc = torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16)
+    vc = torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16)
+    qkv = torch.randn(new, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16)
+    qn = torch.ones(d, dtype=torch.bfloat16)
+    kn = torch.ones(d, dtype=torch.bfloat16)
+    positions = torch.arange(cached, total, dtype=torch.int32)
+    q = qkv[:, : hq * d].view(new, hq, d)
+    k = qkv[:, hq * d : (hq + hkv) * d].view(new, hkv, d)
+    v = qkv[:, (hq + hkv) * d :].view(new, hkv, d)
+    qr = oops.apply_rope(oops.rmsnorm(q, qn, eps), cos[positions.long()], sin[positions.long()])
+    kr = oops.apply_rope(oops.rmsnorm(k, kn, eps), cos[positions.long()], sin[positions.long()])
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+    kc_ref[slots[cached:].long()] = kr
+    vc_ref[slots[cached:].long()] = v
+    expected = oops.attention(qr, kc_ref[slots.long()], vc_ref[slots.long()], positions, scale)
+    dev = cuda_device
+    table = torch.zeros(1, 64, dtype=torch.int32)
+    table[0, :total] = slots
+    kcd, vcd = kc.to(dev), vc.to(dev)
+    qbuf = torch.empty(new, hq * d, dtype=torch.bfloat16, device=dev)
+    ops.qk_norm_rope_store(
+        qkv=qkv.to(dev), num_qo_heads=hq, num_kv_heads=hkv, head_dim=d, q_norm_w=qn.to(dev), k_norm_w=kn.to(dev),
+        eps=eps, cos=cos_b, sin=sin_b, positions=positions.to(dev), out_loc=slots[cached:].to(dev),
+        k_cache=kcd, v_cache=vcd, q_out=qbuf,
+    )
+    tile = ops.prefill_tile_tokens(hq, hkv)
+    meta, ntiles = ops.prefill_meta([new], [cached], [0], tile)
+    out = torch.empty(new, hq * d, dtype=torch.bfloat16, device=dev)
+    ops.attention_prefill(
+        q=qbuf, out=out, k_cache=kcd, v_cache=vcd, page_table=table.to(dev),
+        meta=torch.tensor(meta, dtype=torch.int32, device=dev), num_requests=1, num_tiles=ntiles,
+        tile_tokens=tile, num_qo_heads=hq, num_kv_heads=hkv, head_dim=d, scale=scale,
+    )
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    assert torch.equal(qbuf.cpu().view(new, hq, d), qr)
+    assert torch.equal(kcd[slots[cached:].long()].cpu(), kr)
+    _bf16_close(out.view(new, hq, d), expected, ulps=2.0, atol=2e-3)
+
+
+@pytest.mark.parametrize("temperature,top_k,top_p", [(0.8, 50, 0.9), (0.75, 96, 0.95), (1.0, 1, 1.0), (0.35, 50, 1.0), (0.9, 0, 1.0)])
+def test_sampler_tokens_bit_exact(cuda_device, temperature: float, top_k: int, top_p: float) -> None:
+    g = torch.Generator().manual_seed(int(temperature * 100) + top_k)
+    rows, vocab = 64, 16384
+    logits = (torch.randn(rows, vocab, generator=g) * 2.0).to(torch.bfloat16)
+    u = osamp.stateless_uniforms(list(range(1000, 1000 + rows)), 1)[:, 0]
+    forbidden = [2, 3, 4]
+    ban_rows = torch.randint(0, vocab, (rows, 3), generator=g)
+    exp_tok, exp_lp = osamp.sample_with_logprobs(
+        logits, temperature=temperature, top_k=top_k, top_p=top_p, uniforms=u,
+        forbidden_token_ids=forbidden, forbidden_token_ids_by_row=ban_rows,
+    )
+    tok, lp = ops.sample(
+        logits.to(cuda_device), temperature=temperature, top_k=top_k, top_p=top_p,
+        greedy=osamp.is_greedy(temperature, top_k, top_p), uniforms=u.to(cuda_device),
+        forbidden=torch.tensor(forbidden, dtype=torch.int32, device=cuda_device),
+        forbidden_rows=ban_rows.to(cuda_device),
+    )
+    torch.cuda.synchronize()
+    mism = (tok.cpu() != exp_tok).squeeze(-1)
+    if bool(mism.any()):
+        margins = osamp.sample_margin(logits, temperature=temperature, top_k=top_k, top_p=top_p, uniforms=u)
+        # a mismatch is only acceptable as a CDF-boundary rounding tie
+        assert float(margins[mism.numpy()].max()) < 1e-6, f"token mismatch rows {mism.nonzero().flatten().tolist()}"
+    torch.testing.assert_close(lp.cpu(), exp_lp, rtol=0, atol=2e-5)
+
+
+def test_stateless_uniforms_bit_exact(cuda_device) -> None:
+    seeds = [20260814 + 100003 * 8 + i for i in range(8)] + [0, 1, 2**40 + 7]
+    expected = osamp.stateless_uniforms(seeds, 16)
+    got = ops.stateless_uniforms_device(torch.tensor(seeds, dtype=torch.int64, device=cuda_device), 16)
+    assert torch.equal(got.cpu(), expected)
+
+
+def test_slot_fifo_matches_reference_order(cuda_device) -> None:
+    cap = 50
+    ring = torch.arange(cap, dtype=torch.int32, device=cuda_device)
+    model = list(range(cap))
+    head, tail = 0, cap
+    a = ops.slot_alloc(ring, head, 13)
+    head += 13
+    assert a.cpu().tolist() == model[:13]
+    model = model[13:]
+    ops.slot_free(ring, tail, a[5:9])
+    tail += 4
+    model += a[5:9].cpu().tolist()
+    b = ops.slot_alloc(ring, head, 30)
+    head += 30
+    assert b.cpu().tolist() == model[:30]
+    model = model[30:]
+    # free b's range straight from the ring (overlapping wrap-around copy)
+    ops.slot_free_range(ring, head - 30, 30, tail)
+    tail += 30
+    model += b.cpu().tolist()
+    c = ops.slot_alloc(ring, head, tail - head)
+    assert c.cpu().tolist() == model
