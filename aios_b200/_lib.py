@@ -37,6 +37,7 @@ DEVICE_STATUS_NAMES = {
 
 EPI_STORE = 0
 EPI_SILU_MUL = 1
+EPI_ADD = 2
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -101,6 +102,7 @@ class GroupPtrs(ctypes.Structure):
         ("seq_lens", _p),
         ("out_loc", _p),
         ("row_page", _p),
+        ("row_table", _p),
         ("terminal_ids", _p),
         ("minlen_ids", _p),
         ("banned", _p),
@@ -114,13 +116,14 @@ class GroupPtrs(ctypes.Structure):
 _SIGNATURES = {
     "aiosb_version": ([], _i32),
     "aiosb_last_error": ([ctypes.c_char_p, ctypes.c_size_t], _i32),
+    "aiosb_host_device_pointer": ([_p, ctypes.POINTER(_p)], _i32),
     "aiosb_kv_store": ([_p, _p, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _p, _p], _i32),
     "aiosb_attnres_mix": ([_p, _i64, _i64, _i64, _p, _p, _f32, _p, _p], _i32),
     "aiosb_rmsnorm": ([_p, _i64, _i64, _i64, _i64, _p, _f32, _p, _i64, _p], _i32),
     "aiosb_add_rmsnorm": ([_p, _p, _i64, _i64, _p, _f32, _p], _i32),
     "aiosb_silu_mul": ([_p, _i64, _i64, _p, _p], _i32),
     "aiosb_embedding": ([_p, _i32, _i64, _p, _i64, _i64, _p, _p, _p], _i32),
-    "aiosb_linear": ([_p, _i64, _i64, _p, _i64, _p, _i64, _i32, _p, _p], _i32),
+    "aiosb_linear": ([_p, _i64, _i64, _p, _i64, _p, _i64, _i32, _p, _i64, _p, _p], _i32),
     "aiosb_attention_decode": (
         [_p, _i64, _p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p,
          _i64, _i64, _i64, _i64, _f32, _p, _i64, _p, _p],
@@ -141,6 +144,7 @@ _SIGNATURES = {
         _i32,
     ),
     "aiosb_stateless_uniforms": ([_p, _i64, _i64, _p, _p], _i32),
+    "aiosb_token_logprobs": ([_p, _i64, _i64, _i64, _p, _p, _p, _p], _i32),
     "aiosb_slot_alloc": ([_p, _i64, _i64, _i64, _p, _p], _i32),
     "aiosb_slot_free": ([_p, _i64, _i64, _p, _i64, _p], _i32),
     "aiosb_slot_free_range": ([_p, _i64, _i64, _i64, _i64, _p], _i32),

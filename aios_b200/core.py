@@ -79,6 +79,9 @@ class Batch:
     out_loc: torch.Tensor = field(init=False)
     attn_metadata: "BaseAttentionMetadata" = field(init=False)
     return_all_logits: bool = False
+    # Optional preallocated [rows, vocab] buffer the LM head writes into (lets a
+    # captured decode step leave its logits where the next sampling step reads).
+    logits_out: torch.Tensor | None = None
 
     @property
     def is_prefill(self) -> bool:

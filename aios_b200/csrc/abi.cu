@@ -41,6 +41,15 @@ int check_launch(const char* what) {
 
 extern "C" int aiosb_version(void) { return 100; }
 
+extern "C" int aiosb_host_device_pointer(void* host, void** device) {
+  AIOSB_REQUIRE(host != nullptr && device != nullptr, AIOSB_ERR_INVALID_ARG, "host_device_pointer: null pointer");
+  cudaError_t e = cudaHostGetDevicePointer(device, host, 0);
+  if (e != cudaSuccess)
+    return aiosb::set_error(AIOSB_ERR_INVALID_ARG, "host_device_pointer: %s (is the buffer page-locked?)",
+                     cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
 extern "C" int aiosb_last_error(char* buf, size_t len) {
   if (buf != nullptr && len > 0) {
     strncpy(buf, g_msg, len - 1);

@@ -42,7 +42,7 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
 
 }  // namespace aiosb
 
-#define AIOSB_REQUIRE(cond, code, ...)                   \
+#define AIOSB_REQUIRE(cond, code, ...) \
   do {                                                   \
     if (!(cond)) return ::aiosb::set_error(code, __VA_ARGS__); \
   } while (0)

@@ -37,6 +37,8 @@ struct GemmArgs {
   int64_t n;             // weight rows
   int64_t y_row_stride;  // elements
   __nv_bfloat16* y;
+  const __nv_bfloat16* residual;  // AIOSB_EPI_ADD: y = residual + bf16(x W^T)
+  int64_t residual_stride;
   int32_t* status;
   int chunks_per_split;  // 64-wide K chunks handled by one CTA
   int stages;
@@ -176,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t rank = split > 1 ? cluster_ctarank() : 0u;
     const uint32_t red_addr = smem_u32(red);
     const int64_t t0 = (int64_t)n_tile * BN;
-    if (a.epilogue == AIOSB_EPI_STORE) {
+    if (a.epilogue == AIOSB_EPI_STORE || a.epilogue == AIOSB_EPI_ADD) {
       // 32 float4 per column; 128 threads handle 4 columns per pass.
       for (int idx = tid; idx < BN * 32; idx += kThreads) {
         const int c = idx >> 5, m4 = idx & 31;
@@ -192,6 +194,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
         }
         __nv_bfloat16* dst = a.y + t * a.y_row_stride + (int64_t)m_tile * kBM + m4 * 4;
+        if (a.epilogue == AIOSB_EPI_ADD) {
+          // residual + delta with the delta rounded to bf16 first, as the
+          // reference's bf16 `partial + delta` (aios/models/minimind_ime.py:237-252).
+          const uint2 rv = *reinterpret_cast<const uint2*>(a.residual + t * a.residual_stride +
+                                                          (int64_t)m_tile * kBM + m4 * 4);
+          acc.x = bf16_lo(rv.x) + round_bf16(acc.x);
+          acc.y = bf16_hi(rv.x) + round_bf16(acc.y);
+          acc.z = bf16_lo(rv.y) + round_bf16(acc.z);
+          acc.w = bf16_hi(rv.y) + round_bf16(acc.w);
+        }
         uint2 o = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
         *reinterpret_cast<uint2*>(dst) = o;
       }
@@ -326,13 +338,17 @@ int choose_split(int64_t tiles, int64_t chunks, int sms) {
 using namespace aiosb;
 
 extern "C" int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
-                            int64_t y_row_stride, int epilogue, int32_t* status, void* stream) {
+                            int64_t y_row_stride, int epilogue, const void* residual, int64_t residual_stride,
+                            int32_t* status, void* stream) {
   AIOSB_REQUIRE(rows >= 0 && k > 0 && n > 0, AIOSB_ERR_INVALID_ARG, "linear: bad sizes");
   AIOSB_REQUIRE(n % kBM == 0, AIOSB_ERR_UNSUPPORTED, "linear: n=%lld must be a multiple of 128", (long long)n);
   AIOSB_REQUIRE(k % kBK == 0, AIOSB_ERR_UNSUPPORTED, "linear: k=%lld must be a multiple of 64", (long long)k);
-  AIOSB_REQUIRE(epilogue == AIOSB_EPI_STORE || epilogue == AIOSB_EPI_SILU_MUL, AIOSB_ERR_INVALID_ARG,
-                "linear: unknown epilogue %d", epilogue);
-  const int64_t y_cols = epilogue == AIOSB_EPI_STORE ? n : n / 2;
+  AIOSB_REQUIRE(epilogue == AIOSB_EPI_STORE || epilogue == AIOSB_EPI_SILU_MUL || epilogue == AIOSB_EPI_ADD,
+                AIOSB_ERR_INVALID_ARG, "linear: unknown epilogue %d", epilogue);
+  AIOSB_REQUIRE(epilogue != AIOSB_EPI_ADD ||
+                    (residual != nullptr && aligned16(residual) && residual_stride >= n && residual_stride % 8 == 0),
+                AIOSB_ERR_INVALID_ARG, "linear: the add epilogue needs an aligned residual [rows, >= n]");
+  const int64_t y_cols = epilogue == AIOSB_EPI_SILU_MUL ? n / 2 : n;
   AIOSB_REQUIRE(y_row_stride >= y_cols && y_row_stride % 8 == 0, AIOSB_ERR_INVALID_ARG,
                 "linear: y row stride must cover the output and be a multiple of 8");
   if (rows == 0) return AIOSB_OK;
@@ -348,6 +364,8 @@ extern "C" int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* 
   a.n = n;
   a.y_row_stride = y_row_stride;
   a.y = (__nv_bfloat16*)y;
+  a.residual = (const __nv_bfloat16*)residual;
+  a.residual_stride = residual_stride;
   a.status = status;
   a.epilogue = epilogue;
   a.split = choose_split(m_tiles * n_tiles, chunks, sm_count());

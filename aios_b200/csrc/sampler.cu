@@ -507,6 +507,7 @@ __global__ void group_begin_kernel(aiosb_group_ptrs g, const __nv_bfloat16* __re
     g.active[i] = i < attempts ? 1 : 0;
     g.row_page[i] = -1;
     g.out_loc[i] = -1;
+    g.row_table[i] = st->row_offset + (int32_t)i;
   }
 }
 
@@ -556,6 +557,29 @@ __global__ void __launch_bounds__(1024) slot_free_range_kernel(int32_t* ring, in
 }
 
 size_t sample_smem(int V) { return sizeof(RowSmem) + (size_t)V * sizeof(float); }
+
+// Raw log-probability of a given target per row (teacher-forced scoring).
+__global__ void __launch_bounds__(kSampThreads)
+    token_logprob_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int V,
+                         const int64_t* __restrict__ targets, float* __restrict__ out, int32_t* status) {
+  extern __shared__ uint8_t smem_raw[];
+  RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
+  float* row = reinterpret_cast<float*>(smem_raw + sizeof(RowSmem));
+  pdl_wait();
+  const int r = blockIdx.x;
+  const __nv_bfloat16* lrow = logits + (int64_t)r * row_stride;
+  float mx, lse;
+  load_row(s, row, lrow, V, mx, lse);
+  if (threadIdx.x == 0) {
+    const int64_t t = targets[r];
+    if (t < 0 || t >= V) {
+      report(status, AIOSB_DEV_TOKEN_RANGE);
+      out[r] = -INFINITY;
+    } else {
+      out[r] = (row[t] - mx) - lse;
+    }
+  }
+}
 
 }  // namespace
 }  // namespace aiosb
@@ -610,6 +634,21 @@ extern "C" int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t
   cudaError_t e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads), sample_smem((int)vocab),
                              as_stream(stream), *g);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_token_logprobs(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                                    const int64_t* targets, float* out, int32_t* status, void* stream) {
+  AIOSB_REQUIRE(rows >= 0 && vocab > 0 && vocab <= kMaxVocab && row_stride >= vocab, AIOSB_ERR_INVALID_ARG,
+                "token_logprobs: bad sizes (vocab must be in [1, %d])", kMaxVocab);
+  if (rows == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(logits && targets && out, AIOSB_ERR_INVALID_ARG, "token_logprobs: null pointer");
+  cudaFuncSetAttribute(token_logprob_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       (int)sample_smem(kMaxVocab));
+  cudaError_t e = launch_pdl(token_logprob_kernel, dim3((unsigned)rows), dim3(kSampThreads),
+                             sample_smem((int)vocab), as_stream(stream), (const __nv_bfloat16*)logits, row_stride,
+                             (int)vocab, targets, out, status);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "token_logprobs: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }
 

@@ -8,6 +8,8 @@ status word that :func:`check_status` turns into a ``RuntimeError``.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from .. import _lib
@@ -37,6 +39,15 @@ def check_status(device: torch.device, reset: bool = True) -> None:
         if reset:
             st.zero_()
         raise RuntimeError(f"aios_b200 device status {code}: {_lib.DEVICE_STATUS_NAMES.get(code, 'unknown')}")
+
+
+def host_device_pointer(pinned: torch.Tensor) -> int:
+    """Device address of a page-locked host tensor (for host-mapped flags)."""
+    if not pinned.is_pinned():
+        raise ValueError("host_device_pointer needs a pinned CPU tensor")
+    out = ctypes.c_void_p()
+    _lib.call("aiosb_host_device_pointer", pinned.data_ptr(), ctypes.byref(out))
+    return int(out.value)
 
 
 def _require_cuda(*tensors: torch.Tensor, what: str) -> None:
@@ -262,15 +273,22 @@ def linear(
     weight: torch.Tensor,
     out: torch.Tensor | None = None,
     epilogue: int = _lib.EPI_STORE,
+    residual: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """y = x @ weight.T on the tensor cores (bf16 in, fp32 accumulate, bf16 out)."""
+    """y = x @ weight.T on the tensor cores (bf16 in, fp32 accumulate, bf16 out).
+
+    ``epilogue=EPI_ADD`` returns ``residual + bf16(x @ weight.T)`` (residual may
+    be ``out`` for an in-place add)."""
     _require_cuda(x, weight, what="linear")
     if x.ndim != 2 or weight.ndim != 2 or x.shape[1] != weight.shape[1]:
         raise ValueError("linear expects x [T, K] and weight [N, K]")
     if not x.is_contiguous() or not weight.is_contiguous():
         raise ValueError("linear expects contiguous x and weight")
     n = weight.shape[0]
-    cols = n if epilogue == _lib.EPI_STORE else n // 2
+    cols = n // 2 if epilogue == _lib.EPI_SILU_MUL else n
+    if epilogue == _lib.EPI_ADD:
+        if residual is None or residual.shape != (x.shape[0], n) or residual.stride(1) != 1:
+            raise ValueError("the add epilogue needs a residual [rows, n] with contiguous rows")
     if out is None:
         out = torch.empty((x.shape[0], cols), dtype=x.dtype, device=x.device)
     if out.stride(1) != 1:
@@ -285,6 +303,8 @@ def linear(
         out.data_ptr(),
         out.stride(0),
         epilogue,
+        _ptr(residual) if epilogue == _lib.EPI_ADD else None,
+        residual.stride(0) if (epilogue == _lib.EPI_ADD and residual is not None) else 0,
         status_word(x.device).data_ptr(),
         _stream(x.device),
     )
@@ -525,6 +545,16 @@ def sample(
         _stream(dev),
     )
     return tok, lp
+
+
+def token_logprobs(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+    """log_softmax(logits.float())[r, targets[r]] per row, fp32."""
+    rows, vocab = logits.shape
+    t = targets.to(device=logits.device, dtype=torch.int64).contiguous()
+    out = torch.empty(rows, dtype=torch.float32, device=logits.device)
+    _lib.call("aiosb_token_logprobs", logits.data_ptr(), rows, vocab, logits.stride(0), t.data_ptr(),
+              out.data_ptr(), status_word(logits.device).data_ptr(), _stream(logits.device))
+    return out
 
 
 def stateless_uniforms_device(seeds: torch.Tensor, steps: int) -> torch.Tensor:

@@ -1,0 +1,166 @@
+"""MiniMind-IME model (aios/models/minimind_ime.py) on the sm_100a kernels.
+
+Standard-residual bundles reuse the Qwen3 decoder. Block AttnRes bundles
+(0.214B: 32 layers, 8 blocks, 65 depth mixers) run each mixer as one fused
+kernel (RMS score + depth softmax + weighted sum), and fold the block-local
+residual adds ``partial + delta`` into the o_proj / down_proj GEMM epilogues;
+the last layer of a block writes its partial straight into the bank slot.
+"""
+
+from __future__ import annotations
+
+from typing import TYPE_CHECKING
+
+import torch
+
+from .. import _lib
+from ..attention import B200AttentionBackend
+from ..core import get_global_ctx
+from ..kernel import ops
+from ..layers import BaseOP, Embedding, LMHead, OPList, RMSNorm, RotaryEmbedding
+from .qwen3 import Qwen3Attention, Qwen3ForCausalLM, Qwen3MLP
+
+if TYPE_CHECKING:
+    from ..core import Batch
+    from ..kvcache import MHAKVCache
+    from .config import ModelConfig
+
+
+class BlockAttnResMixer(BaseOP):
+    """Kimi Block AttnRes depth mixer for ``alpha = 1``; weights ``query`` and
+    ``key_norm.weight`` as in the reference checkpoints."""
+
+    def __init__(self, hidden_size: int, eps: float, backend: str = "b200") -> None:
+        self.query = torch.empty(hidden_size)
+        self.key_norm = RMSNorm(hidden_size, eps)
+        self._backend = backend
+        self._weighted_query: torch.Tensor | None = None
+
+    def on_weights_loaded(self) -> None:
+        self._weighted_query = None
+
+    def _routing_query(self) -> torch.Tensor:
+        """query * key_norm.weight folded once in fp32 (aios/models/minimind_ime.py:106-117)."""
+        cached = self._weighted_query
+        if cached is None or cached.device != self.query.device or cached.shape != self.query.shape:
+            cached = (self.query.float() * self.key_norm.weight.float()).contiguous()
+            self._weighted_query = cached
+        return cached
+
+    def forward(
+        self,
+        bank: torch.Tensor,
+        partial: torch.Tensor | None = None,
+        *,
+        score_buffer: torch.Tensor | None = None,
+        output_buffer: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        if bank.ndim != 3:
+            raise ValueError(f"AttnRes bank must have shape [S,N,D], got {tuple(bank.shape)}")
+        if bank.shape[-1] != self.query.numel():
+            raise ValueError("AttnRes bank hidden size does not match query")
+        if partial is not None and partial.shape != bank.shape[1:]:
+            raise ValueError("AttnRes partial must have shape [N,D] matching bank")
+        return ops.b200_attnres_mix(
+            bank, partial, self._routing_query(), self.key_norm.eps,
+            score_buffer=score_buffer, output_buffer=output_buffer,
+        )
+
+
+class MiniMindAttnResDecoderLayer(BaseOP):
+    """One attention/MLP pair that contributes deltas to its block's partial."""
+
+    def __init__(self, config: ModelConfig, layer_idx: int, attn_backend: B200AttentionBackend) -> None:
+        self.self_attn = Qwen3Attention(config, layer_idx, attn_backend)
+        self.mlp = Qwen3MLP(config)
+        self.input_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self.attn_res_mixer = BlockAttnResMixer(config.hidden_size, config.rms_norm_eps, config.attnres_backend)
+        self.mlp_res_mixer = BlockAttnResMixer(config.hidden_size, config.rms_norm_eps, config.attnres_backend)
+
+    def forward(
+        self,
+        bank: torch.Tensor,
+        partial: torch.Tensor | None,
+        rotary: RotaryEmbedding,
+        paged_kv_cache: MHAKVCache,
+        batch: Batch,
+        mixed: torch.Tensor,
+        out: torch.Tensor | None = None,
+    ) -> torch.Tensor:
+        hidden = self.attn_res_mixer.forward(bank, partial, output_buffer=mixed)
+        attn = self.self_attn.attend(self.input_layernorm.forward(hidden), rotary, paged_kv_cache, batch)
+        w_o = self.self_attn.o_proj.weight
+        if partial is None:
+            partial = ops.linear(attn, w_o)
+        else:
+            ops.linear(attn, w_o, out=partial, epilogue=_lib.EPI_ADD, residual=partial)
+        hidden = self.mlp_res_mixer.forward(bank, partial, output_buffer=mixed)
+        act = self.mlp.gate_up_proj.forward_silu_mul(self.post_attention_layernorm.forward(hidden))
+        target = partial if out is None else out
+        ops.linear(act, self.mlp.down_proj.weight, out=target, epilogue=_lib.EPI_ADD, residual=partial)
+        return target
+
+
+class MiniMindBlockAttnResModel(BaseOP):
+    """Inference trunk with block-local deltas and depth routing."""
+
+    def __init__(self, config: ModelConfig) -> None:
+        self.attn_backend = B200AttentionBackend(config)
+        self.embed_tokens = Embedding(config.vocab_size, config.hidden_size)
+        self.layers = OPList(
+            [MiniMindAttnResDecoderLayer(config, i, self.attn_backend) for i in range(config.num_layers)]
+        )
+        self.final_attn_res_mixer = BlockAttnResMixer(config.hidden_size, config.rms_norm_eps, config.attnres_backend)
+        self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
+        self._rotary_emb = RotaryEmbedding(config.head_dim, config.max_position_embeddings, config.rope_theta)
+        self._num_blocks = config.attnres_num_blocks
+        self._layers_per_block = config.layers_per_attnres_block
+
+    def forward(self) -> torch.Tensor:
+        ctx = get_global_ctx()
+        batch = ctx.batch
+        ids = batch.input_ids
+        tokens = ids.numel()
+        hidden = self.embed_tokens.weight.shape[1]
+        bank_storage = torch.empty(
+            (self._num_blocks + 1, tokens, hidden), dtype=self.embed_tokens.weight.dtype, device=ids.device
+        )
+        ops.embedding(ids, self.embed_tokens.weight, out=bank_storage[0])
+        mixed = torch.empty((tokens, hidden), dtype=bank_storage.dtype, device=ids.device)
+        source_count = 1
+        for block in range(self._num_blocks):
+            partial: torch.Tensor | None = None
+            bank = bank_storage[:source_count]
+            first = block * self._layers_per_block
+            last = first + self._layers_per_block - 1
+            for index in range(first, last + 1):
+                partial = self.layers.op_list[index].forward(
+                    bank, partial, self._rotary_emb, ctx.kv_cache, batch, mixed,
+                    out=bank_storage[source_count] if index == last else None,
+                )
+            source_count += 1
+        hidden_states = self.final_attn_res_mixer.forward(bank_storage[:source_count], output_buffer=mixed)
+        return self.norm.forward(hidden_states)
+
+
+class MiniMindIMEForCausalLM(Qwen3ForCausalLM):
+    """Standard-residual bundles use the Qwen3 decoder; ``block_attnres`` bundles
+    use the Block AttnRes trunk with the same attention, RoPE, SwiGLU, KV-cache
+    and LM-head formats."""
+
+    def __init__(self, config: ModelConfig) -> None:
+        if config.residual_type == "standard":
+            super().__init__(config)
+            return
+        self.model = MiniMindBlockAttnResModel(config)
+        self.attn_backend = self.model.attn_backend
+        self.lm_head = LMHead(
+            config.vocab_size,
+            config.hidden_size,
+            tie_word_embeddings=config.tie_word_embeddings,
+            tied_embedding=self.model.embed_tokens if config.tie_word_embeddings else None,
+        )
+
+    def forward(self) -> torch.Tensor:
+        return self.lm_head.forward(self.model.forward())

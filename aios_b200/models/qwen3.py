@@ -1,0 +1,137 @@
+"""Standard-residual decoder (aios/models/qwen3.py:31-173) on the sm_100a kernels.
+
+Per layer and forward: add+RMSNorm kernel, qkv GEMM (tcgen05), the attention
+kernel that also applies q/k RMSNorm + bf16 RoPE and writes the new K/V, o GEMM,
+add+RMSNorm, gate/up GEMM with the SwiGLU epilogue, down GEMM. The parameter
+names and their order equal the reference's, so checkpoints load unchanged.
+"""
+
+from __future__ import annotations
+
+from typing import TYPE_CHECKING
+
+import torch
+
+from ..attention import B200AttentionBackend, BaseAttentionBackend
+from ..core import get_global_ctx
+from ..layers import (
+    BaseOP,
+    Embedding,
+    Linear,
+    LinearColParallelMerged,
+    LinearQKVMerged,
+    LMHead,
+    OPList,
+    RMSNorm,
+    RMSNormFused,
+    RotaryEmbedding,
+    apply_rotary_pos_emb,
+)
+from .base import BaseLLMModel
+
+if TYPE_CHECKING:
+    from ..core import Batch
+    from ..kvcache import MHAKVCache
+    from .config import ModelConfig
+
+
+class Qwen3Attention(BaseOP):
+    def __init__(self, config: ModelConfig, layer_idx: int, attn_backend: BaseAttentionBackend):
+        self.num_heads = config.num_qo_heads
+        self.num_kv_heads = config.num_kv_heads
+        self.head_dim = config.head_dim
+        self._layer_idx = layer_idx
+        self.q_size = self.num_heads * self.head_dim
+        self.kv_size = self.num_kv_heads * self.head_dim
+        self.qkv_proj = LinearQKVMerged(config.hidden_size, self.q_size, self.kv_size)
+        self.o_proj = Linear(self.num_heads * self.head_dim, config.hidden_size)
+        self.q_norm = RMSNorm(self.head_dim, config.rms_norm_eps)
+        self.k_norm = RMSNorm(self.head_dim, config.rms_norm_eps)
+        self._attn_backend = attn_backend
+
+    def attend(self, hidden_states: torch.Tensor, rotary: RotaryEmbedding, paged_kv_cache: MHAKVCache,
+               batch: Batch) -> torch.Tensor:
+        """Projection + attention, without o_proj: [T, Hq * d]."""
+        qkv = self.qkv_proj.forward(hidden_states)
+        backend = self._attn_backend
+        if isinstance(backend, B200AttentionBackend):
+            cos, sin = rotary.tables()
+            return backend.forward_qkv(
+                qkv, self.q_norm.weight, self.k_norm.weight, cos, sin, paged_kv_cache, self._layer_idx, batch
+            )
+        # A third-party backend plugged into the reference slot gets normalised,
+        # rotated q/k exactly as aios/models/qwen3.py:61-73 hands them over.
+        tokens = qkv.shape[0]
+        q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
+        q = q.view(tokens, self.num_heads, self.head_dim)
+        k = k.view(tokens, self.num_kv_heads, self.head_dim)
+        v = v.view(tokens, self.num_kv_heads, self.head_dim)
+        self.q_norm.forward_inplace(q)
+        self.k_norm.forward_inplace(k)
+        cos, sin = rotary.forward(batch.positions.long())
+        q, k = apply_rotary_pos_emb(q, k, cos, sin)
+        return backend.forward(q, k, v, paged_kv_cache, self._layer_idx, batch).reshape(tokens, -1)
+
+    def forward(self, hidden_states, rotary, paged_kv_cache, batch) -> torch.Tensor:
+        return self.o_proj.forward(self.attend(hidden_states, rotary, paged_kv_cache, batch))
+
+
+class Qwen3MLP(BaseOP):
+    def __init__(self, config: ModelConfig):
+        self.gate_up_proj = LinearColParallelMerged(
+            config.hidden_size, [config.intermediate_size, config.intermediate_size]
+        )
+        self.down_proj = Linear(config.intermediate_size, config.hidden_size)
+        if config.hidden_act != "silu":
+            raise ValueError(f"Unsupported activation: {config.hidden_act}")
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.down_proj.forward(self.gate_up_proj.forward_silu_mul(x))
+
+
+class Qwen3DecoderLayer(BaseOP):
+    def __init__(self, config: ModelConfig, layer_idx: int, attn_backend: BaseAttentionBackend):
+        self.self_attn = Qwen3Attention(config, layer_idx, attn_backend)
+        self.mlp = Qwen3MLP(config)
+        self.input_layernorm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
+        self.post_attention_layernorm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
+
+    def forward(self, hidden_states, rotary, paged_kv_cache, batch, residual):
+        hidden_states, residual = self.input_layernorm.forward(hidden_states, residual)
+        hidden_states = self.self_attn.forward(hidden_states, rotary, paged_kv_cache, batch)
+        hidden_states, residual = self.post_attention_layernorm.forward(hidden_states, residual)
+        hidden_states = self.mlp.forward(hidden_states)
+        return hidden_states, residual
+
+
+class Qwen3Model(BaseOP):
+    def __init__(self, config: ModelConfig):
+        self.attn_backend = B200AttentionBackend(config)
+        self.embed_tokens = Embedding(config.vocab_size, config.hidden_size)
+        self.layers = OPList([Qwen3DecoderLayer(config, i, self.attn_backend) for i in range(config.num_layers)])
+        self.norm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
+        self._rotary_emb = RotaryEmbedding(config.head_dim, config.max_position_embeddings, config.rope_theta)
+
+    def forward(self) -> torch.Tensor:
+        ctx = get_global_ctx()
+        batch = ctx.batch
+        hidden_states = self.embed_tokens.forward(batch.input_ids)
+        residual: torch.Tensor | None = None
+        for layer in self.layers.op_list:
+            hidden_states, residual = layer.forward(hidden_states, self._rotary_emb, ctx.kv_cache, batch, residual)
+        return self.norm.forward(hidden_states, residual)[0]
+
+
+class Qwen3ForCausalLM(BaseLLMModel):
+    def __init__(self, config: ModelConfig):
+        self.model = Qwen3Model(config)
+        self.attn_backend = self.model.attn_backend
+        self.lm_head = LMHead(
+            config.vocab_size,
+            config.hidden_size,
+            tie_word_embeddings=config.tie_word_embeddings,
+            tied_embedding=self.model.embed_tokens if config.tie_word_embeddings else None,
+        )
+
+    def forward(self) -> torch.Tensor:
+        return self.lm_head.forward(self.model.forward())

@@ -1,0 +1,293 @@
+"""CandidateGroup branch-batch runtime: the device-side replacement of
+``ImeCompletionEngine._generate_branch_batch``'s step loop (aios/ime.py:891-1054).
+
+One round of ``attempts`` candidate rows runs as
+
+    group_begin                      (reset rows, broadcast prefix logits, uniforms)
+    [group_step + decode forward] x (max_new_tokens - 1)   (one CUDA graph replay each)
+    group_step                       (last sample, no forward)
+
+``group_step`` samples every active row, does the EOS/terminal bookkeeping,
+compacts finished rows and allocates the next KV slots from the device FIFO in
+active-row order, then writes the decode forward's ids / positions / slots; the
+forward (every layer's kernels) reads them from fixed device buffers, so the
+whole step is one graph replay with no host round trip. Finished rows stay in
+their slot but are masked out (no KV write, no attention), which keeps each
+row's outputs identical to the reference's compacted batch.
+
+The host never synchronises inside a round: it keeps at most two steps queued
+ahead of the device by polling a host-mapped progress word, stops launching once
+the device reports the group done, and reads all results back with one event
+wait at the end. Cancellation is observed by the device between steps through a
+host-mapped flag that ``CancellationToken.cancel`` writes.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import time
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from .. import _lib
+from ..attention import B200AttentionMetadata
+from ..core import Batch, Req, SamplingParams
+from ..kernel import ops
+
+MAX_TERMINAL = 16
+MAX_MINLEN = 32
+
+
+@dataclass
+class RoundResult:
+    output_ids: np.ndarray  # [attempts, max_new] int32 (pad where nothing was emitted)
+    token_logprobs: np.ndarray  # [attempts, max_new] float32
+    counts: list[int]
+    logprob_sums: list[float]
+    stop_codes: list[int]
+    pages_consumed: int  # FIFO entries this round took (freed by the caller)
+    active_model_tokens: int
+    cancelled: bool
+    steps: int
+
+
+class CandidateGroupRuntime:
+    def __init__(self, llm, max_rows: int = 16, max_steps: int = 64, max_banned: int = 64,
+                 max_banned_width: int = 64) -> None:
+        self.llm = llm
+        dev = llm.device
+        self.device = dev
+        self.max_rows = max_rows
+        self.max_steps = max_steps
+        self.max_banned = max_banned
+        self.max_banned_width = max_banned_width
+        self.vocab = llm.config.vocab_size
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.state = torch.zeros(ctypes.sizeof(_lib.GroupState), dtype=torch.uint8, device=dev)
+        self._state_host = torch.zeros(ctypes.sizeof(_lib.GroupState), dtype=torch.uint8).pin_memory()
+        self._state_struct = _lib.GroupState.from_address(self._state_host.data_ptr())
+        self.logits = torch.zeros((max_rows, self.vocab), dtype=torch.bfloat16, device=dev)
+        self.uniforms = torch.zeros((max_rows, max_steps), dtype=torch.float32, device=dev)
+        self.output_ids = torch.zeros((max_rows, max_steps), **i32)
+        self.token_logprobs = torch.zeros((max_rows, max_steps), dtype=torch.float32, device=dev)
+        self.counts = torch.zeros(max_rows, **i32)
+        self.logprob_sums = torch.zeros(max_rows, dtype=torch.float32, device=dev)
+        self.stop_codes = torch.zeros(max_rows, **i32)
+        self.active = torch.zeros(max_rows, **i32)
+        self.finished = torch.zeros(max_rows, **i32)
+        self.tokens = torch.zeros(max_rows, **i32)
+        self.positions = torch.zeros(max_rows, **i32)
+        self.seq_lens = torch.zeros(max_rows, **i32)
+        self.out_loc = torch.zeros(max_rows, **i32)
+        self.row_page = torch.zeros(max_rows, **i32)
+        self.row_table = torch.zeros(max_rows, **i32)
+        # id lists in one device buffer, filled by one H2D copy per round:
+        # [terminal ids | min-length ids | banned lengths | banned sequences]
+        self._ids_host = torch.zeros(MAX_TERMINAL + MAX_MINLEN + max_banned * (1 + max_banned_width),
+                                     dtype=torch.int32).pin_memory()
+        self._ids_dev = torch.zeros_like(self._ids_host, device=dev)
+        self._off_len = MAX_TERMINAL + MAX_MINLEN
+        self._off_seq = self._off_len + max_banned
+        self.cancel_flag = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.host_mirror = torch.zeros(4, dtype=torch.int32).pin_memory()
+        self._mirror_np = self.host_mirror.numpy()
+        # results read back once per round
+        self._res_ids = torch.zeros((max_rows, max_steps), dtype=torch.int32).pin_memory()
+        self._res_lp = torch.zeros((max_rows, max_steps), dtype=torch.float32).pin_memory()
+        self._res_rows = torch.zeros((3, max_rows), dtype=torch.int32).pin_memory()
+        self._res_sums = torch.zeros(max_rows, dtype=torch.float32).pin_memory()
+        self._res_state = torch.zeros_like(self._state_host).pin_memory()
+        self._done_event = torch.cuda.Event()
+        state_i32 = self.state.view(torch.int32)
+        self.prefix_len_view = state_i32[3:4]  # aiosb_group_state.prefix_len (offset 12)
+        self.ptrs = _lib.GroupPtrs(
+            state=self.state.data_ptr(),
+            cancel_flag=ops.host_device_pointer(self.cancel_flag),
+            host_mirror=ops.host_device_pointer(self.host_mirror),
+            logits=self.logits.data_ptr(),
+            uniforms=self.uniforms.data_ptr(),
+            output_ids=self.output_ids.data_ptr(),
+            token_logprobs=self.token_logprobs.data_ptr(),
+            counts=self.counts.data_ptr(),
+            logprob_sums=self.logprob_sums.data_ptr(),
+            stop_codes=self.stop_codes.data_ptr(),
+            active=self.active.data_ptr(),
+            finished=self.finished.data_ptr(),
+            tokens=self.tokens.data_ptr(),
+            positions=self.positions.data_ptr(),
+            seq_lens=self.seq_lens.data_ptr(),
+            out_loc=self.out_loc.data_ptr(),
+            row_page=self.row_page.data_ptr(),
+            row_table=self.row_table.data_ptr(),
+            terminal_ids=self._ids_dev.data_ptr(),
+            minlen_ids=self._ids_dev[MAX_TERMINAL:].data_ptr(),
+            banned=self._ids_dev[self._off_seq :].data_ptr(),
+            banned_len=self._ids_dev[self._off_len :].data_ptr(),
+            page_table=llm.ctx.page_table.data_ptr(),
+            ring=llm.cache_manager.ring.data_ptr(),
+            status=ops.status_word(dev).data_ptr(),
+        )
+        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._pool = None
+        self._top_k_cap = 2048
+
+    # ------------------------------------------------------------------ graphs
+    def _decode_batch(self, rows: int) -> Batch:
+        reqs = [Req(input_ids=torch.empty(1, dtype=torch.long), cached_len=0, output_len=1, uid=i,
+                    sampling_params=SamplingParams(max_tokens=1), table_idx=i) for i in range(rows)]
+        batch = Batch(reqs=reqs, phase="decode", logits_out=self.logits[:rows])
+        batch.input_ids = self.tokens[:rows]
+        batch.positions = self.positions[:rows]
+        batch.out_loc = self.out_loc[:rows]
+        batch.attn_metadata = B200AttentionMetadata(
+            phase="decode", positions=self.positions[:rows], out_loc=self.out_loc[:rows],
+            row_table=self.row_table[:rows], seq_lens=self.seq_lens[:rows], prefix_len=self.prefix_len_view,
+            active=self.active[:rows],
+        )
+        return batch
+
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def _step_and_forward(self, rows: int, batch: Batch) -> None:
+        lib = _lib.load()
+        _lib.check(lib.aiosb_group_step(ctypes.byref(self.ptrs), rows, self.vocab, self._top_k_cap, self._stream()),
+                   "group_step")
+        with self.llm.ctx.forward_batch(batch):
+            self.llm.model.forward()
+
+    def _graph(self, rows: int) -> torch.cuda.CUDAGraph:
+        graph = self._graphs.get(rows)
+        if graph is not None:
+            return graph
+        batch = self._decode_batch(rows)
+        # Eager warm-up with the group marked done: every kernel runs once (its
+        # attributes get set) while all rows are inactive, so nothing is written.
+        self._write_state(dict(done=1, rows=rows, max_steps=2, vocab=self.vocab, page_size=1, capacity=1,
+                               table_stride=self.llm.ctx.page_table.stride(0)))
+        self.active.zero_()
+        self._step_and_forward(rows, batch)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, pool=self._pool):
+            self._step_and_forward(rows, batch)
+        if self._pool is None:
+            self._pool = graph.pool()
+        torch.cuda.synchronize(self.device)
+        self._graphs[rows] = graph
+        return graph
+
+    # ------------------------------------------------------------------ round
+    def _write_state(self, fields: dict) -> None:
+        ctypes.memset(self._state_host.data_ptr(), 0, ctypes.sizeof(_lib.GroupState))
+        for name, value in fields.items():
+            setattr(self._state_struct, name, value)
+        self.state.copy_(self._state_host, non_blocking=True)
+
+    def run_round(
+        self,
+        *,
+        prefix_logits: torch.Tensor,
+        prefix_len: int,
+        row_offset: int,
+        attempts: int,
+        max_new_tokens: int,
+        min_new_tokens: int,
+        seed: int,
+        temperature: float,
+        top_k: int,
+        top_p: float,
+        terminal_ids: list[int],
+        minlen_ids: list[int],
+        banned_sequences: list[list[int]],
+        ban_min_prefix: int,
+        eos_id: int,
+        pad_id: int,
+        cancellation=None,
+    ) -> RoundResult:
+        if not 1 <= attempts <= self.max_rows:
+            raise ValueError(f"attempts must be in [1, {self.max_rows}]")
+        if max_new_tokens > self.max_steps:
+            raise ValueError(f"max_new_tokens above the runtime's {self.max_steps}")
+        if len(terminal_ids) > MAX_TERMINAL or len(minlen_ids) > MAX_MINLEN:
+            raise ValueError("too many terminal / minimum-length ids")
+        if len(banned_sequences) > self.max_banned or any(len(s) > self.max_banned_width for s in banned_sequences):
+            raise ValueError("refill ban list exceeds the runtime's capacity")
+        cm = self.llm.cache_manager
+        graph = self._graph(attempts)
+        head0 = cm.head
+        greedy = (temperature <= 0.0 or top_k == 1) and top_p == 1.0
+        width = max((len(s) for s in banned_sequences), default=0)
+        self._write_state(dict(
+            step=0, max_steps=max_new_tokens, min_new_tokens=min_new_tokens, prefix_len=prefix_len,
+            row_offset=row_offset, rows=attempts, vocab=self.vocab, eos_id=eos_id, pad_id=pad_id,
+            greedy=int(greedy), top_k=top_k, temperature=temperature, top_p=top_p, page_size=cm.page_size,
+            n_terminal=len(terminal_ids), n_minlen=len(minlen_ids), n_banned=len(banned_sequences),
+            banned_width=width, ban_min_prefix=ban_min_prefix, head=cm.head, tail=cm.tail,
+            capacity=cm.num_pages, table_stride=self.llm.ctx.page_table.stride(0),
+        ))
+        ids = self._ids_host.numpy()
+        ids[:MAX_TERMINAL + MAX_MINLEN] = 0
+        ids[: len(terminal_ids)] = terminal_ids
+        ids[MAX_TERMINAL : MAX_TERMINAL + len(minlen_ids)] = minlen_ids
+        off_len, off_seq = self._off_len, self._off_seq
+        for b, seq in enumerate(banned_sequences):
+            ids[off_len + b] = len(seq)
+            row = np.full(self.max_banned_width, pad_id, dtype=np.int32)
+            row[: len(seq)] = seq
+            ids[off_seq + b * width : off_seq + (b + 1) * width] = row[:width]
+        n_ids = off_seq + len(banned_sequences) * width
+        self._ids_dev[:n_ids].copy_(self._ids_host[:n_ids], non_blocking=True)
+        self.cancel_flag.zero_()
+        self._mirror_np[:] = 0
+        if cancellation is not None:
+            cancellation._attach_flag(self.cancel_flag)
+        lib = _lib.load()
+        _lib.check(lib.aiosb_group_begin(ctypes.byref(self.ptrs), prefix_logits.data_ptr(), seed & (2**64 - 1),
+                                         attempts, attempts, self._stream()), "group_begin")
+        launched = 0
+        for step in range(max_new_tokens):
+            if cancellation is not None and cancellation.cancelled:
+                break
+            if step >= 2:
+                # keep <= 2 steps queued; stop once the device reports completion
+                while int(self._mirror_np[0]) < step - 1 and not int(self._mirror_np[1]):
+                    time.sleep(0)
+                if int(self._mirror_np[1]):
+                    break
+            if step + 1 < max_new_tokens:
+                graph.replay()
+            else:
+                _lib.check(lib.aiosb_group_step(ctypes.byref(self.ptrs), attempts, self.vocab, self._top_k_cap,
+                                                self._stream()), "group_step")
+            launched += 1
+        # [rows, steps] arrays use the round's max_new_tokens as their row stride
+        n = attempts * max_new_tokens
+        self._res_ids.view(-1)[:n].copy_(self.output_ids.view(-1)[:n], non_blocking=True)
+        self._res_lp.view(-1)[:n].copy_(self.token_logprobs.view(-1)[:n], non_blocking=True)
+        self._res_rows[0, :attempts].copy_(self.counts[:attempts], non_blocking=True)
+        self._res_rows[1, :attempts].copy_(self.stop_codes[:attempts], non_blocking=True)
+        self._res_sums[:attempts].copy_(self.logprob_sums[:attempts], non_blocking=True)
+        self._res_state.copy_(self.state, non_blocking=True)
+        self._done_event.record()
+        self._done_event.synchronize()
+        if cancellation is not None:
+            cancellation._detach_flag(self.cancel_flag)
+        ops.check_status(self.device)
+        final = _lib.GroupState.from_buffer_copy(self._res_state.numpy().tobytes())
+        consumed = int(final.head) - head0
+        cm.advance_head(int(final.head))
+        host_cancelled = cancellation is not None and cancellation.cancelled and launched < max_new_tokens
+        return RoundResult(
+            output_ids=self._res_ids.view(-1)[:n].numpy().reshape(attempts, max_new_tokens).copy(),
+            token_logprobs=self._res_lp.view(-1)[:n].numpy().reshape(attempts, max_new_tokens).copy(),
+            counts=self._res_rows[0, :attempts].tolist(),
+            logprob_sums=self._res_sums[:attempts].tolist(),
+            stop_codes=self._res_rows[1, :attempts].tolist(),
+            pages_consumed=consumed,
+            active_model_tokens=int(final.active_model_tokens),
+            cancelled=bool(final.cancelled) or host_cancelled,
+            steps=int(final.step),
+        )

@@ -53,6 +53,7 @@ extern "C" {
 #define AIOSB_EPI_STORE 0    /* y = x W^T, bf16                                         */
 #define AIOSB_EPI_SILU_MUL 1 /* W rows interleaved in 64-row gate/up blocks;
                                 y[:, f] = silu(x Wg^T) * (x Wu^T), bf16              */
+#define AIOSB_EPI_ADD 2      /* y = residual + bf16(x W^T), bf16 (residual may be y)  */
 
 /* Library version (major*10000 + minor*100 + patch). */
 AIOSB_API int aiosb_version(void);
@@ -60,6 +61,10 @@ AIOSB_API int aiosb_version(void);
 /* Copies the calling thread's last error message (NUL-terminated, truncated to
  * len) and returns its AIOSB_ERR_* code (0 if none). */
 AIOSB_API int aiosb_last_error(char* buf, size_t len);
+
+/* Device address of page-locked host memory (for host-mapped flags the device
+ * polls or writes, e.g. the CandidateGroup cancel flag and progress mirror). */
+AIOSB_API int aiosb_host_device_pointer(void* host, void** device);
 
 /* ---- KV cache scatter ----------------------------------------------------
  * Replaces aios/kernel/store.py:32-61 (store_cache) as called by
@@ -116,11 +121,14 @@ AIOSB_API int aiosb_embedding(const void* ids, int ids_is_int64, int64_t num_tok
  * and aios/layers/embedding.py:34-41 (LMHead.forward): y = x W^T.
  * x: [rows, k] bf16 row-major, row stride k; w: [n, k] bf16 row-major;
  * y: [rows, y_cols] bf16 with row stride y_row_stride, where y_cols = n
- * (AIOSB_EPI_STORE) or n/2 (AIOSB_EPI_SILU_MUL, w rows packed as
- * [gate 0..63 | up 0..63 | gate 64..127 | up 64..127 | ...]).
+ * (AIOSB_EPI_STORE, AIOSB_EPI_ADD) or n/2 (AIOSB_EPI_SILU_MUL, w rows packed
+ * as [gate 0..63 | up 0..63 | gate 64..127 | up 64..127 | ...]). For
+ * AIOSB_EPI_ADD, residual is [rows, >= n] with row stride residual_stride and may
+ * alias y (each element is read before it is written by the same thread).
  * Requires n % 128 == 0, k % 64 == 0, 16-byte aligned x/w/y. */
 AIOSB_API int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
-                 int64_t y_row_stride, int epilogue, int32_t* status, void* stream);
+                           int64_t y_row_stride, int epilogue, const void* residual, int64_t residual_stride,
+                           int32_t* status, void* stream);
 
 /* ---- Attention ---------------------------------------------------------------
  * KV slots: token slot s of one layer lives at k_cache + s * num_kv_heads *
@@ -189,6 +197,11 @@ AIOSB_API int aiosb_sample(const void* logits, int64_t rows, int64_t vocab, int6
                  int64_t n_forbidden, const int64_t* forbidden_rows, int64_t n_forbidden_rows, int64_t* token_out,
                  float* logprob_out, int32_t* status, void* stream);
 
+/* Teacher-forced scoring (aios/ime.py:731, 827-832, 858-860): out[r] =
+ * log_softmax(float(logits[r]))[targets[r]] in fp32. */
+AIOSB_API int aiosb_token_logprobs(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
+                                   const int64_t* targets, float* out, int32_t* status, void* stream);
+
 /* Replaces stateless_uniforms (aios/engine/sample.py:12-45): out[r, t] is the
  * splitmix64 uniform of (seeds[r], t), computed in fp64 and rounded to fp32. */
 AIOSB_API int aiosb_stateless_uniforms(const int64_t* seeds, int64_t rows, int64_t steps, float* out, void* stream);
@@ -256,6 +269,7 @@ typedef struct aiosb_group_ptrs {
   int32_t* seq_lens;          /* [rows]                                             */
   int32_t* out_loc;           /* [rows] KV slot of the decode token                 */
   int32_t* row_page;          /* [rows] current suffix page (page_size > 1)         */
+  int32_t* row_table;         /* [rows] page-table row of each local row            */
   const int32_t* terminal_ids;
   const int32_t* minlen_ids;
   const int32_t* banned;      /* [n_banned, banned_width]                           */
@@ -266,8 +280,8 @@ typedef struct aiosb_group_ptrs {
 } aiosb_group_ptrs;
 
 /* Round start: resets the per-row outputs, copies the prefix logits [vocab] into
- * every row of `logits`, draws the uniform streams of seeds seed_base + r and
- * marks rows [0, attempts) active. */
+ * every row of `logits`, draws the uniform streams of seeds seed_base + r, sets
+ * row_table[r] = row_offset + r and marks rows [0, attempts) active. */
 AIOSB_API int aiosb_group_begin(const aiosb_group_ptrs* g, const void* prefix_logits, uint64_t seed_base, int64_t attempts,
                       int64_t rows, void* stream);
 

@@ -1,0 +1,368 @@
+"""Generates the golden fixtures of tests/golden/ by running the UNMODIFIED
+reference implementation (7155/aios, Python) on the CPU.
+
+The reference's GPU-only pieces are replaced by the smallest possible shims:
+  1. FlashInfer rmsnorm / fused_add_rmsnorm / silu_and_mul -> torch expressions of
+     FlashInfer's arithmetic (fp32 math, one rounding to the storage dtype);
+  2. the attention backend -> a CPU backend that stores K/V in a
+     [2, L, pages, 1, Hkv, d] buffer and calls the reference's own
+     _sdpa_prefill_attention for prefill and decode;
+  3. torch.cuda.Event -> a no-op timer;
+  4. the tokenizer -> aios_b200's SyntheticTokenizer (ids <-> CJK characters).
+Weights are the seeded synthetic weights of the benchmark protocol.
+
+Usage (only where the reference checkout exists; the fixtures are committed):
+    AIOS_REFERENCE=/root/reference/python python tests/golden/make_golden.py
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import os
+import sys
+import types
+from pathlib import Path
+
+import torch
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parents[1]
+REF = Path(os.environ.get("AIOS_REFERENCE", "/root/reference/python"))
+sys.path.insert(0, str(REPO))
+sys.path.insert(0, str(REF))
+
+import flashinfer  # noqa: E402
+
+
+def _fi_rmsnorm(x, w, eps, out=None, **_):
+    xf = x.float()
+    y = (xf * (1.0 / torch.sqrt((xf * xf).mean(-1, keepdim=True) + eps)) * w.float()).to(x.dtype)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def _fi_fused_add_rmsnorm(x, residual, w, eps, **_):
+    s = x.float() + residual.float()
+    residual.copy_(s.to(residual.dtype))
+    x.copy_((s * (1.0 / torch.sqrt((s * s).mean(-1, keepdim=True) + eps)) * w.float()).to(x.dtype))
+
+
+def _fi_silu_and_mul(x, out=None, **_):
+    f = x.shape[-1] // 2
+    g, u = x[..., :f].float(), x[..., f:].float()
+    y = (g / (1.0 + torch.exp(-g)) * u).to(x.dtype)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+flashinfer.rmsnorm = _fi_rmsnorm
+flashinfer.fused_add_rmsnorm = _fi_fused_add_rmsnorm
+flashinfer.silu_and_mul = _fi_silu_and_mul
+
+import aios.core as ref_core  # noqa: E402
+from aios.attention.base import BaseAttentionBackend, BaseAttentionMetadata  # noqa: E402
+from aios.attention.flashinfer import _sdpa_prefill_attention  # noqa: E402
+from aios.engine import sample as ref_sample  # noqa: E402
+from aios.ime import ImeCompletionEngine, ImeGenerationConfig  # noqa: E402
+from aios.models.config import ModelConfig as RefConfig  # noqa: E402
+from aios.models.minimind_ime import BlockAttnResMixer, MiniMindIMEForCausalLM  # noqa: E402
+from aios.scheduler.cache import CacheManager  # noqa: E402
+
+from aios_b200.models import shapes  # noqa: E402
+from aios_b200.models.weight import synthetic_state_dict  # noqa: E402
+from aios_b200.tokenizer import SyntheticTokenizer  # noqa: E402
+
+
+class _Event:
+    def __init__(self, *a, **k):
+        pass
+
+    def record(self, *a, **k):
+        pass
+
+    def synchronize(self):
+        pass
+
+    def elapsed_time(self, other):
+        return 0.0
+
+
+torch.cuda.Event = _Event
+
+
+@dataclasses.dataclass
+class _Meta(BaseAttentionMetadata):
+    cu: torch.Tensor
+
+    def get_last_indices(self, bs):
+        return self.cu[1 : 1 + bs].long() - 1
+
+
+class CpuBackend(BaseAttentionBackend):
+    def __init__(self, config):
+        self.hkv, self.d = config.num_kv_heads, config.head_dim
+        self.scale = config.head_dim**-0.5
+
+    def prepare_metadata(self, batch):
+        cu = torch.tensor([0] + [r.extend_len for r in batch.reqs]).cumsum(0)
+        batch.attn_metadata = _Meta(cu=cu)
+        return batch.attn_metadata
+
+    def forward(self, q, k, v, kv, layer, batch):
+        ctx = ref_core.get_global_ctx()
+        kv.store_kv(k, v, batch.out_loc.view(-1), layer)
+        kc = kv.k_cache(layer).view(-1, self.hkv, self.d)
+        vc = kv.v_cache(layer).view(-1, self.hkv, self.d)
+        outs, off = [], 0
+        for req in batch.reqs:
+            n = req.extend_len
+            idx = ctx.page_table[req.table_idx, : req.device_len].long()
+            outs.append(_sdpa_prefill_attention(q[off : off + n], kc[idx], vc[idx], cached_len=req.cached_len,
+                                                sm_scale=self.scale))
+            off += n
+        return torch.cat(outs).reshape(q.shape[0], -1)
+
+
+class CpuKV:
+    def __init__(self, L, pages, hkv, d, dtype):
+        self.buf = torch.zeros((2, L, pages, 1, hkv, d), dtype=dtype)
+        self._shape = (pages, hkv, d)
+
+    def k_cache(self, i):
+        return self.buf[0, i]
+
+    def v_cache(self, i):
+        return self.buf[1, i]
+
+    def store_kv(self, k, v, loc, layer):
+        self.buf[0, layer].view(self._shape)[loc.long()] = k
+        self.buf[1, layer].view(self._shape)[loc.long()] = v
+
+    @property
+    def dtype(self):
+        return self.buf.dtype
+
+
+def ref_config(cfg, **changes) -> RefConfig:
+    values = {f.name: getattr(cfg, f.name) for f in dataclasses.fields(cfg)}
+    values.update(attnres_backend="eager", **changes)
+    return RefConfig(**values)
+
+
+def build_llm(cfg, dtype, num_pages: int):
+    rcfg = ref_config(cfg)
+    with torch.device("meta"):
+        model = MiniMindIMEForCausalLM(rcfg)
+    state = {k: v.to(dtype) for k, v in synthetic_state_dict(model, seed=0).items()}
+    model.load_state_dict(state)
+    model.model._rotary_emb.set_device(torch.device("cpu"))
+    backend = CpuBackend(rcfg)
+    model.attn_backend = backend
+    model.model.attn_backend = backend
+    for layer in model.model.layers.op_list:
+        layer.self_attn._attn_backend = backend
+    ref_core._GLOBAL_CTX = None
+    ctx = ref_core.Context(page_size=1)
+    ctx.kv_cache = CpuKV(rcfg.num_layers, num_pages, rcfg.num_kv_heads, rcfg.head_dim, dtype)
+    ctx.attn_backend = backend
+    ref_core.set_global_ctx(ctx)
+    return types.SimpleNamespace(
+        model=model, tokenizer=SyntheticTokenizer(rcfg.vocab_size), device=torch.device("cpu"), ctx=ctx,
+        config=rcfg, num_pages=num_pages, cache_manager=CacheManager(torch.device("cpu"), num_pages),
+    )
+
+
+class Recorder:
+    """Hooks that record what the reference engine did, step by step."""
+
+    def __init__(self):
+        self.events = []
+
+    def install(self):
+        rec = self
+        orig_sample = ref_sample.Sampler.sample_with_logprobs
+        orig_decode = ImeCompletionEngine._decode_step
+        orig_branch = ImeCompletionEngine._generate_branch_batch
+
+        def sample(self, logits, **kw):
+            tok, lp = orig_sample(self, logits, **kw)
+            rec.events.append(("sample", tok.squeeze(-1).tolist(), lp.squeeze(-1).tolist()))
+            return tok, lp
+
+        def decode(self, token_ids, page_table, *, cached_len, row_indices):
+            logits, pages = orig_decode(self, token_ids, page_table, cached_len=cached_len, row_indices=row_indices)
+            rec.events.append(("decode", token_ids.tolist(), cached_len, row_indices.tolist(), pages.tolist()))
+            return logits, pages
+
+        def branch(self, **kw):
+            rec.events.append(("round", dict(
+                row_offset=kw["row_offset"], attempts=kw["attempts"], seed=kw["seed"],
+                temperature=kw["temperature"], top_k=kw["top_k"], top_p=kw["top_p"],
+                forbidden=[list(s) for s in kw["forbidden_sequences"]],
+            )))
+            return orig_branch(self, **kw)
+
+        ref_sample.Sampler.sample_with_logprobs = sample
+        ImeCompletionEngine._decode_step = decode
+        ImeCompletionEngine._generate_branch_batch = branch
+        import aios.ime as ref_ime
+
+        ref_ime.Sampler = ref_sample.Sampler
+
+    def take(self):
+        out, self.events = self.events, []
+        return out
+
+
+# ---------------------------------------------------------------------------
+# fixtures
+# ---------------------------------------------------------------------------
+SAMPLER_CASES = [
+    dict(temperature=0.8, top_k=50, top_p=0.9),
+    dict(temperature=0.75, top_k=96, top_p=0.95),
+    dict(temperature=0.35, top_k=50, top_p=1.0),
+    dict(temperature=0.9, top_k=-1, top_p=0.9),
+    dict(temperature=1.0, top_k=-1, top_p=1.0),
+    dict(temperature=0.5, top_k=1, top_p=1.0),
+    dict(temperature=0.0, top_k=-1, top_p=1.0),
+]
+
+
+def gen_sampler() -> dict:
+    g = torch.Generator().manual_seed(1234)
+    logits = torch.randn(16, 2048, generator=g) * 3.0  # fp32: no ties, tie order irrelevant
+    seeds = [20260814 + i for i in range(16)]
+    uniforms = ref_sample.stateless_uniforms(seeds, 5, torch.device("cpu"))
+    ban_rows = torch.randint(0, 2048, (16, 3), generator=g)
+    out = {"logits": logits, "seeds": seeds, "uniforms": uniforms, "ban_rows": ban_rows, "cases": []}
+    for case in SAMPLER_CASES:
+        sp = ref_core.SamplingParams(**case)
+        s = ref_sample.Sampler(sp)
+        tok, lp = s.sample_with_logprobs(logits, uniforms=uniforms[:, 2], forbidden_token_ids=(3, 7, 11),
+                                         forbidden_token_ids_by_row=ban_rows)
+        out["cases"].append(dict(params=case, tokens=tok.squeeze(-1), logprobs=lp.squeeze(-1)))
+    big = [2**63 - 5, 2**64 - 1, 0, 17, 20260814 + 3 * 100003]
+    out["uniform_seeds"] = big
+    out["uniform_values"] = ref_sample.stateless_uniforms(big, 24, torch.device("cpu"))
+    return out
+
+
+def gen_mixer() -> dict:
+    """the 65-mixer dependency chain of
+    benchmark/profile_attnres.py (banks of depth 1..9 + one partial), [8, 768],
+    N(0,1) sources, query N(0, 0.02), norm weight 1, seed 0, fp32, eager backend."""
+    g = torch.Generator().manual_seed(0)
+    banks = [torch.randn(depth, 8, 768, generator=g) for depth in range(1, 10)]
+    partial = torch.randn(8, 768, generator=g)
+    queries = [torch.randn(768, generator=g) * 0.02 for _ in range(65)]
+    outputs = []
+    idx = 0
+
+    def mix(bank, part):
+        nonlocal idx
+        m = BlockAttnResMixer(768, 1e-6, "eager")
+        m.query = queries[idx].clone()
+        m.key_norm.weight = torch.ones(768)
+        idx += 1
+        return m.forward(bank, part)
+
+    for block in range(8):
+        for layer in range(4):
+            outputs.append(mix(banks[block], None if layer == 0 else partial))
+            outputs.append(mix(banks[block], partial))
+    outputs.append(mix(banks[8], None))
+    stats = torch.stack([torch.stack([o.sum(), o.square().sum(), o.abs().max()]) for o in outputs])
+    keep = [0, 1, 7, 31, 64]
+    return {"keep": keep, "outputs": torch.stack([outputs[i] for i in keep]), "stats": stats}
+
+
+def gen_attention() -> dict:
+    g = torch.Generator().manual_seed(17)
+    cases = []
+    for cached in (0, 2, 9):
+        n = 5
+        q = torch.randn(n, 8, 96, generator=g)
+        k = torch.randn(cached + n, 2, 96, generator=g)
+        v = torch.randn(cached + n, 2, 96, generator=g)
+        out = _sdpa_prefill_attention(q, k, v, cached_len=cached, sm_scale=96**-0.5)
+        cases.append(dict(cached=cached, q=q, k=k, v=v, out=out))
+    return {"cases": cases}
+
+
+def _keystroke(engine, llm, rec, prefix_ids, cfg):
+    text = llm.tokenizer.text_for(prefix_ids[1:])
+    result = engine.complete(text, cfg)
+    events = rec.take()
+    return dict(
+        prefix_ids=prefix_ids,
+        events=events,
+        page_table=llm.ctx.page_table.clone(),
+        free_after=llm.cache_manager._free_slots.clone(),
+        prefix_logits=engine._prefix_logits.float().clone(),
+        result=dict(
+            candidates=[c.text for c in result.candidates],
+            raw=[(c.text, c.token_count, c.average_logprob, c.base_score, c.stop_reason, c.invalid_reasons)
+                 for c in result.raw_candidates],
+            sampling_attempts=result.sampling_attempts, generated_tokens=result.generated_tokens,
+            active_model_tokens=result.active_model_tokens, unique_kv_pages=result.unique_kv_pages,
+            reused_prefix_tokens=result.reused_prefix_tokens, refill_rounds=result.refill_rounds,
+            refill_stop_reason=result.refill_stop_reason,
+        ),
+    )
+
+
+def gen_model(name: str, cfg, dtype, rec: Recorder) -> dict:
+    """A reduced-depth model of a benchmark shape: one keystroke stream through
+    the reference engine (prefill, LCP extension, identical repeat, backspace),
+    plus a refill run and a greedy run."""
+    llm = build_llm(cfg, dtype, num_pages=1024)
+    engine = ImeCompletionEngine(llm)
+    rec.take()  # drop events of earlier fixtures
+    g = torch.Generator().manual_seed(0)
+    base = [1] + torch.randint(10, cfg.vocab_size, (14,), generator=g).tolist()
+    sampled = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=8, refill_batch_size=8,
+                                  max_new_tokens=6, temperature=0.8, seed=0)
+    keystrokes = []
+    for ids in (base[:11], base[:13], base[:13], base[:12], base):
+        keystrokes.append(_keystroke(engine, llm, rec, ids, sampled))
+    refill = ImeGenerationConfig(sampling_attempts=4, max_sampling_attempts=12, refill_batch_size=4,
+                                 min_refill_batch_size=2, max_new_tokens=5, temperature=0.8, seed=5)
+    keystrokes.append(_keystroke(engine, llm, rec, base[:9], refill))
+    greedy = ImeGenerationConfig(sampling_attempts=4, max_sampling_attempts=4, refill_batch_size=4,
+                                 max_new_tokens=6, temperature=1.0, top_k=1, top_p=1.0, min_new_tokens=0, seed=2)
+    keystrokes.append(_keystroke(engine, llm, rec, base[:10], greedy))
+    return {"name": name, "config": {f.name: getattr(cfg, f.name) for f in dataclasses.fields(cfg)},
+            "dtype": str(dtype), "num_pages": 1024,
+            "configs": {"sampled": dataclasses.asdict(sampled), "refill": dataclasses.asdict(refill),
+                        "greedy": dataclasses.asdict(greedy)},
+            "keystrokes": keystrokes}
+
+
+def reduced(cfg, layers: int, **extra):
+    return dataclasses.replace(cfg, num_layers=layers, **extra)
+
+
+def main() -> None:
+    torch.manual_seed(0)
+    rec = Recorder()
+    rec.install()
+    torch.save(gen_sampler(), HERE / "sampler.pt")
+    torch.save(gen_mixer(), HERE / "mixer.pt")
+    torch.save(gen_attention(), HERE / "attention.pt")
+    models = {
+        "s10_l2_fp32": (reduced(shapes.S10, 2), torch.float32),
+        "s10_l2_bf16": (reduced(shapes.S10, 2), torch.bfloat16),
+        "s06_l2_fp32": (reduced(shapes.S06, 2), torch.float32),
+        "s21_l4_fp32": (reduced(shapes.S21, 4, attnres_num_blocks=2), torch.float32),
+    }
+    for key, (cfg, dtype) in models.items():
+        torch.save(gen_model(key, cfg, dtype, rec), HERE / f"model_{key}.pt")
+        print("wrote", key)
+
+
+if __name__ == "__main__":
+    main()
