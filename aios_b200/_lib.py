@@ -195,5 +195,20 @@ def check(rc: int, what: str) -> None:
     raise RuntimeError(msg or f"{what}: launch failed ({rc})")
 
 
+# Entry points that launch kernels; `launches` counts their successful calls
+# (the bench reports it as the number of this library's kernel launches).
+_NON_LAUNCHING = frozenset({"aiosb_version", "aiosb_last_error", "aiosb_host_device_pointer",
+                            "aiosb_prefill_tile_tokens"})
+launches = 0
+
+
 def call(name: str, *args) -> None:
+    global launches
     check(getattr(load(), name)(*args), name)
+    if name not in _NON_LAUNCHING:
+        launches += 1
+
+
+def count_launches(n: int = 1) -> None:
+    global launches
+    launches += n

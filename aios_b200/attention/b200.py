@@ -55,6 +55,7 @@ class B200AttentionMetadata(BaseAttentionMetadata):
 
 def _to_device_i32(values: list[int], device: torch.device) -> torch.Tensor:
     host = torch.tensor(values, dtype=torch.int32).pin_memory()
+    ops.transfer_bytes["h2d"] += 4 * len(values)
     return host.to(device, non_blocking=True)
 
 

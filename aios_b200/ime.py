@@ -217,6 +217,8 @@ class ImeCompletionEngine:
         started.record()
         cancelled = False
         cm = self.llm.cache_manager
+        # a fresh table per keystroke, as the reference allocates one (aios/ime.py:482-485)
+        self._page_table[:max_attempts].zero_()
         prefix_logits, prefix_pages, reused = self._prepare_prefix(token_ids, max_attempts)
         peak_unique_pages = len(prefix_pages)
         raw_candidates: list[ImeCandidate] = []
@@ -380,6 +382,7 @@ class ImeCompletionEngine:
         batch = Batch(reqs=[req], phase="prefill")
         host = torch.tensor([*token_ids[cached_len:], *range(cached_len, len(token_ids))], dtype=torch.int32)
         staged = host.pin_memory().to(dev, non_blocking=True)
+        ops.transfer_bytes["h2d"] += 4 * host.numel()
         new = len(token_ids) - cached_len
         batch.input_ids = staged[:new]
         batch.positions = staged[new:]

@@ -16,6 +16,10 @@ from .. import _lib
 
 _STATUS: dict[int, torch.Tensor] = {}
 
+# Bytes the host side stages to / from the device outside the runtime's own
+# counters (prefill ids, attention metadata); read by the benchmark.
+transfer_bytes = {"h2d": 0, "d2h": 0}
+
 
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream

@@ -130,7 +130,18 @@ class CandidateGroupRuntime:
             status=ops.status_word(dev).data_ptr(),
         )
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._graph_launches: dict[int, int] = {}
+        self.h2d_bytes = 0  # host->device bytes copied by rounds (bench accounting)
+        self.d2h_bytes = 0
         self._pool = None
+        # When `record` is set, every round's parameters and results are kept in
+        # `rounds` (used by parity tests to replay the round on the CPU oracle).
+        self.record = False
+        self.rounds: list[tuple[dict, RoundResult]] = []
+        # With `record_logits`, each round also keeps the logits every step sampled
+        # from ([attempts, vocab] fp32 per step; synchronises after every step).
+        self.record_logits = False
+        self.step_logits: list[torch.Tensor] = []
         self._top_k_cap = 2048
 
     # ------------------------------------------------------------------ graphs
@@ -151,10 +162,11 @@ class CandidateGroupRuntime:
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
 
+    def _group_step(self, rows: int) -> None:
+        _lib.call("aiosb_group_step", ctypes.byref(self.ptrs), rows, self.vocab, self._top_k_cap, self._stream())
+
     def _step_and_forward(self, rows: int, batch: Batch) -> None:
-        lib = _lib.load()
-        _lib.check(lib.aiosb_group_step(ctypes.byref(self.ptrs), rows, self.vocab, self._top_k_cap, self._stream()),
-                   "group_step")
+        self._group_step(rows)
         with self.llm.ctx.forward_batch(batch):
             self.llm.model.forward()
 
@@ -171,8 +183,11 @@ class CandidateGroupRuntime:
         self._step_and_forward(rows, batch)
         torch.cuda.synchronize(self.device)
         graph = torch.cuda.CUDAGraph()
+        before = _lib.launches
         with torch.cuda.graph(graph, pool=self._pool):
             self._step_and_forward(rows, batch)
+        self._graph_launches[rows] = _lib.launches - before
+        _lib.launches = before
         if self._pool is None:
             self._pool = graph.pool()
         torch.cuda.synchronize(self.device)
@@ -244,10 +259,14 @@ class CandidateGroupRuntime:
         self._mirror_np[:] = 0
         if cancellation is not None:
             cancellation._attach_flag(self.cancel_flag)
-        lib = _lib.load()
-        _lib.check(lib.aiosb_group_begin(ctypes.byref(self.ptrs), prefix_logits.data_ptr(), seed & (2**64 - 1),
-                                         attempts, attempts, self._stream()), "group_begin")
+        _lib.call("aiosb_group_begin", ctypes.byref(self.ptrs), prefix_logits.data_ptr(), seed & (2**64 - 1),
+                  attempts, attempts, self._stream())
+        self.h2d_bytes += self._state_host.numel() + 4 * n_ids
         launched = 0
+        step_logits: list[torch.Tensor] = []
+        if self.record_logits:
+            torch.cuda.synchronize(self.device)
+            step_logits.append(prefix_logits.float().cpu().expand(attempts, -1).clone())
         for step in range(max_new_tokens):
             if cancellation is not None and cancellation.cancelled:
                 break
@@ -259,9 +278,12 @@ class CandidateGroupRuntime:
                     break
             if step + 1 < max_new_tokens:
                 graph.replay()
+                _lib.count_launches(self._graph_launches[attempts])
+                if self.record_logits:
+                    torch.cuda.synchronize(self.device)
+                    step_logits.append(self.logits[:attempts].float().cpu())
             else:
-                _lib.check(lib.aiosb_group_step(ctypes.byref(self.ptrs), attempts, self.vocab, self._top_k_cap,
-                                                self._stream()), "group_step")
+                self._group_step(attempts)
             launched += 1
         # [rows, steps] arrays use the round's max_new_tokens as their row stride
         n = attempts * max_new_tokens
@@ -271,6 +293,7 @@ class CandidateGroupRuntime:
         self._res_rows[1, :attempts].copy_(self.stop_codes[:attempts], non_blocking=True)
         self._res_sums[:attempts].copy_(self.logprob_sums[:attempts], non_blocking=True)
         self._res_state.copy_(self.state, non_blocking=True)
+        self.d2h_bytes += 8 * n + 12 * attempts + self._res_state.numel()
         self._done_event.record()
         self._done_event.synchronize()
         if cancellation is not None:
@@ -280,7 +303,7 @@ class CandidateGroupRuntime:
         consumed = int(final.head) - head0
         cm.advance_head(int(final.head))
         host_cancelled = cancellation is not None and cancellation.cancelled and launched < max_new_tokens
-        return RoundResult(
+        result = RoundResult(
             output_ids=self._res_ids.view(-1)[:n].numpy().reshape(attempts, max_new_tokens).copy(),
             token_logprobs=self._res_lp.view(-1)[:n].numpy().reshape(attempts, max_new_tokens).copy(),
             counts=self._res_rows[0, :attempts].tolist(),
@@ -291,3 +314,11 @@ class CandidateGroupRuntime:
             cancelled=bool(final.cancelled) or host_cancelled,
             steps=int(final.step),
         )
+        if self.record:
+            self.rounds.append((dict(
+                prefix_len=prefix_len, row_offset=row_offset, attempts=attempts, max_new_tokens=max_new_tokens,
+                min_new_tokens=min_new_tokens, seed=seed, temperature=temperature, top_k=top_k, top_p=top_p,
+                banned_sequences=[list(x) for x in banned_sequences], ban_min_prefix=ban_min_prefix,
+                head=head0, step_logits=step_logits,
+            ), result))
+        return result

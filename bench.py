@@ -1,0 +1,420 @@
+"""Benchmark of the B200 CandidateGroup keystroke (one JSON line on rank 0).
+
+Workload (one "step" = one keystroke through the public API
+``ImeCompletionEngine.complete``): the 0.1B-shaped MiniMind-IME model (S10: 14
+layers, hidden 768, 12 q / 4 kv heads of 64, vocab 16384) with seeded random
+weights, a fresh [BOS] + 12-token prefix per keystroke (ids uniform over the
+CJK range, seeded), 8 candidates x 12 decode tokens at temperature 0.8,
+top-k 50, top-p 0.9, one round (no refill), KV in 16-token pages of a 256-page
+pool. Every keystroke prefills its prefix from scratch and streams the 201 MB of
+weights once per decode step, so the working set exceeds the 126 MB L2.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+``--impl reference`` times the CPU restatement of the reference algorithm
+(oracle/, fp32, all host cores) on the same workload. With N > 1 (torchrun)
+every GPU serves an independent keystroke stream (replicas; no data exchange);
+the barrier and the max-over-ranks timing use a small NCCL all-reduce.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+HBM_FALLBACK_GBS = 6650.0
+
+
+def percentile(values, q):
+    ordered = sorted(values)
+    return ordered[max(0, min(len(ordered) - 1, math.ceil(q * len(ordered)) - 1))]
+
+
+def measured_peaks() -> dict:
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples: list[list[str]] = []
+        self._proc = None
+
+    def __enter__(self):
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._thread = threading.Thread(target=self._read, daemon=True)
+            self._thread.start()
+        except OSError:
+            self._proc = None
+        return self
+
+    def _read(self):
+        for line in self._proc.stdout:
+            self.samples.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+
+    def summary(self) -> dict:
+        rows = [s for s in self.samples if len(s) >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [v for v in (num(r[0]) for r in rows) if v is not None]
+        reasons = set()
+        for r in rows:
+            for name, col in (("hw_slowdown", 4), ("hw_thermal_slowdown", 5), ("sw_thermal_slowdown", 6),
+                              ("sw_power_cap", 7)):
+                if r[col].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][1]),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+WORKLOAD = ("S10 keystroke: [BOS]+12 prefix, 8 candidates x 12 tokens, T=0.8 top-k 50 top-p 0.9, "
+            "one round, 16-token pages x 256")
+
+
+def keystroke_config():
+    from aios_b200 import ImeGenerationConfig
+
+    return ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=8, refill_batch_size=8,
+                               max_new_tokens=12, temperature=0.8, top_k=50, top_p=0.9, seed=0)
+
+
+def prefixes(tokenizer, vocab: int, count: int, seed: int) -> list[str]:
+    g = torch.Generator().manual_seed(seed)
+    return [tokenizer.text_for(torch.randint(10, vocab, (12,), generator=g).tolist()) for _ in range(count)]
+
+
+# ---------------------------------------------------------------------------
+# CPU arm (oracle restatement of the reference algorithm)
+# ---------------------------------------------------------------------------
+def run_cpu(keystrokes: int, warmup: int) -> dict:
+    """Times the oracle keystroke (fp32, all host threads) on the bench workload."""
+    from aios_b200.models import shapes
+    from aios_b200.models.minimind_ime import MiniMindIMEForCausalLM
+    from aios_b200.models.weight import synthetic_state_dict
+    from aios_b200.tokenizer import SyntheticTokenizer
+    from oracle.engine import OracleEngine
+    from oracle.model import OracleModel
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = shapes.S10
+    with torch.device("meta"):
+        meta = MiniMindIMEForCausalLM(cfg)
+    model = OracleModel(cfg, synthetic_state_dict(meta, seed=0), dtype=torch.float32, num_slots=256 * 16)
+    tok = SyntheticTokenizer(cfg.vocab_size)
+    eng = OracleEngine(model, tok, num_pages=256, page_size=16)
+    kc = keystroke_config()
+    texts = prefixes(tok, cfg.vocab_size, warmup + keystrokes, seed=1234)
+    times = []
+    for i, text in enumerate(texts):
+        ids = [1, *tok.encode(text)]
+        eng.reset_prefix()
+        t0 = time.perf_counter()
+        logits, _, _ = eng.prepare_prefix(ids, kc.max_sampling_attempts)
+        tr = eng.run_round(prefix_logits=logits, prefix_len=len(ids), row_offset=0, attempts=8,
+                           max_new_tokens=kc.max_new_tokens, min_new_tokens=kc.min_new_tokens, seed=kc.seed,
+                           temperature=kc.temperature, top_k=kc.top_k, top_p=kc.top_p)
+        eng.release(tr.allocated)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    return {"value": len(times) / total, "unit": "keystrokes/s", "cores": threads, "kind": "port",
+            "p50_ms": statistics.median(times) * 1e3,
+            "sample": f"{len(times)} keystrokes of the bench workload (fp32, oracle restatement, "
+                      f"{threads} threads), {total:.1f} s"}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def decode_linear_roofline(llm, peaks: dict) -> dict:
+    """Times the tcgen05 GEMM launches of one decode step (8 rows: 14 x
+    {qkv, o, gate_up+SwiGLU, down} + LM head, the same shapes and weights as the
+    keystroke) as a captured graph, with CUDA events on the launching stream."""
+    from aios_b200 import _lib
+    from aios_b200.kernel import ops
+
+    dev = llm.device
+    cfg = llm.config
+    rows = 8
+    layers = llm.model.model.layers.op_list
+    x768 = torch.randn(rows, cfg.hidden_size, device=dev).to(torch.bfloat16)
+    xo = torch.randn(rows, cfg.num_qo_heads * cfg.head_dim, device=dev).to(torch.bfloat16)
+    xf = torch.randn(rows, cfg.intermediate_size, device=dev).to(torch.bfloat16)
+    outs = {}
+
+    def run():
+        for i, layer in enumerate(layers):
+            a, m = layer.self_attn, layer.mlp
+            outs["qkv"] = ops.linear(x768, a.qkv_proj.weight)
+            outs["o"] = ops.linear(xo, a.o_proj.weight)
+            outs["gu"] = ops.linear(x768, m.gate_up_proj.packed_weight(), epilogue=_lib.EPI_SILU_MUL)
+            outs["d"] = ops.linear(xf, m.down_proj.weight)
+        outs["lm"] = ops.linear(x768, llm.model.model.embed_tokens.weight)
+
+    run()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run()
+    for _ in range(3):
+        g.replay()
+    iters = 50
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    start.record(stream)
+    for _ in range(iters):
+        g.replay()
+    end.record(stream)
+    end.synchronize()
+    ms = start.elapsed_time(end) / iters
+    launches = 4 * len(layers) + 1
+    wbytes = sum(layer.self_attn.qkv_proj.weight.numel() + layer.self_attn.o_proj.weight.numel()
+                 + layer.mlp.gate_up_proj.weight.numel() + layer.mlp.down_proj.weight.numel() for layer in layers)
+    wbytes = 2 * (wbytes + llm.model.model.embed_tokens.weight.numel())
+    achieved = wbytes / (ms * 1e-3) / 1e9
+    peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
+    return {"bound": "hbm", "kernel": "gemm_tc_kernel (decode linears, 8 rows)", "achieved": round(achieved, 1),
+            "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": None, "algorithmic_bytes_per_step": wbytes,
+            "launches_per_step": launches, "us_per_step": round(ms * 1e3, 2),
+            "us_per_launch": round(ms * 1e3 / launches, 3)}
+
+
+def mixer_chain(dev) -> dict:
+    """BASELINE config 1 on the GPU: 65-mixer chain (banks of depth 1..9 + partial,
+    [8, 768] bf16) and a bandwidth point at 32768 rows (sources >> L2)."""
+    from aios_b200.kernel import ops
+
+    g = torch.Generator(device=dev).manual_seed(0)
+    banks = [torch.randn(d, 8, 768, generator=g, device=dev).to(torch.bfloat16) for d in range(1, 10)]
+    partial = torch.randn(8, 768, generator=g, device=dev).to(torch.bfloat16)
+    wq = [torch.randn(768, generator=g, device=dev) * 0.02 for _ in range(65)]
+    out = torch.empty(8, 768, dtype=torch.bfloat16, device=dev)
+
+    def chain():
+        i = 0
+        for b in range(8):
+            for layer in range(4):
+                ops.b200_attnres_mix(banks[b], None if layer == 0 else partial, wq[i], 1e-6, output_buffer=out)
+                ops.b200_attnres_mix(banks[b], partial, wq[i + 1], 1e-6, output_buffer=out)
+                i += 2
+        ops.b200_attnres_mix(banks[8], None, wq[64], 1e-6, output_buffer=out)
+
+    chain()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        chain()
+    for _ in range(3):
+        graph.replay()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    s.record()
+    for _ in range(20):
+        graph.replay()
+    e.record()
+    e.synchronize()
+    chain_us = s.elapsed_time(e) / 20 * 1e3
+    chain_bytes = 0
+    for b in range(8):
+        d = b + 1
+        chain_bytes += (d * 8 * 768 * 2 + 8 * 768 * 2 + 768 * 4)  # layer 0 of the block: no partial
+        chain_bytes += 7 * ((d + 1) * 8 * 768 * 2 + 8 * 768 * 2 + 768 * 4)
+    chain_bytes += 9 * 8 * 768 * 2 + 8 * 768 * 2 + 768 * 4
+    n = 32768
+    big = torch.randn(8, n, 768, generator=g, device=dev).to(torch.bfloat16)
+    bp = torch.randn(n, 768, generator=g, device=dev).to(torch.bfloat16)
+    bo = torch.empty(n, 768, dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        ops.b200_attnres_mix(big, bp, wq[0], 1e-6, output_buffer=bo)
+    torch.cuda.synchronize(dev)
+    s.record()
+    for _ in range(20):
+        ops.b200_attnres_mix(big, bp, wq[0], 1e-6, output_buffer=bo)
+    e.record()
+    e.synchronize()
+    big_ms = s.elapsed_time(e) / 20
+    big_bytes = 9 * n * 768 * 2 + n * 768 * 2 + 768 * 4
+    return {"chain65_us": round(chain_us, 2), "chain65_gbs": round(chain_bytes / (chain_us * 1e-6) / 1e9, 1),
+            "n32768_gbs": round(big_bytes / (big_ms * 1e-3) / 1e9, 1)}
+
+
+def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
+    import torch.distributed as dist
+
+    from aios_b200 import ImeCompletionEngine, LLM, _lib
+    from aios_b200.kernel import ops
+    from aios_b200.models import shapes
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    llm = LLM(config=shapes.S10, seed=0, page_size=16, num_pages=256, device=f"cuda:{local_rank}")
+    engine = ImeCompletionEngine(llm)
+    cfg = keystroke_config()
+    texts = prefixes(llm.tokenizer, llm.config.vocab_size, args.warmup + args.steps, seed=1234 + rank)
+    for text in texts[: args.warmup]:
+        engine.reset_prefix_cache()
+        engine.complete(text, cfg)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    rt = engine._runtime
+    h2d0 = rt.h2d_bytes + ops.transfer_bytes["h2d"]
+    d2h0 = rt.d2h_bytes + ops.transfer_bytes["d2h"]
+    launches0 = _lib.launches
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    results = []
+    with ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else 0) as clocks:
+        torch.cuda.synchronize(dev)
+        wall0 = time.perf_counter()
+        torch.cuda.nvtx.range_push("timed")
+        start.record(stream)
+        for text in texts[args.warmup :]:
+            engine.reset_prefix_cache()
+            results.append(engine.complete(text, cfg))
+        end.record(stream)
+        torch.cuda.nvtx.range_pop()
+        end.synchronize()
+        wall = time.perf_counter() - wall0
+    device_ms = start.elapsed_time(end)
+    launches = _lib.launches - launches0
+    h2d = (rt.h2d_bytes + ops.transfer_bytes["h2d"] - h2d0) / args.steps
+    d2h = (rt.d2h_bytes + ops.transfer_bytes["d2h"] - d2h0) / args.steps
+    t = torch.tensor([device_ms, wall], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    device_ms, wall = float(t[0]), float(t[1])
+    if rank != 0:
+        return None
+    peaks = measured_peaks()
+    roof = None if args.no_extras else decode_linear_roofline(llm, peaks)
+    mixer = None if args.no_extras else mixer_chain(dev)
+    lat = [r.latency_ms for r in results]
+    gpu_lat = [r.gpu_latency_ms for r in results]
+    gen = sum(r.generated_tokens for r in results)
+    active = sum(r.active_model_tokens for r in results)
+    line = {
+        "metric": "Top-3 keystroke latency p50/p95 ms (8 cand), decode tok/s, mixer HBM GB/s",
+        "value": round(world * args.steps / (device_ms * 1e-3), 3),
+        "unit": "keystrokes/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(device_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded random weights, seeded prefixes, synthetic tokenizer)",
+        "config": {"workload": WORKLOAD, "model": "MiniMind-IME 0.1B shape (S10)", "prefix_tokens": 13,
+                   "candidates": 8, "max_new_tokens": 12, "page_size": 16, "num_pages": 256,
+                   "l2": "inputs larger than L2: every decode step streams the 201 MB of weights",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "latency_ms": {"p50": round(statistics.median(lat), 3), "p95": round(percentile(lat, 0.95), 3),
+                       "gpu_p50": round(statistics.median(gpu_lat), 3),
+                       "gpu_p95": round(percentile(gpu_lat, 0.95), 3)},
+        "decode_tok_s": round(world * gen / (device_ms * 1e-3), 1),
+        "active_model_tok_s": round(active / (sum(gpu_lat) * 1e-3), 1),
+        "mixer": mixer,
+        "e2e": {"value": round(world * args.steps / wall, 3), "unit": "keystrokes/s",
+                "h2d_bytes_per_step": int(round(h2d)), "d2h_bytes_per_step": int(round(d2h))},
+        "gpu_launches": launches,
+        "roofline": roof,
+        "clocks": clocks.summary(),
+    }
+    return line
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-sample", type=int, default=15, help="keystrokes timed for the CPU baseline (0: skip)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the roofline / mixer micro-benchmarks (profiling runs of the keystroke only)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cpu = run_cpu(args.steps, args.warmup)
+        print(json.dumps({
+            "impl": "reference",
+            "metric": "Top-3 keystroke latency p50/p95 ms (8 cand), decode tok/s, mixer HBM GB/s",
+            "value": round(cpu["value"], 4), "unit": "keystrokes/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1000.0 / cpu["value"], 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+            "config": {"workload": WORKLOAD},
+            "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": round(cpu["value"], 4), "unit": "keystrokes/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+        }))
+        return
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+    line = run_gpu(args, rank, world, local_rank)
+    if rank == 0 and line is not None:
+        if world == 1 and args.cpu_sample > 0:
+            cpu = run_cpu(args.cpu_sample, 1)
+            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

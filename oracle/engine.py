@@ -38,6 +38,8 @@ class StepTrace:
     logprobs: list[float]  # raw logprob of `tokens` under the oracle logits
     margins: list[float]  # CDF-boundary / top-2 margin of the oracle draw
     slots: list[int] = field(default_factory=list)  # decode slots allocated after this step
+    ext_tokens: list[int] | None = None  # draw from external (GPU) logits, if given
+    logits: torch.Tensor | None = None  # oracle logits of the active rows
 
 
 @dataclass
@@ -142,6 +144,7 @@ class OracleEngine:
         ban_min_prefix: int = 2,
         forced: dict | None = None,
         forced_steps: list[list[int]] | None = None,
+        external_logits: list[torch.Tensor] | None = None,
     ) -> RoundTrace:
         eos, pad = self.tok.eos_token_id, self.tok.pad_token_id
         S = max_new_tokens
@@ -171,6 +174,11 @@ class OracleEngine:
                     by_row.append(ids)
                 by_row = torch.tensor(by_row)
             batch_logits = torch.stack([logits[r] for r in active])
+            ext = None
+            if external_logits is not None:
+                # also draw from logits produced elsewhere (the GPU's, same step and
+                # rows), to check the sampling + bookkeeping logic bit for bit
+                ext = external_logits[step][active].to(torch.bfloat16)
             u = uniforms[active, step]
             own, lp_own = osamp.sample_with_logprobs(
                 batch_logits, temperature=temperature, top_k=top_k, top_p=top_p, uniforms=u,
@@ -178,6 +186,14 @@ class OracleEngine:
                 tie_order=self.tie_order,
             )
             own = own.squeeze(-1).tolist()
+            ext_tokens = None
+            if ext is not None:
+                et, _ = osamp.sample_with_logprobs(
+                    ext, temperature=temperature, top_k=top_k, top_p=top_p, uniforms=u,
+                    forbidden_token_ids=minlen if step < min_new_tokens else (), forbidden_token_ids_by_row=by_row,
+                    tie_order=self.tie_order,
+                )
+                ext_tokens = et.squeeze(-1).tolist()
             raw = torch.log_softmax(batch_logits.float(), dim=-1)
             if osamp.is_greedy(temperature, top_k, top_p):
                 top2 = batch_logits.float().topk(2, dim=-1).values
@@ -192,7 +208,8 @@ class OracleEngine:
             elif forced_steps is not None:
                 toks = list(forced_steps[step])  # tokens of the active rows, in active order
             lps = [float(raw[i, t]) for i, t in enumerate(toks)]
-            trace = StepTrace(step=step, rows=list(active), own=own, tokens=toks, logprobs=lps, margins=margins)
+            trace = StepTrace(step=step, rows=list(active), own=own, tokens=toks, logprobs=lps, margins=margins,
+                              ext_tokens=ext_tokens, logits=batch_logits)
             steps.append(trace)
             finished = []
             for i, r in enumerate(active):

@@ -1,0 +1,165 @@
+"""CPU tests of the host-side engine logic: the same known answers the
+reference pins in tests/test_ime.py and tests/test_ime_attnres.py, run against
+aios_b200 (candidate keys, terminal truncation, filters, MMR, LCP, config
+validation, pool statistics, adaptive refill, AttnRes config gates and
+checkpoint names)."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from aios_b200 import (
+    ImeGenerationConfig,
+    adaptive_refill_attempts,
+    candidate_pool_stats,
+    token_longest_common_prefix,
+    truncate_at_terminal,
+)
+from aios_b200.ime import ImeCandidate, candidate_key, invalid_reasons, ngram_similarity, select_top_candidates
+from aios_b200.models.config import ModelConfig
+
+
+def candidate(text: str, score: float) -> ImeCandidate:
+    return ImeCandidate(text=text, token_count=3, average_logprob=score, base_score=score, selection_score=score,
+                        stop_reason="eos", invalid_reasons=())
+
+
+def invalid_candidate(text: str, reason: str = "unfinished_fragment") -> ImeCandidate:
+    return ImeCandidate(text=text, token_count=2, average_logprob=-0.1, base_score=float("-inf"),
+                        selection_score=float("-inf"), stop_reason="max_new_tokens", invalid_reasons=(reason,))
+
+
+def test_candidate_key_collapses_display_punctuation() -> None:
+    assert candidate_key(" 我晚点回复。 ") == candidate_key("我晚点回复")
+
+
+def test_decoded_terminal_recovers_first_complete_sentence() -> None:
+    text, stopped = truncate_at_terminal("我马上处理好。后面的句子不应显示")
+    assert stopped and text == "我马上处理好。"
+    phrase, stopped = truncate_at_terminal("我先确认一下，再回复你")
+    assert not stopped and phrase == "我先确认一下，再回复你"
+
+
+def test_invalid_reasons_reject_empty_assistant_and_repeat() -> None:
+    config = ImeGenerationConfig()
+    assert invalid_reasons("", config) == ("empty",)
+    assert "assistant_template" in invalid_reasons("作为一个AI，我建议", config)
+    assert "repeated_ngram" in invalid_reasons("好的好的好的", config)
+    assert "unfinished_fragment" in invalid_reasons("我晚点再", config)
+    assert "boundary_repeat" in invalid_reasons("好好休息", config, prefix="你好")
+    assert "too_short" in invalid_reasons("好", config)
+    assert "too_long" in invalid_reasons("好" * 40, ImeGenerationConfig(max_candidate_chars=32))
+
+
+def test_boundary_repeat_allows_natural_word_boundary() -> None:
+    assert "boundary_repeat" not in invalid_reasons("天气有点热，我先喝点水", ImeGenerationConfig(), prefix="今天")
+
+
+def test_mmr_selection_keeps_quality_and_diversity() -> None:
+    items = [
+        candidate("我晚点给你发消息", -0.10),
+        candidate("我晚一点给你发消息", -0.11),
+        candidate("等我回来再联系你", -0.16),
+        candidate("处理完以后回复你", -0.18),
+    ]
+    texts = [item.text for item in select_top_candidates(items, count=3, diversity_lambda=0.8)]
+    assert texts[0] == "我晚点给你发消息"
+    assert "等我回来再联系你" in texts
+    assert "处理完以后回复你" in texts
+
+
+def test_ngram_similarity_is_bounded() -> None:
+    assert 0.0 < ngram_similarity("我晚点回复你", "我晚一点回复你") < 1.0
+
+
+def test_token_longest_common_prefix_handles_retokenized_tail() -> None:
+    assert token_longest_common_prefix([1, 2, 3, 4], [1, 2, 8]) == 2
+    assert token_longest_common_prefix([1, 2], [1, 2, 3]) == 2
+
+
+def test_generation_config_rejects_invalid_settings() -> None:
+    with pytest.raises(ValueError, match="max_sampling_attempts"):
+        ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=7).validate()
+    with pytest.raises(ValueError, match="min_new_tokens"):
+        ImeGenerationConfig(max_new_tokens=2, min_new_tokens=3).validate()
+    with pytest.raises(ValueError, match="temperatures must be positive"):
+        ImeGenerationConfig(temperature=0.0).validate()
+
+
+def test_candidate_pool_stats_count_invalid_and_display_duplicates() -> None:
+    items = [candidate("我马上回去", -0.1), candidate("我马上回去。", -0.2), candidate("我晚点回去", -0.3),
+             invalid_candidate("我等会再")]
+    stats = candidate_pool_stats(items)
+    assert (stats.attempts, stats.valid_candidates, stats.valid_unique_candidates) == (4, 3, 2)
+    assert (stats.invalid_candidates, stats.duplicate_candidates) == (1, 1)
+
+
+def test_adaptive_refill_scales_with_filtered_unique_yield() -> None:
+    config = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=24, refill_batch_size=8)
+    duplicate_heavy = [candidate("我马上回去", -0.1)] * 4 + [invalid_candidate(f"坏候选{i}") for i in range(4)]
+    assert adaptive_refill_attempts(duplicate_heavy, config, 8) == 8
+    two_unique = [candidate("我马上回去", -0.1), candidate("我晚点回去", -0.2),
+                  *[invalid_candidate(f"坏候选{i}") for i in range(6)]]
+    assert adaptive_refill_attempts(two_unique, config, 8) == 4
+    full = [candidate("我马上回去", -0.1), candidate("我晚点回去", -0.2), candidate("我明天回去", -0.3)]
+    assert adaptive_refill_attempts(full, config, 8) == 0
+
+
+def test_adaptive_refill_respects_remaining_attempt_budget() -> None:
+    config = ImeGenerationConfig(max_sampling_attempts=10)
+    assert adaptive_refill_attempts([invalid_candidate(f"坏候选{i}") for i in range(8)], config, 8) == 2
+
+
+def test_refill_schedule_matches_reference_arithmetic() -> None:
+    cfg = ImeGenerationConfig()
+    assert cfg.refill_schedule(1) == (0.75, 96, 0.95)
+    t, k, p = cfg.refill_schedule(2)
+    assert abs(t - 0.85) < 1e-12 and k == 128
+    t, k, _ = cfg.refill_schedule(5)
+    assert t == 0.95 and k == 160
+
+
+def tiny_config(**changes) -> ModelConfig:
+    values = dict(num_layers=8, num_qo_heads=2, num_kv_heads=1, head_dim=64, hidden_size=128, vocab_size=32,
+                  intermediate_size=128, hidden_act="silu", rms_norm_eps=1e-6, rope_theta=100_000.0,
+                  max_position_embeddings=32, tie_word_embeddings=True, model_type="minimind_ime_v3",
+                  architecture_revision="tiny_block_attnres", residual_type="block_attnres", attnres_num_blocks=2,
+                  attnres_alpha=1.0)
+    values.update(changes)
+    return ModelConfig(**values)
+
+
+def test_attnres_config_rejects_partial_migration_and_bad_partition() -> None:
+    with pytest.raises(ValueError, match="alpha=1.0"):
+        tiny_config(attnres_alpha=0.5)
+    with pytest.raises(ValueError, match="divisible"):
+        tiny_config(num_layers=7)
+    with pytest.raises(ValueError, match="b200"):
+        tiny_config(attnres_backend="triton")
+
+
+def test_attnres_model_state_dict_preserves_checkpoint_names() -> None:
+    from aios_b200.models.minimind_ime import MiniMindIMEForCausalLM
+
+    with torch.device("meta"):
+        model = MiniMindIMEForCausalLM(tiny_config())
+    names = set(model.state_dict())
+    assert "model.layers.0.attn_res_mixer.query" in names
+    assert "model.layers.7.mlp_res_mixer.key_norm.weight" in names
+    assert "model.final_attn_res_mixer.query" in names
+    assert "lm_head.weight" not in names
+    assert model.model._layers_per_block == 4
+    assert model.model._num_blocks == 2
+
+
+def test_product_kernels_refuse_cpu_tensors() -> None:
+    """No CPU fallback: every kernel wrapper rejects host tensors."""
+    from aios_b200.kernel import b200_attnres_mix, ops
+
+    with pytest.raises(ValueError, match="CUDA"):
+        b200_attnres_mix(torch.zeros(2, 3, 8), None, torch.zeros(8), 1e-6)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.linear(torch.zeros(2, 64, dtype=torch.bfloat16), torch.zeros(128, 64, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.rmsnorm(torch.zeros(2, 8), torch.ones(8), 1e-6)
