@@ -124,6 +124,9 @@ _SIGNATURES = {
     "aiosb_silu_mul": ([_p, _i64, _i64, _p, _p], _i32),
     "aiosb_embedding": ([_p, _i32, _i64, _p, _i64, _i64, _p, _p, _p], _i32),
     "aiosb_linear": ([_p, _i64, _i64, _p, _i64, _p, _i64, _i32, _p, _i64, _p, _p], _i32),
+    "aiosb_linear_rmsnorm": (
+        [_p, _p, _p, _p, _f32, _i64, _i64, _p, _i64, _p, _i64, _i32, _p, _i64, _p, _p], _i32
+    ),
     "aiosb_attention_decode": (
         [_p, _i64, _p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p,
          _i64, _i64, _i64, _i64, _f32, _p, _i64, _p, _p],

@@ -168,157 +168,186 @@ struct DecodeArgs {
   int32_t* status;
 };
 
+// ---- cascade decode -----------------------------------------------------------
+// CTA (h, r) owns KV head h of candidate row r; the R CTAs of a head form one
+// thread-block cluster. The shared prefix is split into 64-key chunks; chunk c
+// is fetched from HBM once, by CTA c % R, into that CTA's shared memory, and the
+// other rows of the head copy it over distributed shared memory. Each CTA then
+// folds the prefix chunks and its own row's suffix keys into the online softmax
+// of its g query heads (one warp per query head). Chunks beyond the cluster's
+// staging capacity, and every key when the launch has no cluster, are read from
+// the paged cache directly.
+constexpr int kDecThreads = 128;
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kStageChunks = 2;  // prefix chunks one CTA keeps for its cluster peers
+constexpr int kMaxGroupQ = 2 * kDecWarps;
+
+__device__ __forceinline__ uint4 ld_dsmem_u4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared::cluster.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
 template <int D>
-__global__ void __launch_bounds__(kAttnThreads)
-    attn_decode_kernel(const DecodeArgs a) {
+__device__ __forceinline__ void fold_chunk(QState<D>& st, const float* qv, const __nv_bfloat16* Ks,
+                                           const __nv_bfloat16* Vs, int nk, float scale, int lane) {
+  const __nv_bfloat162* K2 = reinterpret_cast<const __nv_bfloat162*>(Ks);
+  const float s0 = lane < nk ? dot_q_k<D>(qv, K2 + lane * (D / 2 + 1)) * scale : -INFINITY;
+  const float s1 = lane + 32 < nk ? dot_q_k<D>(qv, K2 + (lane + 32) * (D / 2 + 1)) * scale : -INFINITY;
+  fold_scores<D>(st, s0, s1, nk, [&](int j, int i) { return bf16_to_f(Vs[j * D + i * 32 + lane]); });
+}
+
+template <int D>
+__global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const DecodeArgs a, int cluster_rows) {
   constexpr int DPL = D / 32;
-  extern __shared__ uint8_t smem_raw[];
+  constexpr int kKChunk = kKeyChunk * (D + 2);  // bf16 elements of one staged K chunk
+  constexpr int kVChunk = kKeyChunk * D;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
   const int h = blockIdx.x;
+  const int r = blockIdx.y;
   const int g = a.hq / a.hkv;
-  const int Q = a.rows * g;
-  float* q_s = reinterpret_cast<float*>(smem_raw);                          // [Q][D]
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(q_s + Q * D);        // [64][D+2]
-  __nv_bfloat16* Vs = Ks + kKeyChunk * (D + 2);                              // [64][D]
-  float* tmp = reinterpret_cast<float*>(Vs + kKeyChunk * D);                 // [warps][D]
+  float* q_s = reinterpret_cast<float*>(smem_raw);  // [g][D]
+  float* tmp = q_s + g * D;                          // [warps][D]
+  __nv_bfloat16* stK = reinterpret_cast<__nv_bfloat16*>(tmp + kDecWarps * D);
+  __nv_bfloat16* stV = stK + kStageChunks * kKChunk;
+  __nv_bfloat16* wK = stV + kStageChunks * kVChunk;
+  __nv_bfloat16* wV = wK + kKChunk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tok_stride = (int64_t)a.hkv * D;
+  const bool clustered = cluster_rows > 1;
 
-  pdl_wait();
+  pdl_enter();
   const int P = a.prefix_len != nullptr ? *a.prefix_len : 0;
+  const bool act = a.active == nullptr || a.active[r] != 0;
 
-  // ---- prologue: q heads of this group (+ new k/v of this head) per row.
-  const int items = a.rows * (g + 1);
-  for (int it = warp; it < items; it += kAttnWarps) {
-    const int r = it / (g + 1), j = it % (g + 1);
-    const bool act = a.active == nullptr || a.active[r] != 0;
-    float* tw = tmp + warp * D;
-    if (j < g) {
+  // ---- prologue: q heads of this group + the new k/v of head h, for row r.
+  if (act) {
+    for (int it = warp; it < g + 1; it += kDecWarps) {
+      float* tw = tmp + warp * D;
       float x[DPL];
-      const int qh = h * g + j;
-      if (act) {
+      int pos = a.positions[r];
+      if (pos < 0 || pos >= a.max_pos) {
+        if (lane == 0 && a.qkv != nullptr) report(a.status, AIOSB_DEV_POSITION_RANGE);
+        pos = 0;
+      }
+      if (it < g) {
+        const int qh = h * g + it;
         if (a.qkv != nullptr) {
           const __nv_bfloat16* src = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)qh * D;
 #pragma unroll
           for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(src[i * 32 + lane]);
-          int pos = a.positions[r];
-          if (pos < 0 || pos >= a.max_pos) {
-            if (lane == 0) report(a.status, AIOSB_DEV_POSITION_RANGE);
-            pos = 0;
-          }
-          norm_rope<D>(x, a.q_norm_w, a.eps, a.cos_tab + (int64_t)pos * D, a.sin_tab + (int64_t)pos * D, true, true,
-                       lane, tw);
+          norm_rope<D>(x, a.q_norm_w, a.eps, a.cos_tab + (int64_t)pos * D, a.sin_tab + (int64_t)pos * D, true,
+                       true, lane, tw);
         } else {
           const __nv_bfloat16* src = a.q + (int64_t)r * a.q_stride + (int64_t)qh * D;
 #pragma unroll
           for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(src[i * 32 + lane]);
         }
-      } else {
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) x[i] = 0.f;
-      }
+        for (int i = 0; i < DPL; ++i) q_s[it * D + i * 32 + lane] = x[i];
+      } else if (a.qkv != nullptr) {
+        const __nv_bfloat16* ksrc = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(a.hq + h) * D;
+        const __nv_bfloat16* vsrc = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(a.hq + a.hkv + h) * D;
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) q_s[(r * g + j) * D + i * 32 + lane] = x[i];
-    } else if (act && a.qkv != nullptr) {
-      const __nv_bfloat16* ksrc = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(a.hq + h) * D;
-      const __nv_bfloat16* vsrc = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(a.hq + a.hkv + h) * D;
-      float x[DPL];
+        for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(ksrc[i * 32 + lane]);
+        norm_rope<D>(x, a.k_norm_w, a.eps, a.cos_tab + (int64_t)pos * D, a.sin_tab + (int64_t)pos * D, true, true,
+                     lane, tw);
+        const int64_t slot = a.out_loc[r];
+        if (slot >= 0 && slot < a.num_slots) {
+          __nv_bfloat16* kd = a.k_cache + slot * tok_stride + (int64_t)h * D;
+          __nv_bfloat16* vd = a.v_cache + slot * tok_stride + (int64_t)h * D;
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(ksrc[i * 32 + lane]);
-      int pos = a.positions[r];
-      if (pos < 0 || pos >= a.max_pos) {
-        if (lane == 0) report(a.status, AIOSB_DEV_POSITION_RANGE);
-        pos = 0;
-      }
-      norm_rope<D>(x, a.k_norm_w, a.eps, a.cos_tab + (int64_t)pos * D, a.sin_tab + (int64_t)pos * D, true, true,
-                   lane, tw);
-      const int64_t slot = a.out_loc[r];
-      if (slot >= 0 && slot < a.num_slots) {
-        __nv_bfloat16* kd = a.k_cache + slot * tok_stride + (int64_t)h * D;
-        __nv_bfloat16* vd = a.v_cache + slot * tok_stride + (int64_t)h * D;
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) {
-          kd[i * 32 + lane] = f_to_bf16(x[i]);
-          vd[i * 32 + lane] = vsrc[i * 32 + lane];
-        }
-      } else if (lane == 0) {
-        report(a.status, AIOSB_DEV_SLOT_RANGE);
-      }
-    }
-  }
-  __syncthreads();  // q_s complete; new K/V visible to the whole CTA
-
-  QState<D> st[kMaxQPerWarp];
-#pragma unroll
-  for (int s = 0; s < kMaxQPerWarp; ++s) qstate_init<D>(st[s]);
-
-  // ---- shared prefix: each slot staged once, scored against every query.
-  if (P > 0) {
-    const int32_t* pslots = a.page_table + (int64_t)a.row_table[0] * a.table_stride;
-    for (int k0 = 0; k0 < P; k0 += kKeyChunk) {
-      const int nk = min(kKeyChunk, P - k0);
-      stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, pslots, k0, nk, a.num_slots, Ks, Vs, a.status);
-      __syncthreads();
-#pragma unroll
-      for (int s = 0; s < kMaxQPerWarp; ++s) {
-        const int qi = warp + s * kAttnWarps;
-        if (qi < Q) {
-          const int r = qi / g;
-          if (a.active == nullptr || a.active[r] != 0) {
-            const float* qv = q_s + qi * D;
-            const __nv_bfloat162* K2 = reinterpret_cast<const __nv_bfloat162*>(Ks);
-            const float s0 = lane < nk ? dot_q_k<D>(qv, K2 + lane * (D / 2 + 1)) * a.scale : -INFINITY;
-            const float s1 = lane + 32 < nk ? dot_q_k<D>(qv, K2 + (lane + 32) * (D / 2 + 1)) * a.scale : -INFINITY;
-            fold_scores<D>(st[s], s0, s1, nk, [&](int j, int i) { return bf16_to_f(Vs[j * D + i * 32 + lane]); });
+          for (int i = 0; i < DPL; ++i) {
+            kd[i * 32 + lane] = f_to_bf16(x[i]);
+            vd[i * 32 + lane] = vsrc[i * 32 + lane];
           }
+        } else if (lane == 0) {
+          report(a.status, AIOSB_DEV_SLOT_RANGE);
         }
+      }
+    }
+  }
+
+  // ---- stage this CTA's share of the prefix (chunks r, r + R, ...).
+  const int nchunks = (P + kKeyChunk - 1) / kKeyChunk;
+  const int32_t* pslots = a.page_table + (int64_t)a.row_table[0] * a.table_stride;
+  if (clustered) {
+    for (int s = 0; s < kStageChunks; ++s) {
+      const int c = r + s * cluster_rows;
+      if (c < nchunks)
+        stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, pslots, c * kKeyChunk, min(kKeyChunk, P - c * kKeyChunk),
+                       a.num_slots, stK + s * kKChunk, stV + s * kVChunk, a.status);
+    }
+  }
+  __syncthreads();  // q_s ready, staged chunks ready, new K/V visible to this CTA
+  if (clustered) cluster_sync();
+
+  QState<D> st[2];
+  qstate_init<D>(st[0]);
+  qstate_init<D>(st[1]);
+
+  // ---- shared prefix
+  for (int c = 0; c < nchunks; ++c) {
+    const int nk = min(kKeyChunk, P - c * kKeyChunk);
+    const __nv_bfloat16* K = wK;
+    const __nv_bfloat16* V = wV;
+    const int owner = clustered ? c % cluster_rows : 0;
+    const int slot = clustered ? c / cluster_rows : kStageChunks;
+    if (slot < kStageChunks && owner == r) {
+      K = stK + slot * kKChunk;
+      V = stV + slot * kVChunk;
+    } else if (slot < kStageChunks) {
+      const uint32_t rk = map_shared_rank(smem_u32(stK + slot * kKChunk), (uint32_t)owner);
+      const uint32_t rv = map_shared_rank(smem_u32(stV + slot * kVChunk), (uint32_t)owner);
+      for (int i = threadIdx.x; i < kKChunk / 8; i += kDecThreads)
+        reinterpret_cast<uint4*>(wK)[i] = ld_dsmem_u4(rk + i * 16);
+      for (int i = threadIdx.x; i < kVChunk / 8; i += kDecThreads)
+        reinterpret_cast<uint4*>(wV)[i] = ld_dsmem_u4(rv + i * 16);
+      __syncthreads();
+    } else {
+      stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, pslots, c * kKeyChunk, nk, a.num_slots, wK, wV, a.status);
+      __syncthreads();
+    }
+    if (act) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int j = warp + t * kDecWarps;
+        if (j < g) fold_chunk<D>(st[t], q_s + j * D, K, V, nk, a.scale, lane);
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- this row's own keys [P, seq_len)
+  if (act) {
+    const int32_t* rslots = a.page_table + (int64_t)a.row_table[r] * a.table_stride;
+    const int L = a.seq_lens[r];
+    for (int k0 = P; k0 < L; k0 += kKeyChunk) {
+      const int nk = min(kKeyChunk, L - k0);
+      stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, rslots, k0, nk, a.num_slots, wK, wV, a.status);
+      __syncthreads();
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int j = warp + t * kDecWarps;
+        if (j < g) fold_chunk<D>(st[t], q_s + j * D, wK, wV, nk, a.scale, lane);
       }
       __syncthreads();
     }
   }
 
-  // ---- per-row suffix keys [P, seq_len) straight from the paged cache.
+  // ---- normalise and store (zeros for inactive rows)
 #pragma unroll
-  for (int s = 0; s < kMaxQPerWarp; ++s) {
-    const int qi = warp + s * kAttnWarps;
-    if (qi < Q) {
-      const int r = qi / g;
-      if (a.active == nullptr || a.active[r] != 0) {
-        const int32_t* rslots = a.page_table + (int64_t)a.row_table[r] * a.table_stride;
-        const int L = a.seq_lens[r];
-        const float* qv = q_s + qi * D;
-        for (int k0 = P; k0 < L; k0 += 64) {
-          const int nk = min(64, L - k0);
-          int64_t sl0 = lane < nk ? rslots[k0 + lane] : 0;
-          int64_t sl1 = lane + 32 < nk ? rslots[k0 + lane + 32] : 0;
-          if (sl0 < 0 || sl0 >= a.num_slots) { report(a.status, AIOSB_DEV_SLOT_RANGE); sl0 = 0; }
-          if (sl1 < 0 || sl1 >= a.num_slots) { report(a.status, AIOSB_DEV_SLOT_RANGE); sl1 = 0; }
-          const float s0 = lane < nk ? dot_q_k<D>(qv, reinterpret_cast<const __nv_bfloat162*>(
-                                                          a.k_cache + sl0 * tok_stride + (int64_t)h * D)) * a.scale
-                                     : -INFINITY;
-          const float s1 = lane + 32 < nk ? dot_q_k<D>(qv, reinterpret_cast<const __nv_bfloat162*>(
-                                                               a.k_cache + sl1 * tok_stride + (int64_t)h * D)) * a.scale
-                                          : -INFINITY;
-          fold_scores<D>(st[s], s0, s1, nk, [&](int j, int i) {
-            const int64_t sj = __shfl_sync(0xffffffffu, j < 32 ? sl0 : sl1, j & 31);
-            return bf16_to_f(a.v_cache[sj * tok_stride + (int64_t)h * D + i * 32 + lane]);
-          });
-        }
-      }
-    }
-  }
-
-  // ---- normalise and store.
-#pragma unroll
-  for (int s = 0; s < kMaxQPerWarp; ++s) {
-    const int qi = warp + s * kAttnWarps;
-    if (qi < Q) {
-      const int r = qi / g, j = qi % g;
-      const float inv = st[s].l > 0.f ? 1.0f / st[s].l : 0.f;
+  for (int t = 0; t < 2; ++t) {
+    const int j = warp + t * kDecWarps;
+    if (j < g) {
+      const float inv = act && st[t].l > 0.f ? 1.0f / st[t].l : 0.f;
       __nv_bfloat16* dst = a.out + (int64_t)r * a.out_stride + (int64_t)(h * g + j) * D;
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st[s].acc[i] * inv);
+      for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st[t].acc[i] * inv);
     }
   }
+  if (clustered) cluster_sync();  // peers may still be copying from this CTA's stage buffers
 }
 
 }  // namespace
@@ -355,7 +384,7 @@ template <int D>
 __global__ void __launch_bounds__(kAttnThreads) qk_norm_rope_store_kernel(const PrologueArgs a) {
   constexpr int DPL = D / 32;
   __shared__ float tmp_all[kAttnWarps][D];
-  pdl_wait();
+  pdl_enter();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int heads = a.hq + a.hkv;
   const int64_t item = (int64_t)blockIdx.x * kAttnWarps + warp;
@@ -438,7 +467,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const Prefil
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tok_stride = (int64_t)a.hkv * D;
 
-  pdl_wait();
+  pdl_enter();
   const int req = a.tile_req[tile];
   const int q0 = a.tile_q0[tile];
   const int qlen = a.req_q_len[req];
@@ -492,9 +521,38 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const Prefil
 }
 
 template <int D>
-size_t decode_smem(int queries) {
-  return (size_t)queries * D * 4 + (size_t)kKeyChunk * (D + 2) * 2 + (size_t)kKeyChunk * D * 2 +
-         (size_t)kAttnWarps * D * 4;
+size_t decode_smem(int group) {
+  const size_t chunk = (size_t)kKeyChunk * (D + 2) * 2 + (size_t)kKeyChunk * D * 2;
+  return (size_t)group * D * 4 + (size_t)kDecWarps * D * 4 + (kStageChunks + 1) * chunk;
+}
+
+template <int D>
+cudaError_t launch_decode(const DecodeArgs& a, int rows, int hkv, int group, cudaStream_t stream) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = attn_decode_kernel<D>;
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem<D>(kMaxGroupQ));
+    cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    configured[dev] = true;
+  }
+  const int cluster_rows = rows <= 16 ? rows : 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)hkv, (unsigned)rows);
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = decode_smem<D>(group);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = (unsigned)cluster_rows;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, a, cluster_rows);
 }
 template <int D>
 size_t prefill_smem(int queries) {
@@ -524,8 +582,8 @@ extern "C" int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const
   AIOSB_REQUIRE(head_dim == 64 || head_dim == 96 || head_dim == 128, AIOSB_ERR_UNSUPPORTED,
                 "attention_decode: head_dim %lld unsupported (64, 96, 128)", (long long)head_dim);
   const int64_t g = num_qo_heads / num_kv_heads;
-  AIOSB_REQUIRE(rows * g <= kMaxQueries, AIOSB_ERR_UNSUPPORTED,
-                "attention_decode: rows * group = %lld exceeds %d", (long long)(rows * g), kMaxQueries);
+  AIOSB_REQUIRE(g <= kMaxGroupQ, AIOSB_ERR_UNSUPPORTED,
+                "attention_decode: %lld query heads per KV head exceeds %d", (long long)g, kMaxGroupQ);
   if (rows == 0) return AIOSB_OK;
   AIOSB_REQUIRE((qkv != nullptr) != (q != nullptr), AIOSB_ERR_INVALID_ARG,
                 "attention_decode: pass exactly one of qkv (fused prologue) or q (pre-rotated)");
@@ -562,20 +620,11 @@ extern "C" int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const
   a.out = (__nv_bfloat16*)out;
   a.out_stride = out_stride;
   a.status = status;
-  const int Q = (int)(rows * g);
   cudaError_t e;
-  const dim3 grid((unsigned)num_kv_heads), block(kAttnThreads);
   cudaStream_t s = as_stream(stream);
-  if (head_dim == 64) {
-    allow_smem(attn_decode_kernel<64>, decode_smem<64>(kMaxQueries));
-    e = launch_pdl(attn_decode_kernel<64>, grid, block, decode_smem<64>(Q), s, a);
-  } else if (head_dim == 96) {
-    allow_smem(attn_decode_kernel<96>, decode_smem<96>(kMaxQueries));
-    e = launch_pdl(attn_decode_kernel<96>, grid, block, decode_smem<96>(Q), s, a);
-  } else {
-    allow_smem(attn_decode_kernel<128>, decode_smem<128>(kMaxQueries));
-    e = launch_pdl(attn_decode_kernel<128>, grid, block, decode_smem<128>(Q), s, a);
-  }
+  if (head_dim == 64) e = launch_decode<64>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+  else if (head_dim == 96) e = launch_decode<96>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+  else e = launch_decode<128>(a, (int)rows, (int)num_kv_heads, (int)g, s);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attention_decode: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }

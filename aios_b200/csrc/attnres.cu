@@ -24,7 +24,7 @@ __global__ void __launch_bounds__(kMixWarps * 32)
     attnres_reg_kernel(const uint4* __restrict__ bank, int nsrc_bank, int64_t tokens, int hidden,
                        const uint4* __restrict__ partial, const float* __restrict__ wq, float eps,
                        uint4* __restrict__ out) {
-  pdl_wait();
+  pdl_enter();
   const int64_t t = (int64_t)blockIdx.x * kMixWarps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (t >= tokens) return;
@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(kMixWarps * 32)
     attnres_generic_kernel(const uint4* __restrict__ bank, int nsrc_bank, int64_t tokens, int hidden,
                            const uint4* __restrict__ partial, const float* __restrict__ wq, float eps,
                            uint4* __restrict__ out) {
-  pdl_wait();
+  pdl_enter();
   const int64_t t = (int64_t)blockIdx.x * kMixWarps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (t >= tokens) return;

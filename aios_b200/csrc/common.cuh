@@ -251,5 +251,12 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// Kernel entry on the decode/prefill chains: let the next kernel launch now (its
+// weight prefetch then overlaps this kernel; it still waits for this grid's
+// completion before touching dependent data), then wait for the previous one.
+__device__ __forceinline__ void pdl_enter() {
+  pdl_launch_dependents();
+  pdl_wait();
+}
 
 }  // namespace aiosb

@@ -18,7 +18,7 @@ __global__ void kv_store_kernel(__nv_bfloat16* __restrict__ k_cache, __nv_bfloat
                                 int64_t num_tokens, const __nv_bfloat16* __restrict__ k, int64_t k_stride,
                                 const __nv_bfloat16* __restrict__ v, int64_t v_stride, int64_t width, bool vec,
                                 int32_t* status) {
-  pdl_wait();
+  pdl_enter();
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (t >= num_tokens) return;
@@ -50,7 +50,7 @@ __global__ void kv_store_kernel(__nv_bfloat16* __restrict__ k_cache, __nv_bfloat
 __global__ void rmsnorm_kernel(const __nv_bfloat16* x, int64_t rows, int hidden, int64_t hpt, int64_t token_stride,
                                const __nv_bfloat16* __restrict__ w, float eps, __nv_bfloat16* out,
                                int64_t out_token_stride, bool vec) {
-  pdl_wait();
+  pdl_enter();
   const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -102,7 +102,7 @@ constexpr int kMaxVecPerLane = 16;
 template <int VPL>
 __global__ void add_rmsnorm_kernel(__nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ res, int64_t rows,
                                    int hidden, const __nv_bfloat16* __restrict__ w, float eps) {
-  pdl_wait();
+  pdl_enter();
   const int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -153,7 +153,7 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g));
 
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ x, int64_t rows, int64_t f,
                                 __nv_bfloat16* __restrict__ out) {
-  pdl_wait();
+  pdl_enter();
   const int64_t nvec = f / 8;
   const int64_t total = rows * nvec;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -173,7 +173,7 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ x, int64_t row
 // ---- Embedding gather (aios/layers/embedding.py:17-18) --------------------
 __global__ void embedding_kernel(const void* __restrict__ ids, bool ids64, int64_t n, const uint4* __restrict__ w,
                                  int64_t vocab, int64_t hidden, uint4* __restrict__ out, int32_t* status) {
-  pdl_wait();
+  pdl_enter();
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (t >= n) return;

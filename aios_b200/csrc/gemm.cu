@@ -16,6 +16,8 @@
 // keeps ~all SMs streaming weights even for 768-row projections; the partial
 // tiles are reduced deterministically through distributed shared memory.
 // No TMA load uses cluster multicast: each CTA loads its own K slice.
+#include <string.h>
+
 #include <algorithm>
 #include <mutex>
 
@@ -44,7 +46,18 @@ struct GemmArgs {
   int stages;
   int split;
   int epilogue;
+  // Fused RMSNorm prologue (norm != 0): the B operand is rmsnorm(nx [+ nres]) * nw,
+  // computed by the CTA itself instead of loaded by TMA; nres_out <- nx + nres.
+  int norm;
+  int64_t k_total;
+  const __nv_bfloat16* nx;
+  const __nv_bfloat16* nres;
+  __nv_bfloat16* nres_out;
+  const __nv_bfloat16* nw;
+  float neps;
 };
+
+constexpr int kMaxNormRows = 64;
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -55,9 +68,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const uint32_t pipe_bytes = (uint32_t)a.stages * kStageBytes;
+  const bool norm = a.norm != 0;
+  const uint32_t stage_bytes = norm ? kABytes : kStageBytes;
+  uint8_t* bnorm = smem + a.stages * stage_bytes;  // norm mode: every B chunk of this CTA
+  const uint32_t pipe_bytes = (uint32_t)a.stages * stage_bytes + (norm ? (uint32_t)a.chunks_per_split * kBBytes : 0u);
   const uint32_t red_bytes = BN * kBM * 4;
   const uint32_t body = pipe_bytes > red_bytes ? pipe_bytes : red_bytes;
+  __shared__ float rcp_s[kMaxNormRows];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + body);
   uint64_t* empty = full + kMaxStages;
   uint64_t* accum = empty + kMaxStages;
@@ -72,6 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nch = a.chunks_per_split;
   const int k_chunk0 = split_idx * nch;
 
+  pdl_launch_dependents();  // the next kernel may start its own weight prefetch now
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(&full[s], 1);
@@ -94,17 +112,88 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // ---- weights do not depend on the previous kernel: request the first stages'
+  // weight tiles before waiting on it (programmatic dependent launch).
+  const int pre = nch < a.stages ? nch : a.stages;
   if (tid == 0) {
-    // ---- TMA producer. Weights do not depend on the previous kernel, so the
-    // first stages' weight tiles are requested before waiting on it (PDL).
-    const int pre = nch < a.stages ? nch : a.stages;
     for (int i = 0; i < pre; ++i) {
-      mbar_arrive_expect_tx(&full[i], kStageBytes);
-      tma_load_2d(smem + i * kStageBytes, &tm_w, &full[i], (k_chunk0 + i) * kBK, m_tile * kBM);
+      mbar_arrive_expect_tx(&full[i], stage_bytes);
+      tma_load_2d(smem + i * stage_bytes, &tm_w, &full[i], (k_chunk0 + i) * kBK, m_tile * kBM);
     }
-    pdl_wait();
+  }
+  pdl_wait();
+  if (norm) {
+    // ---- fused RMSNorm: per-row 1/rms over the full K, then this CTA's K chunks
+    // of the normalised rows written straight into the UMMA B layout
+    // (128-byte rows, 16-byte units swizzled by row % 8, as TMA SWIZZLE_128B).
+    const int64_t K = a.k_total;
+    const int nvec = (int)(K / 8);
+    for (int t = warp; t < BN; t += kThreads / 32) {
+      const int64_t tg = (int64_t)n_tile * BN + t;
+      float ss = 0.f;
+      if (tg < a.rows) {
+        const uint4* xr = reinterpret_cast<const uint4*>(a.nx + tg * K);
+        const uint4* rr = a.nres ? reinterpret_cast<const uint4*>(a.nres + tg * K) : nullptr;
+        for (int i = lane; i < nvec; i += 32) {
+          const uint4 xv = xr[i];
+          const uint32_t px[4] = {xv.x, xv.y, xv.z, xv.w};
+          uint32_t pr[4] = {0u, 0u, 0u, 0u};
+          if (rr) {
+            const uint4 rv = rr[i];
+            pr[0] = rv.x; pr[1] = rv.y; pr[2] = rv.z; pr[3] = rv.w;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float lo = bf16_lo(px[q]) + bf16_lo(pr[q]);
+            const float hi = bf16_hi(px[q]) + bf16_hi(pr[q]);
+            ss += lo * lo + hi * hi;
+          }
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) rcp_s[t] = 1.0f / sqrtf(ss / (float)K + a.neps);
+    }
+    __syncthreads();
+    const int units = nch * BN * 8;
+    for (int u = tid; u < units; u += kThreads) {
+      const int i = u / (BN * 8), rem = u % (BN * 8), t = rem >> 3, c16 = rem & 7;
+      const int64_t kk = (int64_t)(k_chunk0 + i) * kBK + c16 * 8;
+      const int64_t tg = (int64_t)n_tile * BN + t;
+      uint4 o = make_uint4(0u, 0u, 0u, 0u);
+      if (tg < a.rows) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(a.nx + tg * K + kk);
+        const uint4 wv = *reinterpret_cast<const uint4*>(a.nw + kk);
+        const uint32_t px[4] = {xv.x, xv.y, xv.z, xv.w}, pw[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t pr[4] = {0u, 0u, 0u, 0u};
+        if (a.nres) {
+          const uint4 rv = *reinterpret_cast<const uint4*>(a.nres + tg * K + kk);
+          pr[0] = rv.x; pr[1] = rv.y; pr[2] = rv.z; pr[3] = rv.w;
+        }
+        const float rcp = rcp_s[t];
+        uint32_t po[4], ps[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float lo = bf16_lo(px[q]) + bf16_lo(pr[q]);
+          const float hi = bf16_hi(px[q]) + bf16_hi(pr[q]);
+          ps[q] = pack_bf16x2(lo, hi);
+          po[q] = pack_bf16x2(lo * rcp * bf16_lo(pw[q]), hi * rcp * bf16_hi(pw[q]));
+        }
+        o = make_uint4(po[0], po[1], po[2], po[3]);
+        if (a.nres_out != nullptr && m_tile == 0)
+          *reinterpret_cast<uint4*>(a.nres_out + tg * K + kk) = make_uint4(ps[0], ps[1], ps[2], ps[3]);
+      }
+      *reinterpret_cast<uint4*>(bnorm + (size_t)i * kBBytes + t * 128 + ((c16 ^ (t & 7)) << 4)) = o;
+    }
+    // generic-proxy smem writes -> visible to the tensor core (async proxy)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+  } else if (tid == 0) {
     for (int i = 0; i < pre; ++i)
-      tma_load_2d(smem + i * kStageBytes + kABytes, &tm_x, &full[i], (k_chunk0 + i) * kBK, n_tile * BN);
+      tma_load_2d(smem + i * stage_bytes + kABytes, &tm_x, &full[i], (k_chunk0 + i) * kBK, n_tile * BN);
+  }
+
+  if (tid == 0) {
+    // ---- TMA producer for the remaining stages.
     for (int i = pre; i < nch; ++i) {
       const int s = i % a.stages;
       if (!mbar_wait(&empty[s], ((i / a.stages) & 1) ^ 1)) {
@@ -112,13 +201,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
         break;
       }
-      mbar_arrive_expect_tx(&full[s], kStageBytes);
-      tma_load_2d(smem + s * kStageBytes, &tm_w, &full[s], (k_chunk0 + i) * kBK, m_tile * kBM);
-      tma_load_2d(smem + s * kStageBytes + kABytes, &tm_x, &full[s], (k_chunk0 + i) * kBK, n_tile * BN);
+      mbar_arrive_expect_tx(&full[s], stage_bytes);
+      tma_load_2d(smem + s * stage_bytes, &tm_w, &full[s], (k_chunk0 + i) * kBK, m_tile * kBM);
+      if (!norm)
+        tma_load_2d(smem + s * stage_bytes + kABytes, &tm_x, &full[s], (k_chunk0 + i) * kBK, n_tile * BN);
     }
   } else if (tid == 32) {
     // ---- MMA issuer.
-    pdl_wait();
     constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
     bool ok = true;
     for (int i = 0; i < nch; ++i) {
@@ -130,8 +219,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t a_base = smem_u32(smem + s * kStageBytes);
-      const uint32_t b_base = a_base + kABytes;
+      const uint32_t a_base = smem_u32(smem + s * stage_bytes);
+      const uint32_t b_base = norm ? smem_u32(bnorm + (size_t)i * kBBytes) : a_base + kABytes;
 #pragma unroll
       for (int kk = 0; kk < kBK / 16; ++kk) {
         tc_mma_bf16(tmem, umma_desc_sw128(a_base + kk * 32), umma_desc_sw128(b_base + kk * 32), idesc,
@@ -140,8 +229,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(&empty[s]);
     }
     if (ok) tc_commit(accum);
-  } else {
-    pdl_wait();
   }
 
   // ---- Epilogue: TMEM -> registers -> shared [BN][128] fp32.
@@ -155,7 +242,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   have = __all_sync(0xffffffffu, have);
   tc_fence_after();
   if (have) {
-    pdl_launch_dependents();
 #pragma unroll
     for (int cb = 0; cb < BN / 16; ++cb) {
       float v[16];
@@ -284,11 +370,14 @@ int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, uint3
 constexpr int max_stages_for(int bn) { return bn >= 256 ? 4 : bn >= 128 ? 5 : kMaxStages; }
 
 template <int BN>
-size_t smem_bytes(int stages) {
-  const size_t pipe = (size_t)stages * (kABytes + BN * kBK * 2);
+size_t smem_bytes(int stages, bool norm = false, int chunks = 0) {
+  const size_t pipe = norm ? (size_t)stages * kABytes + (size_t)chunks * BN * kBK * 2
+                           : (size_t)stages * (kABytes + BN * kBK * 2);
   const size_t red = (size_t)BN * kBM * 4;
   return std::max(pipe, red) + 1024 /*alignment*/ + 256 /*barriers*/;
 }
+
+constexpr int kMaxDynSmem = 227 * 1024 - 1024;  // opt-in limit minus the static rcp table
 
 template <int BN>
 int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, GemmArgs a, int m_tiles, int n_tiles,
@@ -298,14 +387,14 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, GemmArgs a, int m_
   cudaGetDevice(&dev);
   auto kern = gemm_tc_kernel<BN>;
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<BN>(max_stages_for(BN)));
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
     cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     configured[dev] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)m_tiles, (unsigned)a.split, (unsigned)n_tiles);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem_bytes<BN>(a.stages);
+  cfg.dynamicSmemBytes = smem_bytes<BN>(a.stages, a.norm != 0, a.chunks_per_split);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -337,45 +426,36 @@ int choose_split(int64_t tiles, int64_t chunks, int sms) {
 
 using namespace aiosb;
 
-extern "C" int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
-                            int64_t y_row_stride, int epilogue, const void* residual, int64_t residual_stride,
-                            int32_t* status, void* stream) {
-  AIOSB_REQUIRE(rows >= 0 && k > 0 && n > 0, AIOSB_ERR_INVALID_ARG, "linear: bad sizes");
-  AIOSB_REQUIRE(n % kBM == 0, AIOSB_ERR_UNSUPPORTED, "linear: n=%lld must be a multiple of 128", (long long)n);
-  AIOSB_REQUIRE(k % kBK == 0, AIOSB_ERR_UNSUPPORTED, "linear: k=%lld must be a multiple of 64", (long long)k);
-  AIOSB_REQUIRE(epilogue == AIOSB_EPI_STORE || epilogue == AIOSB_EPI_SILU_MUL || epilogue == AIOSB_EPI_ADD,
-                AIOSB_ERR_INVALID_ARG, "linear: unknown epilogue %d", epilogue);
-  AIOSB_REQUIRE(epilogue != AIOSB_EPI_ADD ||
-                    (residual != nullptr && aligned16(residual) && residual_stride >= n && residual_stride % 8 == 0),
-                AIOSB_ERR_INVALID_ARG, "linear: the add epilogue needs an aligned residual [rows, >= n]");
-  const int64_t y_cols = epilogue == AIOSB_EPI_SILU_MUL ? n / 2 : n;
-  AIOSB_REQUIRE(y_row_stride >= y_cols && y_row_stride % 8 == 0, AIOSB_ERR_INVALID_ARG,
-                "linear: y row stride must cover the output and be a multiple of 8");
-  if (rows == 0) return AIOSB_OK;
-  AIOSB_REQUIRE(x && w && y, AIOSB_ERR_INVALID_ARG, "linear: null pointer");
-  AIOSB_REQUIRE(aligned16(x) && aligned16(w) && aligned16(y), AIOSB_ERR_MISALIGNED,
-                "linear: x, w and y must be 16-byte aligned");
+namespace aiosb {
+namespace {
+
+int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* stream) {
   const int bn = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256;
   const int64_t m_tiles = n / kBM;
   const int64_t n_tiles = (rows + bn - 1) / bn;
   const int64_t chunks = k / kBK;
-  GemmArgs a;
   a.rows = rows;
   a.n = n;
-  a.y_row_stride = y_row_stride;
-  a.y = (__nv_bfloat16*)y;
-  a.residual = (const __nv_bfloat16*)residual;
-  a.residual_stride = residual_stride;
-  a.status = status;
-  a.epilogue = epilogue;
+  a.k_total = k;
   a.split = choose_split(m_tiles * n_tiles, chunks, sm_count());
-  a.chunks_per_split = (int)(chunks / a.split);
-  a.stages = std::min(a.chunks_per_split, max_stages_for(bn));
+  auto plan = [&]() {
+    a.chunks_per_split = (int)(chunks / a.split);
+    a.stages = std::min(a.chunks_per_split, max_stages_for(bn));
+    // keep the norm-mode B buffer + weight stages inside the shared-memory budget
+    while (a.norm && a.stages > 1 &&
+           (size_t)a.stages * kABytes + (size_t)a.chunks_per_split * bn * kBK * 2 + 2048 > (size_t)kMaxDynSmem)
+      --a.stages;
+  };
+  plan();
   CUtensorMap tw, tx;
   int rc = make_map(&tw, w, n, k, kBM);
   if (rc) return rc;
-  rc = make_map(&tx, x, rows, k, (uint32_t)bn);
-  if (rc) return rc;
+  if (!a.norm) {
+    rc = make_map(&tx, x, rows, k, (uint32_t)bn);
+    if (rc) return rc;
+  } else {
+    tx = tw;  // unused in norm mode
+  }
   cudaStream_t s = as_stream(stream);
   auto launch = [&]() {
     switch (bn) {
@@ -392,9 +472,75 @@ extern "C" int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* 
     (void)cudaGetLastError();
     g_max_split = 8;
     a.split = choose_split(m_tiles * n_tiles, chunks, sm_count());
-    a.chunks_per_split = (int)(chunks / a.split);
-    a.stages = std::min(a.chunks_per_split, max_stages_for(bn));
+    plan();
     rc = launch();
   }
   return rc;
+}
+
+int check_common(const void* w, int64_t rows, int64_t k, int64_t n, void* y, int64_t y_row_stride, int epilogue,
+                 const void* residual, int64_t residual_stride) {
+  AIOSB_REQUIRE(rows >= 0 && k > 0 && n > 0, AIOSB_ERR_INVALID_ARG, "linear: bad sizes");
+  AIOSB_REQUIRE(n % kBM == 0, AIOSB_ERR_UNSUPPORTED, "linear: n=%lld must be a multiple of 128", (long long)n);
+  AIOSB_REQUIRE(k % kBK == 0, AIOSB_ERR_UNSUPPORTED, "linear: k=%lld must be a multiple of 64", (long long)k);
+  AIOSB_REQUIRE(epilogue == AIOSB_EPI_STORE || epilogue == AIOSB_EPI_SILU_MUL || epilogue == AIOSB_EPI_ADD,
+                AIOSB_ERR_INVALID_ARG, "linear: unknown epilogue %d", epilogue);
+  AIOSB_REQUIRE(epilogue != AIOSB_EPI_ADD ||
+                    (residual != nullptr && aligned16(residual) && residual_stride >= n && residual_stride % 8 == 0),
+                AIOSB_ERR_INVALID_ARG, "linear: the add epilogue needs an aligned residual [rows, >= n]");
+  const int64_t y_cols = epilogue == AIOSB_EPI_SILU_MUL ? n / 2 : n;
+  AIOSB_REQUIRE(y_row_stride >= y_cols && y_row_stride % 8 == 0, AIOSB_ERR_INVALID_ARG,
+                "linear: y row stride must cover the output and be a multiple of 8");
+  if (rows == 0) return 1;
+  AIOSB_REQUIRE(w && y, AIOSB_ERR_INVALID_ARG, "linear: null pointer");
+  AIOSB_REQUIRE(aligned16(w) && aligned16(y), AIOSB_ERR_MISALIGNED, "linear: w and y must be 16-byte aligned");
+  return AIOSB_OK;
+}
+
+GemmArgs base_args(void* y, int64_t y_row_stride, int epilogue, const void* residual, int64_t residual_stride,
+                   int32_t* status) {
+  GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.y_row_stride = y_row_stride;
+  a.y = (__nv_bfloat16*)y;
+  a.residual = (const __nv_bfloat16*)residual;
+  a.residual_stride = residual_stride;
+  a.status = status;
+  a.epilogue = epilogue;
+  return a;
+}
+
+}  // namespace
+}  // namespace aiosb
+
+extern "C" int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
+                            int64_t y_row_stride, int epilogue, const void* residual, int64_t residual_stride,
+                            int32_t* status, void* stream) {
+  int rc = check_common(w, rows, k, n, y, y_row_stride, epilogue, residual, residual_stride);
+  if (rc != AIOSB_OK) return rc == 1 ? AIOSB_OK : rc;
+  AIOSB_REQUIRE(x && aligned16(x), AIOSB_ERR_MISALIGNED, "linear: x must be a 16-byte aligned pointer");
+  return linear_impl(base_args(y, y_row_stride, epilogue, residual, residual_stride, status), x, rows, k, w, n,
+                     stream);
+}
+
+extern "C" int aiosb_linear_rmsnorm(const void* x, const void* res, void* res_out, const void* norm_w, float eps,
+                                    int64_t rows, int64_t k, const void* w, int64_t n, void* y, int64_t y_row_stride,
+                                    int epilogue, const void* residual, int64_t residual_stride, int32_t* status,
+                                    void* stream) {
+  int rc = check_common(w, rows, k, n, y, y_row_stride, epilogue, residual, residual_stride);
+  if (rc != AIOSB_OK) return rc == 1 ? AIOSB_OK : rc;
+  AIOSB_REQUIRE(rows <= kMaxNormRows, AIOSB_ERR_UNSUPPORTED, "linear_rmsnorm: at most %d rows", kMaxNormRows);
+  AIOSB_REQUIRE(x && norm_w && aligned16(x) && aligned16(norm_w) && (res == nullptr || aligned16(res)) &&
+                    (res_out == nullptr || aligned16(res_out)),
+                AIOSB_ERR_MISALIGNED, "linear_rmsnorm: x / res / res_out / norm_w must be 16-byte aligned");
+  AIOSB_REQUIRE(res_out == nullptr || (res_out != res && res_out != x), AIOSB_ERR_INVALID_ARG,
+                "linear_rmsnorm: res_out must not alias x or res (other CTAs still read them)");
+  GemmArgs a = base_args(y, y_row_stride, epilogue, residual, residual_stride, status);
+  a.norm = 1;
+  a.nx = (const __nv_bfloat16*)x;
+  a.nres = (const __nv_bfloat16*)res;
+  a.nres_out = (__nv_bfloat16*)res_out;
+  a.nw = (const __nv_bfloat16*)norm_w;
+  a.neps = eps;
+  return linear_impl(a, x, rows, k, w, n, stream);
 }

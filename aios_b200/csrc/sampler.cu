@@ -44,7 +44,8 @@ struct RowSmem {
   float cval[kMaxSortK];                // candidate scaled logits in sorted order
   int cid[kMaxSortK];
   float prob[kMaxSortK];
-  unsigned int hist[256];
+  unsigned int hist[kSampThreads / 32][256];  // per-warp private radix histograms
+  unsigned int hsum[256];
   float red[32];
   int ired[32];
   int misc[8];
@@ -142,25 +143,54 @@ __device__ int sample_row(RowSmem& s, float* row, int V, const SampleParams& p, 
     sorted_path = true;  // full descending sort (sample.py:131-132)
   }
   if (sorted_path) {
-    // ---- radix select of the k-th largest order key.
+    // ---- radix select of the k-th largest order key: four 8-bit passes, each a
+    // per-warp private histogram (no cross-warp atomic contention) summed per bin,
+    // then a warp-parallel scan from the top bin down.
     uint32_t prefix = 0, mask = 0;
     int remaining = k;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nwarps = blockDim.x >> 5;
     for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = tid; b < 256; b += blockDim.x) s.hist[b] = 0;
+      for (int b = tid; b < nwarps * 256; b += blockDim.x) (&s.hist[0][0])[b] = 0;
       __syncthreads();
       for (int i = tid; i < V; i += blockDim.x) {
         const uint32_t key = order_key(row[i]);
-        if ((key & mask) == prefix) atomicAdd(&s.hist[(key >> shift) & 0xFFu], 1u);
+        if ((key & mask) == prefix) atomicAdd(&s.hist[warp][(key >> shift) & 0xFFu], 1u);
       }
       __syncthreads();
-      if (tid == 0) {
-        int acc = 0, b = 255;
-        for (; b > 0; --b) {
-          if (acc + (int)s.hist[b] >= remaining) break;
-          acc += (int)s.hist[b];
+      for (int b = tid; b < 256; b += blockDim.x) {
+        unsigned int t = 0;
+        for (int w = 0; w < nwarps; ++w) t += s.hist[w][b];
+        s.hsum[b] = t;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        // lane l owns bins 255-8l .. 248-8l (descending); find the bin holding
+        // the `remaining`-th largest key
+        int local[8];
+        int tot = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          local[j] = (int)s.hsum[255 - 8 * lane - j];
+          tot += local[j];
         }
-        s.misc[0] = b;
-        s.misc[1] = remaining - acc;
+        int incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const int excl = incl - tot;
+        const bool mine = excl < remaining && incl >= remaining;
+        if (mine) {
+          int acc = excl, j = 0;
+          for (; j < 7; ++j) {
+            if (acc + local[j] >= remaining) break;
+            acc += local[j];
+          }
+          s.misc[0] = 255 - 8 * lane - j;
+          s.misc[1] = remaining - acc;
+        }
       }
       __syncthreads();
       prefix |= (uint32_t)s.misc[0] << shift;
@@ -323,7 +353,7 @@ __global__ void __launch_bounds__(kSampThreads)
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
   float* row = reinterpret_cast<float*>(smem_raw + sizeof(RowSmem));
-  pdl_wait();
+  pdl_enter();
   const int r = blockIdx.x;
   const __nv_bfloat16* lrow = logits + (int64_t)r * row_stride;
   float mx, lse;
@@ -354,7 +384,7 @@ __global__ void __launch_bounds__(kSampThreads) group_step_kernel(aiosb_group_pt
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
   float* row = reinterpret_cast<float*>(smem_raw + sizeof(RowSmem));
-  pdl_wait();
+  pdl_enter();
   aiosb_group_state* st = g.state;
   const int r = blockIdx.x;
   const int step = st->step;
@@ -487,7 +517,7 @@ __device__ __forceinline__ float splitmix_uniform(uint64_t seed, uint64_t step) 
 
 __global__ void group_begin_kernel(aiosb_group_ptrs g, const __nv_bfloat16* __restrict__ prefix_logits,
                                    uint64_t seed_base, int attempts) {
-  pdl_wait();
+  pdl_enter();
   aiosb_group_state* st = g.state;
   const int R = st->rows, S = st->max_steps, V = st->vocab;
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -565,7 +595,7 @@ __global__ void __launch_bounds__(kSampThreads)
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
   float* row = reinterpret_cast<float*>(smem_raw + sizeof(RowSmem));
-  pdl_wait();
+  pdl_enter();
   const int r = blockIdx.x;
   const __nv_bfloat16* lrow = logits + (int64_t)r * row_stride;
   float mx, lse;

@@ -315,6 +315,55 @@ def linear(
     return out
 
 
+MAX_NORM_ROWS = 64  # rows the fused-RMSNorm GEMM prologue handles
+
+
+def linear_rmsnorm(
+    x: torch.Tensor,
+    residual_in: torch.Tensor | None,
+    norm_weight: torch.Tensor,
+    eps: float,
+    weight: torch.Tensor,
+    *,
+    residual_out: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    epilogue: int = _lib.EPI_STORE,
+) -> torch.Tensor:
+    """``linear(rmsnorm(x + residual_in) * norm_weight, weight)`` in one kernel
+    (rows <= 64); ``residual_out`` receives ``x + residual_in`` when given."""
+    _require_cuda(x, norm_weight, weight, what="linear_rmsnorm")
+    rows, k = x.shape
+    if rows > MAX_NORM_ROWS:
+        raise ValueError(f"linear_rmsnorm handles at most {MAX_NORM_ROWS} rows")
+    for t in (x, residual_in, residual_out):
+        if t is not None and (t.shape != (rows, k) or not t.is_contiguous()):
+            raise ValueError("linear_rmsnorm expects contiguous [rows, k] x / residual tensors")
+    n = weight.shape[0]
+    cols = n // 2 if epilogue == _lib.EPI_SILU_MUL else n
+    if out is None:
+        out = torch.empty((rows, cols), dtype=x.dtype, device=x.device)
+    _lib.call(
+        "aiosb_linear_rmsnorm",
+        x.data_ptr(),
+        _ptr(residual_in),
+        _ptr(residual_out),
+        norm_weight.data_ptr(),
+        float(eps),
+        rows,
+        k,
+        weight.data_ptr(),
+        n,
+        out.data_ptr(),
+        out.stride(0),
+        epilogue,
+        None,
+        0,
+        status_word(x.device).data_ptr(),
+        _stream(x.device),
+    )
+    return out
+
+
 def pack_gate_up(weight: torch.Tensor) -> torch.Tensor:
     """[gate | up] rows ([2F, K]) -> 64-row interleaved blocks for EPI_SILU_MUL."""
     two_f, k = weight.shape

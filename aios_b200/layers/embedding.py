@@ -32,17 +32,41 @@ class LMHead(BaseOP):
         if not tie_word_embeddings:
             self.weight = torch.empty(num_embeddings, embedding_dim)
 
+    @staticmethod
+    def _select(batch, *tensors):
+        """Rows the logits are needed for (the last token of each prefill request)."""
+        if not (batch.is_prefill and not batch.return_all_logits):
+            return tensors
+        md = batch.attn_metadata
+        rows = getattr(md, "last_rows", ())
+        if len(rows) == 1:  # one request: views, no gather
+            return tuple(None if t is None else t[rows[0] : rows[0] + 1] for t in tensors)
+        idx = md.get_last_indices(batch.size)
+        return tuple(None if t is None else t.index_select(0, idx) for t in tensors)
+
+    def _w(self) -> torch.Tensor:
+        return self._tied_embedding.weight if self._tie_word_embeddings else self.weight
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         batch = get_global_ctx().batch
-        if batch.is_prefill and not batch.return_all_logits:
-            md = batch.attn_metadata
-            rows = getattr(md, "last_rows", ())
-            if len(rows) == 1:
-                x = x[rows[0] : rows[0] + 1]  # one request: a view, no gather
+        (x,) = self._select(batch, x)
+        return ops.linear(x.contiguous(), self._w(), out=batch.logits_out)
+
+    def forward_normed(self, x: torch.Tensor, residual: torch.Tensor | None, norm_weight: torch.Tensor,
+                       eps: float) -> torch.Tensor:
+        """LM head on rmsnorm(x + residual) * norm_weight: the final norm runs
+        inside the LM-head GEMM (rows <= 64), only for the rows that need logits."""
+        batch = get_global_ctx().batch
+        x, residual = self._select(batch, x, residual)
+        if x.shape[0] > ops.MAX_NORM_ROWS:
+            if residual is None:
+                h = ops.rmsnorm(x.contiguous(), norm_weight, eps)
             else:
-                x = x.index_select(0, md.get_last_indices(batch.size))
-        w = self._tied_embedding.weight if self._tie_word_embeddings else self.weight
-        return ops.linear(x.contiguous(), w, out=batch.logits_out)
+                h = x.contiguous().clone()
+                ops.fused_add_rmsnorm(h, residual.contiguous().clone(), norm_weight, eps)
+            return ops.linear(h, self._w(), out=batch.logits_out)
+        return ops.linear_rmsnorm(x.contiguous(), None if residual is None else residual.contiguous(), norm_weight,
+                                  eps, self._w(), out=batch.logits_out)
 
     def load_state_dict(self, state_dict: Dict[str, torch.Tensor], *, prefix: str = "", _internal: bool = False) -> None:
         if self._tie_word_embeddings:

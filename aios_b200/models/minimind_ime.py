@@ -78,6 +78,18 @@ class MiniMindAttnResDecoderLayer(BaseOP):
         self.attn_res_mixer = BlockAttnResMixer(config.hidden_size, config.rms_norm_eps, config.attnres_backend)
         self.mlp_res_mixer = BlockAttnResMixer(config.hidden_size, config.rms_norm_eps, config.attnres_backend)
 
+    def _attend_normed(self, hidden, rotary, paged_kv_cache, batch) -> torch.Tensor:
+        """input_layernorm + qkv projection (fused for <= 64 rows) + attention."""
+        attn = self.self_attn
+        backend = attn._attn_backend
+        if hidden.shape[0] > ops.MAX_NORM_ROWS or not isinstance(backend, B200AttentionBackend):
+            return attn.attend(self.input_layernorm.forward(hidden), rotary, paged_kv_cache, batch)
+        norm = self.input_layernorm
+        qkv = ops.linear_rmsnorm(hidden, None, norm.weight, norm.eps, attn.qkv_proj.weight)
+        cos, sin = rotary.tables()
+        return backend.forward_qkv(qkv, attn.q_norm.weight, attn.k_norm.weight, cos, sin, paged_kv_cache,
+                                   attn._layer_idx, batch)
+
     def forward(
         self,
         bank: torch.Tensor,
@@ -89,14 +101,19 @@ class MiniMindAttnResDecoderLayer(BaseOP):
         out: torch.Tensor | None = None,
     ) -> torch.Tensor:
         hidden = self.attn_res_mixer.forward(bank, partial, output_buffer=mixed)
-        attn = self.self_attn.attend(self.input_layernorm.forward(hidden), rotary, paged_kv_cache, batch)
+        attn = self._attend_normed(hidden, rotary, paged_kv_cache, batch)
         w_o = self.self_attn.o_proj.weight
         if partial is None:
             partial = ops.linear(attn, w_o)
         else:
             ops.linear(attn, w_o, out=partial, epilogue=_lib.EPI_ADD, residual=partial)
         hidden = self.mlp_res_mixer.forward(bank, partial, output_buffer=mixed)
-        act = self.mlp.gate_up_proj.forward_silu_mul(self.post_attention_layernorm.forward(hidden))
+        if hidden.shape[0] <= ops.MAX_NORM_ROWS:
+            norm = self.post_attention_layernorm
+            act = ops.linear_rmsnorm(hidden, None, norm.weight, norm.eps, self.mlp.gate_up_proj.packed_weight(),
+                                     epilogue=_lib.EPI_SILU_MUL)
+        else:
+            act = self.mlp.gate_up_proj.forward_silu_mul(self.post_attention_layernorm.forward(hidden))
         target = partial if out is None else out
         ops.linear(act, self.mlp.down_proj.weight, out=target, epilogue=_lib.EPI_ADD, residual=partial)
         return target
@@ -117,7 +134,8 @@ class MiniMindBlockAttnResModel(BaseOP):
         self._num_blocks = config.attnres_num_blocks
         self._layers_per_block = config.layers_per_attnres_block
 
-    def forward(self) -> torch.Tensor:
+    def forward_hidden(self) -> torch.Tensor:
+        """Trunk up to the final mixer (before the final norm)."""
         ctx = get_global_ctx()
         batch = ctx.batch
         ids = batch.input_ids
@@ -140,8 +158,10 @@ class MiniMindBlockAttnResModel(BaseOP):
                     out=bank_storage[source_count] if index == last else None,
                 )
             source_count += 1
-        hidden_states = self.final_attn_res_mixer.forward(bank_storage[:source_count], output_buffer=mixed)
-        return self.norm.forward(hidden_states)
+        return self.final_attn_res_mixer.forward(bank_storage[:source_count], output_buffer=mixed)
+
+    def forward(self) -> torch.Tensor:
+        return self.norm.forward(self.forward_hidden())
 
 
 class MiniMindIMEForCausalLM(Qwen3ForCausalLM):
@@ -163,4 +183,7 @@ class MiniMindIMEForCausalLM(Qwen3ForCausalLM):
         )
 
     def forward(self) -> torch.Tensor:
-        return self.lm_head.forward(self.model.forward())
+        if isinstance(self.model, MiniMindBlockAttnResModel):
+            norm = self.model.norm
+            return self.lm_head.forward_normed(self.model.forward_hidden(), None, norm.weight, norm.eps)
+        return super().forward()

@@ -13,7 +13,9 @@ from typing import TYPE_CHECKING
 import torch
 
 from ..attention import B200AttentionBackend, BaseAttentionBackend
+from .. import _lib
 from ..core import get_global_ctx
+from ..kernel import ops
 from ..layers import (
     BaseOP,
     Embedding,
@@ -97,11 +99,29 @@ class Qwen3DecoderLayer(BaseOP):
         self.post_attention_layernorm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
 
     def forward(self, hidden_states, rotary, paged_kv_cache, batch, residual):
-        hidden_states, residual = self.input_layernorm.forward(hidden_states, residual)
-        hidden_states = self.self_attn.forward(hidden_states, rotary, paged_kv_cache, batch)
-        hidden_states, residual = self.post_attention_layernorm.forward(hidden_states, residual)
-        hidden_states = self.mlp.forward(hidden_states)
-        return hidden_states, residual
+        if hidden_states.shape[0] > ops.MAX_NORM_ROWS or not isinstance(self.self_attn._attn_backend,
+                                                                      B200AttentionBackend):
+            hidden_states, residual = self.input_layernorm.forward(hidden_states, residual)
+            hidden_states = self.self_attn.forward(hidden_states, rotary, paged_kv_cache, batch)
+            hidden_states, residual = self.post_attention_layernorm.forward(hidden_states, residual)
+            return self.mlp.forward(hidden_states), residual
+        # Decode / short prefill: each residual add + RMSNorm runs inside the GEMM
+        # that consumes it (B operand built by the GEMM's CTAs), so a layer is
+        # qkv-GEMM, attention, o-GEMM, gate/up-GEMM(+SwiGLU), down-GEMM.
+        attn, mlp = self.self_attn, self.mlp
+        eps = self.input_layernorm.eps
+        new_res = None if residual is None else torch.empty_like(hidden_states)
+        qkv = ops.linear_rmsnorm(hidden_states, residual, self.input_layernorm.weight, eps, attn.qkv_proj.weight,
+                                 residual_out=new_res)
+        residual = hidden_states if residual is None else new_res
+        cos, sin = rotary.tables()
+        a = attn._attn_backend.forward_qkv(qkv, attn.q_norm.weight, attn.k_norm.weight, cos, sin, paged_kv_cache,
+                                           attn._layer_idx, batch)
+        o = attn.o_proj.forward(a)
+        new_res = torch.empty_like(o)
+        act = ops.linear_rmsnorm(o, residual, self.post_attention_layernorm.weight, eps,
+                                 mlp.gate_up_proj.packed_weight(), residual_out=new_res, epilogue=_lib.EPI_SILU_MUL)
+        return mlp.down_proj.forward(act), new_res
 
 
 class Qwen3Model(BaseOP):
@@ -112,13 +132,18 @@ class Qwen3Model(BaseOP):
         self.norm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
         self._rotary_emb = RotaryEmbedding(config.head_dim, config.max_position_embeddings, config.rope_theta)
 
-    def forward(self) -> torch.Tensor:
+    def forward_hidden(self) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """Decoder trunk without the final norm: (hidden, residual)."""
         ctx = get_global_ctx()
         batch = ctx.batch
         hidden_states = self.embed_tokens.forward(batch.input_ids)
         residual: torch.Tensor | None = None
         for layer in self.layers.op_list:
             hidden_states, residual = layer.forward(hidden_states, self._rotary_emb, ctx.kv_cache, batch, residual)
+        return hidden_states, residual
+
+    def forward(self) -> torch.Tensor:
+        hidden_states, residual = self.forward_hidden()
         return self.norm.forward(hidden_states, residual)[0]
 
 
@@ -134,4 +159,6 @@ class Qwen3ForCausalLM(BaseLLMModel):
         )
 
     def forward(self) -> torch.Tensor:
-        return self.lm_head.forward(self.model.forward())
+        hidden_states, residual = self.model.forward_hidden()
+        norm = self.model.norm
+        return self.lm_head.forward_normed(hidden_states, residual, norm.weight, norm.eps)

@@ -130,6 +130,18 @@ AIOSB_API int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* w
                            int64_t y_row_stride, int epilogue, const void* residual, int64_t residual_stride,
                            int32_t* status, void* stream);
 
+/* Linear with a fused RMSNorm on its input, for rows <= 64: y = (rmsnorm(x + res)
+ * * norm_w) W^T, with the epilogues of aiosb_linear. Replaces the pair
+ * RMSNormFused.forward (aios/layers/norm.py:25-39; res == NULL: plain RMSNorm,
+ * aios/layers/norm.py:10-22) + Linear.forward: the normalised rows are built by
+ * the GEMM's own CTAs straight into the tensor-core operand layout, and
+ * res_out (when not NULL) receives the new residual bf16(x + res); res_out must
+ * not alias x or res. x, res, res_out: [rows, k] contiguous bf16. */
+AIOSB_API int aiosb_linear_rmsnorm(const void* x, const void* res, void* res_out, const void* norm_w, float eps,
+                                   int64_t rows, int64_t k, const void* w, int64_t n, void* y, int64_t y_row_stride,
+                                   int epilogue, const void* residual, int64_t residual_stride, int32_t* status,
+                                   void* stream);
+
 /* ---- Attention ---------------------------------------------------------------
  * KV slots: token slot s of one layer lives at k_cache + s * num_kv_heads *
  * head_dim (the MHAKVCache layout [pages, page_size, Hkv, d] flattened); slot

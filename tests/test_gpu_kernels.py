@@ -315,3 +315,36 @@ def test_slot_fifo_matches_reference_order(cuda_device) -> None:
     model += b.cpu().tolist()
     c = ops.slot_alloc(ring, head, tail - head)
     assert c.cpu().tolist() == model
+
+
+@pytest.mark.parametrize("rows", [1, 8, 13, 33, 64])
+@pytest.mark.parametrize("with_res,epi", [(True, "store"), (False, "store"), (True, "silu")])
+def test_linear_with_fused_rmsnorm(cuda_device, rows: int, with_res: bool, epi: str) -> None:
+    g = torch.Generator().manual_seed(50 + rows)
+    k = 768
+    n = 4096 if epi == "silu" else 1280
+    x = torch.randn(rows, k, generator=g).to(torch.bfloat16)
+    r = torch.randn(rows, k, generator=g).to(torch.bfloat16) if with_res else None
+    nw = (1.0 + 0.1 * torch.randn(k, generator=g)).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    if with_res:
+        normed, new_res = oops.fused_add_rmsnorm(x, r, nw, 1e-6)
+    else:
+        normed, new_res = oops.rmsnorm(x, nw, 1e-6), None
+    ref = normed.float() @ w.float().T
+    dev = cuda_device
+    res_out = torch.empty(rows, k, dtype=torch.bfloat16, device=dev) if with_res else None
+    if epi == "silu":
+        y = ops.linear_rmsnorm(x.to(dev), None if r is None else r.to(dev), nw.to(dev), 1e-6,
+                               ops.pack_gate_up(w.to(dev)), residual_out=res_out, epilogue=_lib.EPI_SILU_MUL)
+        ref = oops.silu_and_mul(ref.to(torch.bfloat16))
+    else:
+        y = ops.linear_rmsnorm(x.to(dev), None if r is None else r.to(dev), nw.to(dev), 1e-6, w.to(dev),
+                               residual_out=res_out)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    # the normalised operand may differ from the oracle by one bf16 ulp (fp32 sum
+    # order), so allow 2 ulps on the output
+    _bf16_close(y, ref, ulps=2.0, atol=2e-3)
+    if with_res:
+        assert torch.equal(res_out.cpu(), new_res)
