@@ -147,6 +147,7 @@ _SIGNATURES = {
         _i32,
     ),
     "aiosb_stateless_uniforms": ([_p, _i64, _i64, _p, _p], _i32),
+    "aiosb_page_table_fill": ([_p, _i64, _i64, _i64, _p, _i64, _p], _i32),
     "aiosb_token_logprobs": ([_p, _i64, _i64, _i64, _p, _p, _p, _p], _i32),
     "aiosb_slot_alloc": ([_p, _i64, _i64, _i64, _p, _p], _i32),
     "aiosb_slot_free": ([_p, _i64, _i64, _p, _i64, _p], _i32),

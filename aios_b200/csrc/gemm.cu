@@ -16,6 +16,7 @@
 // keeps ~all SMs streaming weights even for 768-row projections; the partial
 // tiles are reduced deterministically through distributed shared memory.
 // No TMA load uses cluster multicast: each CTA loads its own K slice.
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -412,7 +413,13 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, GemmArgs a, int m_
 
 // Split-K factor: the largest divisor of the K chunk count (<= 16) that keeps
 // the grid within one wave of CTAs.
-int g_max_split = kMaxSplit;  // lowered to 8 if 16-CTA clusters cannot launch
+// Largest split-K cluster; AIOSB_GEMM_MAX_SPLIT (1..16) lowers it, and it drops
+// to 8 by itself if 16-CTA clusters cannot launch on the device.
+int g_max_split = [] {
+  const char* env = getenv("AIOSB_GEMM_MAX_SPLIT");
+  const int v = env ? atoi(env) : kMaxSplit;
+  return v >= 1 && v <= kMaxSplit ? v : kMaxSplit;
+}();
 
 int choose_split(int64_t tiles, int64_t chunks, int sms) {
   int best = 1;

@@ -155,7 +155,11 @@ __device__ int sample_row(RowSmem& s, float* row, int V, const SampleParams& p, 
       __syncthreads();
       for (int i = tid; i < V; i += blockDim.x) {
         const uint32_t key = order_key(row[i]);
-        if ((key & mask) == prefix) atomicAdd(&s.hist[warp][(key >> shift) & 0xFFu], 1u);
+        const bool hit = (key & mask) == prefix;
+        const unsigned bin = hit ? (key >> shift) & 0xFFu : 0x100u;
+        // warp-aggregated: one atomic per distinct bin (logit keys share their top bytes)
+        const unsigned peers = __match_any_sync(__activemask(), bin);
+        if (hit && (__ffs(peers) - 1) == lane) atomicAdd(&s.hist[warp][bin], (unsigned)__popc(peers));
       }
       __syncthreads();
       for (int b = tid; b < 256; b += blockDim.x) {
@@ -588,6 +592,19 @@ __global__ void __launch_bounds__(1024) slot_free_range_kernel(int32_t* ring, in
 
 size_t sample_smem(int V) { return sizeof(RowSmem) + (size_t)V * sizeof(float); }
 
+// Page-table reset for a keystroke: rows [0, rows) get the prefix slots in
+// columns [0, n) and zeros in [n, width) (the reference builds a fresh zero table
+// per keystroke and writes the prefix slots into every row, aios/ime.py:482-485,1155).
+__global__ void page_table_fill_kernel(int32_t* __restrict__ table, int64_t stride, int rows, int width,
+                                       const int32_t* __restrict__ prefix, int n) {
+  pdl_enter();
+  const int64_t total = (int64_t)rows * width;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / width), c = (int)(i % width);
+    table[(int64_t)r * stride + c] = c < n ? prefix[c] : 0;
+  }
+}
+
 // Raw log-probability of a given target per row (teacher-forced scoring).
 __global__ void __launch_bounds__(kSampThreads)
     token_logprob_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int V,
@@ -679,6 +696,19 @@ extern "C" int aiosb_token_logprobs(const void* logits, int64_t rows, int64_t vo
                              sample_smem((int)vocab), as_stream(stream), (const __nv_bfloat16*)logits, row_stride,
                              (int)vocab, targets, out, status);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "token_logprobs: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_page_table_fill(int32_t* table, int64_t stride, int64_t rows, int64_t width,
+                                     const int32_t* prefix, int64_t n, void* stream) {
+  AIOSB_REQUIRE(rows >= 0 && width >= 0 && n >= 0 && n <= width && stride >= width, AIOSB_ERR_INVALID_ARG,
+                "page_table_fill: bad sizes");
+  if (rows == 0 || width == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(table && (n == 0 || prefix), AIOSB_ERR_INVALID_ARG, "page_table_fill: null pointer");
+  const int64_t total = rows * width;
+  cudaError_t e = launch_pdl(page_table_fill_kernel, dim3((unsigned)std::min<int64_t>((total + 255) / 256, 148)),
+                             dim3(256), 0, as_stream(stream), table, stride, (int)rows, (int)width, prefix, (int)n);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "page_table_fill: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }
 

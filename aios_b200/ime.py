@@ -46,6 +46,7 @@ from .ime_text import (  # noqa: F401  (re-exported public names)
 )
 from .kernel import ops
 from .runtime.group import CandidateGroupRuntime, RoundResult
+from .runtime.prefill import PrefixRunner
 
 TERMINAL_SYMBOLS = "。！？；!?;"
 
@@ -94,8 +95,8 @@ class ImeCompletionEngine:
         self._generation_lock = threading.Lock()
         self._run_lock = threading.Lock()
         self._prefix_token_ids: list[int] = []
-        self._prefix_pages: torch.Tensor | None = None
-        self._prefix_slots: torch.Tensor | None = None
+        self._prefix_pages: list[int] | None = None
+        self._prefix_slots: list[int] | None = None
         self._prefix_logits: torch.Tensor | None = None
         self.page_size = llm.cache_manager.page_size
         self._page_table = torch.zeros(
@@ -111,6 +112,7 @@ class ImeCompletionEngine:
         eos = llm.tokenizer.eos_token_id
         self._minlen_ids = sorted({*self._terminal_token_ids, *((eos,) if eos is not None else ())})
         self._runtime = CandidateGroupRuntime(llm)
+        self._prefix_runner = PrefixRunner(llm)
 
     # ------------------------------------------------------------------ API
     def new_generation(self) -> CancellationToken:
@@ -127,8 +129,8 @@ class ImeCompletionEngine:
             self._reset_prefix_cache_unlocked()
 
     def _reset_prefix_cache_unlocked(self) -> None:
-        if self._prefix_pages is not None and len(self._prefix_pages):
-            self.llm.cache_manager._free(self._prefix_pages)
+        if self._prefix_pages:
+            self.llm.cache_manager.give(self._prefix_pages)
         self._prefix_token_ids = []
         self._prefix_pages = None
         self._prefix_slots = None
@@ -217,9 +219,9 @@ class ImeCompletionEngine:
         started.record()
         cancelled = False
         cm = self.llm.cache_manager
-        # a fresh table per keystroke, as the reference allocates one (aios/ime.py:482-485)
-        self._page_table[:max_attempts].zero_()
-        prefix_logits, prefix_pages, reused = self._prepare_prefix(token_ids, max_attempts)
+        # rows [0, max_attempts) are reset to the prefix + zeros, like the fresh
+        # table the reference allocates per keystroke (aios/ime.py:482-485)
+        prefix_logits, prefix_pages, reused = self._prepare_prefix(token_ids, max_attempts, max_total_len)
         peak_unique_pages = len(prefix_pages)
         raw_candidates: list[ImeCandidate] = []
         actual_attempts = 0
@@ -330,66 +332,44 @@ class ImeCompletionEngine:
         return out
 
     # ------------------------------------------------------------------ prefix
-    def _slots_for_pages(self, pages: torch.Tensor, start_token: int, count: int) -> torch.Tensor:
-        """Token slots [start_token, start_token + count) of a prefix laid out on `pages`."""
+    def _slots_for_pages(self, pages: list[int], count: int) -> list[int]:
+        """Token slots [0, count) of a prefix laid out on `pages` (page_size slots each)."""
         p = self.page_size
-        idx = torch.arange(start_token, start_token + count, device=pages.device)
-        return (pages.long()[idx // p] * p + idx % p).to(torch.int32)
+        if p == 1:
+            return list(pages[:count])
+        return [pages[t // p] * p + t % p for t in range(count)]
 
-    def _prepare_prefix(self, token_ids: list[int], table_rows: int) -> tuple[torch.Tensor, torch.Tensor, int]:
+    def _prepare_prefix(self, token_ids: list[int], table_rows: int, width: int) -> tuple[torch.Tensor, list[int], int]:
         """Build or incrementally extend the persistent latest-prefix KV
-        (aios/ime.py:1116-1168); returns (logits [1, V], prefix pages, reused)."""
+        (aios/ime.py:1116-1168); resets page-table rows [0, table_rows) to the
+        prefix (zeros up to `width`); returns (logits [1, V], prefix pages, reused).
+        Slot ids are known on the host (the FIFO has an exact host mirror), so the
+        prefill inputs travel in one copy and the forward replays as a CUDA graph."""
         cm = self.llm.cache_manager
         old_ids = self._prefix_token_ids
         old_pages = self._prefix_pages
         reused = token_longest_common_prefix(old_ids, token_ids)
         n = len(token_ids)
         if old_pages is not None and self._prefix_logits is not None and reused == len(old_ids) == n:
-            self._page_table[:table_rows, :n] = self._prefix_slots.unsqueeze(0)
+            self._prefix_runner.fill_table(self._page_table, table_rows, width, n)
             return self._prefix_logits, old_pages, reused
         # Backspace only: the old cache holds no logits at the new last token.
         if old_ids and reused == n < len(old_ids):
             reused = 0
-        p = self.page_size
         keep_pages = self._pages_for(reused)
+        kept: list[int] = []
         if old_pages is not None:
-            released = old_pages[keep_pages:]
             kept = old_pages[:keep_pages]
-            if len(released):
-                cm._free(released)
-        else:
-            kept = torch.empty(0, dtype=torch.int32, device=self.llm.device)
-        new_pages = cm.allocate(self._pages_for(n) - keep_pages)
-        prefix_pages = torch.cat([kept, new_pages]) if len(kept) else new_pages
-        if p == 1:
-            prefix_slots = prefix_pages
-        else:
-            prefix_slots = self._slots_for_pages(prefix_pages, 0, n)
-        self._page_table[:table_rows, :n] = prefix_slots.unsqueeze(0)
-        logits = self._forward_prefix(token_ids, reused, prefix_slots[reused:])
+            if len(old_pages) > keep_pages:
+                cm.give(old_pages[keep_pages:])
+        prefix_pages = kept + cm.take(self._pages_for(n) - keep_pages)
+        prefix_slots = self._slots_for_pages(prefix_pages, n)
+        logits = self._prefix_runner.run(token_ids, reused, prefix_slots, self._page_table, table_rows, width)
         self._prefix_token_ids = list(token_ids)
         self._prefix_pages = prefix_pages
         self._prefix_slots = prefix_slots
         self._prefix_logits = logits
         return logits, prefix_pages, reused
-
-    def _forward_prefix(self, token_ids: list[int], cached_len: int, out_slots: torch.Tensor) -> torch.Tensor:
-        """One prefill (or extension prefill) of tokens [cached_len, len) into row 0
-        of the page table (aios/ime.py:1170-1217)."""
-        dev = self.llm.device
-        req = Req(input_ids=torch.empty(len(token_ids), dtype=torch.long), cached_len=cached_len, output_len=1,
-                  uid=0, sampling_params=SamplingParams(max_tokens=1), table_idx=0)
-        batch = Batch(reqs=[req], phase="prefill")
-        host = torch.tensor([*token_ids[cached_len:], *range(cached_len, len(token_ids))], dtype=torch.int32)
-        staged = host.pin_memory().to(dev, non_blocking=True)
-        ops.transfer_bytes["h2d"] += 4 * host.numel()
-        new = len(token_ids) - cached_len
-        batch.input_ids = staged[:new]
-        batch.positions = staged[new:]
-        batch.out_loc = out_slots
-        self.llm.model.attn_backend.prepare_metadata(batch)
-        with self.llm.ctx.forward_batch(batch):
-            return self.llm.model.forward()
 
     # ------------------------------------------------------------------ scoring
     @torch.inference_mode()
@@ -431,24 +411,26 @@ class ImeCompletionEngine:
         started = torch.cuda.Event(enable_timing=True)
         ended = torch.cuda.Event(enable_timing=True)
         started.record()
-        allocated: list[torch.Tensor] = []
+        allocated: list[int] = []
         try:
             reqs, slots = [], []
+            table_rows = torch.zeros((len(sequences), max_total), dtype=torch.int32)
             for row, seq in enumerate(sequences):
-                pages = cm.allocate(self._pages_for(len(seq)))
-                allocated.append(pages)
-                s = pages if self.page_size == 1 else self._slots_for_pages(pages, 0, len(seq))
-                self._page_table[row, : len(seq)] = s
-                slots.append(s)
+                pages = cm.take(self._pages_for(len(seq)))
+                allocated += pages
+                s = self._slots_for_pages(pages, len(seq))
+                table_rows[row, : len(seq)] = torch.tensor(s, dtype=torch.int32)
+                slots += s
                 reqs.append(Req(input_ids=torch.empty(len(seq), dtype=torch.long), cached_len=0, output_len=1,
                                 uid=row, sampling_params=SamplingParams(max_tokens=1), table_idx=row))
+            self._page_table[: len(sequences), :max_total].copy_(table_rows.pin_memory(), non_blocking=True)
             batch = Batch(reqs=reqs, phase="prefill", return_all_logits=True)
             flat = [t for s in sequences for t in s]
             pos = [i for s in sequences for i in range(len(s))]
-            staged = torch.tensor(flat + pos, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+            staged = torch.tensor(flat + pos + slots, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
             batch.input_ids = staged[: len(flat)]
-            batch.positions = staged[len(flat) :]
-            batch.out_loc = torch.cat(slots)
+            batch.positions = staged[len(flat) : 2 * len(flat)]
+            batch.out_loc = staged[2 * len(flat) :]
             self.llm.model.attn_backend.prepare_metadata(batch)
             with self.llm.ctx.forward_batch(batch):
                 logits = self.llm.model.forward()
@@ -479,12 +461,12 @@ class ImeCompletionEngine:
             scored.sort(key=lambda item: item.average_logprob, reverse=True)
             return ImeScoringResult(
                 prefix=prefix, candidates=tuple(scored), latency_ms=(time.perf_counter() - wall_started) * 1000.0,
-                gpu_latency_ms=started.elapsed_time(ended), unique_kv_pages=sum(len(p) for p in allocated),
+                gpu_latency_ms=started.elapsed_time(ended), unique_kv_pages=len(allocated),
                 reused_prefix_tokens=0,
             )
         finally:
             if allocated:
-                cm._free(torch.cat(allocated))
+                cm.give(allocated)
 
     def _score_shared_locked(self, prefix: str, candidates: list[str]) -> ImeScoringResult:
         wall_started = time.perf_counter()
@@ -511,9 +493,9 @@ class ImeCompletionEngine:
         started = torch.cuda.Event(enable_timing=True)
         ended = torch.cuda.Event(enable_timing=True)
         started.record()
-        allocated: list[torch.Tensor] = []
+        allocated: list[int] = []
         try:
-            prefix_logits, prefix_pages, reused = self._prepare_prefix(prefix_ids, len(candidates))
+            prefix_logits, prefix_pages, reused = self._prepare_prefix(prefix_ids, len(candidates), max_total)
             sums = torch.zeros(len(candidates), dtype=torch.float32, device=dev)
             first = [i for i, ids in enumerate(cand_ids) if ids]
             if first:
@@ -525,18 +507,19 @@ class ImeCompletionEngine:
                 if not active:
                     break
                 cached_len = len(prefix_ids) + step - 1
-                pages = cm.allocate(len(active))
-                allocated.append(pages)
-                self._page_table[torch.tensor(active, device=dev), cached_len] = pages
+                pages = cm.take(len(active))
+                allocated += pages
                 reqs = [Req(input_ids=torch.empty(cached_len + 1, dtype=torch.long), cached_len=cached_len,
                             output_len=1, uid=i, sampling_params=SamplingParams(max_tokens=1), table_idx=i)
                         for i in active]
                 batch = Batch(reqs=reqs, phase="decode")
-                host = [cand_ids[i][step - 1] for i in active] + [cached_len] * len(active)
+                host = [cand_ids[i][step - 1] for i in active] + [cached_len] * len(active) + pages + active
                 staged = torch.tensor(host, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
-                batch.input_ids = staged[: len(active)]
-                batch.positions = staged[len(active) :]
-                batch.out_loc = pages
+                n_act = len(active)
+                batch.input_ids = staged[:n_act]
+                batch.positions = staged[n_act : 2 * n_act]
+                batch.out_loc = staged[2 * n_act : 3 * n_act]
+                self._page_table[staged[3 * n_act :].long(), cached_len] = batch.out_loc
                 self.llm.model.attn_backend.prepare_metadata(batch)
                 with self.llm.ctx.forward_batch(batch):
                     logits = self.llm.model.forward()
@@ -555,8 +538,8 @@ class ImeCompletionEngine:
             return ImeScoringResult(
                 prefix=prefix, candidates=tuple(scored), latency_ms=(time.perf_counter() - wall_started) * 1000.0,
                 gpu_latency_ms=started.elapsed_time(ended),
-                unique_kv_pages=len(prefix_pages) + sum(len(p) for p in allocated), reused_prefix_tokens=reused,
+                unique_kv_pages=len(prefix_pages) + len(allocated), reused_prefix_tokens=reused,
             )
         finally:
             if allocated:
-                cm._free(torch.cat(allocated))
+                cm.give(allocated)

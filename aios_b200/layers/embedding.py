@@ -54,19 +54,17 @@ class LMHead(BaseOP):
 
     def forward_normed(self, x: torch.Tensor, residual: torch.Tensor | None, norm_weight: torch.Tensor,
                        eps: float) -> torch.Tensor:
-        """LM head on rmsnorm(x + residual) * norm_weight: the final norm runs
-        inside the LM-head GEMM (rows <= 64), only for the rows that need logits."""
+        """LM head on rmsnorm(x + residual) * norm_weight, computed only for the
+        rows that need logits (the last token of each prefill request)."""
         batch = get_global_ctx().batch
         x, residual = self._select(batch, x, residual)
-        if x.shape[0] > ops.MAX_NORM_ROWS:
-            if residual is None:
-                h = ops.rmsnorm(x.contiguous(), norm_weight, eps)
-            else:
-                h = x.contiguous().clone()
-                ops.fused_add_rmsnorm(h, residual.contiguous().clone(), norm_weight, eps)
-            return ops.linear(h, self._w(), out=batch.logits_out)
-        return ops.linear_rmsnorm(x.contiguous(), None if residual is None else residual.contiguous(), norm_weight,
-                                  eps, self._w(), out=batch.logits_out)
+        if residual is None:
+            h = ops.rmsnorm(x.contiguous(), norm_weight, eps)
+        else:
+            h = x.contiguous().clone() if not x.is_contiguous() else x
+            r = residual.contiguous().clone() if not residual.is_contiguous() else residual
+            ops.fused_add_rmsnorm(h, r, norm_weight, eps)
+        return ops.linear(h, self._w(), out=batch.logits_out)
 
     def load_state_dict(self, state_dict: Dict[str, torch.Tensor], *, prefix: str = "", _internal: bool = False) -> None:
         if self._tie_word_embeddings:

@@ -80,15 +80,7 @@ class MiniMindAttnResDecoderLayer(BaseOP):
 
     def _attend_normed(self, hidden, rotary, paged_kv_cache, batch) -> torch.Tensor:
         """input_layernorm + qkv projection (fused for <= 64 rows) + attention."""
-        attn = self.self_attn
-        backend = attn._attn_backend
-        if hidden.shape[0] > ops.MAX_NORM_ROWS or not isinstance(backend, B200AttentionBackend):
-            return attn.attend(self.input_layernorm.forward(hidden), rotary, paged_kv_cache, batch)
-        norm = self.input_layernorm
-        qkv = ops.linear_rmsnorm(hidden, None, norm.weight, norm.eps, attn.qkv_proj.weight)
-        cos, sin = rotary.tables()
-        return backend.forward_qkv(qkv, attn.q_norm.weight, attn.k_norm.weight, cos, sin, paged_kv_cache,
-                                   attn._layer_idx, batch)
+        return self.self_attn.attend(self.input_layernorm.forward(hidden), rotary, paged_kv_cache, batch)
 
     def forward(
         self,
@@ -108,12 +100,7 @@ class MiniMindAttnResDecoderLayer(BaseOP):
         else:
             ops.linear(attn, w_o, out=partial, epilogue=_lib.EPI_ADD, residual=partial)
         hidden = self.mlp_res_mixer.forward(bank, partial, output_buffer=mixed)
-        if hidden.shape[0] <= ops.MAX_NORM_ROWS:
-            norm = self.post_attention_layernorm
-            act = ops.linear_rmsnorm(hidden, None, norm.weight, norm.eps, self.mlp.gate_up_proj.packed_weight(),
-                                     epilogue=_lib.EPI_SILU_MUL)
-        else:
-            act = self.mlp.gate_up_proj.forward_silu_mul(self.post_attention_layernorm.forward(hidden))
+        act = self.mlp.gate_up_proj.forward_silu_mul(self.post_attention_layernorm.forward(hidden))
         target = partial if out is None else out
         ops.linear(act, self.mlp.down_proj.weight, out=target, epilogue=_lib.EPI_ADD, residual=partial)
         return target

@@ -99,29 +99,10 @@ class Qwen3DecoderLayer(BaseOP):
         self.post_attention_layernorm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
 
     def forward(self, hidden_states, rotary, paged_kv_cache, batch, residual):
-        if hidden_states.shape[0] > ops.MAX_NORM_ROWS or not isinstance(self.self_attn._attn_backend,
-                                                                      B200AttentionBackend):
-            hidden_states, residual = self.input_layernorm.forward(hidden_states, residual)
-            hidden_states = self.self_attn.forward(hidden_states, rotary, paged_kv_cache, batch)
-            hidden_states, residual = self.post_attention_layernorm.forward(hidden_states, residual)
-            return self.mlp.forward(hidden_states), residual
-        # Decode / short prefill: each residual add + RMSNorm runs inside the GEMM
-        # that consumes it (B operand built by the GEMM's CTAs), so a layer is
-        # qkv-GEMM, attention, o-GEMM, gate/up-GEMM(+SwiGLU), down-GEMM.
-        attn, mlp = self.self_attn, self.mlp
-        eps = self.input_layernorm.eps
-        new_res = None if residual is None else torch.empty_like(hidden_states)
-        qkv = ops.linear_rmsnorm(hidden_states, residual, self.input_layernorm.weight, eps, attn.qkv_proj.weight,
-                                 residual_out=new_res)
-        residual = hidden_states if residual is None else new_res
-        cos, sin = rotary.tables()
-        a = attn._attn_backend.forward_qkv(qkv, attn.q_norm.weight, attn.k_norm.weight, cos, sin, paged_kv_cache,
-                                           attn._layer_idx, batch)
-        o = attn.o_proj.forward(a)
-        new_res = torch.empty_like(o)
-        act = ops.linear_rmsnorm(o, residual, self.post_attention_layernorm.weight, eps,
-                                 mlp.gate_up_proj.packed_weight(), residual_out=new_res, epilogue=_lib.EPI_SILU_MUL)
-        return mlp.down_proj.forward(act), new_res
+        hidden_states, residual = self.input_layernorm.forward(hidden_states, residual)
+        hidden_states = self.self_attn.forward(hidden_states, rotary, paged_kv_cache, batch)
+        hidden_states, residual = self.post_attention_layernorm.forward(hidden_states, residual)
+        return self.mlp.forward(hidden_states), residual
 
 
 class Qwen3Model(BaseOP):

@@ -300,7 +300,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     if world > 1:
         dist.barrier()
     rt = engine._runtime
-    h2d0 = rt.h2d_bytes + ops.transfer_bytes["h2d"]
+    pr = engine._prefix_runner
+    h2d0 = rt.h2d_bytes + pr.h2d_bytes + ops.transfer_bytes["h2d"]
     d2h0 = rt.d2h_bytes + ops.transfer_bytes["d2h"]
     launches0 = _lib.launches
     stream = torch.cuda.current_stream(dev)
@@ -320,7 +321,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         wall = time.perf_counter() - wall0
     device_ms = start.elapsed_time(end)
     launches = _lib.launches - launches0
-    h2d = (rt.h2d_bytes + ops.transfer_bytes["h2d"] - h2d0) / args.steps
+    h2d = (rt.h2d_bytes + pr.h2d_bytes + ops.transfer_bytes["h2d"] - h2d0) / args.steps
     d2h = (rt.d2h_bytes + ops.transfer_bytes["d2h"] - d2h0) / args.steps
     t = torch.tensor([device_ms, wall], dtype=torch.float64, device=dev)
     if world > 1:

@@ -229,6 +229,11 @@ AIOSB_API int aiosb_slot_alloc(const int32_t* ring, int64_t capacity, int64_t he
 AIOSB_API int aiosb_slot_free(int32_t* ring, int64_t capacity, int64_t tail, const int32_t* slots, int64_t n, void* stream);
 AIOSB_API int aiosb_slot_free_range(int32_t* ring, int64_t capacity, int64_t begin, int64_t n, int64_t tail, void* stream);
 
+/* Keystroke page-table reset (aios/ime.py:482-485, 1155): rows [0, rows) of the
+ * table get prefix[0..n) in columns [0, n) and zeros in [n, width). */
+AIOSB_API int aiosb_page_table_fill(int32_t* table, int64_t stride, int64_t rows, int64_t width,
+                                   const int32_t* prefix, int64_t n, void* stream);
+
 /* ---- CandidateGroup step -----------------------------------------------------
  * Device state of one branch batch (aios/ime.py:891-1054), written by the host
  * at round start and advanced by aiosb_group_step. */
