@@ -1,14 +1,19 @@
 // Raw-logprob sampler (replaces aios/engine/sample.py:54-163) and the
 // CandidateGroup step bookkeeping of aios/ime.py:970-1054, on the device.
 //
-// One CTA samples one logits row, entirely in shared memory:
+// One CTA samples one logits row; the row lives in registers (16-byte loads)
+// and its sampling keys in shared memory:
 //   raw log-softmax of the bf16 logits (fp32, aios/engine/sample.py:74);
-//   forbidden ids -> -inf on the sampling copy only (sample.py:76-111);
+//   forbidden ids -> -inf on the sampling copy only (sample.py:76-111), kept as
+//   a bitmap;
 //   greedy: first index of the maximum (torch argmax);
-//   otherwise: scaled = logits / T (fp32), top-k by an exact 4-pass radix select
-//   of the k-th largest key, candidates sorted by (value desc, token id asc),
-//   softmax, top-p keep-mask with the one-position shift of sample.py:140-146,
-//   re-softmax, index = #(cumsum < u) clamped (sample.py:161-165).
+//   otherwise: scaled = logits / T (fp32) as order-preserving uint32 keys;
+//   top-k <= 512: a lower bound of the k-th largest key from the 512 thread
+//   maxima, then only the keys above it are compacted and sorted; larger k (or a
+//   degenerate row) by an exact 4-pass radix select; candidates sorted by
+//   (value desc, token id asc), softmax, top-p keep-mask with the one-position
+//   shift of sample.py:140-146, re-softmax, index = #(cumsum < u) clamped
+//   (sample.py:161-165).
 // Cumulative sums accumulate in fp64 and round each prefix to fp32, the way
 // torch's CPU cumsum does for float tensors. Equal logits are ordered by
 // ascending token id; torch.topk leaves that order unspecified.
@@ -23,6 +28,9 @@ namespace {
 constexpr int kSampThreads = 512;
 constexpr int kMaxVocab = 32768;
 constexpr int kMaxSortK = 2048;  // candidates sorted in shared memory (top-k path)
+constexpr int kVecPer = kMaxVocab / 8 / kSampThreads;  // 8-token groups a thread holds in registers
+constexpr int kBanWords = kMaxVocab / 32;
+constexpr int kFastTopK = 512;  // top-k bound of the thread-maximum threshold path
 
 struct SampleParams {
   float temperature;
@@ -36,20 +44,36 @@ __device__ __forceinline__ uint32_t order_key(float v) {
   const uint32_t u = __float_as_uint(v);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+// Inverse of order_key.
+__device__ __forceinline__ float key_value(uint32_t key) {
+  return __uint_as_float((key & 0x80000000u) ? (key & 0x7fffffffu) : ~key);
+}
 
-// Fixed part of the per-CTA shared memory; the fp32 logits row (V floats)
-// follows it in dynamic shared memory.
-struct RowSmem {
+// Fixed part of the per-CTA shared memory; the uint32 order keys of the
+// sampling values (V entries) follow it in dynamic shared memory.
+struct alignas(16) RowSmem {
   unsigned long long cand[kMaxSortK];   // (~key << 32 | id) sort keys
   float cval[kMaxSortK];                // candidate scaled logits in sorted order
   int cid[kMaxSortK];
-  float prob[kMaxSortK];
   unsigned int hist[kSampThreads / 32][256];  // per-warp private radix histograms
   unsigned int hsum[256];
+  unsigned int ban[kBanWords];          // forbidden-id bitmap of the sampling copy
+  double dred[32];
   float red[32];
   int ired[32];
   int misc[8];
 };
+
+// The bf16 logits row in registers: thread t holds the 8-token groups
+// t, t + 512, t + 1024, ... (16-byte loads).
+struct RowRegs {
+  uint4 v[kVecPer];
+};
+
+__device__ __forceinline__ float group_elem(const uint4& g, int e) {
+  const uint32_t w = e < 4 ? (e < 2 ? g.x : g.y) : (e < 6 ? g.z : g.w);
+  return (e & 1) ? bf16_hi(w) : bf16_lo(w);
+}
 
 // Block reduction of (value, index): max value, lowest index among ties.
 __device__ __forceinline__ void block_argmax(float v, int i, RowSmem& s, float& out_v, int& out_i) {
@@ -111,25 +135,395 @@ __device__ __forceinline__ int block_exclusive_scan(int x, RowSmem& s, int& tota
   return res;
 }
 
-// Samples one row held in row[0..V) (sampling logits, forbidden already -inf).
-// Returns the token id (same value in every thread).
-__device__ int sample_row(RowSmem& s, float* row, int V, const SampleParams& p, float u) {
-  const int tid = threadIdx.x;
-  if (p.greedy) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = tid; i < V; i += blockDim.x) {
-      const float v = row[i];
-      if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
-    }
-    float mv;
-    int mi;
-    block_argmax(bv, bi, s, mv, mi);
-    return mi == 0x7fffffff ? 0 : mi;
+// Exclusive block scan of one double per thread. Callers use it only when every
+// partial sum is exactly representable, so the association order is irrelevant.
+__device__ __forceinline__ double block_exclusive_scan_f64(double x, RowSmem& s) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double incl = x;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
   }
-  // scaled = sampling_logits.float() / temperature  (sample.py:120)
-  for (int i = tid; i < V; i += blockDim.x) row[i] = row[i] / p.temperature;
   __syncthreads();
+  if (lane == 31) s.dred[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    const double w = lane < nw ? s.dred[lane] : 0.0;
+    double wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    if (lane < nw) s.dred[lane] = wi - w;
+  }
+  __syncthreads();
+  const double res = s.dred[warp] + (incl - x);
+  __syncthreads();
+  return res;
+}
+
+// Loads a bf16 logits row into registers, clears the forbidden bitmap and returns
+// the raw log-softmax pieces (max, log-sum-exp) of the unmasked row
+// (aios/engine/sample.py:74). Ends with a barrier.
+__device__ __forceinline__ void load_row(RowSmem& s, RowRegs& rr, const __nv_bfloat16* lrow, int V, float& mx,
+                                         float& lse) {
+  const int tid = threadIdx.x;
+  const int ngroups = (V + 7) >> 3;
+  const bool vec = (reinterpret_cast<uintptr_t>(lrow) & 15u) == 0;
+  const uint16_t* h = reinterpret_cast<const uint16_t*>(lrow);
+#pragma unroll
+  for (int q = 0; q < kVecPer; ++q) {
+    const int j = tid + q * kSampThreads;
+    uint4 x = make_uint4(0u, 0u, 0u, 0u);
+    if (j < ngroups) {
+      if (vec && 8 * j + 8 <= V) {
+        x = *reinterpret_cast<const uint4*>(lrow + 8 * j);
+      } else {  // ragged tail or a row that is not 16-byte aligned
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        for (int e = 0; e < 8; ++e)
+          if (8 * j + e < V) w[e >> 1] |= (uint32_t)h[8 * j + e] << ((e & 1) * 16);
+        x = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    rr.v[q] = x;
+  }
+  for (int w = tid; w < (V + 31) / 32; w += kSampThreads) s.ban[w] = 0u;
+  float m = -INFINITY;
+#pragma unroll
+  for (int q = 0; q < kVecPer; ++q) {
+    const int j = tid + q * kSampThreads;
+    if (j < ngroups) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (8 * j + e < V) m = fmaxf(m, group_elem(rr.v[q], e));
+    }
+  }
+  m = block_max(m, s.red);
+  float se = 0.f;
+#pragma unroll
+  for (int q = 0; q < kVecPer; ++q) {
+    const int j = tid + q * kSampThreads;
+    if (j < ngroups) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (8 * j + e < V) se += expf(group_elem(rr.v[q], e) - m);
+    }
+  }
+  se = block_sum(se, s.red);
+  mx = m;
+  lse = logf(se);
+  __syncthreads();
+}
+
+// Forbids one id on the sampling copy (-inf, aios/engine/sample.py:76-111).
+__device__ __forceinline__ void ban_id(RowSmem& s, int id) { atomicOr(&s.ban[id >> 5], 1u << (id & 31)); }
+
+// Writes the order keys of the sampling values (forbidden -> -inf, then
+// scaled = value / temperature, aios/engine/sample.py:120) into keys[] and
+// returns the thread's largest key (0 when it holds no token).
+__device__ __forceinline__ uint32_t make_keys(const RowSmem& s, const RowRegs& rr, uint32_t* keys, int V,
+                                              float temperature) {
+  const int ngroups = (V + 7) >> 3;
+  uint32_t best = 0u;
+#pragma unroll
+  for (int q = 0; q < kVecPer; ++q) {
+    const int j = threadIdx.x + q * kSampThreads;
+    if (j < ngroups) {
+      const uint32_t bits = s.ban[j >> 2] >> ((j & 3) * 8);  // 8 tokens of a group share a word
+      uint32_t kk[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float v = group_elem(rr.v[q], e);
+        if ((bits >> e) & 1u) v = -INFINITY;
+        kk[e] = 8 * j + e < V ? order_key(v / temperature) : 0u;
+        best = kk[e] > best ? kk[e] : best;
+      }
+      if (8 * j + 8 <= V) {
+        *reinterpret_cast<uint4*>(keys + 8 * j) = make_uint4(kk[0], kk[1], kk[2], kk[3]);
+        *reinterpret_cast<uint4*>(keys + 8 * j + 4) = make_uint4(kk[4], kk[5], kk[6], kk[7]);
+      } else {
+        for (int e = 0; e < 8; ++e)
+          if (8 * j + e < V) keys[8 * j + e] = kk[e];
+      }
+    }
+  }
+  return best;
+}
+
+// Greedy: first index of the maximum of the masked (unscaled) row (torch argmax).
+__device__ __forceinline__ int greedy_pick(RowSmem& s, const RowRegs& rr, int V) {
+  const int ngroups = (V + 7) >> 3;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+#pragma unroll
+  for (int q = 0; q < kVecPer; ++q) {
+    const int j = threadIdx.x + q * kSampThreads;
+    if (j < ngroups) {
+      const uint32_t bits = s.ban[j >> 2] >> ((j & 3) * 8);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int i = 8 * j + e;
+        float v = group_elem(rr.v[q], e);
+        if ((bits >> e) & 1u) v = -INFINITY;
+        if (i < V && (v > bv || (v == bv && i < bi))) { bv = v; bi = i; }
+      }
+    }
+  }
+  float mv;
+  int mi;
+  block_argmax(bv, bi, s, mv, mi);
+  return mi == 0x7fffffff ? 0 : mi;
+}
+
+// Number of leading prefixes i of the probability sequence prob(0..k) with
+// fl32(cumsum_i) < thr (strict) or <= thr. The cumulative sums accumulate in fp64
+// and each prefix rounds to fp32, as torch's CPU cumsum does for float tensors.
+// When every non-zero probability is >= 2^-29, every fp64 partial sum (< 2) is an
+// exact multiple of 2^-52, so a parallel scan reproduces the sequential sums bit
+// for bit; otherwise thread 0 runs the sequential loop.
+template <class Prob>
+__device__ int count_prefix(RowSmem& s, const Prob& prob, int k, int lo, int hi, float thr, bool strict) {
+  bool ok = true;
+  double tsum = 0.0;
+  for (int i = lo; i < hi; ++i) {
+    const float p = prob(i);
+    ok &= (p == 0.f || p >= 0x1p-29f);
+    tsum += (double)p;
+  }
+  if (__syncthreads_and(ok)) {
+    double acc = block_exclusive_scan_f64(tsum, s);
+    int cnt = 0;
+    for (int i = lo; i < hi; ++i) {
+      acc += (double)prob(i);
+      const float f = __double2float_rn(acc);
+      cnt += strict ? (f < thr) : (f <= thr);
+    }
+    int total;
+    block_exclusive_scan(cnt, s, total);
+    return total;
+  }
+  if (threadIdx.x == 0) {
+    double acc = 0.0;
+    int cnt = 0;
+    for (int i = 0; i < k; ++i) {
+      acc += (double)prob(i);
+      const float f = __double2float_rn(acc);
+      if (strict ? (f < thr) : (f <= thr)) cnt = i + 1;
+      else break;
+    }
+    s.misc[4] = cnt;
+  }
+  __syncthreads();
+  const int cnt = s.misc[4];
+  __syncthreads();
+  return cnt;
+}
+
+// Softmax over the k candidate values val(0..k) (in candidate order), top-p with
+// the one-position shifted mask (aios/engine/sample.py:134-146), re-softmax and
+// the inverse CDF index = #(cumsum < u) clamped to k - 1 (sample.py:161-165).
+template <class Val>
+__device__ int pick_index(RowSmem& s, const Val& val, int k, float top_p, float u) {
+  const int seg = (k + kSampThreads - 1) / kSampThreads;
+  const int lo = min(k, (int)threadIdx.x * seg), hi = min(k, lo + seg);
+  float mx = -INFINITY;
+  for (int i = lo; i < hi; ++i) mx = fmaxf(mx, val(i));
+  mx = block_max(mx, s.red);
+  float sum = 0.f;
+  for (int i = lo; i < hi; ++i) sum += expf(val(i) - mx);
+  sum = block_sum(sum, s.red);
+  const float inv = 1.0f / sum;  // torch's softmax scales by the reciprocal
+  int keep = k;
+  float inv2 = inv;
+  if (top_p < 1.0f) {
+    const auto p1 = [&](int i) { return expf(val(i) - mx) * inv; };
+    const int n_le = count_prefix(s, p1, k, lo, hi, top_p, false);
+    keep = n_le < k ? n_le + 1 : k;  // remove[i] = cumsum[i-1] > top_p, first kept
+    float sum2 = 0.f;
+    for (int i = lo; i < min(hi, keep); ++i) sum2 += expf(val(i) - mx);
+    sum2 = block_sum(sum2, s.red);
+    inv2 = 1.0f / sum2;
+  }
+  const auto p2 = [&](int i) { return i < keep ? expf(val(i) - mx) * inv2 : 0.f; };
+  const int idx = count_prefix(s, p2, k, lo, hi, u, true);
+  return idx > k - 1 ? k - 1 : idx;
+}
+
+// Bitonic sort (ascending) of np = 32 * E 64-bit keys held by one warp, E per lane
+// in blocked order (lane l holds a[l*E .. l*E+E)).
+template <int E>
+__device__ __forceinline__ void warp_bitonic(unsigned long long* a) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long x[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) x[e] = a[lane * E + e];
+#pragma unroll
+  for (int size = 2; size <= 32 * E; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride >= E) {
+        const int ls = stride / E;
+        const bool lower = (lane & ls) == 0;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const unsigned long long y = __shfl_xor_sync(0xffffffffu, x[e], ls);
+          const bool up = ((lane * E + e) & size) == 0;
+          const unsigned long long lo = x[e] < y ? x[e] : y, hi = x[e] < y ? y : x[e];
+          x[e] = (lower == up) ? lo : hi;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          if ((e & stride) == 0) {
+            const int f = e | stride;
+            const bool up = ((lane * E + e) & size) == 0;
+            const unsigned long long p = x[e], q = x[f];
+            if ((p > q) == up) { x[e] = q; x[f] = p; }
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) a[lane * E + e] = x[e];
+}
+
+// Sorts s.cand[0..n) ascending (n <= kMaxSortK); pads to a power of two with ~0.
+__device__ void sort_candidates(RowSmem& s, int n) {
+  const int tid = threadIdx.x;
+  int np = 32;
+  while (np < n) np <<= 1;
+  for (int i = n + tid; i < np; i += blockDim.x) s.cand[i] = ~0ull;
+  __syncthreads();
+  if (np <= 256) {
+    if (tid < 32) {
+      switch (np) {
+        case 32: warp_bitonic<1>(s.cand); break;
+        case 64: warp_bitonic<2>(s.cand); break;
+        case 128: warp_bitonic<4>(s.cand); break;
+        default: warp_bitonic<8>(s.cand); break;
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  for (int size = 2; size <= np; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < np; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const unsigned long long a = s.cand[i], b = s.cand[j];
+          if ((a > b) == up) { s.cand[i] = b; s.cand[j] = a; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// Exact top-k candidates by a four-pass radix select of the k-th largest key,
+// collected in index order into s.cand[0..k) (ties at the threshold: lowest ids).
+__device__ void radix_candidates(RowSmem& s, const uint32_t* keys, int V, int k) {
+  const int tid = threadIdx.x;
+  // four 8-bit passes, each a per-warp private histogram (no cross-warp atomic
+  // contention) summed per bin, then a warp-parallel scan from the top bin down
+  uint32_t prefix = 0, mask = 0;
+  int remaining = k;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = tid; b < nwarps * 256; b += blockDim.x) (&s.hist[0][0])[b] = 0;
+    __syncthreads();
+    for (int i = tid; i < V; i += blockDim.x) {
+      const uint32_t key = keys[i];
+      const bool hit = (key & mask) == prefix;
+      const unsigned bin = hit ? (key >> shift) & 0xFFu : 0x100u;
+      // warp-aggregated: one atomic per distinct bin (logit keys share their top bytes)
+      const unsigned peers = __match_any_sync(__activemask(), bin);
+      if (hit && (__ffs(peers) - 1) == lane) atomicAdd(&s.hist[warp][bin], (unsigned)__popc(peers));
+    }
+    __syncthreads();
+    for (int b = tid; b < 256; b += blockDim.x) {
+      unsigned int t = 0;
+      for (int w = 0; w < nwarps; ++w) t += s.hist[w][b];
+      s.hsum[b] = t;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l owns bins 255-8l .. 248-8l (descending); find the bin holding
+      // the `remaining`-th largest key
+      int local[8];
+      int tot = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        local[j] = (int)s.hsum[255 - 8 * lane - j];
+        tot += local[j];
+      }
+      int incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int excl = incl - tot;
+      if (excl < remaining && incl >= remaining) {
+        int acc = excl, j = 0;
+        for (; j < 7; ++j) {
+          if (acc + local[j] >= remaining) break;
+          acc += local[j];
+        }
+        s.misc[0] = 255 - 8 * lane - j;
+        s.misc[1] = remaining - acc;
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)s.misc[0] << shift;
+    mask |= 0xFFu << shift;
+    remaining = s.misc[1];
+    __syncthreads();
+  }
+  const uint32_t thr = prefix;    // key of the k-th largest value
+  const int need_eq = remaining;  // how many keys == thr to take (lowest ids first)
+  // each thread owns a contiguous id range; the counting walk starts at a
+  // thread-dependent offset so that the 32 lanes of a warp hit 32 banks
+  const int per = (V + blockDim.x - 1) / blockDim.x;
+  const int lo = min(V, tid * per), hi = min(V, lo + per);
+  const int cnt = hi - lo;
+  int n_gt = 0, n_eq = 0;
+  for (int t = 0; t < cnt; ++t) {
+    const uint32_t key = keys[lo + (t + tid) % cnt];
+    n_gt += key > thr;
+    n_eq += key == thr;
+  }
+  int tot_gt, tot_eq;
+  const int off_gt = block_exclusive_scan(n_gt, s, tot_gt);
+  const int off_eq = block_exclusive_scan(n_eq, s, tot_eq);
+  if (n_gt + n_eq > 0) {
+    int wg = off_gt, we = off_eq;
+    for (int i = lo; i < hi; ++i) {
+      const uint32_t key = keys[i];
+      int slot = -1;
+      if (key > thr) slot = wg++;
+      else if (key == thr) {
+        if (we < need_eq) slot = tot_gt + we;
+        ++we;
+      }
+      if (slot >= 0 && slot < kMaxSortK)
+        s.cand[slot] = ((unsigned long long)(~key) << 32) | (unsigned long long)(uint32_t)i;
+    }
+  }
+  __syncthreads();
+}
+
+// Samples one row. rr holds the bf16 logits, s.ban the forbidden ids; keys[] is
+// V uint32 of scratch. Returns the token id (same value in every thread).
+__device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, const SampleParams& p, float u) {
+  const int tid = threadIdx.x;
+  if (p.greedy) return greedy_pick(s, rr, V);
   int k;
   bool sorted_path;
   if (p.top_k > 0) {
@@ -142,196 +536,70 @@ __device__ int sample_row(RowSmem& s, float* row, int V, const SampleParams& p, 
     k = V;
     sorted_path = true;  // full descending sort (sample.py:131-132)
   }
-  if (sorted_path) {
-    // ---- radix select of the k-th largest order key: four 8-bit passes, each a
-    // per-warp private histogram (no cross-warp atomic contention) summed per bin,
-    // then a warp-parallel scan from the top bin down.
-    uint32_t prefix = 0, mask = 0;
-    int remaining = k;
-    const int warp = tid >> 5, lane = tid & 31;
-    const int nwarps = blockDim.x >> 5;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = tid; b < nwarps * 256; b += blockDim.x) (&s.hist[0][0])[b] = 0;
-      __syncthreads();
-      for (int i = tid; i < V; i += blockDim.x) {
-        const uint32_t key = order_key(row[i]);
-        const bool hit = (key & mask) == prefix;
-        const unsigned bin = hit ? (key >> shift) & 0xFFu : 0x100u;
-        // warp-aggregated: one atomic per distinct bin (logit keys share their top bytes)
-        const unsigned peers = __match_any_sync(__activemask(), bin);
-        if (hit && (__ffs(peers) - 1) == lane) atomicAdd(&s.hist[warp][bin], (unsigned)__popc(peers));
-      }
-      __syncthreads();
-      for (int b = tid; b < 256; b += blockDim.x) {
-        unsigned int t = 0;
-        for (int w = 0; w < nwarps; ++w) t += s.hist[w][b];
-        s.hsum[b] = t;
-      }
-      __syncthreads();
-      if (warp == 0) {
-        // lane l owns bins 255-8l .. 248-8l (descending); find the bin holding
-        // the `remaining`-th largest key
-        int local[8];
-        int tot = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          local[j] = (int)s.hsum[255 - 8 * lane - j];
-          tot += local[j];
-        }
-        int incl = tot;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
-        }
-        const int excl = incl - tot;
-        const bool mine = excl < remaining && incl >= remaining;
-        if (mine) {
-          int acc = excl, j = 0;
-          for (; j < 7; ++j) {
-            if (acc + local[j] >= remaining) break;
-            acc += local[j];
-          }
-          s.misc[0] = 255 - 8 * lane - j;
-          s.misc[1] = remaining - acc;
-        }
-      }
-      __syncthreads();
-      prefix |= (uint32_t)s.misc[0] << shift;
-      mask |= 0xFFu << shift;
-      remaining = s.misc[1];
-      __syncthreads();
-    }
-    const uint32_t thr = prefix;  // key of the k-th largest value
-    const int need_eq = remaining;  // how many keys == thr to take (lowest ids first)
-    // ---- collect candidates in index order: each thread owns a contiguous id range.
-    const int per = (V + blockDim.x - 1) / blockDim.x;
-    const int lo = min(V, tid * per), hi = min(V, lo + per);
-    int n_gt = 0, n_eq = 0;
-    for (int i = lo; i < hi; ++i) {
-      const uint32_t key = order_key(row[i]);
-      n_gt += key > thr;
-      n_eq += key == thr;
-    }
-    int tot_gt, tot_eq;
-    const int off_gt = block_exclusive_scan(n_gt, s, tot_gt);
-    const int off_eq = block_exclusive_scan(n_eq, s, tot_eq);
-    int wg = off_gt, we = off_eq;
-    for (int i = lo; i < hi; ++i) {
-      const float v = row[i];
-      const uint32_t key = order_key(v);
-      int slot = -1;
-      if (key > thr) slot = wg++;
-      else if (key == thr) {
-        if (we < need_eq) slot = tot_gt + we;
-        ++we;
-      }
-      if (slot >= 0 && slot < kMaxSortK)
-        s.cand[slot] = ((unsigned long long)(~key) << 32) | (unsigned long long)(uint32_t)i;
-    }
-    // ---- bitonic sort ascending on (~key, id) = value desc, id asc.
-    int np = 1;
-    while (np < k) np <<= 1;
-    for (int i = k + tid; i < np; i += blockDim.x) s.cand[i] = ~0ull;
-    __syncthreads();
-    for (int size = 2; size <= np; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int i = tid; i < np; i += blockDim.x) {
-          const int j = i ^ stride;
-          if (j > i) {
-            const bool up = (i & size) == 0;
-            const unsigned long long a = s.cand[i], b = s.cand[j];
-            if ((a > b) == up) { s.cand[i] = b; s.cand[j] = a; }
-          }
-        }
-        __syncthreads();
-      }
-    }
-    for (int i = tid; i < k; i += blockDim.x) {
-      const int id = (int)(uint32_t)(s.cand[i] & 0xffffffffull);
-      s.cid[i] = id;
-      s.cval[i] = row[id];
-    }
-    __syncthreads();
+  // the host rejects sorted candidate sets above kMaxSortK; never index past them
+  if (sorted_path && k > kMaxSortK) k = kMaxSortK;
+  const uint32_t tmax = make_keys(s, rr, keys, V, p.temperature);
+  __syncthreads();
+  if (!sorted_path) {
+    const auto val = [&](int i) { return key_value(keys[i]); };
+    return pick_index(s, val, V, p.top_p, u);
   }
-  // ---- softmax over the candidates (sample.py:134), index order = sorted order.
-  const float* cv = sorted_path ? s.cval : row;
-  float mx = -INFINITY;
-  for (int i = tid; i < k; i += blockDim.x) mx = fmaxf(mx, cv[i]);
-  mx = block_max(mx, s.red);
-  float* pr = sorted_path ? s.prob : row;  // full-vocab path rewrites the row in place
-  float sum = 0.f;
+  bool collected = false;
+  if (k <= kFastTopK) {
+    // The k-th largest of the 512 thread maxima is a lower bound L of the row's
+    // k-th largest key (those k maxima are k keys >= L), so every top-k token is
+    // in C = {key >= L}; |C| is close to k for non-degenerate rows. L by bisection
+    // on the key bits with block-wide counts.
+    uint32_t L = 0u;
+    for (int b = 31; b >= 0; --b) {
+      const uint32_t c = L | (1u << b);
+      if (__syncthreads_count(tmax >= c) >= k) L = c;
+    }
+    const int ngroups = (V + 7) >> 3;
+    int n = 0;
+#pragma unroll
+    for (int q = 0; q < kVecPer; ++q) {
+      const int j = tid + q * kSampThreads;
+      if (j < ngroups && tmax >= L) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) n += (8 * j + e < V && keys[8 * j + e] >= L) ? 1 : 0;
+      }
+    }
+    int total;
+    int off = block_exclusive_scan(n, s, total);
+    if (total <= kMaxSortK) {
+      if (n > 0) {
+#pragma unroll
+        for (int q = 0; q < kVecPer; ++q) {
+          const int j = tid + q * kSampThreads;
+          if (j < ngroups) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int i = 8 * j + e;
+              if (i < V && keys[i] >= L)
+                s.cand[off++] = ((unsigned long long)(~keys[i]) << 32) | (unsigned long long)(uint32_t)i;
+            }
+          }
+        }
+      }
+      __syncthreads();
+      sort_candidates(s, total);
+      collected = true;
+    }
+  }
+  if (!collected) {
+    radix_candidates(s, keys, V, k);
+    sort_candidates(s, k);
+  }
   for (int i = tid; i < k; i += blockDim.x) {
-    const float e = expf(cv[i] - mx);
-    pr[i] = e;
-    sum += e;
-  }
-  sum = block_sum(sum, s.red);
-  __syncthreads();
-  const float inv_sum = 1.0f / sum;  // torch's softmax scales by the reciprocal
-  for (int i = tid; i < k; i += blockDim.x) pr[i] = pr[i] * inv_sum;
-  __syncthreads();
-  if (p.top_p < 1.0f) {
-    // remove[i] = cumsum[i-1] > top_p for i >= 1 (shifted mask, first kept).
-    if (tid == 0) {
-      double acc = 0.0;
-      int keep = 1;
-      for (int i = 0; i < k; ++i) {
-        acc += (double)pr[i];
-        if ((float)acc > p.top_p) { keep = i + 1; break; }
-        keep = i + 1;
-      }
-      s.misc[2] = keep;
-    }
-    __syncthreads();
-    const int keep = s.misc[2];
-    // re-softmax over the kept prefix (masked entries are -inf -> probability 0).
-    float sum2 = 0.f;
-    for (int i = tid; i < k; i += blockDim.x) {
-      const float e = i < keep ? expf(cv[i] - mx) : 0.f;
-      pr[i] = e;
-      sum2 += e;
-    }
-    sum2 = block_sum(sum2, s.red);
-    __syncthreads();
-    const float inv_sum2 = 1.0f / sum2;
-    for (int i = tid; i < k; i += blockDim.x) pr[i] = pr[i] * inv_sum2;
-    __syncthreads();
-  }
-  // ---- inverse CDF: index = #(cumsum < u), clamped to k-1.
-  if (tid == 0) {
-    double acc = 0.0;
-    int idx = 0;
-    for (int i = 0; i < k; ++i) {
-      acc += (double)pr[i];
-      if ((float)acc < u) idx = i + 1;
-      else break;
-    }
-    if (idx > k - 1) idx = k - 1;
-    s.misc[3] = sorted_path ? s.cid[idx] : idx;
+    const unsigned long long c = s.cand[i];
+    s.cid[i] = (int)(uint32_t)(c & 0xffffffffull);
+    s.cval[i] = key_value(~(uint32_t)(c >> 32));
   }
   __syncthreads();
-  const int tok = s.misc[3];
-  __syncthreads();
-  return tok;
-}
-
-// Loads a bf16 logits row into s.row and returns its raw log-softmax pieces.
-__device__ __forceinline__ void load_row(RowSmem& s, float* row, const __nv_bfloat16* lrow, int V, float& mx,
-                                         float& lse) {
-  float m = -INFINITY;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = bf16_to_f(lrow[i]);
-    row[i] = v;
-    m = fmaxf(m, v);
-  }
-  m = block_max(m, s.red);
-  float se = 0.f;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) se += expf(row[i] - m);
-  se = block_sum(se, s.red);
-  mx = m;
-  lse = logf(se);
-  __syncthreads();
+  const auto val = [&](int i) { return s.cval[i]; };
+  const int idx = pick_index(s, val, k, p.top_p, u);
+  return s.cid[idx];
 }
 
 }  // namespace
@@ -340,39 +608,41 @@ __device__ __forceinline__ void load_row(RowSmem& s, float* row, const __nv_bflo
 namespace aiosb {
 namespace {
 
-// Applies forbidden ids to the sampling row: a shared list, then per-row ids.
-__device__ __forceinline__ void apply_forbidden(float* row, int V, const int32_t* ids, int n) {
+// Forbids a shared list of ids on the sampling copy (ids outside the vocabulary
+// are ignored, like the reference's index_fill on a filtered list).
+__device__ __forceinline__ void apply_forbidden(RowSmem& s, int V, const int32_t* ids, int n) {
   for (int j = threadIdx.x; j < n; j += blockDim.x) {
     const int id = ids[j];
-    if (id >= 0 && id < V) row[id] = -INFINITY;
+    if (id >= 0 && id < V) ban_id(s, id);
   }
 }
 
 // ---- generic sampler: Sampler.sample_with_logprobs ------------------------
-__global__ void __launch_bounds__(kSampThreads)
+__global__ void __launch_bounds__(kSampThreads, 1)
     sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int V, SampleParams p,
                   const float* __restrict__ uniforms, const int32_t* __restrict__ forbidden, int n_forbidden,
                   const int64_t* __restrict__ forbidden_rows, int n_forbidden_rows, int64_t* __restrict__ tok_out,
                   float* __restrict__ lp_out, int32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
-  float* row = reinterpret_cast<float*>(smem_raw + sizeof(RowSmem));
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw + sizeof(RowSmem));
   pdl_enter();
   const int r = blockIdx.x;
   const __nv_bfloat16* lrow = logits + (int64_t)r * row_stride;
+  RowRegs rr;
   float mx, lse;
-  load_row(s, row, lrow, V, mx, lse);
-  apply_forbidden(row, V, forbidden, n_forbidden);
+  load_row(s, rr, lrow, V, mx, lse);
+  apply_forbidden(s, V, forbidden, n_forbidden);
   if (forbidden_rows != nullptr) {
     for (int j = threadIdx.x; j < n_forbidden_rows; j += blockDim.x) {
       const int64_t id = forbidden_rows[(int64_t)r * n_forbidden_rows + j];
-      if (id >= 0 && id < V) row[id] = -INFINITY;
+      if (id >= 0 && id < V) ban_id(s, (int)id);
       else report(status, AIOSB_DEV_TOKEN_RANGE);
     }
   }
   __syncthreads();
   const float u = uniforms != nullptr ? uniforms[r] : 0.5f;
-  const int tok = sample_row(s, row, V, p, u);
+  const int tok = sample_row(s, rr, keys, V, p, u);
   if (threadIdx.x == 0) {
     tok_out[r] = tok;
     lp_out[r] = (bf16_to_f(lrow[tok]) - mx) - lse;
@@ -384,10 +654,10 @@ __global__ void __launch_bounds__(kSampThreads)
 // to finish runs the step's host-free epilogue: compaction of finished rows,
 // FIFO slot allocation in active-row order (aios/scheduler/cache.py:46-51),
 // page-table writes (aios/ime.py:1229) and the next forward's metadata.
-__global__ void __launch_bounds__(kSampThreads) group_step_kernel(aiosb_group_ptrs g) {
+__global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group_ptrs g) {
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
-  float* row = reinterpret_cast<float*>(smem_raw + sizeof(RowSmem));
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw + sizeof(RowSmem));
   pdl_enter();
   aiosb_group_state* st = g.state;
   const int r = blockIdx.x;
@@ -397,9 +667,10 @@ __global__ void __launch_bounds__(kSampThreads) group_step_kernel(aiosb_group_pt
   const bool run = st->done == 0 && g.active[r] != 0;
   if (run) {
     const __nv_bfloat16* lrow = reinterpret_cast<const __nv_bfloat16*>(g.logits) + (int64_t)r * V;
+    RowRegs rr;
     float mx, lse;
-    load_row(s, row, lrow, V, mx, lse);
-    if (step < st->min_new_tokens) apply_forbidden(row, V, g.minlen_ids, st->n_minlen);
+    load_row(s, rr, lrow, V, mx, lse);
+    if (step < st->min_new_tokens) apply_forbidden(s, V, g.minlen_ids, st->n_minlen);
     // Refill exact-repeat bans (aios/ime.py:974-996): for every banned sequence
     // b, ban its token at `step` if this row's output so far equals its prefix,
     // otherwise ban the pad id (the reference fills non-matching slots with pad).
@@ -409,7 +680,7 @@ __global__ void __launch_bounds__(kSampThreads) group_step_kernel(aiosb_group_pt
         bool match = g.banned_len[b] > step;
         for (int t = 0; t < step && match; ++t) match = g.output_ids[(int64_t)r * S + t] == seq[t];
         const int id = match ? seq[step] : st->pad_id;
-        if (id >= 0 && id < V) row[id] = -INFINITY;
+        if (id >= 0 && id < V) ban_id(s, id);
       }
     }
     __syncthreads();
@@ -419,7 +690,7 @@ __global__ void __launch_bounds__(kSampThreads) group_step_kernel(aiosb_group_pt
     p.top_p = st->top_p;
     p.greedy = st->greedy;
     const float u = g.uniforms[(int64_t)r * S + step];
-    const int tok = sample_row(s, row, V, p, u);
+    const int tok = sample_row(s, rr, keys, V, p, u);
     if (threadIdx.x == 0) {
       const float lp = (bf16_to_f(lrow[tok]) - mx) - lse;
       const bool eos = tok == st->eos_id;
@@ -590,7 +861,7 @@ __global__ void __launch_bounds__(1024) slot_free_range_kernel(int32_t* ring, in
   }
 }
 
-size_t sample_smem(int V) { return sizeof(RowSmem) + (size_t)V * sizeof(float); }
+size_t sample_smem(int V) { return sizeof(RowSmem) + (size_t)V * sizeof(uint32_t); }
 
 // Page-table reset for a keystroke: rows [0, rows) get the prefix slots in
 // columns [0, n) and zeros in [n, width) (the reference builds a fresh zero table
@@ -611,19 +882,19 @@ __global__ void __launch_bounds__(kSampThreads)
                          const int64_t* __restrict__ targets, float* __restrict__ out, int32_t* status) {
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
-  float* row = reinterpret_cast<float*>(smem_raw + sizeof(RowSmem));
   pdl_enter();
   const int r = blockIdx.x;
   const __nv_bfloat16* lrow = logits + (int64_t)r * row_stride;
+  RowRegs rr;
   float mx, lse;
-  load_row(s, row, lrow, V, mx, lse);
+  load_row(s, rr, lrow, V, mx, lse);
   if (threadIdx.x == 0) {
     const int64_t t = targets[r];
     if (t < 0 || t >= V) {
       report(status, AIOSB_DEV_TOKEN_RANGE);
       out[r] = -INFINITY;
     } else {
-      out[r] = (row[t] - mx) - lse;
+      out[r] = (bf16_to_f(lrow[t]) - mx) - lse;
     }
   }
 }

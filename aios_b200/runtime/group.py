@@ -230,10 +230,13 @@ class CandidateGroupRuntime:
             raise ValueError("too many terminal / minimum-length ids")
         if len(banned_sequences) > self.max_banned or any(len(s) > self.max_banned_width for s in banned_sequences):
             raise ValueError("refill ban list exceeds the runtime's capacity")
+        greedy = (temperature <= 0.0 or top_k == 1) and top_p == 1.0
+        sort_k = min(top_k, self.vocab) if top_k > 0 else (self.vocab if top_p < 1.0 else 0)
+        if not greedy and sort_k > self._top_k_cap:
+            raise ValueError(f"top-k/top-p candidate set of {sort_k} exceeds the {self._top_k_cap}-entry sort")
         cm = self.llm.cache_manager
         graph = self._graph(attempts)
         head0 = cm.head
-        greedy = (temperature <= 0.0 or top_k == 1) and top_p == 1.0
         width = max((len(s) for s in banned_sequences), default=0)
         self._write_state(dict(
             step=0, max_steps=max_new_tokens, min_new_tokens=min_new_tokens, prefix_len=prefix_len,

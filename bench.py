@@ -167,6 +167,12 @@ def run_cpu(keystrokes: int, warmup: int) -> dict:
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+# dram__bytes_read.sum + dram__bytes_write.sum summed over the 57 GEMM launches of
+# one decode step, from one ncu capture of the `linears` NVTX range below
+# (profiles/gemm_tc_decode_linears_s10.md).
+DECODE_LINEAR_TRAFFIC = 204_784_640
+
+
 def decode_linear_roofline(llm, peaks: dict) -> dict:
     """Times the tcgen05 GEMM launches of one decode step (8 rows: 14 x
     {qkv, o, gate_up+SwiGLU, down} + LM head, the same shapes and weights as the
@@ -222,7 +228,8 @@ def decode_linear_roofline(llm, peaks: dict) -> dict:
     peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
     return {"bound": "hbm", "kernel": "gemm_tc_kernel (decode linears, 8 rows)", "achieved": round(achieved, 1),
             "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": None, "algorithmic_bytes_per_step": wbytes,
+            "frac": round(achieved / peak, 4), "traffic": DECODE_LINEAR_TRAFFIC,
+            "traffic_unit": "bytes per decode step (57 launches)", "algorithmic_bytes_per_step": wbytes,
             "launches_per_step": launches, "us_per_step": round(ms * 1e3, 2),
             "us_per_launch": round(ms * 1e3 / launches, 3)}
 

@@ -286,6 +286,67 @@ def test_sampler_tokens_bit_exact(cuda_device, temperature: float, top_k: int, t
     torch.testing.assert_close(lp.cpu(), exp_lp, rtol=0, atol=2e-5)
 
 
+# Every branch of the device sampler: the thread-maximum threshold path (k <= 512)
+# and its fallbacks (k > 512: radix select; a row of ties: |C| > 2048), the full
+# sort (top_k 0, top_p < 1), the sequential cumsum (probabilities below 2^-29),
+# ragged and unaligned rows (scalar loads).
+SAMPLER_PATHS = [
+    ("k160", 16384, 0.75, 160, 0.95, "randn"),
+    ("k512", 16384, 0.8, 512, 0.9, "randn"),
+    ("k513_radix", 16384, 0.8, 513, 0.9, "randn"),
+    ("k2048_radix", 16384, 1.0, 2048, 0.99, "randn"),
+    ("ties_fallback", 16384, 0.8, 50, 0.9, "const"),
+    ("few_distinct", 16384, 0.8, 50, 0.9, "coarse"),
+    ("full_sort", 2048, 0.8, 0, 0.9, "randn"),
+    ("tiny_probs", 16384, 0.5, 512, 1.0, "spread"),
+    ("tiny_probs_topp", 16384, 0.5, 400, 0.999999, "spread"),
+    ("s06_vocab", 6400, 0.8, 50, 0.9, "randn"),
+    ("ragged_vocab", 6401, 0.8, 50, 0.9, "randn"),
+    ("unaligned_row", 16384, 0.8, 50, 0.9, "unaligned"),
+    ("greedy_unaligned", 6401, 1.0, 1, 1.0, "unaligned"),
+]
+
+
+@pytest.mark.parametrize("name,vocab,temperature,top_k,top_p,mode", SAMPLER_PATHS, ids=[c[0] for c in SAMPLER_PATHS])
+def test_sampler_paths_bit_exact(cuda_device, name, vocab, temperature, top_k, top_p, mode) -> None:
+    g = torch.Generator().manual_seed(len(name) * 7 + vocab)
+    rows = 24
+    if mode == "const":
+        logits = torch.zeros(rows, vocab).to(torch.bfloat16)
+    elif mode == "coarse":
+        logits = torch.randint(-3, 4, (rows, vocab), generator=g).float().to(torch.bfloat16)
+    elif mode == "spread":
+        logits = (torch.randn(rows, vocab, generator=g) * 12.0).to(torch.bfloat16)
+    else:
+        logits = (torch.randn(rows, vocab, generator=g) * 2.0).to(torch.bfloat16)
+    u = osamp.stateless_uniforms(list(range(77, 77 + rows)), 1)[:, 0]
+    forbidden = [5, 6, 7, 100]
+    ban_rows = torch.randint(0, vocab, (rows, 2), generator=g)
+    exp_tok, exp_lp = osamp.sample_with_logprobs(
+        logits, temperature=temperature, top_k=top_k, top_p=top_p, uniforms=u,
+        forbidden_token_ids=forbidden, forbidden_token_ids_by_row=ban_rows,
+    )
+    if mode == "unaligned":
+        wide = torch.zeros(rows, vocab + 1, dtype=torch.bfloat16)
+        wide[:, 1:] = logits
+        dev_logits = wide.to(cuda_device)[:, 1:]  # 2-byte offset rows: scalar loads
+    else:
+        dev_logits = logits.to(cuda_device)
+    tok, lp = ops.sample(
+        dev_logits, temperature=temperature, top_k=top_k, top_p=top_p,
+        greedy=osamp.is_greedy(temperature, top_k, top_p), uniforms=u.to(cuda_device),
+        forbidden=torch.tensor(forbidden, dtype=torch.int32, device=cuda_device),
+        forbidden_rows=ban_rows.to(cuda_device),
+    )
+    torch.cuda.synchronize()
+    ops.check_status(cuda_device)
+    mism = (tok.cpu() != exp_tok).squeeze(-1)
+    if bool(mism.any()):
+        margins = osamp.sample_margin(logits, temperature=temperature, top_k=top_k, top_p=top_p, uniforms=u)
+        assert float(margins[mism.numpy()].max()) < 1e-6, f"{name}: token mismatch rows {mism.nonzero().flatten().tolist()}"
+    torch.testing.assert_close(lp.cpu(), exp_lp, rtol=0, atol=2e-5)
+
+
 def test_stateless_uniforms_bit_exact(cuda_device) -> None:
     seeds = [20260814 + 100003 * 8 + i for i in range(8)] + [0, 1, 2**40 + 7]
     expected = osamp.stateless_uniforms(seeds, 16)
