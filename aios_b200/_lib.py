@@ -123,9 +123,14 @@ _SIGNATURES = {
     "aiosb_add_rmsnorm": ([_p, _p, _i64, _i64, _p, _f32, _p], _i32),
     "aiosb_silu_mul": ([_p, _i64, _i64, _p, _p], _i32),
     "aiosb_embedding": ([_p, _i32, _i64, _p, _i64, _i64, _p, _p, _p], _i32),
+    "aiosb_embedding_stat": ([_p, _i32, _i64, _p, _i64, _i64, _p, _p, _p, _p, _p], _i32),
     "aiosb_linear": ([_p, _i64, _i64, _p, _i64, _p, _i64, _i32, _p, _i64, _p, _p], _i32),
     "aiosb_linear_rmsnorm": (
         [_p, _p, _p, _p, _f32, _i64, _i64, _p, _i64, _p, _i64, _i32, _p, _i64, _p, _p], _i32
+    ),
+    "aiosb_linear_add_stat": ([_p, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _p, _p], _i32),
+    "aiosb_linear_stat_norm": (
+        [_p, _p, _i64, _i64, _p, _f32, _i64, _i64, _p, _i64, _p, _i64, _i32, _p, _i64, _p, _p], _i32
     ),
     "aiosb_attention_decode": (
         [_p, _i64, _p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p,

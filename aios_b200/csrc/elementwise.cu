@@ -171,8 +171,12 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ x, int64_t row
 }
 
 // ---- Embedding gather (aios/layers/embedding.py:17-18) --------------------
+// One warp per token. With stat_x, also writes the row in fp32 and its sum of
+// squares (stat_ss[t], a single part): the statistics a following
+// aiosb_linear_stat_norm normalises from.
 __global__ void embedding_kernel(const void* __restrict__ ids, bool ids64, int64_t n, const uint4* __restrict__ w,
-                                 int64_t vocab, int64_t hidden, uint4* __restrict__ out, int32_t* status) {
+                                 int64_t vocab, int64_t hidden, uint4* __restrict__ out, float* __restrict__ stat_x,
+                                 float* __restrict__ stat_ss, int32_t* status) {
   pdl_enter();
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -181,7 +185,24 @@ __global__ void embedding_kernel(const void* __restrict__ ids, bool ids64, int64
   const int64_t nv = hidden / 8;
   const bool ok = id >= 0 && id < vocab;
   if (!ok && lane == 0) report(status, AIOSB_DEV_TOKEN_RANGE);
-  for (int64_t i = lane; i < nv; i += 32) out[t * nv + i] = ok ? w[id * nv + i] : make_uint4(0, 0, 0, 0);
+  float ss = 0.f;
+  for (int64_t i = lane; i < nv; i += 32) {
+    const uint4 v = ok ? w[id * nv + i] : make_uint4(0, 0, 0, 0);
+    out[t * nv + i] = v;
+    if (stat_x != nullptr) {
+      const float f[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
+                          bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
+      float4* dst = reinterpret_cast<float4*>(stat_x + t * hidden + 8 * i);
+      dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+      dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+    }
+  }
+  if (stat_x != nullptr) {
+    ss = warp_sum(ss);
+    if (lane == 0) stat_ss[t] = ss;
+  }
 }
 
 inline unsigned row_blocks(int64_t rows) { return (unsigned)((rows + kRowThreads / 32 - 1) / (kRowThreads / 32)); }
@@ -272,7 +293,23 @@ extern "C" int aiosb_embedding(const void* ids, int ids_is_int64, int64_t num_to
                 "embedding: weight/out must be 16-byte aligned");
   cudaError_t e = launch_pdl(embedding_kernel, dim3(row_blocks(num_tokens)), dim3(kRowThreads), 0,
                              as_stream(stream), ids, ids_is_int64 != 0, num_tokens, (const uint4*)weight, vocab,
-                             hidden, (uint4*)out, status);
+                             hidden, (uint4*)out, (float*)nullptr, (float*)nullptr, status);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "embedding: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_embedding_stat(const void* ids, int ids_is_int64, int64_t num_tokens, const void* weight,
+                                    int64_t vocab, int64_t hidden, void* out, float* stat_x, float* stat_ss,
+                                    int32_t* status, void* stream) {
+  AIOSB_REQUIRE(num_tokens >= 0 && vocab > 0 && hidden > 0, AIOSB_ERR_INVALID_ARG, "embedding_stat: bad sizes");
+  AIOSB_REQUIRE(hidden % 8 == 0, AIOSB_ERR_UNSUPPORTED, "embedding_stat: hidden must be a multiple of 8");
+  if (num_tokens == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(ids && weight && out && stat_x && stat_ss, AIOSB_ERR_INVALID_ARG, "embedding_stat: null pointer");
+  AIOSB_REQUIRE(aligned16(weight) && aligned16(out) && aligned16(stat_x), AIOSB_ERR_MISALIGNED,
+                "embedding_stat: weight/out/stat_x must be 16-byte aligned");
+  cudaError_t e = launch_pdl(embedding_kernel, dim3(row_blocks(num_tokens)), dim3(kRowThreads), 0,
+                             as_stream(stream), ids, ids_is_int64 != 0, num_tokens, (const uint4*)weight, vocab,
+                             hidden, (uint4*)out, stat_x, stat_ss, status);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "embedding_stat: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }

@@ -56,9 +56,22 @@ struct GemmArgs {
   __nv_bfloat16* nres_out;
   const __nv_bfloat16* nw;
   float neps;
+  // Statistics mode (norm == 2): B = bf16(s * rcp * nw) with s = stat_x [rows, K]
+  // fp32 and rcp from stat_parts partial sums of squares stat_ss[p * stat_ss_stride + row].
+  const float* stat_x;
+  const float* stat_ss;
+  int64_t stat_ss_stride;
+  int stat_parts;
+  // AIOSB_EPI_ADD with out_stat_x: also store s = residual + bf16(acc) in fp32 into
+  // out_stat_x [rows, n] and each 128-column tile's sum of squares of s into
+  // out_stat_ss[m_tile * out_ss_stride + row].
+  float* out_stat_x;
+  float* out_stat_ss;
+  int64_t out_ss_stride;
 };
 
 constexpr int kMaxNormRows = 64;
+constexpr int kMaxStatParts = 16;
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -75,7 +88,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t pipe_bytes = (uint32_t)a.stages * stage_bytes + (norm ? (uint32_t)a.chunks_per_split * kBBytes : 0u);
   const uint32_t red_bytes = BN * kBM * 4;
   const uint32_t body = pipe_bytes > red_bytes ? pipe_bytes : red_bytes;
-  __shared__ float rcp_s[kMaxNormRows];
+  __shared__ float rcp_s[256];  // per-token 1/rms (norm modes; BN <= 256)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + body);
   uint64_t* empty = full + kMaxStages;
   uint64_t* accum = empty + kMaxStages;
@@ -123,7 +136,84 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   pdl_wait();
-  if (norm) {
+  if (a.norm == 2) {
+    // ---- RMSNorm from the producer's statistics: B = bf16(s * rcp * w), where s
+    // is the fp32 residual stream the previous GEMM's ADD epilogue wrote and
+    // rcp = 1 / sqrt(sum_p ss_p / K + eps) sums its per-tile partials in tile order.
+    // Every load of a round is issued before any use (one L2 round trip per round);
+    // with at most one unit per thread (decode) the partials ride in that round.
+    const int64_t K = a.k_total;
+    const int units = nch * BN * 8;
+    const int P = a.stat_parts;
+    const bool inline_rcp = units <= kThreads;
+    if (!inline_rcp) {
+      for (int t = tid; t < BN; t += kThreads) {
+        const int64_t tg = (int64_t)n_tile * BN + t;
+        float ss = 0.f;
+        if (tg < a.rows) {
+#pragma unroll
+          for (int p = 0; p < kMaxStatParts; ++p)
+            if (p < P) ss += a.stat_ss[p * a.stat_ss_stride + tg];
+        }
+        rcp_s[t] = 1.0f / sqrtf(ss / (float)K + a.neps);
+      }
+      __syncthreads();
+    }
+    constexpr int kU = 4;
+    for (int u0 = tid; u0 < units; u0 += kThreads * kU) {
+      float4 s0[kU], s1[kU];
+      uint4 wv[kU];
+      float rc[kU];
+#pragma unroll
+      for (int j = 0; j < kU; ++j) {
+        const int u = u0 + j * kThreads;
+        s0[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        s1[j] = s0[j];
+        wv[j] = make_uint4(0u, 0u, 0u, 0u);
+        rc[j] = 0.f;
+        if (u < units) {
+          const int i = u / (BN * 8), rem = u % (BN * 8), t = rem >> 3, c16 = rem & 7;
+          const int64_t kk = (int64_t)(k_chunk0 + i) * kBK + c16 * 8;
+          const int64_t tg = (int64_t)n_tile * BN + t;
+          if (tg < a.rows) {
+            const float4* sp = reinterpret_cast<const float4*>(a.stat_x + tg * K + kk);
+            s0[j] = sp[0];
+            s1[j] = sp[1];
+            wv[j] = *reinterpret_cast<const uint4*>(a.nw + kk);
+            if (inline_rcp) {
+              float part[kMaxStatParts];
+#pragma unroll
+              for (int p = 0; p < kMaxStatParts; ++p) part[p] = p < P ? a.stat_ss[p * a.stat_ss_stride + tg] : 0.f;
+              float ss = 0.f;
+#pragma unroll
+              for (int p = 0; p < kMaxStatParts; ++p) ss += part[p];
+              rc[j] = 1.0f / sqrtf(ss / (float)K + a.neps);
+            } else {
+              rc[j] = rcp_s[t];
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kU; ++j) {
+        const int u = u0 + j * kThreads;
+        if (u < units) {
+          const int i = u / (BN * 8), rem = u % (BN * 8), t = rem >> 3, c16 = rem & 7;
+          const float sv[8] = {s0[j].x, s0[j].y, s0[j].z, s0[j].w, s1[j].x, s1[j].y, s1[j].z, s1[j].w};
+          const uint32_t pw[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+          uint32_t po[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            po[q] = pack_bf16x2(sv[2 * q] * rc[j] * bf16_lo(pw[q]), sv[2 * q + 1] * rc[j] * bf16_hi(pw[q]));
+          *reinterpret_cast<uint4*>(bnorm + (size_t)i * kBBytes + t * 128 + ((c16 ^ (t & 7)) << 4)) =
+              make_uint4(po[0], po[1], po[2], po[3]);
+        }
+      }
+    }
+    // generic-proxy smem writes -> visible to the tensor core (async proxy)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+  } else if (norm) {
     // ---- fused RMSNorm: per-row 1/rms over the full K, then this CTA's K chunks
     // of the normalised rows written straight into the UMMA B layout
     // (128-byte rows, 16-byte units swizzled by row % 8, as TMA SWIZZLE_128B).
@@ -290,6 +380,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc.y = bf16_hi(rv.x) + round_bf16(acc.y);
           acc.z = bf16_lo(rv.y) + round_bf16(acc.z);
           acc.w = bf16_hi(rv.y) + round_bf16(acc.w);
+          if (a.out_stat_x != nullptr) {
+            // one warp owns column c: its 32 lanes cover the tile's 128 rows
+            *reinterpret_cast<float4*>(a.out_stat_x + t * a.n + (int64_t)m_tile * kBM + m4 * 4) = acc;
+            float ss = acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+            ss = warp_sum(ss);
+            if (lane == 0) a.out_stat_ss[(int64_t)m_tile * a.out_ss_stride + t] = ss;
+          }
         }
         uint2 o = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
         *reinterpret_cast<uint2*>(dst) = o;
@@ -378,7 +475,7 @@ size_t smem_bytes(int stages, bool norm = false, int chunks = 0) {
   return std::max(pipe, red) + 1024 /*alignment*/ + 256 /*barriers*/;
 }
 
-constexpr int kMaxDynSmem = 227 * 1024 - 1024;  // opt-in limit minus the static rcp table
+constexpr int kMaxDynSmem = 227 * 1024 - 2048;  // opt-in limit minus the static rcp table
 
 template <int BN>
 int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, GemmArgs a, int m_tiles, int n_tiles,
@@ -550,4 +647,46 @@ extern "C" int aiosb_linear_rmsnorm(const void* x, const void* res, void* res_ou
   a.nw = (const __nv_bfloat16*)norm_w;
   a.neps = eps;
   return linear_impl(a, x, rows, k, w, n, stream);
+}
+
+extern "C" int aiosb_linear_add_stat(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
+                                     int64_t y_row_stride, const void* residual, int64_t residual_stride,
+                                     float* stat_x, float* stat_ss, int64_t stat_ss_stride, int32_t* status,
+                                     void* stream) {
+  int rc = check_common(w, rows, k, n, y, y_row_stride, AIOSB_EPI_ADD, residual, residual_stride);
+  if (rc != AIOSB_OK) return rc == 1 ? AIOSB_OK : rc;
+  AIOSB_REQUIRE(x && aligned16(x), AIOSB_ERR_MISALIGNED, "linear_add_stat: x must be a 16-byte aligned pointer");
+  AIOSB_REQUIRE(stat_x && stat_ss && aligned16(stat_x), AIOSB_ERR_MISALIGNED,
+                "linear_add_stat: stat_x must be a 16-byte aligned pointer and stat_ss non-null");
+  AIOSB_REQUIRE(stat_ss_stride >= rows, AIOSB_ERR_INVALID_ARG, "linear_add_stat: stat_ss stride below rows");
+  AIOSB_REQUIRE(n / kBM <= kMaxStatParts, AIOSB_ERR_UNSUPPORTED, "linear_add_stat: n above %d",
+                kMaxStatParts * kBM);
+  GemmArgs a = base_args(y, y_row_stride, AIOSB_EPI_ADD, residual, residual_stride, status);
+  a.out_stat_x = stat_x;
+  a.out_stat_ss = stat_ss;
+  a.out_ss_stride = stat_ss_stride;
+  return linear_impl(a, x, rows, k, w, n, stream);
+}
+
+extern "C" int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, int64_t stat_ss_stride,
+                                      int64_t parts, const void* norm_w, float eps, int64_t rows, int64_t k,
+                                      const void* w, int64_t n, void* y, int64_t y_row_stride, int epilogue,
+                                      const void* residual, int64_t residual_stride, int32_t* status,
+                                      void* stream) {
+  int rc = check_common(w, rows, k, n, y, y_row_stride, epilogue, residual, residual_stride);
+  if (rc != AIOSB_OK) return rc == 1 ? AIOSB_OK : rc;
+  AIOSB_REQUIRE(parts >= 1 && parts <= kMaxStatParts, AIOSB_ERR_INVALID_ARG,
+                "linear_stat_norm: parts must be in [1, %d]", kMaxStatParts);
+  AIOSB_REQUIRE(stat_ss_stride >= rows, AIOSB_ERR_INVALID_ARG, "linear_stat_norm: stat_ss stride below rows");
+  AIOSB_REQUIRE(stat_x && stat_ss && norm_w && aligned16(stat_x) && aligned16(norm_w), AIOSB_ERR_MISALIGNED,
+                "linear_stat_norm: stat_x and norm_w must be 16-byte aligned, stat_ss non-null");
+  GemmArgs a = base_args(y, y_row_stride, epilogue, residual, residual_stride, status);
+  a.norm = 2;
+  a.stat_x = stat_x;
+  a.stat_ss = stat_ss;
+  a.stat_ss_stride = stat_ss_stride;
+  a.stat_parts = (int)parts;
+  a.nw = (const __nv_bfloat16*)norm_w;
+  a.neps = eps;
+  return linear_impl(a, nullptr, rows, k, w, n, stream);
 }

@@ -364,6 +364,88 @@ def linear_rmsnorm(
     return out
 
 
+class RowStats:
+    """RMSNorm statistics of a residual stream handed from one GEMM to the next:
+    ``x`` [T, D] fp32 (the un-rounded residual sum) and ``ss`` [parts, T] fp32
+    (sums of squares over each 128-column tile, or over the whole row)."""
+
+    __slots__ = ("x", "ss")
+
+    def __init__(self, x: torch.Tensor, ss: torch.Tensor):
+        self.x, self.ss = x, ss
+
+    @classmethod
+    def empty(cls, rows: int, hidden: int, parts: int, device: torch.device) -> "RowStats":
+        return cls(torch.empty((rows, hidden), dtype=torch.float32, device=device),
+                   torch.empty((parts, rows), dtype=torch.float32, device=device))
+
+    @property
+    def parts(self) -> int:
+        return self.ss.shape[0]
+
+    def rows(self, start: int, stop: int) -> "RowStats":
+        return RowStats(self.x[start:stop], self.ss[:, start:stop])
+
+    def select(self, idx: torch.Tensor) -> "RowStats":
+        return RowStats(self.x.index_select(0, idx).contiguous(), self.ss.index_select(1, idx).contiguous())
+
+
+def embedding_stat(ids: torch.Tensor, weight: torch.Tensor) -> tuple[torch.Tensor, RowStats]:
+    """Embedding rows plus their RMSNorm statistics (one part per row)."""
+    _require_cuda(ids, weight, what="embedding_stat")
+    ids = ids.contiguous()
+    if ids.dtype not in (torch.int64, torch.int32):
+        raise ValueError("embedding ids must be int32 or int64")
+    t, d = ids.numel(), weight.shape[1]
+    out = torch.empty((t, d), dtype=weight.dtype, device=weight.device)
+    st = RowStats.empty(t, d, 1, weight.device)
+    _lib.call("aiosb_embedding_stat", ids.data_ptr(), int(ids.dtype == torch.int64), t, weight.data_ptr(),
+              weight.shape[0], d, out.data_ptr(), st.x.data_ptr(), st.ss.data_ptr(),
+              status_word(ids.device).data_ptr(), _stream(ids.device))
+    return out, st
+
+
+def linear_add_stat(x: torch.Tensor, weight: torch.Tensor, residual: torch.Tensor) -> RowStats:
+    """residual <- bf16(residual + bf16(x @ weight.T)) in place, returning the
+    RMSNorm statistics of the new residual stream."""
+    _require_cuda(x, weight, residual, what="linear_add_stat")
+    if x.ndim != 2 or weight.ndim != 2 or x.shape[1] != weight.shape[1] or not x.is_contiguous():
+        raise ValueError("linear_add_stat expects contiguous x [T, K] and weight [N, K]")
+    rows, n = x.shape[0], weight.shape[0]
+    if residual.shape != (rows, n) or residual.stride(1) != 1:
+        raise ValueError("linear_add_stat needs a residual [rows, n] with contiguous rows")
+    st = RowStats.empty(rows, n, n // 128, x.device)
+    _lib.call("aiosb_linear_add_stat", x.data_ptr(), rows, x.shape[1], weight.data_ptr(), n, residual.data_ptr(),
+              residual.stride(0), residual.data_ptr(), residual.stride(0), st.x.data_ptr(), st.ss.data_ptr(),
+              st.ss.stride(0), status_word(x.device).data_ptr(), _stream(x.device))
+    return st
+
+
+def linear_stat_norm(
+    stats: RowStats,
+    norm_weight: torch.Tensor,
+    eps: float,
+    weight: torch.Tensor,
+    *,
+    out: torch.Tensor | None = None,
+    epilogue: int = _lib.EPI_STORE,
+) -> torch.Tensor:
+    """``linear(rmsnorm(s) * norm_weight, weight)`` with s and its sums of squares
+    from ``stats``; the normalised rows exist only inside the GEMM."""
+    _require_cuda(stats.x, norm_weight, weight, what="linear_stat_norm")
+    rows, k = stats.x.shape
+    if weight.shape[1] != k or stats.x.stride(1) != 1 or stats.x.stride(0) != k or stats.ss.stride(1) != 1:
+        raise ValueError("linear_stat_norm expects contiguous statistics [rows, k] matching the weight")
+    n = weight.shape[0]
+    cols = n // 2 if epilogue == _lib.EPI_SILU_MUL else n
+    if out is None:
+        out = torch.empty((rows, cols), dtype=weight.dtype, device=weight.device)
+    _lib.call("aiosb_linear_stat_norm", stats.x.data_ptr(), stats.ss.data_ptr(), stats.ss.stride(0), stats.parts,
+              norm_weight.data_ptr(), float(eps), rows, k, weight.data_ptr(), n, out.data_ptr(), out.stride(0),
+              epilogue, None, 0, status_word(weight.device).data_ptr(), _stream(weight.device))
+    return out
+
+
 def pack_gate_up(weight: torch.Tensor) -> torch.Tensor:
     """[gate | up] rows ([2F, K]) -> 64-row interleaved blocks for EPI_SILU_MUL."""
     two_f, k = weight.shape

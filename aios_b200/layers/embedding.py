@@ -66,6 +66,19 @@ class LMHead(BaseOP):
             ops.fused_add_rmsnorm(h, r, norm_weight, eps)
         return ops.linear(h, self._w(), out=batch.logits_out)
 
+    def forward_stat(self, stats: ops.RowStats, norm_weight: torch.Tensor, eps: float) -> torch.Tensor:
+        """LM head on the final RMSNorm of a residual stream given by its
+        statistics, for the rows that need logits only."""
+        batch = get_global_ctx().batch
+        if batch.is_prefill and not batch.return_all_logits:
+            md = batch.attn_metadata
+            rows = getattr(md, "last_rows", ())
+            if len(rows) == 1:
+                stats = stats.rows(rows[0], rows[0] + 1)
+            else:
+                stats = stats.select(md.get_last_indices(batch.size))
+        return ops.linear_stat_norm(stats, norm_weight, eps, self._w(), out=batch.logits_out)
+
     def load_state_dict(self, state_dict: Dict[str, torch.Tensor], *, prefix: str = "", _internal: bool = False) -> None:
         if self._tie_word_embeddings:
             key = _concat_prefix(prefix, "weight")

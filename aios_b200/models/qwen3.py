@@ -1,8 +1,13 @@
 """Standard-residual decoder (aios/models/qwen3.py:31-173) on the sm_100a kernels.
 
-Per layer and forward: add+RMSNorm kernel, qkv GEMM (tcgen05), the attention
-kernel that also applies q/k RMSNorm + bf16 RoPE and writes the new K/V, o GEMM,
-add+RMSNorm, gate/up GEMM with the SwiGLU epilogue, down GEMM. The parameter
+Per layer and forward (``forward_stat``, the path the B200 backend runs): qkv
+GEMM that normalises its own input from the residual statistics, the attention
+kernel that also applies q/k RMSNorm + bf16 RoPE and writes the new K/V, o GEMM
+whose epilogue adds the residual and emits the next statistics, gate/up GEMM
+(normalising input, SwiGLU epilogue), down GEMM (residual add + statistics).
+RMSNormFused (aios/layers/norm.py:34-40) is thereby split across the GEMM before
+and the GEMM after it, and no normalised tensor is written. ``forward`` keeps the
+reference's call structure for any other attention backend. The parameter
 names and their order equal the reference's, so checkpoints load unchanged.
 """
 
@@ -54,7 +59,11 @@ class Qwen3Attention(BaseOP):
     def attend(self, hidden_states: torch.Tensor, rotary: RotaryEmbedding, paged_kv_cache: MHAKVCache,
                batch: Batch) -> torch.Tensor:
         """Projection + attention, without o_proj: [T, Hq * d]."""
-        qkv = self.qkv_proj.forward(hidden_states)
+        return self.attend_qkv(self.qkv_proj.forward(hidden_states), rotary, paged_kv_cache, batch)
+
+    def attend_qkv(self, qkv: torch.Tensor, rotary: RotaryEmbedding, paged_kv_cache: MHAKVCache,
+                   batch: Batch) -> torch.Tensor:
+        """Attention on a packed [T, (Hq + 2 Hkv) * d] projection: [T, Hq * d]."""
         backend = self._attn_backend
         if isinstance(backend, B200AttentionBackend):
             cos, sin = rotary.tables()
@@ -104,6 +113,20 @@ class Qwen3DecoderLayer(BaseOP):
         hidden_states, residual = self.post_attention_layernorm.forward(hidden_states, residual)
         return self.mlp.forward(hidden_states), residual
 
+    def forward_stat(self, stats: ops.RowStats, residual: torch.Tensor, rotary, paged_kv_cache,
+                     batch) -> ops.RowStats:
+        """The same layer with both norms folded into the GEMMs: ``stats`` describe
+        the residual stream entering the layer, ``residual`` (bf16, updated in
+        place) is that stream rounded; returns the statistics leaving it."""
+        attn, mlp = self.self_attn, self.mlp
+        n1, n2 = self.input_layernorm, self.post_attention_layernorm
+        qkv = ops.linear_stat_norm(stats, n1.weight, n1.eps, attn.qkv_proj.weight)
+        a = attn.attend_qkv(qkv, rotary, paged_kv_cache, batch)
+        stats = ops.linear_add_stat(a, attn.o_proj.weight, residual)
+        act = ops.linear_stat_norm(stats, n2.weight, n2.eps, mlp.gate_up_proj.packed_weight(),
+                                   epilogue=_lib.EPI_SILU_MUL)
+        return ops.linear_add_stat(act, mlp.down_proj.weight, residual)
+
 
 class Qwen3Model(BaseOP):
     def __init__(self, config: ModelConfig):
@@ -123,6 +146,16 @@ class Qwen3Model(BaseOP):
             hidden_states, residual = layer.forward(hidden_states, self._rotary_emb, ctx.kv_cache, batch, residual)
         return hidden_states, residual
 
+    def forward_stats(self) -> ops.RowStats:
+        """Decoder trunk with every RMSNorm folded into the GEMMs; returns the
+        statistics of the final residual stream (the final norm's input)."""
+        ctx = get_global_ctx()
+        batch = ctx.batch
+        residual, stats = ops.embedding_stat(batch.input_ids, self.embed_tokens.weight)
+        for layer in self.layers.op_list:
+            stats = layer.forward_stat(stats, residual, self._rotary_emb, ctx.kv_cache, batch)
+        return stats
+
     def forward(self) -> torch.Tensor:
         hidden_states, residual = self.forward_hidden()
         return self.norm.forward(hidden_states, residual)[0]
@@ -140,6 +173,8 @@ class Qwen3ForCausalLM(BaseLLMModel):
         )
 
     def forward(self) -> torch.Tensor:
-        hidden_states, residual = self.model.forward_hidden()
         norm = self.model.norm
+        if isinstance(self.attn_backend, B200AttentionBackend):
+            return self.lm_head.forward_stat(self.model.forward_stats(), norm.weight, norm.eps)
+        hidden_states, residual = self.model.forward_hidden()
         return self.lm_head.forward_normed(hidden_states, residual, norm.weight, norm.eps)

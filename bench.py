@@ -184,19 +184,25 @@ def decode_linear_roofline(llm, peaks: dict) -> dict:
     cfg = llm.config
     rows = 8
     layers = llm.model.model.layers.op_list
-    x768 = torch.randn(rows, cfg.hidden_size, device=dev).to(torch.bfloat16)
     xo = torch.randn(rows, cfg.num_qo_heads * cfg.head_dim, device=dev).to(torch.bfloat16)
     xf = torch.randn(rows, cfg.intermediate_size, device=dev).to(torch.bfloat16)
+    res = torch.randn(rows, cfg.hidden_size, device=dev).to(torch.bfloat16)
+    stats = ops.RowStats(torch.randn(rows, cfg.hidden_size, device=dev),
+                         torch.rand(cfg.hidden_size // 128, rows, device=dev) * 100)
+    nw = torch.ones(cfg.hidden_size, dtype=torch.bfloat16, device=dev)
     outs = {}
 
     def run():
+        # the model's decode GEMMs: norm-from-statistics qkv / gate_up / LM head,
+        # residual-add + statistics o / down
         for i, layer in enumerate(layers):
             a, m = layer.self_attn, layer.mlp
-            outs["qkv"] = ops.linear(x768, a.qkv_proj.weight)
-            outs["o"] = ops.linear(xo, a.o_proj.weight)
-            outs["gu"] = ops.linear(x768, m.gate_up_proj.packed_weight(), epilogue=_lib.EPI_SILU_MUL)
-            outs["d"] = ops.linear(xf, m.down_proj.weight)
-        outs["lm"] = ops.linear(x768, llm.model.model.embed_tokens.weight)
+            outs["qkv"] = ops.linear_stat_norm(stats, nw, 1e-6, a.qkv_proj.weight)
+            outs["o"] = ops.linear_add_stat(xo, a.o_proj.weight, res)
+            outs["gu"] = ops.linear_stat_norm(stats, nw, 1e-6, m.gate_up_proj.packed_weight(),
+                                              epilogue=_lib.EPI_SILU_MUL)
+            outs["d"] = ops.linear_add_stat(xf, m.down_proj.weight, res)
+        outs["lm"] = ops.linear_stat_norm(stats, nw, 1e-6, llm.model.model.embed_tokens.weight)
 
     run()
     torch.cuda.synchronize(dev)

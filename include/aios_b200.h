@@ -116,6 +116,15 @@ AIOSB_API int aiosb_silu_mul(const void* x, int64_t rows, int64_t f, void* out, 
 AIOSB_API int aiosb_embedding(const void* ids, int ids_is_int64, int64_t num_tokens, const void* weight, int64_t vocab,
                     int64_t hidden, void* out, int32_t* status, void* stream);
 
+/* Embedding gather that also emits the RMSNorm statistics of its rows, for a
+ * first layer whose input norm is a plain RMSNorm of the embeddings
+ * (aios/models/qwen3.py:113 with residual None, aios/layers/norm.py:34-38):
+ * stat_x [num_tokens, hidden] fp32 = the rows, stat_ss[t] = sum of squares of
+ * row t (one part). aiosb_linear_stat_norm consumes them. */
+AIOSB_API int aiosb_embedding_stat(const void* ids, int ids_is_int64, int64_t num_tokens, const void* weight,
+                                   int64_t vocab, int64_t hidden, void* out, float* stat_x, float* stat_ss,
+                                   int32_t* status, void* stream);
+
 /* ---- Linear (tcgen05 tensor-core GEMM) -------------------------------------
  * Replaces the cuBLAS GEMMs behind aios/layers/linear.py:16-17 (Linear.forward)
  * and aios/layers/embedding.py:34-41 (LMHead.forward): y = x W^T.
@@ -141,6 +150,31 @@ AIOSB_API int aiosb_linear_rmsnorm(const void* x, const void* res, void* res_out
                                    int64_t rows, int64_t k, const void* w, int64_t n, void* y, int64_t y_row_stride,
                                    int epilogue, const void* residual, int64_t residual_stride, int32_t* status,
                                    void* stream);
+
+/* Residual GEMM that also emits RMSNorm statistics (producer half of a
+ * residual add + RMSNorm split across two GEMMs). Replaces Linear.forward
+ * followed by the add of RMSNormFused.forward (aios/layers/linear.py:21-22,
+ * aios/layers/norm.py:34-40, as used at aios/models/qwen3.py:106-120):
+ * y = bf16(s), s = residual + bf16(x W^T) in fp32 (residual may alias y),
+ * stat_x [rows, n] fp32 = s, and for each 128-column tile p the sum of squares of
+ * s over its columns: stat_ss[p * stat_ss_stride + row]. n <= 2048. */
+AIOSB_API int aiosb_linear_add_stat(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
+                                    int64_t y_row_stride, const void* residual, int64_t residual_stride,
+                                    float* stat_x, float* stat_ss, int64_t stat_ss_stride, int32_t* status,
+                                    void* stream);
+
+/* GEMM on RMSNorm-ed rows given their statistics (consumer half): the
+ * normalisation of RMSNormFused.forward (aios/layers/norm.py:34-40) followed by
+ * Linear.forward / the SwiGLU or residual epilogues of aiosb_linear:
+ * y = epilogue(bf16(s * rcp * norm_w) W^T), rcp = 1 / sqrt(sum_p stat_ss[p *
+ * stat_ss_stride + row] / k + eps) with the parts summed in order, s = stat_x
+ * [rows, k] fp32. The normalised rows are built by the GEMM's CTAs straight
+ * into the tensor-core operand layout; no normalised tensor is written. */
+AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, int64_t stat_ss_stride,
+                                     int64_t parts, const void* norm_w, float eps, int64_t rows, int64_t k,
+                                     const void* w, int64_t n, void* y, int64_t y_row_stride, int epilogue,
+                                     const void* residual, int64_t residual_stride, int32_t* status,
+                                     void* stream);
 
 /* ---- Attention ---------------------------------------------------------------
  * KV slots: token slot s of one layer lives at k_cache + s * num_kv_heads *

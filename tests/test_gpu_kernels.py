@@ -409,3 +409,56 @@ def test_linear_with_fused_rmsnorm(cuda_device, rows: int, with_res: bool, epi: 
     _bf16_close(y, ref, ulps=2.0, atol=2e-3)
     if with_res:
         assert torch.equal(res_out.cpu(), new_res)
+
+
+@pytest.mark.parametrize("rows", [1, 8, 13, 64, 100, 300])
+@pytest.mark.parametrize("epi", ["store", "silu"])
+def test_residual_statistics_chain(cuda_device, rows: int, epi: str) -> None:
+    """o_proj with the add+statistics epilogue, then a GEMM that normalises its
+    input from those statistics: equals fused_add_rmsnorm followed by a linear."""
+    g = torch.Generator().manual_seed(900 + rows)
+    dev = cuda_device
+    d, ka = 768, 768
+    a = torch.randn(rows, ka, generator=g).to(torch.bfloat16)
+    wo = (torch.randn(d, ka, generator=g) * 0.02).to(torch.bfloat16)
+    res = torch.randn(rows, d, generator=g).to(torch.bfloat16)
+    nw = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    n = 4096 if epi == "silu" else 1280
+    w = (torch.randn(n, d, generator=g) * 0.02).to(torch.bfloat16)
+    # reference: o = bf16(a Wo^T) from the same GEMM; fused_add_rmsnorm(o, res)
+    o = ops.linear(a.to(dev), wo.to(dev)).cpu()
+    normed, new_res = oops.fused_add_rmsnorm(o, res, nw, 1e-6)
+    s_ref = o.float() + res.float()
+    ref = normed.float() @ w.float().T
+    res_dev = res.to(dev)
+    stats = ops.linear_add_stat(a.to(dev), wo.to(dev), res_dev)
+    if epi == "silu":
+        y = ops.linear_stat_norm(stats, nw.to(dev), 1e-6, ops.pack_gate_up(w.to(dev)), epilogue=_lib.EPI_SILU_MUL)
+        ref = oops.silu_and_mul(ref.to(torch.bfloat16))
+    else:
+        y = ops.linear_stat_norm(stats, nw.to(dev), 1e-6, w.to(dev))
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    # the residual update is bit-exact (same GEMM, same rounding points)
+    assert torch.equal(res_dev.cpu(), new_res)
+    assert torch.equal(stats.x.cpu(), s_ref)
+    part = (s_ref * s_ref).view(rows, d // 128, 128).sum(-1).T
+    torch.testing.assert_close(stats.ss.cpu(), part, rtol=1e-5, atol=1e-5)
+    _bf16_close(y, ref, ulps=2.0, atol=2e-3)
+
+
+def test_embedding_statistics(cuda_device) -> None:
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(1000, 768, generator=g).to(torch.bfloat16)
+    ids = torch.tensor([3, 999, 0, 512, 3], dtype=torch.int64)
+    out, st = ops.embedding_stat(ids.to(cuda_device), w.to(cuda_device))
+    torch.cuda.synchronize()
+    ops.check_status(cuda_device)
+    assert torch.equal(out.cpu(), w[ids])
+    assert torch.equal(st.x.cpu(), w[ids].float())
+    torch.testing.assert_close(st.ss.cpu()[0], (w[ids].float() ** 2).sum(-1), rtol=1e-5, atol=1e-4)
+    nw = torch.ones(768, dtype=torch.bfloat16)
+    lin = (torch.randn(1280, 768, generator=g) * 0.02).to(torch.bfloat16)
+    y = ops.linear_stat_norm(st, nw.to(cuda_device), 1e-6, lin.to(cuda_device))
+    ref = oops.rmsnorm(w[ids], nw, 1e-6).float() @ lin.float().T
+    _bf16_close(y, ref, ulps=2.0, atol=2e-3)
