@@ -128,7 +128,7 @@ _SIGNATURES = {
     "aiosb_linear_rmsnorm": (
         [_p, _p, _p, _p, _f32, _i64, _i64, _p, _i64, _p, _i64, _i32, _p, _i64, _p, _p], _i32
     ),
-    "aiosb_linear_add_stat": ([_p, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _p, _p], _i32),
+    "aiosb_linear_add_stat": ([_p, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _p, _p, _i64, _p, _p, _p], _i32),
     "aiosb_linear_stat_norm": (
         [_p, _p, _i64, _i64, _p, _f32, _i64, _i64, _p, _i64, _p, _i64, _i32, _p, _i64, _p, _p], _i32
     ),

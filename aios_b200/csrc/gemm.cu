@@ -23,6 +23,7 @@
 #include <mutex>
 
 #include "abi_util.h"
+#include "gemv.h"
 #include "common.cuh"
 
 namespace aiosb {
@@ -71,7 +72,7 @@ struct GemmArgs {
 };
 
 constexpr int kMaxNormRows = 64;
-constexpr int kMaxStatParts = 16;
+constexpr int kMaxStatParts = 256;  // sum-of-squares parts (8-column groups of n <= 2048)
 
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -151,9 +152,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t tg = (int64_t)n_tile * BN + t;
         float ss = 0.f;
         if (tg < a.rows) {
-#pragma unroll
-          for (int p = 0; p < kMaxStatParts; ++p)
-            if (p < P) ss += a.stat_ss[p * a.stat_ss_stride + tg];
+#pragma unroll 8
+          for (int p = 0; p < P; ++p) ss += a.stat_ss[p * a.stat_ss_stride + tg];
         }
         rcp_s[t] = 1.0f / sqrtf(ss / (float)K + a.neps);
       }
@@ -181,12 +181,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             s1[j] = sp[1];
             wv[j] = *reinterpret_cast<const uint4*>(a.nw + kk);
             if (inline_rcp) {
-              float part[kMaxStatParts];
-#pragma unroll
-              for (int p = 0; p < kMaxStatParts; ++p) part[p] = p < P ? a.stat_ss[p * a.stat_ss_stride + tg] : 0.f;
               float ss = 0.f;
-#pragma unroll
-              for (int p = 0; p < kMaxStatParts; ++p) ss += part[p];
+#pragma unroll 8
+              for (int p = 0; p < P; ++p) ss += a.stat_ss[p * a.stat_ss_stride + tg];
               rc[j] = 1.0f / sqrtf(ss / (float)K + a.neps);
             } else {
               rc[j] = rcp_s[t];
@@ -472,7 +469,7 @@ size_t smem_bytes(int stages, bool norm = false, int chunks = 0) {
   const size_t pipe = norm ? (size_t)stages * kABytes + (size_t)chunks * BN * kBK * 2
                            : (size_t)stages * (kABytes + BN * kBK * 2);
   const size_t red = (size_t)BN * kBM * 4;
-  return std::max(pipe, red) + 1024 /*alignment*/ + 256 /*barriers*/;
+  return std::max(pipe, red) + 1024 /*alignment*/ + 512 /*barriers*/;
 }
 
 constexpr int kMaxDynSmem = 227 * 1024 - 2048;  // opt-in limit minus the static rcp table
@@ -541,8 +538,33 @@ int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* 
   a.rows = rows;
   a.n = n;
   a.k_total = k;
-  a.split = choose_split(m_tiles * n_tiles, chunks, sm_count());
+  const int64_t n_out = a.epilogue == AIOSB_EPI_SILU_MUL ? n / 2 : n;
+  if (a.norm != 1 && gemv_eligible(rows, k, n_out)) {
+    // decode widths: CUDA-core GEMV (weights requested before the dependency wait)
+    GemvArgs g;
+    memset(&g, 0, sizeof(g));
+    g.x = (const __nv_bfloat16*)x;
+    g.x_stride = k;
+    g.stat_x = a.norm == 2 ? a.stat_x : nullptr;
+    g.nw = a.nw;
+    g.eps = a.neps;
+    g.w = (const __nv_bfloat16*)w;
+    g.n = n;
+    g.n_out = n_out;
+    g.k = k;
+    g.rows = (int)rows;
+    g.y = a.y;
+    g.y_stride = a.y_row_stride;
+    g.epilogue = a.epilogue;
+    g.residual = a.residual;
+    g.residual_stride = a.residual_stride;
+    g.out_stat_x = a.out_stat_x;
+    g.out_stat_ss = a.out_stat_ss;
+    g.out_ss_stride = a.out_ss_stride;
+    return gemv_launch(g, as_stream(stream));
+  }
   auto plan = [&]() {
+    a.split = choose_split(m_tiles * n_tiles, chunks, sm_count());
     a.chunks_per_split = (int)(chunks / a.split);
     a.stages = std::min(a.chunks_per_split, max_stages_for(bn));
     // keep the norm-mode B buffer + weight stages inside the shared-memory budget
@@ -575,7 +597,6 @@ int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* 
     // Non-portable 16-CTA clusters are an opt-in; fall back to portable sizes.
     (void)cudaGetLastError();
     g_max_split = 8;
-    a.split = choose_split(m_tiles * n_tiles, chunks, sm_count());
     plan();
     rc = launch();
   }
@@ -651,16 +672,18 @@ extern "C" int aiosb_linear_rmsnorm(const void* x, const void* res, void* res_ou
 
 extern "C" int aiosb_linear_add_stat(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
                                      int64_t y_row_stride, const void* residual, int64_t residual_stride,
-                                     float* stat_x, float* stat_ss, int64_t stat_ss_stride, int32_t* status,
-                                     void* stream) {
+                                     float* stat_x, float* stat_ss, int64_t stat_ss_stride, int64_t* stat_parts,
+                                     int32_t* status, void* stream) {
+  if (stat_parts != nullptr)
+    *stat_parts = gemv_eligible(rows, k, n) ? n / kGemvStatGroup : n / kBM;
   int rc = check_common(w, rows, k, n, y, y_row_stride, AIOSB_EPI_ADD, residual, residual_stride);
   if (rc != AIOSB_OK) return rc == 1 ? AIOSB_OK : rc;
   AIOSB_REQUIRE(x && aligned16(x), AIOSB_ERR_MISALIGNED, "linear_add_stat: x must be a 16-byte aligned pointer");
   AIOSB_REQUIRE(stat_x && stat_ss && aligned16(stat_x), AIOSB_ERR_MISALIGNED,
                 "linear_add_stat: stat_x must be a 16-byte aligned pointer and stat_ss non-null");
   AIOSB_REQUIRE(stat_ss_stride >= rows, AIOSB_ERR_INVALID_ARG, "linear_add_stat: stat_ss stride below rows");
-  AIOSB_REQUIRE(n / kBM <= kMaxStatParts, AIOSB_ERR_UNSUPPORTED, "linear_add_stat: n above %d",
-                kMaxStatParts * kBM);
+  AIOSB_REQUIRE(n / kGemvStatGroup <= kMaxStatParts, AIOSB_ERR_UNSUPPORTED, "linear_add_stat: n above %d",
+                kMaxStatParts * kGemvStatGroup);
   GemmArgs a = base_args(y, y_row_stride, AIOSB_EPI_ADD, residual, residual_stride, status);
   a.out_stat_x = stat_x;
   a.out_stat_ss = stat_ss;

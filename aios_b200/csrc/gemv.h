@@ -1,0 +1,41 @@
+// Decode-width linears on the CUDA cores (gemv.cu), dispatched from the C-ABI
+// linear entry points in gemm.cu for at most kMaxGemvRows token rows.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace aiosb {
+
+constexpr int kMaxGemvRows = 16;
+constexpr int kMaxGemvK = 2048;
+
+struct GemvArgs {
+  const __nv_bfloat16* x;  // [rows, k] bf16 operand rows (row stride x_stride), or NULL:
+  int64_t x_stride;
+  const float* stat_x;      // statistics mode: rows = bf16(stat_x * rcp * nw), rcp from the row itself
+  const __nv_bfloat16* nw;
+  float eps;
+  const __nv_bfloat16* w;   // [n, k] weights
+  int64_t n;                // weight rows
+  int64_t n_out;            // output features (n, or n / 2 for SwiGLU)
+  int64_t k;
+  int rows;
+  __nv_bfloat16* y;
+  int64_t y_stride;
+  int epilogue;
+  const __nv_bfloat16* residual;
+  int64_t residual_stride;
+  float* out_stat_x;        // ADD: fp32 s [rows, n_out] and per-8-column sums of squares
+  float* out_stat_ss;       // out_stat_ss[group * out_ss_stride + row], group = column / 8
+  int64_t out_ss_stride;
+};
+
+// Columns per sum-of-squares part written by the GEMV residual epilogue.
+constexpr int kGemvStatGroup = 8;
+
+bool gemv_eligible(int64_t rows, int64_t k, int64_t n_out);
+int gemv_launch(const GemvArgs& a, cudaStream_t stream);
+
+}  // namespace aiosb

@@ -414,11 +414,12 @@ def linear_add_stat(x: torch.Tensor, weight: torch.Tensor, residual: torch.Tenso
     rows, n = x.shape[0], weight.shape[0]
     if residual.shape != (rows, n) or residual.stride(1) != 1:
         raise ValueError("linear_add_stat needs a residual [rows, n] with contiguous rows")
-    st = RowStats.empty(rows, n, n // 128, x.device)
+    st = RowStats.empty(rows, n, n // 8, x.device)
+    parts = ctypes.c_int64(0)
     _lib.call("aiosb_linear_add_stat", x.data_ptr(), rows, x.shape[1], weight.data_ptr(), n, residual.data_ptr(),
               residual.stride(0), residual.data_ptr(), residual.stride(0), st.x.data_ptr(), st.ss.data_ptr(),
-              st.ss.stride(0), status_word(x.device).data_ptr(), _stream(x.device))
-    return st
+              st.ss.stride(0), ctypes.byref(parts), status_word(x.device).data_ptr(), _stream(x.device))
+    return RowStats(st.x, st.ss[: parts.value])
 
 
 def linear_stat_norm(

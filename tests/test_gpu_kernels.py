@@ -442,7 +442,9 @@ def test_residual_statistics_chain(cuda_device, rows: int, epi: str) -> None:
     # the residual update is bit-exact (same GEMM, same rounding points)
     assert torch.equal(res_dev.cpu(), new_res)
     assert torch.equal(stats.x.cpu(), s_ref)
-    part = (s_ref * s_ref).view(rows, d // 128, 128).sum(-1).T
+    # parts: 128-column tiles (tcgen05) or 8-column groups (decode widths)
+    assert stats.parts == (d // 8 if rows <= 16 else d // 128)
+    part = (s_ref * s_ref).view(rows, stats.parts, d // stats.parts).sum(-1).T
     torch.testing.assert_close(stats.ss.cpu(), part, rtol=1e-5, atol=1e-5)
     _bf16_close(y, ref, ulps=2.0, atol=2e-3)
 
