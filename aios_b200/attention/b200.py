@@ -47,6 +47,9 @@ class B200AttentionMetadata(BaseAttentionMetadata):
     seq_lens: torch.Tensor | None = None  # int32 [rows] (decode)
     prefix_len: torch.Tensor | None = None  # int32 [1]: shared prefix keys (decode)
     active: torch.Tensor | None = None  # int32 [rows] (decode)
+    # decode: the row table, prefix length and every key before the current
+    # position were written by earlier launches (the CandidateGroup runtime)
+    stable_history: bool = False
 
     def get_last_indices(self, bs: int) -> torch.Tensor:
         assert self.cu_seqlens_q is not None, "last indices exist for prefill batches"
@@ -143,7 +146,7 @@ class B200AttentionBackend(BaseAttentionBackend):
             seq_lens=md.seq_lens, positions=md.positions, num_qo_heads=self.num_heads,
             num_kv_heads=self.num_kv_heads, head_dim=self.head_dim, scale=self.sm_scale, qkv=qkv,
             q_norm_w=q_norm_w, k_norm_w=k_norm_w, eps=self.eps, cos=cos, sin=sin, out_loc=md.out_loc,
-            prefix_len=md.prefix_len, active=md.active,
+            prefix_len=md.prefix_len, active=md.active, stable_history=md.stable_history,
         )
 
     # -- reference slot API (q/k already normalised and rotated) ---------------

@@ -350,6 +350,206 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const DecodeAr
   if (clustered) cluster_sync();  // peers may still be copying from this CTA's stage buffers
 }
 
+// ---- decode with the key history staged before the dependency wait -----------
+// Used when the caller guarantees that the row table, the prefix length, the
+// page-table entries before each row's current position and the K/V they point
+// to were all written by earlier launches (the CandidateGroup runtime: prefix
+// from the prefill, older suffix keys from earlier steps). CTA (h, r) then copies
+// the prefix keys (up to kHistPrefix), row r's older suffix keys (up to
+// kHistSuffix - 1), the RoPE rows of positions [P, P + kRopeWin) and the norm
+// weights into shared memory BEFORE griddepcontrol.wait, i.e. while the qkv
+// projection still runs. After the wait it loads one round (the projection row,
+// position, key count, output slot, active flag), applies q/k RMSNorm + bf16 RoPE,
+// stores the new K/V and folds everything from shared memory, the new key from
+// its own registers. Table entries past a row's current position are read
+// (clamped to slot 0) but never used. Longer histories stream the rest from the
+// cache after the wait.
+constexpr int kHistPrefix = 128;
+constexpr int kHistSuffix = 32;
+constexpr int kRopeWin = 32;
+
+template <int D>
+size_t hist_decode_smem(int group) {
+  const size_t krow = (size_t)(D + 2) * 2, vrow = (size_t)D * 2;
+  return (size_t)group * D * 4 + (size_t)kDecWarps * D * 4 +
+         (size_t)(kHistPrefix + kHistSuffix + kKeyChunk) * (krow + vrow) + (size_t)2 * kRopeWin * D * 2 +
+         (size_t)2 * D * 2;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const DecodeArgs a) {
+  constexpr int DPL = D / 32;
+  constexpr int KR = D + 2;  // padded K row (odd 32-bit word stride)
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __shared__ int32_t slot_s[kHistPrefix + kHistSuffix];
+  const int h = blockIdx.x, r = blockIdx.y;
+  const int g = a.hq / a.hkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* q_s = reinterpret_cast<float*>(smem_raw);  // [g][D]
+  float* tmp = q_s + g * D;                          // [warps][D]
+  __nv_bfloat16* Kp = reinterpret_cast<__nv_bfloat16*>(tmp + kDecWarps * D);  // [kHistPrefix][KR]
+  __nv_bfloat16* Ks = Kp + kHistPrefix * KR;   // [kHistSuffix][KR]: older suffix, then the new key
+  __nv_bfloat16* Kw = Ks + kHistSuffix * KR;   // [kKeyChunk][KR]: streamed overflow
+  __nv_bfloat16* Vp = Kw + kKeyChunk * KR;     // [kHistPrefix][D]
+  __nv_bfloat16* Vs = Vp + kHistPrefix * D;    // [kHistSuffix][D]
+  __nv_bfloat16* Vw = Vs + kHistSuffix * D;    // [kKeyChunk][D]
+  __nv_bfloat16* cos_w = Vw + kKeyChunk * D;   // [kRopeWin][D]
+  __nv_bfloat16* sin_w = cos_w + kRopeWin * D;
+  __nv_bfloat16* nq = sin_w + kRopeWin * D;    // [D]
+  __nv_bfloat16* nk = nq + D;                  // [D]
+  const int64_t tok_stride = (int64_t)a.hkv * D;
+  pdl_launch_dependents();
+
+  // ---- before the wait: history fixed since earlier launches
+  const int P = a.prefix_len != nullptr ? *a.prefix_len : 0;
+  const int64_t prow = a.row_table[0], rrow = a.row_table[r];
+  const int np = min(P, kHistPrefix);
+  const int64_t room = a.table_stride - P;  // table entries after the prefix
+  const int ns_cap = room <= 0 ? 0 : (room < kHistSuffix - 1 ? (int)room : kHistSuffix - 1);
+  for (int i = threadIdx.x; i < np + ns_cap; i += kDecThreads)
+    slot_s[i] = a.page_table[i < np ? prow * a.table_stride + i : rrow * a.table_stride + P + (i - np)];
+  for (int i = threadIdx.x; i < D; i += kDecThreads) {
+    nq[i] = a.q_norm_w[i];
+    nk[i] = a.k_norm_w[i];
+  }
+  for (int i = threadIdx.x; i < kRopeWin * (D / 8); i += kDecThreads) {
+    const int row = i / (D / 8), c = i % (D / 8);
+    const int pos = P + row;
+    if (pos < a.max_pos) {
+      reinterpret_cast<uint4*>(cos_w + row * D)[c] = reinterpret_cast<const uint4*>(a.cos_tab + (int64_t)pos * D)[c];
+      reinterpret_cast<uint4*>(sin_w + row * D)[c] = reinterpret_cast<const uint4*>(a.sin_tab + (int64_t)pos * D)[c];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < (np + ns_cap) * (D / 8); i += kDecThreads) {
+    const int j = i / (D / 8), c = i % (D / 8);
+    int64_t slot = slot_s[j];
+    if (slot < 0 || slot >= a.num_slots) slot = 0;  // checked again after the wait for the keys in use
+    const uint4 kv = reinterpret_cast<const uint4*>(a.k_cache + slot * tok_stride + (int64_t)h * D)[c];
+    const uint4 vv = reinterpret_cast<const uint4*>(a.v_cache + slot * tok_stride + (int64_t)h * D)[c];
+    uint32_t* kd = reinterpret_cast<uint32_t*>(j < np ? Kp + j * KR : Ks + (j - np) * KR) + c * 4;
+    kd[0] = kv.x;
+    kd[1] = kv.y;
+    kd[2] = kv.z;
+    kd[3] = kv.w;
+    reinterpret_cast<uint4*>(j < np ? Vp + j * D : Vs + (j - np) * D)[c] = vv;
+  }
+
+  pdl_wait();
+  // ---- after the wait: this step's row (one round of loads)
+  const int pos_in = a.positions[r];
+  const int L_in = a.seq_lens[r];
+  const bool act = a.active == nullptr || a.active[r] != 0;
+  const int64_t oslot = a.out_loc[r];
+  // keys of this row: the prefix, its older suffix keys and the new one
+  const int L_lo = L_in > P + 1 ? L_in : P + 1;
+  const int L = (int64_t)L_lo > a.table_stride ? (int)a.table_stride : L_lo;
+  if (act && threadIdx.x == 0 && (L_in < P + 1 || L_in > a.table_stride)) report(a.status, AIOSB_DEV_POSITION_RANGE);
+  const int ns_old = L - 1 - P;  // older suffix keys of this row (>= 0)
+  const int new_row = ns_old <= ns_cap ? ns_old : kHistSuffix - 1;
+  if (act) {
+    int pos = pos_in;
+    if (pos < 0 || pos >= a.max_pos) {
+      if (threadIdx.x == 0) report(a.status, AIOSB_DEV_POSITION_RANGE);
+      pos = 0;
+    }
+    const bool in_win = pos >= P && pos < P + kRopeWin;
+    const __nv_bfloat16* cos_row = in_win ? cos_w + (pos - P) * D : a.cos_tab + (int64_t)pos * D;
+    const __nv_bfloat16* sin_row = in_win ? sin_w + (pos - P) * D : a.sin_tab + (int64_t)pos * D;
+    for (int it = warp; it < g + 1; it += kDecWarps) {
+      float* tw = tmp + warp * D;
+      float x[DPL];
+      if (it < g) {
+        const __nv_bfloat16* src = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(h * g + it) * D;
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(src[i * 32 + lane]);
+        norm_rope<D>(x, nq, a.eps, cos_row, sin_row, true, true, lane, tw);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) q_s[it * D + i * 32 + lane] = x[i];
+      } else {
+        const __nv_bfloat16* ksrc = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(a.hq + h) * D;
+        const __nv_bfloat16* vsrc = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(a.hq + a.hkv + h) * D;
+        __nv_bfloat16 vraw[DPL];
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          x[i] = bf16_to_f(ksrc[i * 32 + lane]);
+          vraw[i] = vsrc[i * 32 + lane];
+        }
+        norm_rope<D>(x, nk, a.eps, cos_row, sin_row, true, true, lane, tw);
+        const bool slot_ok = oslot >= 0 && oslot < a.num_slots;
+        if (!slot_ok && lane == 0) report(a.status, AIOSB_DEV_SLOT_RANGE);
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) {
+          const __nv_bfloat16 kb = f_to_bf16(x[i]);
+          Ks[new_row * KR + i * 32 + lane] = kb;
+          Vs[new_row * D + i * 32 + lane] = vraw[i];
+          if (slot_ok) {
+            a.k_cache[oslot * tok_stride + (int64_t)h * D + i * 32 + lane] = kb;
+            a.v_cache[oslot * tok_stride + (int64_t)h * D + i * 32 + lane] = vraw[i];
+          }
+        }
+      }
+    }
+    if (threadIdx.x == 0) {  // the staged keys this row uses must be real slots
+      bool bad = false;
+      for (int j = 0; j < np + min(ns_old, ns_cap); ++j) bad |= slot_s[j] < 0 || slot_s[j] >= a.num_slots;
+      if (bad) report(a.status, AIOSB_DEV_SLOT_RANGE);
+    }
+  }
+  __syncthreads();
+
+  QState<D> st[2];
+  qstate_init<D>(st[0]);
+  qstate_init<D>(st[1]);
+  auto fold_all = [&](const __nv_bfloat16* K, const __nv_bfloat16* V, int nk) {
+    if (!act) return;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int j = warp + t * kDecWarps;
+      if (j < g) fold_chunk<D>(st[t], q_s + j * D, K, V, nk, a.scale, lane);
+    }
+  };
+  const int32_t* pslots = a.page_table + prow * a.table_stride;
+  const int32_t* rslots = a.page_table + rrow * a.table_stride;
+  // prefix: staged part, then any overflow streamed from the cache
+  for (int c0 = 0; c0 < np; c0 += kKeyChunk) fold_all(Kp + c0 * KR, Vp + c0 * D, min(kKeyChunk, np - c0));
+  for (int k0 = np; k0 < P; k0 += kKeyChunk) {
+    const int n = min(kKeyChunk, P - k0);
+    stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, pslots, k0, n, a.num_slots, Kw, Vw, a.status);
+    __syncthreads();
+    fold_all(Kw, Vw, n);
+    __syncthreads();
+  }
+  // suffix: older keys (+ the new key when contiguous), overflow, new key
+  if (act) {
+    if (ns_old <= ns_cap) {
+      fold_all(Ks, Vs, ns_old + 1);
+    } else {
+      fold_all(Ks, Vs, ns_cap);
+      for (int k0 = P + ns_cap; k0 < L - 1; k0 += kKeyChunk) {
+        const int n = min(kKeyChunk, L - 1 - k0);
+        stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, rslots, k0, n, a.num_slots, Kw, Vw, a.status);
+        __syncthreads();
+        fold_all(Kw, Vw, n);
+        __syncthreads();
+      }
+      fold_all(Ks + (kHistSuffix - 1) * KR, Vs + (kHistSuffix - 1) * D, 1);
+    }
+  }
+
+  // ---- normalise and store (zeros for inactive rows)
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int j = warp + t * kDecWarps;
+    if (j < g) {
+      const float inv = act && st[t].l > 0.f ? 1.0f / st[t].l : 0.f;
+      __nv_bfloat16* dst = a.out + (int64_t)r * a.out_stride + (int64_t)(h * g + j) * D;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st[t].acc[i] * inv);
+    }
+  }
+}
+
 }  // namespace
 }  // namespace aiosb
 
@@ -555,6 +755,20 @@ cudaError_t launch_decode(const DecodeArgs& a, int rows, int hkv, int group, cud
   return cudaLaunchKernelEx(&cfg, kern, a, cluster_rows);
 }
 template <int D>
+cudaError_t launch_decode_hist(const DecodeArgs& a, int rows, int hkv, int group, cudaStream_t stream) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = attn_decode_hist_kernel<D>;
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_decode_smem<D>(kMaxGroupQ));
+    configured[dev] = true;
+  }
+  return launch_pdl(kern, dim3((unsigned)hkv, (unsigned)rows), dim3(kDecThreads), hist_decode_smem<D>(group), stream,
+                    a);
+}
+
+template <int D>
 size_t prefill_smem(int queries) {
   return (size_t)queries * D * 4 + (size_t)kKeyChunk * (D + 2) * 2 + (size_t)kKeyChunk * D * 2;
 }
@@ -575,8 +789,9 @@ extern "C" int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const
                                       const int32_t* out_loc, void* k_cache, void* v_cache, int64_t num_slots,
                                       const int32_t* page_table, int64_t table_stride, const int32_t* row_table,
                                       const int32_t* seq_lens, const int32_t* prefix_len, const int32_t* active,
-                                      int64_t rows, int64_t num_qo_heads, int64_t num_kv_heads, int64_t head_dim,
-                                      float scale, void* out, int64_t out_stride, int32_t* status, void* stream) {
+                                      int stable_history, int64_t rows, int64_t num_qo_heads, int64_t num_kv_heads,
+                                      int64_t head_dim, float scale, void* out, int64_t out_stride, int32_t* status,
+                                      void* stream) {
   AIOSB_REQUIRE(rows >= 0 && num_kv_heads > 0 && num_qo_heads > 0 && num_qo_heads % num_kv_heads == 0,
                 AIOSB_ERR_INVALID_ARG, "query head count must be divisible by KV head count");
   AIOSB_REQUIRE(head_dim == 64 || head_dim == 96 || head_dim == 128, AIOSB_ERR_UNSUPPORTED,
@@ -622,9 +837,17 @@ extern "C" int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const
   a.status = status;
   cudaError_t e;
   cudaStream_t s = as_stream(stream);
-  if (head_dim == 64) e = launch_decode<64>(a, (int)rows, (int)num_kv_heads, (int)g, s);
-  else if (head_dim == 96) e = launch_decode<96>(a, (int)rows, (int)num_kv_heads, (int)g, s);
-  else e = launch_decode<128>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+  if (stable_history && qkv != nullptr) {
+    if (head_dim == 64) e = launch_decode_hist<64>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+    else if (head_dim == 96) e = launch_decode_hist<96>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+    else e = launch_decode_hist<128>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+  } else if (head_dim == 64) {
+    e = launch_decode<64>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+  } else if (head_dim == 96) {
+    e = launch_decode<96>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+  } else {
+    e = launch_decode<128>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+  }
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attention_decode: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }

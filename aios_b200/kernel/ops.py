@@ -484,7 +484,12 @@ def attention_decode(
     out_loc: torch.Tensor | None = None,
     prefix_len: torch.Tensor | None = None,
     active: torch.Tensor | None = None,
+    stable_history: bool = False,
 ) -> torch.Tensor:
+    """Decode attention. ``stable_history`` (fused ``qkv`` mode): the row table,
+    prefix length, page-table entries before each row's current position and their
+    K/V were written before the previous kernel on the stream began, so the kernel
+    may stage them before waiting on that kernel."""
     rows = out.shape[0]
     num_slots = k_cache.numel() // (num_kv_heads * head_dim)
     src = qkv if qkv is not None else q
@@ -511,6 +516,7 @@ def attention_decode(
         seq_lens.data_ptr(),
         _ptr(prefix_len),
         _ptr(active),
+        int(bool(stable_history)),
         rows,
         num_qo_heads,
         num_kv_heads,

@@ -155,7 +155,7 @@ class CandidateGroupRuntime:
         batch.attn_metadata = B200AttentionMetadata(
             phase="decode", positions=self.positions[:rows], out_loc=self.out_loc[:rows],
             row_table=self.row_table[:rows], seq_lens=self.seq_lens[:rows], prefix_len=self.prefix_len_view,
-            active=self.active[:rows],
+            active=self.active[:rows], stable_history=True,
         )
         return batch
 

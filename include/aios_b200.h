@@ -195,14 +195,21 @@ AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, 
  * row row_table[r]. Pass either qkv (raw projection [rows, qkv_stride]: q | k | v
  * heads) or q (already normalised and rotated [rows, q_stride]). Rows with
  * active[r] == 0 are skipped (output zeros, no store); active may be NULL.
- * rows * (num_qo_heads / num_kv_heads) <= 64. out: [rows, out_stride] bf16. */
+ * rows * (num_qo_heads / num_kv_heads) <= 64. out: [rows, out_stride] bf16. *
+ * stable_history != 0 (fused mode only) asserts that row_table, *prefix_len, the
+ * page-table entries before each row's current position and the K/V they point
+ * to were written by launches that completed before the previous kernel on this
+ * stream began (the CandidateGroup runtime: prefix from the prefill, older
+ * suffix keys from earlier steps). The kernel then copies that history into
+ * shared memory before waiting on the previous kernel, and after the wait only
+ * this step's projection row and metadata stay on its critical path. */
 AIOSB_API int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const void* q, int64_t q_stride,
                            const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_tab,
                            const void* sin_tab, int64_t max_pos, const int32_t* positions, const int32_t* out_loc,
                            void* k_cache, void* v_cache, int64_t num_slots, const int32_t* page_table,
                            int64_t table_stride, const int32_t* row_table, const int32_t* seq_lens,
-                           const int32_t* prefix_len, const int32_t* active, int64_t rows, int64_t num_qo_heads,
-                           int64_t num_kv_heads, int64_t head_dim, float scale, void* out, int64_t out_stride,
+                           const int32_t* prefix_len, const int32_t* active, int stable_history,
+                           int64_t rows, int64_t num_qo_heads, int64_t num_kv_heads, int64_t head_dim, float scale, void* out, int64_t out_stride,
                            int32_t* status, void* stream);
 
 /* Prefill prologue: replaces the q/k RMSNorm (aios/models/qwen3.py:66-67),

@@ -140,20 +140,35 @@ def _rope_tables(d: int, max_pos: int, device):
     return cos, sin, cos.to(torch.bfloat16).to(device), sin.to(torch.bfloat16).to(device)
 
 
+DECODE_CASES = [
+    # prefix, suffix (incl. the new token), page_size, stable_history, inactive rows
+    (13, 5, 1, False, False),
+    (13, 5, 16, False, False),
+    (13, 5, 1, True, False),
+    (13, 5, 16, True, False),
+    (13, 1, 1, True, False),     # first decode step: no older suffix keys
+    (150, 40, 1, True, True),    # history beyond the staged prefix / suffix capacity
+    (0, 9, 1, True, False),      # no shared prefix
+    (150, 40, 1, False, True),
+]
+
+
 @pytest.mark.parametrize("hq,hkv,d", [(12, 4, 64), (8, 2, 96)])
-@pytest.mark.parametrize("page_size", [1, 16])
-def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int, d: int, page_size: int) -> None:
-    """8 candidate rows sharing a 13-token prefix, 5 suffix tokens each (the
-    newest one stored by the kernel itself)."""
-    g = torch.Generator().manual_seed(hq * d + page_size)
-    rows, prefix, suffix = 8, 13, 5
-    num_pages = 64
+@pytest.mark.parametrize("prefix,suffix,page_size,stable,inactive", DECODE_CASES)
+def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int, d: int, prefix: int, suffix: int,
+                                                 page_size: int, stable: bool, inactive: bool) -> None:
+    """8 candidate rows sharing a prefix, `suffix` own keys each (the newest one
+    normalised, rotated and stored by the kernel itself); both kernel paths."""
+    g = torch.Generator().manual_seed(hq * d + page_size + prefix + suffix)
+    rows = 8
+    num_pages = 64 if page_size == 16 else 1024
     num_slots = num_pages * page_size
+    width = 256
     cos, sin, cos_b, sin_b = _rope_tables(d, 512, cuda_device)
     eps, scale = 1e-6, d**-0.5
-    kc = torch.zeros(num_slots, hkv, d, dtype=torch.bfloat16)
-    vc = torch.zeros_like(kc)
-    table = torch.zeros(rows, 64, dtype=torch.int32)
+    kc = torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16)
+    vc = torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16)
+    table = torch.zeros(rows, width, dtype=torch.int32)
     if page_size == 1:
         perm = torch.randperm(num_slots, generator=g)
         prefix_slots = perm[:prefix]
@@ -166,15 +181,14 @@ def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int,
     for r in range(rows):
         table[r, :prefix] = prefix_slots.to(torch.int32)
         table[r, prefix : prefix + suffix] = suffix_slots[r].to(torch.int32)
-    # pre-existing cache content (already normalised/rotated as the model stores it)
-    for s in range(num_slots):
-        kc[s] = torch.randn(hkv, d, generator=g).to(torch.bfloat16)
-        vc[s] = torch.randn(hkv, d, generator=g).to(torch.bfloat16)
     qkv = torch.randn(rows, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16)
     qn = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
     kn = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
     pos = prefix + suffix - 1
     out_loc = table[:, pos].clone()
+    active = torch.ones(rows, dtype=torch.int32)
+    if inactive:
+        active[[1, 6]] = 0
     # oracle: norm + rope + store + attention
     q = qkv[:, : hq * d].view(rows, hq, d)
     k = qkv[:, hq * d : (hq + hkv) * d].view(rows, hkv, d)
@@ -182,11 +196,12 @@ def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int,
     qr = oops.apply_rope(oops.rmsnorm(q, qn, eps), cos[[pos] * rows], sin[[pos] * rows])
     kr = oops.apply_rope(oops.rmsnorm(k, kn, eps), cos[[pos] * rows], sin[[pos] * rows])
     kc_ref, vc_ref = kc.clone(), vc.clone()
-    kc_ref[out_loc.long()] = kr
-    vc_ref[out_loc.long()] = v
+    on = active.bool()
+    kc_ref[out_loc[on].long()] = kr[on]
+    vc_ref[out_loc[on].long()] = v[on]
     expected = torch.stack([
         oops.attention(qr[r : r + 1], kc_ref[table[r, : pos + 1].long()], vc_ref[table[r, : pos + 1].long()],
-                       torch.tensor([pos]), scale)[0]
+                       torch.tensor([pos]), scale)[0] if on[r] else torch.zeros(hq, d)
         for r in range(rows)
     ])
     dev = cuda_device
@@ -200,12 +215,14 @@ def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int,
         num_qo_heads=hq, num_kv_heads=hkv, head_dim=d, scale=scale,
         qkv=qkv.to(dev), q_norm_w=qn.to(dev), k_norm_w=kn.to(dev), eps=eps, cos=cos_b, sin=sin_b,
         out_loc=out_loc.to(dev), prefix_len=torch.tensor([prefix], dtype=torch.int32, device=dev),
+        active=active.to(dev), stable_history=stable,
     )
     torch.cuda.synchronize()
     ops.check_status(dev)
-    # the stored K must be the bf16 rope of the bf16 norm, bit for bit
-    assert torch.equal(kcd[out_loc.long()].cpu(), kr)
-    assert torch.equal(vcd[out_loc.long()].cpu(), v)
+    # the stored K must be the bf16 rope of the bf16 norm, bit for bit (active rows
+    # only; an inactive row's slot keeps its old content)
+    assert torch.equal(kcd.cpu(), kc_ref)
+    assert torch.equal(vcd.cpu(), vc_ref)
     _bf16_close(out.view(rows, hq, d), expected, ulps=2.0, atol=2e-3)
 
 
