@@ -167,14 +167,14 @@ def run_cpu(keystrokes: int, warmup: int) -> dict:
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
-# dram__bytes_read.sum + dram__bytes_write.sum summed over the 57 GEMM launches of
-# one decode step, from one ncu capture of the `linears` NVTX range below
-# (profiles/gemm_tc_decode_linears_s10.md).
-DECODE_LINEAR_TRAFFIC = 204_784_640
+# dram__bytes_read.sum + dram__bytes_write.sum summed over the 57 linear launches
+# of one decode step, from one ncu capture of the `linears` NVTX range below
+# (profiles/gemv_decode_linears_s10.md).
+DECODE_LINEAR_TRAFFIC = 204_558_080
 
 
 def decode_linear_roofline(llm, peaks: dict) -> dict:
-    """Times the tcgen05 GEMM launches of one decode step (8 rows: 14 x
+    """Times the linear launches of one decode step (8 rows: 14 x
     {qkv, o, gate_up+SwiGLU, down} + LM head, the same shapes and weights as the
     keystroke) as a captured graph, with CUDA events on the launching stream."""
     from aios_b200 import _lib
@@ -232,7 +232,7 @@ def decode_linear_roofline(llm, peaks: dict) -> dict:
     wbytes = 2 * (wbytes + llm.model.model.embed_tokens.weight.numel())
     achieved = wbytes / (ms * 1e-3) / 1e9
     peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
-    return {"bound": "hbm", "kernel": "gemm_tc_kernel (decode linears, 8 rows)", "achieved": round(achieved, 1),
+    return {"bound": "hbm", "kernel": "gemv_kernel (decode linears, 8 rows, CUDA cores)", "achieved": round(achieved, 1),
             "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": DECODE_LINEAR_TRAFFIC,
             "traffic_unit": "bytes per decode step (57 launches)", "algorithmic_bytes_per_step": wbytes,
