@@ -957,8 +957,9 @@ extern "C" int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t
 
 extern "C" int aiosb_token_logprobs(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
                                     const int64_t* targets, float* out, int32_t* status, void* stream) {
-  AIOSB_REQUIRE(rows >= 0 && vocab > 0 && vocab <= kMaxVocab && row_stride >= vocab, AIOSB_ERR_INVALID_ARG,
-                "token_logprobs: bad sizes (vocab must be in [1, %d])", kMaxVocab);
+  AIOSB_REQUIRE(rows >= 0 && vocab > 0 && vocab <= kMaxVocab && (row_stride >= vocab || row_stride == 0),
+                AIOSB_ERR_INVALID_ARG,
+                "token_logprobs: bad sizes (vocab must be in [1, %d], row stride >= vocab or 0)", kMaxVocab);
   if (rows == 0) return AIOSB_OK;
   AIOSB_REQUIRE(logits && targets && out, AIOSB_ERR_INVALID_ARG, "token_logprobs: null pointer");
   cudaFuncSetAttribute(token_logprob_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

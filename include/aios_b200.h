@@ -255,7 +255,9 @@ AIOSB_API int aiosb_sample(const void* logits, int64_t rows, int64_t vocab, int6
                  float* logprob_out, int32_t* status, void* stream);
 
 /* Teacher-forced scoring (aios/ime.py:731, 827-832, 858-860): out[r] =
- * log_softmax(float(logits[r]))[targets[r]] in fp32. */
+ * log_softmax(float(logits[r]))[targets[r]] in fp32. Row r starts at
+ * logits + r * row_stride; row_stride 0 scores every target against one shared
+ * row (the prefix logits of the shared-decode scoring mode). */
 AIOSB_API int aiosb_token_logprobs(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
                                    const int64_t* targets, float* out, int32_t* status, void* stream);
 
