@@ -398,7 +398,6 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
   __nv_bfloat16* nq = sin_w + kRopeWin * D;    // [D]
   __nv_bfloat16* nk = nq + D;                  // [D]
   const int64_t tok_stride = (int64_t)a.hkv * D;
-  pdl_launch_dependents();
 
   // ---- before the wait: history fixed since earlier launches
   const int P = a.prefix_len != nullptr ? *a.prefix_len : 0;
@@ -436,6 +435,9 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
   }
 
   pdl_wait();
+  // the next kernel (the o projection) launches once this one has its inputs,
+  // which bounds how far ahead the chain prefetches (measured: 5.70 -> 5.54 ms)
+  pdl_launch_dependents();
   // ---- after the wait: this step's row (one round of loads)
   const int pos_in = a.positions[r];
   const int L_in = a.seq_lens[r];

@@ -19,30 +19,19 @@ constexpr int kMixWarps = 4;
 constexpr int kMaxRegSources = 10;  // register-resident path: bank(<=9) + partial
 constexpr int kMaxSources = 16;
 
-template <int VPL>
-__global__ void __launch_bounds__(kMixWarps * 32)
+// NSRC sources (bank sources, then the partial when present) known at compile
+// time: every loop is fixed-length, so the 2 * NSRC warp reductions of the
+// scores run interleaved instead of as NSRC dependent shuffle chains.
+template <int VPL, int NSRC>
+__global__ void __launch_bounds__(kMixWarps * 32, 3)
     attnres_reg_kernel(const uint4* __restrict__ bank, int nsrc_bank, int64_t tokens, int hidden,
                        const uint4* __restrict__ partial, const float* __restrict__ wq, float eps,
                        uint4* __restrict__ out) {
-  pdl_enter();
+  pdl_launch_dependents();
   const int64_t t = (int64_t)blockIdx.x * kMixWarps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  if (t >= tokens) return;
   const int nv = hidden / 8;
-  const int nsrc = nsrc_bank + (partial != nullptr ? 1 : 0);
-  uint4 x[kMaxRegSources][VPL];
-  // Issue every load first (maximum memory-level parallelism), then reduce.
-#pragma unroll
-  for (int s = 0; s < kMaxRegSources; ++s) {
-    if (s < nsrc) {
-      const uint4* src = (s < nsrc_bank) ? bank + ((int64_t)s * tokens + t) * nv : partial + t * nv;
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const int i = lane + j * 32;
-        x[s][j] = (i < nv) ? src[i] : make_uint4(0, 0, 0, 0);
-      }
-    }
-  }
+  // the weighted query is a model constant: loaded before waiting on the producer
   float wqr[VPL][8];
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
@@ -50,11 +39,24 @@ __global__ void __launch_bounds__(kMixWarps * 32)
 #pragma unroll
     for (int e = 0; e < 8; ++e) wqr[j][e] = (i < nv) ? wq[i * 8 + e] : 0.f;
   }
-  float score[kMaxRegSources];
+  pdl_wait();
+  if (t >= tokens) return;
+  uint4 x[NSRC][VPL];
+  // Issue every load first (maximum memory-level parallelism), then reduce.
+#pragma unroll
+  for (int s = 0; s < NSRC; ++s) {
+    const uint4* src = (s < nsrc_bank) ? bank + ((int64_t)s * tokens + t) * nv : partial + t * nv;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int i = lane + j * 32;
+      x[s][j] = (i < nv) ? src[i] : make_uint4(0, 0, 0, 0);
+    }
+  }
+  float score[NSRC];
   float mx = -INFINITY;
 #pragma unroll
-  for (int s = 0; s < kMaxRegSources; ++s) {
-    if (s < nsrc) {
+  for (int s = 0; s < NSRC; ++s) {
+    {
       float dot = 0.f, ss = 0.f;
 #pragma unroll
       for (int j = 0; j < VPL; ++j) {
@@ -74,29 +76,24 @@ __global__ void __launch_bounds__(kMixWarps * 32)
   }
   float denom = 0.f;
 #pragma unroll
-  for (int s = 0; s < kMaxRegSources; ++s) {
-    if (s < nsrc) {
-      score[s] = expf(score[s] - mx);
-      denom += score[s];
-    }
+  for (int s = 0; s < NSRC; ++s) {
+    score[s] = expf(score[s] - mx);
+    denom += score[s];
   }
 #pragma unroll
-  for (int s = 0; s < kMaxRegSources; ++s)
-    if (s < nsrc) score[s] = round_bf16(score[s] / denom);
+  for (int s = 0; s < NSRC; ++s) score[s] = round_bf16(score[s] / denom);
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int i = lane + j * 32;
     if (i < nv) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int s = 0; s < kMaxRegSources; ++s) {
-        if (s < nsrc) {
-          const uint32_t p[4] = {x[s][j].x, x[s][j].y, x[s][j].z, x[s][j].w};
+      for (int s = 0; s < NSRC; ++s) {
+        const uint32_t p[4] = {x[s][j].x, x[s][j].y, x[s][j].z, x[s][j].w};
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            acc[2 * q] += score[s] * bf16_lo(p[q]);
-            acc[2 * q + 1] += score[s] * bf16_hi(p[q]);
-          }
+        for (int q = 0; q < 4; ++q) {
+          acc[2 * q] += score[s] * bf16_lo(p[q]);
+          acc[2 * q + 1] += score[s] * bf16_hi(p[q]);
         }
       }
       out[t * nv + i] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
@@ -180,8 +177,21 @@ extern "C" int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t toke
   const int64_t nv = hidden / 8;
   cudaError_t e;
   if (total <= kMaxRegSources && nv <= 3 * 32) {
-    e = launch_pdl(attnres_reg_kernel<3>, grid, dim3(kMixWarps * 32), 0, as_stream(stream), (const uint4*)bank,
-                   (int)sources, tokens, (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out);
+    auto kern = attnres_reg_kernel<3, 1>;
+    switch (total) {
+      case 1: kern = attnres_reg_kernel<3, 1>; break;
+      case 2: kern = attnres_reg_kernel<3, 2>; break;
+      case 3: kern = attnres_reg_kernel<3, 3>; break;
+      case 4: kern = attnres_reg_kernel<3, 4>; break;
+      case 5: kern = attnres_reg_kernel<3, 5>; break;
+      case 6: kern = attnres_reg_kernel<3, 6>; break;
+      case 7: kern = attnres_reg_kernel<3, 7>; break;
+      case 8: kern = attnres_reg_kernel<3, 8>; break;
+      case 9: kern = attnres_reg_kernel<3, 9>; break;
+      default: kern = attnres_reg_kernel<3, 10>; break;
+    }
+    e = launch_pdl(kern, grid, dim3(kMixWarps * 32), 0, as_stream(stream), (const uint4*)bank, (int)sources, tokens,
+                   (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out);
   } else {
     e = launch_pdl(attnres_generic_kernel, grid, dim3(kMixWarps * 32), 0, as_stream(stream), (const uint4*)bank,
                    (int)sources, tokens, (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out);
