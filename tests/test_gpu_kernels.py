@@ -110,7 +110,8 @@ def test_embedding_and_kv_store_bit_exact(cuda_device) -> None:
     assert int(kc.cpu()[untouched].abs().sum()) == 0
 
 
-@pytest.mark.parametrize("sources,tokens,partial", [(8, 8, True), (1, 8, True), (9, 8, False), (4, 33, True), (8, 4096, True)])
+@pytest.mark.parametrize("sources,tokens,partial", [(8, 8, True), (1, 8, True), (9, 8, False), (4, 33, True), (8, 4096, True),
+                                                    (9, 5003, True), (1, 4096, False), (3, 9000, False)])
 def test_attnres_mix_matches_oracle(cuda_device, sources: int, tokens: int, partial: bool) -> None:
     g = torch.Generator().manual_seed(11 + sources + tokens)
     bank = torch.randn(sources, tokens, 768, generator=g).to(torch.bfloat16)
@@ -121,7 +122,17 @@ def test_attnres_mix_matches_oracle(cuda_device, sources: int, tokens: int, part
     )
     fused = oops.attnres_mix_fused(bank, part, wq, 1e-6)
     eager = oops.attnres_mix_eager(bank, part, wq, 1e-6)
-    _bf16_close(out, fused, ulps=1.0, atol=1e-5)
+    # the depth weights are rounded to bf16 (as the reference does); a score that
+    # differs from the oracle's in its last fp32 bits can flip one weight's
+    # rounding, which moves that token's outputs by up to one weight ulp (2^-8)
+    # times the source value: every element within that, and at most 0.1% of the
+    # elements beyond 1 ulp of the output
+    src_max = float(bank.float().abs().max()) if part is None else max(float(bank.float().abs().max()),
+                                                                      float(part.float().abs().max()))
+    _bf16_close(out, fused, ulps=1.0, atol=2.0**-8 * src_max)
+    a, e = out.float().cpu(), fused.float()
+    over = (a - e).abs() > torch.clamp(e.abs(), min=2.0**-126) * 2.0**-7 + 1e-5
+    assert float(over.float().mean()) <= 1e-3, f"{int(over.sum())} of {over.numel()} elements beyond 1 ulp"
     # the parity bar vs the eager (training) semantics: 1e-2 relative
     torch.testing.assert_close(out.float().cpu(), eager.float(), rtol=1e-2, atol=1e-2)
 
