@@ -707,7 +707,10 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
       g.tokens[r] = tok;
     }
   }
-  // ---- last CTA: step epilogue.
+  // ---- last CTA: step epilogue, one lane of warp 0 per row: every flag and
+  // state field is read in one round, the surviving rows' FIFO ranks come from a
+  // ballot (row order, as the reference's allocate of active rows), and each lane
+  // writes its own row's page-table entry and next-forward metadata.
   __syncthreads();
   __shared__ int is_last;
   if (threadIdx.x == 0) {
@@ -716,66 +719,69 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
     is_last = prev == (int)gridDim.x - 1;
   }
   __syncthreads();
-  if (!is_last || threadIdx.x != 0) return;
-  __threadfence();
-  st->arrive = 0;
+  if (!is_last || threadIdx.x >= 32) return;
+  __threadfence();  // the other CTAs' row results are visible to every lane
+  const int lane = threadIdx.x;
+  if (lane == 0) st->arrive = 0;
   if (st->done) return;
   const int R = st->rows;
+  const int64_t head = st->head, tail = st->tail, cap = st->capacity;
+  const int P = st->page_size;
+  const int pos = st->prefix_len + step;  // position of the token sampled now
+  const int64_t row_base = (int64_t)st->row_offset * st->table_stride;
   const bool cancel = g.cancel_flag != nullptr && *reinterpret_cast<volatile const int32_t*>(g.cancel_flag) != 0;
-  int n = 0;
-  for (int i = 0; i < R; ++i) {
-    if (g.active[i] && g.finished[i]) g.active[i] = 0;
-    n += g.active[i] != 0;
-  }
+  const bool mine = lane < R;
+  const bool alive = mine && g.active[lane] != 0 && g.finished[lane] == 0;
+  const unsigned alive_mask = __ballot_sync(0xffffffffu, alive);
+  const int n = __popc(alive_mask);
+  const int rank = __popc(alive_mask & ((1u << lane) - 1u));
   bool done = step + 1 >= S || n == 0 || cancel;
-  if (!done) {
-    const int pos = st->prefix_len + step;  // position of the token sampled now
-    const int P = st->page_size;
-    const bool new_page = P <= 1 || (step % P) == 0;
-    int64_t k = 0;
-    const int64_t need = new_page ? n : 0;
-    if (st->head + need > st->tail) {
-      report(g.status, AIOSB_DEV_POOL_EMPTY);
-      done = true;
+  const bool new_page = P <= 1 || (step % P) == 0;
+  const int64_t need = new_page ? n : 0;
+  if (!done && head + need > tail) {
+    if (lane == 0) report(g.status, AIOSB_DEV_POOL_EMPTY);
+    done = true;
+  }
+  if (!done && alive) {
+    int64_t slot;
+    if (P <= 1) {
+      slot = g.ring[(head + rank) % cap];
     } else {
-      for (int i = 0; i < R; ++i) {
-        if (!g.active[i]) continue;
-        int64_t slot;
-        if (P <= 1) {
-          slot = g.ring[(st->head + k) % st->capacity];
-          ++k;
-        } else {
-          if (new_page) {
-            g.row_page[i] = g.ring[(st->head + k) % st->capacity];
-            ++k;
-          }
-          slot = (int64_t)g.row_page[i] * P + (step % P);
-        }
-        g.page_table[(int64_t)(st->row_offset + i) * st->table_stride + pos] = (int32_t)slot;
-        g.out_loc[i] = (int32_t)slot;
-        g.positions[i] = pos;
-        g.seq_lens[i] = pos + 1;
+      int32_t page;
+      if (new_page) {
+        page = g.ring[(head + rank) % cap];
+        g.row_page[lane] = page;
+      } else {
+        page = g.row_page[lane];
       }
-      st->head += k;
+      slot = (int64_t)page * P + (step % P);
+    }
+    g.page_table[row_base + (int64_t)lane * st->table_stride + pos] = (int32_t)slot;
+    g.out_loc[lane] = (int32_t)slot;
+    g.positions[lane] = pos;
+    g.seq_lens[lane] = pos + 1;
+  }
+  if (mine) g.active[lane] = (!done && alive) ? 1 : 0;
+  if (lane == 0) {
+    if (!done) {
+      st->head = head + need;
       st->active_model_tokens += n;
       st->n_active = n;
       st->step = step + 1;
+    } else {
+      st->done = 1;
+      st->cancelled = cancel ? 1 : 0;
+      st->n_active = 0;
     }
-  }
-  if (done) {
-    st->done = 1;
-    st->cancelled = cancel ? 1 : 0;
-    for (int i = 0; i < R; ++i) g.active[i] = 0;
-    st->n_active = 0;
-  }
-  if (g.host_mirror != nullptr) {
-    volatile int32_t* m = g.host_mirror;
-    m[1] = st->done;
-    m[2] = st->cancelled;
-    m[3] = st->n_active;
-    __threadfence_system();
-    m[0] = step + 1;  // steps sampled so far; written last
-    __threadfence_system();
+    if (g.host_mirror != nullptr) {
+      volatile int32_t* m = g.host_mirror;
+      m[1] = done ? 1 : 0;
+      m[2] = (done && cancel) ? 1 : 0;
+      m[3] = done ? 0 : n;
+      __threadfence_system();
+      m[0] = step + 1;  // steps sampled so far; written last
+      __threadfence_system();
+    }
   }
 }
 
@@ -948,6 +954,7 @@ extern "C" int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t
   AIOSB_REQUIRE(rows >= 1 && vocab > 0 && vocab <= kMaxVocab, AIOSB_ERR_INVALID_ARG,
                 "group_step: rows >= 1 and vocab in [1, %d]", kMaxVocab);
   AIOSB_REQUIRE(top_k_max <= kMaxSortK, AIOSB_ERR_UNSUPPORTED, "group_step: top_k above %d", kMaxSortK);
+  AIOSB_REQUIRE(rows <= 32, AIOSB_ERR_UNSUPPORTED, "group_step: at most 32 rows per group");
   cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem(kMaxVocab));
   cudaError_t e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads), sample_smem((int)vocab),
                              as_stream(stream), *g);

@@ -230,17 +230,21 @@ def soft_penalty(text: str) -> float:
     return penalty
 
 
-def ngram_similarity(left: str, right: str, width: int = 2) -> float:
-    def grams(text: str) -> set[str]:
-        compact = candidate_key(text)
-        if len(compact) < width:
-            return {compact} if compact else set()
-        return {compact[i : i + width] for i in range(len(compact) - width + 1)}
+def _grams(text: str, width: int = 2) -> set[str]:
+    compact = candidate_key(text)
+    if len(compact) < width:
+        return {compact} if compact else set()
+    return {compact[i : i + width] for i in range(len(compact) - width + 1)}
 
-    a, b = grams(left), grams(right)
+
+def _jaccard(a: set[str], b: set[str]) -> float:
     if not a or not b:
         return 0.0
     return len(a & b) / len(a | b)
+
+
+def ngram_similarity(left: str, right: str, width: int = 2) -> float:
+    return _jaccard(_grams(left, width), _grams(right, width))
 
 
 def _valid(candidate: ImeCandidate) -> bool:
@@ -260,15 +264,20 @@ def select_top_candidates(candidates: list[ImeCandidate], count: int, diversity_
             best[key] = cand
     pool = list(best.values())
     chosen: list[ImeCandidate] = []
+    # bigram sets computed once per candidate; each pool entry keeps its running
+    # maximum similarity to the chosen ones, updated against the newest pick only
+    grams = {id(c): _grams(c.text) for c in pool}
+    max_sim = {id(c): 0.0 for c in pool}
 
     def mmr(cand: ImeCandidate) -> float:
-        sim = max((ngram_similarity(cand.text, c.text) for c in chosen), default=0.0)
-        return cand.base_score - diversity_lambda * sim
+        return cand.base_score - diversity_lambda * max_sim[id(cand)]
 
     while pool and len(chosen) < count:
         pick = max(pool, key=mmr)
         score = mmr(pick)
         pool.remove(pick)
+        for c in pool:
+            max_sim[id(c)] = max(max_sim[id(c)], _jaccard(grams[id(c)], grams[id(pick)]))
         chosen.append(ImeCandidate(
             text=pick.text, token_count=pick.token_count, average_logprob=pick.average_logprob,
             base_score=pick.base_score, selection_score=score, stop_reason=pick.stop_reason,

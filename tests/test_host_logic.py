@@ -163,3 +163,39 @@ def test_product_kernels_refuse_cpu_tensors() -> None:
         ops.linear(torch.zeros(2, 64, dtype=torch.bfloat16), torch.zeros(128, 64, dtype=torch.bfloat16))
     with pytest.raises(ValueError, match="CUDA"):
         ops.rmsnorm(torch.zeros(2, 8), torch.ones(8), 1e-6)
+
+
+def test_mmr_selection_matches_direct_restatement() -> None:
+    """The incremental MMR (cached bigram sets, running maximum similarity) picks
+    exactly what the direct form picks: for every round, the first pool entry
+    maximising base_score - lambda * max similarity to the chosen ones."""
+    import random
+
+    from aios_b200.ime_text import ngram_similarity as sim
+
+    rng = random.Random(7)
+    alphabet = "我你他的是了在有一个不这人们来到上大为和国地以中要会"
+    for trial in range(200):
+        items = []
+        for i in range(rng.randint(1, 24)):
+            text = "".join(rng.choice(alphabet) for _ in range(rng.randint(2, 7)))
+            score = rng.choice([rng.uniform(-3, 0), -1.5, -2.0])  # repeated scores exercise ties
+            items.append(ImeCandidate(text=text, token_count=len(text), average_logprob=score, base_score=score,
+                                      selection_score=score, stop_reason="eos", invalid_reasons=()))
+        lam = rng.choice([0.0, 0.35, 0.8, 2.0])
+        count = rng.randint(1, 5)
+        got = [(c.text, c.selection_score) for c in select_top_candidates(items, count=count, diversity_lambda=lam)]
+        best = {}
+        for c in items:
+            key = candidate_key(c.text)
+            if key not in best or c.base_score > best[key].base_score:
+                best[key] = c
+        pool, chosen, scores = list(best.values()), [], []
+        while pool and len(chosen) < count:
+            def mmr(c):
+                return c.base_score - lam * max((sim(c.text, x.text) for x in chosen), default=0.0)
+            pick = max(pool, key=mmr)
+            scores.append(mmr(pick))
+            chosen.append(pick)
+            pool.remove(pick)
+        assert got == [(c.text, s) for c, s in zip(chosen, scores)], trial
