@@ -159,6 +159,7 @@ _SIGNATURES = {
     "aiosb_slot_free_range": ([_p, _i64, _i64, _i64, _i64, _p], _i32),
     "aiosb_group_begin": ([ctypes.POINTER(GroupPtrs), _p, _u64, _i64, _i64, _p], _i32),
     "aiosb_group_step": ([ctypes.POINTER(GroupPtrs), _i64, _i64, _i64, _p], _i32),
+    "aiosb_group_step_static": ([ctypes.POINTER(GroupPtrs), _i64, _i64, _i64, _p], _i32),
 }
 
 EXPORTED = tuple(_SIGNATURES)

@@ -18,6 +18,7 @@
 // torch's CPU cumsum does for float tensors. Equal logits are ordered by
 // ascending token id; torch.topk leaves that order unspecified.
 #include <algorithm>
+#include <mutex>
 
 #include "abi_util.h"
 #include "common.cuh"
@@ -1028,4 +1029,64 @@ extern "C" int aiosb_slot_free_range(int32_t* ring, int64_t capacity, int64_t be
   AIOSB_REQUIRE(ring, AIOSB_ERR_INVALID_ARG, "slot_free_range: null pointer");
   slot_free_range_kernel<<<1, 1024, 0, as_stream(stream)>>>(ring, capacity, begin, n, tail);
   return check_launch("slot_free_range");
+}
+
+// ---- CandidateGroup step for callers that cannot allocate device memory -----
+// aiosb_group_step hands each row's finish flag from the row's sampling CTA to
+// the epilogue CTA through g->finished, a [rows] int32 array the caller
+// allocates. This variant keeps those flags in a fixed array of the library
+// instead. The array is part of the library image: every GPU that loads the
+// library holds it until the process exits, and all calls share it.
+constexpr int kStaticStepRows = 32;  // rows one call may step (the group limit)
+static __device__ __align__(256) int32_t g_static_step_finished[kStaticStepRows];
+
+namespace {
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_step_mu;
+void* g_static_step_addr[kStaticMaxDevices];  // device address per device ordinal
+
+// Device address of g_static_step_finished on the current device. The host-side
+// name of a __device__ array is only a stand-in, so the address is looked up
+// once per device (with that device current) and cached.
+int static_step_scratch(int32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step_static: cudaGetDevice: %s", cudaGetErrorString(e));
+  AIOSB_REQUIRE(dev >= 0 && dev < kStaticMaxDevices, AIOSB_ERR_UNSUPPORTED,
+                "group_step_static: device ordinal %d above %d", dev, kStaticMaxDevices - 1);
+  std::lock_guard<std::mutex> lock(g_static_step_mu);
+  if (g_static_step_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_step_finished);
+    if (e != cudaSuccess || p == nullptr)
+      return set_error(AIOSB_ERR_LAUNCH, "group_step_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_static_step_addr[dev] = p;
+  }
+  *out = static_cast<int32_t*>(g_static_step_addr[dev]);
+  return AIOSB_OK;
+}
+}  // namespace
+
+extern "C" int aiosb_group_step_static(const aiosb_group_ptrs* g, int64_t rows, int64_t vocab, int64_t top_k_max,
+                                       void* stream) {
+  AIOSB_REQUIRE(g && g->state, AIOSB_ERR_INVALID_ARG, "group_step_static: null pointer");
+  AIOSB_REQUIRE(rows >= 1 && vocab > 0 && vocab <= kMaxVocab, AIOSB_ERR_INVALID_ARG,
+                "group_step_static: rows >= 1 and vocab in [1, %d]", kMaxVocab);
+  AIOSB_REQUIRE(top_k_max <= kMaxSortK, AIOSB_ERR_UNSUPPORTED, "group_step_static: top_k above %d", kMaxSortK);
+  AIOSB_REQUIRE(rows <= kStaticStepRows, AIOSB_ERR_UNSUPPORTED,
+                "group_step_static: %lld rows exceed the %d-row static scratch", (long long)rows, kStaticStepRows);
+  int32_t* finished = nullptr;
+  const int rc = static_step_scratch(&finished);
+  if (rc != AIOSB_OK) return rc;
+  // The array keeps the previous call's flags; start every call from zeros, as
+  // aiosb_group_begin leaves a caller's g->finished.
+  cudaError_t e = cudaMemsetAsync(finished, 0, kStaticStepRows * sizeof(int32_t), as_stream(stream));
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step_static: memset: %s", cudaGetErrorString(e));
+  aiosb_group_ptrs local = *g;
+  local.finished = finished;
+  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem(kMaxVocab));
+  e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads), sample_smem((int)vocab),
+                 as_stream(stream), local);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step_static: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
 }

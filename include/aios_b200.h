@@ -355,6 +355,30 @@ AIOSB_API int aiosb_group_begin(const aiosb_group_ptrs* g, const void* prefix_lo
  * memory, so one captured launch serves every step of every round. */
 AIOSB_API int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t vocab, int64_t top_k_max, void* stream);
 
+/* aiosb_group_step without the caller's scratch array. No counterpart in the
+ * reference: it is an addition for callers that cannot call cudaMalloc, such as
+ * a plugin inside a host process that owns all device memory through its own
+ * allocator (a caching pool that has reserved the free HBM, or a fixed budget
+ * handed out up front) and gives the plugin only the buffers it needs, so a
+ * cudaMalloc of the plugin's own fails or escapes the host's accounting; and a
+ * per-keystroke path where a cudaMalloc / cudaFree pair would synchronise the
+ * device in the middle of a keystroke.
+ * Same arguments, results and errors as aiosb_group_step, except that
+ * g->finished is neither read nor written (it may be NULL here): the per-row
+ * finish flags go through a 32-entry int32 array inside the library, so rows
+ * above 32 are rejected with AIOSB_ERR_UNSUPPORTED. aiosb_group_begin still
+ * zeroes g->finished at round start; a caller without that array may point it
+ * at g->stop_codes, which group_begin zeroes as well.
+ * The call allocates and frees nothing. Its first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress, on the current device) and
+ * should come before any stream capture. Each call clears the array with an
+ * asynchronous memset on `stream` before the step kernel. Every GPU that loads
+ * the library holds the array until the process exits, and all calls on a device
+ * share it: calls that overlap on the GPU (two groups stepping on different
+ * streams at once) race on it. */
+AIOSB_API int aiosb_group_step_static(const aiosb_group_ptrs* g, int64_t rows, int64_t vocab, int64_t top_k_max,
+                                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif
