@@ -229,6 +229,7 @@ class ImeCompletionEngine:
         active_model_tokens = len(token_ids) - reused
         refill_rounds = 0
         refill_stop_reason = "max_attempts"
+        selected: list[ImeCandidate] = []
         while actual_attempts < max_attempts:
             if actual_attempts == 0:
                 attempts = config.sampling_attempts
@@ -270,7 +271,8 @@ class ImeCompletionEngine:
         ended.record()
         ended.synchronize()
         gpu_latency_ms = started.elapsed_time(ended)
-        selected = select_top_candidates(raw_candidates, config.display_candidates, config.diversity_lambda)
+        # `selected` was computed after the last round was added (the loop only
+        # leaves before adding a round when the refill deadline or budget ends it)
         stats = candidate_pool_stats(raw_candidates)
         if (
             refill_stop_reason == "max_attempts"

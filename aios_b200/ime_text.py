@@ -17,6 +17,8 @@ from typing import Any
 ASSISTANT_PATTERN = re.compile(r"以下是|首先|其次|综上所述|作为(?:一个)?AI|我是AI|我来回答")
 REPEAT_PATTERN = re.compile(r"(.)\1{3,}")
 TERMINAL_TEXT_PATTERN = re.compile(r"[。！？!?；;]")
+WHITESPACE_PATTERN = re.compile(r"\s+")
+REDUPLICATION_PATTERN = re.compile(r"([\u3400-\u9fff])\1")
 FUNCTION_WORD_ENDINGS = (
     "的", "地", "得", "和", "与", "或", "但", "而", "在", "把", "被", "给",
     "对", "从", "向", "为", "再", "就", "会", "能", "如果", "因为", "所以",
@@ -170,7 +172,7 @@ def token_longest_common_prefix(left: list[int], right: list[int]) -> int:
 
 
 def normalize_candidate(text: str) -> str:
-    return re.sub(r"\s+", "", text.replace("\ufffd", "")).strip()
+    return WHITESPACE_PATTERN.sub("", text.replace("\ufffd", "")).strip()
 
 
 def truncate_at_terminal(text: str) -> tuple[str, bool]:
@@ -186,7 +188,10 @@ def candidate_key(text: str) -> str:
 
 
 def repeated_ngram(text: str) -> bool:
-    compact = normalize_candidate(text)
+    return _repeated_ngram_compact(normalize_candidate(text))
+
+
+def _repeated_ngram_compact(compact: str) -> bool:
     if REPEAT_PATTERN.search(compact):
         return True
     for width in (2, 3, 4):
@@ -208,7 +213,7 @@ def invalid_reasons(text: str, config: ImeGenerationConfig, prefix: str = "") ->
         reasons.append("too_long")
     if ASSISTANT_PATTERN.search(compact):
         reasons.append("assistant_template")
-    if repeated_ngram(compact):
+    if _repeated_ngram_compact(compact):
         reasons.append("repeated_ngram")
     if compact.rstrip(DISPLAY_PUNCTUATION).endswith(FUNCTION_WORD_ENDINGS):
         reasons.append("unfinished_fragment")
@@ -222,7 +227,7 @@ def invalid_reasons(text: str, config: ImeGenerationConfig, prefix: str = "") ->
 def soft_penalty(text: str) -> float:
     compact = normalize_candidate(text)
     penalty = 0.0
-    for match in re.finditer(r"([\u3400-\u9fff])\1", compact):
+    for match in REDUPLICATION_PATTERN.finditer(compact):
         if match.group(0) not in NATURAL_REDUPLICATIONS:
             penalty += 0.45
     if len(compact) <= 3:
