@@ -19,9 +19,86 @@ constexpr int kMixWarps = 4;
 constexpr int kMaxRegSources = 10;  // register-resident path: bank(<=9) + partial
 constexpr int kMaxSources = 16;
 
-// NSRC sources (bank sources, then the partial when present) known at compile
-// time: every loop is fixed-length, so the 2 * NSRC warp reductions of the
-// scores run interleaved instead of as NSRC dependent shuffle chains.
+// Score, depth softmax and weighted sum of one token whose NSRC source rows
+// (bank sources, then the partial when present) are read through `rows`: lane l
+// takes the 16-byte chunks l, l + 32, ... of every row, and wqr the same chunks
+// of the weighted query. NSRC is known at compile time, so every loop is
+// fixed-length and the 2 * NSRC warp reductions of the scores run interleaved
+// instead of as NSRC dependent shuffle chains. rows(s, j) returns chunk
+// lane + 32 j of source s; rows.between_phases() runs between the score pass and
+// the weighted-sum pass.
+template <int VPL, int NSRC, class Rows>
+__device__ __forceinline__ void mix_token(const Rows& rows, const float (&wqr)[VPL][8], int nv, int hidden,
+                                          float eps, int lane, uint4* __restrict__ out_row) {
+  float score[NSRC];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int s = 0; s < NSRC; ++s) {
+    float dot = 0.f, ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const uint4 u = rows(s, j);
+      const uint32_t p[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float a = bf16_lo(p[q]), b = bf16_hi(p[q]);
+        dot += a * wqr[j][2 * q] + b * wqr[j][2 * q + 1];
+        ss += a * a + b * b;
+      }
+    }
+    dot = warp_sum(dot);
+    ss = warp_sum(ss);
+    score[s] = dot * (1.0f / sqrtf(ss / (float)hidden + eps));
+    mx = fmaxf(mx, score[s]);
+  }
+  float denom = 0.f;
+#pragma unroll
+  for (int s = 0; s < NSRC; ++s) {
+    score[s] = expf(score[s] - mx);
+    denom += score[s];
+  }
+#pragma unroll
+  for (int s = 0; s < NSRC; ++s) score[s] = round_bf16(score[s] / denom);
+  rows.between_phases();
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int i = lane + j * 32;
+    if (i < nv) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < NSRC; ++s) {
+        const uint4 u = rows(s, j);
+        const uint32_t p[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[2 * q] += score[s] * bf16_lo(p[q]);
+          acc[2 * q + 1] += score[s] * bf16_hi(p[q]);
+        }
+      }
+      out_row[i] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                              pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+    }
+  }
+}
+
+// Source rows already in registers. between_phases() marks them as rewritten,
+// so the compiler converts them to fp32 again in the second pass instead of
+// keeping 8 fp32 values per chunk live across the softmax (which spilled).
+template <int VPL, int NSRC>
+struct RegRows {
+  uint4 (&x)[NSRC][VPL];
+  __device__ __forceinline__ uint4 operator()(int s, int j) const { return x[s][j]; }
+  __device__ __forceinline__ void between_phases() const {
+#pragma unroll
+    for (int s = 0; s < NSRC; ++s)
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        asm volatile("" : "+r"(x[s][j].x), "+r"(x[s][j].y), "+r"(x[s][j].z), "+r"(x[s][j].w));
+  }
+};
+
+// One warp per token, every source row loaded straight into registers. The
+// weighted query, a model constant, is loaded before the wait on the producer.
 template <int VPL, int NSRC>
 __global__ void __launch_bounds__(kMixWarps * 32, 3)
     attnres_reg_kernel(const uint4* __restrict__ bank, int nsrc_bank, int64_t tokens, int hidden,
@@ -31,7 +108,6 @@ __global__ void __launch_bounds__(kMixWarps * 32, 3)
   const int64_t t = (int64_t)blockIdx.x * kMixWarps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   const int nv = hidden / 8;
-  // the weighted query is a model constant: loaded before waiting on the producer
   float wqr[VPL][8];
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
@@ -52,54 +128,7 @@ __global__ void __launch_bounds__(kMixWarps * 32, 3)
       x[s][j] = (i < nv) ? src[i] : make_uint4(0, 0, 0, 0);
     }
   }
-  float score[NSRC];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int s = 0; s < NSRC; ++s) {
-    {
-      float dot = 0.f, ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < VPL; ++j) {
-        const uint32_t p[4] = {x[s][j].x, x[s][j].y, x[s][j].z, x[s][j].w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float a = bf16_lo(p[q]), b = bf16_hi(p[q]);
-          dot += a * wqr[j][2 * q] + b * wqr[j][2 * q + 1];
-          ss += a * a + b * b;
-        }
-      }
-      dot = warp_sum(dot);
-      ss = warp_sum(ss);
-      score[s] = dot * (1.0f / sqrtf(ss / (float)hidden + eps));
-      mx = fmaxf(mx, score[s]);
-    }
-  }
-  float denom = 0.f;
-#pragma unroll
-  for (int s = 0; s < NSRC; ++s) {
-    score[s] = expf(score[s] - mx);
-    denom += score[s];
-  }
-#pragma unroll
-  for (int s = 0; s < NSRC; ++s) score[s] = round_bf16(score[s] / denom);
-#pragma unroll
-  for (int j = 0; j < VPL; ++j) {
-    const int i = lane + j * 32;
-    if (i < nv) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int s = 0; s < NSRC; ++s) {
-        const uint32_t p[4] = {x[s][j].x, x[s][j].y, x[s][j].z, x[s][j].w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          acc[2 * q] += score[s] * bf16_lo(p[q]);
-          acc[2 * q + 1] += score[s] * bf16_hi(p[q]);
-        }
-      }
-      out[t * nv + i] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                                   pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
-    }
-  }
+  mix_token<VPL, NSRC>(RegRows<VPL, NSRC>{x}, wqr, nv, hidden, eps, lane, out + t * nv);
 }
 
 // Any hidden size / up to 16 sources: two passes over the sources (scores, then

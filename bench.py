@@ -294,8 +294,88 @@ def mixer_chain(dev) -> dict:
     e.synchronize()
     big_ms = s.elapsed_time(e) / 20
     big_bytes = 9 * n * 768 * 2 + n * 768 * 2 + 768 * 4
+    del big, bp, bo
+    # bandwidth sweep over token counts: 8 bank sources + the partial, [N, 768]
+    sweep = {}
+    for n in (8, 64, 512, 4096, 32768, 131072):
+        sb = torch.randn(8, n, 768, generator=g, device=dev).to(torch.bfloat16)
+        sp = torch.randn(n, 768, generator=g, device=dev).to(torch.bfloat16)
+        so = torch.empty(n, 768, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            ops.b200_attnres_mix(sb, sp, wq[0], 1e-6, output_buffer=so)
+        iters = 20 if n >= 4096 else 100
+        torch.cuda.synchronize(dev)
+        s.record()
+        for _ in range(iters):
+            ops.b200_attnres_mix(sb, sp, wq[0], 1e-6, output_buffer=so)
+        e.record()
+        e.synchronize()
+        us = s.elapsed_time(e) / iters * 1e3
+        sweep[str(n)] = {"us": round(us, 2), "gbs": round((10 * n * 768 * 2 + 768 * 4) / (us * 1e-6) / 1e9, 1)}
+        del sb, sp, so
     return {"chain65_us": round(chain_us, 2), "chain65_gbs": round(chain_bytes / (chain_us * 1e-6) / 1e9, 1),
-            "n32768_gbs": round(big_bytes / (big_ms * 1e-3) / 1e9, 1)}
+            "n32768_gbs": round(big_bytes / (big_ms * 1e-3) / 1e9, 1), "sweep_9src": sweep}
+
+
+def stream_texts(tokenizer, vocab: int, seed: int, keystrokes: int = 40) -> tuple[list[str], int]:
+    """a seeded typing stream. Every keystroke appends 1-2
+    random tokens to the previous prefix, except 10% backspaces that drop the
+    last token (which the engine answers with a full re-prefill)."""
+    import random
+
+    rng = random.Random(seed)
+    ids = [rng.randint(10, vocab - 1) for _ in range(2)]
+    texts, backspaces = [], 0
+    for _ in range(keystrokes):
+        if rng.random() < 0.1 and len(ids) > 1:
+            ids = ids[:-1]
+            backspaces += 1
+        else:
+            ids = ids + [rng.randint(10, vocab - 1) for _ in range(rng.randint(1, 2))]
+        texts.append(tokenizer.text_for(ids))
+    return texts, backspaces
+
+
+def keystroke_stream(engine, llm, seed: int) -> dict:
+    """Config 5 on one GPU, through ``complete``: the 40-keystroke stream with
+    token-LCP reuse of the prefix KV, run once to warm the prefill graphs and
+    once timed (keystrokes in sequence, as with a 30-150 ms think time); then the
+    forced-overlap variant, where every next keystroke arrives 2 ms after the
+    previous one started, so latest-wins cancels the group in flight."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    cfg = keystroke_config()
+    texts, backspaces = stream_texts(llm.tokenizer, llm.config.vocab_size, seed)
+    out = {"keystrokes": len(texts), "backspaces": backspaces}
+    for _ in range(2):
+        engine.reset_prefix_cache()
+        res = [engine.complete(t, cfg) for t in texts]
+    lat = [r.latency_ms for r in res]
+    out.update(p50_ms=round(statistics.median(lat), 3), p95_ms=round(percentile(lat, 0.95), 3),
+               gpu_p50_ms=round(statistics.median([r.gpu_latency_ms for r in res]), 3),
+               reused_prefix_tokens=sum(r.reused_prefix_tokens for r in res))
+    engine.reset_prefix_cache()
+    device = llm.device
+
+    def complete_on_device(text, token):
+        torch.cuda.set_device(device)
+        return engine.complete(text, cfg, token)
+
+    with ThreadPoolExecutor(max_workers=4) as pool:
+        futures = []
+        for t in texts:
+            token = engine.new_generation()  # cancels the keystroke in flight
+            futures.append((time.perf_counter(), pool.submit(complete_on_device, t, token)))
+            time.sleep(0.002)
+        done = []
+        for t0, fut in futures:
+            r = fut.result()
+            done.append((r, (time.perf_counter() - t0) * 1e3))
+    final = done[-1]
+    out["overlap"] = {"arrival_gap_ms": 2.0, "cancelled": sum(r.cancelled for r, _ in done),
+                      "completed": sum(not r.cancelled for r, _ in done),
+                      "last_keystroke_ms": round(final[1], 3), "last_cancelled": final[0].cancelled}
+    return out
 
 
 def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
@@ -350,6 +430,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     peaks = measured_peaks()
     roof = None if args.no_extras else decode_linear_roofline(llm, peaks)
     mixer = None if args.no_extras else mixer_chain(dev)
+    kstream = None if args.no_extras else keystroke_stream(engine, llm, seed=4321 + rank)
     lat = [r.latency_ms for r in results]
     gpu_lat = [r.gpu_latency_ms for r in results]
     gen = sum(r.generated_tokens for r in results)
@@ -377,6 +458,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "decode_tok_s": round(world * gen / (device_ms * 1e-3), 1),
         "active_model_tok_s": round(active / (sum(gpu_lat) * 1e-3), 1),
         "mixer": mixer,
+        "stream": kstream,
         "e2e": {"value": round(world * args.steps / wall, 3), "unit": "keystrokes/s",
                 "h2d_bytes_per_step": int(round(h2d)), "d2h_bytes_per_step": int(round(d2h))},
         "gpu_launches": launches,
