@@ -137,6 +137,25 @@ def test_attnres_mix_matches_oracle(cuda_device, sources: int, tokens: int, part
     torch.testing.assert_close(out.float().cpu(), eager.float(), rtol=1e-2, atol=1e-2)
 
 
+@pytest.mark.parametrize("sources,partial", [(1, False), (1, True), (5, True), (8, True), (9, False), (9, True)])
+def test_attnres_stream_kernel_matches_register_kernel(cuda_device, sources: int, partial: bool) -> None:
+    """From 2048 tokens the mixer streams tiles through shared memory; its
+    outputs equal the small-count register kernel's bit for bit (the same
+    arithmetic), checked on windows of 8 tokens mixed on their own."""
+    tokens = 4099  # not a multiple of the 4-token tile
+    g = torch.Generator().manual_seed(5 + sources)
+    bank = torch.randn(sources, tokens, 768, generator=g).to(torch.bfloat16).to(cuda_device)
+    part = torch.randn(tokens, 768, generator=g).to(torch.bfloat16).to(cuda_device) if partial else None
+    wq = (torch.randn(768, generator=g) * 0.02).to(cuda_device)
+    out = ops.b200_attnres_mix(bank, part, wq, 1e-6)
+    for start in (0, 4, 1000, 2047, 4091):
+        win = slice(start, start + 8)
+        small = ops.b200_attnres_mix(bank[:, win].contiguous(), None if part is None else part[win].contiguous(),
+                                     wq, 1e-6)
+        assert torch.equal(out[win], small), f"window at {start}"
+    assert not torch.isnan(out.float()).any()
+
+
 def test_attnres_mix_rejects_bad_layout(cuda_device) -> None:
     bank = torch.zeros(2, 3, 768, dtype=torch.bfloat16, device=cuda_device)
     wq = torch.zeros(768, device=cuda_device)
