@@ -277,6 +277,233 @@ int launch(const GemvArgs& a, cudaStream_t stream) {
   return AIOSB_OK;
 }
 
+// ---- register-operand tensor-core GEMV (mma.sync m16n8k16, bf16 -> fp32) ----
+// A CTA computes one 16-row weight tile (16 output features; SwiGLU: 8 gate + 8
+// up rows of 8 output features) for up to NT * 8 token rows. Its 8 warps split
+// K; warp w owns the 32-wide K blocks [w * kb, (w + 1) * kb). Within a block the
+// K order is permuted per lane so that every fragment is one 16-byte load: lane
+// (g = lane / 4, t = lane % 4) takes physical elements [32 b + 8 t, 32 b + 8 t + 8)
+// of weight rows g and g + 8 (A) and of token row g (B), and feeds them as the
+// logical K positions {2t, 2t+1, 2t+8, 2t+9} of two consecutive k16 MMAs. A dot
+// product is invariant under a permutation of K applied to both operands, so no
+// shuffle or shared-memory staging is needed: the weights go to registers before
+// griddepcontrol.wait, the activations straight from global memory after it.
+// Partial tiles of the 8 warps are summed in warp order through shared memory.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int NT, int KB, bool STAT>
+__global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a) {
+  constexpr int TM = NT * 8;  // token rows covered
+  __shared__ float red[kGemvFeat][NT][32][4];  // [warp][n tile][lane][fragment]
+  __shared__ float tile[TM][17];               // reduced [token][row] (padded)
+  __shared__ float ssw[kGemvFeat][TM];          // statistics mode: per-warp sums of squares
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int K = (int)a.k;
+  const int kb = K / 256;  // 32-wide blocks per warp
+  const int T = a.rows;
+  const bool silu = a.epilogue == AIOSB_EPI_SILU_MUL;
+  const int feat_per_tile = silu ? 8 : 16;
+  const int ntiles = (int)(a.n_out / feat_per_tile);
+  const int64_t kbase = (int64_t)warp * kb * 32 + 8 * t4;  // this lane's first element, block 0
+
+  // weight rows of tile `tl` held by this lane (rows g and g + 8 of the M tile)
+  auto load_w = [&](int tl, uint4 (&wa)[KB], uint4 (&wb)[KB]) {
+    int64_t r0, r1;
+    if (silu) {  // packed [g0..63 | u0..63 | g64..]: gate and up rows of feature f
+      const int64_t f = (int64_t)tl * 8 + g;
+      r0 = (f / 64) * 128 + (f % 64);
+      r1 = r0 + 64;
+    } else {
+      r0 = (int64_t)tl * 16 + g;
+      r1 = r0 + 8;
+    }
+#pragma unroll
+    for (int b = 0; b < KB; ++b) {
+      const bool ok = tl < ntiles && b < kb;
+      wa[b] = ok ? *reinterpret_cast<const uint4*>(a.w + r0 * K + kbase + b * 32) : make_uint4(0u, 0u, 0u, 0u);
+      wb[b] = ok ? *reinterpret_cast<const uint4*>(a.w + r1 * K + kbase + b * 32) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  uint4 wa[KB], wb[KB];
+  load_w(blockIdx.x, wa, wb);
+  uint4 nwv[KB];
+  if (STAT) {
+#pragma unroll
+    for (int b = 0; b < KB; ++b)
+      nwv[b] = b < kb ? *reinterpret_cast<const uint4*>(a.nw + kbase + b * 32) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+
+  // ---- B fragments: token row n = nt * 8 + g, this lane's 8 elements per block
+  uint4 xb[NT][KB];
+  if (!STAT) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int n = nt * 8 + g;
+#pragma unroll
+      for (int b = 0; b < KB; ++b)
+        xb[nt][b] = (n < T && b < kb) ? *reinterpret_cast<const uint4*>(a.x + (int64_t)n * a.x_stride + kbase + b * 32)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+    }
+  } else {
+    // rows normalised from the fp32 residual stream s (RMSNormFused,
+    // aios/layers/norm.py:34-40): the sum of squares of a whole row is reduced
+    // over the 4 lanes of a row and the 8 warps (in warp order)
+    float4 sv[NT][KB][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int n = nt * 8 + g;
+#pragma unroll
+      for (int b = 0; b < KB; ++b) {
+        const bool ok = n < T && b < kb;
+        const float4* src = reinterpret_cast<const float4*>(a.stat_x + (int64_t)n * K + kbase + b * 32);
+        sv[nt][b][0] = ok ? src[0] : make_float4(0.f, 0.f, 0.f, 0.f);
+        sv[nt][b][1] = ok ? src[1] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float ss = 0.f;
+#pragma unroll
+      for (int b = 0; b < KB; ++b)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          ss += sv[nt][b][h].x * sv[nt][b][h].x + sv[nt][b][h].y * sv[nt][b][h].y +
+                sv[nt][b][h].z * sv[nt][b][h].z + sv[nt][b][h].w * sv[nt][b][h].w;
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      if (t4 == 0) ssw[warp][nt * 8 + g] = ss;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float ss = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGemvFeat; ++w) ss += ssw[w][nt * 8 + g];
+      const float rcp = 1.0f / sqrtf(ss / (float)K + a.eps);
+#pragma unroll
+      for (int b = 0; b < KB; ++b) {
+        const uint32_t p[4] = {nwv[b].x, nwv[b].y, nwv[b].z, nwv[b].w};
+        const float4 s0 = sv[nt][b][0], s1 = sv[nt][b][1];
+        xb[nt][b] = make_uint4(
+            pack_bf16x2(s0.x * rcp * bf16_lo(p[0]), s0.y * rcp * bf16_hi(p[0])),
+            pack_bf16x2(s0.z * rcp * bf16_lo(p[1]), s0.w * rcp * bf16_hi(p[1])),
+            pack_bf16x2(s1.x * rcp * bf16_lo(p[2]), s1.y * rcp * bf16_hi(p[2])),
+            pack_bf16x2(s1.z * rcp * bf16_lo(p[3]), s1.w * rcp * bf16_hi(p[3])));
+      }
+    }
+  }
+
+  for (int tl = blockIdx.x; tl < ntiles; tl += gridDim.x) {
+    uint4 na[KB], nb[KB];
+    load_w(tl + gridDim.x, na, nb);  // next tile, in flight during this one
+    float d[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) d[nt][0] = d[nt][1] = d[nt][2] = d[nt][3] = 0.f;
+#pragma unroll
+    for (int b = 0; b < KB; ++b) {
+      if (b < kb) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_bf16_16816(d[nt], wa[b].x, wb[b].x, wa[b].y, wb[b].y, xb[nt][b].x, xb[nt][b].y);
+          mma_bf16_16816(d[nt], wa[b].z, wb[b].z, wa[b].w, wb[b].w, xb[nt][b].z, xb[nt][b].w);
+        }
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      *reinterpret_cast<float4*>(&red[warp][nt][lane][0]) = make_float4(d[nt][0], d[nt][1], d[nt][2], d[nt][3]);
+    __syncthreads();
+    // sum the 8 warps' partial tiles in warp order; element (row, token) of the
+    // fragment layout: row = lane / 4 + 8 (j / 2), token = nt * 8 + 2 (lane % 4) + j % 2
+    for (int i = tid; i < NT * 128; i += kGemvThreads) {
+      const int nt = i / 128, l = (i / 4) % 32, j = i % 4;
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGemvFeat; ++w) sum += red[w][nt][l][j];
+      tile[nt * 8 + 2 * (l & 3) + (j & 1)][(l >> 2) + 8 * (j >> 1)] = sum;
+    }
+    __syncthreads();
+    // ---- epilogue: thread (token, half) writes 8 features (16 bytes)
+    if (tid < TM * 2) {
+      const int tk = tid >> 1, h = tid & 1;
+      if (tk < T && (!silu || h == 0)) {
+        float o[8];
+        int64_t f0;
+        if (silu) {
+          f0 = (int64_t)tl * 8;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            // gate_up output is bf16 before silu_and_mul (aios/models/qwen3.py:90-92)
+            const float gt = round_bf16(tile[tk][j]), up = round_bf16(tile[tk][8 + j]);
+            o[j] = gt / (1.0f + expf(-gt)) * up;
+          }
+        } else {
+          f0 = (int64_t)tl * 16 + 8 * h;
+          if (a.epilogue == AIOSB_EPI_ADD) {
+            const uint4 rv = *reinterpret_cast<const uint4*>(a.residual + (int64_t)tk * a.residual_stride + f0);
+            const uint32_t p[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float res = (j & 1) ? bf16_hi(p[j >> 1]) : bf16_lo(p[j >> 1]);
+              o[j] = res + round_bf16(tile[tk][8 * h + j]);
+            }
+            if (a.out_stat_x != nullptr) {
+              float4* sx = reinterpret_cast<float4*>(a.out_stat_x + (int64_t)tk * a.n_out + f0);
+              sx[0] = make_float4(o[0], o[1], o[2], o[3]);
+              sx[1] = make_float4(o[4], o[5], o[6], o[7]);
+              float ss = 0.f;
+#pragma unroll
+              for (int j = 0; j < 8; ++j) ss += o[j] * o[j];
+              a.out_stat_ss[(f0 / kGemvStatGroup) * a.out_ss_stride + tk] = ss;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) o[j] = tile[tk][8 * h + j];
+          }
+        }
+        *reinterpret_cast<uint4*>(a.y + (int64_t)tk * a.y_stride + f0) =
+            make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                       pack_bf16x2(o[6], o[7]));
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < KB; ++b) {
+      wa[b] = na[b];
+      wb[b] = nb[b];
+    }
+  }
+}
+
+template <int NT, int KB, bool STAT>
+int launch_mma(const GemvArgs& a, cudaStream_t stream) {
+  auto kern = gemv_mma_kernel<NT, KB, STAT>;
+  const int64_t tiles = a.n_out / (a.epilogue == AIOSB_EPI_SILU_MUL ? 8 : 16);
+  const unsigned blocks = (unsigned)std::min<int64_t>(tiles, 2 * (int64_t)sm_count());
+  cudaError_t e = launch_pdl(kern, dim3(blocks), dim3(kGemvThreads), 0, stream, a);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "linear (gemv mma): %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+template <int NT, int KB>
+int launch_mma_rows(const GemvArgs& a, cudaStream_t stream) {
+  return a.stat_x != nullptr ? launch_mma<NT, KB, true>(a, stream) : launch_mma<NT, KB, false>(a, stream);
+}
+
+bool g_gemv_mma = [] {
+  const char* env = getenv("AIOSB_GEMV_MMA");
+  return env != nullptr && atoi(env) != 0;
+}();
+
 bool g_gemv_enabled = [] {
   const char* env = getenv("AIOSB_DECODE_GEMV");
   return env == nullptr || atoi(env) != 0;
@@ -298,6 +525,10 @@ int launch_rows(const GemvArgs& a, cudaStream_t stream) {
 
 int gemv_launch(const GemvArgs& a, cudaStream_t stream) {
   const bool k3 = a.k <= 768;  // the 768-wide model dimension: 3 chunks, fewer registers
+  if (g_gemv_mma && (a.epilogue == AIOSB_EPI_SILU_MUL || a.n_out % 16 == 0)) {
+    if (a.rows <= 8) return k3 ? launch_mma_rows<1, 3>(a, stream) : launch_mma_rows<1, kMaxGemvK / 256>(a, stream);
+    return k3 ? launch_mma_rows<2, 3>(a, stream) : launch_mma_rows<2, kMaxGemvK / 256>(a, stream);
+  }
   if (a.rows <= 8) return k3 ? launch_rows<8, 3>(a, stream) : launch_rows<8, kMaxGemvK / 256>(a, stream);
   return k3 ? launch_rows<16, 3>(a, stream) : launch_rows<16, kMaxGemvK / 256>(a, stream);
 }
