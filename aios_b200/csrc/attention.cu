@@ -433,6 +433,11 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
     kd[3] = kv.w;
     reinterpret_cast<uint4*>(j < np ? Vp + j * D : Vs + (j - np) * D)[c] = vv;
   }
+  // The staged rows include this step's own position (its slot was not known
+  // to be written yet), and after the wait one warp overwrites that row with the
+  // new key: every staging store must land before any thread passes this point.
+  // griddepcontrol.wait is not a block barrier.
+  __syncthreads();
 
   pdl_wait();
   // the next kernel (the o projection) launches once this one has its inputs,
@@ -902,6 +907,9 @@ extern "C" int aiosb_qk_norm_rope_store(const void* qkv, int64_t qkv_stride, int
 extern "C" int aiosb_prefill_tile_tokens(int64_t num_qo_heads, int64_t num_kv_heads) {
   if (num_kv_heads <= 0 || num_qo_heads <= 0 || num_qo_heads % num_kv_heads) return 0;
   const int64_t g = num_qo_heads / num_kv_heads;
+  // one query vector per warp: a keystroke prefill has few tokens, and small
+  // tiles spread them over more CTAs (each re-stages the short key list)
+  if (g <= kAttnWarps) return (int)(kAttnWarps / g);
   return g > kMaxQueries ? 0 : (int)(kMaxQueries / g);
 }
 

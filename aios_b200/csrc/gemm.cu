@@ -540,7 +540,7 @@ int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* 
   a.k_total = k;
   const int64_t n_out = a.epilogue == AIOSB_EPI_SILU_MUL ? n / 2 : n;
   if (a.norm != 1 && gemv_eligible(rows, k, n_out)) {
-    // decode widths: CUDA-core GEMV (weights requested before the dependency wait)
+    // decode widths: register-operand MMA GEMV (weights requested before the dependency wait)
     GemvArgs g;
     memset(&g, 0, sizeof(g));
     g.x = (const __nv_bfloat16*)x;

@@ -1,4 +1,4 @@
-// Decode-width linears on the CUDA cores (gemv.cu), dispatched from the C-ABI
+// Decode-width linears on register-operand MMAs (gemv.cu), dispatched from the C-ABI
 // linear entry points in gemm.cu for at most kMaxGemvRows token rows.
 #pragma once
 

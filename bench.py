@@ -232,7 +232,7 @@ def decode_linear_roofline(llm, peaks: dict) -> dict:
     wbytes = 2 * (wbytes + llm.model.model.embed_tokens.weight.numel())
     achieved = wbytes / (ms * 1e-3) / 1e9
     peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
-    return {"bound": "hbm", "kernel": "gemv_kernel (decode linears, 8 rows, CUDA cores)", "achieved": round(achieved, 1),
+    return {"bound": "hbm", "kernel": "gemv_mma_kernel (decode linears, 8 rows, register-operand MMA)", "achieved": round(achieved, 1),
             "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": DECODE_LINEAR_TRAFFIC,
             "traffic_unit": "bytes per decode step (57 launches)", "algorithmic_bytes_per_step": wbytes,

@@ -135,8 +135,8 @@ AIOSB_API int aiosb_embedding_stat(const void* ids, int ids_is_int64, int64_t nu
  * AIOSB_EPI_ADD, residual is [rows, >= n] with row stride residual_stride and may
  * alias y (each element is read before it is written by the same thread).
  * Requires n % 128 == 0, k % 64 == 0, 16-byte aligned x/w/y. Decode widths
- * (rows <= 16, k % 256 == 0, k <= 2048) run on a CUDA-core kernel that requests
- * its weights before waiting on the previous kernel; larger calls on tcgen05. */
+ * (rows <= 16, k % 256 == 0, k <= 2048) run on a register-operand MMA kernel that
+ * requests its weights before waiting on the previous kernel; larger calls on tcgen05. */
 AIOSB_API int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
                            int64_t y_row_stride, int epilogue, const void* residual, int64_t residual_stride,
                            int32_t* status, void* stream);
@@ -160,7 +160,7 @@ AIOSB_API int aiosb_linear_rmsnorm(const void* x, const void* res, void* res_out
  * y = bf16(s), s = residual + bf16(x W^T) in fp32 (residual may alias y),
  * stat_x [rows, n] fp32 = s, and the sums of squares of s over column groups:
  * stat_ss[p * stat_ss_stride + row] for parts p < *stat_parts. A part is 128
- * columns, or 8 when rows <= 16 (the CUDA-core decode path); stat_ss must hold
+ * columns, or 8 when rows <= 16 (the register-MMA decode path); stat_ss must hold
  * n / 8 parts. *stat_parts is written before any check. n <= 2048. */
 AIOSB_API int aiosb_linear_add_stat(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
                                     int64_t y_row_stride, const void* residual, int64_t residual_stride,
