@@ -169,8 +169,8 @@ def run_cpu(keystrokes: int, warmup: int) -> dict:
 # ---------------------------------------------------------------------------
 # dram__bytes_read.sum + dram__bytes_write.sum summed over the 57 linear launches
 # of one decode step, from one ncu capture of the `linears` NVTX range below
-# (profiles/gemv_decode_linears_s10.md).
-DECODE_LINEAR_TRAFFIC = 204_558_080
+# (profiles/gemv_mma_decode_linears_s10.md).
+DECODE_LINEAR_TRAFFIC = 204_203_520
 
 
 def decode_linear_roofline(llm, peaks: dict) -> dict:
@@ -468,6 +468,50 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     return line
 
 
+def kernel_case(name: str) -> None:
+    """Small single-kernel workloads for full ncu captures (1 GPU, a few GB).
+    linears: the decode linears of every S10 layer in order, 8 rows, eagerly
+    (the 176 MB of layer weights exceed L2, so each launch reads DRAM);
+    mixer: the AttnRes mixer on 32768 tokens of 8 bank sources + partial
+    (the stream kernel; 504 MB of traffic per launch)."""
+    from aios_b200 import LLM, _lib
+    from aios_b200.kernel import ops
+    from aios_b200.models import shapes
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if name == "linears":
+        llm = LLM(config=shapes.S10, seed=0, page_size=16, num_pages=16, device="cuda:0")
+        cfg = llm.config
+        rows = 8
+        xo = torch.randn(rows, cfg.num_qo_heads * cfg.head_dim, device=dev).to(torch.bfloat16)
+        xf = torch.randn(rows, cfg.intermediate_size, device=dev).to(torch.bfloat16)
+        res = torch.randn(rows, cfg.hidden_size, device=dev).to(torch.bfloat16)
+        stats = ops.RowStats(torch.randn(rows, cfg.hidden_size, device=dev),
+                             torch.rand(cfg.hidden_size // 128, rows, device=dev) * 100)
+        nw = torch.ones(cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+        for _ in range(2):
+            for layer in llm.model.model.layers.op_list:
+                a, m = layer.self_attn, layer.mlp
+                ops.linear_stat_norm(stats, nw, 1e-6, a.qkv_proj.weight)
+                ops.linear_add_stat(xo, a.o_proj.weight, res)
+                ops.linear_stat_norm(stats, nw, 1e-6, m.gate_up_proj.packed_weight(), epilogue=_lib.EPI_SILU_MUL)
+                ops.linear_add_stat(xf, m.down_proj.weight, res)
+    elif name == "mixer":
+        g = torch.Generator(device=dev).manual_seed(0)
+        bank = torch.randn(8, 32768, 768, generator=g, device=dev).to(torch.bfloat16)
+        part = torch.randn(32768, 768, generator=g, device=dev).to(torch.bfloat16)
+        wq = torch.randn(768, generator=g, device=dev) * 0.02
+        out = torch.empty(32768, 768, dtype=torch.bfloat16, device=dev)
+        for _ in range(4):
+            ops.b200_attnres_mix(bank, part, wq, 1e-6, output_buffer=out)
+    else:
+        raise SystemExit(f"unknown kernel case {name}")
+    torch.cuda.synchronize(dev)
+    ops.check_status(dev)
+    print(f"kernel case {name}: ok")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -477,7 +521,12 @@ def main() -> None:
     ap.add_argument("--cpu-sample", type=int, default=15, help="keystrokes timed for the CPU baseline (0: skip)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the roofline / mixer micro-benchmarks (profiling runs of the keystroke only)")
+    ap.add_argument("--kernel-case", choices=["linears", "mixer"],
+                    help="run one small single-kernel workload for a full ncu capture, then exit")
     args = ap.parse_args()
+    if args.kernel_case:
+        kernel_case(args.kernel_case)
+        return
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     rank = int(os.environ.get("RANK", 0))
