@@ -163,6 +163,18 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
     }
   }
 
+  // epilogue thread (token, half) of the residual add: its 8 residual values are
+  // requested now, so their round trip overlaps the activation loads and MMAs
+  const bool epi_thread = tid < TM * 2 && (tid >> 1) < T && !silu;
+  const int64_t epi_row = (int64_t)(tid >> 1);
+  auto load_res = [&](int tl) {
+    return (epi_thread && a.epilogue == AIOSB_EPI_ADD && tl < ntiles)
+               ? *reinterpret_cast<const uint4*>(a.residual + epi_row * a.residual_stride + (int64_t)tl * 16 +
+                                                 8 * (tid & 1))
+               : make_uint4(0u, 0u, 0u, 0u);
+  };
+  uint4 rv = load_res(blockIdx.x);
+
   for (int tl = blockIdx.x; tl < ntiles; tl += gridDim.x) {
     uint4 na[KB], nb[KB];
     load_w(tl + gridDim.x, na, nb);  // next tile, in flight during this one
@@ -210,7 +222,6 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
         } else {
           f0 = (int64_t)tl * 16 + 8 * h;
           if (a.epilogue == AIOSB_EPI_ADD) {
-            const uint4 rv = *reinterpret_cast<const uint4*>(a.residual + (int64_t)tk * a.residual_stride + f0);
             const uint32_t p[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -236,6 +247,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
                        pack_bf16x2(o[6], o[7]));
       }
     }
+    if (tl + (int)gridDim.x < ntiles) rv = load_res(tl + gridDim.x);
 #pragma unroll
     for (int b = 0; b < KB; ++b) {
       wa[b] = na[b];
