@@ -351,29 +351,28 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const DecodeAr
 }
 
 // ---- decode with the key history staged before the dependency wait -----------
-// Used when the caller guarantees that the row table, the prefix length, the
-// page-table entries before each row's current position and the K/V they point
-// to were all written by earlier launches (the CandidateGroup runtime: prefix
-// from the prefill, older suffix keys from earlier steps). CTA (h, r) then copies
-// the prefix keys (up to kHistPrefix), row r's older suffix keys (up to
-// kHistSuffix - 1), the RoPE rows of positions [P, P + kRopeWin) and the norm
-// weights into shared memory BEFORE griddepcontrol.wait, i.e. while the qkv
-// projection still runs. After the wait it loads one round (the projection row,
-// position, key count, output slot, active flag), applies q/k RMSNorm + bf16 RoPE,
-// stores the new K/V and folds everything from shared memory, the new key from
-// its own registers. Table entries past a row's current position are read
-// (clamped to slot 0) but never used. Longer histories stream the rest from the
-// cache after the wait.
+// Used when the caller guarantees that everything but this step's projection row
+// was written by launches at least two kernels back on the stream: the row table,
+// the prefix length, each row's position, key count, output slot and active flag,
+// the page-table entries before its current position and the K/V they point to
+// (the CandidateGroup runtime: the prefix from the prefill, older suffix keys from
+// earlier steps, the row metadata from this step's group step, which precedes the
+// embedding and the qkv projection). CTA (h, r) then copies exactly the keys row r
+// uses (the prefix up to kHistPrefix and its older suffix up to kHistSuffix - 1,
+// contiguous), the RoPE rows of its position and the norm weights into shared
+// memory BEFORE griddepcontrol.wait, i.e. while the qkv projection still runs.
+// After the wait it loads the projection row, applies q/k RMSNorm + bf16 RoPE,
+// stores the new K/V (also as the staged row after the history) and folds all
+// keys from shared memory in one pass per 64 keys. Longer histories stream the
+// rest from the cache after the wait.
 constexpr int kHistPrefix = 128;
 constexpr int kHistSuffix = 32;
-constexpr int kRopeWin = 32;
 
 template <int D>
 size_t hist_decode_smem(int group) {
   const size_t krow = (size_t)(D + 2) * 2, vrow = (size_t)D * 2;
   return (size_t)group * D * 4 + (size_t)kDecWarps * D * 4 +
-         (size_t)(kHistPrefix + kHistSuffix + kKeyChunk) * (krow + vrow) + (size_t)2 * kRopeWin * D * 2 +
-         (size_t)2 * D * 2;
+         (size_t)(kHistPrefix + kHistSuffix + kKeyChunk) * (krow + vrow) + (size_t)4 * D * 2;
 }
 
 template <int D>
@@ -387,82 +386,69 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* q_s = reinterpret_cast<float*>(smem_raw);  // [g][D]
   float* tmp = q_s + g * D;                          // [warps][D]
-  __nv_bfloat16* Kp = reinterpret_cast<__nv_bfloat16*>(tmp + kDecWarps * D);  // [kHistPrefix][KR]
-  __nv_bfloat16* Ks = Kp + kHistPrefix * KR;   // [kHistSuffix][KR]: older suffix, then the new key
-  __nv_bfloat16* Kw = Ks + kHistSuffix * KR;   // [kKeyChunk][KR]: streamed overflow
-  __nv_bfloat16* Vp = Kw + kKeyChunk * KR;     // [kHistPrefix][D]
-  __nv_bfloat16* Vs = Vp + kHistPrefix * D;    // [kHistSuffix][D]
-  __nv_bfloat16* Vw = Vs + kHistSuffix * D;    // [kKeyChunk][D]
-  __nv_bfloat16* cos_w = Vw + kKeyChunk * D;   // [kRopeWin][D]
-  __nv_bfloat16* sin_w = cos_w + kRopeWin * D;
-  __nv_bfloat16* nq = sin_w + kRopeWin * D;    // [D]
-  __nv_bfloat16* nk = nq + D;                  // [D]
+  // staged keys, contiguous: [prefix | older suffix | the new key]
+  __nv_bfloat16* Kh = reinterpret_cast<__nv_bfloat16*>(tmp + kDecWarps * D);  // [kHistPrefix + kHistSuffix][KR]
+  __nv_bfloat16* Kw = Kh + (kHistPrefix + kHistSuffix) * KR;  // [kKeyChunk][KR]: streamed overflow
+  __nv_bfloat16* Vh = Kw + kKeyChunk * KR;                     // [kHistPrefix + kHistSuffix][D]
+  __nv_bfloat16* Vw = Vh + (kHistPrefix + kHistSuffix) * D;   // [kKeyChunk][D]
+  __nv_bfloat16* cos_r = Vw + kKeyChunk * D;                   // [D]: RoPE rows of this position
+  __nv_bfloat16* sin_r = cos_r + D;
+  __nv_bfloat16* nq = sin_r + D;  // [D]
+  __nv_bfloat16* nk = nq + D;     // [D]
   const int64_t tok_stride = (int64_t)a.hkv * D;
 
-  // ---- before the wait: history fixed since earlier launches
+  // ---- before the wait. Everything read here was written by launches at least
+  // two kernels back on this stream (the prefill, earlier steps, and this step's
+  // group step for the row's position, key count, slot and active flag). The
+  // previous kernel launched this one only after its own griddepcontrol.wait, so
+  // those launches have completed and their writes are visible.
   const int P = a.prefix_len != nullptr ? *a.prefix_len : 0;
   const int64_t prow = a.row_table[0], rrow = a.row_table[r];
-  const int np = min(P, kHistPrefix);
-  const int64_t room = a.table_stride - P;  // table entries after the prefix
-  const int ns_cap = room <= 0 ? 0 : (room < kHistSuffix - 1 ? (int)room : kHistSuffix - 1);
-  for (int i = threadIdx.x; i < np + ns_cap; i += kDecThreads)
+  const bool act = a.active == nullptr || a.active[r] != 0;
+  const int pos_in = a.positions[r];
+  const int L_in = a.seq_lens[r];
+  const int64_t oslot = a.out_loc[r];
+  const int L_lo = L_in > P + 1 ? L_in : P + 1;
+  const int L = (int64_t)L_lo > a.table_stride ? (int)a.table_stride : L_lo;
+  const int ns_old = L - 1 - P;                // older suffix keys of this row (>= 0)
+  const int np = min(P, kHistPrefix);           // staged prefix keys
+  const int ns = min(ns_old, kHistSuffix - 1);  // staged older suffix keys
+  const int nst = act ? np + ns : 0;            // the new key goes to row np + ns
+  const bool pos_ok = pos_in >= 0 && pos_in < a.max_pos;
+  const int pos = pos_ok ? pos_in : 0;
+  for (int i = threadIdx.x; i < nst; i += kDecThreads)
     slot_s[i] = a.page_table[i < np ? prow * a.table_stride + i : rrow * a.table_stride + P + (i - np)];
   for (int i = threadIdx.x; i < D; i += kDecThreads) {
     nq[i] = a.q_norm_w[i];
     nk[i] = a.k_norm_w[i];
-  }
-  for (int i = threadIdx.x; i < kRopeWin * (D / 8); i += kDecThreads) {
-    const int row = i / (D / 8), c = i % (D / 8);
-    const int pos = P + row;
-    if (pos < a.max_pos) {
-      reinterpret_cast<uint4*>(cos_w + row * D)[c] = reinterpret_cast<const uint4*>(a.cos_tab + (int64_t)pos * D)[c];
-      reinterpret_cast<uint4*>(sin_w + row * D)[c] = reinterpret_cast<const uint4*>(a.sin_tab + (int64_t)pos * D)[c];
-    }
+    cos_r[i] = a.cos_tab[(int64_t)pos * D + i];
+    sin_r[i] = a.sin_tab[(int64_t)pos * D + i];
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < (np + ns_cap) * (D / 8); i += kDecThreads) {
+  for (int i = threadIdx.x; i < nst * (D / 8); i += kDecThreads) {
     const int j = i / (D / 8), c = i % (D / 8);
     int64_t slot = slot_s[j];
-    if (slot < 0 || slot >= a.num_slots) slot = 0;  // checked again after the wait for the keys in use
+    if (slot < 0 || slot >= a.num_slots) slot = 0;  // reported after the wait
     const uint4 kv = reinterpret_cast<const uint4*>(a.k_cache + slot * tok_stride + (int64_t)h * D)[c];
     const uint4 vv = reinterpret_cast<const uint4*>(a.v_cache + slot * tok_stride + (int64_t)h * D)[c];
-    uint32_t* kd = reinterpret_cast<uint32_t*>(j < np ? Kp + j * KR : Ks + (j - np) * KR) + c * 4;
+    uint32_t* kd = reinterpret_cast<uint32_t*>(Kh + j * KR) + c * 4;
     kd[0] = kv.x;
     kd[1] = kv.y;
     kd[2] = kv.z;
     kd[3] = kv.w;
-    reinterpret_cast<uint4*>(j < np ? Vp + j * D : Vs + (j - np) * D)[c] = vv;
+    reinterpret_cast<uint4*>(Vh + j * D)[c] = vv;
   }
-  // The staged rows include this step's own position (its slot was not known
-  // to be written yet), and after the wait one warp overwrites that row with the
-  // new key: every staging store must land before any thread passes this point.
-  // griddepcontrol.wait is not a block barrier.
-  __syncthreads();
+  // (no barrier needed here: after the wait only row np + ns, which staging
+  // never writes, is stored before the barrier that precedes the folds)
 
   pdl_wait();
   // the next kernel (the o projection) launches once this one has its inputs,
   // which bounds how far ahead the chain prefetches (measured: 5.70 -> 5.54 ms)
   pdl_launch_dependents();
-  // ---- after the wait: this step's row (one round of loads)
-  const int pos_in = a.positions[r];
-  const int L_in = a.seq_lens[r];
-  const bool act = a.active == nullptr || a.active[r] != 0;
-  const int64_t oslot = a.out_loc[r];
-  // keys of this row: the prefix, its older suffix keys and the new one
-  const int L_lo = L_in > P + 1 ? L_in : P + 1;
-  const int L = (int64_t)L_lo > a.table_stride ? (int)a.table_stride : L_lo;
-  if (act && threadIdx.x == 0 && (L_in < P + 1 || L_in > a.table_stride)) report(a.status, AIOSB_DEV_POSITION_RANGE);
-  const int ns_old = L - 1 - P;  // older suffix keys of this row (>= 0)
-  const int new_row = ns_old <= ns_cap ? ns_old : kHistSuffix - 1;
+  // ---- after the wait: this step's projection row
   if (act) {
-    int pos = pos_in;
-    if (pos < 0 || pos >= a.max_pos) {
-      if (threadIdx.x == 0) report(a.status, AIOSB_DEV_POSITION_RANGE);
-      pos = 0;
-    }
-    const bool in_win = pos >= P && pos < P + kRopeWin;
-    const __nv_bfloat16* cos_row = in_win ? cos_w + (pos - P) * D : a.cos_tab + (int64_t)pos * D;
-    const __nv_bfloat16* sin_row = in_win ? sin_w + (pos - P) * D : a.sin_tab + (int64_t)pos * D;
+    if (threadIdx.x == 0 && (!pos_ok || L_in < P + 1 || L_in > a.table_stride))
+      report(a.status, AIOSB_DEV_POSITION_RANGE);
     for (int it = warp; it < g + 1; it += kDecWarps) {
       float* tw = tmp + warp * D;
       float x[DPL];
@@ -470,7 +456,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
         const __nv_bfloat16* src = a.qkv + (int64_t)r * a.qkv_stride + (int64_t)(h * g + it) * D;
 #pragma unroll
         for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(src[i * 32 + lane]);
-        norm_rope<D>(x, nq, a.eps, cos_row, sin_row, true, true, lane, tw);
+        norm_rope<D>(x, nq, a.eps, cos_r, sin_r, true, true, lane, tw);
 #pragma unroll
         for (int i = 0; i < DPL; ++i) q_s[it * D + i * 32 + lane] = x[i];
       } else {
@@ -482,14 +468,14 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
           x[i] = bf16_to_f(ksrc[i * 32 + lane]);
           vraw[i] = vsrc[i * 32 + lane];
         }
-        norm_rope<D>(x, nk, a.eps, cos_row, sin_row, true, true, lane, tw);
+        norm_rope<D>(x, nk, a.eps, cos_r, sin_r, true, true, lane, tw);
         const bool slot_ok = oslot >= 0 && oslot < a.num_slots;
         if (!slot_ok && lane == 0) report(a.status, AIOSB_DEV_SLOT_RANGE);
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
           const __nv_bfloat16 kb = f_to_bf16(x[i]);
-          Ks[new_row * KR + i * 32 + lane] = kb;
-          Vs[new_row * D + i * 32 + lane] = vraw[i];
+          Kh[nst * KR + i * 32 + lane] = kb;
+          Vh[nst * D + i * 32 + lane] = vraw[i];
           if (slot_ok) {
             a.k_cache[oslot * tok_stride + (int64_t)h * D + i * 32 + lane] = kb;
             a.v_cache[oslot * tok_stride + (int64_t)h * D + i * 32 + lane] = vraw[i];
@@ -499,7 +485,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
     }
     if (threadIdx.x == 0) {  // the staged keys this row uses must be real slots
       bool bad = false;
-      for (int j = 0; j < np + min(ns_old, ns_cap); ++j) bad |= slot_s[j] < 0 || slot_s[j] >= a.num_slots;
+      for (int j = 0; j < nst; ++j) bad |= slot_s[j] < 0 || slot_s[j] >= a.num_slots;
       if (bad) report(a.status, AIOSB_DEV_SLOT_RANGE);
     }
   }
@@ -518,8 +504,12 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
   };
   const int32_t* pslots = a.page_table + prow * a.table_stride;
   const int32_t* rslots = a.page_table + rrow * a.table_stride;
-  // prefix: staged part, then any overflow streamed from the cache
-  for (int c0 = 0; c0 < np; c0 += kKeyChunk) fold_all(Kp + c0 * KR, Vp + c0 * D, min(kKeyChunk, np - c0));
+  // staged keys [prefix | older suffix] and, without a suffix overflow, the new
+  // key right after them: one pass per 64 keys
+  const int nfold = act ? nst + (ns_old == ns ? 1 : 0) : 0;
+  for (int c0 = 0; c0 < nfold; c0 += kKeyChunk) fold_all(Kh + c0 * KR, Vh + c0 * D, min(kKeyChunk, nfold - c0));
+  // longer histories: the prefix beyond the staged part, then the older suffix
+  // beyond it, streamed from the cache, and the new key last
   for (int k0 = np; k0 < P; k0 += kKeyChunk) {
     const int n = min(kKeyChunk, P - k0);
     stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, pslots, k0, n, a.num_slots, Kw, Vw, a.status);
@@ -527,21 +517,15 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
     fold_all(Kw, Vw, n);
     __syncthreads();
   }
-  // suffix: older keys (+ the new key when contiguous), overflow, new key
-  if (act) {
-    if (ns_old <= ns_cap) {
-      fold_all(Ks, Vs, ns_old + 1);
-    } else {
-      fold_all(Ks, Vs, ns_cap);
-      for (int k0 = P + ns_cap; k0 < L - 1; k0 += kKeyChunk) {
-        const int n = min(kKeyChunk, L - 1 - k0);
-        stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, rslots, k0, n, a.num_slots, Kw, Vw, a.status);
-        __syncthreads();
-        fold_all(Kw, Vw, n);
-        __syncthreads();
-      }
-      fold_all(Ks + (kHistSuffix - 1) * KR, Vs + (kHistSuffix - 1) * D, 1);
+  if (act && ns_old > ns) {
+    for (int k0 = P + ns; k0 < L - 1; k0 += kKeyChunk) {
+      const int n = min(kKeyChunk, L - 1 - k0);
+      stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, rslots, k0, n, a.num_slots, Kw, Vw, a.status);
+      __syncthreads();
+      fold_all(Kw, Vw, n);
+      __syncthreads();
     }
+    fold_all(Kh + nst * KR, Vh + nst * D, 1);
   }
 
   // ---- normalise and store (zeros for inactive rows)

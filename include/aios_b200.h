@@ -196,13 +196,14 @@ AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, 
  * heads) or q (already normalised and rotated [rows, q_stride]). Rows with
  * active[r] == 0 are skipped (output zeros, no store); active may be NULL.
  * rows * (num_qo_heads / num_kv_heads) <= 64. out: [rows, out_stride] bf16. *
- * stable_history != 0 (fused mode only) asserts that row_table, *prefix_len, the
- * page-table entries before each row's current position and the K/V they point
- * to were written by launches that completed before the previous kernel on this
- * stream began (the CandidateGroup runtime: prefix from the prefill, older
- * suffix keys from earlier steps). The kernel then copies that history into
- * shared memory before waiting on the previous kernel, and after the wait only
- * this step's projection row and metadata stay on its critical path. */
+ * stable_history != 0 (fused mode only) asserts that row_table, *prefix_len,
+ * positions, seq_lens, out_loc, active, the page-table entries before each row's
+ * current position and the K/V they point to were written by launches at least
+ * two kernels back on this stream (the CandidateGroup runtime: prefix from the
+ * prefill, older suffix keys from earlier steps, row metadata from this step's
+ * group step). The kernel then copies the keys each row uses into shared memory
+ * before waiting on the previous kernel, and after the wait only this step's
+ * projection row stays on its critical path. */
 AIOSB_API int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const void* q, int64_t q_stride,
                            const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_tab,
                            const void* sin_tab, int64_t max_pos, const int32_t* positions, const int32_t* out_loc,
