@@ -323,11 +323,79 @@ __device__ int count_prefix(RowSmem& s, const Prob& prob, int k, int lo, int hi,
   return cnt;
 }
 
+// pick_index for k <= 64 on warp 0 alone (lane l holds candidates l and l + 32),
+// with the association of every sum and scan exactly as pick_index's block form
+// has it for k <= 64 (one candidate per thread): the same results, no barriers.
+template <class Val>
+__device__ int pick_index_warp(const Val& val, int k, float top_p, float u) {
+  const int lane = threadIdx.x & 31;
+  const bool h0 = lane < k, h1 = lane + 32 < k;
+  const float v0 = h0 ? val(lane) : -INFINITY, v1 = h1 ? val(lane + 32) : -INFINITY;
+  const float mx = warp_max(fmaxf(v0, v1));
+  const float e0 = h0 ? expf(v0 - mx) : 0.f, e1 = h1 ? expf(v1 - mx) : 0.f;
+  // block_sum: each warp's tree sum, then the sum of the two warp totals
+  const float inv = 1.0f / (warp_sum(e0) + warp_sum(e1));
+  // #prefixes i with fl32(cumsum_i) compared to thr, cumsums in fp64 (exact when
+  // every non-zero term is >= 2^-29, else the candidates are walked in order)
+  const auto count = [&](float p0, float p1, float thr, bool strict) {
+    const bool ok = __all_sync(0xffffffffu, (p0 == 0.f || p0 >= 0x1p-29f) && (p1 == 0.f || p1 >= 0x1p-29f));
+    if (ok) {
+      double a0 = p0, a1 = p1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double y0 = __shfl_up_sync(0xffffffffu, a0, o), y1 = __shfl_up_sync(0xffffffffu, a1, o);
+        if (lane >= o) {
+          a0 += y0;
+          a1 += y1;
+        }
+      }
+      a1 += __shfl_sync(0xffffffffu, a0, 31);
+      const float f0 = __double2float_rn(a0), f1 = __double2float_rn(a1);
+      const bool c0 = h0 && (strict ? f0 < thr : f0 <= thr), c1 = h1 && (strict ? f1 < thr : f1 <= thr);
+      return __popc(__ballot_sync(0xffffffffu, c0)) + __popc(__ballot_sync(0xffffffffu, c1));
+    }
+    // sequential: every lane walks the candidates in order (each value fetched
+    // from its lane by a shuffle, so the loop stays warp-uniform)
+    int cnt = 0;
+    double acc = 0.0;
+    bool stop = false;
+    for (int i = 0; i < k; ++i) {
+      const float p = i < 32 ? __shfl_sync(0xffffffffu, p0, i) : __shfl_sync(0xffffffffu, p1, i - 32);
+      acc += (double)p;
+      const float f = __double2float_rn(acc);
+      if (!stop && (strict ? (f < thr) : (f <= thr))) cnt = i + 1;
+      else stop = true;
+    }
+    return cnt;
+  };
+  int keep = k;
+  float inv2 = inv;
+  if (top_p < 1.0f) {
+    const int n_le = count(e0 * inv, e1 * inv, top_p, false);
+    keep = n_le < k ? n_le + 1 : k;  // remove[i] = cumsum[i-1] > top_p, first kept
+    const float s0 = lane < keep ? e0 : 0.f, s1 = lane + 32 < keep ? e1 : 0.f;
+    inv2 = 1.0f / (warp_sum(s0) + warp_sum(s1));
+  }
+  const float q0 = lane < keep ? e0 * inv2 : 0.f, q1 = lane + 32 < keep ? e1 * inv2 : 0.f;
+  const int idx = count(q0, q1, u, true);
+  return idx > k - 1 ? k - 1 : idx;
+}
+
 // Softmax over the k candidate values val(0..k) (in candidate order), top-p with
 // the one-position shifted mask (aios/engine/sample.py:134-146), re-softmax and
 // the inverse CDF index = #(cumsum < u) clamped to k - 1 (sample.py:161-165).
 template <class Val>
 __device__ int pick_index(RowSmem& s, const Val& val, int k, float top_p, float u) {
+  if (k <= 64) {
+    if (threadIdx.x < 32) {
+      const int idx = pick_index_warp(val, k, top_p, u);
+      if (threadIdx.x == 0) s.misc[5] = idx;
+    }
+    __syncthreads();
+    const int idx = s.misc[5];
+    __syncthreads();
+    return idx;
+  }
   const int seg = (k + kSampThreads - 1) / kSampThreads;
   const int lo = min(k, (int)threadIdx.x * seg), hi = min(k, lo + seg);
   float mx = -INFINITY;
@@ -775,13 +843,23 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
       st->n_active = 0;
     }
     if (g.host_mirror != nullptr) {
-      volatile int32_t* m = g.host_mirror;
-      m[1] = done ? 1 : 0;
-      m[2] = (done && cancel) ? 1 : 0;
-      m[3] = done ? 0 : n;
-      __threadfence_system();
-      m[0] = step + 1;  // steps sampled so far; written last
-      __threadfence_system();
+      // [steps sampled so far, done, cancelled, active rows] in one 16-byte store
+      // to the page-locked mirror: the host sees the four words together, so no
+      // system-scope fence has to order them (the host only paces its launches
+      // by them; results are read after an event wait)
+      const int w0 = step + 1, w1 = done ? 1 : 0, w2 = (done && cancel) ? 1 : 0, w3 = done ? 0 : n;
+      if ((reinterpret_cast<uintptr_t>(g.host_mirror) & 15u) == 0) {
+        asm volatile("st.volatile.global.v4.s32 [%0], {%1, %2, %3, %4};" ::"l"(g.host_mirror), "r"(w0), "r"(w1),
+                     "r"(w2), "r"(w3)
+                     : "memory");
+      } else {
+        volatile int32_t* m = g.host_mirror;
+        m[1] = w1;
+        m[2] = w2;
+        m[3] = w3;
+        __threadfence_system();
+        m[0] = w0;  // written last
+      }
     }
   }
 }

@@ -319,7 +319,7 @@ typedef struct aiosb_group_state {
 typedef struct aiosb_group_ptrs {
   aiosb_group_state* state;
   const int32_t* cancel_flag; /* host-mapped word set by the canceller, or NULL    */
-  int32_t* host_mirror;       /* host-mapped [steps_done, done, cancelled, n_active] */
+  int32_t* host_mirror;       /* host-mapped [steps_done, done, cancelled, n_active]; 16-byte aligned: one store */
   void* logits;               /* [rows, vocab] bf16: next step's logits            */
   float* uniforms;            /* [rows, max_steps]                                  */
   int32_t* output_ids;        /* [rows, max_steps]                                  */
