@@ -208,7 +208,7 @@ __device__ __forceinline__ void load_row(RowSmem& s, RowRegs& rr, const __nv_bfl
   for (int q = 0; q < kVecPer; ++q) {
     const int j = tid + q * kSampThreads;
     if (j < ngroups) {
-#pragma unroll
+#pragma unroll 1  // compact code: the step kernel runs cold each decode step
       for (int e = 0; e < 8; ++e)
         if (8 * j + e < V) se += expf(group_elem(rr.v[q], e) - m);
     }
@@ -234,20 +234,15 @@ __device__ __forceinline__ uint32_t make_keys(const RowSmem& s, const RowRegs& r
     const int j = threadIdx.x + q * kSampThreads;
     if (j < ngroups) {
       const uint32_t bits = s.ban[j >> 2] >> ((j & 3) * 8);  // 8 tokens of a group share a word
-      uint32_t kk[8];
-#pragma unroll
+#pragma unroll 1  // compact code: the step kernel runs cold each decode step
       for (int e = 0; e < 8; ++e) {
         float v = group_elem(rr.v[q], e);
         if ((bits >> e) & 1u) v = -INFINITY;
-        kk[e] = 8 * j + e < V ? order_key(v / temperature) : 0u;
-        best = kk[e] > best ? kk[e] : best;
-      }
-      if (8 * j + 8 <= V) {
-        *reinterpret_cast<uint4*>(keys + 8 * j) = make_uint4(kk[0], kk[1], kk[2], kk[3]);
-        *reinterpret_cast<uint4*>(keys + 8 * j + 4) = make_uint4(kk[4], kk[5], kk[6], kk[7]);
-      } else {
-        for (int e = 0; e < 8; ++e)
-          if (8 * j + e < V) keys[8 * j + e] = kk[e];
+        if (8 * j + e < V) {
+          const uint32_t kk = order_key(v / temperature);
+          keys[8 * j + e] = kk;
+          best = kk > best ? kk : best;
+        }
       }
     }
   }
@@ -264,7 +259,7 @@ __device__ __forceinline__ int greedy_pick(RowSmem& s, const RowRegs& rr, int V)
     const int j = threadIdx.x + q * kSampThreads;
     if (j < ngroups) {
       const uint32_t bits = s.ban[j >> 2] >> ((j & 3) * 8);
-#pragma unroll
+#pragma unroll 1  // compact code: the step kernel runs cold each decode step
       for (int e = 0; e < 8; ++e) {
         const int i = 8 * j + e;
         float v = group_elem(rr.v[q], e);
@@ -630,7 +625,7 @@ __device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, 
     for (int q = 0; q < kVecPer; ++q) {
       const int j = tid + q * kSampThreads;
       if (j < ngroups && tmax >= L) {
-#pragma unroll
+#pragma unroll 1  // compact code: the step kernel runs cold each decode step
         for (int e = 0; e < 8; ++e) n += (8 * j + e < V && keys[8 * j + e] >= L) ? 1 : 0;
       }
     }
@@ -642,7 +637,7 @@ __device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, 
         for (int q = 0; q < kVecPer; ++q) {
           const int j = tid + q * kSampThreads;
           if (j < ngroups) {
-#pragma unroll
+#pragma unroll 1  // compact code: the step kernel runs cold each decode step
             for (int e = 0; e < 8; ++e) {
               const int i = 8 * j + e;
               if (i < V && keys[i] >= L)
