@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import math
 import re
+from functools import lru_cache
 from dataclasses import asdict, dataclass
 from typing import Any
 
@@ -19,6 +20,8 @@ REPEAT_PATTERN = re.compile(r"(.)\1{3,}")
 TERMINAL_TEXT_PATTERN = re.compile(r"[。！？!?；;]")
 WHITESPACE_PATTERN = re.compile(r"\s+")
 REDUPLICATION_PATTERN = re.compile(r"([\u3400-\u9fff])\1")
+# a unit of 2-4 characters repeated three times in a row
+TRIPLE_UNIT_PATTERN = re.compile(r"(.{2,4})\1\1", re.DOTALL)
 FUNCTION_WORD_ENDINGS = (
     "的", "地", "得", "和", "与", "或", "但", "而", "在", "把", "被", "给",
     "对", "从", "向", "为", "再", "就", "会", "能", "如果", "因为", "所以",
@@ -171,7 +174,9 @@ def token_longest_common_prefix(left: list[int], right: list[int]) -> int:
     return n
 
 
+@lru_cache(maxsize=4096)
 def normalize_candidate(text: str) -> str:
+    # pure; cached because one keystroke normalises each candidate several times
     return WHITESPACE_PATTERN.sub("", text.replace("\ufffd", "")).strip()
 
 
@@ -183,6 +188,7 @@ def truncate_at_terminal(text: str) -> tuple[str, bool]:
     return text[: found.end()], True
 
 
+@lru_cache(maxsize=4096)
 def candidate_key(text: str) -> str:
     return normalize_candidate(text).rstrip(DISPLAY_PUNCTUATION).casefold()
 
@@ -192,14 +198,8 @@ def repeated_ngram(text: str) -> bool:
 
 
 def _repeated_ngram_compact(compact: str) -> bool:
-    if REPEAT_PATTERN.search(compact):
-        return True
-    for width in (2, 3, 4):
-        for start in range(max(0, len(compact) - 3 * width + 1)):
-            unit = compact[start : start + width]
-            if unit and compact[start : start + 3 * width] == unit * 3:
-                return True
-    return False
+    # a character four times in a row, or a 2-4 character unit three times
+    return REPEAT_PATTERN.search(compact) is not None or TRIPLE_UNIT_PATTERN.search(compact) is not None
 
 
 def invalid_reasons(text: str, config: ImeGenerationConfig, prefix: str = "") -> tuple[str, ...]:
@@ -268,21 +268,30 @@ def select_top_candidates(candidates: list[ImeCandidate], count: int, diversity_
         if held is None or cand.base_score > held.base_score:
             best[key] = cand
     pool = list(best.values())
-    chosen: list[ImeCandidate] = []
     # bigram sets computed once per candidate; each pool entry keeps its running
     # maximum similarity to the chosen ones, updated against the newest pick only
-    grams = {id(c): _grams(c.text) for c in pool}
-    max_sim = {id(c): 0.0 for c in pool}
-
-    def mmr(cand: ImeCandidate) -> float:
-        return cand.base_score - diversity_lambda * max_sim[id(cand)]
-
-    while pool and len(chosen) < count:
-        pick = max(pool, key=mmr)
-        score = mmr(pick)
-        pool.remove(pick)
-        for c in pool:
-            max_sim[id(c)] = max(max_sim[id(c)], _jaccard(grams[id(c)], grams[id(pick)]))
+    grams = [_grams(c.text) for c in pool]
+    max_sim = [0.0] * len(pool)
+    alive = list(range(len(pool)))
+    chosen: list[ImeCandidate] = []
+    while alive and len(chosen) < count:
+        # the first entry with the largest MMR score (as max() picks it)
+        pick_i = alive[0]
+        score = pool[pick_i].base_score - diversity_lambda * max_sim[pick_i]
+        for i in alive[1:]:
+            value = pool[i].base_score - diversity_lambda * max_sim[i]
+            if value > score:
+                pick_i, score = i, value
+        alive.remove(pick_i)
+        picked = grams[pick_i]
+        if picked:
+            for i in alive:
+                other = grams[i]
+                if other:
+                    sim = len(other & picked) / len(other | picked)
+                    if sim > max_sim[i]:
+                        max_sim[i] = sim
+        pick = pool[pick_i]
         chosen.append(ImeCandidate(
             text=pick.text, token_count=pick.token_count, average_logprob=pick.average_logprob,
             base_score=pick.base_score, selection_score=score, stop_reason=pick.stop_reason,

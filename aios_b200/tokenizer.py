@@ -27,6 +27,8 @@ class SyntheticTokenizer:
             raise ValueError("vocab_size too small for the synthetic tokenizer")
         self.vocab_size = vocab_size
         self._punct = {ch: 3 + i for i, ch in enumerate(TERMINALS)}
+        # decode table: the text of every id, "" for the special ids
+        self._table = ["", "", ""] + [self.id_to_char(i) for i in range(3, vocab_size)]
 
     def id_to_char(self, token_id: int) -> str:
         if 3 <= token_id < FIRST_CJK_ID:
@@ -50,6 +52,9 @@ class SyntheticTokenizer:
         return ids
 
     def decode(self, ids: Iterable[int], skip_special_tokens: bool = True, clean_up_tokenization_spaces: bool = False) -> str:
+        if skip_special_tokens:
+            table, vocab = self._table, self.vocab_size
+            return "".join([table[i] if 0 <= i < vocab else "" for i in map(int, ids)])
         out = []
         for token_id in ids:
             token_id = int(token_id)

@@ -199,3 +199,35 @@ def test_mmr_selection_matches_direct_restatement() -> None:
             chosen.append(pick)
             pool.remove(pick)
         assert got == [(c.text, s) for c, s in zip(chosen, scores)], trial
+
+
+def test_repeated_ngram_matches_direct_restatement() -> None:
+    """The regex repeat check equals the direct scan of the reference's filter:
+    a character four times in a row, or a 2-4 character unit three times."""
+    import random
+
+    from aios_b200.ime_text import REPEAT_PATTERN, _repeated_ngram_compact
+
+    def direct(compact: str) -> bool:
+        if REPEAT_PATTERN.search(compact):
+            return True
+        for width in (2, 3, 4):
+            for start in range(max(0, len(compact) - 3 * width + 1)):
+                unit = compact[start : start + width]
+                if unit and compact[start : start + 3 * width] == unit * 3:
+                    return True
+        return False
+
+    rng = random.Random(0)
+    alphabet = "你好天气很不错的了吗。"
+    cases = ["", "a", "哈哈哈哈", "你好你好你好", "今天天气很好", "abcabcab", "abcabcabc", "abcdabcdabcd", "ababa"]
+    for _ in range(3000):
+        n = rng.randint(0, 14)
+        text = "".join(rng.choice(alphabet[: rng.randint(2, len(alphabet))]) for _ in range(n))
+        if rng.random() < 0.3 and n >= 2:  # plant a repeated unit
+            w = rng.randint(2, 4)
+            pos = rng.randint(0, n)
+            text = text[:pos] + text[:w] * rng.randint(2, 3) + text[pos:]
+        cases.append(text)
+    for text in cases:
+        assert _repeated_ngram_compact(text) == direct(text), text
