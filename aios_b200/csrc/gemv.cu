@@ -100,8 +100,14 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
     for (int b = 0; b < KB; ++b)
       nwv[b] = b < kb ? *reinterpret_cast<const uint4*>(a.nw + kbase + b * 32) : make_uint4(0u, 0u, 0u, 0u);
   }
+  // A residual-add linear (o, down) lets its successor launch at once: that
+  // successor is a linear whose weights can stream in meanwhile (measured: 5.5 us
+  // less per decode step). The others launch it only after their own wait, so a
+  // kernel that follows them may read, before its own wait, anything written two
+  // or more kernels back (the decode attention after the qkv linear does).
+  if (a.epilogue == AIOSB_EPI_ADD) pdl_launch_dependents();
   pdl_wait();
-  pdl_launch_dependents();
+  if (a.epilogue != AIOSB_EPI_ADD) pdl_launch_dependents();
 
   // ---- B fragments: token row n = nt * 8 + g, this lane's 8 elements per block
   uint4 xb[NT][KB];

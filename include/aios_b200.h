@@ -136,7 +136,9 @@ AIOSB_API int aiosb_embedding_stat(const void* ids, int ids_is_int64, int64_t nu
  * alias y (each element is read before it is written by the same thread).
  * Requires n % 128 == 0, k % 64 == 0, 16-byte aligned x/w/y. Decode widths
  * (rows <= 16, k % 256 == 0, k <= 2048) run on a register-operand MMA kernel that
- * requests its weights before waiting on the previous kernel; larger calls on tcgen05. */
+ * requests its weights before waiting on the previous kernel; larger calls on tcgen05.
+ * A decode-width AIOSB_EPI_ADD call lets the next kernel on the stream launch at
+ * once; the other epilogues let it launch only after their own wait. */
 AIOSB_API int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
                            int64_t y_row_stride, int epilogue, const void* residual, int64_t residual_stride,
                            int32_t* status, void* stream);
@@ -199,9 +201,10 @@ AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, 
  * stable_history != 0 (fused mode only) asserts that row_table, *prefix_len,
  * positions, seq_lens, out_loc, active, the page-table entries before each row's
  * current position and the K/V they point to were written by launches at least
- * two kernels back on this stream (the CandidateGroup runtime: prefix from the
- * prefill, older suffix keys from earlier steps, row metadata from this step's
- * group step). The kernel then copies the keys each row uses into shared memory
+ * two kernels back on this stream, and that the previous kernel launches this
+ * one only after its own wait (not a decode-width AIOSB_EPI_ADD linear) (the
+ * CandidateGroup runtime: prefix from the prefill, older suffix keys from earlier
+ * steps, row metadata from this step's group step, the qkv linear just before). The kernel then copies the keys each row uses into shared memory
  * before waiting on the previous kernel, and after the wait only this step's
  * projection row stays on its critical path. */
 AIOSB_API int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const void* q, int64_t q_stride,
