@@ -30,9 +30,14 @@ constexpr int kMaxSources = 16;
 // instead of as NSRC dependent shuffle chains. rows(s, j) returns chunk
 // lane + 32 j of source s; rows.between_phases() runs between the score pass and
 // the weighted-sum pass.
-template <int VPL, int NSRC, class Rows>
+// NORM: the output row is written RMS-normalised, bf16(h * rcp * nw) with h the
+// bf16 mixer output and rcp = 1 / sqrt(mean(h^2) + norm_eps) (RMSNorm.forward,
+// aios/layers/norm.py:10-22, applied to the mixer result); nwr holds this lane's
+// chunks of the norm weight.
+template <int VPL, int NSRC, bool NORM = false, class Rows>
 __device__ __forceinline__ void mix_token(const Rows& rows, const float2 (&wqr)[VPL][4], int nv, int hidden,
-                                          float eps, int lane, uint4* __restrict__ out_row) {
+                                          float eps, int lane, uint4* __restrict__ out_row,
+                                          const uint4 (*nwr)[VPL] = nullptr, float norm_eps = 0.f) {
   float score[NSRC];
   float mx = -INFINITY;
 #pragma unroll
@@ -64,9 +69,11 @@ __device__ __forceinline__ void mix_token(const Rows& rows, const float2 (&wqr)[
 #pragma unroll
   for (int s = 0; s < NSRC; ++s) score[s] = round_bf16(score[s] / denom);
   rows.between_phases();
+  uint4 hbuf[VPL];  // NORM: the bf16 mixer output, normalised once the row is complete
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int i = lane + j * 32;
+    hbuf[j] = make_uint4(0u, 0u, 0u, 0u);
     if (i < nv) {
       float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -77,8 +84,37 @@ __device__ __forceinline__ void mix_token(const Rows& rows, const float2 (&wqr)[
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[q] = __ffma2_rn(w2, make_float2(bf16_lo(p[q]), bf16_hi(p[q])), acc[q]);
       }
-      out_row[i] = make_uint4(pack_bf16x2(acc[0].x, acc[0].y), pack_bf16x2(acc[1].x, acc[1].y),
-                              pack_bf16x2(acc[2].x, acc[2].y), pack_bf16x2(acc[3].x, acc[3].y));
+      const uint4 packed = make_uint4(pack_bf16x2(acc[0].x, acc[0].y), pack_bf16x2(acc[1].x, acc[1].y),
+                                      pack_bf16x2(acc[2].x, acc[2].y), pack_bf16x2(acc[3].x, acc[3].y));
+      if (NORM) hbuf[j] = packed;
+      else out_row[i] = packed;
+    }
+  }
+  if (NORM) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      if (lane + j * 32 < nv) {
+        const uint32_t p[4] = {hbuf[j].x, hbuf[j].y, hbuf[j].z, hbuf[j].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) ss += bf16_lo(p[q]) * bf16_lo(p[q]) + bf16_hi(p[q]) * bf16_hi(p[q]);
+      }
+    }
+    ss = warp_sum(ss);
+    const float rcp = 1.0f / sqrtf(ss / (float)hidden + norm_eps);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int i = lane + j * 32;
+      if (i < nv) {
+        const uint32_t p[4] = {hbuf[j].x, hbuf[j].y, hbuf[j].z, hbuf[j].w};
+        const uint4 wv = (*nwr)[j];
+        const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          o[q] = pack_bf16x2(bf16_lo(p[q]) * rcp * bf16_lo(w[q]), bf16_hi(p[q]) * rcp * bf16_hi(w[q]));
+        out_row[i] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
     }
   }
 }
@@ -113,17 +149,21 @@ struct RegRows {
 
 // One warp per token, every source row loaded straight into registers. The
 // weighted query, a model constant, is loaded before the wait on the producer.
-template <int VPL, int NSRC>
+template <int VPL, int NSRC, bool NORM = false>
 __global__ void __launch_bounds__(kMixWarps * 32, 3)
     attnres_reg_kernel(const uint4* __restrict__ bank, int nsrc_bank, int64_t tokens, int hidden,
                        const uint4* __restrict__ partial, const float* __restrict__ wq, float eps,
-                       uint4* __restrict__ out) {
+                       uint4* __restrict__ out, const uint4* __restrict__ norm_w = nullptr, float norm_eps = 0.f) {
   pdl_launch_dependents();
   const int64_t t = (int64_t)blockIdx.x * kMixWarps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   const int nv = hidden / 8;
   float2 wqr[VPL][4];
   load_wq<VPL>(wq, nv, lane, wqr);
+  uint4 nwr[VPL];  // the norm weight, a model constant like wq
+#pragma unroll
+  for (int j = 0; j < VPL; ++j)
+    nwr[j] = (NORM && lane + j * 32 < nv) ? norm_w[lane + j * 32] : make_uint4(0u, 0u, 0u, 0u);
   pdl_wait();
   if (t >= tokens) return;
   uint4 x[NSRC][VPL];
@@ -137,7 +177,7 @@ __global__ void __launch_bounds__(kMixWarps * 32, 3)
       x[s][j] = (i < nv) ? src[i] : make_uint4(0, 0, 0, 0);
     }
   }
-  mix_token<VPL, NSRC>(RegRows<VPL, NSRC>{x}, wqr, nv, hidden, eps, lane, out + t * nv);
+  mix_token<VPL, NSRC, NORM>(RegRows<VPL, NSRC>{x}, wqr, nv, hidden, eps, lane, out + t * nv, &nwr, norm_eps);
 }
 
 // Source rows of one token in a shared-memory stage, read once per pass: the
@@ -412,11 +452,43 @@ extern "C" int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t toke
       default: kern = attnres_reg_kernel<3, 10>; break;
     }
     e = launch_pdl(kern, grid, dim3(kMixWarps * 32), 0, as_stream(stream), (const uint4*)bank, (int)sources, tokens,
-                   (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out);
+                   (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out, (const uint4*)nullptr, 0.f);
   } else {
     e = launch_pdl(attnres_generic_kernel, grid, dim3(kMixWarps * 32), 0, as_stream(stream), (const uint4*)bank,
                    (int)sources, tokens, (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out);
   }
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attnres_mix: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_attnres_mix_rmsnorm(const void* bank, int64_t sources, int64_t tokens, int64_t hidden,
+                                         const void* partial, const float* weighted_query, float eps,
+                                         const void* norm_w, float norm_eps, void* out, void* stream) {
+  AIOSB_REQUIRE(sources >= 1 && tokens >= 1 && hidden >= 1, AIOSB_ERR_INVALID_ARG,
+                "bank dimensions must be positive");
+  const int64_t total = sources + (partial != nullptr ? 1 : 0);
+  AIOSB_REQUIRE(total <= kMaxRegSources && hidden % 8 == 0 && hidden / 8 <= 3 * 32, AIOSB_ERR_UNSUPPORTED,
+                "attnres_mix_rmsnorm: at most %d sources and hidden <= 768 (a multiple of 8)", kMaxRegSources);
+  AIOSB_REQUIRE(bank && weighted_query && norm_w && out, AIOSB_ERR_INVALID_ARG, "attnres_mix_rmsnorm: null pointer");
+  AIOSB_REQUIRE(aligned16(bank) && aligned16(out) && aligned16(norm_w) && (partial == nullptr || aligned16(partial)),
+                AIOSB_ERR_MISALIGNED, "attnres_mix_rmsnorm: bank/partial/norm_w/out must be 16-byte aligned");
+  const dim3 grid((unsigned)((tokens + kMixWarps - 1) / kMixWarps));
+  auto kern = attnres_reg_kernel<3, 1, true>;
+  switch (total) {
+    case 1: kern = attnres_reg_kernel<3, 1, true>; break;
+    case 2: kern = attnres_reg_kernel<3, 2, true>; break;
+    case 3: kern = attnres_reg_kernel<3, 3, true>; break;
+    case 4: kern = attnres_reg_kernel<3, 4, true>; break;
+    case 5: kern = attnres_reg_kernel<3, 5, true>; break;
+    case 6: kern = attnres_reg_kernel<3, 6, true>; break;
+    case 7: kern = attnres_reg_kernel<3, 7, true>; break;
+    case 8: kern = attnres_reg_kernel<3, 8, true>; break;
+    case 9: kern = attnres_reg_kernel<3, 9, true>; break;
+    default: kern = attnres_reg_kernel<3, 10, true>; break;
+  }
+  cudaError_t e = launch_pdl(kern, grid, dim3(kMixWarps * 32), 0, as_stream(stream), (const uint4*)bank, (int)sources,
+                             tokens, (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out,
+                             (const uint4*)norm_w, norm_eps);
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attnres_mix_rmsnorm: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }

@@ -183,6 +183,40 @@ def b200_attnres_mix(
     return output
 
 
+def b200_attnres_mix_rmsnorm(
+    bank: torch.Tensor,
+    partial: torch.Tensor | None,
+    weighted_query: torch.Tensor,
+    eps: float,
+    norm_weight: torch.Tensor,
+    norm_eps: float,
+    *,
+    output_buffer: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """rmsnorm(b200_attnres_mix(bank, partial, weighted_query, eps)) * norm_weight
+    in one kernel: the mixer and the RMSNorm that consumes its output in the Block
+    AttnRes layers. The mixer result itself is not returned."""
+    if not (bank.is_cuda and bank.dtype == torch.bfloat16 and bank.ndim == 3 and bank.is_contiguous()):
+        raise ValueError("bank must be a contiguous CUDA bf16 [S,N,D] tensor")
+    sources, tokens, hidden = bank.shape
+    if partial is not None and (partial.shape != bank.shape[1:] or not partial.is_contiguous()
+                                or partial.dtype != torch.bfloat16):
+        raise ValueError("partial must be a contiguous bf16 [N,D] tensor matching bank")
+    if weighted_query.shape != (hidden,) or weighted_query.dtype != torch.float32:
+        raise ValueError("weighted_query must be float32 [D]")
+    if norm_weight.shape != (hidden,) or norm_weight.dtype != torch.bfloat16 or not norm_weight.is_contiguous():
+        raise ValueError("norm_weight must be a contiguous bf16 [D] tensor")
+    output = torch.empty_like(bank[0]) if output_buffer is None else output_buffer
+    if output.shape != bank.shape[1:] or not output.is_contiguous():
+        raise ValueError("output_buffer must be a contiguous [N,D] tensor")
+    _lib.call(
+        "aiosb_attnres_mix_rmsnorm",
+        bank.data_ptr(), sources, tokens, hidden, _ptr(partial), weighted_query.contiguous().data_ptr(), float(eps),
+        norm_weight.data_ptr(), float(norm_eps), output.data_ptr(), _stream(bank.device),
+    )
+    return output
+
+
 # ---------------------------------------------------------------------------
 # Norms / activations / embedding (aios/layers/{norm,activation,embedding}.py)
 # ---------------------------------------------------------------------------

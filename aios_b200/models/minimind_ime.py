@@ -67,6 +67,17 @@ class BlockAttnResMixer(BaseOP):
         )
 
 
+def mix_and_norm(mixer: BlockAttnResMixer, norm: RMSNorm, bank: torch.Tensor, partial: torch.Tensor | None,
+                 output_buffer: torch.Tensor) -> torch.Tensor:
+    """norm(mixer(bank, partial)): one kernel when the sources fit the fused form
+    (<= 10 sources, hidden <= 768), else the mixer and the norm kernels."""
+    sources = bank.shape[0] + (partial is not None)
+    if sources <= 10 and bank.shape[-1] <= 768 and bank.shape[-1] % 8 == 0:
+        return ops.b200_attnres_mix_rmsnorm(bank, partial, mixer._routing_query(), mixer.key_norm.eps, norm.weight,
+                                           norm.eps, output_buffer=output_buffer)
+    return norm.forward(mixer.forward(bank, partial, output_buffer=output_buffer))
+
+
 class MiniMindAttnResDecoderLayer(BaseOP):
     """One attention/MLP pair that contributes deltas to its block's partial."""
 
@@ -78,10 +89,6 @@ class MiniMindAttnResDecoderLayer(BaseOP):
         self.attn_res_mixer = BlockAttnResMixer(config.hidden_size, config.rms_norm_eps, config.attnres_backend)
         self.mlp_res_mixer = BlockAttnResMixer(config.hidden_size, config.rms_norm_eps, config.attnres_backend)
 
-    def _attend_normed(self, hidden, rotary, paged_kv_cache, batch) -> torch.Tensor:
-        """input_layernorm + qkv projection (fused for <= 64 rows) + attention."""
-        return self.self_attn.attend(self.input_layernorm.forward(hidden), rotary, paged_kv_cache, batch)
-
     def forward(
         self,
         bank: torch.Tensor,
@@ -92,15 +99,16 @@ class MiniMindAttnResDecoderLayer(BaseOP):
         mixed: torch.Tensor,
         out: torch.Tensor | None = None,
     ) -> torch.Tensor:
-        hidden = self.attn_res_mixer.forward(bank, partial, output_buffer=mixed)
-        attn = self._attend_normed(hidden, rotary, paged_kv_cache, batch)
+        # the mixer writes the input-normalised rows straight away
+        normed = mix_and_norm(self.attn_res_mixer, self.input_layernorm, bank, partial, mixed)
+        attn = self.self_attn.attend(normed, rotary, paged_kv_cache, batch)
         w_o = self.self_attn.o_proj.weight
         if partial is None:
             partial = ops.linear(attn, w_o)
         else:
             ops.linear(attn, w_o, out=partial, epilogue=_lib.EPI_ADD, residual=partial)
-        hidden = self.mlp_res_mixer.forward(bank, partial, output_buffer=mixed)
-        act = self.mlp.gate_up_proj.forward_silu_mul(self.post_attention_layernorm.forward(hidden))
+        normed = mix_and_norm(self.mlp_res_mixer, self.post_attention_layernorm, bank, partial, mixed)
+        act = self.mlp.gate_up_proj.forward_silu_mul(normed)
         target = partial if out is None else out
         ops.linear(act, self.mlp.down_proj.weight, out=target, epilogue=_lib.EPI_ADD, residual=partial)
         return target
@@ -123,6 +131,11 @@ class MiniMindBlockAttnResModel(BaseOP):
 
     def forward_hidden(self) -> torch.Tensor:
         """Trunk up to the final mixer (before the final norm)."""
+        bank, mixed = self._trunk()
+        return self.final_attn_res_mixer.forward(bank, output_buffer=mixed)
+
+    def _trunk(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """Every block; returns the bank of block outputs and the mixer buffer."""
         ctx = get_global_ctx()
         batch = ctx.batch
         ids = batch.input_ids
@@ -145,10 +158,11 @@ class MiniMindBlockAttnResModel(BaseOP):
                     out=bank_storage[source_count] if index == last else None,
                 )
             source_count += 1
-        return self.final_attn_res_mixer.forward(bank_storage[:source_count], output_buffer=mixed)
+        return bank_storage[:source_count], mixed
 
     def forward(self) -> torch.Tensor:
-        return self.norm.forward(self.forward_hidden())
+        bank, mixed = self._trunk()
+        return mix_and_norm(self.final_attn_res_mixer, self.norm, bank, None, mixed)
 
 
 class MiniMindIMEForCausalLM(Qwen3ForCausalLM):

@@ -118,9 +118,9 @@ def keystroke_config():
                                max_new_tokens=12, temperature=0.8, top_k=50, top_p=0.9, seed=0)
 
 
-def prefixes(tokenizer, vocab: int, count: int, seed: int) -> list[str]:
+def prefixes(tokenizer, vocab: int, count: int, seed: int, length: int = 12) -> list[str]:
     g = torch.Generator().manual_seed(seed)
-    return [tokenizer.text_for(torch.randint(10, vocab, (12,), generator=g).tolist()) for _ in range(count)]
+    return [tokenizer.text_for(torch.randint(10, vocab, (length,), generator=g).tolist()) for _ in range(count)]
 
 
 # ---------------------------------------------------------------------------
@@ -378,6 +378,49 @@ def keystroke_stream(engine, llm, seed: int) -> dict:
     return out
 
 
+def _latencies(engine, texts: list[str], cfg, warmup: int) -> list:
+    results = []
+    for i, text in enumerate(texts):
+        engine.reset_prefix_cache()
+        r = engine.complete(text, cfg)
+        if i >= warmup:
+            results.append(r)
+    return results
+
+
+def config_sweeps(engine, llm, dev) -> dict:
+    """BASELINE configs 3 and 4 through ``complete``.
+    Config 3: the S10 keystroke at prefix lengths 4/8/16/32 after [BOS], 8
+    candidates x 16 tokens. Config 4: the S21 Block-AttnRes model (32 layers, 8
+    blocks, 65 mixers per forward), a 16-token prefix and refill rounds of 8 up to
+    24 candidates, each round freeing the previous round's suffix KV (a 2-character
+    candidate limit makes every candidate invalid, so the refill always runs to
+    the 24-attempt budget)."""
+    from aios_b200 import ImeCompletionEngine, ImeGenerationConfig, LLM
+    from aios_b200.models import shapes
+
+    out = {"s10_prefix_sweep": {}}
+    cfg3 = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=8, refill_batch_size=8,
+                               max_new_tokens=16, temperature=0.8, top_k=50, top_p=0.9, seed=0)
+    for n in (4, 8, 16, 32):
+        res = _latencies(engine, prefixes(llm.tokenizer, llm.config.vocab_size, 13, seed=77 + n, length=n), cfg3, 3)
+        lat = [r.latency_ms for r in res]
+        out["s10_prefix_sweep"][str(n)] = {"p50_ms": round(statistics.median(lat), 3),
+                                           "p95_ms": round(percentile(lat, 0.95), 3)}
+    llm21 = LLM(config=shapes.S21, seed=0, page_size=16, num_pages=256, device=str(dev))
+    eng21 = ImeCompletionEngine(llm21)
+    cfg4 = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=24, refill_batch_size=8,
+                               max_new_tokens=16, temperature=0.8, top_k=50, top_p=0.9, max_candidate_chars=2, seed=0)
+    res = _latencies(eng21, prefixes(llm21.tokenizer, llm21.config.vocab_size, 10, seed=21, length=16), cfg4, 2)
+    lat = [r.latency_ms for r in res]
+    out["s21_refill"] = {"p50_ms": round(statistics.median(lat), 3), "p95_ms": round(percentile(lat, 0.95), 3),
+                         "attempts": res[0].sampling_attempts, "refill_rounds": res[0].refill_rounds,
+                         "decode_tok_s": round(sum(r.generated_tokens for r in res) / (sum(r.gpu_latency_ms for r in res) * 1e-3), 1)}
+    del eng21, llm21
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch.distributed as dist
 
@@ -431,6 +474,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     roof = None if args.no_extras else decode_linear_roofline(llm, peaks)
     mixer = None if args.no_extras else mixer_chain(dev)
     kstream = None if args.no_extras else keystroke_stream(engine, llm, seed=4321 + rank)
+    sweeps = None if args.no_extras else config_sweeps(engine, llm, dev)
     lat = [r.latency_ms for r in results]
     gpu_lat = [r.gpu_latency_ms for r in results]
     gen = sum(r.generated_tokens for r in results)
@@ -459,6 +503,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "active_model_tok_s": round(active / (sum(gpu_lat) * 1e-3), 1),
         "mixer": mixer,
         "stream": kstream,
+        "configs": sweeps,
         "e2e": {"value": round(world * args.steps / wall, 3), "unit": "keystrokes/s",
                 "h2d_bytes_per_step": int(round(h2d)), "d2h_bytes_per_step": int(round(d2h))},
         "gpu_launches": launches,

@@ -88,6 +88,16 @@ AIOSB_API int aiosb_kv_store(void* k_cache, void* v_cache, int64_t cache_token_s
 AIOSB_API int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t tokens, int64_t hidden, const void* partial,
                       const float* weighted_query, float eps, void* out, void* stream);
 
+/* The mixer followed by the RMSNorm that consumes its output in the Block AttnRes
+ * layers (aios/models/minimind_ime.py, the input / post-attention norms after
+ * each mixer; aios/layers/norm.py:10-22): out = bf16(h * rcp * norm_w), h the
+ * bf16 mixer output of aiosb_attnres_mix, rcp = 1 / sqrt(mean(h^2) + norm_eps).
+ * The mixer result itself is not written. sources + (partial != NULL) <= 10,
+ * hidden <= 768 (a multiple of 8); norm_w: [hidden] bf16. */
+AIOSB_API int aiosb_attnres_mix_rmsnorm(const void* bank, int64_t sources, int64_t tokens, int64_t hidden,
+                                        const void* partial, const float* weighted_query, float eps,
+                                        const void* norm_w, float norm_eps, void* out, void* stream);
+
 /* ---- RMSNorm ---------------------------------------------------------------
  * Replaces aios/layers/norm.py:10-22 (RMSNorm.forward / forward_inplace, the
  * FlashInfer rmsnorm). Normalises rows of `hidden` elements:

@@ -156,6 +156,21 @@ def test_attnres_stream_kernel_matches_register_kernel(cuda_device, sources: int
     assert not torch.isnan(out.float()).any()
 
 
+@pytest.mark.parametrize("sources,tokens,partial", [(1, 8, False), (3, 8, True), (9, 8, True), (9, 1, False), (5, 17, True)])
+def test_attnres_mix_rmsnorm_matches_mix_then_norm(cuda_device, sources: int, tokens: int, partial: bool) -> None:
+    """The mixer with the consuming RMSNorm folded in equals the mixer followed by
+    the RMSNorm kernel: the mixer arithmetic is shared, only the sum of squares is
+    reduced in another order (1 bf16 ulp)."""
+    g = torch.Generator().manual_seed(31 + sources + tokens)
+    bank = torch.randn(sources, tokens, 768, generator=g).to(torch.bfloat16).to(cuda_device)
+    part = torch.randn(tokens, 768, generator=g).to(torch.bfloat16).to(cuda_device) if partial else None
+    wq = (torch.randn(768, generator=g) * 0.02).to(cuda_device)
+    nw = (1.0 + 0.1 * torch.randn(768, generator=g)).to(torch.bfloat16).to(cuda_device)
+    fused = ops.b200_attnres_mix_rmsnorm(bank, part, wq, 1e-6, nw, 1e-6)
+    want = ops.rmsnorm(ops.b200_attnres_mix(bank, part, wq, 1e-6), nw, 1e-6)
+    _bf16_close(fused, want, ulps=1.0)
+
+
 def test_attnres_mix_rejects_bad_layout(cuda_device) -> None:
     bank = torch.zeros(2, 3, 768, dtype=torch.bfloat16, device=cuda_device)
     wq = torch.zeros(768, device=cuda_device)
