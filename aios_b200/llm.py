@@ -16,10 +16,11 @@ from __future__ import annotations
 
 import os
 from dataclasses import replace
+from typing import List, Literal
 
 import torch
 
-from .core import Context, reset_global_ctx, set_global_ctx
+from .core import Context, SamplingParams, reset_global_ctx, set_global_ctx
 from .kvcache import MHAKVCache
 from .models import ModelConfig, create_model, init_synthetic_weights, load_weights
 from .models.shapes import shape as named_shape
@@ -112,3 +113,89 @@ class LLM:
         if pages <= 1:
             raise RuntimeError(f"Not enough GPU memory for KV cache (free={free_memory}, per_page={per_page})")
         return pages
+
+    @torch.no_grad()
+    def generate(
+        self,
+        prompts: List[str] | List[List[int]],
+        sampling_params: SamplingParams | List[SamplingParams] | None = None,
+        max_running_reqs: int | None = None,
+        prefill_token_budget: int | None = None,
+        debug_scheduler: bool = False,
+        prompt_mode: Literal["chat", "raw"] = "chat",
+        add_bos: bool = True,
+    ) -> List[dict]:
+        """Generates requests with continuous batching and varlen prefill
+        (aios/llm/llm.py:98-175) on the same kernels as the IME path: prefill-first
+        scheduling, one decode token per running request per step, KV slots
+        (page_size 1) freed as soon as a request finishes. Returns one dict per
+        prompt, in prompt order: uid, token_ids, text."""
+        from .engine.engine import Engine
+        from .scheduler.scheduler import Scheduler
+        from .scheduler.table import TableManager
+
+        if self.page_size != 1:
+            raise ValueError("generate uses page_size 1 KV slots (build the LLM with page_size=1)")
+        if sampling_params is None:
+            sampling_params = SamplingParams()
+        params_list = [sampling_params] * len(prompts) if isinstance(sampling_params, SamplingParams) else sampling_params
+        if len(params_list) != len(prompts):
+            raise ValueError("one SamplingParams per prompt")
+        vocab = self.config.vocab_size
+        for sp in params_list:  # the sampler's sort limit, checked before any KV is taken
+            k = min(sp.top_k, vocab) if sp.top_k > 0 else (vocab if sp.top_p < 1.0 else 0)
+            if not sp.is_greedy and k > 2048:
+                raise ValueError(f"sample: top-k/top-p candidate set of {k} exceeds the 2048-entry sort")
+        all_ids: List[torch.Tensor] = []
+        for prompt in prompts:
+            if isinstance(prompt, str):
+                if prompt_mode == "chat":
+                    if not hasattr(self.tokenizer, "apply_chat_template"):
+                        raise ValueError("chat prompts need a tokenizer with a chat template; use prompt_mode='raw'")
+                    text = self.tokenizer.apply_chat_template([{"role": "user", "content": prompt}], tokenize=False,
+                                                              add_generation_prompt=True, enable_thinking=False)
+                    ids = torch.tensor(self.tokenizer.encode(text), dtype=torch.long)
+                elif prompt_mode == "raw":
+                    token_ids = self.tokenizer.encode(prompt, add_special_tokens=False)
+                    if add_bos and self.tokenizer.bos_token_id is not None:
+                        token_ids = [self.tokenizer.bos_token_id, *token_ids]
+                    ids = torch.tensor(token_ids, dtype=torch.long)
+                else:
+                    raise ValueError(f"Unsupported prompt_mode: {prompt_mode}")
+            else:
+                ids = torch.tensor(prompt, dtype=torch.long)
+            all_ids.append(ids)
+        if not all_ids:
+            return []
+        # the decode attention kernel takes rows * (q heads per KV head) <= 64
+        row_limit = max(1, 64 // (self.config.num_qo_heads // self.config.num_kv_heads))
+        if max_running_reqs is None:
+            max_running_reqs = len(prompts)
+        max_running_reqs = max(1, min(max_running_reqs, len(prompts), row_limit))
+        max_total_len = max(len(ids) + sp.max_tokens for ids, sp in zip(all_ids, params_list))
+        if max_total_len > self.config.max_position_embeddings:
+            raise ValueError(f"prompt + max_tokens exceeds the context: {max_total_len}")
+        page_table = torch.zeros((max_running_reqs, max_total_len), dtype=torch.int32, device=self.device)
+        saved_table = self.ctx.page_table
+        self.ctx.page_table = page_table
+        try:
+            scheduler = Scheduler(table_manager=TableManager(max_running_reqs, page_table),
+                                  cache_manager=self.cache_manager, eos_token_id=self.tokenizer.eos_token_id,
+                                  device=self.device, max_running_reqs=max_running_reqs,
+                                  attn_backend=self.model.attn_backend, prefill_token_budget=prefill_token_budget)
+            engine = Engine(model=self.model, mha_kv_cache=self.mha_kv_cache)
+            for ids, sp in zip(all_ids, params_list):
+                scheduler.add_request(ids, sp)
+            iteration = 0
+            while scheduler.has_work:
+                batch = scheduler.schedule_next_batch()
+                if batch is None:
+                    raise RuntimeError("generate: pending requests do not fit the KV cache")
+                next_tokens = engine.run_batch(batch)
+                scheduler.process_batch_output(batch, next_tokens)
+                if debug_scheduler:
+                    print(f"[{iteration}] {scheduler.debug_state(batch)}")
+                iteration += 1
+            return scheduler.collect_results(self.tokenizer)
+        finally:
+            self.ctx.page_table = saved_table
