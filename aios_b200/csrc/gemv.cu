@@ -266,7 +266,15 @@ template <int NT, int KB, bool STAT>
 int launch_mma(const GemvArgs& a, cudaStream_t stream) {
   auto kern = gemv_mma_kernel<NT, KB, STAT>;
   const int64_t tiles = a.n_out / (a.epilogue == AIOSB_EPI_SILU_MUL ? 8 : 16);
-  const unsigned blocks = (unsigned)std::min<int64_t>(tiles, 2 * (int64_t)sm_count());
+  // as many CTAs as can be resident at once (each prefetches its first tile's
+  // weights before the wait; a CTA with more tiles loads the rest one ahead)
+  static int per_sm = 0;
+  if (per_sm == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, 0) != cudaSuccess || n < 1) n = 2;
+    per_sm = n;
+  }
+  const unsigned blocks = (unsigned)std::min<int64_t>(tiles, (int64_t)per_sm * sm_count());
   cudaError_t e = launch_pdl(kern, dim3(blocks), dim3(kGemvThreads), 0, stream, a);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "linear (gemv mma): %s", cudaGetErrorString(e));
   return AIOSB_OK;
