@@ -249,6 +249,40 @@ __device__ __forceinline__ uint32_t make_keys(const RowSmem& s, const RowRegs& r
   return best;
 }
 
+// Order keys of the unscaled values (forbidden -> -inf) for the sorted paths,
+// whose candidates are divided by the temperature only after selection. For
+// t > 0, v -> fl(v / t) is monotonic, and two distinct bf16 values differ by at
+// least 2^-8 relatively, so their fp32 quotients stay distinct unless the
+// quotient overflows, is subnormal (t >= 2^16) or the value is a NaN: ranking v
+// then ranks fl(v / t), ties included. `hazard` is set when a value of the row
+// is outside that range (|v| > big); the caller then uses make_keys.
+__device__ __forceinline__ uint32_t make_raw_keys(const RowSmem& s, const RowRegs& rr, uint32_t* keys, int V,
+                                                  float big, bool& hazard) {
+  const int ngroups = (V + 7) >> 3;
+  uint32_t best = 0u;
+  bool hz = false;
+#pragma unroll
+  for (int q = 0; q < kVecPer; ++q) {
+    const int j = threadIdx.x + q * kSampThreads;
+    if (j < ngroups) {
+      const uint32_t bits = s.ban[j >> 2] >> ((j & 3) * 8);
+#pragma unroll 1  // compact code: the step kernel runs cold each decode step
+      for (int e = 0; e < 8; ++e) {
+        float v = group_elem(rr.v[q], e);
+        if (8 * j + e < V) {
+          hz |= !(fabsf(v) <= big);  // NaN included
+          if ((bits >> e) & 1u) v = -INFINITY;
+          const uint32_t kk = order_key(v);
+          keys[8 * j + e] = kk;
+          best = kk > best ? kk : best;
+        }
+      }
+    }
+  }
+  hazard = hz;
+  return best;
+}
+
 // Greedy: first index of the maximum of the masked (unscaled) row (torch argmax).
 __device__ __forceinline__ int greedy_pick(RowSmem& s, const RowRegs& rr, int V) {
   const int ngroups = (V + 7) >> 3;
@@ -602,8 +636,22 @@ __device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, 
   }
   // the host rejects sorted candidate sets above kMaxSortK; never index past them
   if (sorted_path && k > kMaxSortK) k = kMaxSortK;
-  const uint32_t tmax = make_keys(s, rr, keys, V, p.temperature);
-  __syncthreads();
+  // Sorted paths rank the unscaled values and divide only the selected
+  // candidates (a block-wide check falls back to scaled keys, see make_raw_keys):
+  // 16384 divisions fewer per row. The raw keys' low 16 bits are all zeros or
+  // all ones (bf16 widened to fp32), so the bound below needs 16 bisection steps.
+  uint32_t tmax;
+  bool raw = false;
+  if (sorted_path) {
+    const float big = p.temperature < 65536.f ? 0x1.fffffep126f * p.temperature : -1.f;
+    bool hz;
+    tmax = make_raw_keys(s, rr, keys, V, big, hz);
+    raw = __syncthreads_or(hz) == 0;
+  }
+  if (!raw) {
+    tmax = make_keys(s, rr, keys, V, p.temperature);
+    __syncthreads();
+  }
   if (!sorted_path) {
     const auto val = [&](int i) { return key_value(keys[i]); };
     return pick_index(s, val, V, p.top_p, u);
@@ -615,7 +663,7 @@ __device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, 
     // in C = {key >= L}; |C| is close to k for non-degenerate rows. L by bisection
     // on the key bits with block-wide counts.
     uint32_t L = 0u;
-    for (int b = 31; b >= 0; --b) {
+    for (int b = 31; b >= (raw ? 16 : 0); --b) {
       const uint32_t c = L | (1u << b);
       if (__syncthreads_count(tmax >= c) >= k) L = c;
     }
@@ -658,7 +706,8 @@ __device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, 
   for (int i = tid; i < k; i += blockDim.x) {
     const unsigned long long c = s.cand[i];
     s.cid[i] = (int)(uint32_t)(c & 0xffffffffull);
-    s.cval[i] = key_value(~(uint32_t)(c >> 32));
+    const float v = key_value(~(uint32_t)(c >> 32));
+    s.cval[i] = raw ? v / p.temperature : v;  // the same fp32 division as make_keys
   }
   __syncthreads();
   const auto val = [&](int i) { return s.cval[i]; };
