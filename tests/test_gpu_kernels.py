@@ -366,6 +366,12 @@ SAMPLER_PATHS = [
     ("ragged_vocab", 6401, 0.8, 50, 0.9, "randn"),
     ("unaligned_row", 16384, 0.8, 50, 0.9, "unaligned"),
     ("greedy_unaligned", 6401, 1.0, 1, 1.0, "unaligned"),
+    # the sorted paths rank unscaled logits unless a value could make two scaled
+    # values collide: |v| near the fp32 limit for t < 2, t >= 2^16, -inf below t 2
+    ("huge_fallback", 16384, 0.5, 50, 0.9, "huge"),
+    ("high_temperature_fallback", 16384, 1e5, 50, 0.9, "randn"),
+    ("neg_inf_fallback", 16384, 0.8, 50, 0.9, "neginf"),
+    ("neg_inf_raw", 16384, 2.5, 50, 0.9, "neginf"),
 ]
 
 
@@ -379,6 +385,14 @@ def test_sampler_paths_bit_exact(cuda_device, name, vocab, temperature, top_k, t
         logits = torch.randint(-3, 4, (rows, vocab), generator=g).float().to(torch.bfloat16)
     elif mode == "spread":
         logits = (torch.randn(rows, vocab, generator=g) * 12.0).to(torch.bfloat16)
+    elif mode in ("huge", "neginf"):
+        logits = torch.randn(rows, vocab, generator=g) * 2.0
+        idx = torch.randint(0, vocab, (rows, 6), generator=g)
+        if mode == "huge":  # finite after scaling (|v| / t < 3.4e38), above the raw-key bound
+            vals = torch.tensor([1e38, -1e38, 6e37, 9e37, -5e37, 1.2e38]).expand(rows, 6)
+        else:
+            vals = torch.full((rows, 6), float("-inf"))
+        logits = logits.scatter(1, idx, vals).to(torch.bfloat16)
     else:
         logits = (torch.randn(rows, vocab, generator=g) * 2.0).to(torch.bfloat16)
     u = osamp.stateless_uniforms(list(range(77, 77 + rows)), 1)[:, 0]
