@@ -425,6 +425,14 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
     sin_r[i] = a.sin_tab[(int64_t)pos * D + i];
   }
   __syncthreads();
+  // the staged keys this row uses must be real slots (checked here, off the
+  // critical path; reported after the wait)
+  bool bad_slot = false;
+  if (warp == 0) {
+    bool b = false;
+    for (int j = lane; j < nst; j += 32) b |= slot_s[j] < 0 || slot_s[j] >= a.num_slots;
+    bad_slot = __any_sync(0xffffffffu, b);
+  }
   for (int i = threadIdx.x; i < nst * (D / 8); i += kDecThreads) {
     const int j = i / (D / 8), c = i % (D / 8);
     int64_t slot = slot_s[j];
@@ -483,11 +491,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
         }
       }
     }
-    if (threadIdx.x == 0) {  // the staged keys this row uses must be real slots
-      bool bad = false;
-      for (int j = 0; j < nst; ++j) bad |= slot_s[j] < 0 || slot_s[j] >= a.num_slots;
-      if (bad) report(a.status, AIOSB_DEV_SLOT_RANGE);
-    }
+    if (threadIdx.x == 0 && bad_slot) report(a.status, AIOSB_DEV_SLOT_RANGE);
   }
   __syncthreads();
 

@@ -271,6 +271,44 @@ def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int,
     _bf16_close(out.view(rows, hq, d), expected, ulps=2.0, atol=2e-3)
 
 
+@pytest.mark.parametrize("stable", [False, True])
+def test_decode_attention_reports_out_of_pool_slot(cuda_device, stable: bool) -> None:
+    """A page-table entry outside the KV pool is read as slot 0 (the kernel never
+    indexes past the pool) and reported through the status word."""
+    g = torch.Generator().manual_seed(11)
+    rows, hq, hkv, d, prefix, suffix = 8, 12, 4, 64, 13, 5
+    num_slots = 512
+    cos, sin, cos_b, sin_b = _rope_tables(d, 512, cuda_device)
+    perm = torch.randperm(num_slots, generator=g)
+    table = torch.zeros(rows, 256, dtype=torch.int32)
+    for r in range(rows):
+        table[r, :prefix] = perm[:prefix].to(torch.int32)
+        table[r, prefix : prefix + suffix] = perm[prefix + r * suffix : prefix + (r + 1) * suffix].to(torch.int32)
+    pos = prefix + suffix - 1
+    out_loc = table[:, pos].clone()
+    table[3, prefix + 1] = num_slots + 7  # an older suffix key of row 3
+    dev = cuda_device
+    ops.check_status(dev)  # start from a clean status word
+    out = torch.empty(rows, hq * d, dtype=torch.bfloat16, device=dev)
+    ops.attention_decode(
+        out=out, k_cache=torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16).to(dev),
+        v_cache=torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16).to(dev), page_table=table.to(dev),
+        row_table=torch.arange(rows, dtype=torch.int32, device=dev),
+        seq_lens=torch.full((rows,), pos + 1, dtype=torch.int32, device=dev),
+        positions=torch.full((rows,), pos, dtype=torch.int32, device=dev),
+        num_qo_heads=hq, num_kv_heads=hkv, head_dim=d, scale=d**-0.5,
+        qkv=torch.randn(rows, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16).to(dev),
+        q_norm_w=torch.ones(d, dtype=torch.bfloat16, device=dev), k_norm_w=torch.ones(d, dtype=torch.bfloat16, device=dev),
+        eps=1e-6, cos=cos_b, sin=sin_b, out_loc=out_loc.to(dev),
+        prefix_len=torch.tensor([prefix], dtype=torch.int32, device=dev),
+        active=torch.ones(rows, dtype=torch.int32, device=dev), stable_history=stable,
+    )
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="KV slot index outside the pool"):
+        ops.check_status(dev)
+    ops.check_status(dev)  # the status word was reset
+
+
 @pytest.mark.parametrize("hq,hkv,d", [(12, 4, 64), (8, 2, 96)])
 def test_prefill_attention_with_cached_prefix(cuda_device, hq: int, hkv: int, d: int) -> None:
     g = torch.Generator().manual_seed(21 + d)
