@@ -65,16 +65,36 @@ class CandidateGroupRuntime:
         self.max_banned_width = max_banned_width
         self.vocab = llm.config.vocab_size
         i32 = dict(dtype=torch.int32, device=dev)
-        self.state = torch.zeros(ctypes.sizeof(_lib.GroupState), dtype=torch.uint8, device=dev)
+        # The state and the round's results share one device block, so that the
+        # round ends with one device-to-host copy (plus the status word):
+        # [state | output_ids | token_logprobs | counts | logprob_sums | stop_codes]
+        state_size = ctypes.sizeof(_lib.GroupState)
+        state_words = (state_size + 7) // 8 * 2  # keeps every part 8-byte aligned
+        rs = max_rows * max_steps
+        self._out_offsets = offs = {}
+        total = 0
+        for name, words in (("state", state_words), ("ids", rs), ("lp", rs), ("counts", max_rows),
+                            ("sums", max_rows), ("stops", max_rows)):
+            offs[name] = total
+            total += words
+        self._out_dev = torch.zeros(total, **i32)
+        self._out_host = torch.zeros(total, dtype=torch.int32).pin_memory()
+        self._status_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+        def part(buf, name, words, dtype=torch.int32):
+            return buf[offs[name] : offs[name] + words].view(dtype)
+
+        self._out_part = part
+        self.state = part(self._out_dev, "state", state_words).view(torch.uint8)[:state_size]
         self._state_host = torch.zeros(ctypes.sizeof(_lib.GroupState), dtype=torch.uint8).pin_memory()
         self._state_struct = _lib.GroupState.from_address(self._state_host.data_ptr())
         self.logits = torch.zeros((max_rows, self.vocab), dtype=torch.bfloat16, device=dev)
         self.uniforms = torch.zeros((max_rows, max_steps), dtype=torch.float32, device=dev)
-        self.output_ids = torch.zeros((max_rows, max_steps), **i32)
-        self.token_logprobs = torch.zeros((max_rows, max_steps), dtype=torch.float32, device=dev)
-        self.counts = torch.zeros(max_rows, **i32)
-        self.logprob_sums = torch.zeros(max_rows, dtype=torch.float32, device=dev)
-        self.stop_codes = torch.zeros(max_rows, **i32)
+        self.output_ids = part(self._out_dev, "ids", rs).view(max_rows, max_steps)
+        self.token_logprobs = part(self._out_dev, "lp", rs, torch.float32).view(max_rows, max_steps)
+        self.counts = part(self._out_dev, "counts", max_rows)
+        self.logprob_sums = part(self._out_dev, "sums", max_rows, torch.float32)
+        self.stop_codes = part(self._out_dev, "stops", max_rows)
         self.active = torch.zeros(max_rows, **i32)
         self.finished = torch.zeros(max_rows, **i32)
         self.tokens = torch.zeros(max_rows, **i32)
@@ -93,12 +113,6 @@ class CandidateGroupRuntime:
         self.cancel_flag = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.host_mirror = torch.zeros(4, dtype=torch.int32).pin_memory()
         self._mirror_np = self.host_mirror.numpy()
-        # results read back once per round
-        self._res_ids = torch.zeros((max_rows, max_steps), dtype=torch.int32).pin_memory()
-        self._res_lp = torch.zeros((max_rows, max_steps), dtype=torch.float32).pin_memory()
-        self._res_rows = torch.zeros((3, max_rows), dtype=torch.int32).pin_memory()
-        self._res_sums = torch.zeros(max_rows, dtype=torch.float32).pin_memory()
-        self._res_state = torch.zeros_like(self._state_host).pin_memory()
         self._done_event = torch.cuda.Event()
         state_i32 = self.state.view(torch.int32)
         self.prefix_len_view = state_i32[3:4]  # aiosb_group_state.prefix_len (offset 12)
@@ -290,28 +304,32 @@ class CandidateGroupRuntime:
             launched += 1
         # [rows, steps] arrays use the round's max_new_tokens as their row stride
         n = attempts * max_new_tokens
-        self._res_ids.view(-1)[:n].copy_(self.output_ids.view(-1)[:n], non_blocking=True)
-        self._res_lp.view(-1)[:n].copy_(self.token_logprobs.view(-1)[:n], non_blocking=True)
-        self._res_rows[0, :attempts].copy_(self.counts[:attempts], non_blocking=True)
-        self._res_rows[1, :attempts].copy_(self.stop_codes[:attempts], non_blocking=True)
-        self._res_sums[:attempts].copy_(self.logprob_sums[:attempts], non_blocking=True)
-        self._res_state.copy_(self.state, non_blocking=True)
-        self.d2h_bytes += 8 * n + 12 * attempts + self._res_state.numel()
+        # one copy of the result block and one of the status word: the status is
+        # checked from the host copy, without a second synchronising read
+        self._out_host.copy_(self._out_dev, non_blocking=True)
+        self._status_host.copy_(ops.status_word(self.device), non_blocking=True)
+        self.d2h_bytes += 4 * (self._out_host.numel() + 1)
         self._done_event.record()
         self._done_event.synchronize()
         if cancellation is not None:
             cancellation._detach_flag(self.cancel_flag)
-        ops.check_status(self.device)
-        final = _lib.GroupState.from_buffer_copy(self._res_state.numpy().tobytes())
+        if int(self._status_host[0]) != 0:
+            ops.check_status(self.device)  # raises, and resets the word
+        host = self._out_host
+        part = self._out_part
+        state_words = self._out_offsets["ids"]
+        final = _lib.GroupState.from_buffer_copy(part(host, "state", state_words).numpy().tobytes())
+        res_ids = part(host, "ids", n).numpy()
+        res_lp = part(host, "lp", n, torch.float32).numpy()
         consumed = int(final.head) - head0
         cm.advance_head(int(final.head))
         host_cancelled = cancellation is not None and cancellation.cancelled and launched < max_new_tokens
         result = RoundResult(
-            output_ids=self._res_ids.view(-1)[:n].numpy().reshape(attempts, max_new_tokens).copy(),
-            token_logprobs=self._res_lp.view(-1)[:n].numpy().reshape(attempts, max_new_tokens).copy(),
-            counts=self._res_rows[0, :attempts].tolist(),
-            logprob_sums=self._res_sums[:attempts].tolist(),
-            stop_codes=self._res_rows[1, :attempts].tolist(),
+            output_ids=res_ids.reshape(attempts, max_new_tokens).copy(),
+            token_logprobs=res_lp.reshape(attempts, max_new_tokens).copy(),
+            counts=part(host, "counts", attempts).tolist(),
+            logprob_sums=part(host, "sums", attempts, torch.float32).tolist(),
+            stop_codes=part(host, "stops", attempts).tolist(),
             pages_consumed=consumed,
             active_model_tokens=int(final.active_model_tokens),
             cancelled=bool(final.cancelled) or host_cancelled,
