@@ -148,6 +148,11 @@ _SIGNATURES = {
          _p, _p],
         _i32,
     ),
+    "aiosb_attention_prefill_fused": (
+        [_p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64,
+         _i64, _i64, _i64, _i64, _f32, _p, _i64, _p, _p],
+        _i32,
+    ),
     "aiosb_sample": (
         [_p, _i64, _i64, _i64, _f32, _i64, _f32, _i32, _p, _p, _i64, _p, _i64, _p, _p, _p, _p],
         _i32,

@@ -43,6 +43,7 @@ class B200AttentionMetadata(BaseAttentionMetadata):
     num_requests: int = 0
     num_tiles: int = 0
     tile_tokens: int = 0
+    max_q_len: int = 0  # longest request of a prefill batch (new tokens); 0 = unknown
     row_table: torch.Tensor | None = None  # int32 [rows] (decode)
     seq_lens: torch.Tensor | None = None  # int32 [rows] (decode)
     prefix_len: torch.Tensor | None = None  # int32 [1]: shared prefix keys (decode)
@@ -102,6 +103,7 @@ class B200AttentionBackend(BaseAttentionBackend):
                 num_requests=len(reqs),
                 num_tiles=num_tiles,
                 tile_tokens=self.tile_tokens,
+                max_q_len=max(q_lens, default=0),
             )
         else:
             packed = _to_device_i32([int(r.table_idx) for r in reqs] + [r.device_len for r in reqs], device)
@@ -133,6 +135,16 @@ class B200AttentionBackend(BaseAttentionBackend):
         tokens = qkv.shape[0]
         out = torch.empty((tokens, self.num_heads * self.head_dim), dtype=qkv.dtype, device=qkv.device)
         kc, vc = paged_kv_cache.k_slots(layer_id), paged_kv_cache.v_slots(layer_id)
+        if md.phase == "prefill" and 1 <= md.max_q_len <= ops.FUSED_PREFILL_MAX_TOKENS:
+            # short requests (a keystroke's prefix): norm, RoPE, K/V store and
+            # attention in one launch; every cached key came from an earlier forward
+            return ops.attention_prefill_fused(
+                qkv=qkv, out=out, q_norm_w=q_norm_w, k_norm_w=k_norm_w, eps=self.eps, cos=cos, sin=sin,
+                positions=md.positions, out_loc=md.out_loc, k_cache=kc, v_cache=vc, page_table=ctx.page_table,
+                meta=md.meta, num_requests=md.num_requests, num_tiles=md.num_tiles, tile_tokens=md.tile_tokens,
+                max_q_len=md.max_q_len, num_qo_heads=self.num_heads, num_kv_heads=self.num_kv_heads,
+                head_dim=self.head_dim, scale=self.sm_scale,
+            )
         if md.phase == "prefill":
             qbuf = torch.empty_like(out)
             ops.qk_norm_rope_store(

@@ -958,3 +958,284 @@ extern "C" int aiosb_attention_prefill(const void* q, int64_t q_stride, const vo
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attention_prefill: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }
+
+namespace aiosb {
+namespace {
+
+// ---- fused prefill: q/k RMSNorm + RoPE + K/V store + causal attention -------
+// For requests of at most kKeyChunk new tokens (a keystroke's prefix prefill).
+// CTA (KV head h, tile) normalises and rotates its own queries and the new keys
+// of its causal window (the request's first q0 + nq new tokens; tiles of one
+// request repeat that small work), and stores the K/V of its own tile's tokens.
+// Keys are folded in the same 64-key chunks as attn_prefill_kernel, each taken
+// from the cache (cached prefix) or from the new-key rows in shared memory, so
+// the output equals qk_norm_rope_store_kernel followed by attn_prefill_kernel
+// bit for bit, one launch and one kernel boundary fewer per layer.
+struct FusedPrefillArgs {
+  const __nv_bfloat16* qkv;  // [tokens, qkv_stride]: q heads | k heads | v heads (raw projection)
+  int64_t qkv_stride;
+  const __nv_bfloat16* q_norm_w;
+  const __nv_bfloat16* k_norm_w;
+  float eps;
+  const __nv_bfloat16* cos_tab;  // [max_pos, D]
+  const __nv_bfloat16* sin_tab;
+  int max_pos;
+  const int32_t* positions;  // [tokens]
+  const int32_t* out_loc;    // [tokens]
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  int64_t num_slots;
+  const int32_t* page_table;
+  int64_t table_stride;
+  const int32_t* req_q_start;
+  const int32_t* req_q_len;
+  const int32_t* req_cached_len;
+  const int32_t* req_table_row;
+  const int32_t* tile_req;
+  const int32_t* tile_q0;
+  int tile_tokens;
+  int hq, hkv;
+  float scale;
+  __nv_bfloat16* out;
+  int64_t out_stride;
+  int32_t* status;
+};
+
+template <int D>
+size_t fused_prefill_smem(int queries) {
+  // q_s | Ks | Vs | NK | NV | warp scratch | raw rows (queries + new keys) | cos | sin | norm weights | positions
+  return (size_t)queries * D * 4 + (size_t)kKeyChunk * (D + 2) * 2 + (size_t)kKeyChunk * D * 2 * 3 +
+         (size_t)kAttnWarps * D * 4 + (size_t)(queries + kKeyChunk) * D * 2 + (size_t)kKeyChunk * D * 2 * 2 +
+         (size_t)D * 2 * 2 + (size_t)kKeyChunk * 4;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads) attn_prefill_fused_kernel(const FusedPrefillArgs a) {
+  constexpr int DPL = D / 32;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int h = blockIdx.x;
+  const int tile = blockIdx.y;
+  const int g = a.hq / a.hkv;
+  const int Qmax = a.tile_tokens * g;
+  float* q_s = reinterpret_cast<float*>(smem_raw);                                // [Qmax][D]
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(q_s + Qmax * D);            // [kKeyChunk][D + 2]
+  __nv_bfloat16* Vs = Ks + kKeyChunk * (D + 2);                                     // [kKeyChunk][D]
+  __nv_bfloat16* NK = Vs + kKeyChunk * D;                                           // new keys, rotated
+  __nv_bfloat16* NV = NK + kKeyChunk * D;                                           // new values
+  float* tmp = reinterpret_cast<float*>(NV + kKeyChunk * D);                        // [warps][D]
+  __nv_bfloat16* RAW = reinterpret_cast<__nv_bfloat16*>(tmp + kAttnWarps * D);      // [Qmax + kKeyChunk][D]
+  __nv_bfloat16* CS = RAW + (Qmax + kKeyChunk) * D;                                  // [kKeyChunk][D]
+  __nv_bfloat16* SN = CS + kKeyChunk * D;                                            // [kKeyChunk][D]
+  __nv_bfloat16* NQW = SN + kKeyChunk * D;                                           // [D]
+  __nv_bfloat16* NKW = NQW + D;                                                      // [D]
+  int* pos_s = reinterpret_cast<int*>(NKW + D);                                      // [kKeyChunk]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t tok_stride = (int64_t)a.hkv * D;
+
+  pdl_enter();
+  const int req = a.tile_req[tile];
+  const int q0 = a.tile_q0[tile];
+  const int qlen = a.req_q_len[req];
+  const int nq = min(a.tile_tokens, qlen - q0);
+  const int cached = a.req_cached_len[req];
+  const int64_t qbase = a.req_q_start[req];
+  const int32_t* slots = a.page_table + (int64_t)a.req_table_row[req] * a.table_stride;
+  const int nnew = q0 + nq;  // new keys in this tile's causal window
+  if (nnew > kKeyChunk) {    // the host admits only requests of <= kKeyChunk new tokens
+    if (threadIdx.x == 0) report(a.status, AIOSB_DEV_POSITION_RANGE);
+    return;
+  }
+  const int Q = nq * g;
+  // ---- prologue. Item it < Q is query (token q0 + it / g, head h * g + it % g);
+  // the others are new key rows 0 .. nnew - 1 of KV head h. Every input is first
+  // staged in two cooperative rounds (projection rows, values, positions and
+  // norm weights; then the RoPE rows of those positions), so that the per-item
+  // work reads shared memory only.
+  constexpr int kVec = D / 8;  // 16-byte vectors per head row
+  const uint4* qkv4 = reinterpret_cast<const uint4*>(a.qkv);
+  const int64_t row4 = a.qkv_stride / 8;
+  for (int idx = threadIdx.x; idx < (Q + 2 * nnew) * kVec; idx += blockDim.x) {
+    const int it = idx / kVec, c = idx % kVec;
+    int j, hh;
+    uint4* dst;
+    if (it < Q) {
+      j = q0 + it / g, hh = h * g + it % g, dst = reinterpret_cast<uint4*>(RAW + it * D);
+    } else if (it < Q + nnew) {
+      j = it - Q, hh = a.hq + h, dst = reinterpret_cast<uint4*>(RAW + it * D);
+    } else {
+      j = it - Q - nnew, hh = a.hq + a.hkv + h, dst = reinterpret_cast<uint4*>(NV + j * D);
+    }
+    dst[c] = qkv4[(qbase + j) * row4 + (int64_t)hh * kVec + c];
+  }
+  for (int j = threadIdx.x; j < nnew; j += blockDim.x) {
+    int pos = a.positions[qbase + j];
+    if (pos < 0 || pos >= a.max_pos) {
+      report(a.status, AIOSB_DEV_POSITION_RANGE);
+      pos = 0;
+    }
+    pos_s[j] = pos;
+  }
+  for (int i = threadIdx.x; i < D; i += blockDim.x) {
+    NQW[i] = a.q_norm_w[i];
+    NKW[i] = a.k_norm_w[i];
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < nnew * kVec; idx += blockDim.x) {
+    const int j = idx / kVec, c = idx % kVec;
+    const int64_t pr = (int64_t)pos_s[j] * kVec + c;
+    reinterpret_cast<uint4*>(CS + j * D)[c] = reinterpret_cast<const uint4*>(a.cos_tab)[pr];
+    reinterpret_cast<uint4*>(SN + j * D)[c] = reinterpret_cast<const uint4*>(a.sin_tab)[pr];
+  }
+  __syncthreads();
+  for (int it = warp; it < Q + nnew; it += kAttnWarps) {
+    const bool is_q = it < Q;
+    const int j = is_q ? q0 + it / g : it - Q;  // token index within the request
+    const int64_t t = qbase + j;
+    float x[DPL];
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) x[i] = bf16_to_f(RAW[it * D + i * 32 + lane]);
+    norm_rope<D>(x, is_q ? NQW : NKW, a.eps, CS + j * D, SN + j * D, true, true, lane, tmp + warp * D);
+    if (is_q) {
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) q_s[it * D + i * 32 + lane] = x[i];
+      continue;
+    }
+    // this tile's own tokens go to the cache (each token belongs to one tile)
+    const bool own = j >= q0;
+    const int64_t slot = own ? a.out_loc[t] : -1;
+    const bool slot_ok = slot >= 0 && slot < a.num_slots;
+    if (own && !slot_ok && lane == 0) report(a.status, AIOSB_DEV_SLOT_RANGE);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) {
+      const __nv_bfloat16 kb = f_to_bf16(x[i]);
+      const __nv_bfloat16 vb = NV[j * D + i * 32 + lane];
+      NK[j * D + i * 32 + lane] = kb;
+      if (slot_ok) {
+        a.k_cache[slot * tok_stride + (int64_t)h * D + i * 32 + lane] = kb;
+        a.v_cache[slot * tok_stride + (int64_t)h * D + i * 32 + lane] = vb;
+      }
+    }
+  }
+  QState<D> st[kMaxQPerWarp];
+#pragma unroll
+  for (int s = 0; s < kMaxQPerWarp; ++s) qstate_init<D>(st[s]);
+  __syncthreads();
+
+  const int kv_end = cached + nnew;
+  for (int k0 = 0; k0 < kv_end; k0 += kKeyChunk) {
+    const int nk = min(kKeyChunk, kv_end - k0);
+    const int nc = max(0, min(nk, cached - k0));  // keys of this chunk in the cache
+    if (nc > 0) stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, slots, k0, nc, a.num_slots, Ks, Vs, a.status);
+    constexpr int kWords = D / 2;
+    for (int idx = threadIdx.x; idx < (nk - nc) * kWords; idx += blockDim.x) {
+      const int jj = idx / kWords, w = idx % kWords;
+      const int src = k0 + nc + jj - cached;  // new-key row
+      reinterpret_cast<uint32_t*>(Ks)[(nc + jj) * (kWords + 1) + w] = reinterpret_cast<const uint32_t*>(NK + src * D)[w];
+      reinterpret_cast<uint32_t*>(Vs)[(nc + jj) * kWords + w] = reinterpret_cast<const uint32_t*>(NV + src * D)[w];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int s = 0; s < kMaxQPerWarp; ++s) {
+      const int qi = warp + s * kAttnWarps;
+      if (qi < Q) {
+        const int qpos = cached + q0 + qi / g;  // absolute position of this query
+        const float* qv = q_s + qi * D;
+        const __nv_bfloat162* K2 = reinterpret_cast<const __nv_bfloat162*>(Ks);
+        const int kp0 = k0 + lane, kp1 = k0 + lane + 32;
+        const float s0 = (lane < nk && kp0 <= qpos) ? dot_q_k<D>(qv, K2 + lane * (D / 2 + 1)) * a.scale : -INFINITY;
+        const float s1 =
+            (lane + 32 < nk && kp1 <= qpos) ? dot_q_k<D>(qv, K2 + (lane + 32) * (D / 2 + 1)) * a.scale : -INFINITY;
+        fold_scores<D>(st[s], s0, s1, nk, [&](int jv, int i) { return bf16_to_f(Vs[jv * D + i * 32 + lane]); });
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int s = 0; s < kMaxQPerWarp; ++s) {
+    const int qi = warp + s * kAttnWarps;
+    if (qi < Q) {
+      const int t = qi / g, j = qi % g;
+      const float inv = st[s].l > 0.f ? 1.0f / st[s].l : 0.f;
+      __nv_bfloat16* dst = a.out + (qbase + q0 + t) * a.out_stride + (int64_t)(h * g + j) * D;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st[s].acc[i] * inv);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace aiosb
+
+extern "C" int aiosb_attention_prefill_fused(
+    const void* qkv, int64_t qkv_stride, const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_tab,
+    const void* sin_tab, int64_t max_pos, const int32_t* positions, const int32_t* out_loc, void* k_cache,
+    void* v_cache, int64_t num_slots, const int32_t* page_table, int64_t table_stride, const int32_t* req_q_start,
+    const int32_t* req_q_len, const int32_t* req_cached_len, const int32_t* req_table_row, const int32_t* tile_req,
+    const int32_t* tile_q0, int64_t num_tiles, int64_t tile_tokens, int64_t max_q_len, int64_t num_qo_heads,
+    int64_t num_kv_heads, int64_t head_dim, float scale, void* out, int64_t out_stride, int32_t* status,
+    void* stream) {
+  AIOSB_REQUIRE(num_tiles >= 0 && num_kv_heads > 0 && num_qo_heads % num_kv_heads == 0, AIOSB_ERR_INVALID_ARG,
+                "query head count must be divisible by KV head count");
+  AIOSB_REQUIRE(head_dim == 64 || head_dim == 96 || head_dim == 128, AIOSB_ERR_UNSUPPORTED,
+                "attention_prefill_fused: head_dim %lld unsupported (64, 96, 128)", (long long)head_dim);
+  AIOSB_REQUIRE(max_q_len >= 0 && max_q_len <= kKeyChunk, AIOSB_ERR_UNSUPPORTED,
+                "attention_prefill_fused: requests of at most %d new tokens (got %lld)", kKeyChunk,
+                (long long)max_q_len);
+  const int64_t g = num_qo_heads / num_kv_heads;
+  AIOSB_REQUIRE(tile_tokens >= 1 && tile_tokens * g <= kMaxQueries, AIOSB_ERR_INVALID_ARG,
+                "attention_prefill_fused: tile_tokens * group must be in [1, %d]", kMaxQueries);
+  if (num_tiles == 0) return AIOSB_OK;
+  AIOSB_REQUIRE(qkv && q_norm_w && k_norm_w && cos_tab && sin_tab && positions && out_loc && k_cache && v_cache &&
+                    page_table && req_q_start && req_q_len && req_cached_len && req_table_row && tile_req &&
+                    tile_q0 && out,
+                AIOSB_ERR_INVALID_ARG, "attention_prefill_fused: null pointer");
+  // the prologue stages projection and RoPE rows with 16-byte loads
+  AIOSB_REQUIRE(qkv_stride % 8 == 0 && ((uintptr_t)qkv & 15u) == 0 && ((uintptr_t)cos_tab & 15u) == 0 &&
+                    ((uintptr_t)sin_tab & 15u) == 0,
+                AIOSB_ERR_MISALIGNED, "attention_prefill_fused: qkv rows and RoPE tables must be 16-byte aligned");
+  FusedPrefillArgs a;
+  a.qkv = (const __nv_bfloat16*)qkv;
+  a.qkv_stride = qkv_stride;
+  a.q_norm_w = (const __nv_bfloat16*)q_norm_w;
+  a.k_norm_w = (const __nv_bfloat16*)k_norm_w;
+  a.eps = eps;
+  a.cos_tab = (const __nv_bfloat16*)cos_tab;
+  a.sin_tab = (const __nv_bfloat16*)sin_tab;
+  a.max_pos = (int)max_pos;
+  a.positions = positions;
+  a.out_loc = out_loc;
+  a.k_cache = (__nv_bfloat16*)k_cache;
+  a.v_cache = (__nv_bfloat16*)v_cache;
+  a.num_slots = num_slots;
+  a.page_table = page_table;
+  a.table_stride = table_stride;
+  a.req_q_start = req_q_start;
+  a.req_q_len = req_q_len;
+  a.req_cached_len = req_cached_len;
+  a.req_table_row = req_table_row;
+  a.tile_req = tile_req;
+  a.tile_q0 = tile_q0;
+  a.tile_tokens = (int)tile_tokens;
+  a.hq = (int)num_qo_heads;
+  a.hkv = (int)num_kv_heads;
+  a.scale = scale;
+  a.out = (__nv_bfloat16*)out;
+  a.out_stride = out_stride;
+  a.status = status;
+  const int Q = (int)(tile_tokens * g);
+  const dim3 grid((unsigned)num_kv_heads, (unsigned)num_tiles), block(kAttnThreads);
+  cudaStream_t s = as_stream(stream);
+  cudaError_t e;
+  if (head_dim == 64) {
+    allow_smem(attn_prefill_fused_kernel<64>, fused_prefill_smem<64>(kMaxQueries));
+    e = launch_pdl(attn_prefill_fused_kernel<64>, grid, block, fused_prefill_smem<64>(Q), s, a);
+  } else if (head_dim == 96) {
+    allow_smem(attn_prefill_fused_kernel<96>, fused_prefill_smem<96>(kMaxQueries));
+    e = launch_pdl(attn_prefill_fused_kernel<96>, grid, block, fused_prefill_smem<96>(Q), s, a);
+  } else {
+    allow_smem(attn_prefill_fused_kernel<128>, fused_prefill_smem<128>(kMaxQueries));
+    e = launch_pdl(attn_prefill_fused_kernel<128>, grid, block, fused_prefill_smem<128>(Q), s, a);
+  }
+  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attention_prefill_fused: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}

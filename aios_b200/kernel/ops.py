@@ -609,6 +609,53 @@ def qk_norm_rope_store(
     return q_out
 
 
+FUSED_PREFILL_MAX_TOKENS = 64  # new tokens per request on the fused prefill
+
+
+def attention_prefill_fused(
+    *,
+    qkv: torch.Tensor,
+    out: torch.Tensor,
+    q_norm_w: torch.Tensor,
+    k_norm_w: torch.Tensor,
+    eps: float,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    positions: torch.Tensor,
+    out_loc: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    page_table: torch.Tensor,
+    meta: torch.Tensor,
+    num_requests: int,
+    num_tiles: int,
+    tile_tokens: int,
+    max_q_len: int,
+    num_qo_heads: int,
+    num_kv_heads: int,
+    head_dim: int,
+    scale: float,
+) -> torch.Tensor:
+    """``qk_norm_rope_store`` and ``attention_prefill`` in one launch, for
+    requests of at most FUSED_PREFILL_MAX_TOKENS new tokens whose cached keys were
+    written by earlier launches; ``meta`` as for ``attention_prefill``. The output
+    and the stored K/V equal the two-call path bit for bit."""
+    _require_cuda(qkv, out, k_cache, v_cache, page_table, meta, what="attention_prefill_fused")
+    num_slots = k_cache.numel() // (num_kv_heads * head_dim)
+    base = meta.data_ptr()
+    r = num_requests * 4
+    _lib.call(
+        "aiosb_attention_prefill_fused",
+        qkv.data_ptr(), qkv.stride(0), q_norm_w.data_ptr(), k_norm_w.data_ptr(), float(eps),
+        cos.data_ptr(), sin.data_ptr(), cos.shape[0], positions.data_ptr(), out_loc.data_ptr(),
+        k_cache.data_ptr(), v_cache.data_ptr(), num_slots, page_table.data_ptr(), page_table.stride(0),
+        base, base + r, base + 2 * r, base + 3 * r, base + 4 * r, base + 4 * r + num_tiles * 4,
+        num_tiles, tile_tokens, max_q_len, num_qo_heads, num_kv_heads, head_dim, float(scale),
+        out.data_ptr(), out.stride(0), status_word(qkv.device).data_ptr(), _stream(qkv.device),
+    )
+    return out
+
+
 def prefill_tile_tokens(num_qo_heads: int, num_kv_heads: int) -> int:
     n = _lib.load().aiosb_prefill_tile_tokens(num_qo_heads, num_kv_heads)
     if n <= 0:

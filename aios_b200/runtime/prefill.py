@@ -61,7 +61,7 @@ class PrefixRunner:
         batch.attn_metadata = B200AttentionMetadata(
             phase="prefill", positions=batch.positions, out_loc=batch.out_loc, last_rows=(n - 1,),
             meta=d[self.off_meta : self.off_meta + 4 + 2 * tiles], num_requests=1, num_tiles=tiles,
-            tile_tokens=self.tile_tokens,
+            tile_tokens=self.tile_tokens, max_q_len=n,
         )
         return batch
 

@@ -254,6 +254,24 @@ AIOSB_API int aiosb_attention_prefill(const void* q, int64_t q_stride, const voi
                             int64_t head_dim, float scale, void* out, int64_t out_stride, int32_t* status,
                             void* stream);
 
+/* Fused prefill: aiosb_qk_norm_rope_store followed by aiosb_attention_prefill in
+ * one launch (aios/layers/attention.py:6-16 and 55-79 with
+ * aios/attention/flashinfer.py:300-326), for batches whose requests have at most
+ * max_q_len <= 64 new tokens (a keystroke's prefix prefill). qkv holds the raw
+ * projection rows of the new tokens; each tile normalises and rotates its
+ * queries and the new keys of its causal window, stores the K/V of its own
+ * tokens at out_loc, and reads cached keys (positions below cached_len) from the
+ * paged cache. Those cached keys must come from earlier launches. The output
+ * and the stored K/V equal the two-call path bit for bit. */
+AIOSB_API int aiosb_attention_prefill_fused(
+    const void* qkv, int64_t qkv_stride, const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_tab,
+    const void* sin_tab, int64_t max_pos, const int32_t* positions, const int32_t* out_loc, void* k_cache,
+    void* v_cache, int64_t num_slots, const int32_t* page_table, int64_t table_stride, const int32_t* req_q_start,
+    const int32_t* req_q_len, const int32_t* req_cached_len, const int32_t* req_table_row, const int32_t* tile_req,
+    const int32_t* tile_q0, int64_t num_tiles, int64_t tile_tokens, int64_t max_q_len, int64_t num_qo_heads,
+    int64_t num_kv_heads, int64_t head_dim, float scale, void* out, int64_t out_stride, int32_t* status,
+    void* stream);
+
 /* ---- Sampler -----------------------------------------------------------------
  * Replaces aios/engine/sample.py:54-163 (Sampler.sample_with_logprobs with
  * uniforms): per row, raw log-softmax of the bf16 logits, forbidden ids (the

@@ -60,6 +60,22 @@ def test_incremental_prefix_reuses_token_lcp(engine) -> None:
     assert [c.text for c in extended.raw_candidates] == [c.text for c in repeated.raw_candidates]
 
 
+def test_long_prefix_prefill_then_short_extension(engine) -> None:
+    """A 100-token prefix prefills more than 64 new tokens (norm/RoPE/store and
+    attention as two launches); extending it by a few tokens prefills over 101
+    cached keys on the one-launch path, whose key chunks mix cached and new keys.
+    Any device-side range report would raise here."""
+    llm = engine.llm
+    engine.reset_prefix_cache()
+    text = _prefix(llm, 104, 23)
+    cfg = ImeGenerationConfig(seed=23, max_sampling_attempts=8)
+    long_result = engine.complete(text[:100], cfg)
+    assert long_result.prefix_tokens == 101 and long_result.reused_prefix_tokens == 0
+    extended = engine.complete(text, cfg)
+    assert extended.prefix_tokens == 105 and extended.reused_prefix_tokens == 101
+    assert len(extended.raw_candidates) == extended.sampling_attempts
+
+
 def test_latest_generation_cancels_old_group_and_frees_pages(engine) -> None:
     llm = engine.llm
     box: dict[str, object] = {}

@@ -359,6 +359,73 @@ def test_prefill_attention_with_cached_prefix(cuda_device, hq: int, hkv: int, d:
     _bf16_close(out.view(new, hq, d), expected, ulps=2.0, atol=2e-3)
 
 
+@pytest.mark.parametrize("hq,hkv,d", [(12, 4, 64), (8, 2, 96), (16, 2, 128)])
+def test_fused_prefill_matches_two_call_path(cuda_device, hq: int, hkv: int, d: int) -> None:
+    """The one-launch prefill (norm, RoPE, K/V store, attention) against
+    qk_norm_rope_store + attention_prefill, bit for bit, on a varlen batch: a
+    fresh 13-token prefix, one token over 40 cached keys, and 64 new tokens over
+    70 cached keys (chunks that mix cached and new keys)."""
+    g = torch.Generator().manual_seed(5 + d)
+    q_lens, cached_lens = [13, 1, 64], [0, 40, 70]
+    num_slots, width = 1024, 256
+    cos, sin, cos_b, sin_b = _rope_tables(d, 512, cuda_device)
+    eps, scale = 1e-6, d**-0.5
+    perm = torch.randperm(num_slots, generator=g)
+    table = torch.zeros(len(q_lens), width, dtype=torch.int32)
+    used = 0
+    positions, out_loc = [], []
+    for r, (n, c) in enumerate(zip(q_lens, cached_lens)):
+        table[r, : c + n] = perm[used : used + c + n].to(torch.int32)
+        used += c + n
+        positions += list(range(c, c + n))
+        out_loc += table[r, c : c + n].tolist()
+    tokens = sum(q_lens)
+    dev = cuda_device
+    qkv = torch.randn(tokens, (hq + 2 * hkv) * d, generator=g).to(torch.bfloat16).to(dev)
+    qn = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16).to(dev)
+    kn = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16).to(dev)
+    kc = torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16).to(dev)
+    vc = torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16).to(dev)
+    pos_d = torch.tensor(positions, dtype=torch.int32, device=dev)
+    loc_d = torch.tensor(out_loc, dtype=torch.int32, device=dev)
+    table_d = table.to(dev)
+    tile = ops.prefill_tile_tokens(hq, hkv)
+    meta_host, ntiles = ops.prefill_meta(q_lens, cached_lens, list(range(len(q_lens))), tile)
+    meta = torch.tensor(meta_host, dtype=torch.int32, device=dev)
+
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+    qbuf = torch.empty(tokens, hq * d, dtype=torch.bfloat16, device=dev)
+    ops.qk_norm_rope_store(
+        qkv=qkv, num_qo_heads=hq, num_kv_heads=hkv, head_dim=d, q_norm_w=qn, k_norm_w=kn, eps=eps, cos=cos_b,
+        sin=sin_b, positions=pos_d, out_loc=loc_d, k_cache=kc_ref, v_cache=vc_ref, q_out=qbuf,
+    )
+    expected = torch.empty(tokens, hq * d, dtype=torch.bfloat16, device=dev)
+    ops.attention_prefill(
+        q=qbuf, out=expected, k_cache=kc_ref, v_cache=vc_ref, page_table=table_d, meta=meta,
+        num_requests=len(q_lens), num_tiles=ntiles, tile_tokens=tile, num_qo_heads=hq, num_kv_heads=hkv,
+        head_dim=d, scale=scale,
+    )
+    out = torch.empty(tokens, hq * d, dtype=torch.bfloat16, device=dev)
+    ops.attention_prefill_fused(
+        qkv=qkv, out=out, q_norm_w=qn, k_norm_w=kn, eps=eps, cos=cos_b, sin=sin_b, positions=pos_d,
+        out_loc=loc_d, k_cache=kc, v_cache=vc, page_table=table_d, meta=meta, num_requests=len(q_lens),
+        num_tiles=ntiles, tile_tokens=tile, max_q_len=max(q_lens), num_qo_heads=hq, num_kv_heads=hkv,
+        head_dim=d, scale=scale,
+    )
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    assert torch.equal(out, expected)
+    assert torch.equal(kc, kc_ref)
+    assert torch.equal(vc, vc_ref)
+    with pytest.raises(Exception, match="at most 64 new tokens"):
+        ops.attention_prefill_fused(
+            qkv=qkv, out=out, q_norm_w=qn, k_norm_w=kn, eps=eps, cos=cos_b, sin=sin_b, positions=pos_d,
+            out_loc=loc_d, k_cache=kc, v_cache=vc, page_table=table_d, meta=meta, num_requests=len(q_lens),
+            num_tiles=ntiles, tile_tokens=tile, max_q_len=65, num_qo_heads=hq, num_kv_heads=hkv,
+            head_dim=d, scale=scale,
+        )
+
+
 @pytest.mark.parametrize("temperature,top_k,top_p", [(0.8, 50, 0.9), (0.75, 96, 0.95), (1.0, 1, 1.0), (0.35, 50, 1.0), (0.9, 0, 1.0)])
 def test_sampler_tokens_bit_exact(cuda_device, temperature: float, top_k: int, top_p: float) -> None:
     g = torch.Generator().manual_seed(int(temperature * 100) + top_k)
