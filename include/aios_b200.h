@@ -255,8 +255,9 @@ AIOSB_API int aiosb_attention_prefill(const void* q, int64_t q_stride, const voi
                             void* stream);
 
 /* Fused prefill: aiosb_qk_norm_rope_store followed by aiosb_attention_prefill in
- * one launch (aios/layers/attention.py:6-16 and 55-79 with
- * aios/attention/flashinfer.py:300-326), for batches whose requests have at most
+ * one launch. It replaces the q/k RMSNorm and RoPE of aios/models/qwen3.py:66-70
+ * (apply_rotary_pos_emb, aios/layers/attention.py:6-16) and the backend's store
+ * and prefill (aios/attention/flashinfer.py:300-326), for batches whose requests have at most
  * max_q_len <= 64 new tokens (a keystroke's prefix prefill). qkv holds the raw
  * projection rows of the new tokens; each tile normalises and rotates its
  * queries and the new keys of its causal window, stores the K/V of its own
