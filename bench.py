@@ -176,6 +176,23 @@ def run_cpu(keystrokes: int, warmup: int) -> dict:
 DECODE_LINEAR_TRAFFIC = 168_907_008
 
 
+def max_over_ranks(values: list[float], world: int, device) -> list[float]:
+    """Each timing's maximum over all ranks (one all-reduce); unchanged for one
+    rank. The slowest replica bounds the job."""
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t]
+
+
+def replica_throughput(world: int, steps: int, device_ms: float) -> float:
+    """Whole-job keystrokes/s: every replica runs `steps` keystrokes, and
+    `device_ms` is the slowest replica's timed region."""
+    return world * steps / (device_ms * 1e-3)
+
+
 def decode_linear_roofline(llm, peaks: dict) -> dict:
     """Times the linear launches of one decode step (8 rows: 14 x
     {qkv, o, gate_up+SwiGLU, down} + LM head, the same shapes and weights as the
@@ -467,10 +484,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     launches = _lib.launches - launches0
     h2d = (rt.h2d_bytes + pr.h2d_bytes + ops.transfer_bytes["h2d"] - h2d0) / args.steps
     d2h = (rt.d2h_bytes + ops.transfer_bytes["d2h"] - d2h0) / args.steps
-    t = torch.tensor([device_ms, wall], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    device_ms, wall = float(t[0]), float(t[1])
+    device_ms, wall = max_over_ranks([device_ms, wall], world, dev)
     if rank != 0:
         return None
     peaks = measured_peaks()
@@ -484,7 +498,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     active = sum(r.active_model_tokens for r in results)
     line = {
         "metric": "Top-3 keystroke latency p50/p95 ms (8 cand), decode tok/s, mixer HBM GB/s",
-        "value": round(world * args.steps / (device_ms * 1e-3), 3),
+        "value": round(replica_throughput(world, args.steps, device_ms), 3),
         "unit": "keystrokes/s",
         "n_gpus": world,
         "steps": args.steps,
