@@ -231,3 +231,26 @@ def test_repeated_ngram_matches_direct_restatement() -> None:
         cases.append(text)
     for text in cases:
         assert _repeated_ngram_compact(text) == direct(text), text
+
+
+def test_prefill_tiles_partition_every_request() -> None:
+    """The prefill tile list covers each request's new tokens exactly once, in
+    order: the fused prefill stores a token's K/V from the one tile that owns it.
+    The packed array is [q_start | q_len | cached_len | table_row | tile_req | tile_q0]."""
+    from aios_b200.kernel import ops
+
+    for tile in (1, 2, 8):
+        for q_lens in ([13], [1, 64, 7], [5, 5, 5, 33], [64] * 3):
+            cached = [3 * i for i in range(len(q_lens))]
+            rows = list(range(len(q_lens)))[::-1]
+            meta, ntiles = ops.prefill_meta(q_lens, cached, rows, tile)
+            r = len(q_lens)
+            assert len(meta) == 4 * r + 2 * ntiles
+            q_start, lens, cl, tr = meta[:r], meta[r : 2 * r], meta[2 * r : 3 * r], meta[3 * r : 4 * r]
+            tile_req, tile_q0 = meta[4 * r : 4 * r + ntiles], meta[4 * r + ntiles :]
+            assert lens == q_lens and cl == cached and tr == rows
+            assert q_start == [sum(q_lens[:i]) for i in range(r)]
+            owned = {i: [] for i in range(r)}
+            for req, q0 in zip(tile_req, tile_q0):
+                owned[req].extend(range(q0, min(q0 + tile, q_lens[req])))
+            assert all(owned[i] == list(range(q_lens[i])) for i in range(r))
