@@ -228,7 +228,7 @@ template <int VPL, int NSRC, int G>
 __global__ void __launch_bounds__((1 + kStreamTok * G) * 32, 1)
     attnres_stream_kernel(const uint4* __restrict__ bank, int nsrc_bank, int64_t tokens, int hidden,
                           const uint4* __restrict__ partial, const float* __restrict__ wq, float eps,
-                          uint4* __restrict__ out, int spg) {
+                          uint4* __restrict__ out, int spg, int32_t* status) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
   __shared__ int abort_flag;
@@ -316,6 +316,7 @@ __global__ void __launch_bounds__((1 + kStreamTok * G) * 32, 1)
   // after a wait ran out, the copies already issued still land in this CTA's
   // shared memory: wait for them (bounded) before exiting
   if (threadIdx.x == 0 && abort_flag) {
+    report(status, AIOSB_DEV_WAIT_TIMEOUT);
     const int64_t n = issued_tiles;
     for (int64_t j = n > stages ? n - stages : 0; j < n; ++j) mbar_wait(&full[stage_of(j)], use_of(j) & 1);
   }
@@ -378,7 +379,8 @@ __global__ void __launch_bounds__(kMixWarps * 32)
 
 template <int G>
 cudaError_t launch_stream(int64_t total, const void* bank, int64_t sources, int64_t tokens, int64_t hidden,
-                          const void* partial, const float* wq, float eps, void* out, int spg, void* stream) {
+                          const void* partial, const float* wq, float eps, void* out, int spg, int32_t* status,
+                          void* stream) {
   auto kern = attnres_stream_kernel<3, 1, G>;
   switch (total) {
     case 1: kern = attnres_stream_kernel<3, 1, G>; break;
@@ -397,7 +399,7 @@ cudaError_t launch_stream(int64_t total, const void* bank, int64_t sources, int6
   const int64_t tiles = (tokens + kStreamTok - 1) / kStreamTok;
   const dim3 grid((unsigned)std::min<int64_t>(tiles, sm_count()));
   return launch_pdl(kern, grid, dim3((1 + kStreamTok * G) * 32), smem, as_stream(stream), (const uint4*)bank,
-                    (int)sources, tokens, (int)hidden, (const uint4*)partial, wq, eps, (uint4*)out, spg);
+                    (int)sources, tokens, (int)hidden, (const uint4*)partial, wq, eps, (uint4*)out, spg, status);
 }
 
 // Token count from which the stream kernel replaces the register kernel
@@ -414,7 +416,7 @@ using namespace aiosb;
 
 extern "C" int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t tokens, int64_t hidden,
                                  const void* partial, const float* weighted_query, float eps, void* out,
-                                 void* stream) {
+                                 int32_t* status, void* stream) {
   AIOSB_REQUIRE(sources >= 1 && tokens >= 1 && hidden >= 1, AIOSB_ERR_INVALID_ARG,
                 "bank dimensions must be positive");
   const int64_t total = sources + (partial != nullptr ? 1 : 0);
@@ -435,8 +437,10 @@ extern "C" int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t toke
       groups >= 1 ? (int)std::min<int64_t>(kStreamMaxStages / groups, kStreamSmemBudget / (groups * stage_bytes)) : 0;
   if (reg_shape && tokens >= g_stream_min_tokens && groups >= 3) {
     e = groups == 4
-            ? launch_stream<4>(total, bank, sources, tokens, hidden, partial, weighted_query, eps, out, spg, stream)
-            : launch_stream<3>(total, bank, sources, tokens, hidden, partial, weighted_query, eps, out, spg, stream);
+            ? launch_stream<4>(total, bank, sources, tokens, hidden, partial, weighted_query, eps, out, spg, status,
+                               stream)
+            : launch_stream<3>(total, bank, sources, tokens, hidden, partial, weighted_query, eps, out, spg, status,
+                               stream);
   } else if (reg_shape) {
     auto kern = attnres_reg_kernel<3, 1>;
     switch (total) {

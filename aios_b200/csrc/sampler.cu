@@ -978,7 +978,8 @@ __global__ void group_begin_kernel(aiosb_group_ptrs g, const __nv_bfloat16* __re
     g.counts[i] = 0;
     g.logprob_sums[i] = 0.f;
     g.stop_codes[i] = 0;
-    g.finished[i] = 0;
+    // NULL for callers of aiosb_group_step_static, which keeps the flags itself
+    if (g.finished != nullptr) g.finished[i] = 0;
     g.active[i] = i < attempts ? 1 : 0;
     g.row_page[i] = -1;
     g.out_loc[i] = -1;
@@ -1204,28 +1205,72 @@ constexpr int kStaticStepRows = 32;  // rows one call may step (the group limit)
 static __device__ __align__(256) int32_t g_static_step_finished[kStaticStepRows];
 
 namespace {
-constexpr int kStaticMaxDevices = 64;
+// The array's device address differs per CUDA context (one per device, and a new
+// one after cudaDeviceReset), so the cache is keyed by the context's process-wide
+// unique id (cuCtxGetId), fetched through the runtime's driver entry points so that
+// the library needs no link to libcuda.
+constexpr int kStaticMaxContexts = 64;
+struct StaticScratchEntry {
+  unsigned long long ctx_id;
+  void* addr;
+};
 std::mutex g_static_step_mu;
-void* g_static_step_addr[kStaticMaxDevices];  // device address per device ordinal
+StaticScratchEntry g_static_step_cache[kStaticMaxContexts];
+int g_static_step_used = 0;
 
-// Device address of g_static_step_finished on the current device. The host-side
-// name of a __device__ array is only a stand-in, so the address is looked up
-// once per device (with that device current) and cached.
+using CtxGetCurrentFn = int (*)(void**);
+using CtxGetIdFn = int (*)(void*, unsigned long long*);
+
+// Id of the calling thread's current context, or 0 when none is current yet.
+unsigned long long current_context_id() {
+  static CtxGetCurrentFn get_current = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<CtxGetCurrentFn>(fn);
+  }();
+  static CtxGetIdFn get_id = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &fn, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<CtxGetIdFn>(fn);
+  }();
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != 0 || ctx == nullptr) return 0;
+  return get_id(ctx, &id) == 0 ? id : 0;
+}
+
+// Device address of g_static_step_finished in the current context. The host-side
+// name of a __device__ array is only a stand-in, so the address is looked up with
+// cudaGetSymbolAddress (with the caller's device current) the first time a context
+// calls, and cached under the context's id.
 int static_step_scratch(int32_t** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step_static: cudaGetDevice: %s", cudaGetErrorString(e));
-  AIOSB_REQUIRE(dev >= 0 && dev < kStaticMaxDevices, AIOSB_ERR_UNSUPPORTED,
-                "group_step_static: device ordinal %d above %d", dev, kStaticMaxDevices - 1);
+  const unsigned long long id = current_context_id();
   std::lock_guard<std::mutex> lock(g_static_step_mu);
-  if (g_static_step_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_static_step_finished);
-    if (e != cudaSuccess || p == nullptr)
-      return set_error(AIOSB_ERR_LAUNCH, "group_step_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_static_step_addr[dev] = p;
+  for (int i = 0; id != 0 && i < g_static_step_used; ++i) {
+    if (g_static_step_cache[i].ctx_id == id) {
+      *out = static_cast<int32_t*>(g_static_step_cache[i].addr);
+      return AIOSB_OK;
+    }
   }
-  *out = static_cast<int32_t*>(g_static_step_addr[dev]);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_static_step_finished);  // creates the context if needed
+  if (e != cudaSuccess || p == nullptr)
+    return set_error(AIOSB_ERR_LAUNCH, "group_step_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+  const unsigned long long now = current_context_id();
+  if (now != 0) {  // without a context id the address is looked up on every call
+    StaticScratchEntry& slot = g_static_step_cache[g_static_step_used < kStaticMaxContexts
+                                                       ? g_static_step_used++
+                                                       : (int)(now % kStaticMaxContexts)];
+    slot.ctx_id = now;
+    slot.addr = p;
+  }
+  *out = static_cast<int32_t*>(p);
   return AIOSB_OK;
 }
 }  // namespace

@@ -178,6 +178,7 @@ def b200_attnres_mix(
         weighted_query.data_ptr(),
         float(eps),
         output.data_ptr(),
+        status_word(bank.device).data_ptr(),
         _stream(bank.device),
     )
     return output

@@ -1,5 +1,4 @@
 from .activation import silu_and_mul
-from .attention import apply_rotary_pos_emb, repeat_kv, rotate_half
 from .base import BaseOP, OPList, StateLessOP, _concat_prefix
 from .embedding import Embedding, LMHead
 from .linear import Linear, LinearColParallelMerged, LinearQKVMerged
@@ -11,6 +10,5 @@ __all__ = [
     "BaseOP", "StateLessOP", "OPList", "_concat_prefix",
     "Linear", "LinearColParallelMerged", "LinearQKVMerged",
     "RMSNorm", "RMSNormFused", "RotaryEmbedding",
-    "apply_rotary_pos_emb", "repeat_kv", "rotate_half",
     "Embedding", "LMHead",
 ]

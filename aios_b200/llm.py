@@ -49,9 +49,8 @@ class LLM:
         else:
             config = self._load_config(model_path)
         backend = kwargs.get("attnres_backend")
-        if backend is not None and str(backend) != "b200":
-            raise ValueError("attnres_backend must be 'b200' (the sm_100a fused mixer)")
-        config = replace(config, attnres_backend="b200")
+        if backend is not None:  # validated by ModelConfig: any reference name runs the sm_100a mixer
+            config = replace(config, attnres_backend=str(backend))
         self.config = config
         self._num_layers = config.num_layers
         with torch.device("meta"):

@@ -1,4 +1,11 @@
-"""Model configuration (aios/models/config.py:8-113) plus the ``b200`` AttnRes backend."""
+"""Model configuration (aios/models/config.py:8-113) plus the ``b200`` AttnRes backend.
+
+The AttnRes backend slot accepts the reference's four names (``reference``,
+``eager``, ``compiled``, ``triton``; aios/models/config.py:27,34-40) and ``b200``.
+This build has one mixer, the sm_100a kernel, so every accepted name runs it; the
+name is kept as given so that a reference config round-trips unchanged. Any other
+name raises the reference's ``ValueError``.
+"""
 
 from __future__ import annotations
 
@@ -6,7 +13,8 @@ import json
 import os
 from dataclasses import dataclass
 
-ATTNRES_BACKENDS = frozenset({"b200"})
+# reference names (all served by the one sm_100a mixer) plus this build's own
+ATTNRES_BACKENDS = frozenset({"reference", "eager", "compiled", "triton", "b200"})
 
 
 @dataclass(frozen=True)
@@ -28,13 +36,14 @@ class ModelConfig:
     residual_type: str = "standard"
     attnres_num_blocks: int = 0
     attnres_alpha: float = 1.0
-    attnres_backend: str = "b200"
+    attnres_backend: str = "triton"  # the reference's default name; runs the sm_100a mixer
 
     def __post_init__(self) -> None:
         if self.residual_type not in {"standard", "block_attnres"}:
             raise ValueError("residual_type must be 'standard' or 'block_attnres'")
         if self.attnres_backend not in ATTNRES_BACKENDS:
-            raise ValueError("attnres_backend must be 'b200' (the sm_100a fused mixer)")
+            raise ValueError("attnres_backend must be 'reference', 'eager', 'compiled', 'triton' or 'b200' "
+                             "(all run the sm_100a fused mixer)")
         if self.residual_type == "block_attnres":
             if self.attnres_num_blocks < 1:
                 raise ValueError("block_attnres requires attnres_num_blocks >= 1")
@@ -71,7 +80,6 @@ class ModelConfig:
             residual_type=get("residual_type", "standard"),
             attnres_num_blocks=get("attnres_num_blocks", 0),
             attnres_alpha=get("attnres_alpha", 1.0),
-            attnres_backend="b200",
         )
 
     @classmethod

@@ -32,7 +32,6 @@ from ..layers import (
     RMSNorm,
     RMSNormFused,
     RotaryEmbedding,
-    apply_rotary_pos_emb,
 )
 from .base import BaseLLMModel
 
@@ -71,16 +70,23 @@ class Qwen3Attention(BaseOP):
                 qkv, self.q_norm.weight, self.k_norm.weight, cos, sin, paged_kv_cache, self._layer_idx, batch
             )
         # A third-party backend plugged into the reference slot gets normalised,
-        # rotated q/k exactly as aios/models/qwen3.py:61-73 hands them over.
+        # rotated q/k and v as aios/models/qwen3.py:61-73 hands them over, and stores
+        # K/V itself (aios/attention/base.py:23-28). The q/k norm and RoPE run on the
+        # prefill prologue kernel, with k and v written to a per-call token buffer
+        # (slot t = token t) instead of the cache.
         tokens = qkv.shape[0]
-        q, k, v = qkv.split([self.q_size, self.kv_size, self.kv_size], dim=-1)
-        q = q.view(tokens, self.num_heads, self.head_dim)
-        k = k.view(tokens, self.num_kv_heads, self.head_dim)
-        v = v.view(tokens, self.num_kv_heads, self.head_dim)
-        self.q_norm.forward_inplace(q)
-        self.k_norm.forward_inplace(k)
-        cos, sin = rotary.forward(batch.positions.long())
-        q, k = apply_rotary_pos_emb(q, k, cos, sin)
+        dev = qkv.device
+        cos, sin = rotary.tables()
+        q = torch.empty(tokens, self.num_heads, self.head_dim, dtype=qkv.dtype, device=dev)
+        k = torch.empty(tokens, self.num_kv_heads, self.head_dim, dtype=qkv.dtype, device=dev)
+        v = torch.empty_like(k)
+        ops.qk_norm_rope_store(
+            qkv=qkv, num_qo_heads=self.num_heads, num_kv_heads=self.num_kv_heads, head_dim=self.head_dim,
+            q_norm_w=self.q_norm.weight, k_norm_w=self.k_norm.weight, eps=self.q_norm.eps, cos=cos, sin=sin,
+            positions=batch.positions.to(torch.int32).contiguous(),
+            out_loc=torch.arange(tokens, dtype=torch.int32, device=dev), k_cache=k, v_cache=v,
+            q_out=q.view(tokens, -1),
+        )
         return backend.forward(q, k, v, paged_kv_cache, self._layer_idx, batch).reshape(tokens, -1)
 
     def forward(self, hidden_states, rotary, paged_kv_cache, batch) -> torch.Tensor:

@@ -11,6 +11,11 @@ device reports and, knowing the ring order, knows every id the device took.
 
 With ``page_size`` 1 an id is a token slot (the reference layout); with 16 an id
 is a page of 16 consecutive token slots.
+
+The ring may also live on the CPU (``device="cpu"``), as the reference's list can:
+the same host logic then runs without a GPU (ids are written straight into the
+ring), which is what the CPU tests of the allocator use. The CandidateGroup
+runtime needs the CUDA ring.
 """
 
 from __future__ import annotations
@@ -22,8 +27,9 @@ from ..core import Req
 
 class CacheManager:
     def __init__(self, device: torch.device, num_pages: int, page_size: int = 1):
-        if device.type != "cuda":
-            raise ValueError("CacheManager keeps its free list on a CUDA device")
+        device = torch.device(device)
+        if device.type not in ("cuda", "cpu"):
+            raise ValueError("CacheManager keeps its free list on a CUDA device (or the CPU)")
         if num_pages < 1:
             raise ValueError("num_pages must be positive")
         self.device = device
@@ -33,9 +39,11 @@ class CacheManager:
         self._host = list(range(num_pages))  # ring contents, index = logical position % num_pages
         self._head = 0
         self._tail = num_pages
-        self._staging = torch.zeros(num_pages, dtype=torch.int32).pin_memory()
-        self._stage_np = self._staging.numpy()
-        self._stage_event = torch.cuda.Event()
+        self._on_cuda = device.type == "cuda"
+        if self._on_cuda:
+            self._staging = torch.zeros(num_pages, dtype=torch.int32).pin_memory()
+            self._stage_np = self._staging.numpy()
+            self._stage_event = torch.cuda.Event()
         self._stage_busy = False
 
     # -- reference API -------------------------------------------------------
@@ -91,12 +99,17 @@ class CacheManager:
         self._tail += n
 
     def _write_ring(self, start: int, ids: list[int]) -> None:
-        if self._stage_busy:
-            self._stage_event.synchronize()  # previous copy still reads the staging buffer
         n = len(ids)
-        self._stage_np[:n] = ids
         cap = self.num_pages
         first = min(n, cap - start)
+        if not self._on_cuda:
+            self.ring[start : start + first] = torch.tensor(ids[:first], dtype=torch.int32)
+            if first < n:
+                self.ring[: n - first] = torch.tensor(ids[first:], dtype=torch.int32)
+            return
+        if self._stage_busy:
+            self._stage_event.synchronize()  # previous copy still reads the staging buffer
+        self._stage_np[:n] = ids
         self.ring[start : start + first].copy_(self._staging[:first], non_blocking=True)
         if first < n:
             self.ring[: n - first].copy_(self._staging[first:n], non_blocking=True)
@@ -104,6 +117,8 @@ class CacheManager:
         self._stage_busy = True
 
     def _to_device(self, ids: list[int]) -> torch.Tensor:
+        if not self._on_cuda:
+            return torch.tensor(ids, dtype=torch.int32)
         return torch.tensor(ids, dtype=torch.int32).pin_memory().to(self.device, non_blocking=True)
 
     # -- device-side allocation support -----------------------------------------

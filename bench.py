@@ -170,7 +170,7 @@ def run_cpu(keystrokes: int, warmup: int) -> dict:
 # dram__bytes_read.sum + dram__bytes_write.sum summed over the 57 linear launches
 # of one decode step, from one ncu capture of the `linears` NVTX range below with
 # `--cache-control none`, so that L2 carries over between launches and replays as
-# it does in the timed loop (profiles/gemv_mma_decode_linears_s10.md). It is
+# it does in the timed loop. It is
 # below the 201,326,592 algorithmic bytes: with cache-streaming weight loads,
 # about 16% of the weights are still in L2 when the next replay reads them.
 DECODE_LINEAR_TRAFFIC = 168_907_008

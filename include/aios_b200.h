@@ -13,8 +13,12 @@
  *   the device (a slot index outside the pool, an exhausted free list, a bounded
  *   wait that ran out) are written as an AIOSB_DEV_* code into the caller's int32
  *   status word (first error wins) and the kernel returns.
- * Threading: stateless apart from the per-thread error message; calls may come
- *   from any host thread as long as the caller orders them on its stream.
+ * Threading: calls may come from any host thread as long as the caller orders
+ *   them on its stream. The library holds no state of its own except the
+ *   per-thread error message and, for aiosb_group_step_static only, a 32-entry
+ *   device array in the library image plus a host cache of its address per CUDA
+ *   context (guarded by a mutex). Calls of aiosb_group_step_static that overlap
+ *   on the GPU share that array and race on it.
  *
  * Each entry point names the reference interface it replaces
  * (paths inside the 7155/aios repository).
@@ -84,9 +88,12 @@ AIOSB_API int aiosb_kv_store(void* k_cache, void* v_cache, int64_t cache_token_s
  * hidden] bf16 or NULL; weighted_query: [hidden] fp32; out: [tokens, hidden] bf16.
  * score = (x . wq) * rsqrt(mean(x^2) + eps) in fp32, softmax over depth in
  * fp32, weights rounded to bf16, out = sum_s w_s x_s accumulated in fp32.
- * hidden must be a multiple of 8; sources + (partial != NULL) <= 16. */
+ * hidden must be a multiple of 8; sources + (partial != NULL) <= 16.
+ * status: the caller's int32 status word, or NULL. From 2048 tokens the mixer
+ * streams its sources through bounded shared-memory waits; a wait that runs out
+ * writes AIOSB_DEV_WAIT_TIMEOUT there (and NaN into the rows it did not mix). */
 AIOSB_API int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t tokens, int64_t hidden, const void* partial,
-                      const float* weighted_query, float eps, void* out, void* stream);
+                      const float* weighted_query, float eps, void* out, int32_t* status, void* stream);
 
 /* The mixer followed by the RMSNorm that consumes its output in the Block AttnRes
  * layers (aios/models/minimind_ime.py, the input / post-attention norms after
@@ -399,12 +406,14 @@ AIOSB_API int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t 
  * Same arguments, results and errors as aiosb_group_step, except that
  * g->finished is neither read nor written (it may be NULL here): the per-row
  * finish flags go through a 32-entry int32 array inside the library, so rows
- * above 32 are rejected with AIOSB_ERR_UNSUPPORTED. aiosb_group_begin still
- * zeroes g->finished at round start; a caller without that array may point it
- * at g->stop_codes, which group_begin zeroes as well.
- * The call allocates and frees nothing. Its first call on a device looks up the
- * array's device address (cudaGetSymbolAddress, on the current device) and
- * should come before any stream capture. Each call clears the array with an
+ * above 32 are rejected with AIOSB_ERR_UNSUPPORTED. aiosb_group_begin zeroes
+ * g->finished at round start when it is not NULL and skips it when it is, so a
+ * caller without that array passes NULL to both calls.
+ * The call allocates and frees nothing. Its first call in a CUDA context (one per
+ * device, and a new one after cudaDeviceReset) looks up the array's device
+ * address (cudaGetSymbolAddress, on the current device) and caches it under the
+ * context's id; that first call should come before any stream capture. Each call
+ * clears the array with an
  * asynchronous memset on `stream` before the step kernel. Every GPU that loads
  * the library holds the array until the process exits, and all calls on a device
  * share it: calls that overlap on the GPU (two groups stepping on different

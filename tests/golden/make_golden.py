@@ -12,7 +12,7 @@ The reference's GPU-only pieces are replaced by the smallest possible shims:
 Weights are the seeded synthetic weights of the benchmark protocol.
 
 Usage (only where the reference checkout exists; the fixtures are committed):
-    AIOS_REFERENCE=/root/reference/python python tests/golden/make_golden.py
+    AIOS_REFERENCE=<reference checkout>/python python tests/golden/make_golden.py
 """
 
 from __future__ import annotations
@@ -27,7 +27,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path(os.environ.get("AIOS_REFERENCE", "/root/reference/python"))
+if not os.environ.get("AIOS_REFERENCE"):
+    raise SystemExit("set AIOS_REFERENCE to the reference checkout's python/ directory (the one holding aios/)")
+REF = Path(os.environ["AIOS_REFERENCE"])
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REF))
 

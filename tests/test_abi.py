@@ -32,7 +32,7 @@ def test_version_and_error_reporting_without_gpu() -> None:
     rc = lib.aiosb_linear(None, 4, 100, None, 128, None, 128, 0, None, 0, None, None)
     assert rc == _lib.ERR_UNSUPPORTED
     assert "multiple of 64" in _lib.last_error()
-    rc = lib.aiosb_attnres_mix(None, 0, 1, 8, None, None, ctypes.c_float(1e-6), None, None)
+    rc = lib.aiosb_attnres_mix(None, 0, 1, 8, None, None, ctypes.c_float(1e-6), None, None, None)
     assert rc == _lib.ERR_INVALID_ARG
     assert "positive" in _lib.last_error()
 

@@ -135,8 +135,54 @@ def test_attnres_config_rejects_partial_migration_and_bad_partition() -> None:
         tiny_config(attnres_alpha=0.5)
     with pytest.raises(ValueError, match="divisible"):
         tiny_config(num_layers=7)
-    with pytest.raises(ValueError, match="b200"):
-        tiny_config(attnres_backend="triton")
+    with pytest.raises(ValueError, match="attnres_backend must be 'reference', 'eager', 'compiled', 'triton'"):
+        tiny_config(attnres_backend="flash")
+
+
+@pytest.mark.parametrize("name", ["reference", "eager", "compiled", "triton", "b200"])
+def test_attnres_backend_accepts_reference_names(name) -> None:
+    """The reference's AttnRes backend names (aios/models/config.py:27,34-40) are
+    all accepted, kept as given, and served by the one sm_100a mixer."""
+    from aios_b200.models.minimind_ime import MiniMindIMEForCausalLM
+
+    cfg = tiny_config(attnres_backend=name)
+    assert cfg.attnres_backend == name
+    with torch.device("meta"):
+        model = MiniMindIMEForCausalLM(cfg)
+    assert model.model.layers.op_list[0].attn_res_mixer._backend == name
+    assert ModelConfig.__dataclass_fields__["attnres_backend"].default == "triton"
+
+
+def test_cache_manager_fifo_exhaustion_and_double_free() -> None:
+    """The free-slot FIFO of aios/scheduler/cache.py:9-51 on a CPU ring: ids come
+    out in arange order, frees append at the tail, asking for more than is free
+    raises the reference's NotImplementedError (leaving the list untouched), and
+    returning more ids than the pool holds is refused."""
+    from aios_b200.scheduler.cache import CacheManager
+
+    cm = CacheManager(torch.device("cpu"), 8)
+    assert cm.available_size == 8
+    a = cm.allocate(3)
+    assert a.tolist() == [0, 1, 2] and a.dtype == torch.int32
+    b = cm.allocate(4)
+    assert b.tolist() == [3, 4, 5, 6] and cm.available_size == 1
+    with pytest.raises(NotImplementedError, match="CacheManager eviction is not implemented."):
+        cm.allocate(2)
+    assert cm.available_size == 1  # a failed allocation takes nothing
+    cm._free(a)  # appended after 7, in the order returned
+    assert cm.available_size == 4
+    assert cm.allocate(4).tolist() == [7, 0, 1, 2]
+    cm._free(torch.tensor([5, 3], dtype=torch.int32))
+    cm._free([])
+    assert cm.allocate(2).tolist() == [5, 3]
+    cm._free(list(range(8)))  # everything back: the pool is full
+    assert cm.available_size == 8
+    with pytest.raises(RuntimeError, match="double free"):
+        cm._free([3])
+    with pytest.raises(ValueError):
+        cm.allocate(-1)
+    # the ring mirrors the host list: the next 8 ids in FIFO order
+    assert [int(cm.ring[(cm.head + i) % 8]) for i in range(8)] == list(range(8))
 
 
 def test_attnres_model_state_dict_preserves_checkpoint_names() -> None:

@@ -26,7 +26,8 @@ from aios_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
-ROWS = 8
+ROWS = 8  # the bench's candidate group
+MAX_ROWS = 32  # the static array's size: the largest group the entry point steps
 VOCAB = 16384
 STEPS = 4
 TABLE_WIDTH = 64
@@ -35,25 +36,25 @@ PREFIX_LEN = 5
 EOS, PAD, TERMINAL = 2, 0, 7
 
 
-def _make_group(dev: torch.device) -> dict:
+def _make_group(dev: torch.device, rows: int = ROWS) -> dict:
     i32 = dict(dtype=torch.int32, device=dev)
     b = dict(
         state=torch.zeros(ctypes.sizeof(_lib.GroupState), dtype=torch.uint8, device=dev),
-        logits=torch.zeros((ROWS, VOCAB), dtype=torch.bfloat16, device=dev),
-        uniforms=torch.zeros((ROWS, STEPS), dtype=torch.float32, device=dev),
-        output_ids=torch.zeros((ROWS, STEPS), **i32),
-        token_logprobs=torch.zeros((ROWS, STEPS), dtype=torch.float32, device=dev),
-        logprob_sums=torch.zeros(ROWS, dtype=torch.float32, device=dev),
+        logits=torch.zeros((rows, VOCAB), dtype=torch.bfloat16, device=dev),
+        uniforms=torch.zeros((rows, STEPS), dtype=torch.float32, device=dev),
+        output_ids=torch.zeros((rows, STEPS), **i32),
+        token_logprobs=torch.zeros((rows, STEPS), dtype=torch.float32, device=dev),
+        logprob_sums=torch.zeros(rows, dtype=torch.float32, device=dev),
         terminal_ids=torch.tensor([TERMINAL], **i32),
-        page_table=torch.zeros((ROWS, TABLE_WIDTH), **i32),
+        page_table=torch.zeros((rows, TABLE_WIDTH), **i32),
         ring=torch.arange(CAPACITY, **i32),
         status=torch.zeros(1, **i32),
     )
     for name in ("counts", "stop_codes", "active", "finished", "tokens", "positions", "seq_lens", "out_loc",
                  "row_page", "row_table"):
-        b[name] = torch.zeros(ROWS, **i32)
+        b[name] = torch.zeros(rows, **i32)
     st = _lib.GroupState(
-        step=0, max_steps=STEPS, min_new_tokens=0, prefix_len=PREFIX_LEN, row_offset=0, rows=ROWS, vocab=VOCAB,
+        step=0, max_steps=STEPS, min_new_tokens=0, prefix_len=PREFIX_LEN, row_offset=0, rows=rows, vocab=VOCAB,
         eos_id=EOS, pad_id=PAD, greedy=0, top_k=50, temperature=0.8, top_p=0.9, page_size=1, n_terminal=1,
         head=0, tail=CAPACITY, capacity=CAPACITY, table_stride=TABLE_WIDTH,
     )
@@ -69,32 +70,44 @@ def _results(b: dict) -> dict:
     return {k: b[k].cpu().clone() for k in names}
 
 
-def _logits(gen: torch.Generator, dev: torch.device, eos_rows: list[int], terminal_rows: list[int]) -> torch.Tensor:
-    x = torch.randn((ROWS, VOCAB), generator=gen)
+def _logits(gen: torch.Generator, dev: torch.device, rows: int, eos_rows: list[int],
+            terminal_rows: list[int]) -> torch.Tensor:
+    x = torch.randn((rows, VOCAB), generator=gen)
     x[:, [EOS, TERMINAL]] = -20.0  # never sampled, except where raised below
     x[eos_rows, EOS] = 20.0  # sampled with probability ~1 at temperature 0.8
     x[terminal_rows, TERMINAL] = 20.0
     return x.to(dev, torch.bfloat16)
 
 
-def test_group_step_static_matches_group_step(cuda_device) -> None:
+# (rows, [(eos rows, terminal rows) per step]): the bench's 8-row group and the
+# 32-row maximum the static array holds
+GROUPS = [
+    (ROWS, [([1, 5], [3]), ([6], [])]),
+    (MAX_ROWS, [([1, 5, 17, 30], [3, 31]), ([6, 20], [0])]),
+]
+
+
+@pytest.mark.parametrize("rows,endings", GROUPS, ids=[f"rows{g[0]}" for g in GROUPS])
+def test_group_step_static_matches_group_step(cuda_device, rows, endings) -> None:
     dev = cuda_device
     stream = torch.cuda.current_stream(dev).cuda_stream
-    gen = torch.Generator().manual_seed(0)
+    gen = torch.Generator().manual_seed(rows)
     prefix_logits = torch.randn(VOCAB, generator=gen).to(dev, torch.bfloat16)
-    ref, nal = _make_group(dev), _make_group(dev)
-    for g in (ref, nal):
-        _lib.call("aiosb_group_begin", ctypes.byref(g["ptrs"]), prefix_logits.data_ptr(), 1234, ROWS, ROWS, stream)
-    # the allocation-free caller has no `finished` array: the entry point must not touch it
+    ref, nal = _make_group(dev, rows), _make_group(dev, rows)
+    # the allocation-free caller has no `finished` array: neither the round start
+    # nor the step may touch it
     nal_ptrs = _lib.GroupPtrs.from_buffer_copy(nal["ptrs"])
     nal_ptrs.finished = None
-    # step 0: rows 1 and 5 end on EOS, row 3 on a terminal id; step 1: row 6 ends on EOS
-    for step, (eos_rows, term_rows) in enumerate([([1, 5], [3]), ([6], [])]):
-        logits = _logits(gen, dev, eos_rows, term_rows)
+    nal["finished"].fill_(-7)  # would show any write through a stale pointer
+    _lib.call("aiosb_group_begin", ctypes.byref(ref["ptrs"]), prefix_logits.data_ptr(), 1234, rows, rows, stream)
+    _lib.call("aiosb_group_begin", ctypes.byref(nal_ptrs), prefix_logits.data_ptr(), 1234, rows, rows, stream)
+    ended: dict[int, int] = {}
+    for step, (eos_rows, term_rows) in enumerate(endings):
+        logits = _logits(gen, dev, rows, eos_rows, term_rows)
         ref["logits"].copy_(logits)
         nal["logits"].copy_(logits)
-        _lib.call("aiosb_group_step", ctypes.byref(ref["ptrs"]), ROWS, VOCAB, 50, stream)
-        _lib.call("aiosb_group_step_static", ctypes.byref(nal_ptrs), ROWS, VOCAB, 50, stream)
+        _lib.call("aiosb_group_step", ctypes.byref(ref["ptrs"]), rows, VOCAB, 50, stream)
+        _lib.call("aiosb_group_step_static", ctypes.byref(nal_ptrs), rows, VOCAB, 50, stream)
         torch.cuda.synchronize(dev)
         want, got = _results(ref), _results(nal)
         # the same kernel on the same inputs: every output is bit-identical
@@ -103,11 +116,17 @@ def test_group_step_static_matches_group_step(cuda_device) -> None:
         assert int(want["status"][0]) == 0
         state = _lib.GroupState.from_buffer_copy(bytes(want["state"].numpy()))
         assert state.step == step + 1 and state.done == 0 and state.arrive == 0
+        ended.update({r: 1 for r in eos_rows})
+        ended.update({r: 2 for r in term_rows})
     # the finished rows were compacted out, the others got consecutive FIFO slots
-    assert want["stop_codes"].tolist() == [0, 1, 0, 2, 0, 1, 1, 0]
-    assert want["active"].tolist() == [1, 0, 1, 0, 1, 0, 0, 1]
-    assert want["out_loc"][[0, 2, 4, 7]].tolist() == [5, 6, 7, 8]
-    assert nal["finished"].abs().sum().item() == 0
+    live = [r for r in range(rows) if r not in ended]
+    assert want["stop_codes"].tolist() == [ended.get(r, 0) for r in range(rows)]
+    assert want["active"].tolist() == [0 if r in ended else 1 for r in range(rows)]
+    # step 0 took one slot per row that survived it (ring entries 0, 1, ...), so
+    # the last step's slots continue from there
+    first = rows - len(set(endings[0][0] + endings[0][1]))
+    assert want["out_loc"][live].tolist() == list(range(first, first + len(live)))
+    assert (nal["finished"] == -7).all(), "the NULL finished array was written"
 
 
 def test_group_step_static_rejects_rows_beyond_its_array(cuda_device) -> None:
