@@ -11,8 +11,9 @@ weights once per decode step, so the working set exceeds the 126 MB L2.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-``--impl reference`` times the CPU restatement of the reference algorithm
-(oracle/, fp32, all host cores) on the same workload. With N > 1 (torchrun)
+``--impl reference`` times the unmodified reference engine (installed under
+baseline/_ref; fp32, all host cores, CPU shims for FlashInfer and the KV buffer)
+on the same workload. With N > 1 (torchrun)
 every GPU serves an independent keystroke stream (replicas; no data exchange);
 the barrier and the max-over-ranks timing use a small NCCL all-reduce.
 """
@@ -111,6 +112,14 @@ WORKLOAD = ("S10 keystroke: [BOS]+12 prefix, 8 candidates x 12 tokens, T=0.8 top
             "one round, 16-token pages x 256")
 
 
+def bench_config(world: int) -> dict:
+    """The `config` of both arms' lines (same workload, same keys)."""
+    return {"workload": WORKLOAD, "model": "MiniMind-IME 0.1B shape (S10)", "prefix_tokens": 13,
+            "candidates": 8, "max_new_tokens": 12, "page_size": 16, "num_pages": 256,
+            "l2": "inputs larger than L2: every decode step streams the 201 MB of weights",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+
+
 def keystroke_config():
     from aios_b200 import ImeGenerationConfig
 
@@ -124,10 +133,43 @@ def prefixes(tokenizer, vocab: int, count: int, seed: int, length: int = 12) -> 
 
 
 # ---------------------------------------------------------------------------
-# CPU arm (oracle restatement of the reference algorithm)
+# Reference arm: the unmodified reference engine on the host cores
 # ---------------------------------------------------------------------------
-def run_cpu(keystrokes: int, warmup: int) -> dict:
-    """Times the oracle keystroke (fp32, all host threads) on the bench workload."""
+def run_reference(keystrokes: int, warmup: int, seed: int = 1234) -> dict:
+    """Times the reference's own ``ImeCompletionEngine.complete`` (aios/ime.py:415-640,
+    installed under baseline/_ref, fp32, all host threads) on the bench workload:
+    the same seeded prefixes and the same weights rule as the GPU arm, one-token
+    pages (the reference's only mode) over the same 4096 KV slots. The four CPU
+    shims of oracle/reference_run.py stand in for FlashInfer and the CUDA-only KV
+    buffer; this process imports nothing from aios_b200."""
+    from oracle import reference_run
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    mods = reference_run.install()
+    llm = reference_run.build_llm(mods, reference_run.SHAPES["S10"], num_pages=256 * 16)
+    engine = mods.ime.ImeCompletionEngine(llm)
+    kc = mods.ime.ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=8, refill_batch_size=8,
+                                      max_new_tokens=12, temperature=0.8, top_k=50, top_p=0.9, seed=0)
+    texts = prefixes(llm.tokenizer, llm.config.vocab_size, warmup + keystrokes, seed=seed)
+    times = []
+    for i, text in enumerate(texts):
+        engine.reset_prefix_cache()
+        t0 = time.perf_counter()
+        engine.complete(text, kc)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    return {"value": len(times) / total, "unit": "keystrokes/s", "cores": threads, "kind": "reference",
+            "p50_ms": statistics.median(times) * 1e3, "p95_ms": percentile(times, 0.95) * 1e3,
+            "sample": f"{len(times)} keystrokes of the bench workload through the unmodified reference "
+                      f"ImeCompletionEngine.complete (fp32, {threads} threads, CPU shims for FlashInfer and "
+                      f"the KV buffer), {total:.1f} s"}
+
+
+def run_port(keystrokes: int, warmup: int) -> dict:
+    """Fallback of the reference arm when no reference install is present: the
+    oracle restatement of the same keystroke (fp32, all host threads)."""
     from aios_b200.models import shapes
     from aios_b200.models.minimind_ime import MiniMindIMEForCausalLM
     from aios_b200.models.weight import synthetic_state_dict
@@ -159,9 +201,22 @@ def run_cpu(keystrokes: int, warmup: int) -> dict:
             times.append(time.perf_counter() - t0)
     total = sum(times)
     return {"value": len(times) / total, "unit": "keystrokes/s", "cores": threads, "kind": "port",
-            "p50_ms": statistics.median(times) * 1e3,
+            "p50_ms": statistics.median(times) * 1e3, "p95_ms": percentile(times, 0.95) * 1e3,
             "sample": f"{len(times)} keystrokes of the bench workload (fp32, oracle restatement, "
                       f"{threads} threads), {total:.1f} s"}
+
+
+def reference_subprocess(keystrokes: int) -> dict | None:
+    """The reference arm in a child process (keeps the reference's import-time
+    shims out of the GPU process); returns its cpu_baseline, or None."""
+    cmd = [sys.executable, str(REPO / "bench.py"), "--impl", "reference", "--steps", str(keystrokes),
+           "--warmup", "3"]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    proc = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=900)
+    for line in reversed(proc.stdout.splitlines()):
+        if line.startswith("{"):
+            return json.loads(line).get("cpu_baseline")
+    return None
 
 
 # ---------------------------------------------------------------------------
@@ -408,8 +463,31 @@ def _latencies(engine, texts: list[str], cfg, warmup: int) -> list:
     return results
 
 
+def shape_keystroke(shape: str, dev, keystrokes: int = 20, warmup: int = 5) -> dict:
+    """The bench keystroke ([BOS]+12, 8 candidates x 12 tokens, T 0.8, top-k 50,
+    top-p 0.9, 16-token pages x 256) on another model shape, through ``complete``:
+    S06 is BASELINE config 2 (8 layers, 8 q / 2 kv heads of 96, vocab 6400), S10L
+    the same dims at 14 layers."""
+    from aios_b200 import ImeCompletionEngine, LLM
+    from aios_b200.models import shapes
+
+    llm_s = LLM(config=getattr(shapes, shape), seed=0, page_size=16, num_pages=256, device=str(dev))
+    eng_s = ImeCompletionEngine(llm_s)
+    res = _latencies(eng_s, prefixes(llm_s.tokenizer, llm_s.config.vocab_size, warmup + keystrokes, seed=606),
+                     keystroke_config(), warmup)
+    lat = [r.latency_ms for r in res]
+    out = {"p50_ms": round(statistics.median(lat), 3), "p95_ms": round(percentile(lat, 0.95), 3),
+           "gpu_p50_ms": round(statistics.median([r.gpu_latency_ms for r in res]), 3),
+           "decode_tok_s": round(sum(r.generated_tokens for r in res) / (sum(r.gpu_latency_ms for r in res) * 1e-3), 1),
+           "layers": llm_s.config.num_layers, "head_dim": llm_s.config.head_dim, "vocab": llm_s.config.vocab_size}
+    del eng_s, llm_s
+    torch.cuda.empty_cache()
+    return out
+
+
 def config_sweeps(engine, llm, dev) -> dict:
-    """BASELINE configs 3 and 4 through ``complete``.
+    """BASELINE configs 2, 3 and 4 through ``complete``.
+    Config 2: the bench keystroke on S06 (and on S10L, S06's dims at 14 layers).
     Config 3: the S10 keystroke at prefix lengths 4/8/16/32 after [BOS], 8
     candidates x 16 tokens. Config 4: the S21 Block-AttnRes model (32 layers, 8
     blocks, 65 mixers per forward), a 16-token prefix and refill rounds of 8 up to
@@ -419,7 +497,8 @@ def config_sweeps(engine, llm, dev) -> dict:
     from aios_b200 import ImeCompletionEngine, ImeGenerationConfig, LLM
     from aios_b200.models import shapes
 
-    out = {"s10_prefix_sweep": {}}
+    out = {"s06_keystroke": shape_keystroke("S06", dev), "s10l_keystroke": shape_keystroke("S10L", dev),
+           "s10_prefix_sweep": {}}
     cfg3 = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=8, refill_batch_size=8,
                                max_new_tokens=16, temperature=0.8, top_k=50, top_p=0.9, seed=0)
     for n in (4, 8, 16, 32):
@@ -509,10 +588,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded random weights, seeded prefixes, synthetic tokenizer)",
-        "config": {"workload": WORKLOAD, "model": "MiniMind-IME 0.1B shape (S10)", "prefix_tokens": 13,
-                   "candidates": 8, "max_new_tokens": 12, "page_size": 16, "num_pages": 256,
-                   "l2": "inputs larger than L2: every decode step streams the 201 MB of weights",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "config": bench_config(world),
         "latency_ms": {"p50": round(statistics.median(lat), 3), "p95": round(percentile(lat, 0.95), 3),
                        "gpu_p50": round(statistics.median(gpu_lat), 3),
                        "gpu_p95": round(percentile(gpu_lat, 0.95), 3)},
@@ -597,14 +673,19 @@ def main() -> None:
     if args.impl == "reference":
         if rank != 0:
             return
-        cpu = run_cpu(args.steps, args.warmup)
+        try:
+            cpu = run_reference(args.steps, args.warmup)
+        except FileNotFoundError:  # no baseline/_ref install: the oracle port stands in
+            cpu = run_port(args.steps, args.warmup)
         print(json.dumps({
             "impl": "reference",
             "metric": "Top-3 keystroke latency p50/p95 ms (8 cand), decode tok/s, mixer HBM GB/s",
             "value": round(cpu["value"], 4), "unit": "keystrokes/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1000.0 / cpu["value"], 2), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-            "config": {"workload": WORKLOAD},
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded random weights, seeded prefixes, synthetic tokenizer)",
+            "config": bench_config(world),
+            "latency_ms": {"p50": round(cpu["p50_ms"], 3), "p95": round(cpu["p95_ms"], 3)},
             "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": round(cpu["value"], 4), "unit": "keystrokes/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
@@ -618,8 +699,7 @@ def main() -> None:
     line = run_gpu(args, rank, world, local_rank)
     if rank == 0 and line is not None:
         if world == 1 and args.cpu_sample > 0:
-            cpu = run_cpu(args.cpu_sample, 1)
-            line["cpu_baseline"] = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            line["cpu_baseline"] = reference_subprocess(args.cpu_sample)
         print(json.dumps(line))
     if world > 1:
         import torch.distributed as dist

@@ -1,13 +1,14 @@
 """Generates the golden fixtures of tests/golden/ by running the UNMODIFIED
 reference implementation (7155/aios, Python) on the CPU.
 
-The reference's GPU-only pieces are replaced by the smallest possible shims:
+The reference's GPU-only pieces are replaced by the shims of
+oracle/reference_run.py (the same ones bench.py's reference arm uses):
   1. FlashInfer rmsnorm / fused_add_rmsnorm / silu_and_mul -> torch expressions of
      FlashInfer's arithmetic (fp32 math, one rounding to the storage dtype);
   2. the attention backend -> a CPU backend that stores K/V in a
      [2, L, pages, 1, Hkv, d] buffer and calls the reference's own
      _sdpa_prefill_attention for prefill and decode;
-  3. torch.cuda.Event -> a no-op timer;
+  3. torch.cuda.Event -> a host-clock event;
   4. the tokenizer -> aios_b200's SyntheticTokenizer (ids <-> CJK characters).
 Weights are the seeded synthetic weights of the benchmark protocol.
 
@@ -33,149 +34,27 @@ REF = Path(os.environ["AIOS_REFERENCE"])
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REF))
 
-import flashinfer  # noqa: E402
+from oracle import reference_run  # noqa: E402  (the shims: FlashInfer norms, CPU attention + KV, host events)
 
-
-def _fi_rmsnorm(x, w, eps, out=None, **_):
-    xf = x.float()
-    y = (xf * (1.0 / torch.sqrt((xf * xf).mean(-1, keepdim=True) + eps)) * w.float()).to(x.dtype)
-    if out is not None:
-        out.copy_(y)
-        return out
-    return y
-
-
-def _fi_fused_add_rmsnorm(x, residual, w, eps, **_):
-    s = x.float() + residual.float()
-    residual.copy_(s.to(residual.dtype))
-    x.copy_((s * (1.0 / torch.sqrt((s * s).mean(-1, keepdim=True) + eps)) * w.float()).to(x.dtype))
-
-
-def _fi_silu_and_mul(x, out=None, **_):
-    f = x.shape[-1] // 2
-    g, u = x[..., :f].float(), x[..., f:].float()
-    y = (g / (1.0 + torch.exp(-g)) * u).to(x.dtype)
-    if out is not None:
-        out.copy_(y)
-        return out
-    return y
-
-
-flashinfer.rmsnorm = _fi_rmsnorm
-flashinfer.fused_add_rmsnorm = _fi_fused_add_rmsnorm
-flashinfer.silu_and_mul = _fi_silu_and_mul
-
-import aios.core as ref_core  # noqa: E402
-from aios.attention.base import BaseAttentionBackend, BaseAttentionMetadata  # noqa: E402
-from aios.attention.flashinfer import _sdpa_prefill_attention  # noqa: E402
-from aios.engine import sample as ref_sample  # noqa: E402
-from aios.ime import ImeCompletionEngine, ImeGenerationConfig  # noqa: E402
-from aios.models.config import ModelConfig as RefConfig  # noqa: E402
-from aios.models.minimind_ime import BlockAttnResMixer, MiniMindIMEForCausalLM  # noqa: E402
-from aios.scheduler.cache import CacheManager  # noqa: E402
+_mods = reference_run.install(REF)
+ref_core = _mods.core
+ref_sample = _mods.sample
+ImeCompletionEngine = _mods.ime.ImeCompletionEngine
+ImeGenerationConfig = _mods.ime.ImeGenerationConfig
+BlockAttnResMixer = _mods.minimind.BlockAttnResMixer
+_sdpa_prefill_attention = _mods.attn_fi._sdpa_prefill_attention
 
 from aios_b200.models import shapes  # noqa: E402
 from aios_b200.models.weight import synthetic_state_dict  # noqa: E402
 from aios_b200.tokenizer import SyntheticTokenizer  # noqa: E402
 
 
-class _Event:
-    def __init__(self, *a, **k):
-        pass
-
-    def record(self, *a, **k):
-        pass
-
-    def synchronize(self):
-        pass
-
-    def elapsed_time(self, other):
-        return 0.0
-
-
-torch.cuda.Event = _Event
-
-
-@dataclasses.dataclass
-class _Meta(BaseAttentionMetadata):
-    cu: torch.Tensor
-
-    def get_last_indices(self, bs):
-        return self.cu[1 : 1 + bs].long() - 1
-
-
-class CpuBackend(BaseAttentionBackend):
-    def __init__(self, config):
-        self.hkv, self.d = config.num_kv_heads, config.head_dim
-        self.scale = config.head_dim**-0.5
-
-    def prepare_metadata(self, batch):
-        cu = torch.tensor([0] + [r.extend_len for r in batch.reqs]).cumsum(0)
-        batch.attn_metadata = _Meta(cu=cu)
-        return batch.attn_metadata
-
-    def forward(self, q, k, v, kv, layer, batch):
-        ctx = ref_core.get_global_ctx()
-        kv.store_kv(k, v, batch.out_loc.view(-1), layer)
-        kc = kv.k_cache(layer).view(-1, self.hkv, self.d)
-        vc = kv.v_cache(layer).view(-1, self.hkv, self.d)
-        outs, off = [], 0
-        for req in batch.reqs:
-            n = req.extend_len
-            idx = ctx.page_table[req.table_idx, : req.device_len].long()
-            outs.append(_sdpa_prefill_attention(q[off : off + n], kc[idx], vc[idx], cached_len=req.cached_len,
-                                                sm_scale=self.scale))
-            off += n
-        return torch.cat(outs).reshape(q.shape[0], -1)
-
-
-class CpuKV:
-    def __init__(self, L, pages, hkv, d, dtype):
-        self.buf = torch.zeros((2, L, pages, 1, hkv, d), dtype=dtype)
-        self._shape = (pages, hkv, d)
-
-    def k_cache(self, i):
-        return self.buf[0, i]
-
-    def v_cache(self, i):
-        return self.buf[1, i]
-
-    def store_kv(self, k, v, loc, layer):
-        self.buf[0, layer].view(self._shape)[loc.long()] = k
-        self.buf[1, layer].view(self._shape)[loc.long()] = v
-
-    @property
-    def dtype(self):
-        return self.buf.dtype
-
-
-def ref_config(cfg, **changes) -> RefConfig:
-    values = {f.name: getattr(cfg, f.name) for f in dataclasses.fields(cfg)}
-    values.update(attnres_backend="eager", **changes)
-    return RefConfig(**values)
-
-
 def build_llm(cfg, dtype, num_pages: int):
-    rcfg = ref_config(cfg)
+    fields = {f.name: getattr(cfg, f.name) for f in dataclasses.fields(cfg) if f.name != "attnres_backend"}
     with torch.device("meta"):
-        model = MiniMindIMEForCausalLM(rcfg)
-    state = {k: v.to(dtype) for k, v in synthetic_state_dict(model, seed=0).items()}
-    model.load_state_dict(state)
-    model.model._rotary_emb.set_device(torch.device("cpu"))
-    backend = CpuBackend(rcfg)
-    model.attn_backend = backend
-    model.model.attn_backend = backend
-    for layer in model.model.layers.op_list:
-        layer.self_attn._attn_backend = backend
-    ref_core._GLOBAL_CTX = None
-    ctx = ref_core.Context(page_size=1)
-    ctx.kv_cache = CpuKV(rcfg.num_layers, num_pages, rcfg.num_kv_heads, rcfg.head_dim, dtype)
-    ctx.attn_backend = backend
-    ref_core.set_global_ctx(ctx)
-    return types.SimpleNamespace(
-        model=model, tokenizer=SyntheticTokenizer(rcfg.vocab_size), device=torch.device("cpu"), ctx=ctx,
-        config=rcfg, num_pages=num_pages, cache_manager=CacheManager(torch.device("cpu"), num_pages),
-    )
+        model = _mods.minimind.MiniMindIMEForCausalLM(_mods.config.ModelConfig(**fields, attnres_backend="eager"))
+    return reference_run.build_llm(_mods, fields, num_pages, dtype=dtype, state=synthetic_state_dict(model, seed=0),
+                                   tokenizer=SyntheticTokenizer(cfg.vocab_size))
 
 
 class Recorder:
@@ -348,13 +227,13 @@ def reduced(cfg, layers: int, **extra):
     return dataclasses.replace(cfg, num_layers=layers, **extra)
 
 
-def main() -> None:
+def main(out_dir: Path = HERE) -> None:
     torch.manual_seed(0)
     rec = Recorder()
     rec.install()
-    torch.save(gen_sampler(), HERE / "sampler.pt")
-    torch.save(gen_mixer(), HERE / "mixer.pt")
-    torch.save(gen_attention(), HERE / "attention.pt")
+    torch.save(gen_sampler(), out_dir / "sampler.pt")
+    torch.save(gen_mixer(), out_dir / "mixer.pt")
+    torch.save(gen_attention(), out_dir / "attention.pt")
     models = {
         "s10_l2_fp32": (reduced(shapes.S10, 2), torch.float32),
         "s10_l2_bf16": (reduced(shapes.S10, 2), torch.bfloat16),
@@ -362,9 +241,9 @@ def main() -> None:
         "s21_l4_fp32": (reduced(shapes.S21, 4, attnres_num_blocks=2), torch.float32),
     }
     for key, (cfg, dtype) in models.items():
-        torch.save(gen_model(key, cfg, dtype, rec), HERE / f"model_{key}.pt")
+        torch.save(gen_model(key, cfg, dtype, rec), out_dir / f"model_{key}.pt")
         print("wrote", key)
 
 
 if __name__ == "__main__":
-    main()
+    main(Path(sys.argv[1]) if len(sys.argv) > 1 else HERE)

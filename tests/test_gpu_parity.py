@@ -5,11 +5,16 @@ Every round the GPU ran is replayed on the oracle teacher-forced with the GPU's
 tokens (the runtime records the logits each step sampled from), then compared:
 * sampling + step bookkeeping: the oracle sampler, run on the GPU's own logits
   with the same uniforms and bans, reproduces every GPU token bit for bit;
-* the model: per-step log-softmax of GPU vs oracle logits within 2e-2 max-abs,
-  and the raw token log-probabilities the GPU returned within 2e-2;
+* the model: the raw log-probability of every token the GPU returned within a
+  flat 2e-2 of the oracle's (the bf16 logprob bar). The whole-vocabulary
+  log-softmax difference per step is reported beside it, with the bf16 ulp of the
+  row's largest logit for scale;
 * KV placement: the page-table entries of every row and the free-slot FIFO
   order, bit for bit (page_size 1: the reference's slot ids; 16: pages);
-* greedy rounds: GPU argmax == oracle argmax except at bf16 near-ties (top-2 gap);
+* greedy rounds: GPU argmax == oracle argmax except at bf16 near-ties (top-2 gap),
+  and, as a reported statistic, the oracle's own free-running greedy rounds
+  (its tokens fed back) against the GPU's: rows identical and tokens before the
+  first divergence;
 * stop codes / counts / active-token accounting by construction of the replay.
 Sampled tokens are not compared with the oracle's own draws from its own
 logits: with random-init weights the top-k distribution is nearly flat, so bf16
@@ -34,18 +39,14 @@ from oracle.model import OracleModel
 
 pytestmark = pytest.mark.gpu
 
-LOGPROB_TOL = 2e-2  # bf16 logprob parity bar
+LOGPROB_TOL = 2e-2  # bf16 logprob parity bar, flat
 GREEDY_MARGIN = 2e-2  # top-1/top-2 logit gap under which a greedy flip is a bf16 near-tie
 
 
-def _lp_bound(logits: torch.Tensor) -> float:
-    """Log-probability bound: 2e-2, or three bf16 ulps of the row's largest logit
-    when that is coarser (from magnitude 2 up, one ulp is already 0.0156, so a
-    single rounding difference of a logit plus the log-sum-exp shift it causes can
-    pass 2e-2 without any arithmetic difference)."""
+def _ulp(logits: torch.Tensor) -> float:
+    """One bf16 ulp at the row's largest |logit| (diagnostic scale only)."""
     top = float(logits.abs().max())
-    ulp = 2.0 ** (math.floor(math.log2(max(top, 1e-30))) - 7)
-    return max(LOGPROB_TOL, 3 * ulp)
+    return 2.0 ** (math.floor(math.log2(max(top, 1e-30))) - 7)
 
 
 def _models(cfg, page_size: int, num_pages: int):
@@ -76,7 +77,7 @@ def _check_keystroke(llm, engine, oeng, ids: list[int], cfg: ImeGenerationConfig
     g_lp = torch.log_softmax(g_logits, -1)
     o_lp = torch.log_softmax(o_logits.float(), -1)
     stats["prefix_lp_maxdiff"] = max(stats.get("prefix_lp_maxdiff", 0.0), float((g_lp - o_lp).abs().max()))
-    assert float((g_lp - o_lp).abs().max()) < _lp_bound(g_logits)
+    stats["max_logit_ulp"] = max(stats.get("max_logit_ulp", 0.0), _ulp(g_logits))
     greedy = cfg.top_k == 1 and cfg.top_p == 1.0
     for params, res in engine._runtime.rounds:
         forced = dict(output_ids=res.output_ids, counts=res.counts, stop_codes=res.stop_codes)
@@ -90,11 +91,11 @@ def _check_keystroke(llm, engine, oeng, ids: list[int], cfg: ImeGenerationConfig
         for st in tr.steps:
             g_rows = params["step_logits"][st.step][st.rows]
             diff = float((torch.log_softmax(g_rows, -1) - torch.log_softmax(st.logits.float(), -1)).abs().max())
+            # whole-vocabulary difference: reported (one bf16 ulp of a logit near the
+            # row maximum, plus the normaliser shift it causes, is rounding noise);
+            # the 2e-2 bar is asserted on the tokens the GPU returned, below
             stats["step_lp_maxdiff"] = max(stats.get("step_lp_maxdiff", 0.0), diff)
-            # whole-vocabulary diagnostic: one bf16 ulp of the largest logit (plus the
-            # normaliser shift it causes) is rounding noise; the 2e-2 bar is on the
-            # log-probabilities of the tokens the GPU returned (checked below)
-            assert diff < _lp_bound(g_rows), (params["row_offset"], st.step, diff)
+            stats["max_logit_ulp"] = max(stats.get("max_logit_ulp", 0.0), _ulp(g_rows))
             assert st.ext_tokens == st.tokens, (params["row_offset"], st.step, st.ext_tokens, st.tokens)
             for i, r in enumerate(st.rows):
                 stats["tokens"] = stats.get("tokens", 0) + 1
@@ -105,7 +106,7 @@ def _check_keystroke(llm, engine, oeng, ids: list[int], cfg: ImeGenerationConfig
                 if st.step < res.counts[r]:
                     diff = abs(float(res.token_logprobs[r, st.step]) - st.logprobs[i])
                     stats["lp_maxdiff"] = max(stats.get("lp_maxdiff", 0.0), diff)
-                    assert diff < _lp_bound(g_rows[i]), (params, st.step, r, diff)
+                    assert diff < LOGPROB_TOL, (params["row_offset"], st.step, r, diff)
         assert tr.active_model_tokens == res.active_model_tokens
         assert len(tr.allocated) == res.pages_consumed
         oeng.release(tr.allocated)
@@ -115,6 +116,38 @@ def _check_keystroke(llm, engine, oeng, ids: list[int], cfg: ImeGenerationConfig
     used_rows = result.sampling_attempts
     assert np.array_equal(gpu_table[:used_rows], oeng.page_table[:used_rows, :width])
     assert _ring_free(llm) == oeng.free
+    if greedy:
+        _free_running_greedy(engine, oeng, o_logits, stats)
+
+
+def _free_running_greedy(engine, oeng, o_logits, stats: dict) -> None:
+    """Reported statistic: the oracle's own greedy rounds (its argmax fed back, no
+    forcing) against the GPU's rounds. The oracle's FIFO and page table are put
+    back afterwards, so the teacher-forced comparison of later keystrokes is
+    unaffected (the slots it wrote were free and are rewritten before any read)."""
+    free, table = list(oeng.free), oeng.page_table.copy()
+    for params, res in engine._runtime.rounds:
+        tr = oeng.run_round(
+            prefix_logits=o_logits, prefix_len=params["prefix_len"], row_offset=params["row_offset"],
+            attempts=params["attempts"], max_new_tokens=params["max_new_tokens"],
+            min_new_tokens=params["min_new_tokens"], seed=params["seed"], temperature=params["temperature"],
+            top_k=params["top_k"], top_p=params["top_p"], banned_sequences=params["banned_sequences"],
+            ban_min_prefix=params["ban_min_prefix"],
+        )
+        for r in range(params["attempts"]):
+            g = list(res.output_ids[r, : res.counts[r]]) + [("stop", res.stop_codes[r])]
+            o = list(tr.output_ids[r, : tr.counts[r]]) + [("stop", tr.stop_codes[r])]
+            agree = 0
+            for a, b in zip(g, o):
+                if a != b:
+                    break
+                agree += 1
+            stats["free_rows"] = stats.get("free_rows", 0) + 1
+            stats["free_rows_identical"] = stats.get("free_rows_identical", 0) + int(g == o)
+            stats["free_tokens"] = stats.get("free_tokens", 0) + res.counts[r]
+            stats["free_tokens_before_divergence"] = (stats.get("free_tokens_before_divergence", 0)
+                                                     + min(agree, res.counts[r]))
+    oeng.free, oeng.page_table = free, table
 
 
 CASES = [
@@ -123,6 +156,7 @@ CASES = [
     ("s06_l2_p16", dataclasses.replace(shapes.S06, num_layers=2), 16, 128),
     ("s21_l4", dataclasses.replace(shapes.S21, num_layers=4, attnres_num_blocks=2), 1, 1024),
     ("s10_full", shapes.S10, 16, 256),
+    ("s06_full", shapes.S06, 16, 256),
 ]
 
 
@@ -143,3 +177,47 @@ def test_keystroke_stream_parity(name, cfg, page_size, num_pages) -> None:
         _check_keystroke(llm, engine, oeng, ids, cfg_k, stats)
     print(name, stats)
     assert stats["tokens"] > 100
+
+
+def test_s21_full_depth_refill_parity() -> None:
+    """BASELINE config 4 at the depth it is benchmarked: S21 (32 layers, 8 AttnRes
+    blocks, 65 mixers per forward), a 16-token prefix after [BOS], a first round of
+    8 candidates and refill rounds of 8 up to 24, 16 tokens each, 16-token pages.
+    A 2-character candidate limit makes every candidate invalid, so the refill
+    runs to the 24-attempt budget (each round freeing the previous round's suffix
+    pages), as in the benchmark; a second keystroke extends the prefix (LCP reuse)."""
+    llm, engine, oeng = _models(shapes.S21, 16, 256)
+    g = torch.Generator().manual_seed(21)
+    ids = [1] + torch.randint(10, shapes.S21.vocab_size, (17,), generator=g).tolist()
+    cfg4 = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=24, refill_batch_size=8,
+                               max_new_tokens=16, temperature=0.8, top_k=50, top_p=0.9, max_candidate_chars=2,
+                               seed=0)
+    stats: dict = {}
+    for k in (ids[:17], ids):
+        _check_keystroke(llm, engine, oeng, k, cfg4, stats)
+        # a first round of 8 plus refills up to the 24-attempt budget
+        assert sum(p["attempts"] for p, _ in engine._runtime.rounds) == 24
+    print("s21_full", stats)
+    assert stats["tokens"] > 300
+
+
+@pytest.mark.parametrize("shape", ["S10", "S10L"])
+def test_greedy_prefix_sweep_parity(shape) -> None:
+    """BASELINE config 3 in greedy mode (top_k 1, top_p 1.0): prefixes of 4, 8, 16
+    and 32 tokens after [BOS], 8 candidates x 16 tokens. The 17- and 33-token
+    prefills run the tcgen05 GEMMs (more than 16 rows), so the tensor-core prefill
+    is inside a keystroke parity run. Greedy tokens are compared teacher-forced
+    (bit-exact except at bf16 near-ties), and the oracle's free-running greedy
+    rounds are reported against the GPU's."""
+    cfg = getattr(shapes, shape)
+    llm, engine, oeng = _models(cfg, 16, 256)
+    greedy = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=8, refill_batch_size=8,
+                                 max_new_tokens=16, temperature=1.0, top_k=1, top_p=1.0, min_new_tokens=0, seed=3)
+    g = torch.Generator().manual_seed(77)
+    stats: dict = {}
+    for n in (4, 8, 16, 32):
+        ids = [1] + torch.randint(10, cfg.vocab_size, (n,), generator=g).tolist()
+        _check_keystroke(llm, engine, oeng, ids, greedy, stats)
+    print(shape, "greedy sweep", stats)
+    assert stats["tokens"] >= 4 * 8 * 8
+    assert stats["free_rows"] == 4 * 8
