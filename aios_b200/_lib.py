@@ -113,6 +113,34 @@ class GroupPtrs(ctypes.Structure):
     ]
 
 
+class DecodeLayer(ctypes.Structure):
+    """Mirror of ``aiosb_decode_layer`` (device addresses)."""
+
+    _fields_ = [(name, _p) for name in ("w_qkv", "w_o", "w_gate_up", "w_down", "in_norm", "post_norm", "q_norm",
+                                        "k_norm", "k_cache", "v_cache")]
+
+
+class DecodeStepArgs(ctypes.Structure):
+    """Mirror of ``aiosb_decode_step_args``."""
+
+    _fields_ = [
+        ("layers", _p),
+        ("num_layers", _i32), ("rows", _i32), ("hidden", _i32), ("intermediate", _i32), ("num_qo_heads", _i32),
+        ("num_kv_heads", _i32), ("head_dim", _i32), ("vocab", _i32),
+        ("eps", _f32), ("scale", _f32),
+        ("embed", _p), ("final_norm", _p), ("lm_head", _p),
+        ("tokens", _p), ("positions", _p), ("out_loc", _p), ("row_table", _p), ("seq_lens", _p),
+        ("prefix_len", _p), ("active", _p), ("page_table", _p),
+        ("table_stride", _i64), ("num_slots", _i64),
+        ("cos_tab", _p), ("sin_tab", _p), ("max_pos", _i32),
+        ("resid_f32", _p), ("resid", _p),
+        ("qkv", _p), ("qkv_stride", _i64), ("attn", _p), ("attn_stride", _i64), ("act", _p), ("act_stride", _i64),
+        ("logits", _p), ("logits_stride", _i64),
+        ("sync", _p), ("status", _p), ("wait_limit_ns", _u64), ("test_extra_arrivals", ctypes.c_uint32),
+        ("grid_ctas", _i32),
+    ]
+
+
 _SIGNATURES = {
     "aiosb_version": ([], _i32),
     "aiosb_last_error": ([ctypes.c_char_p, ctypes.c_size_t], _i32),
@@ -166,6 +194,8 @@ _SIGNATURES = {
     "aiosb_group_begin": ([ctypes.POINTER(GroupPtrs), _p, _u64, _i64, _i64, _p], _i32),
     "aiosb_group_step": ([ctypes.POINTER(GroupPtrs), _i64, _i64, _i64, _p], _i32),
     "aiosb_group_step_static": ([ctypes.POINTER(GroupPtrs), _i64, _i64, _i64, _p], _i32),
+    "aiosb_decode_step_sync_words": ([_i64], _i64),
+    "aiosb_decode_step": ([ctypes.POINTER(DecodeStepArgs), _p], _i32),
 }
 
 EXPORTED = tuple(_SIGNATURES)
@@ -214,7 +244,7 @@ def check(rc: int, what: str) -> None:
 # Entry points that launch kernels; `launches` counts their successful calls
 # (the bench reports it as the number of this library's kernel launches).
 _NON_LAUNCHING = frozenset({"aiosb_version", "aiosb_last_error", "aiosb_host_device_pointer",
-                            "aiosb_prefill_tile_tokens"})
+                            "aiosb_prefill_tile_tokens", "aiosb_decode_step_sync_words"})
 launches = 0
 
 

@@ -25,6 +25,7 @@ host-mapped flag that ``CancellationToken.cancel`` writes.
 from __future__ import annotations
 
 import ctypes
+import os
 import time
 from dataclasses import dataclass
 
@@ -38,6 +39,11 @@ from ..kernel import ops
 
 MAX_TERMINAL = 16
 MAX_MINLEN = 32
+
+# The persistent decode step (one launch per decode forward) serves the
+# standard-residual models with these dims; AIOSB_PERSISTENT_DECODE=0 selects the
+# per-kernel forward instead (both are complete forwards).
+_PERSISTENT = os.environ.get("AIOSB_PERSISTENT_DECODE", "1") != "0"
 
 
 @dataclass
@@ -157,6 +163,74 @@ class CandidateGroupRuntime:
         self.record_logits = False
         self.step_logits: list[torch.Tensor] = []
         self._top_k_cap = 2048
+        self._step_plan = self._persistent_plan() if _PERSISTENT else None
+
+    # ------------------------------------------------------- persistent step
+    def _persistent_plan(self):
+        """Device buffers and argument block of aiosb_decode_step, or None when
+        the model is not one the persistent kernel serves."""
+        from ..models.qwen3 import Qwen3ForCausalLM
+
+        llm, cfg = self.llm, self.llm.config
+        model = llm.model
+        if (not isinstance(model, Qwen3ForCausalLM) or cfg.residual_type != "standard"
+                or type(model.attn_backend).__name__ != "B200AttentionBackend"):
+            return None  # the Block AttnRes trunk keeps the per-kernel forward
+        if (cfg.hidden_size != 768 or cfg.intermediate_size != 2048 or cfg.head_dim not in (64, 96)
+                or cfg.num_qo_heads % cfg.num_kv_heads or cfg.num_qo_heads // cfg.num_kv_heads > 7
+                or cfg.num_qo_heads * cfg.head_dim != 768 or cfg.vocab_size % 16 or self.max_rows > 16):
+            return None
+        dev = self.device
+        rows = self.max_rows
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        nqkv = (cfg.num_qo_heads + 2 * cfg.num_kv_heads) * cfg.head_dim
+        kv = llm.mha_kv_cache
+        layers = model.model.layers.op_list
+        descs = (_lib.DecodeLayer * len(layers))()
+        for i, layer in enumerate(layers):
+            at, mlp = layer.self_attn, layer.mlp
+            descs[i] = _lib.DecodeLayer(
+                w_qkv=at.qkv_proj.weight.data_ptr(), w_o=at.o_proj.weight.data_ptr(),
+                w_gate_up=mlp.gate_up_proj.packed_weight().data_ptr(), w_down=mlp.down_proj.weight.data_ptr(),
+                in_norm=layer.input_layernorm.weight.data_ptr(),
+                post_norm=layer.post_attention_layernorm.weight.data_ptr(),
+                q_norm=at.q_norm.weight.data_ptr(), k_norm=at.k_norm.weight.data_ptr(),
+                k_cache=kv.k_slots(i).data_ptr(), v_cache=kv.v_slots(i).data_ptr(),
+            )
+        plan = dict(
+            layers=torch.frombuffer(bytearray(bytes(descs)), dtype=torch.uint8).to(dev),
+            resid_f32=torch.zeros(rows, 768, dtype=torch.float32, device=dev),
+            resid=torch.zeros(rows, 768, **bf), qkv=torch.zeros(rows, nqkv, **bf),
+            attn=torch.zeros(rows, 768, **bf), act=torch.zeros(rows, 2048, **bf),
+            sync=torch.zeros(int(_lib.load().aiosb_decode_step_sync_words(len(layers))), dtype=torch.int32,
+                             device=dev),
+        )
+        cos, sin = model.model._rotary_emb.tables()
+        embed = model.model.embed_tokens.weight
+        plan["args"] = _lib.DecodeStepArgs(
+            layers=plan["layers"].data_ptr(), num_layers=len(layers), rows=rows, hidden=768, intermediate=2048,
+            num_qo_heads=cfg.num_qo_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
+            vocab=cfg.vocab_size, eps=cfg.rms_norm_eps, scale=cfg.head_dim ** -0.5,
+            embed=embed.data_ptr(), final_norm=model.model.norm.weight.data_ptr(),
+            lm_head=model.lm_head._w().data_ptr(),
+            tokens=self.tokens.data_ptr(), positions=self.positions.data_ptr(), out_loc=self.out_loc.data_ptr(),
+            row_table=self.row_table.data_ptr(), seq_lens=self.seq_lens.data_ptr(),
+            prefix_len=self.prefix_len_view.data_ptr(), active=self.active.data_ptr(),
+            page_table=llm.ctx.page_table.data_ptr(), table_stride=llm.ctx.page_table.stride(0),
+            num_slots=kv.num_slots, cos_tab=cos.data_ptr(), sin_tab=sin.data_ptr(), max_pos=cos.shape[0],
+            resid_f32=plan["resid_f32"].data_ptr(), resid=plan["resid"].data_ptr(),
+            qkv=plan["qkv"].data_ptr(), qkv_stride=nqkv, attn=plan["attn"].data_ptr(), attn_stride=768,
+            act=plan["act"].data_ptr(), act_stride=2048, logits=self.logits.data_ptr(),
+            logits_stride=self.logits.stride(0), sync=plan["sync"].data_ptr(),
+            status=ops.status_word(dev).data_ptr(), wait_limit_ns=0, test_extra_arrivals=0, grid_ctas=0,
+        )
+        self._keep = (plan, descs)  # weights and buffers the argument block points to
+        return plan
+
+    def _decode_step(self, rows: int) -> None:
+        args = _lib.DecodeStepArgs.from_buffer_copy(self._step_plan["args"])
+        args.rows = rows
+        _lib.call("aiosb_decode_step", ctypes.byref(args), self._stream())
 
     # ------------------------------------------------------------------ graphs
     def _decode_batch(self, rows: int) -> Batch:
@@ -181,6 +255,9 @@ class CandidateGroupRuntime:
 
     def _step_and_forward(self, rows: int, batch: Batch) -> None:
         self._group_step(rows)
+        if self._step_plan is not None:
+            self._decode_step(rows)
+            return
         with self.llm.ctx.forward_batch(batch):
             self.llm.model.forward()
 

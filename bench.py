@@ -21,6 +21,7 @@ the barrier and the max-over-ranks timing use a small NCCL all-reduce.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -229,6 +230,9 @@ def reference_subprocess(keystrokes: int) -> dict | None:
 # below the 201,326,592 algorithmic bytes: with cache-streaming weight loads,
 # about 16% of the weights are still in L2 when the next replay reads them.
 DECODE_LINEAR_TRAFFIC = 168_907_008
+# The same for one launch of the persistent decode-step kernel (None until an ncu
+# capture of it exists).
+DECODE_STEP_TRAFFIC = None
 
 
 def max_over_ranks(values: list[float], world: int, device) -> list[float]:
@@ -313,6 +317,83 @@ def decode_linear_roofline(llm, peaks: dict) -> dict:
             "traffic_unit": "bytes per decode step (57 launches)", "algorithmic_bytes_per_step": wbytes,
             "launches_per_step": launches, "us_per_step": round(ms * 1e3, 2),
             "us_per_launch": round(ms * 1e3 / launches, 3)}
+
+
+def decode_step_roofline(engine, llm, peaks: dict) -> dict:
+    """Times the persistent decode-step kernel alone (CUDA events on the launching
+    stream, a graph of back-to-back launches): one decode forward of the bench
+    group, 8 active rows at the first decode position after the 13-token prefix of
+    the last keystroke (so its prefix KV and page-table rows are real). Algorithmic
+    bytes per launch: every weight once (201,326,592 B for S10) plus the
+    attention's K/V reads (the prefix once per KV head, each row's suffix) and its
+    q / o rows (the cascade formula)."""
+    from aios_b200 import _lib
+
+    rt = engine._runtime
+    plan = rt._step_plan
+    if plan is None:
+        return decode_linear_roofline(llm, peaks)
+    dev = llm.device
+    cfg = llm.config
+    rows = 8
+    prefix = engine._prefix_slots
+    p_len = len(prefix)
+    kv = llm.mha_kv_cache
+    rt.active[:rows].fill_(1)
+    rt.positions[:rows].fill_(p_len)
+    rt.seq_lens[:rows].fill_(p_len + 1)
+    rt.row_table[:rows].copy_(torch.arange(rows, dtype=torch.int32, device=dev))
+    rt.prefix_len_view.fill_(p_len)
+    spare = torch.arange(kv.num_slots - rows, kv.num_slots, dtype=torch.int32, device=dev)  # unused pool tail
+    rt.out_loc[:rows].copy_(spare)
+    llm.ctx.page_table[:rows, p_len].copy_(spare)
+    rt.tokens[:rows].copy_(torch.arange(100, 100 + rows, dtype=torch.int32, device=dev))
+    args = _lib.DecodeStepArgs.from_buffer_copy(plan["args"])
+    args.rows = rows
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(3):
+        _lib.call("aiosb_decode_step", ctypes.byref(args), stream.cuda_stream)
+    torch.cuda.synchronize(dev)
+    per_graph = 10
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(per_graph):
+            _lib.call("aiosb_decode_step", ctypes.byref(args), torch.cuda.current_stream(dev).cuda_stream)
+    g.replay()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    start.record(stream)
+    for _ in range(reps):
+        g.replay()
+    end.record(stream)
+    end.synchronize()
+    us = start.elapsed_time(end) / (reps * per_graph) * 1e3
+    # one extra launch in its own NVTX range: the one an ncu traffic capture selects
+    torch.cuda.nvtx.range_push("decode_step")
+    _lib.call("aiosb_decode_step", ctypes.byref(args), stream.cuda_stream)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize(dev)
+    from aios_b200.kernel import ops
+
+    ops.check_status(dev)
+    rt.active.zero_()
+    layers = llm.model.model.layers.op_list
+    wbytes = sum(layer.self_attn.qkv_proj.weight.numel() + layer.self_attn.o_proj.weight.numel()
+                 + layer.mlp.gate_up_proj.weight.numel() + layer.mlp.down_proj.weight.numel() for layer in layers)
+    wbytes = 2 * (wbytes + llm.model.model.embed_tokens.weight.numel())
+    hkv, hd, hq = cfg.num_kv_heads, cfg.head_dim, cfg.num_qo_heads
+    attn_bytes = len(layers) * (p_len * hkv * hd * 2 * 2 + rows * 1 * hkv * hd * 2 * 2 + 2 * rows * hq * hd * 2)
+    total = wbytes + attn_bytes
+    achieved = total / (us * 1e-6) / 1e9
+    peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
+    return {"bound": "hbm", "kernel": "decode_step_kernel (persistent decode forward, 8 rows, one launch per step)",
+            "achieved": round(achieved, 1), "peak": peak,
+            "peak_source": "measured (burst copy)" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": DECODE_STEP_TRAFFIC,
+            "traffic_unit": "bytes per launch (dram read + write, ncu)",
+            "algorithmic_bytes_per_launch": total, "weight_bytes": wbytes, "attention_bytes": attn_bytes,
+            "us_per_launch": round(us, 2), "launches_timed": reps * per_graph}
 
 
 def mixer_chain(dev) -> dict:
@@ -497,8 +578,7 @@ def config_sweeps(engine, llm, dev) -> dict:
     from aios_b200 import ImeCompletionEngine, ImeGenerationConfig, LLM
     from aios_b200.models import shapes
 
-    out = {"s06_keystroke": shape_keystroke("S06", dev), "s10l_keystroke": shape_keystroke("S10L", dev),
-           "s10_prefix_sweep": {}}
+    out = {"s10_prefix_sweep": {}}
     cfg3 = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=8, refill_batch_size=8,
                                max_new_tokens=16, temperature=0.8, top_k=50, top_p=0.9, seed=0)
     for n in (4, 8, 16, 32):
@@ -506,6 +586,10 @@ def config_sweeps(engine, llm, dev) -> dict:
         lat = [r.latency_ms for r in res]
         out["s10_prefix_sweep"][str(n)] = {"p50_ms": round(statistics.median(lat), 3),
                                            "p95_ms": round(percentile(lat, 0.95), 3)}
+    # the other shapes build their own LLM (each takes over the process-global
+    # context), so they run after every keystroke of the S10 engine
+    out["s06_keystroke"] = shape_keystroke("S06", dev)
+    out["s10l_keystroke"] = shape_keystroke("S10L", dev)
     llm21 = LLM(config=shapes.S21, seed=0, page_size=16, num_pages=256, device=str(dev))
     eng21 = ImeCompletionEngine(llm21)
     cfg4 = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=24, refill_batch_size=8,
@@ -567,7 +651,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     if rank != 0:
         return None
     peaks = measured_peaks()
-    roof = None if args.no_extras else decode_linear_roofline(llm, peaks)
+    roof = None if args.no_extras else decode_step_roofline(engine, llm, peaks)
     mixer = None if args.no_extras else mixer_chain(dev)
     kstream = None if args.no_extras else keystroke_stream(engine, llm, seed=4321 + rank)
     sweeps = None if args.no_extras else config_sweeps(engine, llm, dev)
@@ -610,6 +694,8 @@ def kernel_case(name: str) -> None:
     """Small single-kernel workloads for full ncu captures (1 GPU, a few GB).
     linears: the decode linears of every S10 layer in order, 8 rows, eagerly
     (the 176 MB of layer weights exceed L2, so each launch reads DRAM);
+    decode_step: two bench keystrokes (the persistent decode-step kernel, 11
+    launches each, 201 MB of weights per launch);
     mixer: the AttnRes mixer on 32768 tokens of 8 bank sources + partial
     (the stream kernel; 504 MB of traffic per launch)."""
     from aios_b200 import LLM, _lib
@@ -635,6 +721,15 @@ def kernel_case(name: str) -> None:
                 ops.linear_add_stat(xo, a.o_proj.weight, res)
                 ops.linear_stat_norm(stats, nw, 1e-6, m.gate_up_proj.packed_weight(), epilogue=_lib.EPI_SILU_MUL)
                 ops.linear_add_stat(xf, m.down_proj.weight, res)
+    elif name == "decode_step":
+        # two bench keystrokes: 11 persistent decode-step launches each (S10, 8 rows)
+        from aios_b200 import ImeCompletionEngine
+
+        llm = LLM(config=shapes.S10, seed=0, page_size=16, num_pages=256, device="cuda:0")
+        engine = ImeCompletionEngine(llm)
+        for text in prefixes(llm.tokenizer, llm.config.vocab_size, 2, seed=1234):
+            engine.reset_prefix_cache()
+            engine.complete(text, keystroke_config())
     elif name == "mixer":
         g = torch.Generator(device=dev).manual_seed(0)
         bank = torch.randn(8, 32768, 768, generator=g, device=dev).to(torch.bfloat16)
@@ -659,7 +754,7 @@ def main() -> None:
     ap.add_argument("--cpu-sample", type=int, default=15, help="keystrokes timed for the CPU baseline (0: skip)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the roofline / mixer micro-benchmarks (profiling runs of the keystroke only)")
-    ap.add_argument("--kernel-case", choices=["linears", "mixer"],
+    ap.add_argument("--kernel-case", choices=["linears", "mixer", "decode_step"],
                     help="run one small single-kernel workload for a full ncu capture, then exit")
     args = ap.parse_args()
     if args.kernel_case:

@@ -395,6 +395,78 @@ AIOSB_API int aiosb_group_begin(const aiosb_group_ptrs* g, const void* prefix_lo
  * memory, so one captured launch serves every step of every round. */
 AIOSB_API int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t vocab, int64_t top_k_max, void* stream);
 
+/* ---- Persistent decode step ------------------------------------------------
+ * Replaces one decode forward of the standard-residual decoder,
+ * Qwen3ForCausalLM.forward (aios/models/qwen3.py:101-173) as driven by
+ * ImeCompletionEngine._decode_step (aios/ime.py:1219-1251): the embedding, every
+ * layer (RMSNormFused + qkv linear, q/k RMSNorm + RoPE + KV store + paged decode
+ * attention, o linear + residual, RMSNormFused + gate/up linear + SwiGLU, down
+ * linear + residual), the final norm and the LM head, in ONE kernel launch (one
+ * CTA per SM; a producer warp streams each CTA's weight tiles into shared memory
+ * while its consumer warps run the dependent phases, synchronised through the
+ * caller's `sync` words with bounded waits). Serves hidden 768, intermediate
+ * 2048, head_dim 64 or 96, at most 7 query heads per KV head, 1..16 rows. */
+typedef struct aiosb_decode_layer {
+  const void* w_qkv;      /* [(Hq + 2 Hkv) d, 768] bf16 (packed q | k | v)            */
+  const void* w_o;        /* [768, Hq d] bf16                                         */
+  const void* w_gate_up;  /* [4096, 768] bf16 in 64-row blocks [g0..63|u0..63|g64..] */
+  const void* w_down;     /* [768, 2048] bf16                                         */
+  const void* in_norm;    /* [768] bf16 input_layernorm weight                        */
+  const void* post_norm;  /* [768] bf16 post_attention_layernorm weight               */
+  const void* q_norm;     /* [d] bf16                                                 */
+  const void* k_norm;     /* [d] bf16                                                 */
+  void* k_cache;          /* [num_slots, Hkv, d] bf16: this layer's keys              */
+  void* v_cache;          /* [num_slots, Hkv, d] bf16                                 */
+} aiosb_decode_layer;
+
+typedef struct aiosb_decode_step_args {
+  const aiosb_decode_layer* layers; /* device array [num_layers]                       */
+  int32_t num_layers, rows, hidden, intermediate, num_qo_heads, num_kv_heads, head_dim, vocab;
+  float eps;                        /* RMSNorm epsilon                                  */
+  float scale;                      /* attention scale (head_dim^-0.5)                  */
+  const void* embed;                /* [vocab, 768] bf16                                */
+  const void* final_norm;           /* [768] bf16                                       */
+  const void* lm_head;              /* [vocab, 768] bf16 (the embedding when tied)      */
+  /* decode metadata (written by aiosb_group_step before this launch) */
+  const int32_t* tokens;            /* [rows] input ids                                 */
+  const int32_t* positions;         /* [rows]                                           */
+  const int32_t* out_loc;           /* [rows] KV slot of the new token                  */
+  const int32_t* row_table;         /* [rows] page-table row of each local row          */
+  const int32_t* seq_lens;          /* [rows] keys per row including the new one        */
+  const int32_t* prefix_len;        /* device scalar: shared prefix keys                */
+  const int32_t* active;            /* [rows] nonzero = row runs, or NULL               */
+  const int32_t* page_table;
+  int64_t table_stride;
+  int64_t num_slots;
+  const void* cos_tab;              /* [max_pos, d] bf16 RoPE tables                    */
+  const void* sin_tab;
+  int32_t max_pos;
+  /* caller-owned work buffers, 16-byte aligned */
+  float* resid_f32;                 /* [rows, 768] fp32 residual stream                 */
+  void* resid;                      /* [rows, 768] bf16 residual                        */
+  void* qkv;  int64_t qkv_stride;   /* [rows, (Hq + 2 Hkv) d] bf16                      */
+  void* attn; int64_t attn_stride;  /* [rows, Hq d] bf16                                */
+  void* act;  int64_t act_stride;   /* [rows, 2048] bf16                                */
+  void* logits; int64_t logits_stride; /* [rows, vocab] bf16 output                     */
+  uint32_t* sync;                   /* [aiosb_decode_step_sync_words(num_layers)], zero
+                                       before the first launch; every launch leaves it
+                                       zero again                                        */
+  int32_t* status;
+  uint64_t wait_limit_ns;           /* bound of every wait; 0 = 2 s                     */
+  uint32_t test_extra_arrivals;     /* 0. Tests only: every phase wait then needs this
+                                       many arrivals more than the grid has, so it runs
+                                       out and reports AIOSB_DEV_WAIT_TIMEOUT            */
+  int32_t grid_ctas;                /* 0 = one CTA per SM                               */
+} aiosb_decode_step_args;
+
+/* Words of the `sync` array for a model of num_layers layers. */
+AIOSB_API int64_t aiosb_decode_step_sync_words(int64_t num_layers);
+
+/* One decode forward (see above). Launches with programmatic dependent launch: the
+ * weight streaming starts while the previous kernel (the group step) runs; the
+ * phases wait for it. Launches that use the same `sync` array must not overlap. */
+AIOSB_API int aiosb_decode_step(const aiosb_decode_step_args* args, void* stream);
+
 /* aiosb_group_step without the caller's scratch array. No counterpart in the
  * reference: it is an addition for callers that cannot call cudaMalloc, such as
  * a plugin inside a host process that owns all device memory through its own

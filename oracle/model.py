@@ -8,7 +8,11 @@ explicit slot-addressed KV cache (the MHAKVCache layout flattened to
 ``dtype=torch.float32`` is the pure-fp32 restatement (pinned against the
 reference run in fp32); ``dtype=torch.bfloat16`` keeps bf16 storage between ops
 with the reference's rounding points: every linear output, the norms, bf16 RoPE
-arithmetic, the AttnRes weights and the residual adds. Matmuls accumulate in fp32.
+arithmetic, the AttnRes weights and the residual adds. Matmuls accumulate in fp32
+(``accumulate="fp32"``, as the reference's CPU run does), or in fp64
+(``accumulate="fp64"``: every linear output is then the bf16 rounding of the
+exact dot product). The two bf16 variants bound the rounding noise between
+faithful implementations that differ only in summation order.
 """
 
 from __future__ import annotations
@@ -32,9 +36,12 @@ class Request:
 
 class OracleModel:
     def __init__(self, config, state: dict[str, torch.Tensor], dtype: torch.dtype = torch.float32,
-                 num_slots: int = 4096, mixer: str = "fused") -> None:
+                 num_slots: int = 4096, mixer: str = "fused", accumulate: str = "fp32") -> None:
         self.cfg = config
         self.dtype = dtype
+        if accumulate not in ("fp32", "fp64"):
+            raise ValueError("accumulate must be 'fp32' or 'fp64'")
+        self._acc = torch.float64 if accumulate == "fp64" else torch.float32
         self.w = {k: v.detach().to("cpu", dtype) for k, v in state.items()}
         self.hq, self.hkv, self.d = config.num_qo_heads, config.num_kv_heads, config.head_dim
         self.eps = config.rms_norm_eps
@@ -56,7 +63,7 @@ class OracleModel:
 
     # ---- building blocks -------------------------------------------------------
     def _linear(self, x: torch.Tensor, name: str) -> torch.Tensor:
-        return (x.float() @ self.w[name].float().T).to(self.dtype)
+        return (x.to(self._acc) @ self.w[name].to(self._acc).T).float().to(self.dtype)
 
     def _attention(self, layer: int, prefix: str, x: torch.Tensor, reqs: list[Request]) -> torch.Tensor:
         hq, hkv, d = self.hq, self.hkv, self.d

@@ -13,7 +13,7 @@ HEADER = Path(__file__).resolve().parents[1] / "include" / "aios_b200.h"
 
 
 def _declared() -> set[str]:
-    return set(re.findall(r"AIOSB_API\s+int\s+(aiosb_\w+)\s*\(", HEADER.read_text()))
+    return set(re.findall(r"AIOSB_API\s+(?:int|int64_t)\s+(aiosb_\w+)\s*\(", HEADER.read_text()))
 
 
 def test_library_exports_every_declared_symbol() -> None:
