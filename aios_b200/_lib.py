@@ -133,10 +133,8 @@ class DecodeStepArgs(ctypes.Structure):
         ("prefix_len", _p), ("active", _p), ("page_table", _p),
         ("table_stride", _i64), ("num_slots", _i64),
         ("cos_tab", _p), ("sin_tab", _p), ("max_pos", _i32),
-        ("resid_f32", _p), ("resid", _p),
-        ("qkv", _p), ("qkv_stride", _i64), ("attn", _p), ("attn_stride", _i64), ("act", _p), ("act_stride", _i64),
-        ("logits", _p), ("logits_stride", _i64),
-        ("sync", _p), ("status", _p), ("wait_limit_ns", _u64), ("test_extra_arrivals", ctypes.c_uint32),
+        ("work", _p), ("logits", _p), ("logits_stride", _i64),
+        ("sync", _p), ("status", _p), ("wait_limit_ns", _u64), ("test_flag_skew", ctypes.c_uint32),
         ("grid_ctas", _i32),
     ]
 
@@ -194,7 +192,8 @@ _SIGNATURES = {
     "aiosb_group_begin": ([ctypes.POINTER(GroupPtrs), _p, _u64, _i64, _i64, _p], _i32),
     "aiosb_group_step": ([ctypes.POINTER(GroupPtrs), _i64, _i64, _i64, _p], _i32),
     "aiosb_group_step_static": ([ctypes.POINTER(GroupPtrs), _i64, _i64, _i64, _p], _i32),
-    "aiosb_decode_step_sync_words": ([_i64], _i64),
+    "aiosb_decode_step_sync_words": ([], _i64),
+    "aiosb_decode_step_work_bytes": ([_i64, _i64, _i64], _i64),
     "aiosb_decode_step": ([ctypes.POINTER(DecodeStepArgs), _p], _i32),
 }
 
@@ -244,7 +243,8 @@ def check(rc: int, what: str) -> None:
 # Entry points that launch kernels; `launches` counts their successful calls
 # (the bench reports it as the number of this library's kernel launches).
 _NON_LAUNCHING = frozenset({"aiosb_version", "aiosb_last_error", "aiosb_host_device_pointer",
-                            "aiosb_prefill_tile_tokens", "aiosb_decode_step_sync_words"})
+                            "aiosb_prefill_tile_tokens", "aiosb_decode_step_sync_words",
+                            "aiosb_decode_step_work_bytes"})
 launches = 0
 
 

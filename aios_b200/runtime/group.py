@@ -40,10 +40,14 @@ from ..kernel import ops
 MAX_TERMINAL = 16
 MAX_MINLEN = 32
 
-# The persistent decode step (one launch per decode forward) serves the
-# standard-residual models with these dims; AIOSB_PERSISTENT_DECODE=0 selects the
-# per-kernel forward instead (both are complete forwards).
-_PERSISTENT = os.environ.get("AIOSB_PERSISTENT_DECODE", "1") != "0"
+# The persistent decode step (one launch per decode forward, aiosb_decode_step)
+# serves the standard-residual models with these dims when
+# AIOSB_PERSISTENT_DECODE=1. The default is the per-kernel forward: on B200 its
+# chain of programmatic-dependent launches (about 2.5 us per linear) beats the
+# persistent kernel's cross-CTA exchanges through L2 (measured 326-405 us per
+# S10 step against about 220 us). Both are complete forwards with the same
+# rounding points.
+_PERSISTENT = os.environ.get("AIOSB_PERSISTENT_DECODE", "0") == "1"
 
 
 @dataclass
@@ -165,6 +169,15 @@ class CandidateGroupRuntime:
         self._top_k_cap = 2048
         self._step_plan = self._persistent_plan() if _PERSISTENT else None
 
+    def use_persistent_step(self, enabled: bool = True) -> bool:
+        """Switches this runtime's decode forward to (or away from) the persistent
+        decode-step kernel; returns whether it is now in use (False when the model
+        is not one the kernel serves). Captured step graphs are dropped."""
+        self._step_plan = self._persistent_plan() if enabled else None
+        self._graphs.clear()
+        self._graph_launches.clear()
+        return self._step_plan is not None
+
     # ------------------------------------------------------- persistent step
     def _persistent_plan(self):
         """Device buffers and argument block of aiosb_decode_step, or None when
@@ -181,9 +194,6 @@ class CandidateGroupRuntime:
                 or cfg.num_qo_heads * cfg.head_dim != 768 or cfg.vocab_size % 16 or self.max_rows > 16):
             return None
         dev = self.device
-        rows = self.max_rows
-        bf = dict(dtype=torch.bfloat16, device=dev)
-        nqkv = (cfg.num_qo_heads + 2 * cfg.num_kv_heads) * cfg.head_dim
         kv = llm.mha_kv_cache
         layers = model.model.layers.op_list
         descs = (_lib.DecodeLayer * len(layers))()
@@ -197,18 +207,19 @@ class CandidateGroupRuntime:
                 q_norm=at.q_norm.weight.data_ptr(), k_norm=at.k_norm.weight.data_ptr(),
                 k_cache=kv.k_slots(i).data_ptr(), v_cache=kv.v_slots(i).data_ptr(),
             )
+        lib = _lib.load()
+        work_bytes = int(lib.aiosb_decode_step_work_bytes(cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim))
         plan = dict(
             layers=torch.frombuffer(bytearray(bytes(descs)), dtype=torch.uint8).to(dev),
-            resid_f32=torch.zeros(rows, 768, dtype=torch.float32, device=dev),
-            resid=torch.zeros(rows, 768, **bf), qkv=torch.zeros(rows, nqkv, **bf),
-            attn=torch.zeros(rows, 768, **bf), act=torch.zeros(rows, 2048, **bf),
-            sync=torch.zeros(int(_lib.load().aiosb_decode_step_sync_words(len(layers))), dtype=torch.int32,
-                             device=dev),
+            # flagged activation lines passed between the kernel's phases (zero = no flag yet)
+            work=torch.zeros(work_bytes // 4, dtype=torch.int32, device=dev),
+            sync=torch.zeros(int(lib.aiosb_decode_step_sync_words()), dtype=torch.int32, device=dev),
         )
         cos, sin = model.model._rotary_emb.tables()
         embed = model.model.embed_tokens.weight
         plan["args"] = _lib.DecodeStepArgs(
-            layers=plan["layers"].data_ptr(), num_layers=len(layers), rows=rows, hidden=768, intermediate=2048,
+            layers=plan["layers"].data_ptr(), num_layers=len(layers), rows=self.max_rows, hidden=768,
+            intermediate=2048,
             num_qo_heads=cfg.num_qo_heads, num_kv_heads=cfg.num_kv_heads, head_dim=cfg.head_dim,
             vocab=cfg.vocab_size, eps=cfg.rms_norm_eps, scale=cfg.head_dim ** -0.5,
             embed=embed.data_ptr(), final_norm=model.model.norm.weight.data_ptr(),
@@ -218,11 +229,9 @@ class CandidateGroupRuntime:
             prefix_len=self.prefix_len_view.data_ptr(), active=self.active.data_ptr(),
             page_table=llm.ctx.page_table.data_ptr(), table_stride=llm.ctx.page_table.stride(0),
             num_slots=kv.num_slots, cos_tab=cos.data_ptr(), sin_tab=sin.data_ptr(), max_pos=cos.shape[0],
-            resid_f32=plan["resid_f32"].data_ptr(), resid=plan["resid"].data_ptr(),
-            qkv=plan["qkv"].data_ptr(), qkv_stride=nqkv, attn=plan["attn"].data_ptr(), attn_stride=768,
-            act=plan["act"].data_ptr(), act_stride=2048, logits=self.logits.data_ptr(),
-            logits_stride=self.logits.stride(0), sync=plan["sync"].data_ptr(),
-            status=ops.status_word(dev).data_ptr(), wait_limit_ns=0, test_extra_arrivals=0, grid_ctas=0,
+            work=plan["work"].data_ptr(), logits=self.logits.data_ptr(), logits_stride=self.logits.stride(0),
+            sync=plan["sync"].data_ptr(), status=ops.status_word(dev).data_ptr(), wait_limit_ns=0,
+            test_flag_skew=0, grid_ctas=0,
         )
         self._keep = (plan, descs)  # weights and buffers the argument block points to
         return plan

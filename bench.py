@@ -330,9 +330,10 @@ def decode_step_roofline(engine, llm, peaks: dict) -> dict:
     from aios_b200 import _lib
 
     rt = engine._runtime
-    plan = rt._step_plan
-    if plan is None:
+    was_on = rt._step_plan is not None
+    if not rt.use_persistent_step():
         return decode_linear_roofline(llm, peaks)
+    plan = rt._step_plan
     dev = llm.device
     cfg = llm.config
     rows = 8
@@ -378,6 +379,7 @@ def decode_step_roofline(engine, llm, peaks: dict) -> dict:
 
     ops.check_status(dev)
     rt.active.zero_()
+    rt.use_persistent_step(was_on)
     layers = llm.model.model.layers.op_list
     wbytes = sum(layer.self_attn.qkv_proj.weight.numel() + layer.self_attn.o_proj.weight.numel()
                  + layer.mlp.gate_up_proj.weight.numel() + layer.mlp.down_proj.weight.numel() for layer in layers)
@@ -651,7 +653,8 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     if rank != 0:
         return None
     peaks = measured_peaks()
-    roof = None if args.no_extras else decode_step_roofline(engine, llm, peaks)
+    roof = None if args.no_extras else decode_linear_roofline(llm, peaks)
+    step_kernel = None if args.no_extras else decode_step_roofline(engine, llm, peaks)
     mixer = None if args.no_extras else mixer_chain(dev)
     kstream = None if args.no_extras else keystroke_stream(engine, llm, seed=4321 + rank)
     sweeps = None if args.no_extras else config_sweeps(engine, llm, dev)
@@ -685,6 +688,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
                 "h2d_bytes_per_step": int(round(h2d)), "d2h_bytes_per_step": int(round(d2h))},
         "gpu_launches": launches,
         "roofline": roof,
+        "persistent_step": step_kernel,
         "clocks": clocks.summary(),
     }
     return line

@@ -403,9 +403,11 @@ AIOSB_API int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t 
  * attention, o linear + residual, RMSNormFused + gate/up linear + SwiGLU, down
  * linear + residual), the final norm and the LM head, in ONE kernel launch (one
  * CTA per SM; a producer warp streams each CTA's weight tiles into shared memory
- * while its consumer warps run the dependent phases, synchronised through the
- * caller's `sync` words with bounded waits). Serves hidden 768, intermediate
- * 2048, head_dim 64 or 96, at most 7 query heads per KV head, 1..16 rows. */
+ * while its consumer warps run the dependent phases). Activations pass between
+ * CTAs through the caller's `work` area as flagged 16-byte lines, so each phase
+ * waits (bounded) for exactly the values it reads. Serves hidden 768,
+ * intermediate 2048, head_dim 64 or 96, at most 7 query heads per KV head, 1..16
+ * rows, at most 48 layers. */
 typedef struct aiosb_decode_layer {
   const void* w_qkv;      /* [(Hq + 2 Hkv) d, 768] bf16 (packed q | k | v)            */
   const void* w_o;        /* [768, Hq d] bf16                                         */
@@ -441,30 +443,29 @@ typedef struct aiosb_decode_step_args {
   const void* cos_tab;              /* [max_pos, d] bf16 RoPE tables                    */
   const void* sin_tab;
   int32_t max_pos;
-  /* caller-owned work buffers, 16-byte aligned */
-  float* resid_f32;                 /* [rows, 768] fp32 residual stream                 */
-  void* resid;                      /* [rows, 768] bf16 residual                        */
-  void* qkv;  int64_t qkv_stride;   /* [rows, (Hq + 2 Hkv) d] bf16                      */
-  void* attn; int64_t attn_stride;  /* [rows, Hq d] bf16                                */
-  void* act;  int64_t act_stride;   /* [rows, 2048] bf16                                */
-  void* logits; int64_t logits_stride; /* [rows, vocab] bf16 output                     */
-  uint32_t* sync;                   /* [aiosb_decode_step_sync_words(num_layers)], zero
-                                       before the first launch; every launch leaves it
-                                       zero again                                        */
+  void* work;                       /* aiosb_decode_step_work_bytes() bytes, 16-byte
+                                       aligned, zero before the first launch            */
+  void* logits;                     /* [rows, vocab] bf16 output                        */
+  int64_t logits_stride;
+  uint32_t* sync;                   /* [aiosb_decode_step_sync_words()], zero before
+                                       the first launch                                  */
   int32_t* status;
   uint64_t wait_limit_ns;           /* bound of every wait; 0 = 2 s                     */
-  uint32_t test_extra_arrivals;     /* 0. Tests only: every phase wait then needs this
-                                       many arrivals more than the grid has, so it runs
-                                       out and reports AIOSB_DEV_WAIT_TIMEOUT            */
+  uint32_t test_flag_skew;          /* 0. Tests only: every wait then expects a flag no
+                                       producer writes, so it runs out and reports
+                                       AIOSB_DEV_WAIT_TIMEOUT                            */
   int32_t grid_ctas;                /* 0 = one CTA per SM                               */
 } aiosb_decode_step_args;
 
-/* Words of the `sync` array for a model of num_layers layers. */
-AIOSB_API int64_t aiosb_decode_step_sync_words(int64_t num_layers);
+/* Bytes of the `work` area for a model with these heads (any rows <= 16). */
+AIOSB_API int64_t aiosb_decode_step_work_bytes(int64_t num_qo_heads, int64_t num_kv_heads, int64_t head_dim);
+
+/* Words of the `sync` array (launch counter, abort word, flag epoch). */
+AIOSB_API int64_t aiosb_decode_step_sync_words(void);
 
 /* One decode forward (see above). Launches with programmatic dependent launch: the
  * weight streaming starts while the previous kernel (the group step) runs; the
- * phases wait for it. Launches that use the same `sync` array must not overlap. */
+ * phases wait for it. Launches that share `work` / `sync` must not overlap. */
 AIOSB_API int aiosb_decode_step(const aiosb_decode_step_args* args, void* stream);
 
 /* aiosb_group_step without the caller's scratch array. No counterpart in the

@@ -9,10 +9,10 @@
   largest logit over the whole vocabulary. A wrong tile, head or layer would
   show as differences orders of magnitude larger. Greedy tokens agree except
   where the top-2 logit gap is a bf16 near-tie.
-* Bounded waits: a launch whose phase waits need one arrival more than the grid
-  provides (the test hook test_extra_arrivals), with a 2 ms limit, reports
-  AIOSB_DEV_WAIT_TIMEOUT through the status word and returns; the sync words are
-  left at zero and the next ordinary launch works.
+* Bounded waits: a launch whose phases expect a flag no producer writes (the test
+  hook test_flag_skew), with a 2 ms limit, reports AIOSB_DEV_WAIT_TIMEOUT through
+  the status word and returns; the abort and launch-counter words are left at
+  zero, and the next ordinary launch works.
 """
 
 from __future__ import annotations
@@ -46,16 +46,14 @@ def test_persistent_step_matches_per_kernel_forward(shape) -> None:
     llm = LLM(config=cfg, seed=0, page_size=16, num_pages=256)
     engine = ImeCompletionEngine(llm)
     rt = engine._runtime
-    assert rt._step_plan is not None, "the persistent step should serve this shape"
+    assert rt.use_persistent_step(), "the persistent step should serve this shape"
     g = torch.Generator().manual_seed(9)
     text = llm.tokenizer.text_for(torch.randint(10, cfg.vocab_size, (12,), generator=g).tolist())
     greedy = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=8, refill_batch_size=8,
                                  max_new_tokens=12, temperature=1.0, top_k=1, top_p=1.0, min_new_tokens=0, seed=1)
     persistent, res_p = _greedy_steps(engine, text, greedy)
     launches = rt._graph_launches[8]
-    rt._step_plan = None  # the per-kernel forward, same weights and buffers
-    rt._graphs.clear()
-    rt._graph_launches.clear()
+    rt.use_persistent_step(False)  # the per-kernel forward, same weights and buffers
     per_kernel, res_k = _greedy_steps(engine, text, greedy)
     assert launches == 2, "one group step + one persistent forward per decode step"
     assert rt._graph_launches[8] > 2 * cfg.num_layers
@@ -85,6 +83,7 @@ def test_decode_step_wait_runs_out_and_reports() -> None:
     llm = LLM(config=shapes.S10, seed=0, page_size=16, num_pages=64)
     engine = ImeCompletionEngine(llm)
     rt = engine._runtime
+    assert rt.use_persistent_step()
     plan = rt._step_plan
     dev = llm.device
     status = ops.status_word(dev)
@@ -93,12 +92,13 @@ def test_decode_step_wait_runs_out_and_reports() -> None:
     args = _lib.DecodeStepArgs.from_buffer_copy(plan["args"])
     args.rows = 8
     args.wait_limit_ns = 2_000_000  # 2 ms
-    args.test_extra_arrivals = 1  # an arrival that never comes
+    args.test_flag_skew = 1  # every wait expects a flag that no producer writes
     stream = torch.cuda.current_stream(dev).cuda_stream
     _lib.call("aiosb_decode_step", ctypes.byref(args), stream)
     torch.cuda.synchronize(dev)  # returns: every wait is bounded
     assert int(status.item()) == _lib.DEV_WAIT_TIMEOUT
-    assert int(plan["sync"].abs().sum().item()) == 0, "the last CTA leaves the sync words at zero"
+    sync = plan["sync"].cpu().tolist()
+    assert sync[0] == 0 and sync[1] == 0, "the last CTA clears the launch counter and the abort word"
     status.zero_()
     # the context is still usable: an ordinary launch completes and reports nothing
     ok = _lib.DecodeStepArgs.from_buffer_copy(plan["args"])
@@ -106,5 +106,6 @@ def test_decode_step_wait_runs_out_and_reports() -> None:
     _lib.call("aiosb_decode_step", ctypes.byref(ok), stream)
     torch.cuda.synchronize(dev)
     assert int(status.item()) == 0
-    assert int(plan["sync"].abs().sum().item()) == 0
+    after = plan["sync"].cpu().tolist()
+    assert after[0] == 0 and after[1] == 0 and after[2] == sync[2] + 1, "one launch advances the flag epoch"
     assert torch.isfinite(rt.logits[:8].float()).all()
