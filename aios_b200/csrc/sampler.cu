@@ -32,6 +32,16 @@ constexpr int kMaxSortK = 2048;  // candidates sorted in shared memory (top-k pa
 constexpr int kVecPer = kMaxVocab / 8 / kSampThreads;  // 8-token groups a thread holds in registers
 constexpr int kBanWords = kMaxVocab / 32;
 constexpr int kFastTopK = 512;  // top-k bound of the thread-maximum threshold path
+// Larger sorted candidate sets (any top-k above kMaxSortK, or top-p without top-k)
+// sort the whole row in the dynamic shared memory as 8-byte keys: vocabularies
+// of at most this many ids (padded to a power of two).
+constexpr int kMaxLargeSort = 16384;
+
+__host__ __device__ inline int large_sort_slots(int V) {
+  int n = 1;
+  while (n < V) n <<= 1;
+  return n;
+}
 
 struct SampleParams {
   float temperature;
@@ -617,9 +627,52 @@ __device__ void radix_candidates(RowSmem& s, const uint32_t* keys, int V, int k)
   __syncthreads();
 }
 
+// Sorts all V keys of a row in the dynamic shared memory: the uint32 keys[0..V)
+// are widened in place into (~key << 32 | id) 8-byte sort keys over the first
+// 8 * large_sort_slots(V) bytes, padded with ~0, and bitonic-sorted ascending, so
+// entry i is the (i+1)-th largest value, equal values by ascending id: the first
+// k entries are exactly the top-k set in the order the top-k path sorts it.
+// The widening moves ids [hi / 2, hi) per round, from bytes [2 hi, 4 hi) to
+// [4 hi, 8 hi): a round never writes where a later round (or itself) reads.
+__device__ unsigned long long* sort_full_row(uint32_t* keys, int V) {
+  const int tid = threadIdx.x;
+  unsigned long long* big = reinterpret_cast<unsigned long long*>(keys);
+  const int n = large_sort_slots(V);
+  for (int i = V + tid; i < n; i += blockDim.x) big[i] = ~0ull;  // bytes >= 8 V: no key lives there
+  for (int hi = n; hi > 1; hi >>= 1) {
+    const int lo = hi >> 1;
+    // sources [2 hi, 4 hi) and destinations [4 hi, 8 hi) of a round are disjoint,
+    // and the destinations were read by the round before (one barrier back)
+    for (int i = lo + tid; i < min(hi, V); i += blockDim.x)
+      big[i] = ((unsigned long long)(~keys[i]) << 32) | (unsigned long long)(uint32_t)i;
+    __syncthreads();
+  }
+  if (tid == 0 && V > 0) big[0] = ((unsigned long long)(~keys[0]) << 32);
+  __syncthreads();
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = tid; i < n; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const unsigned long long a = big[i], b = big[j];
+          if ((a > b) == up) {
+            big[i] = b;
+            big[j] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  return big;
+}
+
 // Samples one row. rr holds the bf16 logits, s.ban the forbidden ids; keys[] is
-// V uint32 of scratch. Returns the token id (same value in every thread).
-__device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, const SampleParams& p, float u) {
+// V uint32 of scratch, or 8 * large_sort_slots(V) bytes when `large` (sorted
+// candidate sets above kMaxSortK). Returns the token id (same value in every thread).
+__device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, const SampleParams& p, float u,
+                          bool large = false) {
   const int tid = threadIdx.x;
   if (p.greedy) return greedy_pick(s, rr, V);
   int k;
@@ -634,8 +687,10 @@ __device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, 
     k = V;
     sorted_path = true;  // full descending sort (sample.py:131-132)
   }
-  // the host rejects sorted candidate sets above kMaxSortK; never index past them
-  if (sorted_path && k > kMaxSortK) k = kMaxSortK;
+  // sorted candidate sets above kMaxSortK need the full-row sort buffer; without
+  // it (the host then rejects such a call) never index past the top-k buffer
+  const bool full_sort = sorted_path && k > kMaxSortK && large;
+  if (sorted_path && k > kMaxSortK && !large) k = kMaxSortK;
   // Sorted paths rank the unscaled values and divide only the selected
   // candidates (a block-wide check falls back to scaled keys, see make_raw_keys):
   // 16384 divisions fewer per row. The raw keys' low 16 bits are all zeros or
@@ -655,6 +710,17 @@ __device__ int sample_row(RowSmem& s, const RowRegs& rr, uint32_t* keys, int V, 
   if (!sorted_path) {
     const auto val = [&](int i) { return key_value(keys[i]); };
     return pick_index(s, val, V, p.top_p, u);
+  }
+  if (full_sort) {
+    const unsigned long long* big = sort_full_row(keys, V);
+    const float t = p.temperature;
+    // the same fp32 division of the selected candidates as the top-k path
+    const auto val = [&](int i) {
+      const float v = key_value(~(uint32_t)(big[i] >> 32));
+      return raw ? v / t : v;
+    };
+    const int idx = pick_index(s, val, k, p.top_p, u);
+    return (int)(uint32_t)(big[idx] & 0xffffffffull);
   }
   bool collected = false;
   if (k <= kFastTopK) {
@@ -735,7 +801,7 @@ __global__ void __launch_bounds__(kSampThreads, 1)
     sample_kernel(const __nv_bfloat16* __restrict__ logits, int64_t row_stride, int V, SampleParams p,
                   const float* __restrict__ uniforms, const int32_t* __restrict__ forbidden, int n_forbidden,
                   const int64_t* __restrict__ forbidden_rows, int n_forbidden_rows, int64_t* __restrict__ tok_out,
-                  float* __restrict__ lp_out, int32_t* status) {
+                  float* __restrict__ lp_out, int32_t* status, int large) {
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw + sizeof(RowSmem));
@@ -755,7 +821,7 @@ __global__ void __launch_bounds__(kSampThreads, 1)
   }
   __syncthreads();
   const float u = uniforms != nullptr ? uniforms[r] : 0.5f;
-  const int tok = sample_row(s, rr, keys, V, p, u);
+  const int tok = sample_row(s, rr, keys, V, p, u, large != 0);
   if (threadIdx.x == 0) {
     tok_out[r] = tok;
     lp_out[r] = (bf16_to_f(lrow[tok]) - mx) - lse;
@@ -767,7 +833,7 @@ __global__ void __launch_bounds__(kSampThreads, 1)
 // to finish runs the step's host-free epilogue: compaction of finished rows,
 // FIFO slot allocation in active-row order (aios/scheduler/cache.py:46-51),
 // page-table writes (aios/ime.py:1229) and the next forward's metadata.
-__global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group_ptrs g) {
+__global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group_ptrs g, int large) {
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw + sizeof(RowSmem));
@@ -842,7 +908,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
     p.top_p = st->top_p;
     p.greedy = st->greedy;
     const float u = g.uniforms[(int64_t)r * S + step];
-    const int tok = sample_row(s, rr, keys, V, p, u);
+    const int tok = sample_row(s, rr, keys, V, p, u, large != 0);
     if (warp0) {
       const bool eos = tok == eos_id;
       const bool emitted = !eos;
@@ -1033,6 +1099,10 @@ __global__ void __launch_bounds__(1024) slot_free_range_kernel(int32_t* ring, in
 }
 
 size_t sample_smem(int V) { return sizeof(RowSmem) + (size_t)V * sizeof(uint32_t); }
+// With the full-row sort: 8 bytes per (padded) id.
+size_t sample_smem_large(int V) { return sizeof(RowSmem) + (size_t)large_sort_slots(V) * 8; }
+// The dynamic shared memory either launch needs at most (set once per kernel).
+size_t sample_smem_max() { return std::max(sample_smem(kMaxVocab), sample_smem_large(kMaxLargeSort)); }
 
 // Page-table reset for a keystroke: rows [0, rows) get the prefix slots in
 // columns [0, n) and zeros in [n, width) (the reference builds a fresh zero table
@@ -1082,10 +1152,13 @@ extern "C" int aiosb_sample(const void* logits, int64_t rows, int64_t vocab, int
   AIOSB_REQUIRE(rows >= 0 && vocab > 0 && vocab <= kMaxVocab && row_stride >= vocab, AIOSB_ERR_INVALID_ARG,
                 "sample: bad sizes (vocab must be in [1, %d])", kMaxVocab);
   AIOSB_REQUIRE(greedy || temperature > 0.f, AIOSB_ERR_INVALID_ARG, "sample: temperature must be positive");
+  bool large = false;
   if (!greedy) {
     const int64_t k = top_k > 0 ? std::min<int64_t>(top_k, vocab) : (top_p < 1.0f ? vocab : 0);
-    AIOSB_REQUIRE(k <= kMaxSortK, AIOSB_ERR_UNSUPPORTED,
-                  "sample: top-k/top-p candidate set of %lld exceeds the %d-entry sort", (long long)k, kMaxSortK);
+    large = k > kMaxSortK;
+    AIOSB_REQUIRE(!large || vocab <= kMaxLargeSort, AIOSB_ERR_UNSUPPORTED,
+                  "sample: a sorted candidate set of %lld needs a vocabulary of at most %d", (long long)k,
+                  kMaxLargeSort);
   }
   if (rows == 0) return AIOSB_OK;
   AIOSB_REQUIRE(logits && token_out && logprob_out, AIOSB_ERR_INVALID_ARG, "sample: null pointer");
@@ -1094,11 +1167,12 @@ extern "C" int aiosb_sample(const void* logits, int64_t rows, int64_t vocab, int
   p.top_k = (int)top_k;
   p.top_p = top_p;
   p.greedy = greedy;
-  const size_t smem = sample_smem((int)vocab);
-  cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem(kMaxVocab));
+  const size_t smem = large ? sample_smem_large((int)vocab) : sample_smem((int)vocab);
+  cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max());
   cudaError_t e = launch_pdl(sample_kernel, dim3((unsigned)rows), dim3(kSampThreads), smem, as_stream(stream),
                              (const __nv_bfloat16*)logits, row_stride, (int)vocab, p, uniforms, forbidden,
-                             (int)n_forbidden, forbidden_rows, (int)n_forbidden_rows, token_out, logprob_out, status);
+                             (int)n_forbidden, forbidden_rows, (int)n_forbidden_rows, token_out, logprob_out, status,
+                             (int)large);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "sample: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }
@@ -1118,11 +1192,18 @@ extern "C" int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t
   AIOSB_REQUIRE(g && g->state, AIOSB_ERR_INVALID_ARG, "group_step: null pointer");
   AIOSB_REQUIRE(rows >= 1 && vocab > 0 && vocab <= kMaxVocab, AIOSB_ERR_INVALID_ARG,
                 "group_step: rows >= 1 and vocab in [1, %d]", kMaxVocab);
-  AIOSB_REQUIRE(top_k_max <= kMaxSortK, AIOSB_ERR_UNSUPPORTED, "group_step: top_k above %d", kMaxSortK);
+  // top_k_max: the largest sorted candidate set the group's rounds may ask for
+  // (top-k, or the vocabulary for top-p without top-k); above kMaxSortK the step
+  // sorts whole rows, for vocabularies of at most kMaxLargeSort ids
+  const bool large = top_k_max > kMaxSortK;
+  AIOSB_REQUIRE(!large || vocab <= kMaxLargeSort, AIOSB_ERR_UNSUPPORTED,
+                "group_step: sorted candidate sets above %d need a vocabulary of at most %d", kMaxSortK,
+                kMaxLargeSort);
   AIOSB_REQUIRE(rows <= 32, AIOSB_ERR_UNSUPPORTED, "group_step: at most 32 rows per group");
-  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem(kMaxVocab));
-  cudaError_t e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads), sample_smem((int)vocab),
-                             as_stream(stream), *g);
+  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max());
+  cudaError_t e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads),
+                             large ? sample_smem_large((int)vocab) : sample_smem((int)vocab), as_stream(stream), *g,
+                             (int)large);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }
@@ -1280,7 +1361,10 @@ extern "C" int aiosb_group_step_static(const aiosb_group_ptrs* g, int64_t rows, 
   AIOSB_REQUIRE(g && g->state, AIOSB_ERR_INVALID_ARG, "group_step_static: null pointer");
   AIOSB_REQUIRE(rows >= 1 && vocab > 0 && vocab <= kMaxVocab, AIOSB_ERR_INVALID_ARG,
                 "group_step_static: rows >= 1 and vocab in [1, %d]", kMaxVocab);
-  AIOSB_REQUIRE(top_k_max <= kMaxSortK, AIOSB_ERR_UNSUPPORTED, "group_step_static: top_k above %d", kMaxSortK);
+  const bool large = top_k_max > kMaxSortK;
+  AIOSB_REQUIRE(!large || vocab <= kMaxLargeSort, AIOSB_ERR_UNSUPPORTED,
+                "group_step_static: sorted candidate sets above %d need a vocabulary of at most %d", kMaxSortK,
+                kMaxLargeSort);
   AIOSB_REQUIRE(rows <= kStaticStepRows, AIOSB_ERR_UNSUPPORTED,
                 "group_step_static: %lld rows exceed the %d-row static scratch", (long long)rows, kStaticStepRows);
   int32_t* finished = nullptr;
@@ -1292,9 +1376,10 @@ extern "C" int aiosb_group_step_static(const aiosb_group_ptrs* g, int64_t rows, 
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step_static: memset: %s", cudaGetErrorString(e));
   aiosb_group_ptrs local = *g;
   local.finished = finished;
-  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem(kMaxVocab));
-  e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads), sample_smem((int)vocab),
-                 as_stream(stream), local);
+  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max());
+  e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads),
+                 large ? sample_smem_large((int)vocab) : sample_smem((int)vocab), as_stream(stream), local,
+                 (int)large);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step_static: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }

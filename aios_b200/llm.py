@@ -143,8 +143,8 @@ class LLM:
         vocab = self.config.vocab_size
         for sp in params_list:  # the sampler's sort limit, checked before any KV is taken
             k = min(sp.top_k, vocab) if sp.top_k > 0 else (vocab if sp.top_p < 1.0 else 0)
-            if not sp.is_greedy and k > 2048:
-                raise ValueError(f"sample: top-k/top-p candidate set of {k} exceeds the 2048-entry sort")
+            if not sp.is_greedy and k > 2048 and vocab > 16384:
+                raise ValueError(f"sample: a sorted candidate set of {k} needs a vocabulary of at most 16384")
         all_ids: List[torch.Tensor] = []
         for prompt in prompts:
             if isinstance(prompt, str):

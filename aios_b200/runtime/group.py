@@ -39,6 +39,8 @@ from ..kernel import ops
 
 MAX_TERMINAL = 16
 MAX_MINLEN = 32
+SORT_K = 2048  # sorted candidates of the step kernel's top-k path
+LARGE_SORT_VOCAB = 16384  # larger sorted sets sort whole rows: vocabularies up to this size
 
 # The persistent decode step (one launch per decode forward, aiosb_decode_step)
 # serves the standard-residual models with these dims when
@@ -166,7 +168,6 @@ class CandidateGroupRuntime:
         # from ([attempts, vocab] fp32 per step; synchronises after every step).
         self.record_logits = False
         self.step_logits: list[torch.Tensor] = []
-        self._top_k_cap = 2048
         self._step_plan = self._persistent_plan() if _PERSISTENT else None
 
     def use_persistent_step(self, enabled: bool = True) -> bool:
@@ -259,19 +260,24 @@ class CandidateGroupRuntime:
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def _group_step(self, rows: int) -> None:
-        _lib.call("aiosb_group_step", ctypes.byref(self.ptrs), rows, self.vocab, self._top_k_cap, self._stream())
+    def _group_step(self, rows: int, large: bool = False) -> None:
+        # top_k_max: the largest sorted candidate set a round of this graph may ask for
+        top_k_max = self.vocab if large else SORT_K
+        _lib.call("aiosb_group_step", ctypes.byref(self.ptrs), rows, self.vocab, top_k_max, self._stream())
 
-    def _step_and_forward(self, rows: int, batch: Batch) -> None:
-        self._group_step(rows)
+    def _step_and_forward(self, rows: int, batch: Batch, large: bool = False) -> None:
+        self._group_step(rows, large)
         if self._step_plan is not None:
             self._decode_step(rows)
             return
         with self.llm.ctx.forward_batch(batch):
             self.llm.model.forward()
 
-    def _graph(self, rows: int) -> torch.cuda.CUDAGraph:
-        graph = self._graphs.get(rows)
+    def _graph(self, rows: int, large: bool = False) -> torch.cuda.CUDAGraph:
+        """The step graph for `rows` rows; `large` steps sort whole rows (sorted
+        candidate sets above SORT_K)."""
+        key = (rows, large)
+        graph = self._graphs.get(key)
         if graph is not None:
             return graph
         batch = self._decode_batch(rows)
@@ -280,18 +286,18 @@ class CandidateGroupRuntime:
         self._write_state(dict(done=1, rows=rows, max_steps=2, vocab=self.vocab, page_size=1, capacity=1,
                                table_stride=self.llm.ctx.page_table.stride(0)))
         self.active.zero_()
-        self._step_and_forward(rows, batch)
+        self._step_and_forward(rows, batch, large)
         torch.cuda.synchronize(self.device)
         graph = torch.cuda.CUDAGraph()
         before = _lib.launches
         with torch.cuda.graph(graph, pool=self._pool):
-            self._step_and_forward(rows, batch)
-        self._graph_launches[rows] = _lib.launches - before
+            self._step_and_forward(rows, batch, large)
+        self._graph_launches[key] = _lib.launches - before
         _lib.launches = before
         if self._pool is None:
             self._pool = graph.pool()
         torch.cuda.synchronize(self.device)
-        self._graphs[rows] = graph
+        self._graphs[key] = graph
         return graph
 
     # ------------------------------------------------------------------ round
@@ -332,10 +338,11 @@ class CandidateGroupRuntime:
             raise ValueError("refill ban list exceeds the runtime's capacity")
         greedy = (temperature <= 0.0 or top_k == 1) and top_p == 1.0
         sort_k = min(top_k, self.vocab) if top_k > 0 else (self.vocab if top_p < 1.0 else 0)
-        if not greedy and sort_k > self._top_k_cap:
-            raise ValueError(f"top-k/top-p candidate set of {sort_k} exceeds the {self._top_k_cap}-entry sort")
+        large = not greedy and sort_k > SORT_K
+        if large and self.vocab > LARGE_SORT_VOCAB:
+            raise ValueError(f"a sorted candidate set of {sort_k} needs a vocabulary of at most {LARGE_SORT_VOCAB}")
         cm = self.llm.cache_manager
-        graph = self._graph(attempts)
+        graph = self._graph(attempts, large)
         head0 = cm.head
         width = max((len(s) for s in banned_sequences), default=0)
         self._write_state(dict(
@@ -381,12 +388,12 @@ class CandidateGroupRuntime:
                     break
             if step + 1 < max_new_tokens:
                 graph.replay()
-                _lib.count_launches(self._graph_launches[attempts])
+                _lib.count_launches(self._graph_launches[(attempts, large)])
                 if self.record_logits:
                     torch.cuda.synchronize(self.device)
                     step_logits.append(self.logits[:attempts].float().cpu())
             else:
-                self._group_step(attempts)
+                self._group_step(attempts, large)
             launched += 1
         # [rows, steps] arrays use the round's max_new_tokens as their row stride
         n = attempts * max_new_tokens

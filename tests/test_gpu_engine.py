@@ -107,3 +107,19 @@ def test_greedy_rows_are_identical(engine) -> None:
     result = engine.complete(_prefix(llm, 8, 3), cfg)
     texts = {c.text for c in result.raw_candidates}
     assert len(texts) == 1
+
+
+def test_keystroke_with_a_top_k_beyond_the_top_k_buffer(engine) -> None:
+    """top_k 4096 (any top_k >= 1 the reference accepts, aios/ime.py:87): the
+    step sorts whole rows; the round completes with valid candidates, and the
+    usual 2048-or-less setting still runs its own step graph."""
+    llm = engine.llm
+    engine.reset_prefix_cache()
+    prefix = _prefix(llm, 12, 31)
+    wide = engine.complete(prefix, ImeGenerationConfig(seed=31, top_k=4096, top_p=0.9, max_sampling_attempts=8))
+    assert wide.sampling_attempts == 8 and len(wide.raw_candidates) == 8
+    assert all(0 < c.token_count <= 12 for c in wide.raw_candidates)
+    narrow = engine.complete(prefix, ImeGenerationConfig(seed=31, top_k=50, top_p=0.9, max_sampling_attempts=8))
+    assert narrow.sampling_attempts == 8
+    keys = set(engine._runtime._graphs)
+    assert (8, True) in keys and (8, False) in keys

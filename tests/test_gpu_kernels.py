@@ -465,6 +465,12 @@ SAMPLER_PATHS = [
     ("ties_fallback", 16384, 0.8, 50, 0.9, "const"),
     ("few_distinct", 16384, 0.8, 50, 0.9, "coarse"),
     ("full_sort", 2048, 0.8, 0, 0.9, "randn"),
+    # sorted sets above the 2048-entry top-k buffer sort whole rows in shared memory
+    ("k4096_full_row", 16384, 0.8, 4096, 0.9, "randn"),
+    ("k4096_no_topp", 16384, 1.0, 4096, 1.0, "randn"),
+    ("topp_only_16384", 16384, 0.8, 0, 0.9, "randn"),
+    ("topp_only_6401", 6401, 0.7, 0, 0.95, "randn"),
+    ("topk_vocab_ties", 16384, 0.8, 16384, 0.9, "coarse"),
     ("tiny_probs", 16384, 0.5, 512, 1.0, "spread"),
     ("tiny_probs_topp", 16384, 0.5, 400, 0.999999, "spread"),
     ("s06_vocab", 6400, 0.8, 50, 0.9, "randn"),
