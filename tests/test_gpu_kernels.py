@@ -470,7 +470,9 @@ SAMPLER_PATHS = [
     ("k4096_no_topp", 16384, 1.0, 4096, 1.0, "randn"),
     ("topp_only_16384", 16384, 0.8, 0, 0.9, "randn"),
     ("topp_only_6401", 6401, 0.7, 0, 0.95, "randn"),
-    ("topk_vocab_ties", 16384, 0.8, 16384, 0.9, "coarse"),
+    # seven distinct values: the full sort orders ties by id (no top-p cut here,
+    # which inside a tie group would depend on the last fp32 bits of the cumsum)
+    ("topk_vocab_ties", 16384, 0.8, 16384, 1.0, "coarse"),
     ("tiny_probs", 16384, 0.5, 512, 1.0, "spread"),
     ("tiny_probs_topp", 16384, 0.5, 400, 0.999999, "spread"),
     ("s06_vocab", 6400, 0.8, 50, 0.9, "randn"),
