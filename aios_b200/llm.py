@@ -130,8 +130,7 @@ class LLM:
         (page_size 1) freed as soon as a request finishes. Returns one dict per
         prompt, in prompt order: uid, token_ids, text."""
         from .engine.engine import Engine
-        from .scheduler.scheduler import Scheduler
-        from .scheduler.table import TableManager
+        from .scheduler.batcher import ContinuousBatcher
 
         if self.page_size != 1:
             raise ValueError("generate uses page_size 1 KV slots (build the LLM with page_size=1)")
@@ -178,23 +177,22 @@ class LLM:
         saved_table = self.ctx.page_table
         self.ctx.page_table = page_table
         try:
-            scheduler = Scheduler(table_manager=TableManager(max_running_reqs, page_table),
-                                  cache_manager=self.cache_manager, eos_token_id=self.tokenizer.eos_token_id,
-                                  device=self.device, max_running_reqs=max_running_reqs,
-                                  attn_backend=self.model.attn_backend, prefill_token_budget=prefill_token_budget)
+            batcher = ContinuousBatcher(cache_manager=self.cache_manager, page_table=page_table,
+                                        eos_token_id=self.tokenizer.eos_token_id, device=self.device,
+                                        max_running=max_running_reqs, attn_backend=self.model.attn_backend,
+                                        prefill_token_budget=prefill_token_budget)
             engine = Engine(model=self.model, mha_kv_cache=self.mha_kv_cache)
             for ids, sp in zip(all_ids, params_list):
-                scheduler.add_request(ids, sp)
+                batcher.add_request(ids, sp)
             iteration = 0
-            while scheduler.has_work:
-                batch = scheduler.schedule_next_batch()
+            while batcher.has_work:
+                batch = batcher.next_batch()
                 if batch is None:
                     raise RuntimeError("generate: pending requests do not fit the KV cache")
-                next_tokens = engine.run_batch(batch)
-                scheduler.process_batch_output(batch, next_tokens)
+                batcher.commit(batch, engine.run_batch(batch))
                 if debug_scheduler:
-                    print(f"[{iteration}] {scheduler.debug_state(batch)}")
+                    print(f"[{iteration}] {batcher.describe(batch)}")
                 iteration += 1
-            return scheduler.collect_results(self.tokenizer)
+            return batcher.results(self.tokenizer)
         finally:
             self.ctx.page_table = saved_table
