@@ -15,7 +15,9 @@ weights once per decode step, so the working set exceeds the 126 MB L2.
 baseline/_ref; fp32, all host cores, CPU shims for FlashInfer and the KV buffer)
 on the same workload. With N > 1 (torchrun)
 every GPU serves an independent keystroke stream (replicas; no data exchange);
-the barrier and the max-over-ranks timing use a small NCCL all-reduce.
+the barrier and the max-over-ranks timing reduction run over gloo on host
+values (no collective touches the GPUs), and each rank is pinned to its own
+share of the host cores.
 """
 
 from __future__ import annotations
@@ -67,7 +69,7 @@ class ClockSampler:
                  "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._thread = threading.Thread(target=self._read, daemon=True)
             self._thread.start()
@@ -235,15 +237,39 @@ DECODE_LINEAR_TRAFFIC = 168_907_008
 DECODE_STEP_TRAFFIC = None
 
 
-def max_over_ranks(values: list[float], world: int, device) -> list[float]:
-    """Each timing's maximum over all ranks (one all-reduce); unchanged for one
+def pin_rank_cores(local_rank: int, local_world: int) -> list[int]:
+    """Pins this rank's process to its own contiguous share of the host cores it
+    may use (each replica's launch loop then runs without sharing cores with the
+    others); returns the cores."""
+    cores = sorted(os.sched_getaffinity(0))
+    share = max(1, len(cores) // max(1, local_world))
+    mine = cores[local_rank * share : (local_rank + 1) * share] or cores
+    os.sched_setaffinity(0, mine)
+    return mine
+
+
+def max_over_ranks(values: list[float], world: int, device=None) -> list[float]:
+    """Each timing's maximum over all ranks (one all-reduce of host values over
+    the gloo group: the replicas exchange nothing on the GPU); unchanged for one
     rank. The slowest replica bounds the job."""
-    t = torch.tensor(values, dtype=torch.float64, device=device)
+    t = torch.tensor(values, dtype=torch.float64)
     if world > 1:
         import torch.distributed as dist
 
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return [float(x) for x in t]
+
+
+def gather_over_ranks(value: float, world: int) -> list[float]:
+    """Every rank's value, in rank order (host-side gather over gloo)."""
+    if world <= 1:
+        return [value]
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64)
+    out = [torch.zeros(1, dtype=torch.float64) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x) for x in out]
 
 
 def replica_throughput(world: int, steps: int, device_ms: float) -> float:
@@ -314,7 +340,10 @@ def decode_linear_roofline(llm, peaks: dict) -> dict:
     return {"bound": "hbm", "kernel": "gemv_mma_kernel (decode linears, 8 rows, register-operand MMA)", "achieved": round(achieved, 1),
             "peak": peak, "peak_source": "measured" if "hbm_gbs" in peaks else "fallback", "unit": "GB/s",
             "frac": round(achieved / peak, 4), "traffic": DECODE_LINEAR_TRAFFIC,
-            "traffic_unit": "bytes per decode step (57 launches)", "algorithmic_bytes_per_step": wbytes,
+            "traffic_unit": "bytes per decode step (57 launches)",
+            "traffic_source": "one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum, --cache-control none) "
+                              "of the `linears` NVTX range of this function; gemv_mma_kernel is unchanged since",
+            "algorithmic_bytes_per_step": wbytes,
             "launches_per_step": launches, "us_per_step": round(ms * 1e3, 2),
             "us_per_launch": round(ms * 1e3 / launches, 3)}
 
@@ -649,6 +678,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     launches = _lib.launches - launches0
     h2d = (rt.h2d_bytes + pr.h2d_bytes + ops.transfer_bytes["h2d"] - h2d0) / args.steps
     d2h = (rt.d2h_bytes + ops.transfer_bytes["d2h"] - d2h0) / args.steps
+    per_rank_ms = gather_over_ranks(device_ms / args.steps, world)
     device_ms, wall = max_over_ranks([device_ms, wall], world, dev)
     if rank != 0:
         return None
@@ -670,6 +700,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(device_ms / args.steps, 4),
+        "per_rank_ms_per_step": [round(x, 4) for x in per_rank_ms],
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -794,7 +825,10 @@ def main() -> None:
         import torch.distributed as dist
 
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=300))
+        # replicas: the barrier and the max-over-ranks timing reduction are host-side
+        # (gloo); no collective touches the GPUs
+        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=300))
+        pin_rank_cores(local_rank, int(os.environ.get("LOCAL_WORLD_SIZE", world)))
     line = run_gpu(args, rank, world, local_rank)
     if rank == 0 and line is not None:
         if world == 1 and args.cpu_sample > 0:
