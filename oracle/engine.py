@@ -200,7 +200,8 @@ class OracleEngine:
                 margins = (top2[:, 0] - top2[:, 1]).tolist()
             else:
                 margins = osamp.sample_margin(batch_logits, temperature=temperature, top_k=top_k, top_p=top_p,
-                                              uniforms=u).tolist()
+                                              uniforms=u, forbidden_token_ids=minlen if step < min_new_tokens else (),
+                                              forbidden_token_ids_by_row=by_row).tolist()
             toks = list(own)
             if forced is not None:
                 for i, r in enumerate(active):

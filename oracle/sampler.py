@@ -98,21 +98,52 @@ def sample_with_logprobs(
     return token_ids, raw_log_probs.gather(-1, token_ids)
 
 
-def sample_margin(
-    logits: torch.Tensor, *, temperature: float, top_k: int, top_p: float, uniforms: torch.Tensor
-) -> np.ndarray:
-    """Distance of each row's uniform from the nearest CDF boundary (diagnostics:
-    a token mismatch with a tiny margin is a rounding tie, not a logic error)."""
-    scaled = logits.cpu().float() / temperature
+def _sampling_cdfs(
+    logits: torch.Tensor, *, temperature: float, top_k: int, top_p: float,
+    forbidden_token_ids: Sequence[int] = (), forbidden_token_ids_by_row: torch.Tensor | None = None,
+) -> tuple[np.ndarray, np.ndarray]:
+    """The candidate CDF of sample_with_logprobs in its own fp32 arithmetic, and
+    the same CDF in fp64 over the fp32 path's candidates and top-p keep set."""
+    sampling = logits.cpu().float().clone()
+    if forbidden_token_ids:
+        sampling[..., sorted({int(t) for t in forbidden_token_ids})] = -torch.inf
+    if forbidden_token_ids_by_row is not None and forbidden_token_ids_by_row.numel():
+        sampling.scatter_(1, forbidden_token_ids_by_row.cpu().to(torch.long), -torch.inf)
+    scaled = sampling / temperature
     k = min(top_k, scaled.size(-1)) if top_k > 0 else scaled.size(-1)
     vals, _ = _topk(scaled, k, "index")
     probs = F.softmax(vals, dim=-1)
     if top_p < 1.0:
-        cum = probs.cumsum(-1)
-        remove = cum > top_p
+        remove = probs.cumsum(-1) > top_p
         remove[..., 1:] = remove[..., :-1].clone()
         remove[..., 0] = False
-        probs = F.softmax(vals.masked_fill(remove, float("-inf")), dim=-1)
-    cdf = probs.cumsum(-1).numpy()
-    u = uniforms.cpu().numpy()[:, None]
-    return np.abs(cdf - u).min(axis=-1)
+        vals = vals.masked_fill(remove, float("-inf"))
+        probs = F.softmax(vals, dim=-1)
+    return probs.cumsum(-1).numpy(), torch.softmax(vals.double(), dim=-1).cumsum(-1).numpy()
+
+
+def sample_margin(
+    logits: torch.Tensor, *, temperature: float, top_k: int, top_p: float, uniforms: torch.Tensor,
+    forbidden_token_ids: Sequence[int] = (), forbidden_token_ids_by_row: torch.Tensor | None = None,
+) -> np.ndarray:
+    """Distance of each row's uniform from the nearest boundary of the fp32 CDF
+    (diagnostics: a token mismatch with a tiny margin is a rounding tie, not a
+    logic error)."""
+    cdf, _ = _sampling_cdfs(logits, temperature=temperature, top_k=top_k, top_p=top_p,
+                            forbidden_token_ids=forbidden_token_ids,
+                            forbidden_token_ids_by_row=forbidden_token_ids_by_row)
+    return np.abs(cdf - uniforms.cpu().numpy()[:, None]).min(axis=-1)
+
+
+def cdf_rounding_band(
+    logits: torch.Tensor, *, temperature: float, top_k: int, top_p: float,
+    forbidden_token_ids: Sequence[int] = (), forbidden_token_ids_by_row: torch.Tensor | None = None,
+) -> np.ndarray:
+    """Per row, the largest gap between the fp32 CDF (the reference's arithmetic,
+    one summation order of many) and the exact CDF. Another fp32 summation order
+    (a parallel softmax sum over thousands of candidates) lands anywhere inside
+    this band, so a uniform closer than it to a boundary may pick either side."""
+    cdf, exact = _sampling_cdfs(logits, temperature=temperature, top_k=top_k, top_p=top_p,
+                                forbidden_token_ids=forbidden_token_ids,
+                                forbidden_token_ids_by_row=forbidden_token_ids_by_row)
+    return np.abs(cdf - exact).max(axis=-1)
