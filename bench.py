@@ -57,8 +57,9 @@ def measured_peaks() -> dict:
 class ClockSampler:
     """nvidia-smi clock / throttle samples during the timed region."""
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, interval_ms: int = 50):
         self.index = index
+        self.interval_ms = interval_ms
         self.samples: list[list[str]] = []
         self._proc = None
 
@@ -69,7 +70,7 @@ class ClockSampler:
                  "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._thread = threading.Thread(target=self._read, daemon=True)
             self._thread.start()
@@ -662,7 +663,10 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     stream = torch.cuda.current_stream(dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     results = []
-    with ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else 0) as clocks:
+    # one sampler per rank: every 50 ms on one GPU, every 200 ms with more ranks
+    # (eight samplers at 50 ms would compete with the ranks' launch loops)
+    with ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else 0,
+                      50 if world == 1 else 200) as clocks:
         torch.cuda.synchronize(dev)
         wall0 = time.perf_counter()
         torch.cuda.nvtx.range_push("timed")
@@ -783,7 +787,7 @@ def kernel_case(name: str) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cpu-sample", type=int, default=15, help="keystrokes timed for the CPU baseline (0: skip)")
