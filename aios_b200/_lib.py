@@ -38,6 +38,8 @@ DEVICE_STATUS_NAMES = {
 EPI_STORE = 0
 EPI_SILU_MUL = 1
 EPI_ADD = 2
+HISTORY_STAGED = 1  # aiosb_attention_decode stable_history modes
+HISTORY_PREFIX_ONCE = 2
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -161,7 +163,7 @@ _SIGNATURES = {
     ),
     "aiosb_attention_decode": (
         [_p, _i64, _p, _i64, _p, _p, _f32, _p, _p, _i64, _p, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p, _i32,
-         _i64, _i64, _i64, _i64, _f32, _p, _i64, _p, _p],
+         _i64, _i64, _i64, _i64, _i64, _f32, _p, _i64, _p, _p],
         _i32,
     ),
     "aiosb_qk_norm_rope_store": (

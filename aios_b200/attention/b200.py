@@ -50,7 +50,8 @@ class B200AttentionMetadata(BaseAttentionMetadata):
     active: torch.Tensor | None = None  # int32 [rows] (decode)
     # decode: the row table, prefix length and every key before the current
     # position were written by earlier launches (the CandidateGroup runtime)
-    stable_history: bool = False
+    stable_history: bool | int = False  # aiosb_attention_decode's history mode (0, 1 staged, 2 prefix-once)
+    staged_prefix: int = 0  # bound on the prefix keys staged before the wait (0: the kernel's default)
 
     def get_last_indices(self, bs: int) -> torch.Tensor:
         assert self.cu_seqlens_q is not None, "last indices exist for prefill batches"
@@ -159,6 +160,7 @@ class B200AttentionBackend(BaseAttentionBackend):
             num_kv_heads=self.num_kv_heads, head_dim=self.head_dim, scale=self.sm_scale, qkv=qkv,
             q_norm_w=q_norm_w, k_norm_w=k_norm_w, eps=self.eps, cos=cos, sin=sin, out_loc=md.out_loc,
             prefix_len=md.prefix_len, active=md.active, stable_history=md.stable_history,
+            staged_prefix=md.staged_prefix,
         )
 
     # -- reference slot API (q/k already normalised and rotated) ---------------

@@ -52,6 +52,7 @@ struct DecodeArgs {
   const int32_t* seq_lens;    // [R] keys per row including the new token
   const int32_t* prefix_len;  // device scalar: shared prefix keys (0 = none)
   const int32_t* active;      // [R] nonzero = row runs; nullptr = all rows
+  int stage_cap;              // history-staged kernel: prefix keys staged before the wait
   int rows, hq, hkv;
   float scale;
   __nv_bfloat16* out;  // [R, out_stride]
@@ -240,40 +241,96 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const DecodeAr
 // (the CandidateGroup runtime: the prefix from the prefill, older suffix keys from
 // earlier steps, the row metadata from this step's group step, which precedes the
 // embedding and the qkv projection). CTA (h, r) then copies exactly the keys row r
-// uses (the prefix up to kHistPrefix and its older suffix up to kHistSuffix - 1,
-// contiguous), the RoPE rows of its position and the norm weights into shared
-// memory BEFORE griddepcontrol.wait, i.e. while the qkv projection still runs.
-// After the wait it loads the projection row, applies q/k RMSNorm + bf16 RoPE,
-// stores the new K/V (also as the staged row after the history) and folds all
-// keys from shared memory in one pass per 64 keys. Longer histories stream the
-// rest from the cache after the wait.
-constexpr int kHistPrefix = 128;
+// uses (the prefix up to a per-launch capacity: the caller's bound on the
+// prefix length, at most hist_prefix_cap<D>() keys, the whole 512-position
+// context at head_dim 64; and its older suffix up to kHistSuffix - 1 keys,
+// contiguous; the shared-memory allocation follows the capacity),
+// the RoPE rows of its position and the norm weights into shared memory BEFORE
+// griddepcontrol.wait, i.e. while the qkv projection still runs, with cp.async
+// (every copy in flight at once). After the wait it loads the projection row,
+// applies q/k RMSNorm + bf16 RoPE, stores the new K/V (also as the staged row
+// after the history) and folds all keys from shared memory in one pass per 64
+// keys. Longer histories stream the rest from the cache after the wait.
+//
+// Prefix-once mode (cluster_rows > 1): the CTAs of one KV head's rows form a
+// cluster; CTA c of the cluster reads only slice c of the prefix from the cache
+// and pushes it into every peer's shared memory with cp.async.bulk
+// (shared::cta -> shared::cluster, completing on the peer's mbarrier), so each
+// shared-prefix KV row leaves HBM / L2 once per cluster of rows. All of it still
+// happens before the dependency wait; the folds after it are the same.
 constexpr int kHistSuffix = 32;
-
+constexpr int kHistDefaultPrefix = 128;  // staged prefix keys when the caller gives no bound
 template <int D>
-size_t hist_decode_smem(int group) {
-  const size_t krow = (size_t)(D + 2) * 2, vrow = (size_t)D * 2;
-  return (size_t)group * D * 4 + (size_t)kDecWarps * D * 4 +
-         (size_t)(kHistPrefix + kHistSuffix + kKeyChunk) * (krow + vrow) + (size_t)4 * D * 2;
+__host__ __device__ constexpr int hist_prefix_cap() {
+  return D == 64 ? 512 : D == 96 ? 448 : 256;
+}
+
+// Staged K rows are dense (D bf16, 16-byte aligned, so cp.async and bulk copies
+// can fill them) with their 16-byte chunks rotated: chunk c of key row j lives at
+// chunk (c + rot(j)) mod (D / 8). A 16-byte shared-memory load is served in
+// phases of 8 lanes; the fold's lanes read 8 consecutive rows at the same logical
+// chunk, and these rotations put them in 8 distinct bank groups (checked
+// exhaustively for D = 64, 96, 128: row strides of 128, 192 and 256 bytes).
+template <int D>
+__device__ __forceinline__ int k_chunk(int j, int c) {
+  const int p = c + (D == 96 ? (j & 7) >> 1 : (j & 7));
+  return p >= D / 8 ? p - D / 8 : p;
+}
+
+// q (fp32, shared, broadcast) . staged K row j, in the word order of dot_q_k.
+template <int D>
+__device__ __forceinline__ float dot_q_krow(const float* q, const __nv_bfloat16* K, int j) {
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < D / 8; ++c) {
+    const uint4 v = *reinterpret_cast<const uint4*>(K + (int64_t)j * D + k_chunk<D>(j, c) * 8);
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 kv = bf16x2_to_f2(w4[t]);
+      const int w = c * 4 + t;
+      s += q[2 * w] * kv.x + q[2 * w + 1] * kv.y;
+    }
+  }
+  return s;
+}
+
+// Folds staged rows [j0, j0 + nk) (nk <= 64) into `st`.
+template <int D>
+__device__ __forceinline__ void fold_staged(QState<D>& st, const float* qv, const __nv_bfloat16* K,
+                                            const __nv_bfloat16* V, int j0, int nk, float scale, int lane) {
+  const float s0 = lane < nk ? dot_q_krow<D>(qv, K, j0 + lane) * scale : -INFINITY;
+  const float s1 = lane + 32 < nk ? dot_q_krow<D>(qv, K, j0 + lane + 32) * scale : -INFINITY;
+  fold_scores<D>(st, s0, s1, nk, [&](int j, int i) { return bf16_to_f(V[(int64_t)(j0 + j) * D + i * 32 + lane]); });
 }
 
 template <int D>
-__global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const DecodeArgs a) {
+size_t hist_decode_smem(int group, int cap) {
+  const int rows = cap + kHistSuffix;
+  return (size_t)group * D * 4 + (size_t)kDecWarps * D * 4 + (size_t)rows * D * 2 * 2 +
+         (size_t)kKeyChunk * ((D + 2) * 2 + D * 2) + (size_t)4 * D * 2;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const DecodeArgs a, int cluster_rows) {
   constexpr int DPL = D / 32;
-  constexpr int KR = D + 2;  // padded K row (odd 32-bit word stride)
+  constexpr int KR = D + 2;  // padded K row of the streamed overflow chunks
+  const int kCap = a.stage_cap;  // <= hist_prefix_cap<D>() (host)
   extern __shared__ __align__(16) uint8_t smem_raw[];
-  __shared__ int32_t slot_s[kHistPrefix + kHistSuffix];
+  __shared__ int32_t slot_s[hist_prefix_cap<D>() + kHistSuffix];
+  __shared__ __align__(8) uint64_t pbar;  // prefix-once: the peers' slices have landed
   const int h = blockIdx.x, r = blockIdx.y;
   const int g = a.hq / a.hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool clustered = cluster_rows > 1;
   float* q_s = reinterpret_cast<float*>(smem_raw);  // [g][D]
   float* tmp = q_s + g * D;                          // [warps][D]
   // staged keys, contiguous: [prefix | older suffix | the new key]
-  __nv_bfloat16* Kh = reinterpret_cast<__nv_bfloat16*>(tmp + kDecWarps * D);  // [kHistPrefix + kHistSuffix][KR]
-  __nv_bfloat16* Kw = Kh + (kHistPrefix + kHistSuffix) * KR;  // [kKeyChunk][KR]: streamed overflow
-  __nv_bfloat16* Vh = Kw + kKeyChunk * KR;                     // [kHistPrefix + kHistSuffix][D]
-  __nv_bfloat16* Vw = Vh + (kHistPrefix + kHistSuffix) * D;   // [kKeyChunk][D]
-  __nv_bfloat16* cos_r = Vw + kKeyChunk * D;                   // [D]: RoPE rows of this position
+  __nv_bfloat16* Kh = reinterpret_cast<__nv_bfloat16*>(tmp + kDecWarps * D);  // [kCap + kHistSuffix][D], rotated
+  __nv_bfloat16* Vh = Kh + (kCap + kHistSuffix) * D;                           // [kCap + kHistSuffix][D]
+  __nv_bfloat16* Kw = Vh + (kCap + kHistSuffix) * D;                           // [kKeyChunk][KR]: streamed overflow
+  __nv_bfloat16* Vw = Kw + kKeyChunk * KR;                                     // [kKeyChunk][D]
+  __nv_bfloat16* cos_r = Vw + kKeyChunk * D;                                   // [D]: RoPE rows of this position
   __nv_bfloat16* sin_r = cos_r + D;
   __nv_bfloat16* nq = sin_r + D;  // [D]
   __nv_bfloat16* nk = nq + D;     // [D]
@@ -283,23 +340,35 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
   // two kernels back on this stream (the prefill, earlier steps, and this step's
   // group step for the row's position, key count, slot and active flag). The
   // previous kernel launched this one only after its own griddepcontrol.wait, so
-  // those launches have completed and their writes are visible.
-  const int P = a.prefix_len != nullptr ? *a.prefix_len : 0;
-  const int64_t prow = a.row_table[0], rrow = a.row_table[r];
-  const bool act = a.active == nullptr || a.active[r] != 0;
-  const int pos_in = a.positions[r];
-  const int L_in = a.seq_lens[r];
-  const int64_t oslot = a.out_loc[r];
+  // those launches have completed and their writes are visible. Grid rows past
+  // `rows` (prefix-once padding to whole clusters) only stage their slice.
+  const bool real = r < a.rows;
+  const int P_in = a.prefix_len != nullptr ? *a.prefix_len : 0;
+  const int P = (int64_t)P_in > a.table_stride ? (int)a.table_stride : (P_in < 0 ? 0 : P_in);
+  const int64_t prow = a.row_table[0], rrow = real ? a.row_table[r] : prow;
+  const bool act = real && (a.active == nullptr || a.active[r] != 0);
+  const int pos_in = real ? a.positions[r] : 0;
+  const int L_in = real ? a.seq_lens[r] : 0;
+  const int64_t oslot = real ? a.out_loc[r] : -1;
   const int L_lo = L_in > P + 1 ? L_in : P + 1;
   const int L = (int64_t)L_lo > a.table_stride ? (int)a.table_stride : L_lo;
   const int ns_old = L - 1 - P;                // older suffix keys of this row (>= 0)
-  const int np = min(P, kHistPrefix);           // staged prefix keys
+  const int np = min(P, kCap);                 // staged prefix keys
   const int ns = min(ns_old, kHistSuffix - 1);  // staged older suffix keys
-  const int nst = act ? np + ns : 0;            // the new key goes to row np + ns
+  const int nst = act ? np + ns : 0;           // the new key goes to row np + ns
   const bool pos_ok = pos_in >= 0 && pos_in < a.max_pos;
   const int pos = pos_ok ? pos_in : 0;
-  for (int i = threadIdx.x; i < nst; i += kDecThreads)
-    slot_s[i] = a.page_table[i < np ? prow * a.table_stride + i : rrow * a.table_stride + P + (i - np)];
+  // the prefix rows this CTA reads from the cache: all of them, or its slice
+  const uint32_t rank = clustered ? cluster_ctarank() : 0;
+  const int lo = clustered ? (int)(rank * np / cluster_rows) : 0;
+  const int hi = clustered ? (int)((rank + 1) * np / cluster_rows) : (act ? np : 0);
+  if (clustered && threadIdx.x == 0) {
+    mbar_init(&pbar, 1);
+    fence_mbar_init();
+  }
+  for (int i = lo + threadIdx.x; i < hi; i += kDecThreads) slot_s[i] = a.page_table[prow * a.table_stride + i];
+  for (int i = threadIdx.x; i < (act ? ns : 0); i += kDecThreads)
+    slot_s[np + i] = a.page_table[rrow * a.table_stride + P + i];
   for (int i = threadIdx.x; i < D; i += kDecThreads) {
     nq[i] = a.q_norm_w[i];
     nk[i] = a.k_norm_w[i];
@@ -307,34 +376,57 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
     sin_r[i] = a.sin_tab[(int64_t)pos * D + i];
   }
   __syncthreads();
-  // the staged keys this row uses must be real slots (checked here, off the
-  // critical path; reported after the wait)
+  // every incoming byte of the peers' prefix slices, announced before any peer
+  // can push (the cluster barrier below)
+  if (clustered && threadIdx.x == 0) mbar_arrive_expect_tx(&pbar, (uint32_t)(np - (hi - lo)) * D * 2 * 2);
+  // the staged keys must be real slots (checked here, off the critical path;
+  // reported after the wait)
   bool bad_slot = false;
   if (warp == 0) {
     bool b = false;
-    for (int j = lane; j < nst; j += 32) b |= slot_s[j] < 0 || slot_s[j] >= a.num_slots;
+    for (int j = lo + lane; j < hi; j += 32) b |= slot_s[j] < 0 || slot_s[j] >= a.num_slots;
+    for (int j = lane; j < (act ? ns : 0); j += 32) b |= slot_s[np + j] < 0 || slot_s[np + j] >= a.num_slots;
     bad_slot = __any_sync(0xffffffffu, b);
   }
-  for (int i = threadIdx.x; i < nst * (D / 8); i += kDecThreads) {
-    const int j = i / (D / 8), c = i % (D / 8);
-    int64_t slot = slot_s[j];
-    if (slot < 0 || slot >= a.num_slots) slot = 0;  // reported after the wait
-    const uint4 kv = reinterpret_cast<const uint4*>(a.k_cache + slot * tok_stride + (int64_t)h * D)[c];
-    const uint4 vv = reinterpret_cast<const uint4*>(a.v_cache + slot * tok_stride + (int64_t)h * D)[c];
-    uint32_t* kd = reinterpret_cast<uint32_t*>(Kh + j * KR) + c * 4;
-    kd[0] = kv.x;
-    kd[1] = kv.y;
-    kd[2] = kv.z;
-    kd[3] = kv.w;
-    reinterpret_cast<uint4*>(Vh + j * D)[c] = vv;
+  auto stage_rows = [&](int j0, int j1) {
+    for (int i = threadIdx.x; i < (j1 - j0) * (D / 8); i += kDecThreads) {
+      const int j = j0 + i / (D / 8), c = i % (D / 8);
+      int64_t slot = slot_s[j];
+      if (slot < 0 || slot >= a.num_slots) slot = 0;  // reported after the wait
+      const int64_t off = slot * tok_stride + (int64_t)h * D + c * 8;
+      cp_async16(Kh + (int64_t)j * D + k_chunk<D>(j, c) * 8, a.k_cache + off);
+      cp_async16(Vh + (int64_t)j * D + c * 8, a.v_cache + off);
+    }
+  };
+  stage_rows(lo, hi);
+  if (act) stage_rows(np, np + ns);
+  cp_async_wait_all();
+  if (clustered) {
+    // hand the own slice to the peers: the bulk copies read it through the async proxy
+    fence_proxy_async_shared();
+    __syncthreads();
+    cluster_sync();  // every slice staged, every peer barrier armed
+    if (threadIdx.x == 0 && hi > lo) {
+      const uint32_t bytes = (uint32_t)(hi - lo) * D * 2;
+      const uint32_t k_src = smem_u32(Kh + (int64_t)lo * D), v_src = smem_u32(Vh + (int64_t)lo * D);
+      for (int p = 0; p < cluster_rows; ++p) {
+        if (p == (int)rank) continue;
+        const uint32_t bar = map_shared_rank(smem_u32(&pbar), (uint32_t)p);
+        bulk_push_cluster(map_shared_rank(k_src, (uint32_t)p), k_src, bytes, bar);
+        bulk_push_cluster(map_shared_rank(v_src, (uint32_t)p), v_src, bytes, bar);
+      }
+    }
+    if (!mbar_wait(&pbar, 0) && threadIdx.x == 0) report(a.status, AIOSB_DEV_WAIT_TIMEOUT);
+    cluster_sync();  // every push has landed: no CTA leaves while its slice is being read
   }
-  // (no barrier needed here: after the wait only row np + ns, which staging
-  // never writes, is stored before the barrier that precedes the folds)
+  // (no barrier needed here otherwise: after the wait only row np + ns, which
+  // staging never writes, is stored before the barrier that precedes the folds)
 
   pdl_wait();
   // the next kernel (the o projection) launches once this one has its inputs,
   // which bounds how far ahead the chain prefetches (measured: 5.70 -> 5.54 ms)
   pdl_launch_dependents();
+  if (threadIdx.x == 0 && bad_slot) report(a.status, AIOSB_DEV_SLOT_RANGE);
   // ---- after the wait: this step's projection row
   if (act) {
     if (threadIdx.x == 0 && (!pos_ok || L_in < P + 1 || L_in > a.table_stride))
@@ -363,58 +455,67 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
         if (!slot_ok && lane == 0) report(a.status, AIOSB_DEV_SLOT_RANGE);
 #pragma unroll
         for (int i = 0; i < DPL; ++i) {
+          const int e = i * 32 + lane;
           const __nv_bfloat16 kb = f_to_bf16(x[i]);
-          Kh[nst * KR + i * 32 + lane] = kb;
-          Vh[nst * D + i * 32 + lane] = vraw[i];
+          Kh[(int64_t)nst * D + k_chunk<D>(nst, e / 8) * 8 + (e & 7)] = kb;
+          Vh[(int64_t)nst * D + e] = vraw[i];
           if (slot_ok) {
-            a.k_cache[oslot * tok_stride + (int64_t)h * D + i * 32 + lane] = kb;
-            a.v_cache[oslot * tok_stride + (int64_t)h * D + i * 32 + lane] = vraw[i];
+            a.k_cache[oslot * tok_stride + (int64_t)h * D + e] = kb;
+            a.v_cache[oslot * tok_stride + (int64_t)h * D + e] = vraw[i];
           }
         }
       }
     }
-    if (threadIdx.x == 0 && bad_slot) report(a.status, AIOSB_DEV_SLOT_RANGE);
   }
   __syncthreads();
 
   QState<D> st[2];
   qstate_init<D>(st[0]);
   qstate_init<D>(st[1]);
-  auto fold_all = [&](const __nv_bfloat16* K, const __nv_bfloat16* V, int nk) {
-    if (!act) return;
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const int j = warp + t * kDecWarps;
-      if (j < g) fold_chunk<D>(st[t], q_s + j * D, K, V, nk, a.scale, lane);
-    }
-  };
   const int32_t* pslots = a.page_table + prow * a.table_stride;
   const int32_t* rslots = a.page_table + rrow * a.table_stride;
-  // staged keys [prefix | older suffix] and, without a suffix overflow, the new
-  // key right after them: one pass per 64 keys
-  const int nfold = act ? nst + (ns_old == ns ? 1 : 0) : 0;
-  for (int c0 = 0; c0 < nfold; c0 += kKeyChunk) fold_all(Kh + c0 * KR, Vh + c0 * D, min(kKeyChunk, nfold - c0));
-  // longer histories: the prefix beyond the staged part, then the older suffix
-  // beyond it, streamed from the cache, and the new key last
-  for (int k0 = np; k0 < P; k0 += kKeyChunk) {
-    const int n = min(kKeyChunk, P - k0);
-    stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, pslots, k0, n, a.num_slots, Kw, Vw, a.status);
-    __syncthreads();
-    fold_all(Kw, Vw, n);
-    __syncthreads();
-  }
-  if (act && ns_old > ns) {
-    for (int k0 = P + ns; k0 < L - 1; k0 += kKeyChunk) {
-      const int n = min(kKeyChunk, L - 1 - k0);
-      stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, rslots, k0, n, a.num_slots, Kw, Vw, a.status);
+  if (act) {
+    auto fold_rows = [&](int j0, int n) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int j = warp + t * kDecWarps;
+        if (j < g) fold_staged<D>(st[t], q_s + j * D, Kh, Vh, j0, n, a.scale, lane);
+      }
+    };
+    auto fold_stream = [&](int n) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int j = warp + t * kDecWarps;
+        if (j < g) fold_chunk<D>(st[t], q_s + j * D, Kw, Vw, n, a.scale, lane);
+      }
+    };
+    // staged keys [prefix | older suffix] and, without a suffix overflow, the new
+    // key right after them: one pass per 64 keys
+    const int nfold = nst + (ns_old == ns ? 1 : 0);
+    for (int c0 = 0; c0 < nfold; c0 += kKeyChunk) fold_rows(c0, min(kKeyChunk, nfold - c0));
+    // longer histories: the prefix beyond the staged part, then the older suffix
+    // beyond it, streamed from the cache, and the new key last
+    for (int k0 = np; k0 < P; k0 += kKeyChunk) {
+      const int n = min(kKeyChunk, P - k0);
+      stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, pslots, k0, n, a.num_slots, Kw, Vw, a.status);
       __syncthreads();
-      fold_all(Kw, Vw, n);
+      fold_stream(n);
       __syncthreads();
     }
-    fold_all(Kh + nst * KR, Vh + nst * D, 1);
+    if (ns_old > ns) {
+      for (int k0 = P + ns; k0 < L - 1; k0 += kKeyChunk) {
+        const int n = min(kKeyChunk, L - 1 - k0);
+        stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, rslots, k0, n, a.num_slots, Kw, Vw, a.status);
+        __syncthreads();
+        fold_stream(n);
+        __syncthreads();
+      }
+      fold_rows(nst, 1);
+    }
   }
 
   // ---- normalise and store (zeros for inactive rows)
+  if (!real) return;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     const int j = warp + t * kDecWarps;
@@ -632,17 +733,34 @@ cudaError_t launch_decode(const DecodeArgs& a, int rows, int hkv, int group, cud
   return cudaLaunchKernelEx(&cfg, kern, a, cluster_rows);
 }
 template <int D>
-cudaError_t launch_decode_hist(const DecodeArgs& a, int rows, int hkv, int group, cudaStream_t stream) {
+cudaError_t launch_decode_hist(const DecodeArgs& a, int rows, int hkv, int group, int cluster_rows,
+                               cudaStream_t stream) {
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   auto kern = attn_decode_hist_kernel<D>;
   if (dev >= 0 && dev < 64 && !configured[dev]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_decode_smem<D>(kMaxGroupQ));
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)hist_decode_smem<D>(kMaxGroupQ, hist_prefix_cap<D>()));
     configured[dev] = true;
   }
-  return launch_pdl(kern, dim3((unsigned)hkv, (unsigned)rows), dim3(kDecThreads), hist_decode_smem<D>(group), stream,
-                    a);
+  // prefix-once: whole clusters of rows per KV head (padding rows only stage)
+  const int grid_rows = (rows + cluster_rows - 1) / cluster_rows * cluster_rows;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)hkv, (unsigned)grid_rows);
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = hist_decode_smem<D>(group, a.stage_cap);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = (unsigned)cluster_rows;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = cluster_rows > 1 ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kern, a, cluster_rows);
 }
 
 template <int D>
@@ -666,9 +784,9 @@ extern "C" int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const
                                       const int32_t* out_loc, void* k_cache, void* v_cache, int64_t num_slots,
                                       const int32_t* page_table, int64_t table_stride, const int32_t* row_table,
                                       const int32_t* seq_lens, const int32_t* prefix_len, const int32_t* active,
-                                      int stable_history, int64_t rows, int64_t num_qo_heads, int64_t num_kv_heads,
-                                      int64_t head_dim, float scale, void* out, int64_t out_stride, int32_t* status,
-                                      void* stream) {
+                                      int stable_history, int64_t staged_prefix, int64_t rows,
+                                      int64_t num_qo_heads, int64_t num_kv_heads, int64_t head_dim, float scale,
+                                      void* out, int64_t out_stride, int32_t* status, void* stream) {
   AIOSB_REQUIRE(rows >= 0 && num_kv_heads > 0 && num_qo_heads > 0 && num_qo_heads % num_kv_heads == 0,
                 AIOSB_ERR_INVALID_ARG, "query head count must be divisible by KV head count");
   AIOSB_REQUIRE(head_dim == 64 || head_dim == 96 || head_dim == 128, AIOSB_ERR_UNSUPPORTED,
@@ -705,6 +823,7 @@ extern "C" int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const
   a.seq_lens = seq_lens;
   a.prefix_len = prefix_len;
   a.active = active;
+  a.stage_cap = kHistDefaultPrefix;
   a.rows = (int)rows;
   a.hq = (int)num_qo_heads;
   a.hkv = (int)num_kv_heads;
@@ -715,9 +834,19 @@ extern "C" int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const
   cudaError_t e;
   cudaStream_t s = as_stream(stream);
   if (stable_history && qkv != nullptr) {
-    if (head_dim == 64) e = launch_decode_hist<64>(a, (int)rows, (int)num_kv_heads, (int)g, s);
-    else if (head_dim == 96) e = launch_decode_hist<96>(a, (int)rows, (int)num_kv_heads, (int)g, s);
-    else e = launch_decode_hist<128>(a, (int)rows, (int)num_kv_heads, (int)g, s);
+    AIOSB_REQUIRE(stable_history == AIOSB_HISTORY_STAGED || stable_history == AIOSB_HISTORY_PREFIX_ONCE,
+                  AIOSB_ERR_INVALID_ARG, "attention_decode: unknown stable_history mode %d", stable_history);
+    AIOSB_REQUIRE(aligned16(k_cache) && aligned16(v_cache), AIOSB_ERR_MISALIGNED,
+                  "attention_decode: the KV cache must be 16-byte aligned");
+    const int cr = stable_history == AIOSB_HISTORY_PREFIX_ONCE ? (int)std::min<int64_t>(rows, 8) : 1;
+    // staged prefix keys: the caller's bound rounded up to 64, at most what fits
+    const int64_t cap_max = head_dim == 64 ? hist_prefix_cap<64>() : head_dim == 96 ? hist_prefix_cap<96>()
+                                                                                      : hist_prefix_cap<128>();
+    const int64_t want = staged_prefix > 0 ? (staged_prefix + 63) / 64 * 64 : kHistDefaultPrefix;
+    a.stage_cap = (int)std::min(want, cap_max);
+    if (head_dim == 64) e = launch_decode_hist<64>(a, (int)rows, (int)num_kv_heads, (int)g, cr, s);
+    else if (head_dim == 96) e = launch_decode_hist<96>(a, (int)rows, (int)num_kv_heads, (int)g, cr, s);
+    else e = launch_decode_hist<128>(a, (int)rows, (int)num_kv_heads, (int)g, cr, s);
   } else if (head_dim == 64) {
     e = launch_decode<64>(a, (int)rows, (int)num_kv_heads, (int)g, s);
   } else if (head_dim == 96) {

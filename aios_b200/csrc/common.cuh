@@ -31,6 +31,7 @@ __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v 
 __device__ __forceinline__ float bf16_to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ __nv_bfloat16 f_to_bf16(float v) { return __float2bfloat16_rn(v); }
 // Round an fp32 value to the nearest bf16 and return it as fp32 again.
+__device__ __forceinline__ float2 bf16x2_to_f2(uint32_t v) { return make_float2(bf16_lo(v), bf16_hi(v)); }
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
@@ -93,6 +94,12 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+// 16-byte asynchronous global -> shared copy (both addresses 16-byte aligned);
+// cp_async_wait_all waits for all of this thread's copies.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
@@ -234,6 +241,23 @@ __device__ __forceinline__ uint32_t map_shared_rank(uint32_t smem_addr, uint32_t
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
+}
+// Bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from
+// this CTA's shared memory into a peer CTA's shared memory in the cluster,
+// completing on the peer's mbarrier (all three cluster addresses from mapa).
+// Point to point: no multicast.
+__device__ __forceinline__ void bulk_push_cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                  uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (bulk copy) reads of them.
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
   float4 v;

@@ -69,6 +69,11 @@ struct GemmArgs {
   float* out_stat_x;
   float* out_stat_ss;
   int64_t out_ss_stride;
+  // 1: launch the next kernel at entry (its weight prefetch overlaps this one);
+  // 0: only once this CTA's accumulator is complete. A grid of more than one wave
+  // uses 0, so that early-launched dependent CTAs (each holding an SM's shared
+  // memory while it waits) do not take the SMs its later waves need.
+  int early_dependents;
 };
 
 constexpr int kMaxNormRows = 64;
@@ -104,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nch = a.chunks_per_split;
   const int k_chunk0 = split_idx * nch;
 
-  pdl_launch_dependents();  // the next kernel may start its own weight prefetch now
+  if (a.early_dependents) pdl_launch_dependents();  // the next kernel may start its own weight prefetch now
   if (tid == 0) {
     for (int s = 0; s < a.stages; ++s) {
       mbar_init(&full[s], 1);
@@ -325,18 +330,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     report(a.status, AIOSB_DEV_WAIT_TIMEOUT);
     *abort_flag = 1;
   }
+  if (!a.early_dependents) pdl_launch_dependents();
   // tcgen05.ld is warp-collective (.sync.aligned): reconverge and agree first.
   __syncwarp();
   have = __all_sync(0xffffffffu, have);
   tc_fence_after();
   if (have) {
+    // two 16-column loads in flight per wait
 #pragma unroll
-    for (int cb = 0; cb < BN / 16; ++cb) {
-      float v[16];
-      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(cb * 16), v);
+    for (int cb = 0; cb < BN / 16; cb += 2) {
+      float v[2][16];
+      tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(cb * 16), v[0]);
+      if (cb + 1 < BN / 16) tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)((cb + 1) * 16), v[1]);
       tc_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) red[(cb * 16 + j) * kBM + 32 * warp + lane] = v[j];
+      for (int h = 0; h < 2; ++h) {
+        if (cb + h < BN / 16) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) red[((cb + h) * 16 + j) * kBM + 32 * warp + lane] = v[h][j];
+        }
+      }
     }
   }
   tc_fence_before();
@@ -352,72 +365,123 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t rank = split > 1 ? cluster_ctarank() : 0u;
     const uint32_t red_addr = smem_u32(red);
     const int64_t t0 = (int64_t)n_tile * BN;
+    // A thread's partial-tile reads (local, or a peer's over distributed shared
+    // memory) are issued kG units at a time, so that a group costs one DSMEM
+    // round trip per rank instead of one per unit; every unit still sums the
+    // ranks in rank order.
+    constexpr int kG = 8;
+    auto part = [&](uint32_t off, int q) -> float4 {
+      if (split > 1) return ld_dsmem_f4(map_shared_rank(red_addr + off, (uint32_t)q));
+      return *reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(red) + off);
+    };
     if (a.epilogue == AIOSB_EPI_STORE || a.epilogue == AIOSB_EPI_ADD) {
-      // 32 float4 per column; 128 threads handle 4 columns per pass.
-      for (int idx = tid; idx < BN * 32; idx += kThreads) {
-        const int c = idx >> 5, m4 = idx & 31;
-        if ((c % split) != (int)rank) continue;
-        const int64_t t = t0 + c;
-        if (t >= a.rows) continue;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        const uint32_t off = (uint32_t)((c * kBM + m4 * 4) * 4);
-        for (int q = 0; q < split; ++q) {
-          float4 p;
-          if (split > 1) p = ld_dsmem_f4(map_shared_rank(red_addr + off, (uint32_t)q));
-          else p = *reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(red) + off);
-          acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+      // unit idx: column c = idx / 32 (a token), 4 tile rows m4 * 4.. (32 per column);
+      // rank r owns the columns c % split == r
+      const int own = (BN + split - 1 - (int)rank) / split;  // columns of this rank
+      const int units = own * 32;
+      for (int u0 = tid; u0 < units; u0 += kThreads * kG) {
+        float4 acc[kG];
+        uint32_t off[kG];
+        bool live[kG];
+#pragma unroll
+        for (int j = 0; j < kG; ++j) {
+          const int u = u0 + j * kThreads;
+          const int c = (u >> 5) * split + (int)rank, m4 = u & 31;
+          live[j] = u < units && t0 + c < a.rows;
+          off[j] = (uint32_t)((c * kBM + m4 * 4) * 4);
+          acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        __nv_bfloat16* dst = a.y + t * a.y_row_stride + (int64_t)m_tile * kBM + m4 * 4;
-        if (a.epilogue == AIOSB_EPI_ADD) {
-          // residual + delta with the delta rounded to bf16 first, as the
-          // reference's bf16 `partial + delta` (aios/models/minimind_ime.py:237-252).
-          const uint2 rv = *reinterpret_cast<const uint2*>(a.residual + t * a.residual_stride +
-                                                          (int64_t)m_tile * kBM + m4 * 4);
-          acc.x = bf16_lo(rv.x) + round_bf16(acc.x);
-          acc.y = bf16_hi(rv.x) + round_bf16(acc.y);
-          acc.z = bf16_lo(rv.y) + round_bf16(acc.z);
-          acc.w = bf16_hi(rv.y) + round_bf16(acc.w);
-          if (a.out_stat_x != nullptr) {
-            // one warp owns column c: its 32 lanes cover the tile's 128 rows
-            *reinterpret_cast<float4*>(a.out_stat_x + t * a.n + (int64_t)m_tile * kBM + m4 * 4) = acc;
-            float ss = acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
-            ss = warp_sum(ss);
-            if (lane == 0) a.out_stat_ss[(int64_t)m_tile * a.out_ss_stride + t] = ss;
+        for (int q = 0; q < split; ++q) {
+          float4 p[kG];
+#pragma unroll
+          for (int j = 0; j < kG; ++j)
+            if (live[j]) p[j] = part(off[j], q);
+#pragma unroll
+          for (int j = 0; j < kG; ++j) {
+            if (live[j]) {
+              acc[j].x += p[j].x; acc[j].y += p[j].y; acc[j].z += p[j].z; acc[j].w += p[j].w;
+            }
           }
         }
-        uint2 o = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
-        *reinterpret_cast<uint2*>(dst) = o;
+#pragma unroll
+        for (int j = 0; j < kG; ++j) {
+          const int u = u0 + j * kThreads;
+          const int c = (u >> 5) * split + (int)rank, m4 = u & 31;
+          // whole warps share a column (32 units), so `live` is warp-uniform here
+          if (!live[j]) continue;
+          const int64_t t = t0 + c;
+          float4 v = acc[j];
+          __nv_bfloat16* dst = a.y + t * a.y_row_stride + (int64_t)m_tile * kBM + m4 * 4;
+          if (a.epilogue == AIOSB_EPI_ADD) {
+            // residual + delta with the delta rounded to bf16 first, as the
+            // reference's bf16 `partial + delta` (aios/models/minimind_ime.py:237-252).
+            const uint2 rv = *reinterpret_cast<const uint2*>(a.residual + t * a.residual_stride +
+                                                            (int64_t)m_tile * kBM + m4 * 4);
+            v.x = bf16_lo(rv.x) + round_bf16(v.x);
+            v.y = bf16_hi(rv.x) + round_bf16(v.y);
+            v.z = bf16_lo(rv.y) + round_bf16(v.z);
+            v.w = bf16_hi(rv.y) + round_bf16(v.w);
+            if (a.out_stat_x != nullptr) {
+              // one warp owns column c: its 32 lanes cover the tile's 128 rows
+              *reinterpret_cast<float4*>(a.out_stat_x + t * a.n + (int64_t)m_tile * kBM + m4 * 4) = v;
+              float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+              ss = warp_sum(ss);
+              if (lane == 0) a.out_stat_ss[(int64_t)m_tile * a.out_ss_stride + t] = ss;
+            }
+          }
+          *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+        }
       }
     } else {
-      // SILU_MUL: tile rows 0..63 are gate rows, 64..127 the matching up rows.
-      for (int idx = tid; idx < BN * 16; idx += kThreads) {
-        const int c = idx >> 4, m4 = idx & 15;
-        if ((c % split) != (int)rank) continue;
-        const int64_t t = t0 + c;
-        if (t >= a.rows) continue;
-        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
-        const uint32_t og = (uint32_t)((c * kBM + m4 * 4) * 4);
-        const uint32_t ou = og + 64 * 4;
-        for (int q = 0; q < split; ++q) {
-          float4 pg, pu;
-          if (split > 1) {
-            pg = ld_dsmem_f4(map_shared_rank(red_addr + og, (uint32_t)q));
-            pu = ld_dsmem_f4(map_shared_rank(red_addr + ou, (uint32_t)q));
-          } else {
-            pg = *reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(red) + og);
-            pu = *reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(red) + ou);
-          }
-          g.x += pg.x; g.y += pg.y; g.z += pg.z; g.w += pg.w;
-          u.x += pu.x; u.y += pu.y; u.z += pu.z; u.w += pu.w;
-        }
-        // gate_up output is bf16 before silu_and_mul (aios/models/qwen3.py:90-92).
-        const float gv[4] = {round_bf16(g.x), round_bf16(g.y), round_bf16(g.z), round_bf16(g.w)};
-        const float uv[4] = {round_bf16(u.x), round_bf16(u.y), round_bf16(u.z), round_bf16(u.w)};
-        float r[4];
+      // SILU_MUL: tile rows 0..63 are gate rows, 64..127 the matching up rows;
+      // unit idx: column c = idx / 16, 4 gate rows m4 * 4.. and their up rows
+      const int own = (BN + split - 1 - (int)rank) / split;
+      const int units = own * 16;
+      for (int u0 = tid; u0 < units; u0 += kThreads * kG) {
+        float4 g[kG], up[kG];
+        uint32_t og[kG];
+        bool live[kG];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) r[j] = gv[j] / (1.0f + expf(-gv[j])) * uv[j];
-        __nv_bfloat16* dst = a.y + t * a.y_row_stride + (int64_t)m_tile * (kBM / 2) + m4 * 4;
-        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+        for (int j = 0; j < kG; ++j) {
+          const int u = u0 + j * kThreads;
+          const int c = (u >> 4) * split + (int)rank, m4 = u & 15;
+          live[j] = u < units && t0 + c < a.rows;
+          og[j] = (uint32_t)((c * kBM + m4 * 4) * 4);
+          g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          up[j] = g[j];
+        }
+        for (int q = 0; q < split; ++q) {
+          float4 pg[kG], pu[kG];
+#pragma unroll
+          for (int j = 0; j < kG; ++j) {
+            if (live[j]) {
+              pg[j] = part(og[j], q);
+              pu[j] = part(og[j] + 64 * 4, q);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < kG; ++j) {
+            if (live[j]) {
+              g[j].x += pg[j].x; g[j].y += pg[j].y; g[j].z += pg[j].z; g[j].w += pg[j].w;
+              up[j].x += pu[j].x; up[j].y += pu[j].y; up[j].z += pu[j].z; up[j].w += pu[j].w;
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kG; ++j) {
+          if (!live[j]) continue;
+          const int u = u0 + j * kThreads;
+          const int c = (u >> 4) * split + (int)rank, m4 = u & 15;
+          const int64_t t = t0 + c;
+          // gate_up output is bf16 before silu_and_mul (aios/models/qwen3.py:90-92).
+          const float gv[4] = {round_bf16(g[j].x), round_bf16(g[j].y), round_bf16(g[j].z), round_bf16(g[j].w)};
+          const float uv[4] = {round_bf16(up[j].x), round_bf16(up[j].y), round_bf16(up[j].z), round_bf16(up[j].w)};
+          float r[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) r[e] = gv[e] / (1.0f + expf(-gv[e])) * uv[e];
+          __nv_bfloat16* dst = a.y + t * a.y_row_stride + (int64_t)m_tile * (kBM / 2) + m4 * 4;
+          *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+        }
       }
     }
   }
@@ -531,9 +595,9 @@ namespace aiosb {
 namespace {
 
 int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* stream) {
-  const int bn = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256;
+  int bn = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : rows <= 128 ? 128 : 256;
   const int64_t m_tiles = n / kBM;
-  const int64_t n_tiles = (rows + bn - 1) / bn;
+  int64_t n_tiles = (rows + bn - 1) / bn;
   const int64_t chunks = k / kBK;
   a.rows = rows;
   a.n = n;
@@ -572,7 +636,23 @@ int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* 
            (size_t)a.stages * kABytes + (size_t)a.chunks_per_split * bn * kBK * 2 + 2048 > (size_t)kMaxDynSmem)
       --a.stages;
   };
-  plan();
+  // norm modes keep every B chunk of the CTA in shared memory: narrower token
+  // tiles (more of them, so fewer K chunks per CTA) until one weight stage fits
+  auto norm_fits = [&]() {
+    return (size_t)a.stages * kABytes + (size_t)a.chunks_per_split * bn * kBK * 2 + 2048 <= (size_t)kMaxDynSmem;
+  };
+  auto plan_all = [&]() {
+    plan();
+    while (a.norm && !norm_fits() && bn > 16) {
+      bn /= 2;
+      n_tiles = (rows + bn - 1) / bn;
+      plan();
+    }
+    a.early_dependents = m_tiles * n_tiles * a.split <= sm_count() ? 1 : 0;
+  };
+  plan_all();
+  AIOSB_REQUIRE(!a.norm || norm_fits(), AIOSB_ERR_UNSUPPORTED, "linear: normalised operand of k=%lld too large",
+                (long long)k);
   CUtensorMap tw, tx;
   int rc = make_map(&tw, w, n, k, kBM);
   if (rc) return rc;
@@ -597,7 +677,7 @@ int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* 
     // Non-portable 16-CTA clusters are an opt-in; fall back to portable sizes.
     (void)cudaGetLastError();
     g_max_split = 8;
-    plan();
+    plan_all();
     rc = launch();
   }
   return rc;

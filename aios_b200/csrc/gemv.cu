@@ -68,7 +68,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
   const int g = lane >> 2, t4 = lane & 3;
   const int K = (int)a.k;
   const int kb = K / 256;  // 32-wide blocks per warp
-  const int T = a.rows;
+  // grid row y covers token rows [row0, row0 + TM) (prefill widths: several row groups)
+  const int row0 = blockIdx.y * TM;
+  const int T = min(TM, a.rows - row0);
+  const bool streaming = gridDim.y == 1;  // weights read by one row group only
   const bool silu = a.epilogue == AIOSB_EPI_SILU_MUL;
   const int feat_per_tile = silu ? 8 : 16;
   const int ntiles = (int)(a.n_out / feat_per_tile);
@@ -89,12 +92,15 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
     // than L2 holds, so they are loaded cache-streaming (evict first): the
     // activations, the KV cache and the kernels' code stay in L2 across the step
     // instead of being refetched from DRAM (measured: 243.6 -> 220.5 us per S10
-    // decode step; the sampler step kernel alone 35 -> 25 us).
+    // decode step; the sampler step kernel alone 35 -> 25 us). With several row
+    // groups the other groups' CTAs read the same tile, so it stays cached.
 #pragma unroll
     for (int b = 0; b < KB; ++b) {
       const bool ok = tl < ntiles && b < kb;
-      wa[b] = ok ? __ldcs(reinterpret_cast<const uint4*>(a.w + r0 * K + kbase + b * 32)) : make_uint4(0u, 0u, 0u, 0u);
-      wb[b] = ok ? __ldcs(reinterpret_cast<const uint4*>(a.w + r1 * K + kbase + b * 32)) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4* pa = reinterpret_cast<const uint4*>(a.w + r0 * K + kbase + b * 32);
+      const uint4* pb = reinterpret_cast<const uint4*>(a.w + r1 * K + kbase + b * 32);
+      wa[b] = ok ? (streaming ? __ldcs(pa) : __ldg(pa)) : make_uint4(0u, 0u, 0u, 0u);
+      wb[b] = ok ? (streaming ? __ldcs(pb) : __ldg(pb)) : make_uint4(0u, 0u, 0u, 0u);
     }
   };
   uint4 wa[KB], wb[KB];
@@ -122,8 +128,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
       const int n = nt * 8 + g;
 #pragma unroll
       for (int b = 0; b < KB; ++b)
-        xb[nt][b] = (n < T && b < kb) ? *reinterpret_cast<const uint4*>(a.x + (int64_t)n * a.x_stride + kbase + b * 32)
-                                      : make_uint4(0u, 0u, 0u, 0u);
+        xb[nt][b] = (n < T && b < kb)
+                        ? *reinterpret_cast<const uint4*>(a.x + (int64_t)(row0 + n) * a.x_stride + kbase + b * 32)
+                        : make_uint4(0u, 0u, 0u, 0u);
     }
   } else {
     // rows normalised from the fp32 residual stream s (RMSNormFused,
@@ -136,7 +143,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
 #pragma unroll
       for (int b = 0; b < KB; ++b) {
         const bool ok = n < T && b < kb;
-        const float4* src = reinterpret_cast<const float4*>(a.stat_x + (int64_t)n * K + kbase + b * 32);
+        const float4* src = reinterpret_cast<const float4*>(a.stat_x + (int64_t)(row0 + n) * K + kbase + b * 32);
         sv[nt][b][0] = ok ? src[0] : make_float4(0.f, 0.f, 0.f, 0.f);
         sv[nt][b][1] = ok ? src[1] : make_float4(0.f, 0.f, 0.f, 0.f);
       }
@@ -177,7 +184,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
   // epilogue thread (token, half) of the residual add: its 8 residual values are
   // requested now, so their round trip overlaps the activation loads and MMAs
   const bool epi_thread = tid < TM * 2 && (tid >> 1) < T && !silu;
-  const int64_t epi_row = (int64_t)(tid >> 1);
+  const int64_t epi_row = (int64_t)row0 + (tid >> 1);
   auto load_res = [&](int tl) {
     return (epi_thread && a.epilogue == AIOSB_EPI_ADD && tl < ntiles)
                ? *reinterpret_cast<const uint4*>(a.residual + epi_row * a.residual_stride + (int64_t)tl * 16 +
@@ -240,20 +247,20 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
               o[j] = res + round_bf16(tile[tk][8 * h + j]);
             }
             if (a.out_stat_x != nullptr) {
-              float4* sx = reinterpret_cast<float4*>(a.out_stat_x + (int64_t)tk * a.n_out + f0);
+              float4* sx = reinterpret_cast<float4*>(a.out_stat_x + (int64_t)(row0 + tk) * a.n_out + f0);
               sx[0] = make_float4(o[0], o[1], o[2], o[3]);
               sx[1] = make_float4(o[4], o[5], o[6], o[7]);
               float ss = 0.f;
 #pragma unroll
               for (int j = 0; j < 8; ++j) ss += o[j] * o[j];
-              a.out_stat_ss[(f0 / kGemvStatGroup) * a.out_ss_stride + tk] = ss;
+              a.out_stat_ss[(f0 / kGemvStatGroup) * a.out_ss_stride + row0 + tk] = ss;
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 8; ++j) o[j] = tile[tk][8 * h + j];
           }
         }
-        *reinterpret_cast<uint4*>(a.y + (int64_t)tk * a.y_stride + f0) =
+        *reinterpret_cast<uint4*>(a.y + (int64_t)(row0 + tk) * a.y_stride + f0) =
             make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
                        pack_bf16x2(o[6], o[7]));
       }
@@ -279,8 +286,10 @@ int launch_mma(const GemvArgs& a, cudaStream_t stream) {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, 0) != cudaSuccess || n < 1) n = 2;
     per_sm = n;
   }
-  const unsigned blocks = (unsigned)std::min<int64_t>(tiles, (int64_t)per_sm * sm_count());
-  cudaError_t e = launch_pdl(kern, dim3(blocks), dim3(kGemvThreads), 0, stream, a);
+  const int groups = (a.rows + NT * 8 - 1) / (NT * 8);  // token row groups (grid y)
+  const int64_t resident = std::max<int64_t>(1, (int64_t)per_sm * sm_count() / groups);
+  const unsigned blocks = (unsigned)std::min<int64_t>(tiles, resident);
+  cudaError_t e = launch_pdl(kern, dim3(blocks, (unsigned)groups), dim3(kGemvThreads), 0, stream, a);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "linear (gemv mma): %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }
@@ -297,8 +306,17 @@ bool g_gemv_enabled = [] {
 
 }  // namespace
 
+// Widest operand the register-operand path takes (more rows run as several
+// 16-row groups, each re-reading the weight tile from L2); AIOSB_GEMV_MAX_ROWS
+// lowers or raises it (1..kMaxGemvRows).
+int g_gemv_max_rows = [] {
+  const char* env = getenv("AIOSB_GEMV_MAX_ROWS");
+  const int v = env ? atoi(env) : kGemvDefaultRows;
+  return v >= 1 && v <= kMaxGemvRows ? v : kGemvDefaultRows;
+}();
+
 bool gemv_eligible(int64_t rows, int64_t k, int64_t n_out) {
-  return g_gemv_enabled && rows >= 1 && rows <= kMaxGemvRows && k % 256 == 0 && k <= kMaxGemvK &&
+  return g_gemv_enabled && rows >= 1 && rows <= g_gemv_max_rows && k % 256 == 0 && k <= kMaxGemvK &&
          n_out % 16 == 0;
 }
 

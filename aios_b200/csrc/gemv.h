@@ -8,7 +8,13 @@
 
 namespace aiosb {
 
-constexpr int kMaxGemvRows = 16;
+// Token rows: up to 16 in one row group (decode), more as 16-row groups along
+// grid y (prefill widths), up to kMaxGemvRows; rows above kGemvDefaultRows go to
+// the tcgen05 GEMM unless AIOSB_GEMV_MAX_ROWS says otherwise. Measured per S10
+// linear (us, GEMV / tcgen05): 32 rows 2.9 / 6.4-7.3, 64 rows 4.1 / 8.0-8.7,
+// 128 rows 6.1 / 11.4-13.3, 512 rows 19.9 / 16.1-21.4, 2048 rows 78.9 / 27-35.
+constexpr int kMaxGemvRows = 4096;
+constexpr int kGemvDefaultRows = 512;
 constexpr int kMaxGemvK = 2048;
 
 struct GemvArgs {

@@ -519,12 +519,17 @@ def attention_decode(
     out_loc: torch.Tensor | None = None,
     prefix_len: torch.Tensor | None = None,
     active: torch.Tensor | None = None,
-    stable_history: bool = False,
+    stable_history: bool | int = False,
+    staged_prefix: int = 0,
 ) -> torch.Tensor:
     """Decode attention. ``stable_history`` (fused ``qkv`` mode): the row table,
     prefix length, page-table entries before each row's current position and their
     K/V were written before the previous kernel on the stream began, so the kernel
-    may stage them before waiting on that kernel."""
+    may stage them before waiting on that kernel. ``True`` / ``HISTORY_STAGED``:
+    each row reads its keys itself; ``HISTORY_PREFIX_ONCE``: the rows of a KV head
+    read the shared prefix once between them (a cluster of up to 8 rows).
+    ``staged_prefix``: a bound on the prefix length (0: 128); the kernel stages that
+    many prefix keys before its wait and sizes its shared memory by it."""
     rows = out.shape[0]
     num_slots = k_cache.numel() // (num_kv_heads * head_dim)
     src = qkv if qkv is not None else q
@@ -551,7 +556,8 @@ def attention_decode(
         seq_lens.data_ptr(),
         _ptr(prefix_len),
         _ptr(active),
-        int(bool(stable_history)),
+        int(stable_history),
+        int(staged_prefix),
         rows,
         num_qo_heads,
         num_kv_heads,

@@ -51,6 +51,22 @@ LARGE_SORT_VOCAB = 16384  # larger sorted sets sort whole rows: vocabularies up 
 # rounding points.
 _PERSISTENT = os.environ.get("AIOSB_PERSISTENT_DECODE", "0") == "1"
 
+# How the decode attention reads its key history (aiosb_attention_decode's
+# stable_history): "staged" (every row's CTA reads its keys itself, before the
+# dependency wait), "prefix_once" (the rows of a KV head split the shared prefix
+# and exchange it over distributed shared memory, before the wait) or "cascade"
+# (the cluster-cascade kernel, everything after the wait).
+HISTORY_MODES = {"cascade": 0, "staged": _lib.HISTORY_STAGED, "prefix_once": _lib.HISTORY_PREFIX_ONCE}
+_HISTORY = HISTORY_MODES[os.environ.get("AIOSB_DECODE_HISTORY", "staged")]
+# Prefix lengths up to which the decode attention stages the whole prefix before
+# its dependency wait, one step graph per class: its shared memory grows with the
+# class (a 512-key class costs every short keystroke about 2-5%).
+STAGE_CLASSES = (128, 512)
+
+
+def stage_class(prefix_len: int) -> int:
+    return next((c for c in STAGE_CLASSES if prefix_len <= c), STAGE_CLASSES[-1])
+
 
 @dataclass
 class RoundResult:
@@ -169,6 +185,14 @@ class CandidateGroupRuntime:
         self.record_logits = False
         self.step_logits: list[torch.Tensor] = []
         self._step_plan = self._persistent_plan() if _PERSISTENT else None
+        self.history_mode = _HISTORY
+
+    def use_history_mode(self, mode: str) -> None:
+        """Selects the decode attention's history mode (a HISTORY_MODES name) for
+        this runtime's step graphs; captured graphs are dropped."""
+        self.history_mode = HISTORY_MODES[mode]
+        self._graphs.clear()
+        self._graph_launches.clear()
 
     def use_persistent_step(self, enabled: bool = True) -> bool:
         """Switches this runtime's decode forward to (or away from) the persistent
@@ -243,7 +267,7 @@ class CandidateGroupRuntime:
         _lib.call("aiosb_decode_step", ctypes.byref(args), self._stream())
 
     # ------------------------------------------------------------------ graphs
-    def _decode_batch(self, rows: int) -> Batch:
+    def _decode_batch(self, rows: int, stage: int = STAGE_CLASSES[0]) -> Batch:
         reqs = [Req(input_ids=torch.empty(1, dtype=torch.long), cached_len=0, output_len=1, uid=i,
                     sampling_params=SamplingParams(max_tokens=1), table_idx=i) for i in range(rows)]
         batch = Batch(reqs=reqs, phase="decode", logits_out=self.logits[:rows])
@@ -253,7 +277,7 @@ class CandidateGroupRuntime:
         batch.attn_metadata = B200AttentionMetadata(
             phase="decode", positions=self.positions[:rows], out_loc=self.out_loc[:rows],
             row_table=self.row_table[:rows], seq_lens=self.seq_lens[:rows], prefix_len=self.prefix_len_view,
-            active=self.active[:rows], stable_history=True,
+            active=self.active[:rows], stable_history=self.history_mode, staged_prefix=stage,
         )
         return batch
 
@@ -273,14 +297,15 @@ class CandidateGroupRuntime:
         with self.llm.ctx.forward_batch(batch):
             self.llm.model.forward()
 
-    def _graph(self, rows: int, large: bool = False) -> torch.cuda.CUDAGraph:
+    def _graph(self, rows: int, large: bool = False, stage: int = STAGE_CLASSES[0]) -> torch.cuda.CUDAGraph:
         """The step graph for `rows` rows; `large` steps sort whole rows (sorted
-        candidate sets above SORT_K)."""
-        key = (rows, large)
+        candidate sets above SORT_K); `stage` is the prefix-length class the decode
+        attention stages before its wait."""
+        key = (rows, large, stage)
         graph = self._graphs.get(key)
         if graph is not None:
             return graph
-        batch = self._decode_batch(rows)
+        batch = self._decode_batch(rows, stage)
         # Eager warm-up with the group marked done: every kernel runs once (its
         # attributes get set) while all rows are inactive, so nothing is written.
         self._write_state(dict(done=1, rows=rows, max_steps=2, vocab=self.vocab, page_size=1, capacity=1,
@@ -342,7 +367,8 @@ class CandidateGroupRuntime:
         if large and self.vocab > LARGE_SORT_VOCAB:
             raise ValueError(f"a sorted candidate set of {sort_k} needs a vocabulary of at most {LARGE_SORT_VOCAB}")
         cm = self.llm.cache_manager
-        graph = self._graph(attempts, large)
+        stage = stage_class(prefix_len)
+        graph = self._graph(attempts, large, stage)
         head0 = cm.head
         width = max((len(s) for s in banned_sequences), default=0)
         self._write_state(dict(
@@ -388,7 +414,7 @@ class CandidateGroupRuntime:
                     break
             if step + 1 < max_new_tokens:
                 graph.replay()
-                _lib.count_launches(self._graph_launches[(attempts, large)])
+                _lib.count_launches(self._graph_launches[(attempts, large, stage)])
                 if self.record_logits:
                     torch.cuda.synchronize(self.device)
                     step_logits.append(self.logits[:attempts].float().cpu())

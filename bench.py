@@ -40,6 +40,7 @@ REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
 HBM_FALLBACK_GBS = 6650.0
+BF16_FALLBACK_TFLOPS = 1590.0
 
 
 def percentile(values, q):
@@ -349,6 +350,73 @@ def decode_linear_roofline(llm, peaks: dict) -> dict:
             "us_per_launch": round(ms * 1e3 / launches, 3)}
 
 
+PREFILL_GEMM_ROWS = (13, 32, 64, 128, 512, 2048)
+GEMV_MAX_ROWS = int(os.environ.get("AIOSB_GEMV_MAX_ROWS", "512"))  # the library's dispatch bound
+
+
+def prefill_gemm_sweep(llm, peaks: dict) -> dict:
+    """The linears of one S10 forward (14 x {qkv, o + residual add, gate_up +
+    SwiGLU, down + residual add}) at M token rows, M in {13, 128, 512, 2048}:
+    a keystroke prefix through a long prompt. Each pass reads all 176 MB of layer
+    weights (more than L2). Rows <= 16 run the register-operand MMA GEMV, more
+    rows the tcgen05 GEMM. Timed as a captured graph with CUDA events on the
+    launching stream; FLOPs = 2 x M x (weight elements). The kernel that ran is
+    named per M (the GEMV takes up to 512 rows, as 16-row groups above 16)."""
+    from aios_b200 import _lib
+    from aios_b200.kernel import ops
+
+    dev = llm.device
+    cfg = llm.config
+    layers = llm.model.model.layers.op_list
+    welems = sum(l.self_attn.qkv_proj.weight.numel() + l.self_attn.o_proj.weight.numel()
+                 + l.mlp.gate_up_proj.weight.numel() + l.mlp.down_proj.weight.numel() for l in layers)
+    peak = peaks.get("bf16_tflops", BF16_FALLBACK_TFLOPS)
+    out = {"peak_tflops": peak, "peak_source": "measured (burst)" if "bf16_tflops" in peaks else "fallback",
+           "weight_bytes": 2 * welems, "rows": {}}
+    stream = torch.cuda.current_stream(dev)
+    for m in PREFILL_GEMM_ROWS:
+        g = torch.Generator(device=dev).manual_seed(m)
+        x = (torch.randn(m, cfg.hidden_size, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        xo = (torch.randn(m, cfg.num_qo_heads * cfg.head_dim, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        xf = (torch.randn(m, cfg.intermediate_size, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+        res = torch.zeros(m, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+        qkv = torch.empty(m, layers[0].self_attn.qkv_proj.weight.shape[0], dtype=torch.bfloat16, device=dev)
+        act = torch.empty(m, cfg.intermediate_size, dtype=torch.bfloat16, device=dev)
+
+        def run():
+            for layer in layers:
+                a, mlp = layer.self_attn, layer.mlp
+                ops.linear(x, a.qkv_proj.weight, out=qkv)
+                ops.linear(xo, a.o_proj.weight, out=res, epilogue=_lib.EPI_ADD, residual=res)
+                ops.linear(x, mlp.gate_up_proj.packed_weight(), out=act, epilogue=_lib.EPI_SILU_MUL)
+                ops.linear(xf, mlp.down_proj.weight, out=res, epilogue=_lib.EPI_ADD, residual=res)
+
+        run()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            run()
+        for _ in range(2):
+            graph.replay()
+        iters = 10
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        start.record(stream)
+        for _ in range(iters):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+        ms = start.elapsed_time(end) / iters
+        tflops = 2.0 * m * welems / (ms * 1e-3) / 1e12
+        out["rows"][str(m)] = {"kernel": "gemv_mma_kernel" if m <= GEMV_MAX_ROWS else "gemm_tc_kernel",
+                               "us_per_forward": round(ms * 1e3, 2), "us_per_linear": round(ms * 1e3 / (4 * len(layers)), 2),
+                               "tflops": round(tflops, 1), "frac_of_bf16_peak": round(tflops / peak, 4),
+                               "weight_gbs": round(2 * welems / (ms * 1e-3) / 1e9, 1)}
+        del graph
+    ops.check_status(dev)
+    return out
+
+
 def decode_step_roofline(engine, llm, peaks: dict) -> dict:
     """Times the persistent decode-step kernel alone (CUDA events on the launching
     stream, a graph of back-to-back launches): one decode forward of the bench
@@ -598,6 +666,32 @@ def shape_keystroke(shape: str, dev, keystrokes: int = 20, warmup: int = 5) -> d
     return out
 
 
+HISTORY_PREFIXES = (13, 32, 128, 256, 448)
+
+
+def decode_history_crossover(engine, llm) -> dict:
+    """The S10 bench keystroke (8 candidates x 12 tokens) at prefixes of 13 to 448
+    tokens (the 512-position context), with each way the decode attention can
+    read the key history: per-row staging, prefix-once cluster staging, and the
+    cluster-cascade kernel. p50 over 8 keystrokes after 2 warm-up ones; the
+    runtime's default mode is restored afterwards."""
+    rt = engine._runtime
+    default = rt.history_mode
+    out = {}
+    for n in HISTORY_PREFIXES:
+        texts = prefixes(llm.tokenizer, llm.config.vocab_size, 10, seed=500 + n, length=n - 1)
+        row = {}
+        for mode in ("staged", "prefix_once", "cascade"):
+            rt.use_history_mode(mode)
+            lat = [r.latency_ms for r in _latencies(engine, texts, keystroke_config(), 2)]
+            row[mode] = round(statistics.median(lat), 3)
+        out[str(n)] = row
+    from aios_b200.runtime.group import HISTORY_MODES
+
+    rt.use_history_mode(next(k for k, v in HISTORY_MODES.items() if v == default))
+    return out
+
+
 def config_sweeps(engine, llm, dev) -> dict:
     """BASELINE configs 2, 3 and 4 through ``complete``.
     Config 2: the bench keystroke on S06 (and on S10L, S06's dims at 14 layers).
@@ -618,6 +712,7 @@ def config_sweeps(engine, llm, dev) -> dict:
         lat = [r.latency_ms for r in res]
         out["s10_prefix_sweep"][str(n)] = {"p50_ms": round(statistics.median(lat), 3),
                                            "p95_ms": round(percentile(lat, 0.95), 3)}
+    out["decode_history"] = decode_history_crossover(engine, llm)
     # the other shapes build their own LLM (each takes over the process-global
     # context), so they run after every keystroke of the S10 engine
     out["s06_keystroke"] = shape_keystroke("S06", dev)
@@ -689,6 +784,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     peaks = measured_peaks()
     roof = None if args.no_extras else decode_linear_roofline(llm, peaks)
     step_kernel = None if args.no_extras else decode_step_roofline(engine, llm, peaks)
+    prefill_gemm = None if args.no_extras else prefill_gemm_sweep(llm, peaks)
     mixer = None if args.no_extras else mixer_chain(dev)
     kstream = None if args.no_extras else keystroke_stream(engine, llm, seed=4321 + rank)
     sweeps = None if args.no_extras else config_sweeps(engine, llm, dev)
@@ -724,6 +820,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
         "gpu_launches": launches,
         "roofline": roof,
         "persistent_step": step_kernel,
+        "prefill_gemm": prefill_gemm,
         "clocks": clocks.summary(),
     }
     return line
@@ -769,6 +866,36 @@ def kernel_case(name: str) -> None:
         for text in prefixes(llm.tokenizer, llm.config.vocab_size, 2, seed=1234):
             engine.reset_prefix_cache()
             engine.complete(text, keystroke_config())
+    elif name.startswith("gemm_m"):
+        # one S10 layer's four linears at M token rows, eagerly, three times over
+        # the same weights (the 12.6 MB of one layer stay in L2 after the first)
+        from aios_b200 import _lib
+
+        m = int(name[len("gemm_m"):])
+        llm = LLM(config=shapes.S10, seed=0, page_size=16, num_pages=16, device="cuda:0")
+        cfg = llm.config
+        layer = llm.model.model.layers.op_list[0]
+        a, mlp = layer.self_attn, layer.mlp
+        x = (torch.randn(m, cfg.hidden_size, device=dev) * 0.5).to(torch.bfloat16)
+        xf = (torch.randn(m, cfg.intermediate_size, device=dev) * 0.5).to(torch.bfloat16)
+        res = torch.zeros(m, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            ops.linear(x, a.qkv_proj.weight)
+            ops.linear(x, a.o_proj.weight, out=res, epilogue=_lib.EPI_ADD, residual=res)
+            ops.linear(x, mlp.gate_up_proj.packed_weight(), epilogue=_lib.EPI_SILU_MUL)
+            ops.linear(xf, mlp.down_proj.weight, out=res, epilogue=_lib.EPI_ADD, residual=res)
+    elif name.startswith("prefill_attn_t"):
+        # S10 keystrokes whose prefix is T tokens ([BOS] + T - 1 characters): the
+        # prefix prefill runs the one-launch attention (T <= 64) or the two-kernel
+        # path (longer), 14 layers per keystroke
+        from aios_b200 import ImeCompletionEngine
+
+        t = int(name[len("prefill_attn_t"):])
+        llm = LLM(config=shapes.S10, seed=0, page_size=16, num_pages=256, device="cuda:0")
+        engine = ImeCompletionEngine(llm)
+        for text in prefixes(llm.tokenizer, llm.config.vocab_size, 2, seed=1234, length=t - 1):
+            engine.reset_prefix_cache()
+            engine.complete(text, keystroke_config())
     elif name == "mixer":
         g = torch.Generator(device=dev).manual_seed(0)
         bank = torch.randn(8, 32768, 768, generator=g, device=dev).to(torch.bfloat16)
@@ -793,7 +920,9 @@ def main() -> None:
     ap.add_argument("--cpu-sample", type=int, default=15, help="keystrokes timed for the CPU baseline (0: skip)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the roofline / mixer micro-benchmarks (profiling runs of the keystroke only)")
-    ap.add_argument("--kernel-case", choices=["linears", "mixer", "decode_step"],
+    ap.add_argument("--kernel-case",
+                    choices=["linears", "mixer", "decode_step"] + [f"gemm_m{m}" for m in PREFILL_GEMM_ROWS]
+                    + ["prefill_attn_t13", "prefill_attn_t32", "prefill_attn_t64", "prefill_attn_t256"],
                     help="run one small single-kernel workload for a full ncu capture, then exit")
     args = ap.parse_args()
     if args.kernel_case:

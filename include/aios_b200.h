@@ -151,11 +151,13 @@ AIOSB_API int aiosb_embedding_stat(const void* ids, int ids_is_int64, int64_t nu
  * as [gate 0..63 | up 0..63 | gate 64..127 | up 64..127 | ...]). For
  * AIOSB_EPI_ADD, residual is [rows, >= n] with row stride residual_stride and may
  * alias y (each element is read before it is written by the same thread).
- * Requires n % 128 == 0, k % 64 == 0, 16-byte aligned x/w/y. Decode widths
- * (rows <= 16, k % 256 == 0, k <= 2048) run on a register-operand MMA kernel that
- * requests its weights before waiting on the previous kernel; larger calls on tcgen05.
- * A decode-width AIOSB_EPI_ADD call lets the next kernel on the stream launch at
- * once; the other epilogues let it launch only after their own wait. */
+ * Requires n % 128 == 0, k % 64 == 0, 16-byte aligned x/w/y. Up to 512 rows
+ * (k % 256 == 0, k <= 2048; AIOSB_GEMV_MAX_ROWS changes the bound) run on a
+ * register-operand MMA kernel that requests its weights before waiting on the
+ * previous kernel (more than 16 rows as 16-row groups that share each weight tile
+ * through L2); larger calls on tcgen05. Such an AIOSB_EPI_ADD call lets the next
+ * kernel on the stream launch at once; the other epilogues let it launch only
+ * after their own wait. */
 AIOSB_API int aiosb_linear(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
                            int64_t y_row_stride, int epilogue, const void* residual, int64_t residual_stride,
                            int32_t* status, void* stream);
@@ -178,9 +180,10 @@ AIOSB_API int aiosb_linear_rmsnorm(const void* x, const void* res, void* res_out
  * aios/layers/norm.py:34-40, as used at aios/models/qwen3.py:106-120):
  * y = bf16(s), s = residual + bf16(x W^T) in fp32 (residual may alias y),
  * stat_x [rows, n] fp32 = s, and the sums of squares of s over column groups:
- * stat_ss[p * stat_ss_stride + row] for parts p < *stat_parts. A part is 128
- * columns, or 8 when rows <= 16 (the register-MMA decode path); stat_ss must hold
- * n / 8 parts. *stat_parts is written before any check. n <= 2048. */
+ * stat_ss[p * stat_ss_stride + row] for parts p < *stat_parts. A part is 8
+ * columns when the call runs on the register-operand MMA kernel (see
+ * aiosb_linear), else 128; stat_ss must hold n / 8 parts. *stat_parts is written
+ * before any check. n <= 2048. */
 AIOSB_API int aiosb_linear_add_stat(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
                                     int64_t y_row_stride, const void* residual, int64_t residual_stride,
                                     float* stat_x, float* stat_ss, int64_t stat_ss_stride, int64_t* stat_parts,
@@ -223,15 +226,26 @@ AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, 
  * CandidateGroup runtime: prefix from the prefill, older suffix keys from earlier
  * steps, row metadata from this step's group step, the qkv linear just before). The kernel then copies the keys each row uses into shared memory
  * before waiting on the previous kernel, and after the wait only this step's
- * projection row stays on its critical path. */
+ * projection row stays on its critical path. stable_history selects how:
+ * AIOSB_HISTORY_STAGED (1), every row's CTA reads the prefix itself;
+ * AIOSB_HISTORY_PREFIX_ONCE (2), the rows of a KV head (up to 8 per cluster)
+ * split the prefix, each reads its slice once and copies it to the others over
+ * distributed shared memory. Both give identical results; k_cache and v_cache
+ * must be 16-byte aligned. staged_prefix bounds the prefix keys staged before
+ * the wait (rounded up to 64; 0 = 128; at most 512 / 448 / 256 keys for head_dim
+ * 64 / 96 / 128): shared memory is sized by it, and longer prefixes are read
+ * after the wait. */
+#define AIOSB_HISTORY_STAGED 1
+#define AIOSB_HISTORY_PREFIX_ONCE 2
 AIOSB_API int aiosb_attention_decode(const void* qkv, int64_t qkv_stride, const void* q, int64_t q_stride,
                            const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_tab,
                            const void* sin_tab, int64_t max_pos, const int32_t* positions, const int32_t* out_loc,
                            void* k_cache, void* v_cache, int64_t num_slots, const int32_t* page_table,
                            int64_t table_stride, const int32_t* row_table, const int32_t* seq_lens,
                            const int32_t* prefix_len, const int32_t* active, int stable_history,
-                           int64_t rows, int64_t num_qo_heads, int64_t num_kv_heads, int64_t head_dim, float scale, void* out, int64_t out_stride,
-                           int32_t* status, void* stream);
+                           int64_t staged_prefix, int64_t rows, int64_t num_qo_heads, int64_t num_kv_heads,
+                           int64_t head_dim, float scale, void* out, int64_t out_stride, int32_t* status,
+                           void* stream);
 
 /* Prefill prologue: replaces the q/k RMSNorm (aios/models/qwen3.py:66-67),
  * apply_rotary_pos_emb (aios/layers/attention.py:11-16) and store_kv

@@ -52,11 +52,11 @@ def test_persistent_step_matches_per_kernel_forward(shape) -> None:
     greedy = ImeGenerationConfig(sampling_attempts=8, max_sampling_attempts=8, refill_batch_size=8,
                                  max_new_tokens=12, temperature=1.0, top_k=1, top_p=1.0, min_new_tokens=0, seed=1)
     persistent, res_p = _greedy_steps(engine, text, greedy)
-    launches = rt._graph_launches[(8, False)]
+    launches = rt._graph_launches[(8, False, 128)]
     rt.use_persistent_step(False)  # the per-kernel forward, same weights and buffers
     per_kernel, res_k = _greedy_steps(engine, text, greedy)
     assert launches == 2, "one group step + one persistent forward per decode step"
-    assert rt._graph_launches[(8, False)] > 2 * cfg.num_layers
+    assert rt._graph_launches[(8, False, 128)] > 2 * cfg.num_layers
     steps = min(len(persistent), len(per_kernel))
     assert steps >= 2
     worst = 0.0

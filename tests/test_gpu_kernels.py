@@ -28,7 +28,7 @@ def _bf16_close(actual: torch.Tensor, expected: torch.Tensor, ulps: float = 2.0,
     assert not bool(bad.any()), f"{int(bad.sum())} mismatches; max abs diff {float((a - e).abs().max())}"
 
 
-@pytest.mark.parametrize("rows", [1, 8, 13, 33, 100, 300])
+@pytest.mark.parametrize("rows", [1, 8, 13, 33, 100, 300, 700, 2048])
 @pytest.mark.parametrize("n,k", [(1280, 768), (768, 768), (768, 2048), (1152, 768), (16384, 768)])
 def test_linear_tcgen05_matches_fp32(cuda_device, rows: int, n: int, k: int) -> None:
     g = torch.Generator().manual_seed(rows * 7 + n + k)
@@ -42,7 +42,7 @@ def test_linear_tcgen05_matches_fp32(cuda_device, rows: int, n: int, k: int) -> 
     _bf16_close(y, ref, ulps=1.0, atol=1e-4 * math.sqrt(k))
 
 
-@pytest.mark.parametrize("rows", [1, 8, 33])
+@pytest.mark.parametrize("rows", [1, 8, 33, 300, 2048])
 def test_linear_silu_mul_epilogue(cuda_device, rows: int) -> None:
     g = torch.Generator().manual_seed(5 + rows)
     f, k = 2048, 768
@@ -54,6 +54,27 @@ def test_linear_silu_mul_epilogue(cuda_device, rows: int) -> None:
     torch.cuda.synchronize()
     assert y.shape == (rows, f)
     _bf16_close(y, ref, ulps=2.0, atol=1e-4)
+
+
+@pytest.mark.parametrize("rows", [8, 100, 2048])
+@pytest.mark.parametrize("n,k", [(768, 768), (768, 2048)])
+def test_linear_add_epilogue(cuda_device, rows: int, n: int, k: int) -> None:
+    """y = residual + bf16(x W^T) (the o / down projections' residual add), with
+    split-K reductions over clusters at every size."""
+    g = torch.Generator().manual_seed(rows + n + k)
+    x = torch.randn(rows, k, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16)
+    res = torch.randn(rows, n, generator=g).to(torch.bfloat16)
+    delta = (x.float() @ w.float().T).to(torch.bfloat16)
+    ref = res.float() + delta.float()
+    rd = res.to(cuda_device)
+    y = ops.linear(x.to(cuda_device), w.to(cuda_device), out=rd, epilogue=_lib.EPI_ADD, residual=rd)
+    torch.cuda.synchronize()
+    ops.check_status(cuda_device)
+    # the delta may differ from the fp32 reference's rounding by 1 ulp of itself
+    spacing = torch.clamp(delta.float().abs(), min=2.0**-126) * 2.0**-7
+    diff = (y.float().cpu() - ref).abs()
+    assert bool((diff <= spacing + ref.abs() * 2.0**-8 + 1e-4 * math.sqrt(k)).all())
 
 
 def test_rmsnorm_variants(cuda_device) -> None:
@@ -185,31 +206,41 @@ def _rope_tables(d: int, max_pos: int, device):
     return cos, sin, cos.to(torch.bfloat16).to(device), sin.to(torch.bfloat16).to(device)
 
 
+STAGED, PREFIX_ONCE = _lib.HISTORY_STAGED, _lib.HISTORY_PREFIX_ONCE
 DECODE_CASES = [
-    # prefix, suffix (incl. the new token), page_size, stable_history, inactive rows
-    (13, 5, 1, False, False),
-    (13, 5, 16, False, False),
-    (13, 5, 1, True, False),
-    (13, 5, 16, True, False),
-    (13, 1, 1, True, False),     # first decode step: no older suffix keys
-    (150, 40, 1, True, True),    # history beyond the staged prefix / suffix capacity
-    (0, 9, 1, True, False),      # no shared prefix
-    (150, 40, 1, False, True),
+    # prefix, suffix (incl. the new token), page_size, history mode (0 = cascade
+    # kernel, 1 = staged, 2 = prefix-once cluster staging), inactive rows, rows
+    (13, 5, 1, 0, False, 8),
+    (13, 5, 16, 0, False, 8),
+    (13, 5, 1, STAGED, False, 8),
+    (13, 5, 16, STAGED, False, 8),
+    (13, 1, 1, STAGED, False, 8),    # first decode step: no older suffix keys
+    (150, 40, 1, STAGED, True, 8),   # older suffix beyond the staged capacity
+    (0, 9, 1, STAGED, False, 8),     # no shared prefix
+    (150, 40, 1, 0, True, 8),
+    (13, 5, 16, PREFIX_ONCE, False, 8),
+    (13, 1, 1, PREFIX_ONCE, True, 8),
+    (150, 40, 1, PREFIX_ONCE, True, 8),
+    (0, 9, 1, PREFIX_ONCE, False, 8),
+    (5, 3, 1, PREFIX_ONCE, False, 3),    # a 3-row cluster, slices of 1-2 prefix keys
+    (37, 4, 16, PREFIX_ONCE, True, 13),  # clusters of 8 rows: 16 grid rows, 3 of them padding
+    (440, 12, 16, STAGED, False, 8),     # a long prefix, staged whole (head_dim 64 and 96)
+    (440, 12, 16, PREFIX_ONCE, False, 8),
+    (500, 8, 1, PREFIX_ONCE, True, 8),   # beyond the head_dim-96 capacity: the rest streamed
 ]
 
 
-@pytest.mark.parametrize("hq,hkv,d", [(12, 4, 64), (8, 2, 96)])
-@pytest.mark.parametrize("prefix,suffix,page_size,stable,inactive", DECODE_CASES)
-def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int, d: int, prefix: int, suffix: int,
-                                                 page_size: int, stable: bool, inactive: bool) -> None:
-    """8 candidate rows sharing a prefix, `suffix` own keys each (the newest one
-    normalised, rotated and stored by the kernel itself); both kernel paths."""
-    g = torch.Generator().manual_seed(hq * d + page_size + prefix + suffix)
-    rows = 8
+def _decode_case(hq, hkv, d, prefix, suffix, page_size, inactive, rows, device):
+    """Inputs of one decode-attention case and the oracle's output: `rows`
+    candidate rows sharing a prefix, `suffix` own keys each (the newest one
+    normalised, rotated and stored by the kernel)."""
+    g = torch.Generator().manual_seed(hq * d + page_size + prefix + suffix + rows)
     num_pages = 64 if page_size == 16 else 1024
+    if page_size == 16:
+        num_pages = max(num_pages, (prefix + 15) // 16 + rows + 1)
     num_slots = num_pages * page_size
-    width = 256
-    cos, sin, cos_b, sin_b = _rope_tables(d, 512, cuda_device)
+    width = 512 if prefix + suffix > 256 else 256
+    cos, sin, cos_b, sin_b = _rope_tables(d, 512, device)
     eps, scale = 1e-6, d**-0.5
     kc = torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16)
     vc = torch.randn(num_slots, hkv, d, generator=g).to(torch.bfloat16)
@@ -219,10 +250,11 @@ def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int,
         prefix_slots = perm[:prefix]
         suffix_slots = [perm[prefix + r * suffix : prefix + (r + 1) * suffix] for r in range(rows)]
     else:
-        # prefix on pages[0] (13 of 16 tokens used), each row's suffix on its own page
+        # the prefix on its own pages (the last one partly used), each row's suffix on its own page
         pages = torch.randperm(num_pages, generator=g)
-        prefix_slots = pages[0] * page_size + torch.arange(prefix)
-        suffix_slots = [pages[1 + r] * page_size + torch.arange(suffix) for r in range(rows)]
+        npp = (prefix + 15) // 16
+        prefix_slots = (pages[:npp, None] * page_size + torch.arange(16)).flatten()[:prefix]
+        suffix_slots = [pages[npp + r] * page_size + torch.arange(suffix) for r in range(rows)]
     for r in range(rows):
         table[r, :prefix] = prefix_slots.to(torch.int32)
         table[r, prefix : prefix + suffix] = suffix_slots[r].to(torch.int32)
@@ -233,7 +265,7 @@ def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int,
     out_loc = table[:, pos].clone()
     active = torch.ones(rows, dtype=torch.int32)
     if inactive:
-        active[[1, 6]] = 0
+        active[[1, rows - 2]] = 0
     # oracle: norm + rope + store + attention
     q = qkv[:, : hq * d].view(rows, hq, d)
     k = qkv[:, hq * d : (hq + hkv) * d].view(rows, hkv, d)
@@ -249,19 +281,34 @@ def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int,
                        torch.tensor([pos]), scale)[0] if on[r] else torch.zeros(hq, d)
         for r in range(rows)
     ])
-    dev = cuda_device
-    kcd, vcd = kc.to(dev), vc.to(dev)
-    out = torch.empty(rows, hq * d, dtype=torch.bfloat16, device=dev)
-    ops.attention_decode(
-        out=out, k_cache=kcd, v_cache=vcd, page_table=table.to(dev),
-        row_table=torch.arange(rows, dtype=torch.int32, device=dev),
+    dev = device
+    args = dict(
+        page_table=table.to(dev), row_table=torch.arange(rows, dtype=torch.int32, device=dev),
         seq_lens=torch.full((rows,), pos + 1, dtype=torch.int32, device=dev),
         positions=torch.full((rows,), pos, dtype=torch.int32, device=dev),
         num_qo_heads=hq, num_kv_heads=hkv, head_dim=d, scale=scale,
         qkv=qkv.to(dev), q_norm_w=qn.to(dev), k_norm_w=kn.to(dev), eps=eps, cos=cos_b, sin=sin_b,
         out_loc=out_loc.to(dev), prefix_len=torch.tensor([prefix], dtype=torch.int32, device=dev),
-        active=active.to(dev), stable_history=stable,
+        active=active.to(dev),
     )
+    return kc, vc, kc_ref, vc_ref, expected, args
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(12, 4, 64), (8, 2, 96)])
+@pytest.mark.parametrize("prefix,suffix,page_size,stable,inactive,rows", DECODE_CASES)
+def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int, d: int, prefix: int, suffix: int,
+                                                 page_size: int, stable: int, inactive: bool, rows: int) -> None:
+    """Candidate rows sharing a prefix, `suffix` own keys each (the newest one
+    normalised, rotated and stored by the kernel itself); every kernel path."""
+    kc, vc, kc_ref, vc_ref, expected, args = _decode_case(hq, hkv, d, prefix, suffix, page_size, inactive, rows,
+                                                          cuda_device)
+    dev = cuda_device
+    kcd, vcd = kc.to(dev), vc.to(dev)
+    out = torch.empty(rows, hq * d, dtype=torch.bfloat16, device=dev)
+    # long prefixes staged whole (up to the head_dim's capacity); 150 keys with the
+    # default 128-key staging, the rest read after the wait
+    staged = prefix if prefix >= 256 else 0
+    ops.attention_decode(out=out, k_cache=kcd, v_cache=vcd, stable_history=stable, staged_prefix=staged, **args)
     torch.cuda.synchronize()
     ops.check_status(dev)
     # the stored K must be the bf16 rope of the bf16 norm, bit for bit (active rows
@@ -271,8 +318,26 @@ def test_cascade_decode_attention_fused_prologue(cuda_device, hq: int, hkv: int,
     _bf16_close(out.view(rows, hq, d), expected, ulps=2.0, atol=2e-3)
 
 
-@pytest.mark.parametrize("stable", [False, True])
-def test_decode_attention_reports_out_of_pool_slot(cuda_device, stable: bool) -> None:
+@pytest.mark.parametrize("prefix,rows", [(13, 8), (77, 5), (440, 8), (300, 16)])
+def test_prefix_once_staging_matches_per_row_staging(cuda_device, prefix: int, rows: int) -> None:
+    """The prefix-once cluster staging and the per-row staging fold the same keys
+    in the same order: outputs and stored K/V bit for bit."""
+    hq, hkv, d = 12, 4, 64
+    kc, vc, _, _, _, args = _decode_case(hq, hkv, d, prefix, 6, 16, True, rows, cuda_device)
+    outs = []
+    for mode in (STAGED, PREFIX_ONCE):
+        kcd, vcd = kc.to(cuda_device), vc.to(cuda_device)
+        out = torch.empty(rows, hq * d, dtype=torch.bfloat16, device=cuda_device)
+        ops.attention_decode(out=out, k_cache=kcd, v_cache=vcd, stable_history=mode, staged_prefix=prefix, **args)
+        torch.cuda.synchronize()
+        ops.check_status(cuda_device)
+        outs.append((out.cpu(), kcd.cpu(), vcd.cpu()))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("stable", [0, 1, 2])
+def test_decode_attention_reports_out_of_pool_slot(cuda_device, stable: int) -> None:
     """A page-table entry outside the KV pool is read as slot 0 (the kernel never
     indexes past the pool) and reported through the status word."""
     g = torch.Generator().manual_seed(11)
@@ -609,7 +674,7 @@ def test_linear_with_fused_rmsnorm(cuda_device, rows: int, with_res: bool, epi: 
         assert torch.equal(res_out.cpu(), new_res)
 
 
-@pytest.mark.parametrize("rows", [1, 8, 13, 64, 100, 300])
+@pytest.mark.parametrize("rows", [1, 8, 13, 64, 100, 300, 700])
 @pytest.mark.parametrize("epi", ["store", "silu"])
 def test_residual_statistics_chain(cuda_device, rows: int, epi: str) -> None:
     """o_proj with the add+statistics epilogue, then a GEMM that normalises its
@@ -640,8 +705,9 @@ def test_residual_statistics_chain(cuda_device, rows: int, epi: str) -> None:
     # the residual update is bit-exact (same GEMM, same rounding points)
     assert torch.equal(res_dev.cpu(), new_res)
     assert torch.equal(stats.x.cpu(), s_ref)
-    # parts: 128-column tiles (tcgen05) or 8-column groups (decode widths)
-    assert stats.parts == (d // 8 if rows <= 16 else d // 128)
+    # parts: 8-column groups (the register-operand path, up to 512 rows) or
+    # 128-column tiles (tcgen05)
+    assert stats.parts == (d // 8 if rows <= 512 else d // 128)
     part = (s_ref * s_ref).view(rows, stats.parts, d // stats.parts).sum(-1).T
     torch.testing.assert_close(stats.ss.cpu(), part, rtol=1e-5, atol=1e-5)
     _bf16_close(y, ref, ulps=2.0, atol=2e-3)
