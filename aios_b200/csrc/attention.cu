@@ -609,6 +609,203 @@ __global__ void __launch_bounds__(kAttnThreads) qk_norm_rope_store_kernel(const 
 // [0, cached_len + last query + 1) of the request's slot list are staged once
 // per chunk and scored against all tile tokens x GQA heads with the causal mask
 // key_pos <= cached_len + token index (aios/attention/flashinfer.py:33-91).
+// ---- tensor-core prefill fold ------------------------------------------------
+// Query rows of a prefill tile against a 64-key chunk on mma.sync m16n8k16 (bf16
+// in, fp32 accumulate), FlashAttention-2 style: one warp owns 16 query rows,
+// S = Q K^T for the chunk (8 key tiles of 8), masked (causal, chunk end) and
+// scaled, an online softmax per row (the 4 lanes of a row reduce with shuffles),
+// then O += P V with P as the A operand straight from the S accumulators. P is
+// split into bf16 hi + lo halves (two MMAs) so that the PV product keeps about
+// fp32 accuracy, where a single bf16 P would round every probability. Q, K and V
+// are bf16 values already (q after its bf16 RoPE), so QK^T is exact up to fp32
+// accumulation.
+// Chunk rows in shared memory have a stride of D + 8 elements: the B-fragment
+// word loads of K and the ldmatrix row reads of V are then bank-conflict free.
+template <int D>
+struct TcStride {
+  static constexpr int kRow = D + 8;
+};
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Two 8x8 bf16 matrices, transposed: rows from lanes 0-7 (matrix 0) and 8-15
+// (matrix 1), 16 bytes each.
+__device__ __forceinline__ void ldsm_x2_trans(uint32_t& b0, uint32_t& b1, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(b0), "=r"(b1) : "r"(addr));
+}
+
+// 16 query rows of one warp: Q A-fragments, O accumulators, and the running max
+// and sum of rows lane / 4 and lane / 4 + 8.
+template <int D>
+struct TcRows {
+  uint32_t qa[D / 16][4];
+  float o[D / 8][4];
+  float m[2], l[2];
+  int qpos[2];  // absolute position of each row's query (-1: no query)
+};
+
+// q_s: [Q][D] fp32 query rows (bf16 values); rows row0 .. row0 + 15 of them.
+template <int D, class PosFn>
+__device__ __forceinline__ void tc_rows_init(TcRows<D>& t, const float* q_s, int row0, int Q, int lane,
+                                             PosFn qpos_of) {
+  const int g4 = lane >> 2, t4 = lane & 3;
+  const int r[2] = {row0 + g4, row0 + g4 + 8};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    t.m[h] = -INFINITY;
+    t.l[h] = 0.f;
+    t.qpos[h] = r[h] < Q ? qpos_of(r[h]) : -1;
+  }
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int c0 = 16 * kk + 2 * t4, c1 = c0 + 8;
+    t.qa[kk][0] = r[0] < Q ? pack_bf16x2(q_s[r[0] * D + c0], q_s[r[0] * D + c0 + 1]) : 0u;
+    t.qa[kk][1] = r[1] < Q ? pack_bf16x2(q_s[r[1] * D + c0], q_s[r[1] * D + c0 + 1]) : 0u;
+    t.qa[kk][2] = r[0] < Q ? pack_bf16x2(q_s[r[0] * D + c1], q_s[r[0] * D + c1 + 1]) : 0u;
+    t.qa[kk][3] = r[1] < Q ? pack_bf16x2(q_s[r[1] * D + c1], q_s[r[1] * D + c1 + 1]) : 0u;
+  }
+#pragma unroll
+  for (int jn = 0; jn < D / 8; ++jn) t.o[jn][0] = t.o[jn][1] = t.o[jn][2] = t.o[jn][3] = 0.f;
+}
+
+// Folds keys k0 .. k0 + nk - 1 (chunk rows 0 .. nk - 1 of Ks / Vs; the V rows
+// nk .. 63 must hold finite values) into the warp's 16 rows.
+template <int D>
+__device__ __forceinline__ void tc_fold_chunk(TcRows<D>& t, const __nv_bfloat16* Ks, const __nv_bfloat16* Vs, int k0,
+                                              int nk, float scale, int lane) {
+  constexpr int R = TcStride<D>::kRow;
+  const int g4 = lane >> 2, t4 = lane & 3;
+  float s[8][4];
+  const uint32_t* K32 = reinterpret_cast<const uint32_t*>(Ks);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    if (8 * j < nk) {
+      const uint32_t* krow = K32 + (8 * j + g4) * (R / 2);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) mma_16816(s[j], t.qa[kk], krow[8 * kk + t4], krow[8 * kk + 4 + t4]);
+    }
+  }
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int key = 8 * j + 2 * t4 + (e & 1), h = e >> 1;
+      const bool ok = key < nk && k0 + key <= t.qpos[h];
+      s[j][e] = ok ? s[j][e] * scale : -INFINITY;
+      mx[h] = fmaxf(mx[h], s[j][e]);
+    }
+  }
+  float ref[2], corr[2], sum[2] = {0.f, 0.f};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    const float m_new = fmaxf(t.m[h], mx[h]);
+    ref[h] = m_new == -INFINITY ? 0.f : m_new;  // a row with no key yet keeps p = 0
+    corr[h] = expf(t.m[h] - ref[h]);
+    t.m[h] = m_new;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      s[j][e] = expf(s[j][e] - ref[e >> 1]);
+      sum[e >> 1] += s[j][e];
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 1);
+    sum[h] += __shfl_xor_sync(0xffffffffu, sum[h], 2);
+    t.l[h] = t.l[h] * corr[h] + sum[h];
+  }
+#pragma unroll
+  for (int jn = 0; jn < D / 8; ++jn) {
+    t.o[jn][0] *= corr[0];
+    t.o[jn][1] *= corr[0];
+    t.o[jn][2] *= corr[1];
+    t.o[jn][3] *= corr[1];
+  }
+  const uint32_t vbase = smem_u32(Vs) + (uint32_t)((lane & 15) * R * 2);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    if (16 * kk < nk) {
+      uint32_t hi[4], lo[4];
+      const float pv[4][2] = {{s[2 * kk][0], s[2 * kk][1]}, {s[2 * kk][2], s[2 * kk][3]},
+                              {s[2 * kk + 1][0], s[2 * kk + 1][1]}, {s[2 * kk + 1][2], s[2 * kk + 1][3]}};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        hi[q] = pack_bf16x2(pv[q][0], pv[q][1]);
+        lo[q] = pack_bf16x2(pv[q][0] - bf16_lo(hi[q]), pv[q][1] - bf16_hi(hi[q]));
+      }
+#pragma unroll
+      for (int jn = 0; jn < D / 8; ++jn) {
+        uint32_t b0, b1;
+        ldsm_x2_trans(b0, b1, vbase + (uint32_t)((16 * kk * R + 8 * jn) * 2));
+        mma_16816(t.o[jn], hi, b0, b1);
+        mma_16816(t.o[jn], lo, b0, b1);
+      }
+    }
+  }
+}
+
+// Writes the warp's rows: out_of(row) gives the row's output vector (or nullptr).
+template <int D, class OutFn>
+__device__ __forceinline__ void tc_rows_store(const TcRows<D>& t, int row0, int Q, int lane, OutFn out_of) {
+  const int g4 = lane >> 2, t4 = lane & 3;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = row0 + g4 + 8 * h;
+    if (r >= Q) continue;
+    __nv_bfloat16* dst = out_of(r);
+    const float inv = t.l[h] > 0.f ? 1.0f / t.l[h] : 0.f;
+#pragma unroll
+    for (int jn = 0; jn < D / 8; ++jn)
+      *reinterpret_cast<uint32_t*>(dst + 8 * jn + 2 * t4) =
+          pack_bf16x2(t.o[jn][2 * h] * inv, t.o[jn][2 * h + 1] * inv);
+  }
+}
+
+// Stages chunk keys [k0, k0 + nc) from the paged cache and, after them, the new
+// keys src_k / src_v rows [k0 + nc - cached, ...) up to nk rows (prefill-fused:
+// keys of this request not yet in the cache), with the tensor-core row stride;
+// V rows nk .. 63 are zeroed (their probabilities are 0; they must be finite).
+template <int D>
+__device__ __forceinline__ void tc_stage_chunk(const __nv_bfloat16* __restrict__ k_cache,
+                                               const __nv_bfloat16* __restrict__ v_cache, int64_t tok_stride, int h,
+                                               const int32_t* __restrict__ slots, int k0, int nc, int nk,
+                                               const __nv_bfloat16* src_k, const __nv_bfloat16* src_v, int src0,
+                                               int64_t num_slots, __nv_bfloat16* Ks, __nv_bfloat16* Vs,
+                                               int32_t* status) {
+  constexpr int R = TcStride<D>::kRow, kVec = D / 8;
+  for (int idx = threadIdx.x; idx < kKeyChunk * kVec; idx += blockDim.x) {
+    const int j = idx / kVec, c = idx % kVec;
+    uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+    if (j < nc) {
+      int64_t slot = slots[k0 + j];
+      if (slot < 0 || slot >= num_slots) {
+        if (c == 0) report(status, AIOSB_DEV_SLOT_RANGE);
+        slot = 0;
+      }
+      kv = reinterpret_cast<const uint4*>(k_cache + slot * tok_stride + (int64_t)h * D)[c];
+      vv = reinterpret_cast<const uint4*>(v_cache + slot * tok_stride + (int64_t)h * D)[c];
+    } else if (j < nk) {
+      kv = reinterpret_cast<const uint4*>(src_k + (int64_t)(src0 + j - nc) * D)[c];
+      vv = reinterpret_cast<const uint4*>(src_v + (int64_t)(src0 + j - nc) * D)[c];
+    }
+    reinterpret_cast<uint4*>(Ks + j * R)[c] = kv;
+    reinterpret_cast<uint4*>(Vs + j * R)[c] = vv;
+  }
+}
+
 struct PrefillArgs {
   const __nv_bfloat16* q;
   int64_t q_stride;
@@ -633,15 +830,14 @@ struct PrefillArgs {
 
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const PrefillArgs a) {
-  constexpr int DPL = D / 32;
   extern __shared__ uint8_t smem_raw[];
   const int h = blockIdx.x;
   const int tile = blockIdx.y;
   const int g = a.hq / a.hkv;
   float* q_s = reinterpret_cast<float*>(smem_raw);
   const int Qmax = a.tile_tokens * g;
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(q_s + Qmax * D);
-  __nv_bfloat16* Vs = Ks + kKeyChunk * (D + 2);
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(q_s + Qmax * D);  // [kKeyChunk][D + 8]
+  __nv_bfloat16* Vs = Ks + kKeyChunk * TcStride<D>::kRow;                // [kKeyChunk][D + 8]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tok_stride = (int64_t)a.hkv * D;
 
@@ -659,43 +855,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_kernel(const Prefil
     const int t = qi / g, j = qi % g;
     q_s[idx] = bf16_to_f(a.q[(qbase + q0 + t) * a.q_stride + (int64_t)(h * g + j) * D + e]);
   }
-  QState<D> st[kMaxQPerWarp];
-#pragma unroll
-  for (int s = 0; s < kMaxQPerWarp; ++s) qstate_init<D>(st[s]);
   __syncthreads();
+  // query row qi = token (q0 + qi / g), head h * g + qi % g; warp w owns rows 16w..
+  const int row0 = warp * 16;
+  const bool folds = row0 < Q;
+  TcRows<D> tr;
+  tc_rows_init<D>(tr, q_s, row0, Q, lane, [&](int qi) { return cached + q0 + qi / g; });
 
   const int kv_end = cached + q0 + nq;
   for (int k0 = 0; k0 < kv_end; k0 += kKeyChunk) {
     const int nk = min(kKeyChunk, kv_end - k0);
-    stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, slots, k0, nk, a.num_slots, Ks, Vs, a.status);
+    tc_stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, slots, k0, nk, nk, nullptr, nullptr, 0, a.num_slots, Ks,
+                      Vs, a.status);
     __syncthreads();
-#pragma unroll
-    for (int s = 0; s < kMaxQPerWarp; ++s) {
-      const int qi = warp + s * kAttnWarps;
-      if (qi < Q) {
-        const int qpos = cached + q0 + qi / g;  // absolute position of this query
-        const float* qv = q_s + qi * D;
-        const __nv_bfloat162* K2 = reinterpret_cast<const __nv_bfloat162*>(Ks);
-        const int kp0 = k0 + lane, kp1 = k0 + lane + 32;
-        const float s0 = (lane < nk && kp0 <= qpos) ? dot_q_k<D>(qv, K2 + lane * (D / 2 + 1)) * a.scale : -INFINITY;
-        const float s1 =
-            (lane + 32 < nk && kp1 <= qpos) ? dot_q_k<D>(qv, K2 + (lane + 32) * (D / 2 + 1)) * a.scale : -INFINITY;
-        fold_scores<D>(st[s], s0, s1, nk, [&](int j, int i) { return bf16_to_f(Vs[j * D + i * 32 + lane]); });
-      }
-    }
+    if (folds) tc_fold_chunk<D>(tr, Ks, Vs, k0, nk, a.scale, lane);
     __syncthreads();
   }
-#pragma unroll
-  for (int s = 0; s < kMaxQPerWarp; ++s) {
-    const int qi = warp + s * kAttnWarps;
-    if (qi < Q) {
-      const int t = qi / g, j = qi % g;
-      const float inv = st[s].l > 0.f ? 1.0f / st[s].l : 0.f;
-      __nv_bfloat16* dst = a.out + (qbase + q0 + t) * a.out_stride + (int64_t)(h * g + j) * D;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st[s].acc[i] * inv);
-    }
-  }
+  if (folds)
+    tc_rows_store<D>(tr, row0, Q, lane, [&](int qi) {
+      return a.out + (qbase + q0 + qi / g) * a.out_stride + (int64_t)(h * g + qi % g) * D;
+    });
 }
 
 template <int D>
@@ -765,7 +944,7 @@ cudaError_t launch_decode_hist(const DecodeArgs& a, int rows, int hkv, int group
 
 template <int D>
 size_t prefill_smem(int queries) {
-  return (size_t)queries * D * 4 + (size_t)kKeyChunk * (D + 2) * 2 + (size_t)kKeyChunk * D * 2;
+  return (size_t)queries * D * 4 + (size_t)kKeyChunk * TcStride<D>::kRow * 2 * 2;
 }
 
 template <typename K>
@@ -1015,7 +1194,7 @@ struct FusedPrefillArgs {
 template <int D>
 size_t fused_prefill_smem(int queries) {
   // q_s | Ks | Vs | NK | NV | warp scratch | raw rows (queries + new keys) | cos | sin | norm weights | positions
-  return (size_t)queries * D * 4 + (size_t)kKeyChunk * (D + 2) * 2 + (size_t)kKeyChunk * D * 2 * 3 +
+  return (size_t)queries * D * 4 + (size_t)kKeyChunk * TcStride<D>::kRow * 2 * 2 + (size_t)kKeyChunk * D * 2 * 2 +
          (size_t)kAttnWarps * D * 4 + (size_t)(queries + kKeyChunk) * D * 2 + (size_t)kKeyChunk * D * 2 * 2 +
          (size_t)D * 2 * 2 + (size_t)kKeyChunk * 4;
 }
@@ -1029,9 +1208,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_fused_kernel(const 
   const int g = a.hq / a.hkv;
   const int Qmax = a.tile_tokens * g;
   float* q_s = reinterpret_cast<float*>(smem_raw);                                // [Qmax][D]
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(q_s + Qmax * D);            // [kKeyChunk][D + 2]
-  __nv_bfloat16* Vs = Ks + kKeyChunk * (D + 2);                                     // [kKeyChunk][D]
-  __nv_bfloat16* NK = Vs + kKeyChunk * D;                                           // new keys, rotated
+  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(q_s + Qmax * D);            // [kKeyChunk][D + 8]
+  __nv_bfloat16* Vs = Ks + kKeyChunk * TcStride<D>::kRow;                           // [kKeyChunk][D + 8]
+  __nv_bfloat16* NK = Vs + kKeyChunk * TcStride<D>::kRow;                           // new keys, rotated
   __nv_bfloat16* NV = NK + kKeyChunk * D;                                           // new values
   float* tmp = reinterpret_cast<float*>(NV + kKeyChunk * D);                        // [warps][D]
   __nv_bfloat16* RAW = reinterpret_cast<__nv_bfloat16*>(tmp + kAttnWarps * D);      // [Qmax + kKeyChunk][D]
@@ -1127,51 +1306,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_fused_kernel(const 
       }
     }
   }
-  QState<D> st[kMaxQPerWarp];
-#pragma unroll
-  for (int s = 0; s < kMaxQPerWarp; ++s) qstate_init<D>(st[s]);
   __syncthreads();
+  // query row qi = token (q0 + qi / g), head h * g + qi % g; warp w owns rows 16w..
+  const int row0 = warp * 16;
+  const bool folds = row0 < Q;
+  TcRows<D> tr;
+  tc_rows_init<D>(tr, q_s, row0, Q, lane, [&](int qi) { return cached + q0 + qi / g; });
 
   const int kv_end = cached + nnew;
   for (int k0 = 0; k0 < kv_end; k0 += kKeyChunk) {
     const int nk = min(kKeyChunk, kv_end - k0);
-    const int nc = max(0, min(nk, cached - k0));  // keys of this chunk in the cache
-    if (nc > 0) stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, slots, k0, nc, a.num_slots, Ks, Vs, a.status);
-    constexpr int kWords = D / 2;
-    for (int idx = threadIdx.x; idx < (nk - nc) * kWords; idx += blockDim.x) {
-      const int jj = idx / kWords, w = idx % kWords;
-      const int src = k0 + nc + jj - cached;  // new-key row
-      reinterpret_cast<uint32_t*>(Ks)[(nc + jj) * (kWords + 1) + w] = reinterpret_cast<const uint32_t*>(NK + src * D)[w];
-      reinterpret_cast<uint32_t*>(Vs)[(nc + jj) * kWords + w] = reinterpret_cast<const uint32_t*>(NV + src * D)[w];
-    }
+    const int nc = max(0, min(nk, cached - k0));  // keys of this chunk in the cache; the rest are new
+    tc_stage_chunk<D>(a.k_cache, a.v_cache, tok_stride, h, slots, k0, nc, nk, NK, NV, k0 + nc - cached, a.num_slots,
+                      Ks, Vs, a.status);
     __syncthreads();
-#pragma unroll
-    for (int s = 0; s < kMaxQPerWarp; ++s) {
-      const int qi = warp + s * kAttnWarps;
-      if (qi < Q) {
-        const int qpos = cached + q0 + qi / g;  // absolute position of this query
-        const float* qv = q_s + qi * D;
-        const __nv_bfloat162* K2 = reinterpret_cast<const __nv_bfloat162*>(Ks);
-        const int kp0 = k0 + lane, kp1 = k0 + lane + 32;
-        const float s0 = (lane < nk && kp0 <= qpos) ? dot_q_k<D>(qv, K2 + lane * (D / 2 + 1)) * a.scale : -INFINITY;
-        const float s1 =
-            (lane + 32 < nk && kp1 <= qpos) ? dot_q_k<D>(qv, K2 + (lane + 32) * (D / 2 + 1)) * a.scale : -INFINITY;
-        fold_scores<D>(st[s], s0, s1, nk, [&](int jv, int i) { return bf16_to_f(Vs[jv * D + i * 32 + lane]); });
-      }
-    }
+    if (folds) tc_fold_chunk<D>(tr, Ks, Vs, k0, nk, a.scale, lane);
     __syncthreads();
   }
-#pragma unroll
-  for (int s = 0; s < kMaxQPerWarp; ++s) {
-    const int qi = warp + s * kAttnWarps;
-    if (qi < Q) {
-      const int t = qi / g, j = qi % g;
-      const float inv = st[s].l > 0.f ? 1.0f / st[s].l : 0.f;
-      __nv_bfloat16* dst = a.out + (qbase + q0 + t) * a.out_stride + (int64_t)(h * g + j) * D;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st[s].acc[i] * inv);
-    }
-  }
+  if (folds)
+    tc_rows_store<D>(tr, row0, Q, lane, [&](int qi) {
+      return a.out + (qbase + q0 + qi / g) * a.out_stride + (int64_t)(h * g + qi % g) * D;
+    });
 }
 
 }  // namespace

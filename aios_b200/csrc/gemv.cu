@@ -58,7 +58,11 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <int NT, int KB, bool STAT>
+// GROUPS: more than one 16-row group along grid y (prefill widths). The decode
+// instantiations (false) keep row 0 and streaming weight loads as constants, so
+// their register use (and with it how many CTAs share an SM with the previous
+// kernel's) is unchanged by the row-group addressing.
+template <int NT, int KB, bool STAT, bool GROUPS>
 __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a) {
   constexpr int TM = NT * 8;  // token rows covered
   __shared__ float red[kGemvFeat][NT][32][4];  // [warp][n tile][lane][fragment]
@@ -69,9 +73,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
   const int K = (int)a.k;
   const int kb = K / 256;  // 32-wide blocks per warp
   // grid row y covers token rows [row0, row0 + TM) (prefill widths: several row groups)
-  const int row0 = blockIdx.y * TM;
+  const int row0 = GROUPS ? (int)blockIdx.y * TM : 0;
   const int T = min(TM, a.rows - row0);
-  const bool streaming = gridDim.y == 1;  // weights read by one row group only
   const bool silu = a.epilogue == AIOSB_EPI_SILU_MUL;
   const int feat_per_tile = silu ? 8 : 16;
   const int ntiles = (int)(a.n_out / feat_per_tile);
@@ -99,8 +102,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
       const bool ok = tl < ntiles && b < kb;
       const uint4* pa = reinterpret_cast<const uint4*>(a.w + r0 * K + kbase + b * 32);
       const uint4* pb = reinterpret_cast<const uint4*>(a.w + r1 * K + kbase + b * 32);
-      wa[b] = ok ? (streaming ? __ldcs(pa) : __ldg(pa)) : make_uint4(0u, 0u, 0u, 0u);
-      wb[b] = ok ? (streaming ? __ldcs(pb) : __ldg(pb)) : make_uint4(0u, 0u, 0u, 0u);
+      wa[b] = ok ? (GROUPS ? __ldg(pa) : __ldcs(pa)) : make_uint4(0u, 0u, 0u, 0u);
+      wb[b] = ok ? (GROUPS ? __ldg(pb) : __ldcs(pb)) : make_uint4(0u, 0u, 0u, 0u);
     }
   };
   uint4 wa[KB], wb[KB];
@@ -274,9 +277,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
   }
 }
 
-template <int NT, int KB, bool STAT>
+template <int NT, int KB, bool STAT, bool GROUPS>
 int launch_mma(const GemvArgs& a, cudaStream_t stream) {
-  auto kern = gemv_mma_kernel<NT, KB, STAT>;
+  auto kern = gemv_mma_kernel<NT, KB, STAT, GROUPS>;
   const int64_t tiles = a.n_out / (a.epilogue == AIOSB_EPI_SILU_MUL ? 8 : 16);
   // as many CTAs as can be resident at once (each prefetches its first tile's
   // weights before the wait; a CTA with more tiles loads the rest one ahead)
@@ -296,7 +299,9 @@ int launch_mma(const GemvArgs& a, cudaStream_t stream) {
 
 template <int NT, int KB>
 int launch_mma_rows(const GemvArgs& a, cudaStream_t stream) {
-  return a.stat_x != nullptr ? launch_mma<NT, KB, true>(a, stream) : launch_mma<NT, KB, false>(a, stream);
+  if (a.rows > NT * 8)
+    return a.stat_x != nullptr ? launch_mma<NT, KB, true, true>(a, stream) : launch_mma<NT, KB, false, true>(a, stream);
+  return a.stat_x != nullptr ? launch_mma<NT, KB, true, false>(a, stream) : launch_mma<NT, KB, false, false>(a, stream);
 }
 
 bool g_gemv_enabled = [] {

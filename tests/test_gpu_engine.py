@@ -122,4 +122,4 @@ def test_keystroke_with_a_top_k_beyond_the_top_k_buffer(engine) -> None:
     narrow = engine.complete(prefix, ImeGenerationConfig(seed=31, top_k=50, top_p=0.9, max_sampling_attempts=8))
     assert narrow.sampling_attempts == 8
     keys = set(engine._runtime._graphs)
-    assert (8, True) in keys and (8, False) in keys
+    assert {k[:2] for k in keys} >= {(8, True), (8, False)}
