@@ -829,29 +829,74 @@ __global__ void __launch_bounds__(kSampThreads, 1)
 }
 
 // ---- CandidateGroup step ----------------------------------------------------
-// CTA r samples local row r of the group (aios/ime.py:998-1037); the last CTA
-// to finish runs the step's host-free epilogue: compaction of finished rows,
-// FIFO slot allocation in active-row order (aios/scheduler/cache.py:46-51),
-// page-table writes (aios/ime.py:1229) and the next forward's metadata.
-__global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group_ptrs g, int large) {
+// Row r of the group (aios/ime.py:998-1037) is sampled by a cluster of C CTAs
+// (C = 1: one CTA). With C > 1 and a top-k sorted path (top_k <= 512, not
+// greedy), CTA c of the cluster takes the c-th 1/C slice of the vocabulary: its
+// max and sum of exponentials (the raw log-softmax pieces), the order keys of
+// the unscaled values and its own k-th largest key L_c (exact, by bisection on
+// the key bits). The slices exchange these over distributed
+// shared memory; every key >= max_c L_c (at least k of them: CTA argmax_c L_c
+// alone holds k; at most k per slice) goes to the leader (rank 0), which sorts the candidates and
+// picks with the same arithmetic as the one-CTA path, and combines the log-sum-
+// exp as M + log(sum_c s_c exp(m_c - M)). Greedy, top-p without top-k, larger
+// k, more than 2048 candidates (rows of ties) and values where dividing by the
+// temperature could overflow take the one-CTA path on the leader. Only leaders
+// do the row bookkeeping; the last leader to finish runs the step's host-free
+// epilogue: compaction of finished rows, FIFO slot allocation in active-row
+// order (aios/scheduler/cache.py:46-51), page-table writes (aios/ime.py:1229)
+// and the next forward's metadata.
+constexpr int kMaxSplit = 8;
+// Measured on the S10 keystroke (8 rows, one box, two runs each, ms p50):
+// 1 CTA per row 3.057 / 3.046, 2 CTAs 2.944 / 2.941, 4 CTAs 2.934 / 2.964,
+// 8 CTAs 2.982 / 2.970.
+constexpr int kDefaultSplit = 2;
+struct SplitXchg {
+  float m[kMaxSplit], se[kMaxSplit];
+  uint32_t bound[kMaxSplit];
+  int hazard[kMaxSplit];
+  uint32_t count;  // leader: candidates reserved so far
+  int base;
+  int cnt[2][kSampThreads / 32];  // bisection counts per warp (two alternating buffers)
+};
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_u64(uint32_t addr, unsigned long long v) {
+  asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_add_cluster_u32(uint32_t addr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.shared::cluster.add.u32 %0, [%1], %2;" : "=r"(old) : "r"(addr), "r"(v) : "memory");
+  return old;
+}
+
+__global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group_ptrs g, int large, int C) {
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw + sizeof(RowSmem));
+  __shared__ SplitXchg xs;
   pdl_enter();
   aiosb_group_state* st = g.state;
-  const int r = blockIdx.x;
-  const int lane = threadIdx.x & 31;
-  const bool warp0 = threadIdx.x < 32;
+  const int r = blockIdx.x / C;
+  const int c = C > 1 ? (int)cluster_ctarank() : 0;
+  const bool leader = c == 0;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const bool warp0 = tid < 32 && leader;
   const int step = st->step;
   const int V = st->vocab;
   const int S = st->max_steps;
   const int st_done = st->done;
   const bool run = st_done == 0 && g.active[r] != 0;
-  // The bookkeeping and the step epilogue run in warp 0 (of the last CTA for the
-  // epilogue). Their inputs are requested now, so that the round trips overlap
-  // the sampling instead of forming a chain after it: the state fields that only
-  // the epilogue writes (no CTA of this launch writes them before every CTA has
-  // arrived). Measured: 2.5 us less per decode step.
+  // The bookkeeping and the step epilogue run in warp 0 of leaders (of the last
+  // one for the epilogue). Their inputs are requested now, so that the round
+  // trips overlap the sampling instead of forming a chain after it: the state
+  // fields that only the epilogue writes (no CTA of this launch writes them
+  // before every leader has arrived). Measured: 2.5 us less per decode step.
   int R = 0, P = 1, prefix_len = 0, row_offset = 0, n_terminal = 0, eos_id = 0, pad_id = 0, amt = 0;
   int64_t head = 0, tail = 0, cap = 0, table_stride = 0;
   if (warp0) {
@@ -868,10 +913,12 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
     cap = st->capacity;
     table_stride = st->table_stride;
   }
+  SampleParams p;
+  p.temperature = st->temperature;
+  p.top_k = st->top_k;
+  p.top_p = st->top_p;
+  p.greedy = st->greedy;
   const __nv_bfloat16* lrow = reinterpret_cast<const __nv_bfloat16*>(g.logits) + (int64_t)r * V;
-  RowRegs rr;
-  float mx = 0.f, lse = 0.f;
-  if (run) load_row(s, rr, lrow, V, mx, lse);
   // second round of epilogue inputs, addressed by the fields above: lane l holds
   // row l's active flag and suffix page, terminal id l, and the FIFO entry l
   // places past the head (the slot of the alive row of rank l)
@@ -887,13 +934,15 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
       e_lpsum = g.logprob_sums[r];
     }
   }
-  if (run) {
+  // the sampling copy's forbidden ids (aios/engine/sample.py:76-111): the
+  // minimum-length list, and the refill exact-repeat bans (aios/ime.py:974-996):
+  // for every banned sequence b, its token at `step` if this row's output so far
+  // equals its prefix, otherwise the pad id (the reference fills non-matching
+  // slots with pad)
+  auto apply_bans = [&]() {
     if (step < st->min_new_tokens) apply_forbidden(s, V, g.minlen_ids, st->n_minlen);
-    // Refill exact-repeat bans (aios/ime.py:974-996): for every banned sequence
-    // b, ban its token at `step` if this row's output so far equals its prefix,
-    // otherwise ban the pad id (the reference fills non-matching slots with pad).
     if (st->n_banned > 0 && step >= st->ban_min_prefix && step < st->banned_width) {
-      for (int b = threadIdx.x; b < st->n_banned; b += blockDim.x) {
+      for (int b = tid; b < st->n_banned; b += blockDim.x) {
         const int32_t* seq = g.banned + (int64_t)b * st->banned_width;
         bool match = g.banned_len[b] > step;
         for (int t = 0; t < step && match; ++t) match = g.output_ids[(int64_t)r * S + t] == seq[t];
@@ -901,31 +950,162 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
         if (id >= 0 && id < V) ban_id(s, id);
       }
     }
+  };
+  const float u = run ? g.uniforms[(int64_t)r * S + step] : 0.f;
+  int tok = 0;
+  float mx = 0.f, lse = 0.f;
+  bool have = false;
+  const bool split = C > 1 && run && !p.greedy && p.top_k >= 1 && p.top_k <= kFastTopK;
+  if (split) {
+    // ---- this CTA's slice: ids [lo, hi), one 8-id group per thread
+    const int W = (V + 8 * C - 1) / (8 * C) * 8;
+    const int lo = c * W, hi = min(V, lo + W);
+    const int id0 = lo + 8 * tid;
+    const int nvalid = id0 < hi ? min(8, hi - id0) : 0;
+    uint4 x = make_uint4(0u, 0u, 0u, 0u);
+    if (nvalid == 8 && (reinterpret_cast<uintptr_t>(lrow + id0) & 15u) == 0) {
+      x = *reinterpret_cast<const uint4*>(lrow + id0);
+    } else if (nvalid > 0) {
+      const uint16_t* h = reinterpret_cast<const uint16_t*>(lrow);
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      for (int e = 0; e < nvalid; ++e) w[e >> 1] |= (uint32_t)h[id0 + e] << ((e & 1) * 16);
+      x = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    for (int w = lo / 32 + tid; w < (hi + 31) / 32; w += blockDim.x) s.ban[w] = 0u;
+    if (leader && tid == 0) xs.count = 0u;
     __syncthreads();
-    SampleParams p;
-    p.temperature = st->temperature;
-    p.top_k = st->top_k;
-    p.top_p = st->top_p;
-    p.greedy = st->greedy;
-    const float u = g.uniforms[(int64_t)r * S + step];
-    const int tok = sample_row(s, rr, keys, V, p, u, large != 0);
-    if (warp0) {
-      const bool eos = tok == eos_id;
-      const bool emitted = !eos;
-      bool hit = false;
-      for (int j = lane; j < n_terminal; j += 32) hit |= tok == (j == lane ? e_term : g.terminal_ids[j]);
-      const bool terminal = emitted && __any_sync(0xffffffffu, hit);
-      if (lane == 0) {
-        const float lp = (bf16_to_f(lrow[tok]) - mx) - lse;
-        g.output_ids[(int64_t)r * S + step] = emitted ? tok : pad_id;
-        g.counts[r] = e_count + (emitted ? 1 : 0);
-        g.logprob_sums[r] = e_lpsum + (emitted ? lp : 0.f);
-        g.token_logprobs[(int64_t)r * S + step] = emitted ? lp : 0.f;
-        if (eos) g.stop_codes[r] = 1;
-        if (terminal) g.stop_codes[r] = 2;
-        g.finished[r] = (eos || terminal) ? 1 : 0;
-        g.tokens[r] = tok;
+    apply_bans();
+    float m = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (e < nvalid) m = fmaxf(m, group_elem(x, e));
+    m = block_max(m, s.red);
+    float se = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (e < nvalid) se += expf(group_elem(x, e) - m);
+    se = block_sum(se, s.red);  // ends with a barrier: the bans are complete
+    const float big = p.temperature < 65536.f ? 0x1.fffffep126f * p.temperature : -1.f;
+    const uint32_t bits = nvalid > 0 ? s.ban[id0 >> 5] >> (id0 & 31) : 0u;  // id0 % 8 == 0: one word
+    uint32_t kv[8];
+    bool hz = false;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      kv[e] = 0u;
+      if (e < nvalid) {
+        float v = group_elem(x, e);
+        hz |= !(fabsf(v) <= big);  // NaN included
+        if ((bits >> e) & 1u) v = -INFINITY;
+        kv[e] = order_key(v);
       }
+    }
+    const int k = min(p.top_k, V);
+    // L_c: this slice's exact k-th largest key (0 when it holds fewer than k
+    // ids), by bisection on the 16 significant bits of the raw keys with a block
+    // count per step; the per-warp counts alternate between two buffers, so one
+    // barrier per step suffices
+    uint32_t L = 0u;
+    const int warp = tid >> 5;
+    for (int b = 31, buf = 0; b >= 16; --b, buf ^= 1) {
+      const uint32_t cand = L | (1u << b);
+      int n = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) n += kv[e] >= cand ? 1 : 0;
+      n = (int)__reduce_add_sync(0xffffffffu, (unsigned)n);
+      if (lane == 0) xs.cnt[buf][warp] = n;
+      __syncthreads();
+      int tot = 0;
+#pragma unroll
+      for (int w = 0; w < kSampThreads / 32; ++w) tot += xs.cnt[buf][w];
+      if (tot >= k) L = cand;
+    }
+    const int any_hz = __syncthreads_or(hz);
+    // exchange 1: every CTA writes its slot c into every peer's exchange block
+    if (tid < C) {
+      const uint32_t q = (uint32_t)tid;
+      st_cluster_f32(map_shared_rank(smem_u32(&xs.m[c]), q), m);
+      st_cluster_f32(map_shared_rank(smem_u32(&xs.se[c]), q), se);
+      st_cluster_u32(map_shared_rank(smem_u32(&xs.bound[c]), q), L);
+      st_cluster_u32(map_shared_rank(smem_u32(&xs.hazard[c]), q), (uint32_t)any_hz);
+    }
+    cluster_sync();
+    uint32_t Lg = 0u;
+    bool hzg = false;
+    float M = -INFINITY;
+    for (int q = 0; q < C; ++q) {
+      Lg = xs.bound[q] > Lg ? xs.bound[q] : Lg;
+      hzg |= xs.hazard[q] != 0;
+      M = fmaxf(M, xs.m[q]);
+    }
+    if (!hzg) {
+      // exchange 2: candidates (key >= Lg) into the leader's buffer
+      int n = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) n += (e < nvalid && kv[e] >= Lg) ? 1 : 0;
+      int total;
+      int off = block_exclusive_scan(n, s, total);
+      if (tid == 0) xs.base = (int)atom_add_cluster_u32(map_shared_rank(smem_u32(&xs.count), 0u), (uint32_t)total);
+      __syncthreads();
+      off += xs.base;
+      const uint32_t cand0 = map_shared_rank(smem_u32(&s.cand[0]), 0u);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        if (e < nvalid && kv[e] >= Lg) {
+          if (off < kMaxSortK)
+            st_cluster_u64(cand0 + (uint32_t)off * 8u,
+                           ((unsigned long long)(~kv[e]) << 32) | (unsigned long long)(uint32_t)(id0 + e));
+          ++off;
+        }
+      }
+      cluster_sync();
+      if (!leader) return;  // nothing reads this CTA's shared memory after the barrier
+      const int total_all = (int)xs.count;
+      if (total_all <= kMaxSortK) {
+        sort_candidates(s, total_all);
+        for (int i = tid; i < k; i += blockDim.x) {
+          const unsigned long long cv = s.cand[i];
+          s.cid[i] = (int)(uint32_t)(cv & 0xffffffffull);
+          s.cval[i] = key_value(~(uint32_t)(cv >> 32)) / p.temperature;  // the fp32 division of make_keys
+        }
+        __syncthreads();
+        const auto val = [&](int i) { return s.cval[i]; };
+        tok = s.cid[pick_index(s, val, k, p.top_p, u)];
+        float sum = 0.f;
+        for (int q = 0; q < C; ++q) sum += xs.se[q] * expf(xs.m[q] - M);
+        mx = M;
+        lse = logf(sum);
+        have = true;
+      }
+    } else if (!leader) {
+      return;
+    }
+  } else if (!leader) {
+    return;
+  }
+  if (run && !have) {
+    // the one-CTA path: the whole row in this CTA
+    RowRegs rr;
+    load_row(s, rr, lrow, V, mx, lse);
+    apply_bans();
+    __syncthreads();
+    tok = sample_row(s, rr, keys, V, p, u, large != 0);
+  }
+  if (run && warp0) {
+    const bool eos = tok == eos_id;
+    const bool emitted = !eos;
+    bool hit = false;
+    for (int j = lane; j < n_terminal; j += 32) hit |= tok == (j == lane ? e_term : g.terminal_ids[j]);
+    const bool terminal = emitted && __any_sync(0xffffffffu, hit);
+    if (lane == 0) {
+      const float lp = (bf16_to_f(lrow[tok]) - mx) - lse;
+      g.output_ids[(int64_t)r * S + step] = emitted ? tok : pad_id;
+      g.counts[r] = e_count + (emitted ? 1 : 0);
+      g.logprob_sums[r] = e_lpsum + (emitted ? lp : 0.f);
+      g.token_logprobs[(int64_t)r * S + step] = emitted ? lp : 0.f;
+      if (eos) g.stop_codes[r] = 1;
+      if (terminal) g.stop_codes[r] = 2;
+      g.finished[r] = (eos || terminal) ? 1 : 0;
+      g.tokens[r] = tok;
     }
   }
   // ---- last CTA: step epilogue, one lane of warp 0 per row: every flag and
@@ -937,7 +1117,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   if (threadIdx.x == 0) {
     __threadfence();
     const int prev = atomicAdd(&st->arrive, 1);
-    is_last = prev == (int)gridDim.x - 1;
+    is_last = prev == (int)(gridDim.x / C) - 1;  // one arrival per row (leaders)
   }
   __syncthreads();
   if (!is_last || threadIdx.x >= 32) return;
@@ -1145,6 +1325,40 @@ __global__ void __launch_bounds__(kSampThreads)
 
 using namespace aiosb;
 
+namespace aiosb {
+namespace {
+// CTAs per row of the group step (AIOSB_GROUP_SPLIT: 1, 2, 4 or 8), at most
+// 128 CTAs in all (one wave).
+int g_group_split = [] {
+  const char* env = getenv("AIOSB_GROUP_SPLIT");
+  const int v = env ? atoi(env) : kDefaultSplit;
+  return v == 1 || v == 2 || v == 4 || v == 8 ? v : kDefaultSplit;
+}();
+
+int launch_group_step(const aiosb_group_ptrs& g, int64_t rows, int64_t vocab, bool large, cudaStream_t stream) {
+  int C = g_group_split;
+  while (C > 1 && rows * C > 128) C >>= 1;
+  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(rows * C));
+  cfg.blockDim = dim3(kSampThreads);
+  cfg.dynamicSmemBytes = large ? sample_smem_large((int)vocab) : sample_smem((int)vocab);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)C;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = C > 1 ? 2 : 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, group_step_kernel, g, (int)large, C);
+  return e == cudaSuccess ? AIOSB_OK : set_error(AIOSB_ERR_LAUNCH, "group_step: %s", cudaGetErrorString(e));
+}
+}  // namespace
+}  // namespace aiosb
+
 extern "C" int aiosb_sample(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride, float temperature,
                             int64_t top_k, float top_p, int greedy, const float* uniforms, const int32_t* forbidden,
                             int64_t n_forbidden, const int64_t* forbidden_rows, int64_t n_forbidden_rows,
@@ -1200,12 +1414,7 @@ extern "C" int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t
                 "group_step: sorted candidate sets above %d need a vocabulary of at most %d", kMaxSortK,
                 kMaxLargeSort);
   AIOSB_REQUIRE(rows <= 32, AIOSB_ERR_UNSUPPORTED, "group_step: at most 32 rows per group");
-  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max());
-  cudaError_t e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads),
-                             large ? sample_smem_large((int)vocab) : sample_smem((int)vocab), as_stream(stream), *g,
-                             (int)large);
-  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step: %s", cudaGetErrorString(e));
-  return AIOSB_OK;
+  return launch_group_step(*g, rows, vocab, large, as_stream(stream));
 }
 
 extern "C" int aiosb_token_logprobs(const void* logits, int64_t rows, int64_t vocab, int64_t row_stride,
@@ -1376,10 +1585,5 @@ extern "C" int aiosb_group_step_static(const aiosb_group_ptrs* g, int64_t rows, 
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step_static: memset: %s", cudaGetErrorString(e));
   aiosb_group_ptrs local = *g;
   local.finished = finished;
-  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max());
-  e = launch_pdl(group_step_kernel, dim3((unsigned)rows), dim3(kSampThreads),
-                 large ? sample_smem_large((int)vocab) : sample_smem((int)vocab), as_stream(stream), local,
-                 (int)large);
-  if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "group_step_static: %s", cudaGetErrorString(e));
-  return AIOSB_OK;
+  return launch_group_step(local, rows, vocab, large, as_stream(stream));
 }
