@@ -829,8 +829,8 @@ __global__ void __launch_bounds__(kSampThreads, 1)
 }
 
 // ---- CandidateGroup step ----------------------------------------------------
-// Row r of the group (aios/ime.py:998-1037) is sampled by a cluster of C CTAs
-// (C = 1: one CTA). With C > 1 and a top-k sorted path (top_k <= 512, not
+// Row r of the group (aios/ime.py:998-1037) is sampled by one CTA, or by a
+// cluster of C CTAs (AIOSB_GROUP_SPLIT). With C > 1 and a top-k sorted path (top_k <= 512, not
 // greedy), CTA c of the cluster takes the c-th 1/C slice of the vocabulary: its
 // max and sum of exponentials (the raw log-softmax pieces), the order keys of
 // the unscaled values and its own k-th largest key L_c (exact, by bisection on
@@ -846,10 +846,13 @@ __global__ void __launch_bounds__(kSampThreads, 1)
 // order (aios/scheduler/cache.py:46-51), page-table writes (aios/ime.py:1229)
 // and the next forward's metadata.
 constexpr int kMaxSplit = 8;
+constexpr int kSplitVec = kVecPer / 2;  // 8-id groups per thread in a slice of at least 2
 // Measured on the S10 keystroke (8 rows, one box, two runs each, ms p50):
-// 1 CTA per row 3.057 / 3.046, 2 CTAs 2.944 / 2.941, 4 CTAs 2.934 / 2.964,
-// 8 CTAs 2.982 / 2.970.
-constexpr int kDefaultSplit = 2;
+// 1 CTA per row 3.018 / 3.017, 2 CTAs 3.016 / 3.041, 4 CTAs 3.030 / 3.042,
+// 8 CTAs 3.040 / 3.055. The step is bound by its chain of block barriers and
+// cold instruction fetches, not by the per-thread work a split divides, and a
+// split adds two cluster barriers: one CTA per row stays the default.
+constexpr int kDefaultSplit = 1;
 struct SplitXchg {
   float m[kMaxSplit], se[kMaxSplit];
   uint32_t bound[kMaxSplit];
@@ -957,19 +960,25 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   bool have = false;
   const bool split = C > 1 && run && !p.greedy && p.top_k >= 1 && p.top_k <= kFastTopK;
   if (split) {
-    // ---- this CTA's slice: ids [lo, hi), one 8-id group per thread
+    // ---- this CTA's slice: ids [lo, hi) as 8-id groups; thread t holds groups
+    // t, t + 512, ... (at most kSplitVec: C >= 2 halves the widest row)
     const int W = (V + 8 * C - 1) / (8 * C) * 8;
     const int lo = c * W, hi = min(V, lo + W);
-    const int id0 = lo + 8 * tid;
-    const int nvalid = id0 < hi ? min(8, hi - id0) : 0;
-    uint4 x = make_uint4(0u, 0u, 0u, 0u);
-    if (nvalid == 8 && (reinterpret_cast<uintptr_t>(lrow + id0) & 15u) == 0) {
-      x = *reinterpret_cast<const uint4*>(lrow + id0);
-    } else if (nvalid > 0) {
-      const uint16_t* h = reinterpret_cast<const uint16_t*>(lrow);
-      uint32_t w[4] = {0u, 0u, 0u, 0u};
-      for (int e = 0; e < nvalid; ++e) w[e >> 1] |= (uint32_t)h[id0 + e] << ((e & 1) * 16);
-      x = make_uint4(w[0], w[1], w[2], w[3]);
+    const uint16_t* h16 = reinterpret_cast<const uint16_t*>(lrow);
+    uint4 x[kSplitVec];
+    int nvalid[kSplitVec];
+#pragma unroll
+    for (int q = 0; q < kSplitVec; ++q) {
+      const int id0 = lo + 8 * (tid + q * kSampThreads);
+      nvalid[q] = id0 < hi ? min(8, hi - id0) : 0;
+      x[q] = make_uint4(0u, 0u, 0u, 0u);
+      if (nvalid[q] == 8 && (reinterpret_cast<uintptr_t>(lrow + id0) & 15u) == 0) {
+        x[q] = *reinterpret_cast<const uint4*>(lrow + id0);
+      } else if (nvalid[q] > 0) {
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        for (int e = 0; e < nvalid[q]; ++e) w[e >> 1] |= (uint32_t)h16[id0 + e] << ((e & 1) * 16);
+        x[q] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
     }
     for (int w = lo / 32 + tid; w < (hi + 31) / 32; w += blockDim.x) s.ban[w] = 0u;
     if (leader && tid == 0) xs.count = 0u;
@@ -977,26 +986,34 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
     apply_bans();
     float m = -INFINITY;
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (e < nvalid) m = fmaxf(m, group_elem(x, e));
+    for (int q = 0; q < kSplitVec; ++q)
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < nvalid[q]) m = fmaxf(m, group_elem(x[q], e));
     m = block_max(m, s.red);
     float se = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (e < nvalid) se += expf(group_elem(x, e) - m);
+    for (int q = 0; q < kSplitVec; ++q)
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < nvalid[q]) se += expf(group_elem(x[q], e) - m);
     se = block_sum(se, s.red);  // ends with a barrier: the bans are complete
     const float big = p.temperature < 65536.f ? 0x1.fffffep126f * p.temperature : -1.f;
-    const uint32_t bits = nvalid > 0 ? s.ban[id0 >> 5] >> (id0 & 31) : 0u;  // id0 % 8 == 0: one word
-    uint32_t kv[8];
+    uint32_t kv[kSplitVec][8];
     bool hz = false;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      kv[e] = 0u;
-      if (e < nvalid) {
-        float v = group_elem(x, e);
-        hz |= !(fabsf(v) <= big);  // NaN included
-        if ((bits >> e) & 1u) v = -INFINITY;
-        kv[e] = order_key(v);
+    for (int q = 0; q < kSplitVec; ++q) {
+      const int id0 = lo + 8 * (tid + q * kSampThreads);
+      const uint32_t bits = nvalid[q] > 0 ? s.ban[id0 >> 5] >> (id0 & 31) : 0u;  // id0 % 8 == 0: one word
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        kv[q][e] = 0u;
+        if (e < nvalid[q]) {
+          float v = group_elem(x[q], e);
+          hz |= !(fabsf(v) <= big);  // NaN included
+          if ((bits >> e) & 1u) v = -INFINITY;
+          kv[q][e] = order_key(v);
+        }
       }
     }
     const int k = min(p.top_k, V);
@@ -1010,7 +1027,9 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
       const uint32_t cand = L | (1u << b);
       int n = 0;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) n += kv[e] >= cand ? 1 : 0;
+      for (int q = 0; q < kSplitVec; ++q)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) n += kv[q][e] >= cand ? 1 : 0;
       n = (int)__reduce_add_sync(0xffffffffu, (unsigned)n);
       if (lane == 0) xs.cnt[buf][warp] = n;
       __syncthreads();
@@ -1041,7 +1060,9 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
       // exchange 2: candidates (key >= Lg) into the leader's buffer
       int n = 0;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) n += (e < nvalid && kv[e] >= Lg) ? 1 : 0;
+      for (int q = 0; q < kSplitVec; ++q)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) n += (e < nvalid[q] && kv[q][e] >= Lg) ? 1 : 0;
       int total;
       int off = block_exclusive_scan(n, s, total);
       if (tid == 0) xs.base = (int)atom_add_cluster_u32(map_shared_rank(smem_u32(&xs.count), 0u), (uint32_t)total);
@@ -1049,12 +1070,16 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
       off += xs.base;
       const uint32_t cand0 = map_shared_rank(smem_u32(&s.cand[0]), 0u);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (e < nvalid && kv[e] >= Lg) {
-          if (off < kMaxSortK)
-            st_cluster_u64(cand0 + (uint32_t)off * 8u,
-                           ((unsigned long long)(~kv[e]) << 32) | (unsigned long long)(uint32_t)(id0 + e));
-          ++off;
+      for (int q = 0; q < kSplitVec; ++q) {
+        const int id0 = lo + 8 * (tid + q * kSampThreads);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (e < nvalid[q] && kv[q][e] >= Lg) {
+            if (off < kMaxSortK)
+              st_cluster_u64(cand0 + (uint32_t)off * 8u,
+                             ((unsigned long long)(~kv[q][e]) << 32) | (unsigned long long)(uint32_t)(id0 + e));
+            ++off;
+          }
         }
       }
       cluster_sync();

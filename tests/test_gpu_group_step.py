@@ -2,10 +2,11 @@
 branch, against the oracle sampler (aios/engine/sample.py:54-163 with the
 minimum-length bans of aios/ime.py:1008-1012).
 
-The step splits each row over a cluster of CTAs on the top-k path (k <= 512)
-and falls back to one CTA per row for greedy, top-p without top-k, larger k,
-rows whose candidate set overflows (ties) and values that the temperature could
-overflow; each branch has a case here. Tokens are bit-exact (a mismatch only at
+One CTA samples a row by default; with AIOSB_GROUP_SPLIT a cluster of CTAs
+splits each row on the top-k path (k <= 512) and falls back to one CTA for
+greedy, top-p without top-k, larger k, rows whose candidate set overflows (ties)
+and values that the temperature could overflow; each branch has a case here, run
+in process (one CTA) and in child processes with 2, 4 and 8 CTAs per row. Tokens are bit-exact (a mismatch only at
 a CDF-boundary rounding tie), log-probabilities within 2e-5."""
 
 from __future__ import annotations
@@ -117,3 +118,20 @@ def test_group_step_matches_oracle_sampler(cuda_device, name, vocab, temperature
         torch.testing.assert_close(lp, exp_lp.squeeze(-1), rtol=0, atol=2e-5)
     # the step epilogue ran once: one FIFO slot per row, in row order
     assert grp["out_loc"].cpu().tolist() == list(range(ROWS))
+
+
+@pytest.mark.parametrize("split", [2, 4, 8])
+def test_group_step_other_cluster_sizes(split: int) -> None:
+    """The same cases with rows split over 2, 4 and 8 CTAs (the library reads the
+    split once, at load: a child process per size)."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, AIOSB_GROUP_SPLIT=str(split))
+    proc = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", "-m", "gpu",
+                           str(Path(__file__).resolve()), "-k", "matches_oracle"],
+                          cwd=repo, env=env, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-2000:]
