@@ -877,6 +877,8 @@ __device__ __forceinline__ uint32_t atom_add_cluster_u32(uint32_t addr, uint32_t
   return old;
 }
 
+// SPLIT = false: the one-CTA kernel (C == 1), with no cluster code compiled in.
+template <bool SPLIT>
 __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group_ptrs g, int large, int C) {
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
@@ -885,7 +887,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   pdl_enter();
   aiosb_group_state* st = g.state;
   const int r = blockIdx.x / C;
-  const int c = C > 1 ? (int)cluster_ctarank() : 0;
+  const int c = SPLIT ? (int)cluster_ctarank() : 0;
   const bool leader = c == 0;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -958,7 +960,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   int tok = 0;
   float mx = 0.f, lse = 0.f;
   bool have = false;
-  const bool split = C > 1 && run && !p.greedy && p.top_k >= 1 && p.top_k <= kFastTopK;
+  const bool split = SPLIT && run && !p.greedy && p.top_k >= 1 && p.top_k <= kFastTopK;
   if (split) {
     // ---- this CTA's slice: ids [lo, hi) as 8-id groups; thread t holds groups
     // t, t + 512, ... (at most kSplitVec: C >= 2 halves the widest row)
@@ -1363,7 +1365,8 @@ int g_group_split = [] {
 int launch_group_step(const aiosb_group_ptrs& g, int64_t rows, int64_t vocab, bool large, cudaStream_t stream) {
   int C = g_group_split;
   while (C > 1 && rows * C > 128) C >>= 1;
-  cudaFuncSetAttribute(group_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max());
+  auto kern = C > 1 ? group_step_kernel<true> : group_step_kernel<false>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sample_smem_max());
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(rows * C));
   cfg.blockDim = dim3(kSampThreads);
@@ -1378,7 +1381,7 @@ int launch_group_step(const aiosb_group_ptrs& g, int64_t rows, int64_t vocab, bo
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = C > 1 ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, group_step_kernel, g, (int)large, C);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, g, (int)large, C);
   return e == cudaSuccess ? AIOSB_OK : set_error(AIOSB_ERR_LAUNCH, "group_step: %s", cudaGetErrorString(e));
 }
 }  // namespace
