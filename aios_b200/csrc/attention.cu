@@ -259,10 +259,12 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_kernel(const DecodeAr
 // shared-prefix KV row leaves HBM / L2 once per cluster of rows. All of it still
 // happens before the dependency wait; the folds after it are the same.
 constexpr int kHistSuffix = 32;
+constexpr int kHistThreads = 256;  // 8 warps: one per query head of a KV group (g <= 8)
+constexpr int kHistWarps = kHistThreads / 32;
 constexpr int kHistDefaultPrefix = 128;  // staged prefix keys when the caller gives no bound
 template <int D>
 __host__ __device__ constexpr int hist_prefix_cap() {
-  return D == 64 ? 512 : D == 96 ? 448 : 256;
+  return D == 64 ? 512 : D == 96 ? 384 : 256;
 }
 
 // Staged K rows are dense (D bf16, 16-byte aligned, so cp.async and bulk copies
@@ -307,12 +309,13 @@ __device__ __forceinline__ void fold_staged(QState<D>& st, const float* qv, cons
 template <int D>
 size_t hist_decode_smem(int group, int cap) {
   const int rows = cap + kHistSuffix;
-  return (size_t)group * D * 4 + (size_t)kDecWarps * D * 4 + (size_t)rows * D * 2 * 2 +
-         (size_t)kKeyChunk * ((D + 2) * 2 + D * 2) + (size_t)4 * D * 2;
+  return (size_t)group * D * 4 + (size_t)kHistWarps * D * 4 + (size_t)rows * D * 2 * 2 +
+         (size_t)kKeyChunk * ((D + 2) * 2 + D * 2) + (size_t)4 * D * 2 +
+         (size_t)kHistWarps * group * (D + 2) * 4;  // chunk-split partial states
 }
 
 template <int D>
-__global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const DecodeArgs a, int cluster_rows) {
+__global__ void __launch_bounds__(kHistThreads) attn_decode_hist_kernel(const DecodeArgs a, int cluster_rows) {
   constexpr int DPL = D / 32;
   constexpr int KR = D + 2;  // padded K row of the streamed overflow chunks
   const int kCap = a.stage_cap;  // <= hist_prefix_cap<D>() (host)
@@ -326,7 +329,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
   float* q_s = reinterpret_cast<float*>(smem_raw);  // [g][D]
   float* tmp = q_s + g * D;                          // [warps][D]
   // staged keys, contiguous: [prefix | older suffix | the new key]
-  __nv_bfloat16* Kh = reinterpret_cast<__nv_bfloat16*>(tmp + kDecWarps * D);  // [kCap + kHistSuffix][D], rotated
+  __nv_bfloat16* Kh = reinterpret_cast<__nv_bfloat16*>(tmp + kHistWarps * D);  // [kCap + kHistSuffix][D], rotated
   __nv_bfloat16* Vh = Kh + (kCap + kHistSuffix) * D;                           // [kCap + kHistSuffix][D]
   __nv_bfloat16* Kw = Vh + (kCap + kHistSuffix) * D;                           // [kKeyChunk][KR]: streamed overflow
   __nv_bfloat16* Vw = Kw + kKeyChunk * KR;                                     // [kKeyChunk][D]
@@ -334,6 +337,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
   __nv_bfloat16* sin_r = cos_r + D;
   __nv_bfloat16* nq = sin_r + D;  // [D]
   __nv_bfloat16* nk = nq + D;     // [D]
+  float* part = reinterpret_cast<float*>(nk + D);  // [warps][g][D + 2]: chunk-split partial states
   const int64_t tok_stride = (int64_t)a.hkv * D;
 
   // ---- before the wait. Everything read here was written by launches at least
@@ -366,10 +370,10 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
     mbar_init(&pbar, 1);
     fence_mbar_init();
   }
-  for (int i = lo + threadIdx.x; i < hi; i += kDecThreads) slot_s[i] = a.page_table[prow * a.table_stride + i];
-  for (int i = threadIdx.x; i < (act ? ns : 0); i += kDecThreads)
+  for (int i = lo + threadIdx.x; i < hi; i += kHistThreads) slot_s[i] = a.page_table[prow * a.table_stride + i];
+  for (int i = threadIdx.x; i < (act ? ns : 0); i += kHistThreads)
     slot_s[np + i] = a.page_table[rrow * a.table_stride + P + i];
-  for (int i = threadIdx.x; i < D; i += kDecThreads) {
+  for (int i = threadIdx.x; i < D; i += kHistThreads) {
     nq[i] = a.q_norm_w[i];
     nk[i] = a.k_norm_w[i];
     cos_r[i] = a.cos_tab[(int64_t)pos * D + i];
@@ -389,7 +393,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
     bad_slot = __any_sync(0xffffffffu, b);
   }
   auto stage_rows = [&](int j0, int j1) {
-    for (int i = threadIdx.x; i < (j1 - j0) * (D / 8); i += kDecThreads) {
+    for (int i = threadIdx.x; i < (j1 - j0) * (D / 8); i += kHistThreads) {
       const int j = j0 + i / (D / 8), c = i % (D / 8);
       int64_t slot = slot_s[j];
       if (slot < 0 || slot >= a.num_slots) slot = 0;  // reported after the wait
@@ -431,7 +435,7 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
   if (act) {
     if (threadIdx.x == 0 && (!pos_ok || L_in < P + 1 || L_in > a.table_stride))
       report(a.status, AIOSB_DEV_POSITION_RANGE);
-    for (int it = warp; it < g + 1; it += kDecWarps) {
+    for (int it = warp; it < g + 1; it += kHistWarps) {
       float* tw = tmp + warp * D;
       float x[DPL];
       if (it < g) {
@@ -469,30 +473,66 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
   }
   __syncthreads();
 
-  QState<D> st[2];
-  qstate_init<D>(st[0]);
-  qstate_init<D>(st[1]);
+  // warp w owns query head w of the group (g <= kHistWarps) for the folds that
+  // follow the staged ones and for the output
+  QState<D> st;
+  qstate_init<D>(st);
   const int32_t* pslots = a.page_table + prow * a.table_stride;
   const int32_t* rslots = a.page_table + rrow * a.table_stride;
   if (act) {
     auto fold_rows = [&](int j0, int n) {
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int j = warp + t * kDecWarps;
-        if (j < g) fold_staged<D>(st[t], q_s + j * D, Kh, Vh, j0, n, a.scale, lane);
-      }
+      if (warp < g) fold_staged<D>(st, q_s + warp * D, Kh, Vh, j0, n, a.scale, lane);
     };
     auto fold_stream = [&](int n) {
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int j = warp + t * kDecWarps;
-        if (j < g) fold_chunk<D>(st[t], q_s + j * D, Kw, Vw, n, a.scale, lane);
-      }
+      if (warp < g) fold_chunk<D>(st, q_s + warp * D, Kw, Vw, n, a.scale, lane);
     };
     // staged keys [prefix | older suffix] and, without a suffix overflow, the new
-    // key right after them: one pass per 64 keys
+    // key right after them, 64 keys per chunk
     const int nfold = nst + (ns_old == ns ? 1 : 0);
-    for (int c0 = 0; c0 < nfold; c0 += kKeyChunk) fold_rows(c0, min(kKeyChunk, nfold - c0));
+    const int nchunks = (nfold + kKeyChunk - 1) / kKeyChunk;
+    if (nchunks <= 1) {
+      if (nfold > 0) fold_rows(0, nfold);
+    } else {
+      // several chunks: warp w folds chunks w, w + 8, ... for every head, then
+      // head j's partial states are merged by warp j in warp order
+      QState<D> sh[kMaxGroupQ];
+#pragma unroll
+      for (int j = 0; j < kMaxGroupQ; ++j) qstate_init<D>(sh[j]);
+      for (int c = warp; c < nchunks; c += kHistWarps) {
+        const int c0 = c * kKeyChunk, n = min(kKeyChunk, nfold - c0);
+#pragma unroll
+        for (int j = 0; j < kMaxGroupQ; ++j)
+          if (j < g) fold_staged<D>(sh[j], q_s + j * D, Kh, Vh, c0, n, a.scale, lane);
+      }
+#pragma unroll
+      for (int j = 0; j < kMaxGroupQ; ++j) {
+        if (j < g) {
+          float* ps = part + (warp * g + j) * (D + 2);
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) ps[i * 32 + lane] = sh[j].acc[i];
+          if (lane == 0) {
+            ps[D] = sh[j].m;
+            ps[D + 1] = sh[j].l;
+          }
+        }
+      }
+      __syncthreads();
+      if (warp < g) {
+        float m = -INFINITY;
+        for (int w = 0; w < kHistWarps; ++w) m = fmaxf(m, part[(w * g + warp) * (D + 2) + D]);
+        st.m = m;
+        st.l = 0.f;
+        for (int w = 0; w < kHistWarps; ++w) {
+          const float* ps = part + (w * g + warp) * (D + 2);
+          const float mw = ps[D];
+          if (mw == -INFINITY) continue;  // a warp without a chunk
+          const float e = expf(mw - m);
+          st.l += ps[D + 1] * e;
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) st.acc[i] += ps[i * 32 + lane] * e;
+        }
+      }
+    }
     // longer histories: the prefix beyond the staged part, then the older suffix
     // beyond it, streamed from the cache, and the new key last
     for (int k0 = np; k0 < P; k0 += kKeyChunk) {
@@ -516,15 +556,11 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_hist_kernel(const Dec
 
   // ---- normalise and store (zeros for inactive rows)
   if (!real) return;
+  if (warp < g) {
+    const float inv = act && st.l > 0.f ? 1.0f / st.l : 0.f;
+    __nv_bfloat16* dst = a.out + (int64_t)r * a.out_stride + (int64_t)(h * g + warp) * D;
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int j = warp + t * kDecWarps;
-    if (j < g) {
-      const float inv = act && st[t].l > 0.f ? 1.0f / st[t].l : 0.f;
-      __nv_bfloat16* dst = a.out + (int64_t)r * a.out_stride + (int64_t)(h * g + j) * D;
-#pragma unroll
-      for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st[t].acc[i] * inv);
-    }
+    for (int i = 0; i < DPL; ++i) dst[i * 32 + lane] = f_to_bf16(st.acc[i] * inv);
   }
 }
 
@@ -927,7 +963,7 @@ cudaError_t launch_decode_hist(const DecodeArgs& a, int rows, int hkv, int group
   const int grid_rows = (rows + cluster_rows - 1) / cluster_rows * cluster_rows;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)hkv, (unsigned)grid_rows);
-  cfg.blockDim = dim3(kDecThreads);
+  cfg.blockDim = dim3(kHistThreads);
   cfg.dynamicSmemBytes = hist_decode_smem<D>(group, a.stage_cap);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];

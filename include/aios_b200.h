@@ -232,7 +232,7 @@ AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, 
  * split the prefix, each reads its slice once and copies it to the others over
  * distributed shared memory. Both give identical results; k_cache and v_cache
  * must be 16-byte aligned. staged_prefix bounds the prefix keys staged before
- * the wait (rounded up to 64; 0 = 128; at most 512 / 448 / 256 keys for head_dim
+ * the wait (rounded up to 64; 0 = 128; at most 512 / 384 / 256 keys for head_dim
  * 64 / 96 / 128): shared memory is sized by it, and longer prefixes are read
  * after the wait. */
 #define AIOSB_HISTORY_STAGED 1
