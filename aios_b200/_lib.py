@@ -147,7 +147,7 @@ _SIGNATURES = {
     "aiosb_host_device_pointer": ([_p, ctypes.POINTER(_p)], _i32),
     "aiosb_kv_store": ([_p, _p, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _p, _p], _i32),
     "aiosb_attnres_mix": ([_p, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _p], _i32),
-    "aiosb_attnres_mix_rmsnorm": ([_p, _i64, _i64, _i64, _p, _p, _f32, _p, _f32, _p, _p], _i32),
+    "aiosb_attnres_mix_rmsnorm": ([_p, _i64, _i64, _i64, _p, _p, _f32, _p, _f32, _i64, _p, _p], _i32),
     "aiosb_rmsnorm": ([_p, _i64, _i64, _i64, _i64, _p, _f32, _p, _i64, _p], _i32),
     "aiosb_add_rmsnorm": ([_p, _p, _i64, _i64, _p, _f32, _p], _i32),
     "aiosb_silu_mul": ([_p, _i64, _i64, _p, _p], _i32),

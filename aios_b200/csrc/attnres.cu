@@ -148,12 +148,17 @@ struct RegRows {
 };
 
 // One warp per token, every source row loaded straight into registers. The
-// weighted query, a model constant, is loaded before the wait on the producer.
+// weighted query, a model constant, is loaded before the wait on the producer,
+// and so are the first `stable` bank sources: the caller guarantees that they
+// were written before the previous kernel on the stream began (the Block AttnRes
+// trunk: the outputs of finished blocks), so that only the newest source and the
+// partial are read after the wait.
 template <int VPL, int NSRC, bool NORM = false>
 __global__ void __launch_bounds__(kMixWarps * 32, 3)
     attnres_reg_kernel(const uint4* __restrict__ bank, int nsrc_bank, int64_t tokens, int hidden,
                        const uint4* __restrict__ partial, const float* __restrict__ wq, float eps,
-                       uint4* __restrict__ out, const uint4* __restrict__ norm_w = nullptr, float norm_eps = 0.f) {
+                       uint4* __restrict__ out, const uint4* __restrict__ norm_w = nullptr, float norm_eps = 0.f,
+                       int stable = 0) {
   pdl_launch_dependents();
   const int64_t t = (int64_t)blockIdx.x * kMixWarps + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -164,19 +169,26 @@ __global__ void __launch_bounds__(kMixWarps * 32, 3)
 #pragma unroll
   for (int j = 0; j < VPL; ++j)
     nwr[j] = (NORM && lane + j * 32 < nv) ? norm_w[lane + j * 32] : make_uint4(0u, 0u, 0u, 0u);
-  pdl_wait();
-  if (t >= tokens) return;
   uint4 x[NSRC][VPL];
-  // Issue every load first (maximum memory-level parallelism), then reduce.
-#pragma unroll
-  for (int s = 0; s < NSRC; ++s) {
+  // Issue every load of a phase first (maximum memory-level parallelism): the
+  // stable sources before the wait, the others after it; then reduce.
+  const bool row = t < tokens;
+  auto load_source = [&](int s) {
     const uint4* src = (s < nsrc_bank) ? bank + ((int64_t)s * tokens + t) * nv : partial + t * nv;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int i = lane + j * 32;
       x[s][j] = (i < nv) ? src[i] : make_uint4(0, 0, 0, 0);
     }
-  }
+  };
+#pragma unroll
+  for (int s = 0; s < NSRC; ++s)
+    if (row && s < stable) load_source(s);
+  pdl_wait();
+  if (!row) return;
+#pragma unroll
+  for (int s = 0; s < NSRC; ++s)
+    if (s >= stable) load_source(s);
   mix_token<VPL, NSRC, NORM>(RegRows<VPL, NSRC>{x}, wqr, nv, hidden, eps, lane, out + t * nv, &nwr, norm_eps);
 }
 
@@ -456,7 +468,8 @@ extern "C" int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t toke
       default: kern = attnres_reg_kernel<3, 10>; break;
     }
     e = launch_pdl(kern, grid, dim3(kMixWarps * 32), 0, as_stream(stream), (const uint4*)bank, (int)sources, tokens,
-                   (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out, (const uint4*)nullptr, 0.f);
+                   (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out, (const uint4*)nullptr, 0.f,
+                   0);
   } else {
     e = launch_pdl(attnres_generic_kernel, grid, dim3(kMixWarps * 32), 0, as_stream(stream), (const uint4*)bank,
                    (int)sources, tokens, (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out);
@@ -467,7 +480,8 @@ extern "C" int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t toke
 
 extern "C" int aiosb_attnres_mix_rmsnorm(const void* bank, int64_t sources, int64_t tokens, int64_t hidden,
                                          const void* partial, const float* weighted_query, float eps,
-                                         const void* norm_w, float norm_eps, void* out, void* stream) {
+                                         const void* norm_w, float norm_eps, int64_t stable_sources, void* out,
+                                         void* stream) {
   AIOSB_REQUIRE(sources >= 1 && tokens >= 1 && hidden >= 1, AIOSB_ERR_INVALID_ARG,
                 "bank dimensions must be positive");
   const int64_t total = sources + (partial != nullptr ? 1 : 0);
@@ -490,9 +504,11 @@ extern "C" int aiosb_attnres_mix_rmsnorm(const void* bank, int64_t sources, int6
     case 9: kern = attnres_reg_kernel<3, 9, true>; break;
     default: kern = attnres_reg_kernel<3, 10, true>; break;
   }
+  AIOSB_REQUIRE(stable_sources >= 0 && stable_sources <= sources, AIOSB_ERR_INVALID_ARG,
+                "attnres_mix_rmsnorm: stable_sources must be in [0, sources]");
   cudaError_t e = launch_pdl(kern, grid, dim3(kMixWarps * 32), 0, as_stream(stream), (const uint4*)bank, (int)sources,
                              tokens, (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out,
-                             (const uint4*)norm_w, norm_eps);
+                             (const uint4*)norm_w, norm_eps, (int)stable_sources);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attnres_mix_rmsnorm: %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }

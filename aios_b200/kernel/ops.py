@@ -193,10 +193,13 @@ def b200_attnres_mix_rmsnorm(
     norm_eps: float,
     *,
     output_buffer: torch.Tensor | None = None,
+    stable_sources: int = 0,
 ) -> torch.Tensor:
     """rmsnorm(b200_attnres_mix(bank, partial, weighted_query, eps)) * norm_weight
     in one kernel: the mixer and the RMSNorm that consumes its output in the Block
-    AttnRes layers. The mixer result itself is not returned."""
+    AttnRes layers. The mixer result itself is not returned. ``stable_sources``:
+    the first bank sources were written before the previous kernel on the stream
+    began, so the kernel may read them before waiting on it."""
     if not (bank.is_cuda and bank.dtype == torch.bfloat16 and bank.ndim == 3 and bank.is_contiguous()):
         raise ValueError("bank must be a contiguous CUDA bf16 [S,N,D] tensor")
     sources, tokens, hidden = bank.shape
@@ -213,7 +216,7 @@ def b200_attnres_mix_rmsnorm(
     _lib.call(
         "aiosb_attnres_mix_rmsnorm",
         bank.data_ptr(), sources, tokens, hidden, _ptr(partial), weighted_query.contiguous().data_ptr(), float(eps),
-        norm_weight.data_ptr(), float(norm_eps), output.data_ptr(), _stream(bank.device),
+        norm_weight.data_ptr(), float(norm_eps), int(stable_sources), output.data_ptr(), _stream(bank.device),
     )
     return output
 

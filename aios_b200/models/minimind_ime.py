@@ -68,13 +68,22 @@ class BlockAttnResMixer(BaseOP):
 
 
 def mix_and_norm(mixer: BlockAttnResMixer, norm: RMSNorm, bank: torch.Tensor, partial: torch.Tensor | None,
-                 output_buffer: torch.Tensor) -> torch.Tensor:
+                 output_buffer: torch.Tensor, stable: int = 0) -> torch.Tensor:
     """norm(mixer(bank, partial)): one kernel when the sources fit the fused form
-    (<= 10 sources, hidden <= 768), else the mixer and the norm kernels."""
+    (<= 10 sources, hidden <= 768), else the mixer and the norm kernels.
+
+    ``stable``: the first bank sources that were written before the previous
+    kernel on the stream began; the fused kernel reads them before waiting on it.
+    In the trunk every launch follows its predecessor's launch, and the qkv, the
+    attention and the gate/up kernels let their successors launch only after
+    their own wait; a mixer therefore starts after every kernel up to the last of
+    those has finished. That covers every bank source except one written by the
+    kernel just before the mixer: the embedding (block 0), or the down projection
+    that closed the previous block (the first mixer of a block, the final one)."""
     sources = bank.shape[0] + (partial is not None)
     if sources <= 10 and bank.shape[-1] <= 768 and bank.shape[-1] % 8 == 0:
         return ops.b200_attnres_mix_rmsnorm(bank, partial, mixer._routing_query(), mixer.key_norm.eps, norm.weight,
-                                           norm.eps, output_buffer=output_buffer)
+                                           norm.eps, output_buffer=output_buffer, stable_sources=stable)
     return norm.forward(mixer.forward(bank, partial, output_buffer=output_buffer))
 
 
@@ -99,15 +108,19 @@ class MiniMindAttnResDecoderLayer(BaseOP):
         mixed: torch.Tensor,
         out: torch.Tensor | None = None,
     ) -> torch.Tensor:
-        # the mixer writes the input-normalised rows straight away
-        normed = mix_and_norm(self.attn_res_mixer, self.input_layernorm, bank, partial, mixed)
+        # the mixer writes the input-normalised rows straight away; without a
+        # partial this is a block's first layer, whose newest bank source was
+        # written by the kernel just before
+        stable = bank.shape[0] if partial is not None else bank.shape[0] - 1
+        normed = mix_and_norm(self.attn_res_mixer, self.input_layernorm, bank, partial, mixed, stable)
         attn = self.self_attn.attend(normed, rotary, paged_kv_cache, batch)
         w_o = self.self_attn.o_proj.weight
         if partial is None:
             partial = ops.linear(attn, w_o)
         else:
             ops.linear(attn, w_o, out=partial, epilogue=_lib.EPI_ADD, residual=partial)
-        normed = mix_and_norm(self.mlp_res_mixer, self.post_attention_layernorm, bank, partial, mixed)
+        normed = mix_and_norm(self.mlp_res_mixer, self.post_attention_layernorm, bank, partial, mixed,
+                              bank.shape[0])
         act = self.mlp.gate_up_proj.forward_silu_mul(normed)
         target = partial if out is None else out
         ops.linear(act, self.mlp.down_proj.weight, out=target, epilogue=_lib.EPI_ADD, residual=partial)
@@ -162,7 +175,7 @@ class MiniMindBlockAttnResModel(BaseOP):
 
     def forward(self) -> torch.Tensor:
         bank, mixed = self._trunk()
-        return mix_and_norm(self.final_attn_res_mixer, self.norm, bank, None, mixed)
+        return mix_and_norm(self.final_attn_res_mixer, self.norm, bank, None, mixed, bank.shape[0] - 1)
 
 
 class MiniMindIMEForCausalLM(Qwen3ForCausalLM):

@@ -100,10 +100,14 @@ AIOSB_API int aiosb_attnres_mix(const void* bank, int64_t sources, int64_t token
  * each mixer; aios/layers/norm.py:10-22): out = bf16(h * rcp * norm_w), h the
  * bf16 mixer output of aiosb_attnres_mix, rcp = 1 / sqrt(mean(h^2) + norm_eps).
  * The mixer result itself is not written. sources + (partial != NULL) <= 10,
- * hidden <= 768 (a multiple of 8); norm_w: [hidden] bf16. */
+ * hidden <= 768 (a multiple of 8); norm_w: [hidden] bf16. stable_sources (in
+ * [0, sources]): the first bank sources that were written before the previous
+ * kernel on the stream began; the kernel reads them before waiting on that
+ * kernel (0: every read after the wait). */
 AIOSB_API int aiosb_attnres_mix_rmsnorm(const void* bank, int64_t sources, int64_t tokens, int64_t hidden,
                                         const void* partial, const float* weighted_query, float eps,
-                                        const void* norm_w, float norm_eps, void* out, void* stream);
+                                        const void* norm_w, float norm_eps, int64_t stable_sources, void* out,
+                                        void* stream);
 
 /* ---- RMSNorm ---------------------------------------------------------------
  * Replaces aios/layers/norm.py:10-22 (RMSNorm.forward / forward_inplace, the

@@ -190,6 +190,12 @@ def test_attnres_mix_rmsnorm_matches_mix_then_norm(cuda_device, sources: int, to
     fused = ops.b200_attnres_mix_rmsnorm(bank, part, wq, 1e-6, nw, 1e-6)
     want = ops.rmsnorm(ops.b200_attnres_mix(bank, part, wq, 1e-6), nw, 1e-6)
     _bf16_close(fused, want, ulps=1.0)
+    # stable bank sources read before the dependency wait: the same result, bit for bit
+    for stable in (sources - 1, sources):
+        early = ops.b200_attnres_mix_rmsnorm(bank, part, wq, 1e-6, nw, 1e-6, stable_sources=stable)
+        assert torch.equal(early, fused)
+    with pytest.raises(ValueError, match="stable_sources"):
+        ops.b200_attnres_mix_rmsnorm(bank, part, wq, 1e-6, nw, 1e-6, stable_sources=sources + 1)
 
 
 def test_attnres_mix_rejects_bad_layout(cuda_device) -> None:
