@@ -417,6 +417,72 @@ def prefill_gemm_sweep(llm, peaks: dict) -> dict:
     return out
 
 
+def decode_forward_roofline(engine, llm, peaks: dict) -> dict:
+    """The default decode forward (the chain of per-kernel launches the step graphs
+    replay, without the group step) of `llm` at 8 active rows on the first decode
+    position after the last keystroke's prefix (its prefix KV and page-table rows
+    are real), captured 5 times per graph and timed with CUDA events on the
+    launching stream. Algorithmic bytes: every weight once (the tied LM head once)
+    plus the attention's K/V reads and its q / o rows."""
+    from aios_b200.kernel import ops
+    from aios_b200.runtime.group import stage_class
+
+    rt = engine._runtime
+    dev = llm.device
+    cfg = llm.config
+    rows = 8
+    p_len = len(engine._prefix_slots)
+    kv = llm.mha_kv_cache
+    rt.active[:rows].fill_(1)
+    rt.positions[:rows].fill_(p_len)
+    rt.seq_lens[:rows].fill_(p_len + 1)
+    rt.row_table[:rows].copy_(torch.arange(rows, dtype=torch.int32, device=dev))
+    rt.prefix_len_view.fill_(p_len)
+    spare = torch.arange(kv.num_slots - rows, kv.num_slots, dtype=torch.int32, device=dev)  # unused pool tail
+    rt.out_loc[:rows].copy_(spare)
+    llm.ctx.page_table[:rows, p_len].copy_(spare)
+    rt.tokens[:rows].copy_(torch.arange(100, 100 + rows, dtype=torch.int32, device=dev))
+    batch = rt._decode_batch(rows, stage_class(p_len))
+
+    def forward():
+        with llm.ctx.forward_batch(batch):
+            llm.model.forward()
+
+    forward()
+    torch.cuda.synchronize(dev)
+    per_graph = 5
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(per_graph):
+            forward()
+    g.replay()
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    start.record(stream)
+    for _ in range(reps):
+        g.replay()
+    end.record(stream)
+    end.synchronize()
+    us = start.elapsed_time(end) / (reps * per_graph) * 1e3
+    del g
+    ops.check_status(dev)
+    rt.active.zero_()
+    layers = llm.model.model.layers.op_list
+    wbytes = sum(layer.self_attn.qkv_proj.weight.numel() + layer.self_attn.o_proj.weight.numel()
+                 + layer.mlp.gate_up_proj.weight.numel() + layer.mlp.down_proj.weight.numel() for layer in layers)
+    wbytes = 2 * (wbytes + llm.model.model.embed_tokens.weight.numel())
+    hkv, hd, hq = cfg.num_kv_heads, cfg.head_dim, cfg.num_qo_heads
+    attn_bytes = len(layers) * (p_len * hkv * hd * 2 * 2 + rows * hkv * hd * 2 * 2 + 2 * rows * hq * hd * 2)
+    total = wbytes + attn_bytes
+    achieved = total / (us * 1e-6) / 1e9
+    peak = peaks.get("hbm_gbs", HBM_FALLBACK_GBS)
+    return {"bound": "hbm", "us_per_step": round(us, 2), "algorithmic_bytes_per_step": total,
+            "weight_bytes": wbytes, "achieved_gbs": round(achieved, 1), "peak": peak,
+            "frac": round(achieved / peak, 4), "layers": len(layers), "prefix_tokens": p_len}
+
+
 def decode_step_roofline(engine, llm, peaks: dict) -> dict:
     """Times the persistent decode-step kernel alone (CUDA events on the launching
     stream, a graph of back-to-back launches): one decode forward of the bench
@@ -713,6 +779,9 @@ def config_sweeps(engine, llm, dev) -> dict:
         out["s10_prefix_sweep"][str(n)] = {"p50_ms": round(statistics.median(lat), 3),
                                            "p95_ms": round(percentile(lat, 0.95), 3)}
     out["decode_history"] = decode_history_crossover(engine, llm)
+    # the decode forward after one bench keystroke ([BOS]+12 prefix)
+    _latencies(engine, prefixes(llm.tokenizer, llm.config.vocab_size, 1, seed=1234), keystroke_config(), 0)
+    out["s10_decode_forward"] = decode_forward_roofline(engine, llm, measured_peaks())
     # the other shapes build their own LLM (each takes over the process-global
     # context), so they run after every keystroke of the S10 engine
     out["s06_keystroke"] = shape_keystroke("S06", dev)
@@ -725,7 +794,8 @@ def config_sweeps(engine, llm, dev) -> dict:
     lat = [r.latency_ms for r in res]
     out["s21_refill"] = {"p50_ms": round(statistics.median(lat), 3), "p95_ms": round(percentile(lat, 0.95), 3),
                          "attempts": res[0].sampling_attempts, "refill_rounds": res[0].refill_rounds,
-                         "decode_tok_s": round(sum(r.generated_tokens for r in res) / (sum(r.gpu_latency_ms for r in res) * 1e-3), 1)}
+                         "decode_tok_s": round(sum(r.generated_tokens for r in res) / (sum(r.gpu_latency_ms for r in res) * 1e-3), 1),
+                         "decode_forward": decode_forward_roofline(eng21, llm21, measured_peaks())}
     del eng21, llm21
     torch.cuda.empty_cache()
     return out
