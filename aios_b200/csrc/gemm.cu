@@ -793,3 +793,43 @@ extern "C" int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss,
   a.neps = eps;
   return linear_impl(a, nullptr, rows, k, w, n, stream);
 }
+
+extern "C" int aiosb_linear_attnres_rmsnorm(const void* bank, int64_t sources, int64_t stable_sources,
+                                            int64_t tokens, const void* partial, const float* weighted_query,
+                                            float mix_eps, const void* norm_w, float norm_eps, const void* w,
+                                            int64_t n, int64_t k, void* y, int64_t y_row_stride, int epilogue,
+                                            int32_t* status, void* stream) {
+  AIOSB_REQUIRE(epilogue == AIOSB_EPI_STORE || epilogue == AIOSB_EPI_SILU_MUL, AIOSB_ERR_INVALID_ARG,
+                "linear_attnres_rmsnorm: store or SwiGLU epilogue");
+  AIOSB_REQUIRE(n > 0 && n % 128 == 0, AIOSB_ERR_UNSUPPORTED, "linear_attnres_rmsnorm: n must be a multiple of 128");
+  const int64_t n_out = epilogue == AIOSB_EPI_SILU_MUL ? n / 2 : n;
+  AIOSB_REQUIRE(mix_eligible(tokens, k, n_out, sources, stable_sources, partial != nullptr), AIOSB_ERR_UNSUPPORTED,
+                "linear_attnres_rmsnorm: 1..8 rows, k == %d, <= %d sources with at most two read after the wait",
+                kMixMaxK, kMixMaxSources);
+  AIOSB_REQUIRE(bank && weighted_query && norm_w && w && y, AIOSB_ERR_INVALID_ARG,
+                "linear_attnres_rmsnorm: null pointer");
+  AIOSB_REQUIRE(aligned16(bank) && aligned16(norm_w) && aligned16(w) && aligned16(y) &&
+                    (partial == nullptr || aligned16(partial)) && y_row_stride >= n_out && y_row_stride % 8 == 0,
+                AIOSB_ERR_MISALIGNED, "linear_attnres_rmsnorm: 16-byte aligned operands and output rows");
+  GemvArgs g;
+  memset(&g, 0, sizeof(g));
+  g.nw = (const __nv_bfloat16*)norm_w;
+  g.eps = norm_eps;
+  g.w = (const __nv_bfloat16*)w;
+  g.n = n;
+  g.n_out = n_out;
+  g.k = k;
+  g.rows = (int)tokens;
+  g.y = (__nv_bfloat16*)y;
+  g.y_stride = y_row_stride;
+  g.epilogue = epilogue;
+  g.mix_bank = (const __nv_bfloat16*)bank;
+  g.mix_partial = (const __nv_bfloat16*)partial;
+  g.mix_wq = weighted_query;
+  g.mix_eps = mix_eps;
+  g.mix_sources = (int)sources;
+  g.mix_stable = (int)stable_sources;
+  g.mix_tokens = tokens;
+  (void)status;
+  return gemv_launch(g, as_stream(stream));
+}

@@ -62,8 +62,32 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 // instantiations (false) keep row 0 and streaming weight loads as constants, so
 // their register use (and with it how many CTAs share an SM with the previous
 // kernel's) is unchanged by the row-group addressing.
-template <int NT, int KB, bool STAT, bool GROUPS>
+// ---- AttnRes mixer operand (MODE kGemvMix) ----------------------------------
+// this lane's share of a source row's dot product with the routing query and of
+// its sum of squares (8 elements, in order)
+__device__ __forceinline__ void mix_sums(const uint4& v, const float (&wq)[8], float& dot, float& ss) {
+  const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float lo = bf16_lo(p[q]), hi = bf16_hi(p[q]);
+    dot += lo * wq[2 * q] + hi * wq[2 * q + 1];
+    ss += lo * lo + hi * hi;
+  }
+}
+// sums over the 4 lanes of a fragment row (lanes 4g .. 4g + 3)
+__device__ __forceinline__ void quad_sum2(float& x, float& y) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  y += __shfl_xor_sync(0xffffffffu, y, 1);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  y += __shfl_xor_sync(0xffffffffu, y, 2);
+}
+
+// MODE: 0 plain operand rows, 1 rows normalised from residual statistics,
+// 2 the AttnRes mixer's rows, normalised (kGemvMix).
+template <int NT, int KB, int MODE, bool GROUPS>
 __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a) {
+  constexpr bool STAT = MODE == kGemvStat, MIX = MODE == kGemvMix;
+  static_assert(!MIX || (NT == 1 && !GROUPS), "the mixer operand serves one 8-row group");
   constexpr int TM = NT * 8;  // token rows covered
   __shared__ float red[kGemvFeat][NT][32][4];  // [warp][n tile][lane][fragment]
   __shared__ float tile[TM][17];               // reduced [token][row] (padded)
@@ -109,10 +133,53 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
   uint4 wa[KB], wb[KB];
   load_w(blockIdx.x, wa, wb);
   uint4 nwv[KB];
-  if (STAT) {
+  if (STAT || MIX) {
 #pragma unroll
     for (int b = 0; b < KB; ++b)
       nwv[b] = b < kb ? *reinterpret_cast<const uint4*>(a.nw + kbase + b * 32) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  // MIX, before the wait: the stable bank sources' rows of this CTA's tokens go
+  // to shared memory, and this lane's partial dot products with the routing
+  // query and sums of squares of them to mpart
+  extern __shared__ __align__(16) uint8_t gemv_dyn[];
+  const int RS = K + kMixRowPad;  // staged row stride (elements): bank-conflict free 16-byte reads
+  __nv_bfloat16* mvals = reinterpret_cast<__nv_bfloat16*>(gemv_dyn);  // [stable][8][RS]
+  // then [warp][row][source][dot, ss] partial sums and [row][source] weights
+  float* mpart = reinterpret_cast<float*>(gemv_dyn + (size_t)(MIX ? a.mix_stable : 0) * 8 * RS * 2);
+  float* malpha = mpart + kGemvFeat * 8 * kMixMaxSources * 2;
+  auto mix_part = [&](int w, int row, int src) { return mpart + ((w * 8 + row) * kMixMaxSources + src) * 2; };
+  float wqv[MIX ? KB : 1][8];
+  if constexpr (MIX) {
+    const int ST = a.mix_stable;
+    const int nv8 = K / 8;
+    for (int u = tid; u < ST * 8 * nv8; u += kGemvThreads) {
+      const int sr = u / nv8, c = u % nv8, src = sr / 8, row = sr % 8;
+      if (row < T)
+        cp_async16(mvals + (int64_t)sr * RS + c * 8, a.mix_bank + ((int64_t)src * a.mix_tokens + row) * K + c * 8);
+    }
+#pragma unroll
+    for (int b = 0; b < KB; ++b)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wqv[b][e] = b < kb ? a.mix_wq[kbase + b * 32 + e] : 0.f;
+    cp_async_wait_all();
+    __syncthreads();
+    for (int src = 0; src < ST; ++src) {
+      float dot = 0.f, ss = 0.f;
+      if (g < T) {
+#pragma unroll
+        for (int b = 0; b < KB; ++b) {
+          if (b < kb) {
+            const uint4 v = *reinterpret_cast<const uint4*>(mvals + (int64_t)(src * 8 + g) * RS + kbase + b * 32);
+            mix_sums(v, wqv[b], dot, ss);
+          }
+        }
+      }
+      quad_sum2(dot, ss);
+      if (t4 == 0) {
+        mix_part(warp, g, src)[0] = dot;
+        mix_part(warp, g, src)[1] = ss;
+      }
+    }
   }
   // A residual-add linear (o, down) lets its successor launch at once: that
   // successor is a linear whose weights can stream in meanwhile (measured: 5.5 us
@@ -125,7 +192,125 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
 
   // ---- B fragments: token row n = nt * 8 + g, this lane's 8 elements per block
   uint4 xb[NT][KB];
-  if (!STAT) {
+  if constexpr (MIX) {
+    // the sources read after the wait: the newest bank source if it is not
+    // stable, and the partial (the block's running sum)
+    const int S = a.mix_sources, ST = a.mix_stable;
+    const int nlate = S - ST + (a.mix_partial != nullptr ? 1 : 0);  // <= 2 (host)
+    const int ntot = S + (a.mix_partial != nullptr ? 1 : 0);
+    uint4 late[2][KB];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const bool live = i < nlate && g < T;
+      const __nv_bfloat16* src = !live ? nullptr
+                                 : i < S - ST ? a.mix_bank + ((int64_t)(ST + i) * a.mix_tokens + g) * K
+                                              : a.mix_partial + (int64_t)g * K;
+#pragma unroll
+      for (int b = 0; b < KB; ++b)
+        late[i][b] = (live && b < kb) ? *reinterpret_cast<const uint4*>(src + kbase + b * 32)
+                                      : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      if (i < nlate) {
+        float dot = 0.f, ss = 0.f;
+#pragma unroll
+        for (int b = 0; b < KB; ++b)
+          if (b < kb) mix_sums(late[i][b], wqv[b], dot, ss);
+        quad_sum2(dot, ss);
+        if (t4 == 0) {
+          mix_part(warp, g, ST + i)[0] = dot;
+          mix_part(warp, g, ST + i)[1] = ss;
+        }
+      }
+    }
+    __syncthreads();
+    // depth softmax of token row `warp` (aios/kernel/attnres.py:8-127): every
+    // lane sums the 8 warps' partials of every source in warp order and takes
+    // score_s = dot_s / rms_s, the max, exp and their sum in source order, and
+    // the weights rounded to bf16, as the mixer kernel does
+    if (warp < T) {
+      float score[kMixMaxSources];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int s2 = 0; s2 < kMixMaxSources; ++s2) {
+        score[s2] = -INFINITY;
+        if (s2 < ntot) {
+          float dot = 0.f, ss = 0.f;
+#pragma unroll
+          for (int w = 0; w < kGemvFeat; ++w) {
+            dot += mix_part(w, warp, s2)[0];
+            ss += mix_part(w, warp, s2)[1];
+          }
+          score[s2] = dot * (1.0f / sqrtf(ss / (float)K + a.mix_eps));
+          mx = fmaxf(mx, score[s2]);
+        }
+      }
+      float denom = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < kMixMaxSources; ++s2) {
+        if (s2 < ntot) {
+          score[s2] = expf(score[s2] - mx);
+          denom += score[s2];
+        }
+      }
+      if (lane < ntot) {
+        float w8 = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < kMixMaxSources; ++s2)
+          if (s2 == lane) w8 = score[s2];
+        malpha[warp * kMixMaxSources + lane] = round_bf16(w8 / denom);
+      }
+    }
+    __syncthreads();
+    // h = bf16(sum_s alpha_s x_s) (fp32 accumulation in source order), then the
+    // RMSNorm that consumes it: bf16(h * rcp * nw)
+    float ssh = 0.f;
+    uint4 hx[KB];
+#pragma unroll
+    for (int b = 0; b < KB; ++b) {
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+      if (g < T && b < kb) {
+        for (int s2 = 0; s2 < ntot; ++s2) {
+          const float al = malpha[g * kMixMaxSources + s2];
+          uint4 v;
+          if (s2 < ST) v = *reinterpret_cast<const uint4*>(mvals + (int64_t)(s2 * 8 + g) * RS + kbase + b * 32);
+          else v = s2 - ST == 0 ? late[0][b] : late[1][b];
+          const uint32_t p[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            acc[2 * q] = fmaf(al, bf16_lo(p[q]), acc[2 * q]);
+            acc[2 * q + 1] = fmaf(al, bf16_hi(p[q]), acc[2 * q + 1]);
+          }
+        }
+      }
+      hx[b] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                         pack_bf16x2(acc[6], acc[7]));
+      const uint32_t hp[4] = {hx[b].x, hx[b].y, hx[b].z, hx[b].w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) ssh += bf16_lo(hp[q]) * bf16_lo(hp[q]) + bf16_hi(hp[q]) * bf16_hi(hp[q]);
+    }
+    ssh += __shfl_xor_sync(0xffffffffu, ssh, 1);
+    ssh += __shfl_xor_sync(0xffffffffu, ssh, 2);
+    if (t4 == 0) ssw[warp][g] = ssh;
+    __syncthreads();
+    float sst = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGemvFeat; ++w) sst += ssw[w][g];
+    const float rcp = 1.0f / sqrtf(sst / (float)K + a.eps);
+#pragma unroll
+    for (int b = 0; b < KB; ++b) {
+      const uint32_t hp[4] = {hx[b].x, hx[b].y, hx[b].z, hx[b].w};
+      const uint32_t w4[4] = {nwv[b].x, nwv[b].y, nwv[b].z, nwv[b].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        o[q] = pack_bf16x2(bf16_lo(hp[q]) * rcp * bf16_lo(w4[q]), bf16_hi(hp[q]) * rcp * bf16_hi(w4[q]));
+      xb[0][b] = (g < T) ? make_uint4(o[0], o[1], o[2], o[3]) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  } else if (!STAT) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const int n = nt * 8 + g;
@@ -277,22 +462,35 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
   }
 }
 
-template <int NT, int KB, bool STAT, bool GROUPS>
+template <int NT, int KB, int MODE, bool GROUPS>
 int launch_mma(const GemvArgs& a, cudaStream_t stream) {
-  auto kern = gemv_mma_kernel<NT, KB, STAT, GROUPS>;
+  auto kern = gemv_mma_kernel<NT, KB, MODE, GROUPS>;
   const int64_t tiles = a.n_out / (a.epilogue == AIOSB_EPI_SILU_MUL ? 8 : 16);
   // as many CTAs as can be resident at once (each prefetches its first tile's
   // weights before the wait; a CTA with more tiles loads the rest one ahead)
-  static int per_sm = 0;
-  if (per_sm == 0) {
+  // the mixer operand stages its stable bank rows in dynamic shared memory
+  const size_t dyn = MODE == kGemvMix ? mix_smem_bytes(a.mix_stable, a.k) : 0;
+  static int per_sm = 0;  // one dynamic size per instantiation but the mixer's
+  int resident_per_sm = per_sm;
+  if (MODE == kGemvMix) {
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)mix_smem_bytes(kMixMaxSources - 1, kMixMaxK));
+      attr_set = true;
+    }
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, dyn) != cudaSuccess || n < 1) n = 1;
+    resident_per_sm = n;
+  } else if (per_sm == 0) {
     int n = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kGemvThreads, 0) != cudaSuccess || n < 1) n = 2;
-    per_sm = n;
+    per_sm = resident_per_sm = n;
   }
   const int groups = (a.rows + NT * 8 - 1) / (NT * 8);  // token row groups (grid y)
-  const int64_t resident = std::max<int64_t>(1, (int64_t)per_sm * sm_count() / groups);
+  const int64_t resident = std::max<int64_t>(1, (int64_t)resident_per_sm * sm_count() / groups);
   const unsigned blocks = (unsigned)std::min<int64_t>(tiles, resident);
-  cudaError_t e = launch_pdl(kern, dim3(blocks, (unsigned)groups), dim3(kGemvThreads), 0, stream, a);
+  cudaError_t e = launch_pdl(kern, dim3(blocks, (unsigned)groups), dim3(kGemvThreads), dyn, stream, a);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "linear (gemv mma): %s", cudaGetErrorString(e));
   return AIOSB_OK;
 }
@@ -300,8 +498,10 @@ int launch_mma(const GemvArgs& a, cudaStream_t stream) {
 template <int NT, int KB>
 int launch_mma_rows(const GemvArgs& a, cudaStream_t stream) {
   if (a.rows > NT * 8)
-    return a.stat_x != nullptr ? launch_mma<NT, KB, true, true>(a, stream) : launch_mma<NT, KB, false, true>(a, stream);
-  return a.stat_x != nullptr ? launch_mma<NT, KB, true, false>(a, stream) : launch_mma<NT, KB, false, false>(a, stream);
+    return a.stat_x != nullptr ? launch_mma<NT, KB, kGemvStat, true>(a, stream)
+                               : launch_mma<NT, KB, kGemvPlain, true>(a, stream);
+  return a.stat_x != nullptr ? launch_mma<NT, KB, kGemvStat, false>(a, stream)
+                             : launch_mma<NT, KB, kGemvPlain, false>(a, stream);
 }
 
 bool g_gemv_enabled = [] {
@@ -320,12 +520,19 @@ int g_gemv_max_rows = [] {
   return v >= 1 && v <= kMaxGemvRows ? v : kGemvDefaultRows;
 }();
 
+bool mix_eligible(int64_t rows, int64_t k, int64_t n_out, int64_t sources, int64_t stable, bool partial) {
+  return g_gemv_enabled && rows >= 1 && rows <= 8 && k == kMixMaxK && n_out % 16 == 0 && sources >= 1 &&
+         stable >= 0 && stable <= sources && sources - stable + (partial ? 1 : 0) <= 2 &&
+         sources + (partial ? 1 : 0) <= kMixMaxSources;
+}
+
 bool gemv_eligible(int64_t rows, int64_t k, int64_t n_out) {
   return g_gemv_enabled && rows >= 1 && rows <= g_gemv_max_rows && k % 256 == 0 && k <= kMaxGemvK &&
          n_out % 16 == 0;
 }
 
 int gemv_launch(const GemvArgs& a, cudaStream_t stream) {
+  if (a.mix_bank != nullptr) return launch_mma<1, 3, kGemvMix, false>(a, stream);  // mix_eligible() holds
   const bool k3 = a.k <= 768;  // the 768-wide model dimension: 3 blocks per warp, fewer registers
   if (a.rows <= 8) return k3 ? launch_mma_rows<1, 3>(a, stream) : launch_mma_rows<1, kMaxGemvK / 256>(a, stream);
   return k3 ? launch_mma_rows<2, 3>(a, stream) : launch_mma_rows<2, kMaxGemvK / 256>(a, stream);

@@ -36,12 +36,33 @@ struct GemvArgs {
   float* out_stat_x;        // ADD: fp32 s [rows, n_out] and per-8-column sums of squares
   float* out_stat_ss;       // out_stat_ss[group * out_ss_stride + row], group = column / 8
   int64_t out_ss_stride;
+  // mixer mode (mix_bank != NULL): the operand rows are rmsnorm(AttnRes mix of the
+  // bank sources and the partial) * nw with eps, for rows <= 8 and k == 768
+  const __nv_bfloat16* mix_bank;     // [mix_sources, mix_tokens, k]
+  const __nv_bfloat16* mix_partial;  // [rows, k] or NULL
+  const float* mix_wq;               // [k] fp32 routing query (key-norm weight folded in)
+  float mix_eps;                     // the mixer's key-norm epsilon
+  int mix_sources;                   // bank sources
+  int mix_stable;                    // bank sources written before the previous kernel began
+  int64_t mix_tokens;                // rows of one bank source
 };
+
+// Mixer mode: at most this many sources (bank + partial), k of exactly kMixMaxK,
+// and staged bank rows padded by kMixRowPad elements.
+constexpr int kMixMaxSources = 10;
+constexpr int kMixMaxK = 768;
+constexpr int kMixRowPad = 32;
+constexpr int kGemvPlain = 0, kGemvStat = 1, kGemvMix = 2;  // operand modes
+inline size_t mix_smem_bytes(int64_t stable, int64_t k) {
+  return (size_t)stable * 8 * (size_t)(k + kMixRowPad) * 2 + (size_t)8 * 8 * kMixMaxSources * 2 * 4 +
+         (size_t)8 * kMixMaxSources * 4;
+}
 
 // Columns per sum-of-squares part written by the GEMV residual epilogue.
 constexpr int kGemvStatGroup = 8;
 
 bool gemv_eligible(int64_t rows, int64_t k, int64_t n_out);
+bool mix_eligible(int64_t rows, int64_t k, int64_t n_out, int64_t sources, int64_t stable, bool partial);
 int gemv_launch(const GemvArgs& a, cudaStream_t stream);
 
 }  // namespace aiosb

@@ -221,6 +221,51 @@ def b200_attnres_mix_rmsnorm(
     return output
 
 
+MIX_MAX_SOURCES = 10  # aiosb_linear_attnres_rmsnorm: bank + partial
+MIX_MAX_ROWS = 8
+
+
+def linear_attnres_rmsnorm_eligible(bank: torch.Tensor, partial: torch.Tensor | None, stable: int) -> bool:
+    sources, tokens, hidden = bank.shape
+    late = sources - stable + (partial is not None)
+    return (tokens <= MIX_MAX_ROWS and hidden == 768 and 0 <= stable <= sources and late <= 2
+            and sources + (partial is not None) <= MIX_MAX_SOURCES)
+
+
+def linear_attnres_rmsnorm(
+    bank: torch.Tensor,
+    partial: torch.Tensor | None,
+    stable_sources: int,
+    weighted_query: torch.Tensor,
+    mix_eps: float,
+    norm_weight: torch.Tensor,
+    norm_eps: float,
+    weight: torch.Tensor,
+    *,
+    epilogue: int = _lib.EPI_STORE,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """``linear(rmsnorm(attnres_mix(bank, partial)) * norm_weight, weight)`` in one
+    decode kernel (at most 8 tokens, hidden 768): the mixer's rows are built inside
+    the linear. The first ``stable_sources`` bank sources were written before the
+    previous kernel on the stream began."""
+    if not linear_attnres_rmsnorm_eligible(bank, partial, stable_sources):
+        raise ValueError("linear_attnres_rmsnorm: 1..8 tokens, hidden 768, <= 10 sources, <= 2 read late")
+    _require_cuda(bank, weighted_query, norm_weight, weight, what="linear_attnres_rmsnorm")
+    sources, tokens, hidden = bank.shape
+    n = weight.shape[0]
+    cols = n // 2 if epilogue == _lib.EPI_SILU_MUL else n
+    if out is None:
+        out = torch.empty((tokens, cols), dtype=bank.dtype, device=bank.device)
+    _lib.call(
+        "aiosb_linear_attnres_rmsnorm", bank.data_ptr(), sources, int(stable_sources), tokens, _ptr(partial),
+        weighted_query.contiguous().data_ptr(), float(mix_eps), norm_weight.data_ptr(), float(norm_eps),
+        weight.data_ptr(), n, hidden, out.data_ptr(), out.stride(0), epilogue, status_word(bank.device).data_ptr(),
+        _stream(bank.device),
+    )
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Norms / activations / embedding (aios/layers/{norm,activation,embedding}.py)
 # ---------------------------------------------------------------------------

@@ -9,6 +9,8 @@ the last layer of a block writes its partial straight into the bank slot.
 
 from __future__ import annotations
 
+import os
+
 from typing import TYPE_CHECKING
 
 import torch
@@ -67,6 +69,15 @@ class BlockAttnResMixer(BaseOP):
         )
 
 
+# AIOSB_FUSED_MIXER=1: in decode (<= 8 tokens) each layer's two mixers and the
+# RMSNorms after them run inside the qkv and gate/up linears
+# (aiosb_linear_attnres_rmsnorm). Off by default: every CTA of those linears then
+# stages the bank rows of all 8 tokens (up to 100 KB) and rebuilds the mixer's
+# rows, which measured slower than the mixer kernel it removes (S21 decode
+# forward 932 us against 603 us; refill keystroke 45.2 against 30.8 ms).
+_FUSED_MIXER = os.environ.get("AIOSB_FUSED_MIXER", "0") == "1"
+
+
 def mix_and_norm(mixer: BlockAttnResMixer, norm: RMSNorm, bank: torch.Tensor, partial: torch.Tensor | None,
                  output_buffer: torch.Tensor, stable: int = 0) -> torch.Tensor:
     """norm(mixer(bank, partial)): one kernel when the sources fit the fused form
@@ -108,20 +119,32 @@ class MiniMindAttnResDecoderLayer(BaseOP):
         mixed: torch.Tensor,
         out: torch.Tensor | None = None,
     ) -> torch.Tensor:
-        # the mixer writes the input-normalised rows straight away; without a
-        # partial this is a block's first layer, whose newest bank source was
-        # written by the kernel just before
+        # without a partial this is a block's first layer, whose newest bank
+        # source was written by the kernel just before
         stable = bank.shape[0] if partial is not None else bank.shape[0] - 1
-        normed = mix_and_norm(self.attn_res_mixer, self.input_layernorm, bank, partial, mixed, stable)
-        attn = self.self_attn.attend(normed, rotary, paged_kv_cache, batch)
+        mixer, norm = self.attn_res_mixer, self.input_layernorm
+        if _FUSED_MIXER and ops.linear_attnres_rmsnorm_eligible(bank, partial, stable):
+            # decode: the mixer and its norm inside the qkv projection
+            qkv = ops.linear_attnres_rmsnorm(bank, partial, stable, mixer._routing_query(), mixer.key_norm.eps,
+                                             norm.weight, norm.eps, self.self_attn.qkv_proj.weight)
+            attn = self.self_attn.attend_qkv(qkv, rotary, paged_kv_cache, batch)
+        else:
+            # the mixer writes the input-normalised rows straight away
+            normed = mix_and_norm(mixer, norm, bank, partial, mixed, stable)
+            attn = self.self_attn.attend(normed, rotary, paged_kv_cache, batch)
         w_o = self.self_attn.o_proj.weight
         if partial is None:
             partial = ops.linear(attn, w_o)
         else:
             ops.linear(attn, w_o, out=partial, epilogue=_lib.EPI_ADD, residual=partial)
-        normed = mix_and_norm(self.mlp_res_mixer, self.post_attention_layernorm, bank, partial, mixed,
-                              bank.shape[0])
-        act = self.mlp.gate_up_proj.forward_silu_mul(normed)
+        mixer, norm = self.mlp_res_mixer, self.post_attention_layernorm
+        if _FUSED_MIXER and ops.linear_attnres_rmsnorm_eligible(bank, partial, bank.shape[0]):
+            act = ops.linear_attnres_rmsnorm(bank, partial, bank.shape[0], mixer._routing_query(),
+                                             mixer.key_norm.eps, norm.weight, norm.eps,
+                                             self.mlp.gate_up_proj.packed_weight(), epilogue=_lib.EPI_SILU_MUL)
+        else:
+            normed = mix_and_norm(mixer, norm, bank, partial, mixed, bank.shape[0])
+            act = self.mlp.gate_up_proj.forward_silu_mul(normed)
         target = partial if out is None else out
         ops.linear(act, self.mlp.down_proj.weight, out=target, epilogue=_lib.EPI_ADD, residual=partial)
         return target

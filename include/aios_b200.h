@@ -206,6 +206,24 @@ AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, 
                                      const void* residual, int64_t residual_stride, int32_t* status,
                                      void* stream);
 
+/* Decode linear on the Block AttnRes mixer's normalised rows (replaces
+ * BlockAttnResMixer.forward + RMSNorm.forward + Linear.forward,
+ * aios/models/minimind_ime.py:162-190,237-252, aios/kernel/attnres.py:8-127):
+ * y = epilogue(bf16(h * rcp * norm_w) W^T) with h = bf16(sum_s alpha_s x_s), the
+ * sources x_s being bank [sources, tokens, k] and then partial [tokens, k] (when
+ * not NULL), alpha = bf16(softmax_s(dot(x_s, weighted_query) / rms(x_s, mix_eps))),
+ * rcp = 1 / sqrt(mean(h^2) + norm_eps). The mixer's rows exist only inside the
+ * linear's CTAs: every CTA stages the first stable_sources bank sources (written
+ * before the previous kernel on the stream began) before waiting on that kernel,
+ * and reads the others after it. Decode widths only: 1..8 tokens, k == 768,
+ * sources + (partial != NULL) <= 10, at most two of them read after the wait;
+ * epilogue AIOSB_EPI_STORE or AIOSB_EPI_SILU_MUL (packed gate/up weights). */
+AIOSB_API int aiosb_linear_attnres_rmsnorm(const void* bank, int64_t sources, int64_t stable_sources,
+                                           int64_t tokens, const void* partial, const float* weighted_query,
+                                           float mix_eps, const void* norm_w, float norm_eps, const void* w,
+                                           int64_t n, int64_t k, void* y, int64_t y_row_stride, int epilogue,
+                                           int32_t* status, void* stream);
+
 /* ---- Attention ---------------------------------------------------------------
  * KV slots: token slot s of one layer lives at k_cache + s * num_kv_heads *
  * head_dim (the MHAKVCache layout [pages, page_size, Hkv, d] flattened); slot

@@ -198,6 +198,39 @@ def test_attnres_mix_rmsnorm_matches_mix_then_norm(cuda_device, sources: int, to
         ops.b200_attnres_mix_rmsnorm(bank, part, wq, 1e-6, nw, 1e-6, stable_sources=sources + 1)
 
 
+@pytest.mark.parametrize("sources,stable,tokens,partial,silu", [
+    (1, 0, 8, False, False),   # block 0, first layer: the embedding just written
+    (1, 1, 8, True, True),
+    (4, 3, 8, False, False),   # a block's first layer: the newest source read late
+    (4, 4, 8, True, False),
+    (8, 8, 8, True, True),     # the last block
+    (9, 8, 5, False, True),    # the final-mixer shape, ragged rows
+    (3, 3, 1, True, False),
+])
+def test_linear_attnres_rmsnorm_matches_mix_then_linear(cuda_device, sources, stable, tokens, partial, silu) -> None:
+    """The mixer and its RMSNorm built inside the decode linear equal the mixer
+    kernel followed by the linear, to the rounding of the depth weights (their
+    dot products and sums of squares are reduced in another order)."""
+    g = torch.Generator().manual_seed(71 + sources * 8 + tokens + stable)
+    dev = cuda_device
+    bank = torch.randn(sources, tokens, 768, generator=g).to(torch.bfloat16).to(dev)
+    part = torch.randn(tokens, 768, generator=g).to(torch.bfloat16).to(dev) if partial else None
+    wq = (torch.randn(768, generator=g) * 0.05).to(dev)
+    nw = (1.0 + 0.1 * torch.randn(768, generator=g)).to(torch.bfloat16).to(dev)
+    n = 4096 if silu else 1280
+    w = (torch.randn(n, 768, generator=g) * 0.02).to(torch.bfloat16).to(dev)
+    wk = ops.pack_gate_up(w) if silu else w
+    epi = _lib.EPI_SILU_MUL if silu else _lib.EPI_STORE
+    y = ops.linear_attnres_rmsnorm(bank, part, stable, wq, 1e-6, nw, 1e-6, wk, epilogue=epi)
+    normed = ops.b200_attnres_mix_rmsnorm(bank, part, wq, 1e-6, nw, 1e-6)
+    ref = ops.linear(normed, wk, epilogue=epi)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    _bf16_close(y, ref, ulps=3.0, atol=2e-3)
+    with pytest.raises(ValueError):
+        ops.linear_attnres_rmsnorm(bank, part, -1, wq, 1e-6, nw, 1e-6, wk, epilogue=epi)
+
+
 def test_attnres_mix_rejects_bad_layout(cuda_device) -> None:
     bank = torch.zeros(2, 3, 768, dtype=torch.bfloat16, device=cuda_device)
     wq = torch.zeros(768, device=cuda_device)
