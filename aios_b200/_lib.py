@@ -148,6 +148,7 @@ _SIGNATURES = {
     "aiosb_kv_store": ([_p, _p, _i64, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _p, _p], _i32),
     "aiosb_attnres_mix": ([_p, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _p], _i32),
     "aiosb_attnres_mix_rmsnorm": ([_p, _i64, _i64, _i64, _p, _p, _f32, _p, _f32, _i64, _p, _p], _i32),
+    "aiosb_test_attnres_stream_stall": ([_i64, ctypes.c_uint64], _i32),
     "aiosb_linear_attnres_rmsnorm": (
         [_p, _i64, _i64, _i64, _p, _p, _f32, _p, _f32, _p, _i64, _i64, _p, _i64, _i32, _p, _p], _i32
     ),

@@ -240,7 +240,8 @@ template <int VPL, int NSRC, int G>
 __global__ void __launch_bounds__((1 + kStreamTok * G) * 32, 1)
     attnres_stream_kernel(const uint4* __restrict__ bank, int nsrc_bank, int64_t tokens, int hidden,
                           const uint4* __restrict__ partial, const float* __restrict__ wq, float eps,
-                          uint4* __restrict__ out, int spg, int32_t* status) {
+                          uint4* __restrict__ out, int spg, int32_t* status, int64_t stall_tile,
+                          uint64_t wait_ns) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ uint64_t full[kStreamMaxStages], empty[kStreamMaxStages];
   __shared__ int abort_flag;
@@ -279,7 +280,7 @@ __global__ void __launch_bounds__((1 + kStreamTok * G) * 32, 1)
       for (; i < my_tiles; ++i) {
         const int st = stage_of(i);
         const uint32_t use = use_of(i);
-        if (use >= 1 && !mbar_wait(&empty[st], (use - 1) & 1)) {
+        if (use >= 1 && !mbar_wait_for(&empty[st], (use - 1) & 1, wait_ns)) {
           atomicExch(&abort_flag, 1);
           break;
         }
@@ -288,6 +289,9 @@ __global__ void __launch_bounds__((1 + kStreamTok * G) * 32, 1)
         const int64_t tt = tokens - t0 < kStreamTok ? tokens - t0 : kStreamTok;
         const uint32_t bytes = (uint32_t)(tt * row_bytes);
         mbar_arrive_expect_tx(&full[st], NSRC * bytes);
+        // test hook: CTA 0 announces tile `stall_tile` but never copies it, so
+        // its consumers' bounded wait runs out (no fault: nothing is in flight)
+        if (blockIdx.x == 0 && i == stall_tile) continue;
         uint8_t* dst = smem_raw + st * stage_bytes;
 #pragma unroll
         for (int s = 0; s < NSRC; ++s) {
@@ -304,7 +308,7 @@ __global__ void __launch_bounds__((1 + kStreamTok * G) * 32, 1)
       const int st = stage_of(i);
       const uint32_t use = use_of(i);
       const int64_t t = ((int64_t)blockIdx.x + i * gridDim.x) * kStreamTok + tok;
-      const bool ready = mbar_wait(&full[st], use & 1) && !*reinterpret_cast<volatile int*>(&abort_flag);
+      const bool ready = mbar_wait_for(&full[st], use & 1, wait_ns) && !*reinterpret_cast<volatile int*>(&abort_flag);
       if (!ready) {
         atomicExch(&abort_flag, 1);
         for (int64_t k = i; k < my_tiles; k += G) {
@@ -330,7 +334,8 @@ __global__ void __launch_bounds__((1 + kStreamTok * G) * 32, 1)
   if (threadIdx.x == 0 && abort_flag) {
     report(status, AIOSB_DEV_WAIT_TIMEOUT);
     const int64_t n = issued_tiles;
-    for (int64_t j = n > stages ? n - stages : 0; j < n; ++j) mbar_wait(&full[stage_of(j)], use_of(j) & 1);
+    for (int64_t j = n > stages ? n - stages : 0; j < n; ++j)
+      if (!(blockIdx.x == 0 && j == stall_tile)) mbar_wait_for(&full[stage_of(j)], use_of(j) & 1, wait_ns);
   }
 }
 
@@ -389,6 +394,14 @@ __global__ void __launch_bounds__(kMixWarps * 32)
   }
 }
 
+// Test hook of the stream kernel (aiosb_test_attnres_stream_stall): a tile whose
+// copies CTA 0 skips, and the bound of every wait.
+struct StreamTest {
+  int64_t stall_tile = -1;
+  uint64_t wait_ns = kWaitLimitNs;
+};
+StreamTest g_stream_test;
+
 template <int G>
 cudaError_t launch_stream(int64_t total, const void* bank, int64_t sources, int64_t tokens, int64_t hidden,
                           const void* partial, const float* wq, float eps, void* out, int spg, int32_t* status,
@@ -411,7 +424,8 @@ cudaError_t launch_stream(int64_t total, const void* bank, int64_t sources, int6
   const int64_t tiles = (tokens + kStreamTok - 1) / kStreamTok;
   const dim3 grid((unsigned)std::min<int64_t>(tiles, sm_count()));
   return launch_pdl(kern, grid, dim3((1 + kStreamTok * G) * 32), smem, as_stream(stream), (const uint4*)bank,
-                    (int)sources, tokens, (int)hidden, (const uint4*)partial, wq, eps, (uint4*)out, spg, status);
+                    (int)sources, tokens, (int)hidden, (const uint4*)partial, wq, eps, (uint4*)out, spg, status,
+                    g_stream_test.stall_tile, g_stream_test.wait_ns);
 }
 
 // Token count from which the stream kernel replaces the register kernel
@@ -510,5 +524,11 @@ extern "C" int aiosb_attnres_mix_rmsnorm(const void* bank, int64_t sources, int6
                              tokens, (int)hidden, (const uint4*)partial, weighted_query, eps, (uint4*)out,
                              (const uint4*)norm_w, norm_eps, (int)stable_sources);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "attnres_mix_rmsnorm: %s", cudaGetErrorString(e));
+  return AIOSB_OK;
+}
+
+extern "C" int aiosb_test_attnres_stream_stall(int64_t stall_tile, uint64_t wait_limit_ns) {
+  g_stream_test.stall_tile = stall_tile;
+  g_stream_test.wait_ns = wait_limit_ns > 0 ? wait_limit_ns : kWaitLimitNs;
   return AIOSB_OK;
 }

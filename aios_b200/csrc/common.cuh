@@ -125,14 +125,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false (and leaves the barrier untouched) after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Bounded wait: returns false (and leaves the barrier untouched) after limit_ns.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - start > kWaitLimitNs) return false;
+    if (global_ns() - start > limit_ns) return false;
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait_for(bar, parity, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------------

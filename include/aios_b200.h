@@ -109,6 +109,13 @@ AIOSB_API int aiosb_attnres_mix_rmsnorm(const void* bank, int64_t sources, int64
                                         const void* norm_w, float norm_eps, int64_t stable_sources, void* out,
                                         void* stream);
 
+/* Test hook, not for production callers: the next launches of the mixer's
+ * stream kernel (aiosb_attnres_mix from 2048 tokens) have CTA 0 announce its
+ * tile `stall_tile` without copying it, and bound every wait by wait_limit_ns
+ * (0: the default 2 s), so that a bounded mbarrier wait runs out and the kernel
+ * reports AIOSB_DEV_WAIT_TIMEOUT. stall_tile < 0 restores normal operation. */
+AIOSB_API int aiosb_test_attnres_stream_stall(int64_t stall_tile, uint64_t wait_limit_ns);
+
 /* ---- RMSNorm ---------------------------------------------------------------
  * Replaces aios/layers/norm.py:10-22 (RMSNorm.forward / forward_inplace, the
  * FlashInfer rmsnorm). Normalises rows of `hidden` elements:

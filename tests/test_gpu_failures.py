@@ -7,7 +7,12 @@ still usable afterwards (no fault, trap or hang is caused on the device).
   sufficient pool steps normally. The reference raises NotImplementedError in
   the same situation on the host (aios/scheduler/cache.py:46-51); the device
   step cannot raise, so it stops the group and reports.
-* The decode-step bounded wait is covered by tests/test_gpu_decode_step.py.
+* A bounded mbarrier wait that runs out: the mixer's stream kernel with a
+  test hook that announces one tile without copying it (nothing is in flight,
+  so nothing can fault) and a 2 ms wait bound reports AIOSB_DEV_WAIT_TIMEOUT,
+  writes NaN into the rows it could not mix, and the next launch without the
+  hook is exact again.
+* The decode-step bounded flag wait is covered by tests/test_gpu_decode_step.py.
 """
 
 from __future__ import annotations
@@ -72,3 +77,29 @@ def test_exhausted_free_list_reports_pool_empty_and_ends_the_group(cuda_device) 
     assert int(ok["status"][0]) == 0
     assert st.done == 0 and st.head == ROWS  # one slot per row, in FIFO order
     assert ok["out_loc"].tolist() == list(range(ROWS))
+
+
+def test_mixer_stream_wait_that_runs_out_reports_and_recovers(cuda_device) -> None:
+    from aios_b200.kernel import ops
+
+    g = torch.Generator(device=cuda_device).manual_seed(5)
+    tokens = 4096  # the stream kernel (from 2048 tokens)
+    bank = torch.randn(4, tokens, 768, generator=g, device=cuda_device).to(torch.bfloat16)
+    part = torch.randn(tokens, 768, generator=g, device=cuda_device).to(torch.bfloat16)
+    wq = torch.randn(768, generator=g, device=cuda_device) * 0.02
+    good = ops.b200_attnres_mix(bank, part, wq, 1e-6)
+    torch.cuda.synchronize(cuda_device)
+    ops.check_status(cuda_device)
+    _lib.call("aiosb_test_attnres_stream_stall", 0, 2_000_000)
+    try:
+        bad = ops.b200_attnres_mix(bank, part, wq, 1e-6)
+        torch.cuda.synchronize(cuda_device)
+    finally:
+        _lib.call("aiosb_test_attnres_stream_stall", -1, 0)
+    with pytest.raises(RuntimeError, match="wait"):
+        ops.check_status(cuda_device)
+    assert bool(torch.isnan(bad[:4].float()).all())  # CTA 0's first tile was never mixed
+    again = ops.b200_attnres_mix(bank, part, wq, 1e-6)
+    torch.cuda.synchronize(cuda_device)
+    ops.check_status(cuda_device)
+    assert torch.equal(again, good)
