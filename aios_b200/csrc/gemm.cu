@@ -365,52 +365,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t rank = split > 1 ? cluster_ctarank() : 0u;
     const uint32_t red_addr = smem_u32(red);
     const int64_t t0 = (int64_t)n_tile * BN;
-    // A thread's partial-tile reads (local, or a peer's over distributed shared
-    // memory) are issued kG units at a time, so that a group costs one DSMEM
-    // round trip per rank instead of one per unit; every unit still sums the
-    // ranks in rank order.
-    constexpr int kG = 8;
+    // One unit per thread per iteration, four iterations unrolled so that their
+    // partial-tile reads (local, or a peer's over distributed shared memory) are
+    // in flight together; every unit sums the ranks in rank order. (An earlier
+    // form that batched units through arrays and per-unit liveness flags ran
+    // the split-1 epilogue of a 256-token tile in 8.2 us instead of 2.4 us.)
     auto part = [&](uint32_t off, int q) -> float4 {
       if (split > 1) return ld_dsmem_f4(map_shared_rank(red_addr + off, (uint32_t)q));
       return *reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(red) + off);
     };
     if (a.epilogue == AIOSB_EPI_STORE || a.epilogue == AIOSB_EPI_ADD) {
-      // unit idx: column c = idx / 32 (a token), 4 tile rows m4 * 4.. (32 per column);
-      // rank r owns the columns c % split == r
-      const int own = (BN + split - 1 - (int)rank) / split;  // columns of this rank
-      const int units = own * 32;
-      for (int u0 = tid; u0 < units; u0 += kThreads * kG) {
-        float4 acc[kG];
-        uint32_t off[kG];
-        bool live[kG];
-#pragma unroll
-        for (int j = 0; j < kG; ++j) {
-          const int u = u0 + j * kThreads;
-          const int c = (u >> 5) * split + (int)rank, m4 = u & 31;
-          live[j] = u < units && t0 + c < a.rows;
-          off[j] = (uint32_t)((c * kBM + m4 * 4) * 4);
-          acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        for (int q = 0; q < split; ++q) {
-          float4 p[kG];
-#pragma unroll
-          for (int j = 0; j < kG; ++j)
-            if (live[j]) p[j] = part(off[j], q);
-#pragma unroll
-          for (int j = 0; j < kG; ++j) {
-            if (live[j]) {
-              acc[j].x += p[j].x; acc[j].y += p[j].y; acc[j].z += p[j].z; acc[j].w += p[j].w;
-            }
+      // unit u: column c = (u / 32) * split + rank (a token; rank r owns the
+      // columns c % split == r), tile rows m4 * 4 .. m4 * 4 + 3
+      const int own = (BN + split - 1 - (int)rank) / split;
+#pragma unroll 4
+      for (int u = tid; u < own * 32; u += kThreads) {
+        const int c = (u >> 5) * split + (int)rank, m4 = u & 31;
+        const int64_t t = t0 + c;
+        if (t < a.rows) {  // warp-uniform: a warp's 32 units share a column
+          const uint32_t off = (uint32_t)((c * kBM + m4 * 4) * 4);
+          float4 v = part(off, 0);
+          for (int q = 1; q < split; ++q) {
+            const float4 p = part(off, q);
+            v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
           }
-        }
-#pragma unroll
-        for (int j = 0; j < kG; ++j) {
-          const int u = u0 + j * kThreads;
-          const int c = (u >> 5) * split + (int)rank, m4 = u & 31;
-          // whole warps share a column (32 units), so `live` is warp-uniform here
-          if (!live[j]) continue;
-          const int64_t t = t0 + c;
-          float4 v = acc[j];
           __nv_bfloat16* dst = a.y + t * a.y_row_stride + (int64_t)m_tile * kBM + m4 * 4;
           if (a.epilogue == AIOSB_EPI_ADD) {
             // residual + delta with the delta rounded to bf16 first, as the
@@ -434,48 +412,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
       // SILU_MUL: tile rows 0..63 are gate rows, 64..127 the matching up rows;
-      // unit idx: column c = idx / 16, 4 gate rows m4 * 4.. and their up rows
+      // unit u: column c = (u / 16) * split + rank, 4 gate rows m4 * 4 .. and their up rows
       const int own = (BN + split - 1 - (int)rank) / split;
-      const int units = own * 16;
-      for (int u0 = tid; u0 < units; u0 += kThreads * kG) {
-        float4 g[kG], up[kG];
-        uint32_t og[kG];
-        bool live[kG];
-#pragma unroll
-        for (int j = 0; j < kG; ++j) {
-          const int u = u0 + j * kThreads;
-          const int c = (u >> 4) * split + (int)rank, m4 = u & 15;
-          live[j] = u < units && t0 + c < a.rows;
-          og[j] = (uint32_t)((c * kBM + m4 * 4) * 4);
-          g[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-          up[j] = g[j];
-        }
-        for (int q = 0; q < split; ++q) {
-          float4 pg[kG], pu[kG];
-#pragma unroll
-          for (int j = 0; j < kG; ++j) {
-            if (live[j]) {
-              pg[j] = part(og[j], q);
-              pu[j] = part(og[j] + 64 * 4, q);
-            }
+#pragma unroll 4
+      for (int u = tid; u < own * 16; u += kThreads) {
+        const int c = (u >> 4) * split + (int)rank, m4 = u & 15;
+        const int64_t t = t0 + c;
+        if (t < a.rows) {
+          const uint32_t og = (uint32_t)((c * kBM + m4 * 4) * 4), ou = og + 64 * 4;
+          float4 g = part(og, 0), up = part(ou, 0);
+          for (int q = 1; q < split; ++q) {
+            const float4 pg = part(og, q), pu = part(ou, q);
+            g.x += pg.x; g.y += pg.y; g.z += pg.z; g.w += pg.w;
+            up.x += pu.x; up.y += pu.y; up.z += pu.z; up.w += pu.w;
           }
-#pragma unroll
-          for (int j = 0; j < kG; ++j) {
-            if (live[j]) {
-              g[j].x += pg[j].x; g[j].y += pg[j].y; g[j].z += pg[j].z; g[j].w += pg[j].w;
-              up[j].x += pu[j].x; up[j].y += pu[j].y; up[j].z += pu[j].z; up[j].w += pu[j].w;
-            }
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < kG; ++j) {
-          if (!live[j]) continue;
-          const int u = u0 + j * kThreads;
-          const int c = (u >> 4) * split + (int)rank, m4 = u & 15;
-          const int64_t t = t0 + c;
           // gate_up output is bf16 before silu_and_mul (aios/models/qwen3.py:90-92).
-          const float gv[4] = {round_bf16(g[j].x), round_bf16(g[j].y), round_bf16(g[j].z), round_bf16(g[j].w)};
-          const float uv[4] = {round_bf16(up[j].x), round_bf16(up[j].y), round_bf16(up[j].z), round_bf16(up[j].w)};
+          const float gv[4] = {round_bf16(g.x), round_bf16(g.y), round_bf16(g.z), round_bf16(g.w)};
+          const float uv[4] = {round_bf16(up.x), round_bf16(up.y), round_bf16(up.z), round_bf16(up.w)};
           float r[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) r[e] = gv[e] / (1.0f + expf(-gv[e])) * uv[e];
