@@ -74,7 +74,8 @@ class BlockAttnResMixer(BaseOP):
 # (aiosb_linear_attnres_rmsnorm). Off by default: every CTA of those linears then
 # stages the bank rows of all 8 tokens (up to 100 KB) and rebuilds the mixer's
 # rows, which measured slower than the mixer kernel it removes (S21 decode
-# forward 932 us against 603 us; refill keystroke 45.2 against 30.8 ms).
+# forward 932 us against 603 us; refill keystroke 45.2 against 30.8 ms; still
+# 635 against 612 us when only mixers of at most 2 sources are fused).
 _FUSED_MIXER = os.environ.get("AIOSB_FUSED_MIXER", "0") == "1"
 
 
