@@ -112,6 +112,7 @@ class GroupPtrs(ctypes.Structure):
         ("page_table", _p),
         ("ring", _p),
         ("status", _p),
+        ("tile_stats", _p),
     ]
 
 
@@ -149,6 +150,10 @@ _SIGNATURES = {
     "aiosb_attnres_mix": ([_p, _i64, _i64, _i64, _p, _p, _f32, _p, _p, _p], _i32),
     "aiosb_attnres_mix_rmsnorm": ([_p, _i64, _i64, _i64, _p, _p, _f32, _p, _f32, _i64, _p, _p], _i32),
     "aiosb_test_attnres_stream_stall": ([_i64, ctypes.c_uint64], _i32),
+    "aiosb_linear_tile_stats_eligible": ([_i64, _i64, _i64], _i32),
+    "aiosb_linear_stat_norm_tiles": (
+        [_p, _p, _i64, _i64, _p, _f32, _i64, _i64, _p, _i64, _p, _i64, _p, _p, _p], _i32
+    ),
     "aiosb_linear_attnres_rmsnorm": (
         [_p, _i64, _i64, _i64, _p, _p, _f32, _p, _f32, _p, _i64, _i64, _p, _i64, _i32, _p, _p], _i32
     ),
@@ -250,7 +255,7 @@ def check(rc: int, what: str) -> None:
 # (the bench reports it as the number of this library's kernel launches).
 _NON_LAUNCHING = frozenset({"aiosb_version", "aiosb_last_error", "aiosb_host_device_pointer",
                             "aiosb_prefill_tile_tokens", "aiosb_decode_step_sync_words",
-                            "aiosb_decode_step_work_bytes"})
+                            "aiosb_decode_step_work_bytes", "aiosb_linear_tile_stats_eligible"})
 launches = 0
 
 

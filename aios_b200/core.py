@@ -82,6 +82,11 @@ class Batch:
     # Optional preallocated [rows, vocab] buffer the LM head writes into (lets a
     # captured decode step leave its logits where the next sampling step reads).
     logits_out: torch.Tensor | None = None
+    # Optional [vocab / 16, rows, 4] fp32 buffer for the LM head's per-16-id tile
+    # statistics of the logits (a decode step whose sampler reads them); the LM
+    # head sets tile_stats_written when it filled it.
+    tile_stats_out: torch.Tensor | None = None
+    tile_stats_written: bool = False
 
     @property
     def is_prefill(self) -> bool:

@@ -74,6 +74,9 @@ struct GemmArgs {
   // uses 0, so that early-launched dependent CTAs (each holding an SM's shared
   // memory while it waits) do not take the SMs its later waves need.
   int early_dependents;
+  // register-operand path, store epilogue: per 16-column tile statistics of the
+  // output (see GemvArgs::tile_stats); the tcgen05 path does not write them
+  float4* tile_stats;
 };
 
 constexpr int kMaxNormRows = 64;
@@ -578,6 +581,7 @@ int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* 
     g.out_stat_x = a.out_stat_x;
     g.out_stat_ss = a.out_stat_ss;
     g.out_ss_stride = a.out_ss_stride;
+    g.tile_stats = a.tile_stats;
     return gemv_launch(g, as_stream(stream));
   }
   auto plan = [&]() {
@@ -744,6 +748,37 @@ extern "C" int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss,
   a.stat_parts = (int)parts;
   a.nw = (const __nv_bfloat16*)norm_w;
   a.neps = eps;
+  return linear_impl(a, nullptr, rows, k, w, n, stream);
+}
+
+extern "C" int aiosb_linear_tile_stats_eligible(int64_t rows, int64_t k, int64_t n) {
+  return tile_stats_eligible(rows, k, n) ? 1 : 0;
+}
+
+extern "C" int aiosb_linear_stat_norm_tiles(const float* stat_x, const float* stat_ss, int64_t stat_ss_stride,
+                                            int64_t parts, const void* norm_w, float eps, int64_t rows, int64_t k,
+                                            const void* w, int64_t n, void* y, int64_t y_row_stride,
+                                            float* tile_stats, int32_t* status, void* stream) {
+  AIOSB_REQUIRE(tile_stats != nullptr && aligned16(tile_stats), AIOSB_ERR_MISALIGNED,
+                "linear_stat_norm_tiles: tile_stats must be 16-byte aligned");
+  AIOSB_REQUIRE(tile_stats_eligible(rows, k, n), AIOSB_ERR_UNSUPPORTED,
+                "linear_stat_norm_tiles: only on the register-operand path with rows <= 16, k <= 768, k %% 256 == 0");
+  int rc = check_common(w, rows, k, n, y, y_row_stride, AIOSB_EPI_STORE, nullptr, 0);
+  if (rc != AIOSB_OK) return rc == 1 ? AIOSB_OK : rc;
+  AIOSB_REQUIRE(parts >= 1 && parts <= kMaxStatParts, AIOSB_ERR_INVALID_ARG,
+                "linear_stat_norm_tiles: parts must be in [1, %d]", kMaxStatParts);
+  AIOSB_REQUIRE(stat_ss_stride >= rows, AIOSB_ERR_INVALID_ARG, "linear_stat_norm_tiles: stat_ss stride below rows");
+  AIOSB_REQUIRE(stat_x && stat_ss && norm_w && aligned16(stat_x) && aligned16(norm_w), AIOSB_ERR_MISALIGNED,
+                "linear_stat_norm_tiles: stat_x and norm_w must be 16-byte aligned, stat_ss non-null");
+  GemmArgs a = base_args(y, y_row_stride, AIOSB_EPI_STORE, nullptr, 0, status);
+  a.norm = 2;
+  a.stat_x = stat_x;
+  a.stat_ss = stat_ss;
+  a.stat_ss_stride = stat_ss_stride;
+  a.stat_parts = (int)parts;
+  a.nw = (const __nv_bfloat16*)norm_w;
+  a.neps = eps;
+  a.tile_stats = reinterpret_cast<float4*>(tile_stats);
   return linear_impl(a, nullptr, rows, k, w, n, stream);
 }
 

@@ -83,11 +83,14 @@ __device__ __forceinline__ void quad_sum2(float& x, float& y) {
 }
 
 // MODE: 0 plain operand rows, 1 rows normalised from residual statistics,
-// 2 the AttnRes mixer's rows, normalised (kGemvMix).
+// 2 the AttnRes mixer's rows, normalised (kGemvMix), 3 as 1 and the store
+// epilogue also writes per-tile statistics (kGemvStatTiles, the LM head).
 template <int NT, int KB, int MODE, bool GROUPS>
 __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a) {
-  constexpr bool STAT = MODE == kGemvStat, MIX = MODE == kGemvMix;
+  constexpr bool TILES = MODE == kGemvStatTiles;
+  constexpr bool STAT = MODE == kGemvStat || TILES, MIX = MODE == kGemvMix;
   static_assert(!MIX || (NT == 1 && !GROUPS), "the mixer operand serves one 8-row group");
+  static_assert(!TILES || !GROUPS, "tile statistics serve one row group");
   constexpr int TM = NT * 8;  // token rows covered
   __shared__ float red[kGemvFeat][NT][32][4];  // [warp][n tile][lane][fragment]
   __shared__ float tile[TM][17];               // reduced [token][row] (padded)
@@ -412,6 +415,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
     }
     __syncthreads();
     // ---- epilogue: thread (token, half) writes 8 features (16 bytes)
+    float ts_max = -INFINITY, ts_min = INFINITY, ts_sum = 0.f;  // tile statistics of the stored values
+    bool ts_nan = false, ts_live = false;
+    float ts_v[8];
     if (tid < TM * 2) {
       const int tk = tid >> 1, h = tid & 1;
       if (tk < T && (!silu || h == 0)) {
@@ -451,6 +457,36 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
         *reinterpret_cast<uint4*>(a.y + (int64_t)(row0 + tk) * a.y_stride + f0) =
             make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
                        pack_bf16x2(o[6], o[7]));
+        if constexpr (TILES) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            ts_v[j] = round_bf16(o[j]);  // the stored logit
+            ts_max = fmaxf(ts_max, ts_v[j]);
+            ts_min = fminf(ts_min, ts_v[j]);
+            ts_nan |= ts_v[j] != ts_v[j];
+          }
+          ts_live = true;
+        }
+      }
+    }
+    // Tile statistics for the sampler (the LM head, a store epilogue): per 16-id
+    // tile and token row, the max, the sum of exp(v - max) and the min of the
+    // stored bf16 logits (and whether any is NaN). Threads (tk, 0) and (tk, 1)
+    // hold the two halves; warp 0 holds every epilogue thread.
+    if (TILES && warp == 0) {
+      const float pmax = __shfl_xor_sync(0xffffffffu, ts_max, 1);
+      const float pmin = __shfl_xor_sync(0xffffffffu, ts_min, 1);
+      const int pnan = __shfl_xor_sync(0xffffffffu, (int)ts_nan, 1);
+      const float mx = fmaxf(ts_max, pmax);
+      if (ts_live) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ts_sum += expf(ts_v[j] - mx);
+      }
+      const float psum = __shfl_xor_sync(0xffffffffu, ts_sum, 1);
+      if (ts_live && (tid & 1) == 0) {
+        const int tk = tid >> 1;
+        a.tile_stats[(int64_t)tl * a.rows + row0 + tk] =
+            make_float4(mx, ts_sum + psum, fminf(ts_min, pmin), (ts_nan || pnan) ? 1.f : 0.f);
       }
     }
     if (tl + (int)gridDim.x < ntiles) rv = load_res(tl + gridDim.x);
@@ -497,6 +533,10 @@ int launch_mma(const GemvArgs& a, cudaStream_t stream) {
 
 template <int NT, int KB>
 int launch_mma_rows(const GemvArgs& a, cudaStream_t stream) {
+  if (a.tile_stats != nullptr) {  // tile_stats_eligible() holds
+    if constexpr (KB == 3) return launch_mma<NT, 3, kGemvStatTiles, false>(a, stream);
+    return set_error(AIOSB_ERR_UNSUPPORTED, "linear: tile statistics need k <= 768");
+  }
   if (a.rows > NT * 8)
     return a.stat_x != nullptr ? launch_mma<NT, KB, kGemvStat, true>(a, stream)
                                : launch_mma<NT, KB, kGemvPlain, true>(a, stream);
@@ -524,6 +564,10 @@ bool mix_eligible(int64_t rows, int64_t k, int64_t n_out, int64_t sources, int64
   return g_gemv_enabled && rows >= 1 && rows <= 8 && k == kMixMaxK && n_out % 16 == 0 && sources >= 1 &&
          stable >= 0 && stable <= sources && sources - stable + (partial ? 1 : 0) <= 2 &&
          sources + (partial ? 1 : 0) <= kMixMaxSources;
+}
+
+bool tile_stats_eligible(int64_t rows, int64_t k, int64_t n_out) {
+  return gemv_eligible(rows, k, n_out) && rows <= 16 && k <= 768;
 }
 
 bool gemv_eligible(int64_t rows, int64_t k, int64_t n_out) {

@@ -45,6 +45,10 @@ struct GemvArgs {
   int mix_sources;                   // bank sources
   int mix_stable;                    // bank sources written before the previous kernel began
   int64_t mix_tokens;                // rows of one bank source
+  // statistics operand and store epilogue, optional (tile_stats_eligible()): per
+  // 16-column tile and row, (max, sum of exp(v - max), min, 1 if any NaN) of the
+  // stored bf16 values, at tile_stats[tile * rows + row]
+  float4* tile_stats;
 };
 
 // Mixer mode: at most this many sources (bank + partial), k of exactly kMixMaxK,
@@ -52,7 +56,7 @@ struct GemvArgs {
 constexpr int kMixMaxSources = 10;
 constexpr int kMixMaxK = 768;
 constexpr int kMixRowPad = 32;
-constexpr int kGemvPlain = 0, kGemvStat = 1, kGemvMix = 2;  // operand modes
+constexpr int kGemvPlain = 0, kGemvStat = 1, kGemvMix = 2, kGemvStatTiles = 3;  // operand modes
 inline size_t mix_smem_bytes(int64_t stable, int64_t k) {
   return (size_t)stable * 8 * (size_t)(k + kMixRowPad) * 2 + (size_t)8 * 8 * kMixMaxSources * 2 * 4 +
          (size_t)8 * kMixMaxSources * 4;
@@ -62,6 +66,7 @@ inline size_t mix_smem_bytes(int64_t stable, int64_t k) {
 constexpr int kGemvStatGroup = 8;
 
 bool gemv_eligible(int64_t rows, int64_t k, int64_t n_out);
+bool tile_stats_eligible(int64_t rows, int64_t k, int64_t n_out);  // GEMV, rows <= 16, k <= 768
 bool mix_eligible(int64_t rows, int64_t k, int64_t n_out, int64_t sources, int64_t stable, bool partial);
 int gemv_launch(const GemvArgs& a, cudaStream_t stream);
 

@@ -1109,6 +1109,138 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   } else if (!leader) {
     return;
   }
+  // ---- tile-statistics path (one CTA per row; steps whose logits the decode
+  // forward's LM head wrote, with per-16-id tile statistics: max, sum of
+  // exp(v - max), min, NaN flag of the stored logits). The row max is the max
+  // of the tile maxima and the log-sum-exp M + log(sum_t s_t exp(m_t - M)); the
+  // overflow check reads the tile max and min. With B forbidden ids at most
+  // (the minimum-length list and the repeat bans), the (k + B)-th largest tile
+  // max L bounds the k-th largest allowed value from below: those k + B tiles'
+  // maxima are distinct ids >= L, at most B of them forbidden. So only tiles
+  // whose max is >= L can hold a candidate; their 16 logits are read, and the
+  // keys >= L (forbidden -> -inf, as make_raw_keys) are sorted and picked
+  // exactly as the thread-maximum path does, giving the same token. Rows that
+  // could overflow, ask for more tiles than the row has, or hold more than
+  // kMaxSortK candidates take the full path below.
+  if (!SPLIT && run && !have && g.tile_stats != nullptr && step > 0 && !p.greedy && p.top_k >= 1 &&
+      p.top_k <= kFastTopK && (V & 15) == 0 && (reinterpret_cast<uintptr_t>(g.logits) & 15u) == 0) {
+    constexpr int kTilesPer = kMaxVocab / 16 / kSampThreads;
+    const int NT = V >> 4;
+    const float4* ts = reinterpret_cast<const float4*>(g.tile_stats) + r;
+    const int stride = (int)gridDim.x;  // the launch's rows: the LM head's rows
+    float4 tv[kTilesPer];
+#pragma unroll
+    for (int q = 0; q < kTilesPer; ++q) {
+      const int t = tid + q * kSampThreads;
+      tv[q] = t < NT ? ts[(int64_t)t * stride] : make_float4(-INFINITY, 0.f, INFINITY, 0.f);
+    }
+    for (int w = tid; w < (V + 31) / 32; w += blockDim.x) s.ban[w] = 0u;
+    __syncthreads();
+    apply_bans();
+    const float big = p.temperature < 65536.f ? 0x1.fffffep126f * p.temperature : -1.f;
+    float m = -INFINITY;
+    bool hz = false;
+    uint32_t tk[kTilesPer];
+#pragma unroll
+    for (int q = 0; q < kTilesPer; ++q) {
+      const bool valid = tid + q * kSampThreads < NT;
+      tk[q] = valid ? order_key(tv[q].x) : 0u;
+      if (valid) {
+        m = fmaxf(m, tv[q].x);
+        hz |= !(fabsf(tv[q].x) <= big) || !(fabsf(tv[q].z) <= big) || tv[q].w != 0.f;  // NaN included
+      }
+    }
+    const int k = min(p.top_k, V);
+    int nb = step < st->min_new_tokens ? st->n_minlen : 0;
+    if (st->n_banned > 0 && step >= st->ban_min_prefix && step < st->banned_width) nb += st->n_banned;
+    const int need = k + nb;
+    if (__syncthreads_or(hz) == 0 && need <= NT) {  // the barrier also completes the bans
+      m = block_max(m, s.red);
+      float se = 0.f;
+#pragma unroll
+      for (int q = 0; q < kTilesPer; ++q)
+        if (tid + q * kSampThreads < NT) se += tv[q].y * expf(tv[q].x - m);
+      se = block_sum(se, s.red);
+      // L: the need-th largest tile-max key, by bisection on the 16 significant
+      // bits (tile maxima are bf16 values); per-warp counts alternate buffers
+      uint32_t L = 0u;
+      const int warp = tid >> 5;
+      for (int b = 31, buf = 0; b >= 16; --b, buf ^= 1) {
+        const uint32_t cand = L | (1u << b);
+        int n = 0;
+#pragma unroll
+        for (int q = 0; q < kTilesPer; ++q) n += tk[q] >= cand ? 1 : 0;
+        n = (int)__reduce_add_sync(0xffffffffu, (unsigned)n);
+        if (lane == 0) xs.cnt[buf][warp] = n;
+        __syncthreads();
+        int tot = 0;
+#pragma unroll
+        for (int w = 0; w < kSampThreads / 32; ++w) tot += xs.cnt[buf][w];
+        if (tot >= need) L = cand;
+      }
+      uint4 lv[kTilesPer][2];
+      int n = 0;
+#pragma unroll
+      for (int q = 0; q < kTilesPer; ++q) {
+        const int t = tid + q * kSampThreads;
+        lv[q][0] = lv[q][1] = make_uint4(0u, 0u, 0u, 0u);
+        if (t < NT && tk[q] >= L) {
+          const uint4* src = reinterpret_cast<const uint4*>(lrow + 16 * t);
+          lv[q][0] = src[0];
+          lv[q][1] = src[1];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kTilesPer; ++q) {
+        const int t = tid + q * kSampThreads;
+        if (t < NT && tk[q] >= L) {
+          const uint32_t bits = s.ban[t >> 1] >> ((t & 1) * 16);  // the tile's 16 ids share a word
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll 1  // compact code: the step kernel runs cold each decode step
+            for (int e = 0; e < 8; ++e) {
+              const float v = ((bits >> (8 * h + e)) & 1u) ? -INFINITY : group_elem(lv[q][h], e);
+              n += order_key(v) >= L ? 1 : 0;
+            }
+          }
+        }
+      }
+      int total;
+      int off = block_exclusive_scan(n, s, total);
+      if (total >= k && total <= kMaxSortK) {
+#pragma unroll
+        for (int q = 0; q < kTilesPer; ++q) {
+          const int t = tid + q * kSampThreads;
+          if (t < NT && tk[q] >= L) {
+            const uint32_t bits = s.ban[t >> 1] >> ((t & 1) * 16);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll 1
+              for (int e = 0; e < 8; ++e) {
+                const float v = ((bits >> (8 * h + e)) & 1u) ? -INFINITY : group_elem(lv[q][h], e);
+                const uint32_t kk = order_key(v);
+                if (kk >= L)
+                  s.cand[off++] = ((unsigned long long)(~kk) << 32) | (unsigned long long)(uint32_t)(16 * t + 8 * h + e);
+              }
+            }
+          }
+        }
+        __syncthreads();
+        sort_candidates(s, total);
+        for (int i = tid; i < k; i += blockDim.x) {
+          const unsigned long long cv = s.cand[i];
+          s.cid[i] = (int)(uint32_t)(cv & 0xffffffffull);
+          s.cval[i] = key_value(~(uint32_t)(cv >> 32)) / p.temperature;  // the fp32 division of make_keys
+        }
+        __syncthreads();
+        const auto val = [&](int i) { return s.cval[i]; };
+        tok = s.cid[pick_index(s, val, k, p.top_p, u)];
+        mx = m;
+        lse = logf(se);
+        have = true;
+      }
+    }
+  }
   if (run && !have) {
     // the one-CTA path: the whole row in this CTA
     RowRegs rr;

@@ -513,9 +513,13 @@ def linear_stat_norm(
     *,
     out: torch.Tensor | None = None,
     epilogue: int = _lib.EPI_STORE,
+    tile_stats: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """``linear(rmsnorm(s) * norm_weight, weight)`` with s and its sums of squares
-    from ``stats``; the normalised rows exist only inside the GEMM."""
+    from ``stats``; the normalised rows exist only inside the GEMM. With
+    ``tile_stats`` (fp32, [n / 16, rows, 4], see ``tile_stats_eligible``) the
+    store epilogue also writes each 16-column tile's (max, sum of exp(v - max),
+    min, NaN flag) of the stored values."""
     _require_cuda(stats.x, norm_weight, weight, what="linear_stat_norm")
     rows, k = stats.x.shape
     if weight.shape[1] != k or stats.x.stride(1) != 1 or stats.x.stride(0) != k or stats.ss.stride(1) != 1:
@@ -524,10 +528,27 @@ def linear_stat_norm(
     cols = n // 2 if epilogue == _lib.EPI_SILU_MUL else n
     if out is None:
         out = torch.empty((rows, cols), dtype=weight.dtype, device=weight.device)
+    if tile_stats is not None:
+        if epilogue != _lib.EPI_STORE or not tile_stats_eligible(rows, k, n):
+            raise ValueError("tile statistics need the store epilogue, rows <= 16, k <= 768, n % 16 == 0")
+        if tile_stats.dtype != torch.float32 or not tile_stats.is_contiguous() or tile_stats.numel() < n // 16 * rows * 4:
+            raise ValueError("tile_stats must be contiguous fp32 with n / 16 * rows * 4 elements")
+        _lib.call("aiosb_linear_stat_norm_tiles", stats.x.data_ptr(), stats.ss.data_ptr(), stats.ss.stride(0),
+                  stats.parts, norm_weight.data_ptr(), float(eps), rows, k, weight.data_ptr(), n, out.data_ptr(),
+                  out.stride(0), tile_stats.data_ptr(), status_word(weight.device).data_ptr(),
+                  _stream(weight.device))
+        return out
     _lib.call("aiosb_linear_stat_norm", stats.x.data_ptr(), stats.ss.data_ptr(), stats.ss.stride(0), stats.parts,
               norm_weight.data_ptr(), float(eps), rows, k, weight.data_ptr(), n, out.data_ptr(), out.stride(0),
               epilogue, None, 0, status_word(weight.device).data_ptr(), _stream(weight.device))
     return out
+
+
+def tile_stats_eligible(rows: int, k: int, n: int) -> bool:
+    """Whether ``linear_stat_norm`` can write tile statistics for this shape (the
+    library's answer: the register-operand path with rows <= 16, k a multiple of
+    256 up to 768, n % 16 == 0)."""
+    return bool(_lib.load().aiosb_linear_tile_stats_eligible(rows, k, n))
 
 
 def pack_gate_up(weight: torch.Tensor) -> torch.Tensor:

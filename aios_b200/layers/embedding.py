@@ -77,7 +77,12 @@ class LMHead(BaseOP):
                 stats = stats.rows(rows[0], rows[0] + 1)
             else:
                 stats = stats.select(md.get_last_indices(batch.size))
-        return ops.linear_stat_norm(stats, norm_weight, eps, self._w(), out=batch.logits_out)
+        tiles = batch.tile_stats_out
+        w = self._w()
+        if tiles is not None and batch.is_decode and ops.tile_stats_eligible(stats.x.shape[0], w.shape[1], w.shape[0]):
+            batch.tile_stats_written = True
+            return ops.linear_stat_norm(stats, norm_weight, eps, w, out=batch.logits_out, tile_stats=tiles)
+        return ops.linear_stat_norm(stats, norm_weight, eps, w, out=batch.logits_out)
 
     def load_state_dict(self, state_dict: Dict[str, torch.Tensor], *, prefix: str = "", _internal: bool = False) -> None:
         if self._tie_word_embeddings:

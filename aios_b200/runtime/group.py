@@ -64,6 +64,14 @@ _HISTORY = HISTORY_MODES[os.environ.get("AIOSB_DECODE_HISTORY", "staged")]
 STAGE_CLASSES = (128, 512)
 
 
+# Sampling from the LM head's tile statistics (aiosb_group_ptrs.tile_stats): the
+# decode forward's LM head also writes, per 16-id tile of each row, the max, the
+# sum of exponentials, the min and a NaN flag, and the step kernel bounds its
+# top-k candidates and the log-sum-exp from those instead of scanning the row.
+# AIOSB_TILE_SAMPLING=0 keeps the row scan.
+_TILE_SAMPLING = os.environ.get("AIOSB_TILE_SAMPLING", "1") != "0"
+
+
 def stage_class(prefix_len: int) -> int:
     return next((c for c in STAGE_CLASSES if prefix_len <= c), STAGE_CLASSES[-1])
 
@@ -171,6 +179,16 @@ class CandidateGroupRuntime:
             ring=llm.cache_manager.ring.data_ptr(),
             status=ops.status_word(dev).data_ptr(),
         )
+        # [vocab / 16, rows, 4] tile statistics of the decode logits, and per row
+        # count whether the LM head of that count's step graph writes them (known
+        # after the graph's eager warm-up forward)
+        self.tile_stats = (torch.zeros(self.vocab // 16 * max_rows * 4, dtype=torch.float32, device=dev)
+                           if _TILE_SAMPLING and self.vocab % 16 == 0 else None)
+        self._tile_rows: dict[int, bool] = {}
+        self._ptrs_tiles = None
+        if self.tile_stats is not None:
+            self._ptrs_tiles = _lib.GroupPtrs.from_buffer_copy(self.ptrs)
+            self._ptrs_tiles.tile_stats = self.tile_stats.data_ptr()
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self._graph_launches: dict[int, int] = {}
         self.h2d_bytes = 0  # host->device bytes copied by rounds (bench accounting)
@@ -191,6 +209,7 @@ class CandidateGroupRuntime:
         """Selects the decode attention's history mode (a HISTORY_MODES name) for
         this runtime's step graphs; captured graphs are dropped."""
         self.history_mode = HISTORY_MODES[mode]
+        self._tile_rows.clear()
         self._graphs.clear()
         self._graph_launches.clear()
 
@@ -199,6 +218,7 @@ class CandidateGroupRuntime:
         decode-step kernel; returns whether it is now in use (False when the model
         is not one the kernel serves). Captured step graphs are dropped."""
         self._step_plan = self._persistent_plan() if enabled else None
+        self._tile_rows.clear()
         self._graphs.clear()
         self._graph_launches.clear()
         return self._step_plan is not None
@@ -270,7 +290,7 @@ class CandidateGroupRuntime:
     def _decode_batch(self, rows: int, stage: int = STAGE_CLASSES[0]) -> Batch:
         reqs = [Req(input_ids=torch.empty(1, dtype=torch.long), cached_len=0, output_len=1, uid=i,
                     sampling_params=SamplingParams(max_tokens=1), table_idx=i) for i in range(rows)]
-        batch = Batch(reqs=reqs, phase="decode", logits_out=self.logits[:rows])
+        batch = Batch(reqs=reqs, phase="decode", logits_out=self.logits[:rows], tile_stats_out=self.tile_stats)
         batch.input_ids = self.tokens[:rows]
         batch.positions = self.positions[:rows]
         batch.out_loc = self.out_loc[:rows]
@@ -287,7 +307,8 @@ class CandidateGroupRuntime:
     def _group_step(self, rows: int, large: bool = False) -> None:
         # top_k_max: the largest sorted candidate set a round of this graph may ask for
         top_k_max = self.vocab if large else SORT_K
-        _lib.call("aiosb_group_step", ctypes.byref(self.ptrs), rows, self.vocab, top_k_max, self._stream())
+        ptrs = self._ptrs_tiles if self._tile_rows.get(rows, False) else self.ptrs
+        _lib.call("aiosb_group_step", ctypes.byref(ptrs), rows, self.vocab, top_k_max, self._stream())
 
     def _step_and_forward(self, rows: int, batch: Batch, large: bool = False) -> None:
         self._group_step(rows, large)
@@ -313,6 +334,8 @@ class CandidateGroupRuntime:
         self.active.zero_()
         self._step_and_forward(rows, batch, large)
         torch.cuda.synchronize(self.device)
+        # the step kernel reads tile statistics only where this forward wrote them
+        self._tile_rows[rows] = batch.tile_stats_written and self._step_plan is None
         graph = torch.cuda.CUDAGraph()
         before = _lib.launches
         with torch.cuda.graph(graph, pool=self._pool):

@@ -213,6 +213,20 @@ AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, 
                                      const void* residual, int64_t residual_stride, int32_t* status,
                                      void* stream);
 
+/* aiosb_linear_stat_norm with the store epilogue, that also writes, for every
+ * 16-column tile t of the output and row r, tile_stats[(t * rows + r) * 4 + i] =
+ * (max, sum of exp(v - max), min, 1 if any NaN else 0) of the tile's stored bf16
+ * values (the LM head: what the CandidateGroup step needs to bound a row's top-k
+ * and its log-sum-exp without scanning the row). Only on the register-operand
+ * path with rows <= 16 and k <= 768 (else AIOSB_ERR_UNSUPPORTED); tile_stats:
+ * [n / 16, rows, 4] fp32, 16-byte aligned. */
+/* 1 when aiosb_linear_stat_norm_tiles serves this shape, else 0. */
+AIOSB_API int aiosb_linear_tile_stats_eligible(int64_t rows, int64_t k, int64_t n);
+AIOSB_API int aiosb_linear_stat_norm_tiles(const float* stat_x, const float* stat_ss, int64_t stat_ss_stride,
+                                           int64_t parts, const void* norm_w, float eps, int64_t rows, int64_t k,
+                                           const void* w, int64_t n, void* y, int64_t y_row_stride,
+                                           float* tile_stats, int32_t* status, void* stream);
+
 /* Decode linear on the Block AttnRes mixer's normalised rows (replaces
  * BlockAttnResMixer.forward + RMSNorm.forward + Linear.forward,
  * aios/models/minimind_ime.py:162-190,237-252, aios/kernel/attnres.py:8-127):
@@ -424,6 +438,13 @@ typedef struct aiosb_group_ptrs {
   int32_t* page_table;
   const int32_t* ring;        /* free-slot FIFO                                     */
   int32_t* status;
+  /* Optional, or NULL: the LM head's per-16-id tile statistics of `logits`
+   * (aiosb_linear_stat_norm_tiles, [vocab / 16, rows, 4] with `rows` the step's
+   * rows). When set, steps after the first of a round (whose logits the decode
+   * forward wrote, not aiosb_group_begin) bound a top-k row's candidates and its
+   * log-sum-exp from the tiles instead of scanning the row; the tokens are the
+   * same, the log-probabilities agree to fp32 rounding. */
+  const float* tile_stats;
 } aiosb_group_ptrs;
 
 /* Round start: resets the per-row outputs, copies the prefix logits [vocab] into

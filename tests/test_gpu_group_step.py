@@ -12,6 +12,7 @@ a CDF-boundary rounding tie), log-probabilities within 2e-5."""
 from __future__ import annotations
 
 import ctypes
+import math
 
 import pytest
 import torch
@@ -25,7 +26,8 @@ ROWS, STEPS, WIDTH = 8, 4, 64
 MINLEN = [2, 7, 100, 5000]  # forbidden at step 0 (min_new_tokens 1); 2 is EOS
 
 
-def _group(dev, vocab: int, *, temperature: float, top_k: int, top_p: float, greedy: bool) -> dict:
+def _group(dev, vocab: int, *, temperature: float, top_k: int, top_p: float, greedy: bool, step: int = 0,
+           min_new_tokens: int = 1) -> dict:
     i32 = dict(dtype=torch.int32, device=dev)
     b = dict(
         state=torch.zeros(ctypes.sizeof(_lib.GroupState), dtype=torch.uint8, device=dev),
@@ -43,7 +45,7 @@ def _group(dev, vocab: int, *, temperature: float, top_k: int, top_p: float, gre
     for name in ("counts", "stop_codes", "active", "finished", "tokens", "positions", "seq_lens", "out_loc",
                  "row_page", "row_table"):
         b[name] = torch.zeros(ROWS, **i32)
-    st = _lib.GroupState(step=0, max_steps=STEPS, min_new_tokens=1, prefix_len=5, rows=ROWS, vocab=vocab, eos_id=2,
+    st = _lib.GroupState(step=step, max_steps=STEPS, min_new_tokens=min_new_tokens, prefix_len=5, rows=ROWS, vocab=vocab, eos_id=2,
                          pad_id=0, greedy=int(greedy), top_k=top_k, temperature=temperature, top_p=top_p,
                          page_size=1, n_terminal=0, n_minlen=len(MINLEN), head=0, tail=64, capacity=64,
                          table_stride=WIDTH)
@@ -59,6 +61,10 @@ def _logits(mode: str, vocab: int, g: torch.Generator) -> torch.Tensor:
     if mode == "coarse":
         return torch.randint(-3, 4, (ROWS, vocab), generator=g).float().to(torch.bfloat16)
     x = torch.randn(ROWS, vocab, generator=g) * 2.0
+    if mode == "peaked":  # the largest values packed into four neighbouring tiles
+        x[:, 512:576] += 8.0
+    if mode == "banned_top":  # forbidden ids hold the largest values of their tiles
+        x[:, [t for t in MINLEN if t < vocab]] += 12.0
     if mode == "huge":  # finite after scaling, above the raw-key bound
         idx = torch.randint(0, vocab, (ROWS, 3), generator=g)
         x = x.scatter(1, idx, torch.tensor([1e38, -1e38, 6e37]).expand(ROWS, 3))
@@ -135,3 +141,89 @@ def test_group_step_other_cluster_sizes(split: int) -> None:
                            str(Path(__file__).resolve()), "-k", "matches_oracle"],
                           cwd=repo, env=env, capture_output=True, text=True, timeout=600)
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-2000:]
+
+
+def _tile_stats(logits: torch.Tensor) -> torch.Tensor:
+    """[vocab / 16, rows, 4]: per 16-id tile of each row, the max, the sum of
+    exp(v - max), the min and a NaN flag (what the LM head's epilogue writes)."""
+    t = logits.float().view(logits.shape[0], -1, 16)
+    mx = t.amax(-1)
+    return torch.stack((mx, torch.exp(t - mx[..., None]).sum(-1), t.amin(-1), t.isnan().any(-1).float()),
+                       -1).transpose(0, 1).contiguous()
+
+
+TILE_CASES = [
+    # name, vocab, temperature, top_k, top_p, logits, min_new_tokens (> 1: MINLEN forbidden at step 1)
+    ("tiles_k50", 16384, 0.8, 50, 0.9, "randn", 2),
+    ("tiles_k1_sampled", 16384, 0.8, 1, 0.9, "randn", 1),
+    ("tiles_k512", 16384, 1.0, 512, 0.95, "randn", 2),
+    ("tiles_s06_vocab", 6400, 0.8, 50, 0.9, "randn", 2),
+    ("tiles_peaked", 16384, 0.8, 50, 0.9, "peaked", 1),
+    ("tiles_banned_top", 16384, 0.8, 50, 0.9, "banned_top", 2),
+    ("tiles_few_distinct", 16384, 0.8, 50, 1.0, "coarse", 2),  # more than 2048 candidates: the row scan
+    ("tiles_ties", 16384, 0.8, 50, 0.9, "const", 2),  # every tile tied: the row scan
+    ("tiles_hazard", 16384, 0.5, 50, 0.9, "huge", 2),  # values the temperature could overflow: the row scan
+    ("tiles_more_than_tiles", 608, 0.8, 200, 0.9, "randn", 2),  # k + bans above the 38 tiles: the row scan
+    ("tiles_ragged_vocab", 6401, 0.7, 96, 0.9, "randn", 2),  # vocab % 16 != 0: the row scan
+]
+
+
+def _run_step(dev, name, vocab, temperature, top_k, top_p, logits, min_new, tiles):
+    grp = _group(dev, vocab, temperature=temperature, top_k=top_k, top_p=top_p, greedy=False, step=1,
+                 min_new_tokens=min_new)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.call("aiosb_group_begin", ctypes.byref(grp["ptrs"]), grp["logits"][0].clone().data_ptr(), 777 + vocab,
+              ROWS, ROWS, stream)
+    grp["logits"].copy_(logits.to(dev))
+    if tiles is not None:
+        grp["tiles"] = tiles.to(dev)
+        grp["ptrs"].tile_stats = grp["tiles"].data_ptr()
+    _lib.call("aiosb_group_step", ctypes.byref(grp["ptrs"]), ROWS, vocab, top_k, stream)
+    torch.cuda.synchronize(dev)
+    assert int(grp["status"][0]) == 0
+    return grp
+
+
+@pytest.mark.parametrize("name,vocab,temperature,top_k,top_p,mode,min_new", TILE_CASES,
+                         ids=[c[0] for c in TILE_CASES])
+def test_group_step_from_tile_statistics(cuda_device, name, vocab, temperature, top_k, top_p, mode,
+                                         min_new) -> None:
+    """A step after the first (logits written by the decode forward) with the LM
+    head's tile statistics: the same tokens as the row scan and as the oracle,
+    log-probabilities within 2e-5 of the exact log-softmax."""
+    g = torch.Generator().manual_seed(len(name) * 17 + vocab)
+    logits = _logits(mode, vocab, g)
+    tiles = _tile_stats(logits) if vocab % 16 == 0 else torch.zeros(4)
+    fast = _run_step(cuda_device, name, vocab, temperature, top_k, top_p, logits, min_new, tiles)
+    scan = _run_step(cuda_device, name, vocab, temperature, top_k, top_p, logits, min_new, None)
+    tok = fast["tokens"].cpu().long()
+    assert torch.equal(tok, scan["tokens"].cpu().long())
+    assert fast["output_ids"][:, 1].cpu().long().tolist() == tok.tolist()
+    u = fast["uniforms"][:, 1].cpu()
+    bans = dict(forbidden_token_ids=[t for t in MINLEN if t < vocab] if min_new > 1 else [])
+    exp_tok, _ = osamp.sample_with_logprobs(logits, temperature=temperature, top_k=top_k, top_p=top_p,
+                                            uniforms=u, **bans)
+    mism = tok != exp_tok.squeeze(-1)
+    if bool(mism.any()):
+        margins = osamp.sample_margin(logits, temperature=temperature, top_k=top_k, top_p=top_p, uniforms=u, **bans)
+        band = osamp.cdf_rounding_band(logits, temperature=temperature, top_k=top_k, top_p=top_p, **bans)
+        bad = (margins >= band + 1e-6) & mism.numpy()
+        assert not bad.any(), f"{name}: token mismatch rows {bad.nonzero()[0].tolist()}"
+    ref = torch.log_softmax(logits.float(), dim=-1).gather(1, tok[:, None])[:, 0]
+    ok = torch.isfinite(ref)
+    torch.testing.assert_close(fast["token_logprobs"][:, 1].cpu()[ok], ref[ok], rtol=0, atol=2e-5)
+
+
+def test_group_step_reads_the_tile_statistics(cuda_device) -> None:
+    """The top-k step takes its log-sum-exp from the tiles: doubling every tile's
+    sum of exponentials lowers each log-probability by log 2, same tokens."""
+    g = torch.Generator().manual_seed(3)
+    logits = _logits("randn", 16384, g)
+    tiles = _tile_stats(logits)
+    doubled = tiles.clone()
+    doubled[..., 1] *= 2.0
+    a = _run_step(cuda_device, "a", 16384, 0.8, 50, 0.9, logits, 2, tiles)
+    b = _run_step(cuda_device, "b", 16384, 0.8, 50, 0.9, logits, 2, doubled)
+    assert torch.equal(a["tokens"], b["tokens"])
+    lp_a, lp_b = a["token_logprobs"][:, 1].cpu(), b["token_logprobs"][:, 1].cpu()
+    torch.testing.assert_close(lp_a - lp_b, torch.full((ROWS,), math.log(2.0)), rtol=0, atol=1e-5)

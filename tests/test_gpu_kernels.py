@@ -752,6 +752,44 @@ def test_residual_statistics_chain(cuda_device, rows: int, epi: str) -> None:
     _bf16_close(y, ref, ulps=2.0, atol=2e-3)
 
 
+def _tile_stats_of(y: torch.Tensor) -> torch.Tensor:
+    """[n / 16, rows, 4] (max, sum of exp(v - max), min, NaN flag) of y's 16-column tiles."""
+    t = y.float().view(y.shape[0], -1, 16)
+    mx = t.amax(-1)
+    return torch.stack((mx, torch.exp(t - mx[..., None]).sum(-1), t.amin(-1), t.isnan().any(-1).float()),
+                       -1).transpose(0, 1).contiguous()
+
+
+@pytest.mark.parametrize("rows", [1, 8, 13, 16])
+def test_lm_head_tile_statistics(cuda_device, rows: int) -> None:
+    """The LM head's store epilogue with per-16-column tile statistics: the
+    logits are bit-identical to the plain statistics linear, the tile max and
+    min are exact, the sums of exponentials within fp32 rounding."""
+    g = torch.Generator().manual_seed(40 + rows)
+    dev = cuda_device
+    d, vocab = 768, 6400
+    x = torch.randn(rows, d, generator=g).to(torch.bfloat16)
+    nw = (1.0 + 0.1 * torch.randn(d, generator=g)).to(torch.bfloat16)
+    w = (torch.randn(vocab, d, generator=g) * 0.05).to(torch.bfloat16)
+    _, stats = ops.embedding_stat(torch.arange(rows, device=dev), x.to(dev))
+    plain = ops.linear_stat_norm(stats, nw.to(dev), 1e-6, w.to(dev))
+    tiles = torch.full((vocab // 16 * rows * 4,), float("nan"), device=dev)
+    y = ops.linear_stat_norm(stats, nw.to(dev), 1e-6, w.to(dev), tile_stats=tiles)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    assert torch.equal(y, plain)
+    got = tiles.view(vocab // 16, rows, 4).cpu()
+    want = _tile_stats_of(y.cpu())
+    assert torch.equal(got[..., 0], want[..., 0]) and torch.equal(got[..., 2], want[..., 2])
+    assert not got[..., 3].any()
+    torch.testing.assert_close(got[..., 1], want[..., 1], rtol=2e-6, atol=0)
+    assert ops.tile_stats_eligible(16, d, vocab) and not ops.tile_stats_eligible(17, d, vocab)
+    if rows == 16:
+        stats17 = ops.embedding_stat(torch.arange(17, device=dev) % rows, x.to(dev))[1]
+        with pytest.raises(ValueError):
+            ops.linear_stat_norm(stats17, nw.to(dev), 1e-6, w.to(dev), tile_stats=tiles)
+
+
 def test_embedding_statistics(cuda_device) -> None:
     g = torch.Generator().manual_seed(5)
     w = torch.randn(1000, 768, generator=g).to(torch.bfloat16)
