@@ -879,7 +879,7 @@ __device__ __forceinline__ uint32_t atom_add_cluster_u32(uint32_t addr, uint32_t
 
 // SPLIT = false: the one-CTA kernel (C == 1), with no cluster code compiled in.
 template <bool SPLIT>
-__global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group_ptrs g, int large, int C) {
+__global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group_ptrs g, int large, int C, int Vl) {
   extern __shared__ uint8_t smem_raw[];
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw + sizeof(RowSmem));
@@ -892,6 +892,19 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const bool warp0 = tid < 32 && leader;
+  // The tile statistics (see the tile-statistics path below) are requested with
+  // the state: their addresses need only the launch's vocabulary and rows, and
+  // whether this step uses them is known once the state has arrived.
+  constexpr int kTilesPer = kMaxVocab / 16 / kSampThreads;
+  const int NTv = Vl >> 4;
+  const bool tiles_in = !SPLIT && g.tile_stats != nullptr && (Vl & 15) == 0 && Vl <= kMaxVocab;
+  float4 tv[kTilesPer];
+#pragma unroll
+  for (int q = 0; q < kTilesPer; ++q) {
+    const int t = tid + q * kSampThreads;
+    tv[q] = make_float4(-INFINITY, 0.f, INFINITY, 0.f);
+    if (tiles_in && t < NTv) tv[q] = reinterpret_cast<const float4*>(g.tile_stats)[(int64_t)t * gridDim.x + r];
+  }
   const int step = st->step;
   const int V = st->vocab;
   const int S = st->max_steps;
@@ -1114,118 +1127,110 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   // exp(v - max), min, NaN flag of the stored logits). The row max is the max
   // of the tile maxima and the log-sum-exp M + log(sum_t s_t exp(m_t - M)); the
   // overflow check reads the tile max and min. With B forbidden ids at most
-  // (the minimum-length list and the repeat bans), the (k + B)-th largest tile
-  // max L bounds the k-th largest allowed value from below: those k + B tiles'
-  // maxima are distinct ids >= L, at most B of them forbidden. So only tiles
-  // whose max is >= L can hold a candidate; their 16 logits are read, and the
+  // (the minimum-length list and the repeat bans), any L with k + B tiles whose
+  // max is >= L bounds the k-th largest allowed value from below: those tiles'
+  // maxima are distinct ids >= L, at most B of them forbidden. L is the
+  // (k + B)-th largest of the threads' largest tile maxima. Only tiles whose
+  // max is >= L can hold a candidate; their 16 logits are read, and the
   // keys >= L (forbidden -> -inf, as make_raw_keys) are sorted and picked
   // exactly as the thread-maximum path does, giving the same token. Rows that
   // could overflow, ask for more tiles than the row has, or hold more than
   // kMaxSortK candidates take the full path below.
-  if (!SPLIT && run && !have && g.tile_stats != nullptr && step > 0 && !p.greedy && p.top_k >= 1 &&
-      p.top_k <= kFastTopK && (V & 15) == 0 && (reinterpret_cast<uintptr_t>(g.logits) & 15u) == 0) {
-    constexpr int kTilesPer = kMaxVocab / 16 / kSampThreads;
-    const int NT = V >> 4;
-    const float4* ts = reinterpret_cast<const float4*>(g.tile_stats) + r;
-    const int stride = (int)gridDim.x;  // the launch's rows: the LM head's rows
-    float4 tv[kTilesPer];
-#pragma unroll
-    for (int q = 0; q < kTilesPer; ++q) {
-      const int t = tid + q * kSampThreads;
-      tv[q] = t < NT ? ts[(int64_t)t * stride] : make_float4(-INFINITY, 0.f, INFINITY, 0.f);
-    }
+  if (tiles_in && run && !have && V == Vl && NTv >= 16 && step > 0 && !p.greedy && p.top_k >= 1 &&
+      p.top_k <= kFastTopK && (reinterpret_cast<uintptr_t>(g.logits) & 15u) == 0) {
+    const int NT = NTv;
+    const int warp = tid >> 5;
+    const int k = min(p.top_k, V);
+    int nb = step < st->min_new_tokens ? st->n_minlen : 0;
+    if (st->n_banned > 0 && step >= st->ban_min_prefix && step < st->banned_width) nb += st->n_banned;
+    const int need = k + nb;
     for (int w = tid; w < (V + 31) / 32; w += blockDim.x) s.ban[w] = 0u;
     __syncthreads();
     apply_bans();
     const float big = p.temperature < 65536.f ? 0x1.fffffep126f * p.temperature : -1.f;
     float m = -INFINITY;
     bool hz = false;
-    uint32_t tk[kTilesPer];
 #pragma unroll
     for (int q = 0; q < kTilesPer; ++q) {
-      const bool valid = tid + q * kSampThreads < NT;
-      tk[q] = valid ? order_key(tv[q].x) : 0u;
-      if (valid) {
+      const int t = tid + q * kSampThreads;
+      if (t < NT) {
         m = fmaxf(m, tv[q].x);
         hz |= !(fabsf(tv[q].x) <= big) || !(fabsf(tv[q].z) <= big) || tv[q].w != 0.f;  // NaN included
       }
     }
-    const int k = min(p.top_k, V);
-    int nb = step < st->min_new_tokens ? st->n_minlen : 0;
-    if (st->n_banned > 0 && step >= st->ban_min_prefix && step < st->banned_width) nb += st->n_banned;
-    const int need = k + nb;
+    // per-warp max and sum of exponentials relative to it (combined after the
+    // barrier), and this thread's largest tile key
+    const float wm = warp_max(m);
+    float ws = 0.f;
+    uint32_t tmax = 0u;
+#pragma unroll
+    for (int q = 0; q < kTilesPer; ++q) {
+      if (tid + q * kSampThreads < NT) {
+        ws += tv[q].y * expf(tv[q].x - wm);
+        tmax = max(tmax, order_key(tv[q].x));
+      }
+    }
+    ws = warp_sum(ws);
+    if (lane == 0) {
+      s.red[warp] = wm;
+      s.red[kSampThreads / 32 + warp] = ws;
+      if (warp == 0) s.misc[0] = 0;
+    }
     if (__syncthreads_or(hz) == 0 && need <= NT) {  // the barrier also completes the bans
-      m = block_max(m, s.red);
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kSampThreads / 32; ++w) M = fmaxf(M, s.red[w]);
       float se = 0.f;
 #pragma unroll
-      for (int q = 0; q < kTilesPer; ++q)
-        if (tid + q * kSampThreads < NT) se += tv[q].y * expf(tv[q].x - m);
-      se = block_sum(se, s.red);
-      // L: the need-th largest tile-max key, by bisection on the 16 significant
-      // bits (tile maxima are bf16 values); per-warp counts alternate buffers
+      for (int w = 0; w < kSampThreads / 32; ++w) se += s.red[kSampThreads / 32 + w] * expf(s.red[w] - M);
+      // L: the need-th largest of the 512 thread maxima of the tile keys, a lower
+      // bound of the need-th largest tile max (those need maxima are distinct
+      // tiles), by bisection on the 16 significant bits (tile maxima are bf16
+      // values) with one counting barrier per bit
       uint32_t L = 0u;
-      const int warp = tid >> 5;
-      for (int b = 31, buf = 0; b >= 16; --b, buf ^= 1) {
+      for (int b = 31; b >= 16; --b) {
         const uint32_t cand = L | (1u << b);
-        int n = 0;
-#pragma unroll
-        for (int q = 0; q < kTilesPer; ++q) n += tk[q] >= cand ? 1 : 0;
-        n = (int)__reduce_add_sync(0xffffffffu, (unsigned)n);
-        if (lane == 0) xs.cnt[buf][warp] = n;
-        __syncthreads();
-        int tot = 0;
-#pragma unroll
-        for (int w = 0; w < kSampThreads / 32; ++w) tot += xs.cnt[buf][w];
-        if (tot >= need) L = cand;
+        if (__syncthreads_count(tmax >= cand) >= need) L = cand;
       }
-      uint4 lv[kTilesPer][2];
-      int n = 0;
+      // the tiles whose max is >= L into s.cid, one shared atomic per warp and
+      // tile round (the list's order does not matter: the candidates are sorted)
 #pragma unroll
       for (int q = 0; q < kTilesPer; ++q) {
         const int t = tid + q * kSampThreads;
-        lv[q][0] = lv[q][1] = make_uint4(0u, 0u, 0u, 0u);
-        if (t < NT && tk[q] >= L) {
-          const uint4* src = reinterpret_cast<const uint4*>(lrow + 16 * t);
-          lv[q][0] = src[0];
-          lv[q][1] = src[1];
-        }
+        const bool pass = t < NT && order_key(tv[q].x) >= L;
+        const unsigned bal = __ballot_sync(0xffffffffu, pass);
+        int wbase = 0;
+        if (lane == 0 && bal != 0u) wbase = atomicAdd(&s.misc[0], __popc(bal));
+        wbase = __shfl_sync(0xffffffffu, wbase, 0);
+        if (pass) s.cid[wbase + __popc(bal & ((1u << lane) - 1u))] = t;
       }
-#pragma unroll
-      for (int q = 0; q < kTilesPer; ++q) {
-        const int t = tid + q * kSampThreads;
-        if (t < NT && tk[q] >= L) {
-          const uint32_t bits = s.ban[t >> 1] >> ((t & 1) * 16);  // the tile's 16 ids share a word
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-#pragma unroll 1  // compact code: the step kernel runs cold each decode step
-            for (int e = 0; e < 8; ++e) {
-              const float v = ((bits >> (8 * h + e)) & 1u) ? -INFINITY : group_elem(lv[q][h], e);
-              n += order_key(v) >= L ? 1 : 0;
-            }
-          }
+      if (tid == 0) s.misc[1] = 0;
+      __syncthreads();
+      const int npass = s.misc[0];
+      // candidates: half a warp per listed tile, one id per lane; each warp
+      // reserves its slots with one shared atomic (the sort fixes the order)
+      for (int i0 = 0; i0 < npass; i0 += kSampThreads / 16) {
+        const int i = i0 + 2 * warp + (lane >> 4);
+        bool pass = false;
+        uint32_t kk = 0u;
+        int id = 0;
+        if (i < npass) {
+          id = 16 * s.cid[i] + (lane & 15);
+          const float v = ((s.ban[id >> 5] >> (id & 31)) & 1u) ? -INFINITY : bf16_to_f(lrow[id]);
+          kk = order_key(v);
+          pass = kk >= L;
         }
+        const unsigned bal = __ballot_sync(0xffffffffu, pass);
+        int wbase = 0;
+        if (lane == 0 && bal != 0u) wbase = atomicAdd(&s.misc[1], __popc(bal));
+        wbase = __shfl_sync(0xffffffffu, wbase, 0);
+        const int slot = wbase + __popc(bal & ((1u << lane) - 1u));
+        if (pass && slot < kMaxSortK)
+          s.cand[slot] = ((unsigned long long)(~kk) << 32) | (unsigned long long)(uint32_t)id;
       }
-      int total;
-      int off = block_exclusive_scan(n, s, total);
+      __syncthreads();
+      const int total = s.misc[1];
       if (total >= k && total <= kMaxSortK) {
-#pragma unroll
-        for (int q = 0; q < kTilesPer; ++q) {
-          const int t = tid + q * kSampThreads;
-          if (t < NT && tk[q] >= L) {
-            const uint32_t bits = s.ban[t >> 1] >> ((t & 1) * 16);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-#pragma unroll 1
-              for (int e = 0; e < 8; ++e) {
-                const float v = ((bits >> (8 * h + e)) & 1u) ? -INFINITY : group_elem(lv[q][h], e);
-                const uint32_t kk = order_key(v);
-                if (kk >= L)
-                  s.cand[off++] = ((unsigned long long)(~kk) << 32) | (unsigned long long)(uint32_t)(16 * t + 8 * h + e);
-              }
-            }
-          }
-        }
-        __syncthreads();
         sort_candidates(s, total);
         for (int i = tid; i < k; i += blockDim.x) {
           const unsigned long long cv = s.cand[i];
@@ -1235,7 +1240,7 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
         __syncthreads();
         const auto val = [&](int i) { return s.cval[i]; };
         tok = s.cid[pick_index(s, val, k, p.top_p, u)];
-        mx = m;
+        mx = M;
         lse = logf(se);
         have = true;
       }
@@ -1513,7 +1518,7 @@ int launch_group_step(const aiosb_group_ptrs& g, int64_t rows, int64_t vocab, bo
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = C > 1 ? 2 : 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, g, (int)large, C);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, g, (int)large, C, (int)vocab);
   return e == cudaSuccess ? AIOSB_OK : set_error(AIOSB_ERR_LAUNCH, "group_step: %s", cudaGetErrorString(e));
 }
 }  // namespace
