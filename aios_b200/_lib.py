@@ -151,6 +151,7 @@ _SIGNATURES = {
     "aiosb_attnres_mix_rmsnorm": ([_p, _i64, _i64, _i64, _p, _p, _f32, _p, _f32, _i64, _p, _p], _i32),
     "aiosb_test_attnres_stream_stall": ([_i64, ctypes.c_uint64], _i32),
     "aiosb_linear_tile_stats_eligible": ([_i64, _i64, _i64], _i32),
+    "aiosb_linear_tiles": ([_p, _i64, _i64, _p, _i64, _p, _i64, _p, _p, _p], _i32),
     "aiosb_linear_stat_norm_tiles": (
         [_p, _p, _i64, _i64, _p, _f32, _i64, _i64, _p, _i64, _p, _i64, _p, _p, _p], _i32
     ),

@@ -755,6 +755,20 @@ extern "C" int aiosb_linear_tile_stats_eligible(int64_t rows, int64_t k, int64_t
   return tile_stats_eligible(rows, k, n) ? 1 : 0;
 }
 
+extern "C" int aiosb_linear_tiles(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
+                                  int64_t y_row_stride, float* tile_stats, int32_t* status, void* stream) {
+  AIOSB_REQUIRE(tile_stats != nullptr && aligned16(tile_stats), AIOSB_ERR_MISALIGNED,
+                "linear_tiles: tile_stats must be 16-byte aligned");
+  AIOSB_REQUIRE(tile_stats_eligible(rows, k, n), AIOSB_ERR_UNSUPPORTED,
+                "linear_tiles: only on the register-operand path with rows <= 16, k <= 768, k %% 256 == 0");
+  int rc = check_common(w, rows, k, n, y, y_row_stride, AIOSB_EPI_STORE, nullptr, 0);
+  if (rc != AIOSB_OK) return rc == 1 ? AIOSB_OK : rc;
+  AIOSB_REQUIRE(x && aligned16(x), AIOSB_ERR_MISALIGNED, "linear_tiles: x must be a 16-byte aligned pointer");
+  GemmArgs a = base_args(y, y_row_stride, AIOSB_EPI_STORE, nullptr, 0, status);
+  a.tile_stats = reinterpret_cast<float4*>(tile_stats);
+  return linear_impl(a, x, rows, k, w, n, stream);
+}
+
 extern "C" int aiosb_linear_stat_norm_tiles(const float* stat_x, const float* stat_ss, int64_t stat_ss_stride,
                                             int64_t parts, const void* norm_w, float eps, int64_t rows, int64_t k,
                                             const void* w, int64_t n, void* y, int64_t y_row_stride,

@@ -83,12 +83,13 @@ __device__ __forceinline__ void quad_sum2(float& x, float& y) {
 }
 
 // MODE: 0 plain operand rows, 1 rows normalised from residual statistics,
-// 2 the AttnRes mixer's rows, normalised (kGemvMix), 3 as 1 and the store
-// epilogue also writes per-tile statistics (kGemvStatTiles, the LM head).
+// 2 the AttnRes mixer's rows, normalised (kGemvMix), 3 and 4 as 1 and 0 with
+// the store epilogue also writing per-tile statistics (kGemvStatTiles,
+// kGemvPlainTiles: the LM head).
 template <int NT, int KB, int MODE, bool GROUPS>
 __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a) {
-  constexpr bool TILES = MODE == kGemvStatTiles;
-  constexpr bool STAT = MODE == kGemvStat || TILES, MIX = MODE == kGemvMix;
+  constexpr bool TILES = MODE == kGemvStatTiles || MODE == kGemvPlainTiles;
+  constexpr bool STAT = MODE == kGemvStat || MODE == kGemvStatTiles, MIX = MODE == kGemvMix;
   static_assert(!MIX || (NT == 1 && !GROUPS), "the mixer operand serves one 8-row group");
   static_assert(!TILES || !GROUPS, "tile statistics serve one row group");
   constexpr int TM = NT * 8;  // token rows covered
@@ -534,7 +535,9 @@ int launch_mma(const GemvArgs& a, cudaStream_t stream) {
 template <int NT, int KB>
 int launch_mma_rows(const GemvArgs& a, cudaStream_t stream) {
   if (a.tile_stats != nullptr) {  // tile_stats_eligible() holds
-    if constexpr (KB == 3) return launch_mma<NT, 3, kGemvStatTiles, false>(a, stream);
+    if constexpr (KB == 3)
+      return a.stat_x != nullptr ? launch_mma<NT, 3, kGemvStatTiles, false>(a, stream)
+                                 : launch_mma<NT, 3, kGemvPlainTiles, false>(a, stream);
     return set_error(AIOSB_ERR_UNSUPPORTED, "linear: tile statistics need k <= 768");
   }
   if (a.rows > NT * 8)

@@ -56,7 +56,7 @@ struct GemvArgs {
 constexpr int kMixMaxSources = 10;
 constexpr int kMixMaxK = 768;
 constexpr int kMixRowPad = 32;
-constexpr int kGemvPlain = 0, kGemvStat = 1, kGemvMix = 2, kGemvStatTiles = 3;  // operand modes
+constexpr int kGemvPlain = 0, kGemvStat = 1, kGemvMix = 2, kGemvStatTiles = 3, kGemvPlainTiles = 4;  // operand modes
 inline size_t mix_smem_bytes(int64_t stable, int64_t k) {
   return (size_t)stable * 8 * (size_t)(k + kMixRowPad) * 2 + (size_t)8 * 8 * kMixMaxSources * 2 * 4 +
          (size_t)8 * kMixMaxSources * 4;

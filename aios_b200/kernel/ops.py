@@ -361,11 +361,12 @@ def linear(
     out: torch.Tensor | None = None,
     epilogue: int = _lib.EPI_STORE,
     residual: torch.Tensor | None = None,
+    tile_stats: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """y = x @ weight.T on the tensor cores (bf16 in, fp32 accumulate, bf16 out).
 
     ``epilogue=EPI_ADD`` returns ``residual + bf16(x @ weight.T)`` (residual may
-    be ``out`` for an in-place add)."""
+    be ``out`` for an in-place add). ``tile_stats`` as in ``linear_stat_norm``."""
     _require_cuda(x, weight, what="linear")
     if x.ndim != 2 or weight.ndim != 2 or x.shape[1] != weight.shape[1]:
         raise ValueError("linear expects x [T, K] and weight [N, K]")
@@ -380,6 +381,11 @@ def linear(
         out = torch.empty((x.shape[0], cols), dtype=x.dtype, device=x.device)
     if out.stride(1) != 1:
         raise ValueError("linear output rows must be contiguous")
+    if tile_stats is not None:
+        _check_tile_stats(tile_stats, epilogue, x.shape[0], x.shape[1], n)
+        _lib.call("aiosb_linear_tiles", x.data_ptr(), x.shape[0], x.shape[1], weight.data_ptr(), n, out.data_ptr(),
+                  out.stride(0), tile_stats.data_ptr(), status_word(x.device).data_ptr(), _stream(x.device))
+        return out
     _lib.call(
         "aiosb_linear",
         x.data_ptr(),
@@ -529,10 +535,7 @@ def linear_stat_norm(
     if out is None:
         out = torch.empty((rows, cols), dtype=weight.dtype, device=weight.device)
     if tile_stats is not None:
-        if epilogue != _lib.EPI_STORE or not tile_stats_eligible(rows, k, n):
-            raise ValueError("tile statistics need the store epilogue, rows <= 16, k <= 768, n % 16 == 0")
-        if tile_stats.dtype != torch.float32 or not tile_stats.is_contiguous() or tile_stats.numel() < n // 16 * rows * 4:
-            raise ValueError("tile_stats must be contiguous fp32 with n / 16 * rows * 4 elements")
+        _check_tile_stats(tile_stats, epilogue, rows, k, n)
         _lib.call("aiosb_linear_stat_norm_tiles", stats.x.data_ptr(), stats.ss.data_ptr(), stats.ss.stride(0),
                   stats.parts, norm_weight.data_ptr(), float(eps), rows, k, weight.data_ptr(), n, out.data_ptr(),
                   out.stride(0), tile_stats.data_ptr(), status_word(weight.device).data_ptr(),
@@ -542,6 +545,13 @@ def linear_stat_norm(
               norm_weight.data_ptr(), float(eps), rows, k, weight.data_ptr(), n, out.data_ptr(), out.stride(0),
               epilogue, None, 0, status_word(weight.device).data_ptr(), _stream(weight.device))
     return out
+
+
+def _check_tile_stats(tile_stats: torch.Tensor, epilogue: int, rows: int, k: int, n: int) -> None:
+    if epilogue != _lib.EPI_STORE or not tile_stats_eligible(rows, k, n):
+        raise ValueError("tile statistics need the store epilogue, rows <= 16, k <= 768, n % 16 == 0")
+    if tile_stats.dtype != torch.float32 or not tile_stats.is_contiguous() or tile_stats.numel() < n // 16 * rows * 4:
+        raise ValueError("tile_stats must be contiguous fp32 with n / 16 * rows * 4 elements")
 
 
 def tile_stats_eligible(rows: int, k: int, n: int) -> bool:

@@ -64,7 +64,12 @@ class LMHead(BaseOP):
             h = x.contiguous().clone() if not x.is_contiguous() else x
             r = residual.contiguous().clone() if not residual.is_contiguous() else residual
             ops.fused_add_rmsnorm(h, r, norm_weight, eps)
-        return ops.linear(h, self._w(), out=batch.logits_out)
+        w = self._w()
+        tiles = batch.tile_stats_out
+        if tiles is not None and batch.is_decode and ops.tile_stats_eligible(h.shape[0], w.shape[1], w.shape[0]):
+            batch.tile_stats_written = True
+            return ops.linear(h, w, out=batch.logits_out, tile_stats=tiles)
+        return ops.linear(h, w, out=batch.logits_out)
 
     def forward_stat(self, stats: ops.RowStats, norm_weight: torch.Tensor, eps: float) -> torch.Tensor:
         """LM head on the final RMSNorm of a residual stream given by its

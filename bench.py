@@ -63,6 +63,7 @@ class ClockSampler:
         self.interval_ms = interval_ms
         self.samples: list[list[str]] = []
         self._proc = None
+        self._mark = 0
 
     def __enter__(self):
         try:
@@ -77,7 +78,17 @@ class ClockSampler:
             self._thread.start()
         except OSError:
             self._proc = None
+            return self
+        # nvidia-smi's start-up (its NVML initialisation) stalls the GPU's work
+        # for a while: the timed region starts only once it samples
+        deadline = time.perf_counter() + 10.0
+        while not self.samples and self._proc.poll() is None and time.perf_counter() < deadline:
+            time.sleep(0.005)
         return self
+
+    def mark(self) -> None:
+        """Start of the timed region: the summary keeps the samples taken after it."""
+        self._mark = len(self.samples)
 
     def _read(self):
         for line in self._proc.stdout:
@@ -92,7 +103,7 @@ class ClockSampler:
                 self._proc.kill()
 
     def summary(self) -> dict:
-        rows = [s for s in self.samples if len(s) >= 8]
+        rows = [s for s in self.samples[self._mark:] if len(s) >= 8] or [s for s in self.samples if len(s) >= 8]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
 
@@ -833,6 +844,7 @@ def run_gpu(args, rank: int, world: int, local_rank: int) -> dict | None:
     with ClockSampler(local_rank if "CUDA_VISIBLE_DEVICES" not in os.environ else 0,
                       50 if world == 1 else 200) as clocks:
         torch.cuda.synchronize(dev)
+        clocks.mark()
         wall0 = time.perf_counter()
         torch.cuda.nvtx.range_push("timed")
         start.record(stream)

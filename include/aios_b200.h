@@ -220,7 +220,11 @@ AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, 
  * and its log-sum-exp without scanning the row). Only on the register-operand
  * path with rows <= 16 and k <= 768 (else AIOSB_ERR_UNSUPPORTED); tile_stats:
  * [n / 16, rows, 4] fp32, 16-byte aligned. */
-/* 1 when aiosb_linear_stat_norm_tiles serves this shape, else 0. */
+/* aiosb_linear with the store epilogue that also writes the tile statistics of
+ * aiosb_linear_stat_norm_tiles (the LM head on already normalised rows). */
+AIOSB_API int aiosb_linear_tiles(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
+                                 int64_t y_row_stride, float* tile_stats, int32_t* status, void* stream);
+/* 1 when aiosb_linear_tiles / aiosb_linear_stat_norm_tiles serve this shape, else 0. */
 AIOSB_API int aiosb_linear_tile_stats_eligible(int64_t rows, int64_t k, int64_t n);
 AIOSB_API int aiosb_linear_stat_norm_tiles(const float* stat_x, const float* stat_ss, int64_t stat_ss_stride,
                                            int64_t parts, const void* norm_w, float eps, int64_t rows, int64_t k,

@@ -790,6 +790,28 @@ def test_lm_head_tile_statistics(cuda_device, rows: int) -> None:
             ops.linear_stat_norm(stats17, nw.to(dev), 1e-6, w.to(dev), tile_stats=tiles)
 
 
+@pytest.mark.parametrize("rows", [1, 8, 16])
+def test_lm_head_tile_statistics_plain_operand(cuda_device, rows: int) -> None:
+    """The same tile statistics from the plain linear (the LM head on rows the
+    final RMSNorm already wrote, as the Block AttnRes trunk has them)."""
+    g = torch.Generator().manual_seed(70 + rows)
+    dev = cuda_device
+    d, vocab = 768, 16384
+    x = torch.randn(rows, d, generator=g).to(torch.bfloat16).to(dev)
+    w = (torch.randn(vocab, d, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+    plain = ops.linear(x, w)
+    tiles = torch.full((vocab // 16 * rows * 4,), float("nan"), device=dev)
+    y = ops.linear(x, w, tile_stats=tiles)
+    torch.cuda.synchronize()
+    ops.check_status(dev)
+    assert torch.equal(y, plain)
+    got = tiles.view(vocab // 16, rows, 4).cpu()
+    want = _tile_stats_of(y.cpu())
+    assert torch.equal(got[..., 0], want[..., 0]) and torch.equal(got[..., 2], want[..., 2])
+    assert not got[..., 3].any()
+    torch.testing.assert_close(got[..., 1], want[..., 1], rtol=2e-6, atol=0)
+
+
 def test_embedding_statistics(cuda_device) -> None:
     g = torch.Generator().manual_seed(5)
     w = torch.randn(1000, 768, generator=g).to(torch.bfloat16)
