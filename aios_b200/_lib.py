@@ -38,6 +38,7 @@ DEVICE_STATUS_NAMES = {
 EPI_STORE = 0
 EPI_SILU_MUL = 1
 EPI_ADD = 2
+LINEAR_EARLY_DEPENDENTS = 0x100  # OR-ed into a linear's epilogue (aios_b200.h)
 HISTORY_STAGED = 1  # aiosb_attention_decode stable_history modes
 HISTORY_PREFIX_ONCE = 2
 

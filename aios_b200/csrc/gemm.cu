@@ -77,6 +77,7 @@ struct GemmArgs {
   // register-operand path, store epilogue: per 16-column tile statistics of the
   // output (see GemvArgs::tile_stats); the tcgen05 path does not write them
   float4* tile_stats;
+  int user_early;  // AIOSB_LINEAR_EARLY_DEPENDENTS (register-operand path)
 };
 
 constexpr int kMaxNormRows = 64;
@@ -582,6 +583,7 @@ int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* 
     g.out_stat_ss = a.out_stat_ss;
     g.out_ss_stride = a.out_ss_stride;
     g.tile_stats = a.tile_stats;
+    g.early_dependents = a.user_early;
     return gemv_launch(g, as_stream(stream));
   }
   auto plan = [&]() {
@@ -642,6 +644,7 @@ int linear_impl(GemmArgs a, const void* x, int64_t rows, int64_t k, const void* 
 
 int check_common(const void* w, int64_t rows, int64_t k, int64_t n, void* y, int64_t y_row_stride, int epilogue,
                  const void* residual, int64_t residual_stride) {
+  epilogue &= ~AIOSB_LINEAR_EARLY_DEPENDENTS;
   AIOSB_REQUIRE(rows >= 0 && k > 0 && n > 0, AIOSB_ERR_INVALID_ARG, "linear: bad sizes");
   AIOSB_REQUIRE(n % kBM == 0, AIOSB_ERR_UNSUPPORTED, "linear: n=%lld must be a multiple of 128", (long long)n);
   AIOSB_REQUIRE(k % kBK == 0, AIOSB_ERR_UNSUPPORTED, "linear: k=%lld must be a multiple of 64", (long long)k);
@@ -663,6 +666,8 @@ GemmArgs base_args(void* y, int64_t y_row_stride, int epilogue, const void* resi
                    int32_t* status) {
   GemmArgs a;
   memset(&a, 0, sizeof(a));
+  a.user_early = (epilogue & AIOSB_LINEAR_EARLY_DEPENDENTS) ? 1 : 0;
+  epilogue &= ~AIOSB_LINEAR_EARLY_DEPENDENTS;
   a.y_row_stride = y_row_stride;
   a.y = (__nv_bfloat16*)y;
   a.residual = (const __nv_bfloat16*)residual;

@@ -190,9 +190,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
   // less per decode step). The others launch it only after their own wait, so a
   // kernel that follows them may read, before its own wait, anything written two
   // or more kernels back (the decode attention after the qkv linear does).
-  if (a.epilogue == AIOSB_EPI_ADD) pdl_launch_dependents();
+  // The caller may ask for the same early launch for other epilogues
+  // (AIOSB_LINEAR_EARLY_DEPENDENTS) where the successor allows it.
+  const bool early = a.epilogue == AIOSB_EPI_ADD || a.early_dependents;
+  if (early) pdl_launch_dependents();
   pdl_wait();
-  if (a.epilogue != AIOSB_EPI_ADD) pdl_launch_dependents();
+  if (!early) pdl_launch_dependents();
 
   // ---- B fragments: token row n = nt * 8 + g, this lane's 8 elements per block
   uint4 xb[NT][KB];

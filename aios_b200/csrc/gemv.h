@@ -49,6 +49,7 @@ struct GemvArgs {
   // 16-column tile and row, (max, sum of exp(v - max), min, 1 if any NaN) of the
   // stored bf16 values, at tile_stats[tile * rows + row]
   float4* tile_stats;
+  int early_dependents;  // launch the next kernel before the wait (as an ADD epilogue does)
 };
 
 // Mixer mode: at most this many sources (bank + partial), k of exactly kMixMaxK,

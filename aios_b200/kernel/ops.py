@@ -520,9 +520,12 @@ def linear_stat_norm(
     out: torch.Tensor | None = None,
     epilogue: int = _lib.EPI_STORE,
     tile_stats: torch.Tensor | None = None,
+    early_dependents: bool = False,
 ) -> torch.Tensor:
     """``linear(rmsnorm(s) * norm_weight, weight)`` with s and its sums of squares
-    from ``stats``; the normalised rows exist only inside the GEMM. With
+    from ``stats``; the normalised rows exist only inside the GEMM.
+    ``early_dependents``: the next kernel may launch before this one's wait
+    (``LINEAR_EARLY_DEPENDENTS``; the caller vouches for the successor). With
     ``tile_stats`` (fp32, [n / 16, rows, 4], see ``tile_stats_eligible``) the
     store epilogue also writes each 16-column tile's (max, sum of exp(v - max),
     min, NaN flag) of the stored values."""
@@ -541,9 +544,10 @@ def linear_stat_norm(
                   out.stride(0), tile_stats.data_ptr(), status_word(weight.device).data_ptr(),
                   _stream(weight.device))
         return out
+    flags = _lib.LINEAR_EARLY_DEPENDENTS if early_dependents else 0
     _lib.call("aiosb_linear_stat_norm", stats.x.data_ptr(), stats.ss.data_ptr(), stats.ss.stride(0), stats.parts,
               norm_weight.data_ptr(), float(eps), rows, k, weight.data_ptr(), n, out.data_ptr(), out.stride(0),
-              epilogue, None, 0, status_word(weight.device).data_ptr(), _stream(weight.device))
+              epilogue | flags, None, 0, status_word(weight.device).data_ptr(), _stream(weight.device))
     return out
 
 

@@ -58,6 +58,13 @@ extern "C" {
 #define AIOSB_EPI_SILU_MUL 1 /* W rows interleaved in 64-row gate/up blocks;
                                 y[:, f] = silu(x Wg^T) * (x Wu^T), bf16              */
 #define AIOSB_EPI_ADD 2      /* y = residual + bf16(x W^T), bf16 (residual may be y)  */
+/* OR-ed into the epilogue of aiosb_linear / aiosb_linear_stat_norm: on the
+ * register-operand path the next kernel on the stream may launch before this
+ * one's dependency wait, as after an AIOSB_EPI_ADD linear. Only for a successor
+ * whose reads before its own wait do not depend on this kernel's predecessor: a
+ * linear (it reads only its weights there), or a decode attention whose history
+ * and row metadata come from kernels that have completed whenever it can start. */
+#define AIOSB_LINEAR_EARLY_DEPENDENTS 0x100
 
 /* Library version (major*10000 + minor*100 + patch). */
 AIOSB_API int aiosb_version(void);
