@@ -274,11 +274,14 @@ AIOSB_API int aiosb_linear_attnres_rmsnorm(const void* bank, int64_t sources, in
  * rows * (num_qo_heads / num_kv_heads) <= 64. out: [rows, out_stride] bf16. *
  * stable_history != 0 (fused mode only) asserts that row_table, *prefix_len,
  * positions, seq_lens, out_loc, active, the page-table entries before each row's
- * current position and the K/V they point to were written by launches at least
- * two kernels back on this stream, and that the previous kernel launches this
- * one only after its own wait (not a decode-width AIOSB_EPI_ADD linear) (the
- * CandidateGroup runtime: prefix from the prefill, older suffix keys from earlier
- * steps, row metadata from this step's group step, the qkv linear just before). The kernel then copies the keys each row uses into shared memory
+ * current position and the K/V they point to were written by kernels that have
+ * completed whenever this one can start: launches at least two kernels back when
+ * the previous kernel launches this one only after its own wait, further back
+ * when it launches it early (the CandidateGroup runtime: prefix from the
+ * prefill, older suffix keys from earlier steps, row metadata from this step's
+ * group step; the qkv linear just before launches it after its wait in the first
+ * layer and early in the others, whose predecessors by then include a completed
+ * attention of the previous layer). The kernel then copies the keys each row uses into shared memory
  * before waiting on the previous kernel, and after the wait only this step's
  * projection row stays on its critical path. stable_history selects how:
  * AIOSB_HISTORY_STAGED (1), every row's CTA reads the prefix itself;
