@@ -362,11 +362,13 @@ def linear(
     epilogue: int = _lib.EPI_STORE,
     residual: torch.Tensor | None = None,
     tile_stats: torch.Tensor | None = None,
+    early_dependents: bool = False,
 ) -> torch.Tensor:
     """y = x @ weight.T on the tensor cores (bf16 in, fp32 accumulate, bf16 out).
 
     ``epilogue=EPI_ADD`` returns ``residual + bf16(x @ weight.T)`` (residual may
-    be ``out`` for an in-place add). ``tile_stats`` as in ``linear_stat_norm``."""
+    be ``out`` for an in-place add). ``tile_stats`` and ``early_dependents`` as in
+    ``linear_stat_norm``."""
     _require_cuda(x, weight, what="linear")
     if x.ndim != 2 or weight.ndim != 2 or x.shape[1] != weight.shape[1]:
         raise ValueError("linear expects x [T, K] and weight [N, K]")
@@ -395,7 +397,7 @@ def linear(
         n,
         out.data_ptr(),
         out.stride(0),
-        epilogue,
+        epilogue | (_lib.LINEAR_EARLY_DEPENDENTS if early_dependents else 0),
         _ptr(residual) if epilogue == _lib.EPI_ADD else None,
         residual.stride(0) if (epilogue == _lib.EPI_ADD and residual is not None) else 0,
         status_word(x.device).data_ptr(),

@@ -20,7 +20,7 @@ from ..attention import B200AttentionBackend
 from ..core import get_global_ctx
 from ..kernel import ops
 from ..layers import BaseOP, Embedding, LMHead, OPList, RMSNorm, RotaryEmbedding
-from .qwen3 import Qwen3Attention, Qwen3ForCausalLM, Qwen3MLP
+from .qwen3 import _EARLY_LINEARS, Qwen3Attention, Qwen3ForCausalLM, Qwen3MLP
 
 if TYPE_CHECKING:
     from ..core import Batch
@@ -132,7 +132,11 @@ class MiniMindAttnResDecoderLayer(BaseOP):
         else:
             # the mixer writes the input-normalised rows straight away
             normed = mix_and_norm(mixer, norm, bank, partial, mixed, stable)
-            attn = self.self_attn.attend(normed, rotary, paged_kv_cache, batch)
+            # the qkv linear launches the attention early from the second layer
+            # on, and the gate/up linear the down linear (qwen3._EARLY_LINEARS)
+            qkv = ops.linear(normed, self.self_attn.qkv_proj.weight,
+                             early_dependents=_EARLY_LINEARS and self.self_attn._layer_idx > 0)
+            attn = self.self_attn.attend_qkv(qkv, rotary, paged_kv_cache, batch)
         w_o = self.self_attn.o_proj.weight
         if partial is None:
             partial = ops.linear(attn, w_o)
@@ -145,7 +149,8 @@ class MiniMindAttnResDecoderLayer(BaseOP):
                                              self.mlp.gate_up_proj.packed_weight(), epilogue=_lib.EPI_SILU_MUL)
         else:
             normed = mix_and_norm(mixer, norm, bank, partial, mixed, bank.shape[0])
-            act = self.mlp.gate_up_proj.forward_silu_mul(normed)
+            act = ops.linear(normed, self.mlp.gate_up_proj.packed_weight(), epilogue=_lib.EPI_SILU_MUL,
+                             early_dependents=_EARLY_LINEARS)
         target = partial if out is None else out
         ops.linear(act, self.mlp.down_proj.weight, out=target, epilogue=_lib.EPI_ADD, residual=partial)
         return target
