@@ -1258,7 +1258,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_fused_kernel(const 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t tok_stride = (int64_t)a.hkv * D;
 
-  pdl_enter();
+  // ---- before the wait: the request and tile arrays, the positions, the page
+  // table, the norm weights and the RoPE rows were written before this forward
+  // began (one host-to-device copy and the page-table reset precede the prefill
+  // graph), so they are staged while the qkv projection still runs
+  pdl_launch_dependents();
   const int req = a.tile_req[tile];
   const int q0 = a.tile_q0[tile];
   const int qlen = a.req_q_len[req];
@@ -1272,27 +1276,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_fused_kernel(const 
     return;
   }
   const int Q = nq * g;
-  // ---- prologue. Item it < Q is query (token q0 + it / g, head h * g + it % g);
-  // the others are new key rows 0 .. nnew - 1 of KV head h. Every input is first
-  // staged in two cooperative rounds (projection rows, values, positions and
-  // norm weights; then the RoPE rows of those positions), so that the per-item
-  // work reads shared memory only.
   constexpr int kVec = D / 8;  // 16-byte vectors per head row
-  const uint4* qkv4 = reinterpret_cast<const uint4*>(a.qkv);
-  const int64_t row4 = a.qkv_stride / 8;
-  for (int idx = threadIdx.x; idx < (Q + 2 * nnew) * kVec; idx += blockDim.x) {
-    const int it = idx / kVec, c = idx % kVec;
-    int j, hh;
-    uint4* dst;
-    if (it < Q) {
-      j = q0 + it / g, hh = h * g + it % g, dst = reinterpret_cast<uint4*>(RAW + it * D);
-    } else if (it < Q + nnew) {
-      j = it - Q, hh = a.hq + h, dst = reinterpret_cast<uint4*>(RAW + it * D);
-    } else {
-      j = it - Q - nnew, hh = a.hq + a.hkv + h, dst = reinterpret_cast<uint4*>(NV + j * D);
-    }
-    dst[c] = qkv4[(qbase + j) * row4 + (int64_t)hh * kVec + c];
-  }
   for (int j = threadIdx.x; j < nnew; j += blockDim.x) {
     int pos = a.positions[qbase + j];
     if (pos < 0 || pos >= a.max_pos) {
@@ -1311,6 +1295,26 @@ __global__ void __launch_bounds__(kAttnThreads) attn_prefill_fused_kernel(const 
     const int64_t pr = (int64_t)pos_s[j] * kVec + c;
     reinterpret_cast<uint4*>(CS + j * D)[c] = reinterpret_cast<const uint4*>(a.cos_tab)[pr];
     reinterpret_cast<uint4*>(SN + j * D)[c] = reinterpret_cast<const uint4*>(a.sin_tab)[pr];
+  }
+  pdl_wait();
+  // ---- after the wait: this layer's projection rows. Item it < Q is query
+  // (token q0 + it / g, head h * g + it % g); the others are new key rows
+  // 0 .. nnew - 1 of KV head h, staged so that the per-item work reads shared
+  // memory only.
+  const uint4* qkv4 = reinterpret_cast<const uint4*>(a.qkv);
+  const int64_t row4 = a.qkv_stride / 8;
+  for (int idx = threadIdx.x; idx < (Q + 2 * nnew) * kVec; idx += blockDim.x) {
+    const int it = idx / kVec, c = idx % kVec;
+    int j, hh;
+    uint4* dst;
+    if (it < Q) {
+      j = q0 + it / g, hh = h * g + it % g, dst = reinterpret_cast<uint4*>(RAW + it * D);
+    } else if (it < Q + nnew) {
+      j = it - Q, hh = a.hq + h, dst = reinterpret_cast<uint4*>(RAW + it * D);
+    } else {
+      j = it - Q - nnew, hh = a.hq + a.hkv + h, dst = reinterpret_cast<uint4*>(NV + j * D);
+    }
+    dst[c] = qkv4[(qbase + j) * row4 + (int64_t)hh * kVec + c];
   }
   __syncthreads();
   for (int it = warp; it < Q + nnew; it += kAttnWarps) {

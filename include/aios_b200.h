@@ -341,7 +341,12 @@ AIOSB_API int aiosb_attention_prefill(const void* q, int64_t q_stride, const voi
  * queries and the new keys of its causal window, stores the K/V of its own
  * tokens at out_loc, and reads cached keys (positions below cached_len) from the
  * paged cache. Those cached keys must come from earlier launches. The output
- * and the stored K/V equal the two-call path bit for bit. */
+ * and the stored K/V equal the two-call path bit for bit. The request and tile
+ * arrays, positions, page table, norm weights and RoPE tables are read before
+ * the kernel waits on the previous kernel of the stream: they must have been
+ * written by copies, or by kernels that have completed whenever this one can
+ * start (with a previous kernel that launches it after its own wait: two or
+ * more kernels back). Only qkv is read after the wait. */
 AIOSB_API int aiosb_attention_prefill_fused(
     const void* qkv, int64_t qkv_stride, const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_tab,
     const void* sin_tab, int64_t max_pos, const int32_t* positions, const int32_t* out_loc, void* k_cache,
