@@ -39,6 +39,7 @@ EPI_STORE = 0
 EPI_SILU_MUL = 1
 EPI_ADD = 2
 LINEAR_EARLY_DEPENDENTS = 0x100  # OR-ed into a linear's epilogue (aios_b200.h)
+GROUP_AFTER_FORWARD = 1  # aiosb_group_ptrs.flags
 HISTORY_STAGED = 1  # aiosb_attention_decode stable_history modes
 HISTORY_PREFIX_ONCE = 2
 
@@ -114,6 +115,7 @@ class GroupPtrs(ctypes.Structure):
         ("ring", _p),
         ("status", _p),
         ("tile_stats", _p),
+        ("flags", _i64),
     ]
 
 

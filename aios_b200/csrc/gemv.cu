@@ -191,8 +191,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a
   // kernel that follows them may read, before its own wait, anything written two
   // or more kernels back (the decode attention after the qkv linear does).
   // The caller may ask for the same early launch for other epilogues
-  // (AIOSB_LINEAR_EARLY_DEPENDENTS) where the successor allows it.
-  const bool early = a.epilogue == AIOSB_EPI_ADD || a.early_dependents;
+  // (AIOSB_LINEAR_EARLY_DEPENDENTS) where the successor allows it. The LM head
+  // with tile statistics always does: its successor, the CandidateGroup step,
+  // reads only its state before its own wait.
+  const bool early = a.epilogue == AIOSB_EPI_ADD || a.early_dependents || TILES;
   if (early) pdl_launch_dependents();
   pdl_wait();
   if (!early) pdl_launch_dependents();
@@ -528,7 +530,11 @@ int launch_mma(const GemvArgs& a, cudaStream_t stream) {
     per_sm = resident_per_sm = n;
   }
   const int groups = (a.rows + NT * 8 - 1) / (NT * 8);  // token row groups (grid y)
-  const int64_t resident = std::max<int64_t>(1, (int64_t)resident_per_sm * sm_count() / groups);
+  // the LM head with tile statistics leaves one SM per row free, so that the
+  // CandidateGroup step that follows (one CTA per row) starts while it runs
+  constexpr bool TILES = MODE == kGemvStatTiles || MODE == kGemvPlainTiles;
+  const int sms = TILES ? std::max(1, sm_count() - a.rows) : sm_count();
+  const int64_t resident = std::max<int64_t>(1, (int64_t)resident_per_sm * sms / groups);
   const unsigned blocks = (unsigned)std::min<int64_t>(tiles, resident);
   cudaError_t e = launch_pdl(kern, dim3(blocks, (unsigned)groups), dim3(kGemvThreads), dyn, stream, a);
   if (e != cudaSuccess) return set_error(AIOSB_ERR_LAUNCH, "linear (gemv mma): %s", cudaGetErrorString(e));

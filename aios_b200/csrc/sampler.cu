@@ -884,7 +884,14 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   RowSmem& s = *reinterpret_cast<RowSmem*>(smem_raw);
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw + sizeof(RowSmem));
   __shared__ SplitXchg xs;
-  pdl_enter();
+  // After the decode forward (AIOSB_GROUP_AFTER_FORWARD) everything but the
+  // logits and tile statistics was written before that forward began: the
+  // state, the row arrays and the id lists are read while the LM head still
+  // runs, and the wait comes just before the logits. Otherwise (after
+  // group_begin, or any other caller) the step waits first.
+  const bool early_reads = !SPLIT && (g.flags & AIOSB_GROUP_AFTER_FORWARD) != 0;
+  pdl_launch_dependents();
+  if (!early_reads) pdl_wait();
   aiosb_group_state* st = g.state;
   const int r = blockIdx.x / C;
   const int c = SPLIT ? (int)cluster_ctarank() : 0;
@@ -899,12 +906,15 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
   const int NTv = Vl >> 4;
   const bool tiles_in = !SPLIT && g.tile_stats != nullptr && (Vl & 15) == 0 && Vl <= kMaxVocab;
   float4 tv[kTilesPer];
+  auto load_tiles = [&]() {
 #pragma unroll
-  for (int q = 0; q < kTilesPer; ++q) {
-    const int t = tid + q * kSampThreads;
-    tv[q] = make_float4(-INFINITY, 0.f, INFINITY, 0.f);
-    if (tiles_in && t < NTv) tv[q] = reinterpret_cast<const float4*>(g.tile_stats)[(int64_t)t * gridDim.x + r];
-  }
+    for (int q = 0; q < kTilesPer; ++q) {
+      const int t = tid + q * kSampThreads;
+      tv[q] = make_float4(-INFINITY, 0.f, INFINITY, 0.f);
+      if (tiles_in && t < NTv) tv[q] = reinterpret_cast<const float4*>(g.tile_stats)[(int64_t)t * gridDim.x + r];
+    }
+  };
+  if (!early_reads) load_tiles();
   const int step = st->step;
   const int V = st->vocab;
   const int S = st->max_steps;
@@ -970,6 +980,10 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
     }
   };
   const float u = run ? g.uniforms[(int64_t)r * S + step] : 0.f;
+  if (early_reads) {
+    pdl_wait();  // the LM head's logits and tile statistics
+    load_tiles();
+  }
   int tok = 0;
   float mx = 0.f, lse = 0.f;
   bool have = false;

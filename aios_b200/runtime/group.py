@@ -4,8 +4,12 @@
 One round of ``attempts`` candidate rows runs as
 
     group_begin                      (reset rows, broadcast prefix logits, uniforms)
-    [group_step + decode forward] x (max_new_tokens - 1)   (one CUDA graph replay each)
-    group_step                       (last sample, no forward)
+    group_step                       (first sample, from the prefix row)
+    [decode forward + group_step] x (max_new_tokens - 1)   (one CUDA graph replay each)
+
+Inside a step graph the step follows the forward's LM head and reads its state
+before waiting on it (AIOSB_GROUP_AFTER_FORWARD); the LM head leaves one SM per
+row free so that the step's CTAs start while it runs.
 
 ``group_step`` samples every active row, does the EOS/terminal bookkeeping,
 compacts finished rows and allocates the next KV slots from the device FIFO in
@@ -185,9 +189,13 @@ class CandidateGroupRuntime:
         self.tile_stats = (torch.zeros(self.vocab // 16 * max_rows * 4, dtype=torch.float32, device=dev)
                            if _TILE_SAMPLING and self.vocab % 16 == 0 else None)
         self._tile_rows: dict[int, bool] = {}
+        # the steps inside a step graph follow that graph's forward
+        # (GROUP_AFTER_FORWARD: the step reads its state while the LM head runs)
+        self._ptrs_graph = _lib.GroupPtrs.from_buffer_copy(self.ptrs)
+        self._ptrs_graph.flags = _lib.GROUP_AFTER_FORWARD
         self._ptrs_tiles = None
         if self.tile_stats is not None:
-            self._ptrs_tiles = _lib.GroupPtrs.from_buffer_copy(self.ptrs)
+            self._ptrs_tiles = _lib.GroupPtrs.from_buffer_copy(self._ptrs_graph)
             self._ptrs_tiles.tile_stats = self.tile_stats.data_ptr()
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self._graph_launches: dict[int, int] = {}
@@ -304,19 +312,26 @@ class CandidateGroupRuntime:
     def _stream(self) -> int:
         return torch.cuda.current_stream(self.device).cuda_stream
 
-    def _group_step(self, rows: int, large: bool = False) -> None:
+    def _group_step(self, rows: int, large: bool = False, after_forward: bool = False) -> None:
         # top_k_max: the largest sorted candidate set a round of this graph may ask for
         top_k_max = self.vocab if large else SORT_K
-        ptrs = self._ptrs_tiles if self._tile_rows.get(rows, False) else self.ptrs
+        if not after_forward:
+            ptrs = self.ptrs  # a round's first step, after group_begin
+        elif self._tile_rows.get(rows, False):
+            ptrs = self._ptrs_tiles
+        else:
+            ptrs = self._ptrs_graph
         _lib.call("aiosb_group_step", ctypes.byref(ptrs), rows, self.vocab, top_k_max, self._stream())
 
-    def _step_and_forward(self, rows: int, batch: Batch, large: bool = False) -> None:
-        self._group_step(rows, large)
+    def _forward_and_step(self, rows: int, batch: Batch, large: bool = False) -> None:
+        """One decode step after a round's first: the forward on the tokens the
+        previous step sampled, then the step that samples its logits."""
         if self._step_plan is not None:
             self._decode_step(rows)
-            return
-        with self.llm.ctx.forward_batch(batch):
-            self.llm.model.forward()
+        else:
+            with self.llm.ctx.forward_batch(batch):
+                self.llm.model.forward()
+        self._group_step(rows, large, after_forward=True)
 
     def _graph(self, rows: int, large: bool = False, stage: int = STAGE_CLASSES[0]) -> torch.cuda.CUDAGraph:
         """The step graph for `rows` rows; `large` steps sort whole rows (sorted
@@ -332,14 +347,14 @@ class CandidateGroupRuntime:
         self._write_state(dict(done=1, rows=rows, max_steps=2, vocab=self.vocab, page_size=1, capacity=1,
                                table_stride=self.llm.ctx.page_table.stride(0)))
         self.active.zero_()
-        self._step_and_forward(rows, batch, large)
+        self._forward_and_step(rows, batch, large)
         torch.cuda.synchronize(self.device)
         # the step kernel reads tile statistics only where this forward wrote them
         self._tile_rows[rows] = batch.tile_stats_written and self._step_plan is None
         graph = torch.cuda.CUDAGraph()
         before = _lib.launches
         with torch.cuda.graph(graph, pool=self._pool):
-            self._step_and_forward(rows, batch, large)
+            self._forward_and_step(rows, batch, large)
         self._graph_launches[key] = _lib.launches - before
         _lib.launches = before
         if self._pool is None:
@@ -435,14 +450,14 @@ class CandidateGroupRuntime:
                     time.sleep(0)
                 if int(self._mirror_np[1]):
                     break
-            if step + 1 < max_new_tokens:
-                graph.replay()
+            if step == 0:
+                self._group_step(attempts, large)  # samples the broadcast prefix row
+            else:
+                graph.replay()  # the forward on step - 1's tokens, then step `step`
                 _lib.count_launches(self._graph_launches[(attempts, large, stage)])
                 if self.record_logits:
                     torch.cuda.synchronize(self.device)
                     step_logits.append(self.logits[:attempts].float().cpu())
-            else:
-                self._group_step(attempts, large)
             launched += 1
         # [rows, steps] arrays use the round's max_new_tokens as their row stride
         n = attempts * max_new_tokens

@@ -226,7 +226,9 @@ AIOSB_API int aiosb_linear_stat_norm(const float* stat_x, const float* stat_ss, 
  * values (the LM head: what the CandidateGroup step needs to bound a row's top-k
  * and its log-sum-exp without scanning the row). Only on the register-operand
  * path with rows <= 16 and k <= 768 (else AIOSB_ERR_UNSUPPORTED); tile_stats:
- * [n / 16, rows, 4] fp32, 16-byte aligned. */
+ * [n / 16, rows, 4] fp32, 16-byte aligned. It lets the next kernel on the
+ * stream launch at once, and leaves `rows` SMs free for it (the CandidateGroup
+ * step, one CTA per row, with AIOSB_GROUP_AFTER_FORWARD). */
 /* aiosb_linear with the store epilogue that also writes the tile statistics of
  * aiosb_linear_stat_norm_tiles (the LM head on already normalised rows). */
 AIOSB_API int aiosb_linear_tiles(const void* x, int64_t rows, int64_t k, const void* w, int64_t n, void* y,
@@ -464,7 +466,17 @@ typedef struct aiosb_group_ptrs {
    * log-sum-exp from the tiles instead of scanning the row; the tokens are the
    * same, the log-probabilities agree to fp32 rounding. */
   const float* tile_stats;
+  /* AIOSB_GROUP_AFTER_FORWARD, or 0. */
+  int64_t flags;
 } aiosb_group_ptrs;
+
+/* aiosb_group_ptrs.flags: the previous kernel on the stream is the decode
+ * forward's last kernel (the LM head), which writes only `logits` and
+ * `tile_stats`, and every other input of the step (the state, the row arrays,
+ * uniforms, id lists, the FIFO) was written by work that had completed before
+ * that forward began. The step then reads those inputs while the LM head still
+ * runs, and waits on it only for the logits. */
+#define AIOSB_GROUP_AFTER_FORWARD 1
 
 /* Round start: resets the per-row outputs, copies the prefix logits [vocab] into
  * every row of `logits`, draws the uniform streams of seeds seed_base + r, sets

@@ -42,5 +42,5 @@ def test_group_structs_match_header_layout() -> None:
     state_fields = re.findall(r"^\s+(?:int32_t|int64_t|float)\s+(\w+);", text.split("typedef struct aiosb_group_state")[1].split("}")[0], re.M)
     assert state_fields == [f[0] for f in _lib.GroupState._fields_]
     ptr_block = text.split("typedef struct aiosb_group_ptrs")[1].split("} aiosb_group_ptrs")[0]
-    ptr_fields = re.findall(r"\*\s*(\w+);", ptr_block)
+    ptr_fields = re.findall(r"(?:\*\s*|\bint64_t\s+)(\w+);", ptr_block)
     assert ptr_fields == [f[0] for f in _lib.GroupPtrs._fields_]
