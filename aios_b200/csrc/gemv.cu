@@ -87,7 +87,8 @@ __device__ __forceinline__ void quad_sum2(float& x, float& y) {
 // the store epilogue also writing per-tile statistics (kGemvStatTiles,
 // kGemvPlainTiles: the LM head).
 template <int NT, int KB, int MODE, bool GROUPS>
-__global__ void __launch_bounds__(kGemvThreads) gemv_mma_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, ((MODE == kGemvStatTiles || MODE == kGemvPlainTiles) && NT == 1) ? 3 : 1)
+    gemv_mma_kernel(const GemvArgs a) {
   constexpr bool TILES = MODE == kGemvStatTiles || MODE == kGemvPlainTiles;
   constexpr bool STAT = MODE == kGemvStat || MODE == kGemvStatTiles, MIX = MODE == kGemvMix;
   static_assert(!MIX || (NT == 1 && !GROUPS), "the mixer operand serves one 8-row group");
