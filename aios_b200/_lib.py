@@ -116,6 +116,11 @@ class GroupPtrs(ctypes.Structure):
         ("status", _p),
         ("tile_stats", _p),
         ("flags", _i64),
+        ("embed_w", _p),
+        ("embed_out", _p),
+        ("embed_stat_x", _p),
+        ("embed_stat_ss", _p),
+        ("hidden", _i64),
     ]
 
 

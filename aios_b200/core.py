@@ -87,6 +87,10 @@ class Batch:
     # head sets tile_stats_written when it filled it.
     tile_stats_out: torch.Tensor | None = None
     tile_stats_written: bool = False
+    # Optional decode input already embedded (the CandidateGroup step writes it):
+    # (bf16 rows [rows, hidden], RowStats of them); the trunk then starts at its
+    # first linear instead of the embedding
+    pre_embedded: tuple | None = None
 
     @property
     def is_prefill(self) -> bool:

@@ -1268,6 +1268,28 @@ __global__ void __launch_bounds__(kSampThreads, 1) group_step_kernel(aiosb_group
     __syncthreads();
     tok = sample_row(s, rr, keys, V, p, u, large != 0);
   }
+  // the next forward's input row (aiosb_embedding_stat's warp-per-row form, so
+  // the outputs are the same bit for bit): warp 1 of the row's leader CTA
+  if (run && leader && g.embed_w != nullptr && (tid >> 5) == 1) {
+    const int64_t nv = g.hidden / 8;
+    const uint4* w = reinterpret_cast<const uint4*>(g.embed_w);
+    uint4* out = reinterpret_cast<uint4*>(g.embed_out);
+    const bool ok = tok >= 0 && tok < V;
+    float ss = 0.f;
+    for (int64_t i = lane; i < nv; i += 32) {
+      const uint4 v = ok ? w[(int64_t)tok * nv + i] : make_uint4(0u, 0u, 0u, 0u);
+      out[(int64_t)r * nv + i] = v;
+      const float f[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
+                          bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
+      float4* dst = reinterpret_cast<float4*>(g.embed_stat_x + (int64_t)r * g.hidden + 8 * i);
+      dst[0] = make_float4(f[0], f[1], f[2], f[3]);
+      dst[1] = make_float4(f[4], f[5], f[6], f[7]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) g.embed_stat_ss[r] = ss;
+  }
   if (run && warp0) {
     const bool eos = tok == eos_id;
     const bool emitted = !eos;
@@ -1580,9 +1602,25 @@ extern "C" int aiosb_group_begin(const aiosb_group_ptrs* g, const void* prefix_l
   return AIOSB_OK;
 }
 
+namespace aiosb {
+namespace {
+// The optional next-forward embedding of aiosb_group_ptrs: all of it or none.
+int check_group_embed(const aiosb_group_ptrs* g) {
+  if (g->embed_w == nullptr) return AIOSB_OK;
+  AIOSB_REQUIRE(g->embed_out && g->embed_stat_x && g->embed_stat_ss && g->hidden > 0 && g->hidden % 8 == 0,
+                AIOSB_ERR_INVALID_ARG, "group_step: embed_w needs embed_out, embed_stat_x, embed_stat_ss and "
+                "a hidden size that is a positive multiple of 8");
+  AIOSB_REQUIRE(aligned16(g->embed_w) && aligned16(g->embed_out) && aligned16(g->embed_stat_x), AIOSB_ERR_MISALIGNED,
+                "group_step: embed_w, embed_out and embed_stat_x must be 16-byte aligned");
+  return AIOSB_OK;
+}
+}  // namespace
+}  // namespace aiosb
+
 extern "C" int aiosb_group_step(const aiosb_group_ptrs* g, int64_t rows, int64_t vocab, int64_t top_k_max,
                                 void* stream) {
   AIOSB_REQUIRE(g && g->state, AIOSB_ERR_INVALID_ARG, "group_step: null pointer");
+  if (const int rc = check_group_embed(g); rc != AIOSB_OK) return rc;
   AIOSB_REQUIRE(rows >= 1 && vocab > 0 && vocab <= kMaxVocab, AIOSB_ERR_INVALID_ARG,
                 "group_step: rows >= 1 and vocab in [1, %d]", kMaxVocab);
   // top_k_max: the largest sorted candidate set the group's rounds may ask for
@@ -1747,6 +1785,7 @@ int static_step_scratch(int32_t** out) {
 extern "C" int aiosb_group_step_static(const aiosb_group_ptrs* g, int64_t rows, int64_t vocab, int64_t top_k_max,
                                        void* stream) {
   AIOSB_REQUIRE(g && g->state, AIOSB_ERR_INVALID_ARG, "group_step_static: null pointer");
+  if (const int rc = check_group_embed(g); rc != AIOSB_OK) return rc;
   AIOSB_REQUIRE(rows >= 1 && vocab > 0 && vocab <= kMaxVocab, AIOSB_ERR_INVALID_ARG,
                 "group_step_static: rows >= 1 and vocab in [1, %d]", kMaxVocab);
   const bool large = top_k_max > kMaxSortK;

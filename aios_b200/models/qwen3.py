@@ -178,7 +178,10 @@ class Qwen3Model(BaseOP):
         statistics of the final residual stream (the final norm's input)."""
         ctx = get_global_ctx()
         batch = ctx.batch
-        residual, stats = ops.embedding_stat(batch.input_ids, self.embed_tokens.weight)
+        if batch.is_decode and batch.pre_embedded is not None:
+            residual, stats = batch.pre_embedded
+        else:
+            residual, stats = ops.embedding_stat(batch.input_ids, self.embed_tokens.weight)
         for layer in self.layers.op_list:
             stats = layer.forward_stat(stats, residual, self._rotary_emb, ctx.kv_cache, batch)
         return stats

@@ -76,6 +76,21 @@ STAGE_CLASSES = (128, 512)
 _TILE_SAMPLING = os.environ.get("AIOSB_TILE_SAMPLING", "1") != "0"
 
 
+# The CandidateGroup step writes the next forward's embedded rows itself (one
+# kernel fewer per decode step); AIOSB_EMBED_IN_STEP=0 keeps the embedding kernel.
+_EMBED_IN_STEP = os.environ.get("AIOSB_EMBED_IN_STEP", "1") != "0"
+
+
+def _stat_trunk(model) -> bool:
+    """Whether the model's decode forward is the standard-residual trunk of
+    Qwen3Model.forward_stats (the one that takes pre-embedded rows)."""
+    from ..attention import B200AttentionBackend
+    from ..models.qwen3 import Qwen3ForCausalLM, Qwen3Model
+
+    return (isinstance(model, Qwen3ForCausalLM) and type(model.model) is Qwen3Model
+            and isinstance(model.attn_backend, B200AttentionBackend))
+
+
 def stage_class(prefix_len: int) -> int:
     return next((c for c in STAGE_CLASSES if prefix_len <= c), STAGE_CLASSES[-1])
 
@@ -183,6 +198,21 @@ class CandidateGroupRuntime:
             ring=llm.cache_manager.ring.data_ptr(),
             status=ops.status_word(dev).data_ptr(),
         )
+        # The step also embeds the tokens it samples for the next forward when that
+        # forward is the standard-residual trunk (it starts at its first linear)
+        self.pre_embedded = None
+        if _EMBED_IN_STEP and _stat_trunk(llm.model):
+            hidden = llm.config.hidden_size
+            emb_w = llm.model.model.embed_tokens.weight
+            self._emb_out = torch.zeros((max_rows, hidden), dtype=emb_w.dtype, device=dev)
+            self._emb_x = torch.zeros((max_rows, hidden), dtype=torch.float32, device=dev)
+            self._emb_ss = torch.zeros((1, max_rows), dtype=torch.float32, device=dev)
+            self.ptrs.embed_w = emb_w.data_ptr()
+            self.ptrs.embed_out = self._emb_out.data_ptr()
+            self.ptrs.embed_stat_x = self._emb_x.data_ptr()
+            self.ptrs.embed_stat_ss = self._emb_ss.data_ptr()
+            self.ptrs.hidden = hidden
+            self.pre_embedded = (self._emb_out, self._emb_x, self._emb_ss)
         # [vocab / 16, rows, 4] tile statistics of the decode logits, and per row
         # count whether the LM head of that count's step graph writes them (known
         # after the graph's eager warm-up forward)
@@ -299,6 +329,9 @@ class CandidateGroupRuntime:
         reqs = [Req(input_ids=torch.empty(1, dtype=torch.long), cached_len=0, output_len=1, uid=i,
                     sampling_params=SamplingParams(max_tokens=1), table_idx=i) for i in range(rows)]
         batch = Batch(reqs=reqs, phase="decode", logits_out=self.logits[:rows], tile_stats_out=self.tile_stats)
+        if self.pre_embedded is not None:
+            out, x, ss = self.pre_embedded
+            batch.pre_embedded = (out[:rows], ops.RowStats(x[:rows], ss[:, :rows]))
         batch.input_ids = self.tokens[:rows]
         batch.positions = self.positions[:rows]
         batch.out_loc = self.out_loc[:rows]

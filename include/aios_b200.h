@@ -468,6 +468,16 @@ typedef struct aiosb_group_ptrs {
   const float* tile_stats;
   /* AIOSB_GROUP_AFTER_FORWARD, or 0. */
   int64_t flags;
+  /* Optional, or NULL: the next forward's input, written by the step for every
+   * row it samples (the first kernel of the standard-residual forward, done here
+   * instead of in a launch of its own). embed_out[r] = embed_w[token] (bf16
+   * [rows, hidden]), embed_stat_x[r] its fp32 copy and embed_stat_ss[r] its sum
+   * of squares: aiosb_embedding_stat's outputs, bit for bit. */
+  const void* embed_w;   /* [vocab, hidden] bf16 embedding table */
+  void* embed_out;       /* [rows, hidden] bf16 */
+  float* embed_stat_x;   /* [rows, hidden] fp32 */
+  float* embed_stat_ss;  /* [rows] fp32 */
+  int64_t hidden;        /* multiple of 8 */
 } aiosb_group_ptrs;
 
 /* aiosb_group_ptrs.flags: the previous kernel on the stream is the decode

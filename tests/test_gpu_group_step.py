@@ -227,3 +227,41 @@ def test_group_step_reads_the_tile_statistics(cuda_device) -> None:
     assert torch.equal(a["tokens"], b["tokens"])
     lp_a, lp_b = a["token_logprobs"][:, 1].cpu(), b["token_logprobs"][:, 1].cpu()
     torch.testing.assert_close(lp_a - lp_b, torch.full((ROWS,), math.log(2.0)), rtol=0, atol=1e-5)
+
+
+def test_group_step_embeds_the_sampled_tokens(cuda_device) -> None:
+    """With the embedding fields set, each sampled row's next-forward input
+    (embedding row, its fp32 copy and its sum of squares) equals
+    aiosb_embedding_stat of the sampled token bit for bit; unsampled rows are
+    left as they were."""
+    from aios_b200.kernel import ops
+
+    dev = cuda_device
+    vocab, hidden = 16384, 768
+    g = torch.Generator().manual_seed(11)
+    grp = _group(dev, vocab, temperature=0.8, top_k=50, top_p=0.9, greedy=False)
+    emb_w = torch.randn(vocab, hidden, generator=g).to(torch.bfloat16).to(dev)
+    out = torch.full((ROWS, hidden), 7.0, dtype=torch.bfloat16, device=dev)
+    sx = torch.full((ROWS, hidden), 7.0, device=dev)
+    ss = torch.full((ROWS,), 7.0, device=dev)
+    p = grp["ptrs"]
+    p.embed_w, p.embed_out, p.embed_stat_x, p.embed_stat_ss, p.hidden = (
+        emb_w.data_ptr(), out.data_ptr(), sx.data_ptr(), ss.data_ptr(), hidden)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    _lib.call("aiosb_group_begin", ctypes.byref(p), grp["logits"][0].clone().data_ptr(), 5, ROWS - 2, ROWS, stream)
+    grp["logits"].copy_(_logits("randn", vocab, g).to(dev))
+    _lib.call("aiosb_group_step", ctypes.byref(p), ROWS, vocab, 50, stream)
+    torch.cuda.synchronize(dev)
+    assert int(grp["status"][0]) == 0
+    tok = grp["tokens"][: ROWS - 2].long()
+    want_out, want_stats = ops.embedding_stat(tok, emb_w)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(out[: ROWS - 2], want_out)
+    assert torch.equal(sx[: ROWS - 2], want_stats.x)
+    assert torch.equal(ss[: ROWS - 2], want_stats.ss[0])
+    # the two rows the round did not start are not sampled and keep their contents
+    assert bool((out[ROWS - 2 :].float() == 7.0).all()) and bool((ss[ROWS - 2 :] == 7.0).all())
+    # a half-set embedding is refused on the host
+    p.embed_out = 0
+    with pytest.raises(ValueError, match="embed_w needs"):
+        _lib.call("aiosb_group_step", ctypes.byref(p), ROWS, vocab, 50, stream)
