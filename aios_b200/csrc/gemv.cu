@@ -86,6 +86,11 @@ __device__ __forceinline__ void quad_sum2(float& x, float& y) {
 // 2 the AttnRes mixer's rows, normalised (kGemvMix), 3 and 4 as 1 and 0 with
 // the store epilogue also writing per-tile statistics (kGemvStatTiles,
 // kGemvPlainTiles: the LM head).
+// Launch bounds: the 8-row LM head with tile statistics is held to 80 registers
+// so that three CTAs share an SM; the others carry an explicit one-CTA bound,
+// under which ptxas gives the 768-wide decode linears 94 registers instead of
+// 69, and the S10 keystroke is faster with it (2.715 against 2.750 ms p50,
+// three runs each on one box).
 template <int NT, int KB, int MODE, bool GROUPS>
 __global__ void __launch_bounds__(kGemvThreads, ((MODE == kGemvStatTiles || MODE == kGemvPlainTiles) && NT == 1) ? 3 : 1)
     gemv_mma_kernel(const GemvArgs a) {
