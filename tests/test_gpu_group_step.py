@@ -168,7 +168,7 @@ TILE_CASES = [
 ]
 
 
-def _run_step(dev, name, vocab, temperature, top_k, top_p, logits, min_new, tiles):
+def _run_step(dev, name, vocab, temperature, top_k, top_p, logits, min_new, tiles, after_forward=False):
     grp = _group(dev, vocab, temperature=temperature, top_k=top_k, top_p=top_p, greedy=False, step=1,
                  min_new_tokens=min_new)
     stream = torch.cuda.current_stream(dev).cuda_stream
@@ -178,6 +178,8 @@ def _run_step(dev, name, vocab, temperature, top_k, top_p, logits, min_new, tile
     if tiles is not None:
         grp["tiles"] = tiles.to(dev)
         grp["ptrs"].tile_stats = grp["tiles"].data_ptr()
+    if after_forward:  # the state is read before the wait (the logits copy above is a plain kernel)
+        grp["ptrs"].flags = _lib.GROUP_AFTER_FORWARD
     _lib.call("aiosb_group_step", ctypes.byref(grp["ptrs"]), ROWS, vocab, top_k, stream)
     torch.cuda.synchronize(dev)
     assert int(grp["status"][0]) == 0
@@ -196,6 +198,10 @@ def test_group_step_from_tile_statistics(cuda_device, name, vocab, temperature, 
     tiles = _tile_stats(logits) if vocab % 16 == 0 else torch.zeros(4)
     fast = _run_step(cuda_device, name, vocab, temperature, top_k, top_p, logits, min_new, tiles)
     scan = _run_step(cuda_device, name, vocab, temperature, top_k, top_p, logits, min_new, None)
+    early = _run_step(cuda_device, name, vocab, temperature, top_k, top_p, logits, min_new, tiles, after_forward=True)
+    # the after-forward form reads the same inputs earlier: the same results bit for bit
+    assert torch.equal(early["tokens"], fast["tokens"])
+    assert torch.equal(early["token_logprobs"], fast["token_logprobs"])
     tok = fast["tokens"].cpu().long()
     assert torch.equal(tok, scan["tokens"].cpu().long())
     assert fast["output_ids"][:, 1].cpu().long().tolist() == tok.tolist()
