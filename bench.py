@@ -243,8 +243,10 @@ def reference_subprocess(keystrokes: int) -> dict | None:
 # `--cache-control none`, so that L2 carries over between launches and replays as
 # it does in the timed loop. It is
 # below the 201,326,592 algorithmic bytes: with cache-streaming weight loads,
-# about 16% of the weights are still in L2 when the next replay reads them.
-DECODE_LINEAR_TRAFFIC = 168_907_008
+# about 15% of the weights are still in L2 when the next replay reads them.
+# Captured again after the linears gained the early-successor flag and the
+# explicit launch bounds (171,439,616 B read + 322,816 B written).
+DECODE_LINEAR_TRAFFIC = 171_762_432
 # The same for one launch of the persistent decode-step kernel (None until an ncu
 # capture of it exists).
 DECODE_STEP_TRAFFIC = None
@@ -355,7 +357,7 @@ def decode_linear_roofline(llm, peaks: dict) -> dict:
             "frac": round(achieved / peak, 4), "traffic": DECODE_LINEAR_TRAFFIC,
             "traffic_unit": "bytes per decode step (57 launches)",
             "traffic_source": "one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum, --cache-control none) "
-                              "of the `linears` NVTX range of this function; gemv_mma_kernel is unchanged since",
+                              "of the `linears` NVTX range of this function, on the current gemv_mma_kernel",
             "algorithmic_bytes_per_step": wbytes,
             "launches_per_step": launches, "us_per_step": round(ms * 1e3, 2),
             "us_per_launch": round(ms * 1e3 / launches, 3)}
