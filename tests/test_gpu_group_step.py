@@ -7,7 +7,13 @@ splits each row on the top-k path (k <= 512) and falls back to one CTA for
 greedy, top-p without top-k, larger k, rows whose candidate set overflows (ties)
 and values that the temperature could overflow; each branch has a case here, run
 in process (one CTA) and in child processes with 2, 4 and 8 CTAs per row. Tokens are bit-exact (a mismatch only at
-a CDF-boundary rounding tie), log-probabilities within 2e-5."""
+a CDF-boundary rounding tie), log-probabilities within 2e-5.
+
+Decode steps sample from the LM head's per-tile statistics; those cases compare
+that path with the row scan (same tokens) and with the oracle, run the
+after-forward form that reads the state before its wait (bit-identical), and
+check that the step's embedding of the sampled tokens equals
+aiosb_embedding_stat bit for bit."""
 
 from __future__ import annotations
 
